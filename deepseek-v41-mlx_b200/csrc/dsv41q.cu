@@ -1,0 +1,807 @@
+// dsv41q.cu -- C ABI of libdsv41q (declared in include/dsv41q.h).  Single
+// translation unit: the kernels live in the *.cuh files included below.
+#include "common.cuh"
+#include "dequant.cuh"
+#include "act_quant.cuh"
+#include "engram.cuh"
+#include "qgemv.cuh"
+#include "router.cuh"
+#include "moe.cuh"
+
+using namespace dsv41;
+
+#define STREAM(s) (reinterpret_cast<cudaStream_t>(s))
+
+extern "C" const char *dsv41_get_last_error(void) { return g_last_error; }
+extern "C" int dsv41_abi_version(void) { return 1; }
+
+extern "C" int dsv41_device_status(void *stream, uint32_t *flags_out) {
+  DSV41_REQUIRE(flags_out, DSV41_ERR_BAD_ARG, "flags_out is NULL");
+  unsigned int v = 0, z = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&v, g_dev_status, sizeof(v), 0,
+                                            cudaMemcpyDeviceToHost, STREAM(stream));
+  if (e == cudaSuccess) e = cudaStreamSynchronize(STREAM(stream));
+  if (e == cudaSuccess)
+    e = cudaMemcpyToSymbolAsync(g_dev_status, &z, sizeof(z), 0, cudaMemcpyHostToDevice,
+                                STREAM(stream));
+  if (e == cudaSuccess) e = cudaStreamSynchronize(STREAM(stream));
+  *flags_out = v;
+  return cuda_status(e, "dsv41_device_status");
+}
+
+// ======================================================================= decode
+
+extern "C" int dsv41_e8m0_to_float(const uint8_t *scale, int64_t n, float *out, void *stream) {
+  DSV41_REQUIRE(n >= 0, DSV41_ERR_BAD_SHAPE, "n < 0");
+  if (n == 0) return DSV41_OK;
+  DSV41_REQUIRE(scale && out, DSV41_ERR_BAD_ARG, "NULL pointer");
+  k_e8m0_to_float<<<grid_for(n), 256, 0, STREAM(stream)>>>(scale, n, out);
+  DSV41_CHECK_LAUNCH("e8m0_to_float");
+  return DSV41_OK;
+}
+
+extern "C" int dsv41_dequant_fp8_block(const uint8_t *w, const uint8_t *s, int64_t rows,
+                                       int64_t cols, int out_dtype, void *out, void *stream) {
+  DSV41_REQUIRE(rows >= 0 && cols >= 0, DSV41_ERR_BAD_SHAPE, "negative shape");
+  DSV41_REQUIRE(out_dtype == DSV41_F32 || out_dtype == DSV41_BF16, DSV41_ERR_BAD_DTYPE,
+                "out_dtype must be F32 or BF16");
+  if (rows == 0 || cols == 0) return DSV41_OK;
+  DSV41_REQUIRE(w && s && out, DSV41_ERR_BAD_ARG, "NULL pointer");
+  const bool vec = (cols % 8 == 0) && aligned(w, 8);
+  const int64_t n = vec ? rows * cols / 8 : rows * cols;
+  cudaStream_t st = STREAM(stream);
+  if (out_dtype == DSV41_F32) {
+    if (vec) k_dequant_fp8_block<float, true><<<grid_for(n), 256, 0, st>>>(w, s, rows, cols, (float *)out);
+    else k_dequant_fp8_block<float, false><<<grid_for(n), 256, 0, st>>>(w, s, rows, cols, (float *)out);
+  } else {
+    if (vec) k_dequant_fp8_block<__nv_bfloat16, true><<<grid_for(n), 256, 0, st>>>(w, s, rows, cols, (__nv_bfloat16 *)out);
+    else k_dequant_fp8_block<__nv_bfloat16, false><<<grid_for(n), 256, 0, st>>>(w, s, rows, cols, (__nv_bfloat16 *)out);
+  }
+  DSV41_CHECK_LAUNCH("dequant_fp8_block");
+  return DSV41_OK;
+}
+
+static int fp4_launch(const uint8_t *p, const uint8_t *s, int64_t rows, int64_t cols,
+                      int out_dtype, void *out, void *stream, const char *what) {
+  DSV41_REQUIRE(rows >= 0 && cols >= 0 && cols % 2 == 0, DSV41_ERR_BAD_SHAPE,
+                "%s: cols must be even (two values per byte)", what);
+  DSV41_REQUIRE(out_dtype == DSV41_F32 || out_dtype == DSV41_BF16, DSV41_ERR_BAD_DTYPE,
+                "out_dtype must be F32 or BF16");
+  if (rows == 0 || cols == 0) return DSV41_OK;
+  DSV41_REQUIRE(p && out, DSV41_ERR_BAD_ARG, "NULL pointer");
+  const bool vec = (cols % 8 == 0) && aligned(p, 4);
+  const int64_t n = vec ? rows * cols / 8 : rows * cols;
+  cudaStream_t st = STREAM(stream);
+  if (out_dtype == DSV41_F32) {
+    if (vec) k_dequant_fp4<float, true><<<grid_for(n), 256, 0, st>>>(p, s, rows, cols, (float *)out);
+    else k_dequant_fp4<float, false><<<grid_for(n), 256, 0, st>>>(p, s, rows, cols, (float *)out);
+  } else {
+    if (vec) k_dequant_fp4<__nv_bfloat16, true><<<grid_for(n), 256, 0, st>>>(p, s, rows, cols, (__nv_bfloat16 *)out);
+    else k_dequant_fp4<__nv_bfloat16, false><<<grid_for(n), 256, 0, st>>>(p, s, rows, cols, (__nv_bfloat16 *)out);
+  }
+  DSV41_CHECK_LAUNCH(what);
+  return DSV41_OK;
+}
+
+extern "C" int dsv41_unpack_fp4(const uint8_t *packed, int64_t rows, int64_t cols, float *out,
+                                void *stream) {
+  return fp4_launch(packed, nullptr, rows, cols, DSV41_F32, out, stream, "unpack_fp4");
+}
+
+extern "C" int dsv41_dequant_fp4(const uint8_t *packed, const uint8_t *s, int64_t rows,
+                                 int64_t cols, int out_dtype, void *out, void *stream) {
+  DSV41_REQUIRE(s, DSV41_ERR_BAD_ARG, "scale is NULL");
+  return fp4_launch(packed, s, rows, cols, out_dtype, out, stream, "dequant_fp4");
+}
+
+extern "C" int dsv41_dequant_fp8_rows(const uint8_t *w, const uint8_t *s, int64_t rows,
+                                      int64_t d, int64_t block, float *out, void *stream) {
+  DSV41_REQUIRE(rows >= 0 && d >= 0 && block > 0 && d % block == 0, DSV41_ERR_BAD_SHAPE,
+                "d must be a multiple of block");
+  if (rows == 0 || d == 0) return DSV41_OK;
+  DSV41_REQUIRE(w && s && out, DSV41_ERR_BAD_ARG, "NULL pointer");
+  k_dequant_fp8_rows<<<grid_for(rows * d), 256, 0, STREAM(stream)>>>(w, s, rows, d, block, out);
+  DSV41_CHECK_LAUNCH("dequant_fp8_rows");
+  return DSV41_OK;
+}
+
+extern "C" int dsv41_dequant_affine(const uint32_t *wq, const void *scales, const void *biases,
+                                    int sb_dtype, int64_t rows, int64_t cols, int bits, int group,
+                                    int out_dtype, void *out, void *stream) {
+  DSV41_REQUIRE(bits >= 1 && bits <= 8, DSV41_ERR_BAD_ARG, "bits must be in [1, 8]");
+  DSV41_REQUIRE(group > 0 && rows >= 0 && cols >= 0 && cols % group == 0 &&
+                    (cols * bits) % 32 == 0,
+                DSV41_ERR_BAD_SHAPE, "cols must be a multiple of group and cols*bits of 32");
+  DSV41_REQUIRE(out_dtype == DSV41_F32 || out_dtype == DSV41_BF16, DSV41_ERR_BAD_DTYPE,
+                "out_dtype must be F32 or BF16");
+  DSV41_REQUIRE(sb_dtype == DSV41_F32 || sb_dtype == DSV41_BF16 || sb_dtype == DSV41_F16,
+                DSV41_ERR_BAD_DTYPE, "sb_dtype must be F32, BF16 or F16");
+  if (rows == 0 || cols == 0) return DSV41_OK;
+  DSV41_REQUIRE(wq && scales && biases && out, DSV41_ERR_BAD_ARG, "NULL pointer");
+  const int64_t n = rows * cols;
+  cudaStream_t st = STREAM(stream);
+#define AFF_LAUNCH(T, SB) \
+  k_dequant_affine<T, SB><<<grid_for(n), 256, 0, st>>>(wq, scales, biases, rows, cols, bits, group, (T *)out)
+  if (out_dtype == DSV41_F32) {
+    if (sb_dtype == DSV41_F32) AFF_LAUNCH(float, 0);
+    else if (sb_dtype == DSV41_BF16) AFF_LAUNCH(float, 1);
+    else AFF_LAUNCH(float, 2);
+  } else {
+    if (sb_dtype == DSV41_F32) AFF_LAUNCH(__nv_bfloat16, 0);
+    else if (sb_dtype == DSV41_BF16) AFF_LAUNCH(__nv_bfloat16, 1);
+    else AFF_LAUNCH(__nv_bfloat16, 2);
+  }
+#undef AFF_LAUNCH
+  DSV41_CHECK_LAUNCH("dequant_affine");
+  return DSV41_OK;
+}
+
+// ======================================================================= act_quant
+
+extern "C" int dsv41_act_quant_fp8(const void *x, int64_t M, int64_t K, int block,
+                                   int round_scale, uint8_t *q, void *s, int s_dtype,
+                                   void *deq_out, void *stream) {
+  DSV41_REQUIRE(block == 32 || block == 64 || block == 128, DSV41_ERR_BAD_ARG,
+                "block must be 32, 64 or 128");
+  DSV41_REQUIRE(M >= 0 && K >= 0 && K % block == 0, DSV41_ERR_BAD_SHAPE,
+                "K must be a multiple of block");
+  DSV41_REQUIRE(s_dtype == DSV41_F32 || (s_dtype == DSV41_U8 && round_scale), DSV41_ERR_BAD_DTYPE,
+                "scale dtype must be F32, or U8 (ue8m0) with round_scale");
+  if (M == 0 || K == 0) return DSV41_OK;
+  DSV41_REQUIRE(x && q && s, DSV41_ERR_BAD_ARG, "NULL pointer");
+  const int64_t warps = M * (K / block);
+  const unsigned blocks = unsigned((warps * 32 + 255) / 256);
+  cudaStream_t st = STREAM(stream);
+  const __nv_bfloat16 *xb = reinterpret_cast<const __nv_bfloat16 *>(x);
+  __nv_bfloat16 *dq = reinterpret_cast<__nv_bfloat16 *>(deq_out);
+  const int su8 = s_dtype == DSV41_U8;
+  if (block == 32) k_act_quant<1><<<blocks, 256, 0, st>>>(xb, M, K, round_scale, q, s, su8, dq);
+  else if (block == 64) k_act_quant<2><<<blocks, 256, 0, st>>>(xb, M, K, round_scale, q, s, su8, dq);
+  else k_act_quant<4><<<blocks, 256, 0, st>>>(xb, M, K, round_scale, q, s, su8, dq);
+  DSV41_CHECK_LAUNCH("act_quant_fp8");
+  return DSV41_OK;
+}
+
+// ======================================================================= qgemv host side
+
+namespace {
+
+struct WsCarve {
+  uint8_t *base;
+  size_t cap, off;
+  bool ok = true;
+  template <typename T> T *take(size_t count) {
+    off = align_up(off, 256);
+    T *p = reinterpret_cast<T *>(base + off);
+    off += count * sizeof(T);
+    if (off > cap) ok = false;
+    return p;
+  }
+};
+
+constexpr int QG_MAX_SPLIT = 16;
+
+template <int WF, int NMAT, int NT>
+int qgemv_launch(const CUtensorMap &w0, const CUtensorMap &w1, const CUtensorMap &x8,
+                 const CUtensorMap &x16, const CUtensorMap &x32, const QParams &p, int max_items,
+                 cudaStream_t st) {
+  using Cfg = QCfg<WF, NMAT, NT>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(k_qgemv<WF, NMAT, NT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+    if (e != cudaSuccess) return cuda_status(e, "qgemv smem attribute");
+    attr_set[dev] = true;
+  }
+  int grid = 2 * num_sms();
+  if (max_items < grid) grid = max_items;
+  if (grid < 1) grid = 1;
+  k_qgemv<WF, NMAT, NT><<<grid, QG_THREADS, Cfg::SMEM, st>>>(w0, w1, x8, x16, x32, p);
+  DSV41_CHECK_LAUNCH("qgemv");
+  return DSV41_OK;
+}
+
+// x16 tensor maps for box heights 8 / 16 / 32
+int make_x_maps(CUtensorMap (&m)[3], const void *x16, int64_t rows, int64_t K) {
+  const uint32_t boxes[3] = {8, 16, 32};
+  for (int i = 0; i < 3; ++i) {
+    int st = make_tmap_2d(&m[i], x16, CU_TENSOR_MAP_DATA_TYPE_UINT16, (uint64_t)K,
+                          (uint64_t)(rows < 1 ? 1 : rows), (uint64_t)K * 2, 64, boxes[i]);
+    if (st) return st;
+  }
+  return DSV41_OK;
+}
+
+int weight_map(CUtensorMap *m, const void *w, int64_t rows, int64_t row_bytes) {
+  return make_tmap_2d(m, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)row_bytes, (uint64_t)rows,
+                      (uint64_t)row_bytes, 128, QG_ROWS);
+}
+
+int pick_nsplit(int64_t base_items, int kstages) {
+  const int64_t target = 2 * (int64_t)num_sms();
+  int64_t ns = (target + base_items - 1) / base_items;
+  int64_t cap = kstages / 2;
+  if (cap < 1) cap = 1;
+  if (ns > cap) ns = cap;
+  if (ns > QG_MAX_SPLIT) ns = QG_MAX_SPLIT;
+  if (ns < 1) ns = 1;
+  return int(ns);
+}
+
+struct GemvWs {
+  __half *x16;
+  float *xscale, *xsum, *partial;
+  int *counters;
+};
+
+size_t gemv_ws_bytes(int64_t M, int64_t N, int64_t K) {
+  const int64_t tiles = ceil_div(N, QG_ROWS), nch = ceil_div(M, 32);
+  size_t b = 0;
+  b += align_up((size_t)M * K * 2, 256);
+  b += align_up((size_t)M * 4, 256);
+  b += align_up((size_t)M * ceil_div(K, 64) * 4, 256);
+  b += align_up((size_t)tiles * nch * QG_MAX_SPLIT * 32 * QG_CW * 16 * 4, 256);
+  b += align_up((size_t)tiles * nch * 4, 256);
+  return b + 256;
+}
+
+template <int WF>
+int gemv_common(const void *x, int64_t M, int64_t K, const void *w, int64_t w_row_bytes,
+                const uint8_t *s, int64_t sld, const void *aff_s, const void *aff_b, int64_t N,
+                int out_dtype, void *y, void *workspace, size_t ws_bytes, cudaStream_t st) {
+  constexpr int KS = Fmt<WF>::KS;
+  DSV41_REQUIRE(M >= 0 && N >= 0 && K >= 0, DSV41_ERR_BAD_SHAPE, "negative shape");
+  DSV41_REQUIRE(K % Fmt<WF>::GK == 0, DSV41_ERR_BAD_SHAPE, "K must be a multiple of %d",
+                Fmt<WF>::GK);
+  DSV41_REQUIRE(out_dtype == DSV41_F32 || out_dtype == DSV41_BF16, DSV41_ERR_BAD_DTYPE,
+                "out_dtype must be F32 or BF16");
+  if (M == 0 || N == 0) return DSV41_OK;
+  DSV41_REQUIRE(x && w && y, DSV41_ERR_BAD_ARG, "NULL pointer");
+  DSV41_REQUIRE(N <= (int64_t)INT32_MAX && M <= (int64_t)INT32_MAX / 2, DSV41_ERR_BAD_SHAPE,
+                "shape too large");
+  DSV41_REQUIRE(workspace && ws_bytes >= gemv_ws_bytes(M, N, K), DSV41_ERR_WORKSPACE,
+                "workspace too small: need %zu bytes", gemv_ws_bytes(M, N, K));
+  const int64_t tiles = ceil_div(N, QG_ROWS), nch = ceil_div(M, 32);
+  WsCarve wc{reinterpret_cast<uint8_t *>(workspace), ws_bytes, 0};
+  GemvWs ws;
+  ws.x16 = wc.take<__half>(M * K);
+  ws.xscale = wc.take<float>(M);
+  ws.xsum = wc.take<float>(M * ceil_div(K, 64));
+  ws.partial = wc.take<float>((size_t)tiles * nch * QG_MAX_SPLIT * 32 * QG_CW * 16);
+  ws.counters = wc.take<int>(tiles * nch);
+  DSV41_REQUIRE(wc.ok, DSV41_ERR_WORKSPACE, "workspace too small");
+
+  constexpr bool AFF = WF == WF_AFF4 || WF == WF_AFF8;
+  const int perm = WF == WF_AFF4 ? 4 : (WF == WF_AFF8 ? 8 : 0);
+  k_qx_prep<<<unsigned(M), 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16 *>(x), M, K,
+                                          nullptr, nullptr, ws.x16, ws.xscale,
+                                          AFF ? ws.xsum : nullptr, perm);
+  DSV41_CHECK_LAUNCH("qx_prep");
+
+  CUtensorMap wm, xm[3];
+  int rc = weight_map(&wm, w, N, w_row_bytes);
+  if (rc) return rc;
+  rc = make_x_maps(xm, ws.x16, M, K);
+  if (rc) return rc;
+
+  QParams p{};
+  p.scale[0] = s;
+  p.scale[1] = s;
+  p.aff_s = reinterpret_cast<const uint16_t *>(aff_s);
+  p.aff_b = reinterpret_cast<const uint16_t *>(aff_b);
+  p.N = N;
+  p.K = K;
+  p.sld = sld;
+  p.tiles = int(tiles);
+  p.kstages = int(ceil_div(K, KS));
+  p.nsplit = pick_nsplit(tiles * nch, p.kstages);
+  p.xscale = ws.xscale;
+  p.xsum = ws.xsum;
+  p.chunks = nullptr;
+  p.nchunks_host = int(nch);
+  p.dense_m = int(M);
+  p.epi = out_dtype == DSV41_F32 ? EPI_STORE_F32 : EPI_STORE_BF16;
+  p.out = y;
+  p.ldo = N;
+  p.partial = ws.partial;
+  p.counters = ws.counters;
+  if (p.nsplit > 1) {
+    cudaError_t e = cudaMemsetAsync(ws.counters, 0, sizeof(int) * tiles * nch, st);
+    if (e != cudaSuccess) return cuda_status(e, "memset counters");
+  }
+  const int items = int(tiles * nch * p.nsplit);
+  if (M <= 8) return qgemv_launch<WF, 1, 1>(wm, wm, xm[0], xm[1], xm[2], p, items, st);
+  if (M <= 16) return qgemv_launch<WF, 1, 2>(wm, wm, xm[0], xm[1], xm[2], p, items, st);
+  return qgemv_launch<WF, 1, 4>(wm, wm, xm[0], xm[1], xm[2], p, items, st);
+}
+
+}  // namespace
+
+extern "C" size_t dsv41_gemv_workspace_size(int64_t M, int64_t N, int64_t K) {
+  return gemv_ws_bytes(M, N, K);
+}
+
+extern "C" int dsv41_gemv_fp8_block(const void *x, int64_t M, int64_t K, const uint8_t *w,
+                                    const uint8_t *s, int64_t N, int out_dtype, void *y,
+                                    void *workspace, size_t workspace_bytes, void *stream) {
+  DSV41_REQUIRE(s || M == 0 || N == 0, DSV41_ERR_BAD_ARG, "scale is NULL");
+  return gemv_common<WF_FP8B>(x, M, K, w, K, s, ceil_div(K, 32), nullptr, nullptr, N, out_dtype,
+                              y, workspace, workspace_bytes, STREAM(stream));
+}
+
+extern "C" int dsv41_gemv_fp4(const void *x, int64_t M, int64_t K, const uint8_t *w,
+                              const uint8_t *s, int64_t N, int out_dtype, void *y, void *workspace,
+                              size_t workspace_bytes, void *stream) {
+  DSV41_REQUIRE(s || M == 0 || N == 0, DSV41_ERR_BAD_ARG, "scale is NULL");
+  return gemv_common<WF_FP4>(x, M, K, w, K / 2, s, K / 32, nullptr, nullptr, N, out_dtype, y,
+                             workspace, workspace_bytes, STREAM(stream));
+}
+
+extern "C" int dsv41_gemv_affine(const void *x, int64_t M, int64_t K, const uint32_t *wq,
+                                 const void *scales, const void *biases, int bits, int64_t N,
+                                 int out_dtype, void *y, void *workspace, size_t workspace_bytes,
+                                 void *stream) {
+  DSV41_REQUIRE(bits == 4 || bits == 8, DSV41_ERR_UNSUPPORTED,
+                "gemv_affine supports bits 4 and 8 (group 64)");
+  DSV41_REQUIRE((scales && biases) || M == 0 || N == 0, DSV41_ERR_BAD_ARG, "NULL scales/biases");
+  if (bits == 4)
+    return gemv_common<WF_AFF4>(x, M, K, wq, K / 2, nullptr, K / 64, scales, biases, N, out_dtype,
+                                y, workspace, workspace_bytes, STREAM(stream));
+  return gemv_common<WF_AFF8>(x, M, K, wq, K, nullptr, K / 64, scales, biases, N, out_dtype, y,
+                              workspace, workspace_bytes, STREAM(stream));
+}
+
+// ======================================================================= router
+
+namespace {
+int router_nks(int64_t T, int64_t K, int64_t E) {
+  const int64_t base = ceil_div(E, 16) * ceil_div(T, 8);
+  const int64_t target = 4 * (int64_t)num_sms();
+  int64_t want = ceil_div(target, base);
+  const int64_t k32 = K / 32;
+  int64_t best = 1;
+  for (int64_t d = 1; d <= k32 && d <= 64; ++d)
+    if (k32 % d == 0 && d <= want) best = d;
+  return int(best);
+}
+}  // namespace
+
+extern "C" size_t dsv41_moe_route_workspace_size(int64_t T, int64_t D, int64_t E) {
+  return align_up((size_t)64 * T * E * 4, 256) + 256;
+}
+
+static int route_impl(const void *x, int64_t T, int64_t D, const void *gate_w, const float *bias,
+                      int64_t E, int topk, int score_func, float gate_temp, int norm_topk_prob,
+                      float route_scale, float *weights, int32_t *indices, float *partial,
+                      cudaStream_t st) {
+  const int nks = router_nks(T, D, E);
+  const int64_t warps = ceil_div(E, 16) * ceil_div(T, 8) * nks;
+  k_router_scores<<<unsigned(ceil_div(warps * 32, 128)), 128, 0, st>>>(
+      reinterpret_cast<const __nv_bfloat16 *>(x), T, D,
+      reinterpret_cast<const __nv_bfloat16 *>(gate_w), E, nks, partial);
+  DSV41_CHECK_LAUNCH("router_scores");
+  const int threads = int(ceil_div(E, 32) * 32);
+  k_router_select<<<unsigned(T), threads, 0, st>>>(partial, nks, T, E, bias, topk, score_func,
+                                                   gate_temp, norm_topk_prob, route_scale, weights,
+                                                   indices);
+  DSV41_CHECK_LAUNCH("router_select");
+  return DSV41_OK;
+}
+
+static int route_check(int64_t T, int64_t D, int64_t E, int topk, int score_func) {
+  DSV41_REQUIRE(T >= 0 && D > 0 && D % 32 == 0, DSV41_ERR_BAD_SHAPE, "D must be a multiple of 32");
+  DSV41_REQUIRE(E > 0 && E <= 1024, DSV41_ERR_BAD_SHAPE, "1 <= E <= 1024");
+  DSV41_REQUIRE(topk >= 1 && topk <= 64 && topk <= E, DSV41_ERR_BAD_ARG, "1 <= topk <= min(64, E)");
+  DSV41_REQUIRE(score_func >= 0 && score_func <= 2, DSV41_ERR_BAD_ARG, "unknown score_func");
+  return DSV41_OK;
+}
+
+extern "C" int dsv41_moe_route(const void *x, int64_t T, int64_t D, const void *gate_w,
+                               const float *bias, int64_t E, int topk, int score_func,
+                               float gate_temp, int norm_topk_prob, float route_scale,
+                               float *weights, int32_t *indices, void *workspace,
+                               size_t workspace_bytes, void *stream) {
+  int rc = route_check(T, D, E, topk, score_func);
+  if (rc) return rc;
+  if (T == 0) return DSV41_OK;
+  DSV41_REQUIRE(x && gate_w && weights && indices, DSV41_ERR_BAD_ARG, "NULL pointer");
+  DSV41_REQUIRE(workspace && workspace_bytes >= dsv41_moe_route_workspace_size(T, D, E),
+                DSV41_ERR_WORKSPACE, "workspace too small");
+  DSV41_REQUIRE(aligned(x, 16) && aligned(gate_w, 16), DSV41_ERR_MISALIGNED,
+                "x and gate_w must be 16-byte aligned");
+  return route_impl(x, T, D, gate_w, bias, E, topk, score_func, gate_temp, norm_topk_prob,
+                    route_scale, weights, indices, reinterpret_cast<float *>(workspace),
+                    STREAM(stream));
+}
+
+// ======================================================================= MoE decode
+
+namespace {
+
+struct MoeWs {
+  float *rpart, *w;
+  int32_t *idx;
+  MoePlan plan;
+  __half *x16g, *x16, *H, *Hs;
+  float *xsg, *xs, *Y, *Ys;
+  float *part_gu, *part_dn, *part_sgu, *part_sdn;
+  int *cnt_gu, *cnt_dn, *cnt_sgu, *cnt_sdn;
+  size_t used;
+  bool ok;
+};
+
+struct MoeDims {
+  int64_t T, D, I, E, P, Pmax, Cmax, Tp, tiles_gu, tiles_dn;
+};
+
+MoeDims moe_dims(const dsv41_moe_config *c, int64_t T) {
+  MoeDims d;
+  d.T = T;
+  d.D = c->dim;
+  d.I = c->inter;
+  d.E = c->n_experts;
+  d.P = T * c->topk;
+  const int64_t act = d.P < d.E ? d.P : d.E;
+  d.Pmax = d.P + 3 * act;
+  d.Cmax = ceil_div(d.P, MOE_PAIRS_PER_CHUNK) + act;
+  d.Tp = ceil_div(T, 4) * 4;
+  d.tiles_gu = ceil_div(d.I, QG_ROWS);
+  d.tiles_dn = ceil_div(d.D, QG_ROWS);
+  return d;
+}
+
+MoeWs moe_carve(const MoeDims &d, void *base, size_t cap) {
+  WsCarve wc{reinterpret_cast<uint8_t *>(base), cap, 0};
+  MoeWs w;
+  w.rpart = wc.take<float>(64 * d.T * d.E);
+  w.w = wc.take<float>(d.P);
+  w.idx = wc.take<int32_t>(d.P);
+  w.plan.pair_tok = wc.take<int32_t>(d.Pmax);
+  w.plan.pair_row = wc.take<int32_t>(d.Pmax);
+  w.plan.gu_chunks = wc.take<QChunk>(d.Cmax);
+  w.plan.dn_chunks = wc.take<QChunk>(d.Cmax);
+  w.plan.sgu_chunks = wc.take<QChunk>(ceil_div(d.T, 32));
+  w.plan.sdn_chunks = wc.take<QChunk>(ceil_div(d.T, 16));
+  w.plan.counts = wc.take<int>(8);
+  w.x16g = wc.take<__half>(d.Pmax * d.D);
+  w.xsg = wc.take<float>(d.Pmax);
+  w.x16 = wc.take<__half>(d.T * d.D);
+  w.xs = wc.take<float>(d.T);
+  w.H = wc.take<__half>(2 * d.Pmax * d.I);
+  w.Hs = wc.take<__half>(2 * d.Tp * d.I);
+  w.Y = wc.take<float>(d.P * d.D);
+  w.Ys = wc.take<float>(d.T * d.D);
+  const size_t frag2 = 32 * QG_CW * 2 * 4 * 4, frag4 = 32 * QG_CW * 4 * 4;  // NMAT*NT*4 floats
+  w.part_gu = wc.take<float>(d.Cmax * d.tiles_gu * QG_MAX_SPLIT * frag2);
+  w.part_dn = wc.take<float>(d.Cmax * d.tiles_dn * QG_MAX_SPLIT * frag4);
+  w.part_sgu = wc.take<float>(ceil_div(d.T, 32) * d.tiles_gu * QG_MAX_SPLIT * 32 * QG_CW * 2 * 4 * 4);
+  w.part_sdn = wc.take<float>(ceil_div(d.T, 16) * d.tiles_dn * QG_MAX_SPLIT * frag4);
+  w.cnt_gu = wc.take<int>(d.Cmax * d.tiles_gu);
+  w.cnt_dn = wc.take<int>(d.Cmax * d.tiles_dn);
+  w.cnt_sgu = wc.take<int>(ceil_div(d.T, 32) * d.tiles_gu);
+  w.cnt_sdn = wc.take<int>(ceil_div(d.T, 16) * d.tiles_dn);
+  w.used = wc.off + 256;
+  w.ok = wc.ok;
+  return w;
+}
+
+}  // namespace
+
+extern "C" size_t dsv41_moe_decode_workspace_size(const dsv41_moe_config *cfg, int64_t T) {
+  if (!cfg || T < 0) return 0;
+  MoeDims d = moe_dims(cfg, T < 1 ? 1 : T);
+  MoeWs w = moe_carve(d, nullptr, SIZE_MAX);
+  return w.used;
+}
+
+namespace {
+
+int moe_check(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, int64_t T, bool shared) {
+  DSV41_REQUIRE(cfg && W, DSV41_ERR_BAD_ARG, "NULL config/weights");
+  int rc = route_check(T, cfg->dim, cfg->n_experts, cfg->topk, cfg->score_func);
+  if (rc) return rc;
+  DSV41_REQUIRE(cfg->inter > 0 && cfg->inter % 32 == 0, DSV41_ERR_BAD_SHAPE,
+                "inter must be a multiple of 32");
+  DSV41_REQUIRE(cfg->swiglu_limit > 0.0f && cfg->swiglu_limit <= 255.0f, DSV41_ERR_UNSUPPORTED,
+                "decode path needs 0 < swiglu_limit <= 255 (h must fit f16)");
+  DSV41_REQUIRE(T <= 4096, DSV41_ERR_UNSUPPORTED, "decode path is for T <= 4096 tokens");
+  if (T == 0) return DSV41_OK;
+  DSV41_REQUIRE(W->w1 && W->s1 && W->w3 && W->s3 && W->w2 && W->s2, DSV41_ERR_BAD_ARG,
+                "NULL expert pointer");
+  DSV41_REQUIRE(!shared || (W->sw1 && W->ss1 && W->sw3 && W->ss3 && W->sw2 && W->ss2),
+                DSV41_ERR_BAD_ARG, "NULL shared-expert pointer");
+  return DSV41_OK;
+}
+
+// Routed experts (SwitchGLU) for given indices -> Y[t*k + j, :] fp32, and the
+// shared expert -> Ys when `shared`.
+int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, const void *x,
+                     const MoeDims &d, MoeWs &ws, const int32_t *idx, float *Y, bool shared,
+                     cudaStream_t st) {
+  const int64_t T = d.T;
+  const int round = (cfg->flags & DSV41_MOE_ROUND_BF16) ? 1 : 0;
+  int rc;
+  // plan
+  k_moe_plan<<<1, 1024, 3 * d.E * sizeof(int), st>>>(idx, T, cfg->topk, d.E, ws.plan);
+  DSV41_CHECK_LAUNCH("moe_plan");
+  // activations gathered per pair
+  k_qx_prep<<<unsigned(d.Pmax), 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16 *>(x), T, d.D,
+                                                ws.plan.pair_tok, ws.plan.counts + 2, ws.x16g,
+                                                ws.xsg, nullptr, 0);
+  DSV41_CHECK_LAUNCH("qx_prep gathered");
+
+  CUtensorMap m_w1, m_w3, m_w2, xg[3], hx[3];
+  if ((rc = weight_map(&m_w1, W->w1, d.E * d.I, d.D / 2))) return rc;
+  if ((rc = weight_map(&m_w3, W->w3, d.E * d.I, d.D / 2))) return rc;
+  if ((rc = weight_map(&m_w2, W->w2, d.E * d.D, d.I / 2))) return rc;
+  if ((rc = make_x_maps(xg, ws.x16g, d.Pmax, d.D))) return rc;
+  if ((rc = make_x_maps(hx, ws.H, 2 * d.Pmax, d.I))) return rc;
+
+  const int64_t active = d.P < d.E ? d.P : d.E;
+  {  // routed gate/up (+SwiGLU) -> H
+    QParams p{};
+    p.scale[0] = W->s1;
+    p.scale[1] = W->s3;
+    p.N = d.I;
+    p.K = d.D;
+    p.sld = d.D / 32;
+    p.tiles = int(d.tiles_gu);
+    p.kstages = int(ceil_div(d.D, Fmt<WF_FP4>::KS));
+    p.nsplit = pick_nsplit(active * d.tiles_gu, p.kstages);
+    p.xscale = ws.xsg;
+    p.chunks = ws.plan.gu_chunks;
+    p.nchunks_dev = ws.plan.counts + 0;
+    p.epi = EPI_SWIGLU;
+    p.out = ws.H;
+    p.ldo = d.I;
+    p.limit = cfg->swiglu_limit;
+    p.round_gu = round;
+    p.round_h = 0;
+    p.partial = ws.part_gu;
+    p.counters = ws.cnt_gu;
+    if (p.nsplit > 1) {
+      cudaError_t e = cudaMemsetAsync(ws.cnt_gu, 0, sizeof(int) * d.Cmax * d.tiles_gu, st);
+      if (e != cudaSuccess) return cuda_status(e, "memset");
+    }
+    rc = qgemv_launch<WF_FP4, 2, 2>(m_w1, m_w3, xg[0], xg[1], xg[2], p,
+                                     int(d.Cmax * d.tiles_gu * p.nsplit), st);
+    if (rc) return rc;
+  }
+  {  // routed down -> Y[t*k + j]
+    QParams p{};
+    p.scale[0] = W->s2;
+    p.scale[1] = W->s2;
+    p.N = d.D;
+    p.K = d.I;
+    p.sld = d.I / 32;
+    p.tiles = int(d.tiles_dn);
+    p.kstages = int(ceil_div(d.I, Fmt<WF_FP4>::KS));
+    p.nsplit = pick_nsplit(active * d.tiles_dn, p.kstages);
+    p.xscale = nullptr;
+    p.chunks = ws.plan.dn_chunks;
+    p.nchunks_dev = ws.plan.counts + 1;
+    p.epi = EPI_DOWN;
+    p.out = Y;
+    p.ldo = d.D;
+    p.pair_row = ws.plan.pair_row;
+    p.partial = ws.part_dn;
+    p.counters = ws.cnt_dn;
+    if (p.nsplit > 1) {
+      cudaError_t e = cudaMemsetAsync(ws.cnt_dn, 0, sizeof(int) * d.Cmax * d.tiles_dn, st);
+      if (e != cudaSuccess) return cuda_status(e, "memset");
+    }
+    rc = qgemv_launch<WF_FP4, 1, 4>(m_w2, m_w2, hx[0], hx[1], hx[2], p,
+                                     int(d.Cmax * d.tiles_dn * p.nsplit), st);
+    if (rc) return rc;
+  }
+  if (!shared) return DSV41_OK;
+  // shared expert (fp8 32x32): gate/up -> Hs -> down -> Ys
+  k_qx_prep<<<unsigned(T), 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16 *>(x), T, d.D,
+                                          nullptr, nullptr, ws.x16, ws.xs, nullptr, 0);
+  DSV41_CHECK_LAUNCH("qx_prep shared");
+  CUtensorMap m_s1, m_s3, m_s2, xs[3], hs[3];
+  if ((rc = weight_map(&m_s1, W->sw1, d.I, d.D))) return rc;
+  if ((rc = weight_map(&m_s3, W->sw3, d.I, d.D))) return rc;
+  if ((rc = weight_map(&m_s2, W->sw2, d.D, d.I))) return rc;
+  if ((rc = make_x_maps(xs, ws.x16, d.T, d.D))) return rc;
+  if ((rc = make_x_maps(hs, ws.Hs, 2 * d.Tp, d.I))) return rc;
+  {
+    QParams p{};
+    p.scale[0] = W->ss1;
+    p.scale[1] = W->ss3;
+    p.N = d.I;
+    p.K = d.D;
+    p.sld = ceil_div(d.D, 32);
+    p.tiles = int(d.tiles_gu);
+    p.kstages = int(ceil_div(d.D, Fmt<WF_FP8B>::KS));
+    const int64_t nch = ceil_div(T, 32);
+    p.nsplit = pick_nsplit(nch * d.tiles_gu, p.kstages);
+    p.xscale = ws.xs;
+    p.chunks = ws.plan.sgu_chunks;
+    p.nchunks_dev = ws.plan.counts + 3;
+    p.epi = EPI_SWIGLU;
+    p.out = ws.Hs;
+    p.ldo = d.I;
+    p.limit = cfg->swiglu_limit;
+    p.round_gu = round;
+    p.round_h = round;
+    p.partial = ws.part_sgu;
+    p.counters = ws.cnt_sgu;
+    if (p.nsplit > 1) {
+      cudaError_t e = cudaMemsetAsync(ws.cnt_sgu, 0, sizeof(int) * nch * d.tiles_gu, st);
+      if (e != cudaSuccess) return cuda_status(e, "memset");
+    }
+    rc = qgemv_launch<WF_FP8B, 2, 4>(m_s1, m_s3, xs[0], xs[1], xs[2], p,
+                                      int(nch * d.tiles_gu * p.nsplit), st);
+    if (rc) return rc;
+  }
+  {
+    QParams p{};
+    p.scale[0] = W->ss2;
+    p.scale[1] = W->ss2;
+    p.N = d.D;
+    p.K = d.I;
+    p.sld = ceil_div(d.I, 32);
+    p.tiles = int(d.tiles_dn);
+    p.kstages = int(ceil_div(d.I, Fmt<WF_FP8B>::KS));
+    const int64_t nch = ceil_div(T, 16);
+    p.nsplit = pick_nsplit(nch * d.tiles_dn, p.kstages);
+    p.xscale = nullptr;
+    p.chunks = ws.plan.sdn_chunks;
+    p.nchunks_dev = ws.plan.counts + 4;
+    p.epi = EPI_DOWN;
+    p.out = ws.Ys;
+    p.ldo = d.D;
+    p.pair_row = nullptr;
+    p.npairs = int(T);
+    p.round_out = round;
+    p.partial = ws.part_sdn;
+    p.counters = ws.cnt_sdn;
+    if (p.nsplit > 1) {
+      cudaError_t e = cudaMemsetAsync(ws.cnt_sdn, 0, sizeof(int) * nch * d.tiles_dn, st);
+      if (e != cudaSuccess) return cuda_status(e, "memset");
+    }
+    rc = qgemv_launch<WF_FP8B, 1, 4>(m_s2, m_s2, hs[0], hs[1], hs[2], p,
+                                      int(nch * d.tiles_dn * p.nsplit), st);
+    if (rc) return rc;
+  }
+  return DSV41_OK;
+}
+
+}  // namespace
+
+extern "C" int dsv41_moe_experts(const dsv41_moe_config *cfg, const dsv41_moe_weights *W,
+                                 const void *x, int64_t T, const int32_t *indices, float *y,
+                                 void *workspace, size_t workspace_bytes, void *stream) {
+  int rc = moe_check(cfg, W, T, false);
+  if (rc || T == 0) return rc;
+  DSV41_REQUIRE(x && indices && y, DSV41_ERR_BAD_ARG, "NULL pointer");
+  const MoeDims d = moe_dims(cfg, T);
+  DSV41_REQUIRE(workspace, DSV41_ERR_WORKSPACE, "workspace is NULL");
+  MoeWs ws = moe_carve(d, workspace, workspace_bytes);
+  DSV41_REQUIRE(ws.ok && ws.used <= workspace_bytes, DSV41_ERR_WORKSPACE,
+                "workspace too small: need %zu bytes", ws.used);
+  return moe_experts_impl(cfg, W, x, d, ws, indices, y, false, STREAM(stream));
+}
+
+extern "C" int dsv41_moe_decode(const dsv41_moe_config *cfg, const dsv41_moe_weights *W,
+                                const void *x, int64_t T, int out_dtype, void *y,
+                                float *weights_out, int32_t *indices_out, void *workspace,
+                                size_t workspace_bytes, void *stream) {
+  const bool shared = cfg && !(cfg->flags & DSV41_MOE_NO_SHARED);
+  int rc = moe_check(cfg, W, T, shared);
+  if (rc || T == 0) return rc;
+  DSV41_REQUIRE(out_dtype == DSV41_F32 || out_dtype == DSV41_BF16, DSV41_ERR_BAD_DTYPE,
+                "out_dtype must be F32 or BF16");
+  DSV41_REQUIRE(x && y && W->gate_w, DSV41_ERR_BAD_ARG, "NULL pointer");
+  const MoeDims d = moe_dims(cfg, T);
+  DSV41_REQUIRE(workspace, DSV41_ERR_WORKSPACE, "workspace is NULL");
+  MoeWs ws = moe_carve(d, workspace, workspace_bytes);
+  DSV41_REQUIRE(ws.ok && ws.used <= workspace_bytes, DSV41_ERR_WORKSPACE,
+                "workspace too small: need %zu bytes", ws.used);
+  DSV41_REQUIRE(aligned(x, 16) && aligned(W->gate_w, 16), DSV41_ERR_MISALIGNED,
+                "x and gate_w must be 16-byte aligned");
+  cudaStream_t st = STREAM(stream);
+  float *wts = weights_out ? weights_out : ws.w;
+  int32_t *idx = indices_out ? indices_out : ws.idx;
+  rc = route_impl(x, T, d.D, W->gate_w, W->gate_bias, d.E, cfg->topk, cfg->score_func,
+                  cfg->gate_temp, cfg->norm_topk_prob, cfg->route_scale, wts, idx, ws.rpart, st);
+  if (rc) return rc;
+  rc = moe_experts_impl(cfg, W, x, d, ws, idx, ws.Y, shared, st);
+  if (rc) return rc;
+  const int64_t n = T * d.D;
+  if (out_dtype == DSV41_F32)
+    k_moe_combine<float><<<grid_for(n), 256, 0, st>>>(ws.Y, shared ? ws.Ys : nullptr, wts, T,
+                                                      cfg->topk, d.D, (float *)y);
+  else
+    k_moe_combine<__nv_bfloat16><<<grid_for(n), 256, 0, st>>>(
+        ws.Y, shared ? ws.Ys : nullptr, wts, T, cfg->topk, d.D, (__nv_bfloat16 *)y);
+  DSV41_CHECK_LAUNCH("moe_combine");
+  return DSV41_OK;
+}
+
+// ======================================================================= engram
+
+extern "C" int dsv41_engram_hash(const int64_t *input_ids, int64_t B, int64_t L, int64_t start_pos,
+                                 const int64_t *token_map, int64_t vocab, int64_t *ids_cache,
+                                 int64_t max_seq, const int64_t *multipliers,
+                                 const int64_t *primes, const int64_t *offsets, int n_layers,
+                                 int max_ngram, int n_heads, int64_t pad_id, int64_t *out,
+                                 void *stream) {
+  DSV41_REQUIRE(B >= 0 && L >= 0 && start_pos >= 0 && start_pos + L <= max_seq,
+                DSV41_ERR_BAD_SHAPE, "positions [start_pos, start_pos+L) exceed the id cache");
+  DSV41_REQUIRE(n_layers >= 1 && max_ngram >= 2 && n_heads >= 1 && vocab >= 1,
+                DSV41_ERR_BAD_ARG, "bad layout");
+  if (B == 0 || L == 0) return DSV41_OK;
+  DSV41_REQUIRE(input_ids && token_map && ids_cache && multipliers && primes && offsets && out,
+                DSV41_ERR_BAD_ARG, "NULL pointer");
+  cudaStream_t st = STREAM(stream);
+  const int64_t n1 = B * L;
+  k_engram_compress<<<unsigned(ceil_div(n1, 256)), 256, 0, st>>>(input_ids, B, L, start_pos,
+                                                                 token_map, vocab, ids_cache,
+                                                                 max_seq);
+  DSV41_CHECK_LAUNCH("engram_compress");
+  const int64_t n2 = B * L * n_layers;
+  k_engram_hash<<<unsigned(ceil_div(n2, 128)), 128, 0, st>>>(B, L, start_pos, ids_cache, max_seq,
+                                                             multipliers, primes, offsets,
+                                                             n_layers, max_ngram, n_heads, pad_id,
+                                                             out);
+  DSV41_CHECK_LAUNCH("engram_hash");
+  return DSV41_OK;
+}
+
+extern "C" int dsv41_engram_gather_rows(const uint8_t *table, const uint8_t *scale, int64_t rows,
+                                        int64_t row_lo, int64_t d, int64_t block,
+                                        const int64_t *idx, int64_t n_idx, int out_dtype,
+                                        void *out, void *stream) {
+  DSV41_REQUIRE(rows >= 0 && d > 0 && block > 0 && d % block == 0 && d % 8 == 0 && block % 8 == 0,
+                DSV41_ERR_BAD_SHAPE, "need d %% block == 0, 8 | d, 8 | block");
+  DSV41_REQUIRE(out_dtype == DSV41_F32 || out_dtype == DSV41_BF16, DSV41_ERR_BAD_DTYPE,
+                "out_dtype must be F32 or BF16");
+  if (n_idx == 0) return DSV41_OK;
+  DSV41_REQUIRE(table && scale && idx && out, DSV41_ERR_BAD_ARG, "NULL pointer");
+  DSV41_REQUIRE(aligned(table, 8), DSV41_ERR_MISALIGNED, "table must be 8-byte aligned");
+  const unsigned blocks = unsigned(ceil_div(n_idx * 32, 256));
+  if (out_dtype == DSV41_F32)
+    k_engram_gather_rows<float><<<blocks, 256, 0, STREAM(stream)>>>(
+        table, scale, rows, row_lo, d, block, idx, n_idx, (float *)out);
+  else
+    k_engram_gather_rows<__nv_bfloat16><<<blocks, 256, 0, STREAM(stream)>>>(
+        table, scale, rows, row_lo, d, block, idx, n_idx, (__nv_bfloat16 *)out);
+  DSV41_CHECK_LAUNCH("engram_gather_rows");
+  return DSV41_OK;
+}
+
+extern "C" int dsv41_engram_gather_sum(const uint8_t *table, const uint8_t *scale, int64_t rows,
+                                       int64_t row_lo, int64_t d, int64_t block,
+                                       const int64_t *idx, int64_t n_tok, int n_per_tok,
+                                       int out_dtype, void *out, void *stream) {
+  DSV41_REQUIRE(d == 256 || d == 512 || d == 1024, DSV41_ERR_UNSUPPORTED,
+                "gather_sum supports d in {256, 512, 1024}");
+  DSV41_REQUIRE(block >= 8 && block % 8 == 0 && d % block == 0 && rows >= 0 && n_per_tok >= 1,
+                DSV41_ERR_BAD_SHAPE, "need 8 | block and block | d");
+  DSV41_REQUIRE(out_dtype == DSV41_F32 || out_dtype == DSV41_BF16, DSV41_ERR_BAD_DTYPE,
+                "out_dtype must be F32 or BF16");
+  if (n_tok == 0) return DSV41_OK;
+  DSV41_REQUIRE(table && scale && idx && out, DSV41_ERR_BAD_ARG, "NULL pointer");
+  DSV41_REQUIRE(aligned(table, 8), DSV41_ERR_MISALIGNED, "table must be 8-byte aligned");
+  const unsigned blocks = unsigned(ceil_div(n_tok * 32, 256));
+  cudaStream_t st = STREAM(stream);
+#define GS(T, DPL)                                                                           \
+  k_engram_gather_sum<T, DPL><<<blocks, 256, 0, st>>>(table, scale, rows, row_lo, block, idx, \
+                                                      n_tok, n_per_tok, (T *)out)
+  if (out_dtype == DSV41_F32) {
+    if (d == 256) GS(float, 8);
+    else if (d == 512) GS(float, 16);
+    else GS(float, 32);
+  } else {
+    if (d == 256) GS(__nv_bfloat16, 8);
+    else if (d == 512) GS(__nv_bfloat16, 16);
+    else GS(__nv_bfloat16, 32);
+  }
+#undef GS
+  DSV41_CHECK_LAUNCH("engram_gather_sum");
+  return DSV41_OK;
+}

@@ -1,0 +1,601 @@
+// qgemv.cuh -- weight-decode fused into skinny matrix products (decode-time GEMV).
+//
+// y[m, n] = sum_k x[m, k] * W[n, k] for a few tokens m (<= 32 per pass) and a
+// weight W stored in one of the reference's quantized formats:
+//   WF_FP4  : e2m1 nibbles [N, K/2] + ue8m0 per (row, 32 k)      (dequant.py:53-68)
+//   WF_FP8B : e4m3 bytes [N, K] + ue8m0 per (32 rows, 32 k)      (dequant.py:45-50)
+//   WF_AFF4 / WF_AFF8 : MLX affine codes, bf16 scale/bias per (row, 64 k)
+// The weight bytes are the HBM stream this kernel is bounded by.
+//
+// Structure (one CTA = 4 consumer warps + 1 producer warp, persistent):
+//   * the producer warp streams 64-row x 128-byte weight tiles and the matching
+//     activation tiles into a STAGES-deep shared-memory ring with 2D TMA
+//     (128-byte swizzle, no multicast), signalling mbarriers with tx counts;
+//   * each consumer warp owns 16 weight rows; per 32/64-k scale group it decodes
+//     its share of the tile in registers straight to exact f16 (cvt.rn.f16x2.
+//     e2m1x2 / e4m3x2, or the 0x6400 magic for affine codes), runs
+//     mma.sync m16n8k16 f16 x f16 -> f32 against the activations, and folds the
+//     group's scale into an fp32 accumulator (scale * partial [+ bias * sum x]);
+//   * activations arrive as f16 with a per-row power-of-two scale applied by the
+//     producer of x (exact for bf16 inputs, see qx_prep), so every product is
+//     exact and accumulation is fp32.
+// The k order inside a group is permuted per thread (any permutation applied to
+// both operands leaves the dot product unchanged) so that each thread's slice of
+// a group is contiguous in shared memory.
+//
+// Work = chunks (a group of <= NT*8 x rows bound to one weight matrix, e.g. one
+// expert's tokens) x 64-row tiles x K splits.  K splits write fp32 fragments to a
+// workspace and the last CTA of a tile (atomic ticket) sums them in split order,
+// so results are deterministic.
+#pragma once
+#include "common.cuh"
+
+namespace dsv41 {
+
+enum : int { WF_FP4 = 0, WF_FP8B = 1, WF_AFF4 = 2, WF_AFF8 = 3 };
+enum : int { EPI_STORE_F32 = 0, EPI_STORE_BF16 = 1, EPI_SWIGLU = 2, EPI_DOWN = 3 };
+
+template <int WF> struct Fmt;
+template <> struct Fmt<WF_FP4> { static constexpr int KS = 256, GK = 32, NG = 8; };
+template <> struct Fmt<WF_FP8B> { static constexpr int KS = 128, GK = 32, NG = 4; };
+template <> struct Fmt<WF_AFF4> { static constexpr int KS = 256, GK = 64, NG = 4; };
+template <> struct Fmt<WF_AFF8> { static constexpr int KS = 128, GK = 64, NG = 2; };
+
+constexpr int QG_CW = 4;                   // consumer warps
+constexpr int QG_ROWS = 16 * QG_CW;        // weight rows per tile
+constexpr int QG_THREADS = 32 * (QG_CW + 1);
+constexpr int QG_STAGES = 4;
+
+// x-row chunk descriptor (device list for MoE, implicit for dense)
+struct QChunk {
+  int32_t mat;   // weight matrix index (expert); row base = mat * N
+  int32_t xrow;  // first x row
+  int32_t ntok;  // valid x rows
+  int32_t orow;  // output row / pair base
+};
+
+struct QParams {
+  const uint8_t *scale[2];     // FP4 / FP8B scale bytes per matrix
+  const uint16_t *aff_s;       // affine bf16 scales [N, K/64]
+  const uint16_t *aff_b;       // affine bf16 biases
+  int64_t N, K;
+  int64_t sld;                 // scale row stride in elements
+  int tiles;                   // ceil(N / QG_ROWS)
+  int nsplit;
+  int kstages;                 // K / KS
+  const float *xscale;         // per x row multiplier (power of two), or null
+  const float *xsum;           // affine: [xrows, K/64] sums of the f16 x values
+  const QChunk *chunks;        // null -> dense
+  const int *nchunks_dev;
+  int nchunks_host;            // dense: number of chunks
+  int dense_m;                 // dense: total x rows
+  int epi;
+  void *out;
+  int64_t ldo;
+  const int32_t *pair_row;     // EPI_DOWN: pair -> output row (null = identity below npairs)
+  int npairs;
+  float limit;
+  int round_gu;                // SWIGLU: round gate/up to bf16 first
+  int round_h;                 // SWIGLU: round h to bf16 (shared expert, port)
+  int round_out;               // DOWN: round output to bf16 (stored as f32)
+  float *partial;              // split-K fragments
+  int *counters;               // split-K tickets, zero on entry
+};
+
+__device__ __forceinline__ int rhoA(int g) { return ((g & 3) << 1) | (g >> 2); }  // 0,2,4,6,1,3,5,7
+__device__ __forceinline__ int rhoB(int g) { return ((g & 1) << 2) | (g >> 1); }  // 0,4,1,5,2,6,3,7
+
+// Which smem row (mod 8) an mma row g reads, per format: chosen so that the
+// warp's shared-memory loads of one group hit distinct banks (LDS.32 for fp4,
+// LDS.64 pairs of 16-byte chunks for fp8/aff4, LDS.128 chunks for aff8).
+template <int WF> __device__ __forceinline__ int wrow_perm(int g) {
+  return WF == WF_AFF8 ? rhoB(g) : rhoA(g);
+}
+// Which x row (within an n8 tile) mma column c reads.  fp4/fp8 use rhoB (one
+// LDS.128 per group; columns 2t / 2t+1 then hold slots t / 4+t, which the
+// down-projection epilogue relies on), affine uses the identity (two LDS.128).
+template <int WF> __device__ __forceinline__ int xcol_perm(int c) {
+  return (WF == WF_AFF4 || WF == WF_AFF8) ? c : rhoB(c);
+}
+
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(a));
+  return v;
+}
+
+// affine magic decode: f16x2 (1024 + q) - 1024 = exact q
+__device__ __forceinline__ uint32_t aff_pair(uint32_t bits) {
+  uint32_t v = bits | 0x64006400u;
+  __half2 h = __hsub2(*reinterpret_cast<__half2 *>(&v), __halves2half2(__ushort_as_half(0x6400),
+                                                                         __ushort_as_half(0x6400)));
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+
+template <int WF, int NMAT, int NT>
+struct QCfg {
+  static constexpr int KS = Fmt<WF>::KS;
+  static constexpr int NBOX = KS / 64;                       // x boxes per stage
+  static constexpr int W_BYTES = QG_ROWS * 128;              // per matrix per stage
+  static constexpr int XBOX_BYTES = NT * 8 * 128;            // max rows
+  static constexpr int STAGE_BYTES = NMAT * W_BYTES + NBOX * XBOX_BYTES;
+  static constexpr int SMEM = QG_STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int FRAG = NMAT * NT * 4;                 // fp32 per consumer thread
+};
+
+__device__ __forceinline__ void decode_chunk(const QParams &p, int item, int &chunk, int &tile,
+                                             int &split, QChunk &c) {
+  const int per_chunk = p.tiles * p.nsplit;
+  chunk = item / per_chunk;
+  const int rem = item % per_chunk;
+  tile = rem / p.nsplit;
+  split = rem % p.nsplit;
+  if (p.chunks) {
+    c = p.chunks[chunk];
+  } else {
+    c.mat = 0;
+    c.xrow = chunk * 32;  // dense chunks are 32 rows apart (NT <= 4)
+    c.ntok = min(32, p.dense_m - c.xrow);
+    c.orow = c.xrow;
+  }
+}
+
+// ------------------------------------------------------------------ the kernel
+template <int WF, int NMAT, int NT>
+__global__ void __launch_bounds__(QG_THREADS, 2)
+    k_qgemv(const __grid_constant__ CUtensorMap wmap0, const __grid_constant__ CUtensorMap wmap1,
+            const __grid_constant__ CUtensorMap xmap8, const __grid_constant__ CUtensorMap xmap16,
+            const __grid_constant__ CUtensorMap xmap32, const QParams p) {
+  using C = QCfg<WF, NMAT, NT>;
+  constexpr int KS = C::KS;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + QG_STAGES * C::STAGE_BYTES);
+  uint64_t *empty = full + QG_STAGES;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const int nchunks = p.chunks ? *p.nchunks_dev : p.nchunks_host;
+  const int nitems = nchunks * p.tiles * p.nsplit;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < QG_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], QG_CW);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == QG_CW) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      prefetch_tmap(&wmap0);
+      if (NMAT == 2) prefetch_tmap(&wmap1);
+      const uint64_t pol_w = l2_policy_evict_first();
+      const uint64_t pol_x = l2_policy_evict_last();
+      uint32_t it = 0;
+      for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
+        int chunk, tile, split;
+        QChunk c;
+        decode_chunk(p, item, chunk, tile, split, c);
+        const int kb = int((int64_t)p.kstages * split / p.nsplit);
+        const int ke = int((int64_t)p.kstages * (split + 1) / p.nsplit);
+        const int xr = c.ntok <= 8 ? 8 : (c.ntok <= 16 ? 16 : 32);
+        const CUtensorMap *xm = xr == 8 ? &xmap8 : (xr == 16 ? &xmap16 : &xmap32);
+        const uint32_t bytes = NMAT * C::W_BYTES + C::NBOX * xr * 128;
+        const int32_t wrow = int32_t(c.mat * p.N + (int64_t)tile * QG_ROWS);
+        for (int ks = kb; ks < ke; ++ks, ++it) {
+          const int slot = it % QG_STAGES;
+          const uint32_t ph = (it / QG_STAGES) & 1;
+          if (!mbar_wait(&empty[slot], ph ^ 1)) return;
+          uint8_t *st = smem + slot * C::STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[slot], bytes);
+          tma_load_2d(st, &wmap0, &full[slot], ks * 128, wrow, pol_w);
+          if (NMAT == 2) tma_load_2d(st + C::W_BYTES, &wmap1, &full[slot], ks * 128, wrow, pol_w);
+#pragma unroll
+          for (int b = 0; b < C::NBOX; ++b)
+            tma_load_2d(st + NMAT * C::W_BYTES + b * C::XBOX_BYTES, xm, &full[slot],
+                        ks * KS + b * 64, c.xrow, pol_x);
+        }
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ consumers
+  constexpr int NG = Fmt<WF>::NG;
+  constexpr bool AFF = (WF == WF_AFF4 || WF == WF_AFF8);
+  const int g = lane >> 2, t = lane & 3;
+  const int ra = wrow_perm<WF>(g);                // smem row (mod 8) of mma rows g, g+8
+  const int rowA = warp * 16 + ra;                // tile rows rowA, rowA + 8
+  const int xb = xcol_perm<WF>(g);                // x smem row (mod 8) for mma column g
+  const int cs[2] = {xcol_perm<WF>(2 * t), xcol_perm<WF>(2 * t + 1)};  // slots of my columns
+  uint32_t it = 0;
+
+  for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
+    int chunk, tile, split;
+    QChunk c;
+    decode_chunk(p, item, chunk, tile, split, c);
+    const int kb = int((int64_t)p.kstages * split / p.nsplit);
+    const int ke = int((int64_t)p.kstages * (split + 1) / p.nsplit);
+    const int64_t nbase = (int64_t)tile * QG_ROWS;              // row within the matrix
+    const int64_t grow0 = (int64_t)c.mat * p.N + nbase + rowA;  // stacked row of mma row g
+    const int ntiles_x = (c.ntok + 7) / 8;                      // active n8 tiles
+    const bool rok[2] = {nbase + rowA < p.N, nbase + rowA + 8 < p.N};
+    const int64_t fp8_rb = (int64_t)c.mat * ((p.N + 31) / 32) + ((nbase + warp * 16) >> 5);
+    const bool fp8_ok = nbase + warp * 16 < p.N;
+
+    float acc[NMAT][NT][4];
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+      for (int n = 0; n < NT; ++n)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[m][n][i] = 0.0f;
+
+    // per-stage scale operands, loaded one stage ahead (registers double buffer)
+    uint32_t sraw[NMAT][2][NG];    // fp4/fp8: e8m0 byte; affine: bf16 bits (scale)
+    uint32_t braw[2][NG];          // affine: bf16 bits (bias)
+    float xsn[NT][2][NG];          // affine: sums of x over the group per column
+    auto load_scales = [&](int ks, uint32_t (&so)[NMAT][2][NG], uint32_t (&bo)[2][NG],
+                           float (&xo)[NT][2][NG]) {
+      if constexpr (WF == WF_FP4) {
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint8_t *sp = p.scale[m] + (grow0 + 8 * h) * p.sld + (int64_t)ks * NG;
+#pragma unroll
+            for (int q = 0; q < NG; ++q) so[m][h][q] = rok[h] ? __ldg(sp + q) : 0u;
+          }
+      } else if constexpr (WF == WF_FP8B) {
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m) {
+          const uint8_t *sp = p.scale[m] + fp8_rb * p.sld + (int64_t)ks * NG;
+#pragma unroll
+          for (int q = 0; q < NG; ++q) {
+            so[m][0][q] = fp8_ok ? __ldg(sp + q) : 0u;
+            so[m][1][q] = so[m][0][q];
+          }
+        }
+      } else {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int64_t o = (grow0 + 8 * h) * p.sld + (int64_t)ks * NG;
+#pragma unroll
+          for (int q = 0; q < NG; ++q) {
+            so[0][h][q] = rok[h] ? __ldg(p.aff_s + o + q) : 0u;
+            bo[h][q] = rok[h] ? __ldg(p.aff_b + o + q) : 0u;
+          }
+        }
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int slotx = n * 8 + cs[j];
+            const bool ok = slotx < c.ntok;
+            const float *xp = p.xsum + (int64_t)(c.xrow + slotx) * (p.K / 64) + (int64_t)ks * NG;
+#pragma unroll
+            for (int q = 0; q < NG; ++q) xo[n][j][q] = ok ? __ldg(xp + q) : 0.0f;
+          }
+      }
+    };
+    if (kb < ke) load_scales(kb, sraw, braw, xsn);
+
+    for (int ks = kb; ks < ke; ++ks, ++it) {
+      const int slot = it % QG_STAGES;
+      const uint32_t ph = (it / QG_STAGES) & 1;
+      float sc[NMAT][2][NG];
+      float bi[2][NG];
+      float xs[NT][2][NG];
+#pragma unroll
+      for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int q = 0; q < NG; ++q)
+            sc[m][h][q] = AFF ? bf_bits2f(uint16_t(sraw[m][h][q])) : e8m0f(sraw[m][h][q]);
+      if constexpr (AFF) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int q = 0; q < NG; ++q) bi[h][q] = bf_bits2f(uint16_t(braw[h][q]));
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int q = 0; q < NG; ++q) xs[n][j][q] = xsn[n][j][q];
+      }
+      if (ks + 1 < ke) load_scales(ks + 1, sraw, braw, xsn);   // prefetch next stage
+
+      if (!mbar_wait(&full[slot], ph)) return;
+      const uint32_t st = smem_u32(smem + slot * C::STAGE_BYTES);
+      const uint32_t xst = st + NMAT * C::W_BYTES;
+
+#pragma unroll
+      for (int grp = 0; grp < NG; ++grp) {
+        constexpr int STEPS = Fmt<WF>::GK / 16;
+        uint32_t a[NMAT][STEPS][4];
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m) {
+          const uint32_t wb = st + m * C::W_BYTES;
+          const uint32_t r0 = wb + rowA * 128, r1 = wb + (rowA + 8) * 128;
+          if constexpr (WF == WF_FP4) {
+            const uint32_t off = (uint32_t(grp ^ ra) << 4) + 4 * t;
+            const uint32_t w0 = lds32(r0 + off), w1 = lds32(r1 + off);
+            uint32_t h0[4], h1[4];
+            e2m1x8_to_f16x8(w0, h0[0], h0[1], h0[2], h0[3]);
+            e2m1x8_to_f16x8(w1, h1[0], h1[1], h1[2], h1[3]);
+#pragma unroll
+            for (int s2 = 0; s2 < 2; ++s2) {
+              a[m][s2][0] = h0[2 * s2];
+              a[m][s2][1] = h1[2 * s2];
+              a[m][s2][2] = h0[2 * s2 + 1];
+              a[m][s2][3] = h1[2 * s2 + 1];
+            }
+          } else if constexpr (WF == WF_FP8B) {
+            const uint32_t off = (uint32_t((2 * grp + (t >> 1)) ^ ra) << 4) + 8 * (t & 1);
+            const uint2 w0 = lds64(r0 + off), w1 = lds64(r1 + off);
+            uint32_t h0[4], h1[4];
+            e4m3x4_to_f16x4(w0.x, h0[0], h0[1]);
+            e4m3x4_to_f16x4(w0.y, h0[2], h0[3]);
+            e4m3x4_to_f16x4(w1.x, h1[0], h1[1]);
+            e4m3x4_to_f16x4(w1.y, h1[2], h1[3]);
+#pragma unroll
+            for (int s2 = 0; s2 < 2; ++s2) {
+              a[m][s2][0] = h0[2 * s2];
+              a[m][s2][1] = h1[2 * s2];
+              a[m][s2][2] = h0[2 * s2 + 1];
+              a[m][s2][3] = h1[2 * s2 + 1];
+            }
+          } else if constexpr (WF == WF_AFF4) {
+            const uint32_t off = (uint32_t((2 * grp + (t >> 1)) ^ ra) << 4) + 8 * (t & 1);
+            const uint2 w0 = lds64(r0 + off), w1 = lds64(r1 + off);
+            const uint32_t wr0[2] = {w0.x, w0.y}, wr1[2] = {w1.x, w1.y};
+#pragma unroll
+            for (int s2 = 0; s2 < 4; ++s2) {
+              const uint32_t u0 = wr0[s2 >> 1] >> (8 * (s2 & 1));
+              const uint32_t u1 = wr1[s2 >> 1] >> (8 * (s2 & 1));
+              a[m][s2][0] = aff_pair(u0 & 0x000F000Fu);
+              a[m][s2][1] = aff_pair(u1 & 0x000F000Fu);
+              a[m][s2][2] = aff_pair((u0 >> 4) & 0x000F000Fu);
+              a[m][s2][3] = aff_pair((u1 >> 4) & 0x000F000Fu);
+            }
+          } else {  // WF_AFF8
+            const uint32_t off = (uint32_t((4 * grp + t) ^ ra) << 4);
+            const uint4 w0 = lds128(r0 + off), w1 = lds128(r1 + off);
+            const uint32_t wr0[4] = {w0.x, w0.y, w0.z, w0.w}, wr1[4] = {w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+            for (int s2 = 0; s2 < 4; ++s2) {
+              a[m][s2][0] = aff_pair(wr0[s2] & 0x00FF00FFu);
+              a[m][s2][1] = aff_pair(wr1[s2] & 0x00FF00FFu);
+              a[m][s2][2] = aff_pair((wr0[s2] >> 8) & 0x00FF00FFu);
+              a[m][s2][3] = aff_pair((wr1[s2] >> 8) & 0x00FF00FFu);
+            }
+          }
+        }
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+          if (n >= ntiles_x) break;
+          const int xr = n * 8 + xb;                 // x smem row
+          uint32_t b[STEPS][2];
+          if constexpr (Fmt<WF>::GK == 32) {
+            const uint32_t box = xst + (grp >> 1) * C::XBOX_BYTES;
+            const uint32_t off = (uint32_t(((grp & 1) * 4 + t) ^ (xr & 7)) << 4);
+            const uint4 v = lds128(box + xr * 128 + off);
+            b[0][0] = v.x; b[0][1] = v.y; b[1][0] = v.z; b[1][1] = v.w;
+          } else {
+            const uint32_t box = xst + grp * C::XBOX_BYTES;
+            const uint4 v0 = lds128(box + xr * 128 + (uint32_t((2 * t) ^ (xr & 7)) << 4));
+            const uint4 v1 = lds128(box + xr * 128 + (uint32_t((2 * t + 1) ^ (xr & 7)) << 4));
+            b[0][0] = v0.x; b[0][1] = v0.y; b[1][0] = v0.z; b[1][1] = v0.w;
+            b[2][0] = v1.x; b[2][1] = v1.y; b[3][0] = v1.z; b[3][1] = v1.w;
+          }
+#pragma unroll
+          for (int m = 0; m < NMAT; ++m) {
+            float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int s2 = 0; s2 < STEPS; ++s2)
+              mma_f16(d, a[m][s2][0], a[m][s2][1], a[m][s2][2], a[m][s2][3], b[s2][0], b[s2][1]);
+            // fold the group scale (and the affine bias times the group's x sum)
+            acc[m][n][0] = __fmaf_rn(d[0], sc[m][0][grp], acc[m][n][0]);
+            acc[m][n][1] = __fmaf_rn(d[1], sc[m][0][grp], acc[m][n][1]);
+            acc[m][n][2] = __fmaf_rn(d[2], sc[m][1][grp], acc[m][n][2]);
+            acc[m][n][3] = __fmaf_rn(d[3], sc[m][1][grp], acc[m][n][3]);
+            if constexpr (AFF) {
+              acc[m][n][0] = __fmaf_rn(bi[0][grp], xs[n][0][grp], acc[m][n][0]);
+              acc[m][n][1] = __fmaf_rn(bi[0][grp], xs[n][1][grp], acc[m][n][1]);
+              acc[m][n][2] = __fmaf_rn(bi[1][grp], xs[n][0][grp], acc[m][n][2]);
+              acc[m][n][3] = __fmaf_rn(bi[1][grp], xs[n][1][grp], acc[m][n][3]);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+
+    // ---------------------------------------------------------------- split-K fixup
+    if (p.nsplit > 1) {
+      const int tile_id = chunk * p.tiles + tile;
+      const int ctid = threadIdx.x;                        // 0 .. 32*QG_CW-1
+      constexpr int CT = 32 * QG_CW;
+      float *mine = p.partial + ((int64_t)tile_id * p.nsplit + split) * (CT * C::FRAG);
+#pragma unroll
+      for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) __stcg(mine + ((m * NT + n) * 4 + i) * CT + ctid, acc[m][n][i]);
+      __threadfence();
+      asm volatile("bar.sync 1, %0;" ::"n"(CT) : "memory");
+      __shared__ int s_last;
+      if (ctid == 0) {
+        const int prev = atomicAdd(&p.counters[tile_id], 1);
+        s_last = (prev == p.nsplit - 1);
+        if (s_last) p.counters[tile_id] = 0;               // ready for the next call
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(CT) : "memory");
+      const int last = s_last;
+      asm volatile("bar.sync 1, %0;" ::"n"(CT) : "memory");  // s_last reused next item
+      if (!last) continue;
+      __threadfence();
+#pragma unroll
+      for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            float v = 0.0f;
+            for (int sp = 0; sp < p.nsplit; ++sp)
+              v += __ldcg(p.partial + ((int64_t)tile_id * p.nsplit + sp) * (CT * C::FRAG) +
+                          ((m * NT + n) * 4 + i) * CT + ctid);
+            acc[m][n][i] = v;
+          }
+    }
+
+    // ---------------------------------------------------------------- epilogue
+    // acc[m][n][2h + j] is (tile row rowA + 8h, x slot n*8 + cs[j]).
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      if (n >= ntiles_x) break;
+      if (p.epi == EPI_DOWN) {
+        // H rows of pair q: hi at 8*(q/4) + q%4, lo 4 rows later, so slots t and
+        // 4+t of tile n (columns 2t, 2t+1 under rhoB) are the two halves of pair
+        // c.orow + 4n + t.
+        const int q = c.orow + n * 4 + t;
+        const int orow = p.pair_row ? p.pair_row[q] : (q < p.npairs ? q : -1);
+        if (orow < 0) continue;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int64_t nn = nbase + rowA + 8 * h;
+          if (nn >= p.N) continue;
+          float v = acc[0][n][2 * h] + acc[0][n][2 * h + 1];
+          if (p.round_out) v = round_bf16f(v);
+          reinterpret_cast<float *>(p.out)[(int64_t)orow * p.ldo + nn] = v;
+        }
+        continue;
+      }
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int slotx = n * 8 + cs[j];
+        if (slotx >= c.ntok) continue;
+        const float xsc = p.xscale ? p.xscale[c.xrow + slotx] : 1.0f;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int64_t nn = nbase + rowA + 8 * h;
+          if (nn >= p.N) continue;
+          const int i = 2 * h + j;
+          if (p.epi == EPI_SWIGLU) {
+            float gv = acc[0][n][i] * xsc, uv = acc[NMAT - 1][n][i] * xsc;
+            if (p.round_gu) {
+              gv = round_bf16f(gv);
+              uv = round_bf16f(uv);
+            }
+            if (p.limit > 0.0f) {
+              uv = fminf(fmaxf(uv, -p.limit), p.limit);
+              gv = fminf(gv, p.limit);
+            }
+            float hv = __fdiv_rn(gv, 1.0f + expf(-gv)) * uv;
+            if (p.round_h) hv = round_bf16f(hv);
+            const __half hi = __float2half_rn(hv);
+            const __half lo = __float2half_rn(hv - __half2float(hi));
+            const int q = c.xrow + slotx;                 // pair (or token) index
+            __half *H = reinterpret_cast<__half *>(p.out);
+            const int64_t hr = 8 * (q >> 2) + (q & 3);
+            H[hr * p.ldo + nn] = hi;
+            H[(hr + 4) * p.ldo + nn] = lo;
+          } else {
+            const float v = acc[0][n][i] * xsc;
+            const int64_t o = (int64_t)(c.orow + slotx) * p.ldo + nn;
+            if (p.epi == EPI_STORE_F32)
+              reinterpret_cast<float *>(p.out)[o] = v;
+            else
+              reinterpret_cast<__nv_bfloat16 *>(p.out)[o] = __float2bfloat16_rn(v);
+          }
+        }
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ activation prep
+// x bf16 [M, K] -> f16 [M, K] scaled by 2^-E per row (E = floor(log2 amax) - 14,
+// so |x| * 2^-E < 2^15), the multiplier 2^E per row, and (affine) per-64 sums
+// of the scaled values.  bf16 values are exact in f16 within 2^29 of the row max;
+// smaller ones keep an absolute error below 2^-39 of the max.  perm selects the
+// per-16 k order the affine decode expects (0 none, 4 aff4, 8 aff8).
+// One CTA (256 threads) per row; optional gather: row r reads x[gather[r]].
+__global__ void k_qx_prep(const __nv_bfloat16 *__restrict__ x, int64_t M, int64_t K,
+                          const int32_t *__restrict__ gather, const int *__restrict__ nrows_dev,
+                          __half *__restrict__ xq, float *__restrict__ xscale,
+                          float *__restrict__ xsum, int perm) {
+  const int64_t r = blockIdx.x;
+  const int64_t nrows = nrows_dev ? *nrows_dev : M;
+  if (r >= nrows) return;
+  int64_t src = gather ? gather[r] : r;
+  __shared__ float red[8];
+  __shared__ float s_scale;
+  float amax = 0.0f;
+  if (src >= 0) {
+    const __nv_bfloat16 *xr = x + src * K;
+    for (int64_t k = threadIdx.x; k < K; k += blockDim.x) amax = fmaxf(amax, fabsf(__bfloat162float(xr[k])));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float m = 0.0f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) m = fmaxf(m, red[i]);
+    int E = 0;
+    if (m > 0.0f && m < INFINITY) E = int((__float_as_uint(m) >> 23) & 0xFF) - 127 - 14;
+    if (E < -126) E = -126;
+    s_scale = ldexpf(1.0f, E);
+    xscale[r] = s_scale;
+  }
+  __syncthreads();
+  const float inv = 1.0f / s_scale;  // exact power of two
+  for (int64_t k = threadIdx.x; k < K; k += blockDim.x) {
+    const float v = src >= 0 ? __bfloat162float(x[src * K + k]) : 0.0f;
+    int64_t dk = k;
+    if (perm == 4) {  // aff4 order per 16: [0,4,1,5,2,6,3,7, 8,12,9,13,10,14,11,15]
+      const int64_t b16 = k & ~int64_t(15), w = k & 15, half8 = w & 8, i = w & 7;
+      dk = b16 + half8 + ((i & 3) << 1) + (i >> 2);
+    } else if (perm == 8) {  // aff8 order per 4: [0,2,1,3]
+      const int64_t b4 = k & ~int64_t(3), i = k & 3;
+      dk = b4 + ((i & 1) << 1) + (i >> 1);
+    }
+    xq[r * K + dk] = __float2half_rn(v * inv);
+  }
+  if (xsum) {
+    // per-64 sums of the scaled f16 values, in fp32 (one warp per group)
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    for (int64_t gi = wid; gi < K / 64; gi += (blockDim.x >> 5)) {
+      float s = 0.0f;
+      for (int j = lane; j < 64; j += 32) {
+        const float v = src >= 0 ? __bfloat162float(x[src * K + gi * 64 + j]) : 0.0f;
+        s += __half2float(__float2half_rn(v * inv));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      if (lane == 0) xsum[r * (K / 64) + gi] = s;
+    }
+  }
+}
+
+}  // namespace dsv41

@@ -1,0 +1,174 @@
+"""Engram hashing and fp8 row lookup on the GPU -- drop-in for deepseek_v41_mlx/engram.py.
+
+* ``build_layout`` / ``compute_hash_multipliers`` / ``find_next_prime`` are the
+  reference's host-side setup (engram.py:35-87), restated here in numpy (they
+  run once per model, not per token).
+* ``EngramHasher(args, token_map)(input_ids, start_pos, ids_cache)`` runs on the
+  GPU (engram.py:154-180).  ``ids_cache`` is updated in place as the reference
+  does; a numpy cache is accepted and written back.
+* ``EngramEmbedding(num, dim, block)(indices)`` gathers e4m3 rows and their ue8m0
+  scales and returns fp32 rows (engram.py:197-203).  ``row_lo`` makes it the
+  row-sharded ParallelEngramEmbedding (docs/reference/model.py:296-325): ids
+  outside [row_lo, row_lo + rows) give zero rows.
+* ``QuantizedEngramEmbedding`` is the MLX affine table (engram.py:206-223).
+* ``gather_sum`` is the summed form used by the benchmark configuration.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from . import _lib as L
+
+
+def _isprime(n: int) -> bool:
+    if n < 2:
+        return False
+    if n % 2 == 0:
+        return n == 2
+    i = 3
+    while i * i <= n:
+        if n % i == 0:
+            return False
+        i += 2
+    return True
+
+
+def find_next_prime(start: int, seen: set) -> int:
+    c = start + 1
+    while not _isprime(c) or c in seen:
+        c += 1
+    return c
+
+
+def build_layout(args):
+    """engram.py:55-75 -> (primes int64 [nL, G-1, H], offsets int64 [nL, (G-1)*H])."""
+    primes, seen = [], set()
+    for _ in args.engram_layer_ids:
+        per = []
+        for _ in range(args.engram_max_ngram_size - 1):
+            sizes, cur = [], args.engram_vocab_size - 1
+            for _ in range(args.engram_n_heads):
+                cur = find_next_prime(cur, seen)
+                seen.add(cur)
+                sizes.append(cur)
+            per.append(sizes)
+        primes.append(per)
+    flat = [[p for g in layer for p in g] for layer in primes]
+    offsets = [np.cumsum([0, *f[:-1]]) for f in flat]
+    return np.asarray(primes, dtype=np.int64), np.asarray(offsets, dtype=np.int64)
+
+
+def compute_hash_multipliers(layer_ids, max_ngram_size: int, compressed_vocab_size: int):
+    """engram.py:78-87 -- one odd multiplier per (layer, lookback)."""
+    max_long = np.iinfo(np.int64).max
+    bound = max(1, (max_long // compressed_vocab_size) // 2)
+    rows = []
+    for lid in layer_ids:
+        g = np.random.default_rng(10007 * lid)
+        rows.append(g.integers(low=0, high=bound, size=(max_ngram_size,), dtype=np.int64) * 2 + 1)
+    return np.stack(rows)
+
+
+class EngramHasher:
+    """engram.py:127-180 on the GPU."""
+
+    def __init__(self, args, token_map, device=None):
+        t = L.torch()
+        self.args = args
+        self.max_ngram = args.engram_max_ngram_size
+        tm = np.asarray(token_map, dtype=np.int64)
+        n_compressed = int(tm.max()) + 1
+        if args.engram_compressed_vocab_size and n_compressed != args.engram_compressed_vocab_size:
+            raise ValueError(
+                f"compressed vocab {n_compressed} != config {args.engram_compressed_vocab_size}; "
+                f"every hash multiplier is derived from it, so a mismatch silently rehashes the table")
+        self.pad_id = int(tm[args.engram_pad_id])
+        self.primes, self.offsets = build_layout(args)
+        self.multipliers = compute_hash_multipliers(args.engram_layer_ids, self.max_ngram,
+                                                    n_compressed)
+        sums = self.primes.reshape(len(args.engram_layer_ids), -1).sum(-1)
+        if tuple(int(s) for s in sums) != tuple(args.engram_num_embeddings):
+            raise ValueError(f"prime sums {sums} != engram_num_embeddings "
+                             f"{args.engram_num_embeddings}")
+        dev = device or t.device("cuda", t.cuda.current_device())
+        self._dev = {k: t.from_numpy(np.ascontiguousarray(v)).to(dev) for k, v in (
+            ("token_map", tm), ("mult", self.multipliers), ("primes", self.primes),
+            ("offsets", self.offsets))}
+        self.vocab = len(tm)
+
+    def __call__(self, input_ids, start_pos: int, ids_cache):
+        t = L.torch()
+        dev = self._dev["token_map"].device
+        host_cache = isinstance(ids_cache, np.ndarray)
+        cache = t.from_numpy(ids_cache).to(dev) if host_cache else L.cuda_tensor(ids_cache)
+        if cache.dtype != t.int64:
+            raise ValueError("ids_cache must be int64")
+        ids = input_ids if isinstance(input_ids, t.Tensor) else t.as_tensor(np.asarray(input_ids))
+        ids = ids.to(dev, dtype=t.int64).contiguous()
+        B, Lq = ids.shape
+        nL = len(self.args.engram_layer_ids)
+        G, H = self.max_ngram, self.args.engram_n_heads
+        out = t.empty((B, Lq, nL, (G - 1) * H), dtype=t.int64, device=dev)
+        L.call("dsv41_engram_hash", L.ptr(ids), B, Lq, int(start_pos), L.ptr(self._dev["token_map"]),
+               self.vocab, L.ptr(cache), cache.shape[1], L.ptr(self._dev["mult"]),
+               L.ptr(self._dev["primes"]), L.ptr(self._dev["offsets"]), nL, G, H, self.pad_id,
+               L.ptr(out), L.stream_of(out))
+        if host_cache:
+            ids_cache[...] = cache.cpu().numpy()
+        elif cache.data_ptr() != L.as_tensor(ids_cache).data_ptr():
+            ids_cache.copy_(cache)
+        return out
+
+
+class EngramEmbedding:
+    """engram.py:183-203: e4m3 table [rows, d] + ue8m0 [rows, d/block] -> fp32 rows."""
+
+    def __init__(self, num_embeddings: int, dim: int, block: int = 32, row_lo: int = 0):
+        self.num_embeddings, self.dim, self.block, self.row_lo = num_embeddings, dim, block, row_lo
+        self.weight = None
+        self.scale = None
+
+    def __call__(self, indices, out_dtype=None):
+        t = L.torch()
+        w = L.u8(L.cuda_tensor(self.weight, "weight"))
+        s = L.u8(L.cuda_tensor(self.scale, "scale"))
+        idx = L.cuda_tensor(indices, "indices").to(t.int64)
+        odt = out_dtype or t.float32
+        out = t.empty(tuple(idx.shape) + (self.dim,), dtype=odt, device=idx.device)
+        L.call("dsv41_engram_gather_rows", L.ptr(w), L.ptr(s), w.shape[0], self.row_lo, self.dim,
+               self.block, L.ptr(idx), idx.numel(), L.dtype_code(odt), L.ptr(out),
+               L.stream_of(idx))
+        return out
+
+    def gather_sum(self, indices, out_dtype=None):
+        """indices [..., n] -> [..., d]: fp32 sum of each token's n rows in column order."""
+        t = L.torch()
+        w = L.u8(L.cuda_tensor(self.weight, "weight"))
+        s = L.u8(L.cuda_tensor(self.scale, "scale"))
+        idx = L.cuda_tensor(indices, "indices").to(t.int64)
+        n = idx.shape[-1]
+        n_tok = idx.numel() // n
+        odt = out_dtype or t.bfloat16
+        out = t.empty(tuple(idx.shape[:-1]) + (self.dim,), dtype=odt, device=idx.device)
+        L.call("dsv41_engram_gather_sum", L.ptr(w), L.ptr(s), w.shape[0], self.row_lo, self.dim,
+               self.block, L.ptr(idx), n_tok, n, L.dtype_code(odt), L.ptr(out), L.stream_of(idx))
+        return out
+
+
+class QuantizedEngramEmbedding:
+    """engram.py:206-223: MLX affine table, rows dequantized on lookup (fp32 out)."""
+
+    def __init__(self, num_embeddings: int, dim: int, group_size: int = 64, bits: int = 4):
+        self.group_size, self.bits, self.dim = group_size, bits, dim
+        self.weight = self.scales = self.biases = None
+
+    def __call__(self, indices):
+        from .dequant import dequantize_affine
+        t = L.torch()
+        idx = L.cuda_tensor(indices, "indices").to(t.int64).reshape(-1)
+        w = L.cuda_tensor(self.weight).index_select(0, idx)
+        s = L.cuda_tensor(self.scales).index_select(0, idx)
+        b = L.cuda_tensor(self.biases).index_select(0, idx)
+        out = dequantize_affine(w, s, b, self.group_size, self.bits, t.float32)
+        return out.reshape(tuple(indices.shape) + (self.dim,))

@@ -1,0 +1,212 @@
+"""MoE on the GPU -- drop-in for deepseek_v41_mlx/moe.py.
+
+Same classes and attributes as the reference (moe.py:30-112):
+
+* ``ClampedSwiGLU(limit)(x, gate)``          -- silu(min(gate, L)) * clip(x, -L, L), fp32
+* ``Gate(args)(x) -> (weights, indices)``    -- sqrt-softplus router, biased top-k
+* ``SharedExpert(dim, inter, limit)(x)``     -- fp8 32x32 weights (release format)
+* ``MoE(args)(x)``                           -- routed fp4 experts + shared expert;
+  ``MoE.gate`` and ``MoE.experts(xf, indices) -> [T, k, dim]`` stay separately
+  callable (scripts/reap_calibrate.py:47-65 patches ``MoE.__call__`` around them).
+
+Weights are the native release tensors, not converted ones: routed experts
+``experts.{gate,up,down}_proj.weight`` uint8 [E, out, in/2] (e2m1 pairs) with
+``.scales`` uint8 [E, out, in/32] (ue8m0); shared expert ``w1/w2/w3.weight``
+e4m3 [out, in] with ``.scale`` ue8m0 [ceil(out/32), ceil(in/32)]; the router
+``gate.weight`` bf16 [E, dim], ``gate.bias`` f32 [E].
+
+Numerics follow the port (``round_bf16=True``: gate/up outputs and the shared
+expert's intermediates rounded to bf16 as MLX produces them) or keep every
+intermediate in fp32 (``round_bf16=False``).
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+
+from . import _lib as L
+
+
+def _torch():
+    return L.torch()
+
+
+class ClampedSwiGLU:
+    """moe.py:30-43 -- called as activation(x_up, x_gate)."""
+
+    def __init__(self, limit: float = 0.0):
+        self.limit = limit
+
+    def __call__(self, x, gate):
+        t = _torch()
+        x = L.cuda_tensor(x, "x").float()
+        gate = L.cuda_tensor(gate, "gate").float()
+        if self.limit > 0:
+            x = t.clamp(x, -self.limit, self.limit)
+            gate = t.clamp(gate, max=self.limit)
+        return t.nn.functional.silu(gate) * x
+
+
+class Gate:
+    """moe.py:46-74."""
+
+    def __init__(self, args):
+        t = _torch()
+        self.topk = args.n_activated_experts
+        self.score_func = args.score_func
+        self.gate_temp = args.gate_temp
+        self.norm_topk_prob = args.norm_topk_prob
+        self.route_scale = args.route_scale
+        self.weight = t.zeros((args.n_routed_experts, args.dim), dtype=t.bfloat16)
+        self.bias = t.zeros((args.n_routed_experts,), dtype=t.float32)
+        self.bias_vl = t.zeros((args.n_routed_experts,), dtype=t.float32)
+
+    def __call__(self, x):
+        t = _torch()
+        xt = L.cuda_tensor(x, "x")
+        if xt.dtype != t.bfloat16:
+            xt = xt.to(t.bfloat16)
+        w = L.cuda_tensor(self.weight, "gate.weight").to(t.bfloat16)
+        b = L.cuda_tensor(self.bias, "gate.bias").float()
+        D = xt.shape[-1]
+        xf = xt.reshape(-1, D)
+        T, E = xf.shape[0], w.shape[0]
+        weights = t.empty((T, self.topk), dtype=t.float32, device=xf.device)
+        indices = t.empty((T, self.topk), dtype=t.int32, device=xf.device)
+        ws = L.workspace(L.load().dsv41_moe_route_workspace_size(T, D, E), xf.device)
+        L.call("dsv41_moe_route", L.ptr(xf), T, D, L.ptr(w), L.ptr(b), E, self.topk,
+               L.SCORE_FUNCS[self.score_func], float(self.gate_temp), int(self.norm_topk_prob),
+               float(self.route_scale), L.ptr(weights), L.ptr(indices), L.ptr(ws), ws.numel(),
+               L.stream_of(xf))
+        shp = tuple(xt.shape[:-1]) + (self.topk,)
+        return weights.reshape(shp), indices.reshape(shp)
+
+
+class _Proj:
+    """One stacked projection (weight + scales)."""
+
+    def __init__(self, weight=None, scales=None):
+        self.weight = weight
+        self.scales = scales
+
+
+class SwitchGLU:
+    """Stacked fp4 experts (the role of mlx_lm SwitchGLU at moe.py:101-102)."""
+
+    def __init__(self, dim, inter, n_experts, limit):
+        self.dim, self.inter, self.n_experts = dim, inter, n_experts
+        self.activation = ClampedSwiGLU(limit)
+        self.gate_proj, self.up_proj, self.down_proj = _Proj(), _Proj(), _Proj()
+        self._owner = None
+
+    def __call__(self, x, indices):
+        """x [T, dim] bf16, indices [T, k] -> unweighted expert outputs [T, k, dim] fp32."""
+        return self._owner._experts(x, indices)
+
+
+class SharedExpert:
+    """moe.py:77-93 with fp8 32x32 weights (w1 gate, w3 up, w2 down)."""
+
+    def __init__(self, dim, inter_dim, limit=0.0):
+        self.dim, self.inter, self.limit = dim, inter_dim, limit
+        self.w1, self.w2, self.w3 = _Proj(), _Proj(), _Proj()
+
+    def __call__(self, x):
+        from .linear import linear_fp8
+        t = _torch()
+        xt = L.cuda_tensor(x, "x")
+        dtype = xt.dtype
+        g = linear_fp8(xt, self.w1.weight, self.w1.scales, out_dtype=dtype).float()
+        u = linear_fp8(xt, self.w3.weight, self.w3.scales, out_dtype=dtype).float()
+        if self.limit > 0:
+            u = t.clamp(u, -self.limit, self.limit)
+            g = t.clamp(g, max=self.limit)
+        h = t.nn.functional.silu(g) * u
+        return linear_fp8(h.to(dtype), self.w2.weight, self.w2.scales, out_dtype=dtype)
+
+
+class MoE:
+    """moe.py:96-112 (decode path: up to 4096 tokens per call)."""
+
+    def __init__(self, args, round_bf16: bool = True):
+        self.args = args
+        self.dim = args.dim
+        self.gate = Gate(args)
+        self.experts = SwitchGLU(args.dim, args.moe_inter_dim, args.n_routed_experts,
+                                 args.swiglu_limit)
+        self.experts._owner = self
+        self.shared_experts = SharedExpert(args.dim, args.moe_inter_dim, args.swiglu_limit)
+        self.round_bf16 = round_bf16
+        self._ws = None
+
+    # -- plumbing --------------------------------------------------------------
+    def _cfg(self, flags=0):
+        a = self.args
+        return L.MoeConfig(dim=a.dim, inter=a.moe_inter_dim, n_experts=a.n_routed_experts,
+                           topk=a.n_activated_experts, score_func=L.SCORE_FUNCS[a.score_func],
+                           gate_temp=float(a.gate_temp), norm_topk_prob=int(a.norm_topk_prob),
+                           route_scale=float(a.route_scale), swiglu_limit=float(a.swiglu_limit),
+                           flags=(L.MOE_ROUND_BF16 if self.round_bf16 else 0) | flags)
+
+    def _weights(self):
+        t = _torch()
+        self._keep = []
+
+        def p(a, conv=None):
+            if a is None:
+                return None
+            v = L.cuda_tensor(a)
+            if conv is not None:
+                v = conv(v)
+            self._keep.append(v)
+            return L.ptr(v)
+
+        e, s = self.experts, self.shared_experts
+        return L.MoeWeights(
+            gate_w=p(self.gate.weight, lambda v: v.to(t.bfloat16)),
+            gate_bias=p(self.gate.bias, lambda v: v.float()),
+            w1=p(e.gate_proj.weight, L.u8), s1=p(e.gate_proj.scales, L.u8),
+            w3=p(e.up_proj.weight, L.u8), s3=p(e.up_proj.scales, L.u8),
+            w2=p(e.down_proj.weight, L.u8), s2=p(e.down_proj.scales, L.u8),
+            sw1=p(s.w1.weight, L.u8), ss1=p(s.w1.scales, L.u8),
+            sw3=p(s.w3.weight, L.u8), ss3=p(s.w3.scales, L.u8),
+            sw2=p(s.w2.weight, L.u8), ss2=p(s.w2.scales, L.u8))
+
+    def _workspace(self, cfg, T, device):
+        need = L.load().dsv41_moe_decode_workspace_size(C.byref(cfg), T)
+        if self._ws is None or self._ws.numel() < need or self._ws.device != device:
+            self._ws = L.workspace(need, device)
+        return self._ws
+
+    def _experts(self, x, indices):
+        t = _torch()
+        xt = L.cuda_tensor(x, "x").to(t.bfloat16)
+        xf = xt.reshape(-1, self.dim)
+        idx = L.cuda_tensor(indices, "indices").to(t.int32).reshape(xf.shape[0], -1)
+        T, k = idx.shape
+        cfg = self._cfg(L.MOE_NO_SHARED)
+        W = self._weights()
+        y = t.empty((T, k, self.dim), dtype=t.float32, device=xf.device)
+        ws = self._workspace(cfg, T, xf.device)
+        L.call("dsv41_moe_experts", C.byref(cfg), C.byref(W), L.ptr(xf), T, L.ptr(idx), L.ptr(y),
+               L.ptr(ws), ws.numel(), L.stream_of(xf))
+        return y
+
+    def __call__(self, x, with_routing: bool = False, out_dtype=None):
+        t = _torch()
+        xt = L.cuda_tensor(x, "x")
+        shape = xt.shape
+        xf = xt.to(t.bfloat16).reshape(-1, self.dim)
+        T = xf.shape[0]
+        cfg = self._cfg()
+        W = self._weights()
+        odt = out_dtype or (t.float32 if xt.dtype == t.float32 else t.bfloat16)
+        y = t.empty((T, self.dim), dtype=odt, device=xf.device)
+        k = self.args.n_activated_experts
+        weights = t.empty((T, k), dtype=t.float32, device=xf.device)
+        indices = t.empty((T, k), dtype=t.int32, device=xf.device)
+        ws = self._workspace(cfg, T, xf.device)
+        L.call("dsv41_moe_decode", C.byref(cfg), C.byref(W), L.ptr(xf), T, L.dtype_code(odt),
+               L.ptr(y), L.ptr(weights), L.ptr(indices), L.ptr(ws), ws.numel(), L.stream_of(xf))
+        y = y.reshape(shape)
+        return (y, weights, indices) if with_routing else y

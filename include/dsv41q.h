@@ -1,0 +1,224 @@
+/*
+ * dsv41q.h -- C ABI of the B200 (sm_100a) quantized-weight hot path of the
+ * DeepSeek-V4.1-Flash runtime (thedracle/deepseek-v41-mlx).
+ *
+ * Conventions
+ *   - Every entry point returns 0 (DSV41_OK) or one of the DSV41_ERR_* codes
+ *     below; dsv41_get_last_error() gives a one-line reason (thread-local).
+ *   - Pointers are raw DEVICE pointers unless the name says host; sizes are
+ *     element counts (int64).  The caller owns all memory.  Outputs are
+ *     written, inputs are never modified, except the engram id cache, which
+ *     dsv41_engram_hash updates in place exactly as the reference does.
+ *   - Work is enqueued on `stream` (a cudaStream_t passed as void*; NULL means
+ *     the legacy default stream) and is asynchronous with respect to the host.
+ *     Calls on distinct streams may run concurrently if their workspaces do
+ *     not alias.
+ *   - Entry points that need scratch memory take (workspace, workspace_bytes)
+ *     and have a *_workspace_size() query.  The library never calls cudaMalloc
+ *     on a compute path.
+ *   - Shapes, dtypes and alignment are validated on the host; no device
+ *     assert exists in these kernels.  Device-side waits are bounded; a wait
+ *     that runs out sets a device flag read by dsv41_device_status().
+ *
+ * Citations name the reference interface each entry point replaces, as
+ * path:line inside the reference repository.
+ */
+#ifndef DSV41Q_H
+#define DSV41Q_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define DSV41_OK 0
+#define DSV41_ERR_BAD_SHAPE 1
+#define DSV41_ERR_BAD_DTYPE 2
+#define DSV41_ERR_MISALIGNED 3
+#define DSV41_ERR_CUDA 4
+#define DSV41_ERR_NCCL 5
+#define DSV41_ERR_TIMEOUT 6
+#define DSV41_ERR_BAD_ARG 7
+#define DSV41_ERR_UNSUPPORTED 8
+#define DSV41_ERR_WORKSPACE 9
+
+/* ---- dtype codes (outputs / bf16-or-f32 scale operands) ---------------- */
+#define DSV41_F32 0
+#define DSV41_BF16 1
+#define DSV41_F16 2
+#define DSV41_U8 3
+
+/* ---- router score functions (ModelArgs.score_func) ---------------------- */
+#define DSV41_SCORE_SQRTSOFTPLUS 0
+#define DSV41_SCORE_SIGMOID 1
+#define DSV41_SCORE_SOFTMAX 2
+
+/* ---- MoE numerics flags -------------------------------------------------- */
+/* Round the gate/up projection outputs and the shared-expert intermediates to
+ * bf16 where the MLX port's SwitchGLU / SharedExpert produce bf16 arrays
+ * (deepseek_v41_mlx/moe.py:37-43, :85-93).  Without it every intermediate is
+ * kept in fp32 ("exact" mode, used for the 1e-5 fp32 comparison). */
+#define DSV41_MOE_ROUND_BF16 1
+/* Skip the shared expert (output = routed experts only). */
+#define DSV41_MOE_NO_SHARED 2
+
+/* ---- library ------------------------------------------------------------ */
+const char *dsv41_get_last_error(void);
+int dsv41_abi_version(void);
+/* Reads and clears the device-side status flags of the current device
+ * (bit 0: a bounded wait ran out).  Synchronises `stream`. */
+int dsv41_device_status(void *stream, uint32_t *flags_out);
+
+/* ---- a1..a7: release-format decode (bit-exact) --------------------------
+ * e8m0_to_float    replaces deepseek_v41_mlx/dequant.py:33-36
+ * dequant_fp8      replaces deepseek_v41_mlx/dequant.py:45-50 (+ _expand_blocks :39-42)
+ * unpack_fp4       replaces deepseek_v41_mlx/dequant.py:53-60
+ * dequant_fp4      replaces deepseek_v41_mlx/dequant.py:63-68
+ * dequant_fp8_rows replaces deepseek_v41_mlx/dequant.py:71-79                */
+int dsv41_e8m0_to_float(const uint8_t *scale, int64_t n, float *out, void *stream);
+/* w u8 [rows, cols] e4m3 + s u8 [ceil(rows/32), ceil(cols/32)] -> out [rows, cols] */
+int dsv41_dequant_fp8_block(const uint8_t *w, const uint8_t *s, int64_t rows, int64_t cols,
+                            int out_dtype, void *out, void *stream);
+/* packed u8 [rows, cols/2] -> f32 [rows, cols]; low nibble = even column */
+int dsv41_unpack_fp4(const uint8_t *packed, int64_t rows, int64_t cols, float *out,
+                     void *stream);
+/* packed u8 [rows, cols/2] + s u8 [rows, ceil(cols/32)] -> out [rows, cols] */
+int dsv41_dequant_fp4(const uint8_t *packed, const uint8_t *s, int64_t rows, int64_t cols,
+                      int out_dtype, void *out, void *stream);
+/* w u8 [rows, d] + s u8 [rows, d/block] -> f32 [rows, d] */
+int dsv41_dequant_fp8_rows(const uint8_t *w, const uint8_t *s, int64_t rows, int64_t d,
+                           int64_t block, float *out, void *stream);
+
+/* ---- a14/a17: MLX affine group quantization -----------------------------
+ * Replaces mx.dequantize as called at deepseek_v41_mlx/engram.py:219-223 and
+ * the weight layout written by deepseek_v41_mlx/convert.py:156-175.
+ * wq u32 [rows, cols*bits/32] (little-endian bit stream per row, element j at
+ * bits [bits*j, bits*j+bits)), scales/biases [rows, cols/group] of
+ * sb_dtype (BF16, F16 or F32); out = round(fma_f32(s, q, b)) to out_dtype. */
+int dsv41_dequant_affine(const uint32_t *wq, const void *scales, const void *biases,
+                         int sb_dtype, int64_t rows, int64_t cols, int bits, int group,
+                         int out_dtype, void *out, void *stream);
+
+/* ---- a12: upstream act_quant (docs/reference/kernel.py:40-124,
+ * mirrored by tests/kernel_stub.py:47-63).  x bf16 [M, K] (K % block == 0).
+ * round_scale=1: s = 2^ceil(log2(amax/448)) (ue8m0, "scale_fmt" set),
+ * round_scale=0: s = amax/448.  q u8 [M, K] e4m3 codes; s of s_dtype
+ * (F32, or U8 = ue8m0 byte, which needs round_scale=1) [M, K/block].
+ * If deq_out != NULL it also receives q*s as bf16 (the inplace=True form). */
+int dsv41_act_quant_fp8(const void *x, int64_t M, int64_t K, int block, int round_scale,
+                        uint8_t *q, void *s, int s_dtype, void *deq_out, void *stream);
+
+/* ---- a3+a13 / a5+a13 / a14: weight-decode fused into the product --------
+ * y[M, N] = x[M, K] . W^T with x bf16 and W in a release / MLX format.
+ * Replaces the dequant-then-matmul of deepseek_v41_mlx/convert.py:119-127 +
+ * nn.Linear, upstream linear() docs/reference/model.py:181-207 (a16 form:
+ * activations are NOT quantized) and mx.quantized_matmul behind
+ * nn.QuantizedLinear (deepseek_v41_mlx/load.py:124-131).
+ * Requires K % 32 == 0 (fp8/fp4) or K % group == 0 (affine); N arbitrary.
+ * out_dtype F32 or BF16. */
+size_t dsv41_gemv_workspace_size(int64_t M, int64_t N, int64_t K);
+int dsv41_gemv_fp8_block(const void *x, int64_t M, int64_t K, const uint8_t *w,
+                         const uint8_t *s, int64_t N, int out_dtype, void *y, void *workspace,
+                         size_t workspace_bytes, void *stream);
+int dsv41_gemv_fp4(const void *x, int64_t M, int64_t K, const uint8_t *w, const uint8_t *s,
+                   int64_t N, int out_dtype, void *y, void *workspace, size_t workspace_bytes,
+                   void *stream);
+/* affine: bits 4 or 8, group 64; scales/biases bf16 [N, K/64] */
+int dsv41_gemv_affine(const void *x, int64_t M, int64_t K, const uint32_t *wq,
+                      const void *scales, const void *biases, int bits, int64_t N,
+                      int out_dtype, void *y, void *workspace, size_t workspace_bytes,
+                      void *stream);
+
+/* ---- a8: router (deepseek_v41_mlx/moe.py:58-74; upstream
+ * docs/reference/model.py:809-827).  x bf16 [T, D], w bf16 [E, D], bias f32
+ * [E] (may be NULL) -> weights f32 [T, topk], indices int32 [T, topk], in
+ * descending biased-score order (ties: lower expert id first). */
+size_t dsv41_moe_route_workspace_size(int64_t T, int64_t D, int64_t E);
+int dsv41_moe_route(const void *x, int64_t T, int64_t D, const void *gate_w, const float *bias,
+                    int64_t E, int topk, int score_func, float gate_temp, int norm_topk_prob,
+                    float route_scale, float *weights, int32_t *indices, void *workspace,
+                    size_t workspace_bytes, void *stream);
+
+/* ---- a9..a11: MoE layer at decode (deepseek_v41_mlx/moe.py:105-112 with
+ * SwitchGLU :101-102, ClampedSwiGLU :30-43, SharedExpert :77-93).
+ * Routed experts fp4 e2m1 stacked per expert:
+ *   w1 (gate) u8 [E, I, D/2] + s u8 [E, I, D/32];  w3 (up) same;
+ *   w2 (down) u8 [E, D, I/2] + s u8 [E, D, I/32].
+ * Shared expert fp8 e4m3 with 32x32 ue8m0 blocks:
+ *   sw1, sw3 u8 [I, D] + s u8 [I/32, D/32];  sw2 u8 [D, I] + s u8 [D/32, I/32].
+ * Routing weights are applied after w2 and summed in fp32 in top-k order,
+ * then the shared expert is added and the sum rounded to out_dtype.
+ * 0 < swiglu_limit <= 255.  flags: DSV41_MOE_*.  weights_out/indices_out may
+ * be NULL. */
+typedef struct dsv41_moe_weights {
+  const void *gate_w;      /* bf16 [E, D] */
+  const float *gate_bias;  /* f32 [E] or NULL */
+  const uint8_t *w1, *s1;  /* fp4 experts */
+  const uint8_t *w3, *s3;
+  const uint8_t *w2, *s2;
+  const uint8_t *sw1, *ss1; /* fp8 shared expert */
+  const uint8_t *sw3, *ss3;
+  const uint8_t *sw2, *ss2;
+} dsv41_moe_weights;
+
+typedef struct dsv41_moe_config {
+  int64_t dim;        /* D */
+  int64_t inter;      /* I (moe_inter_dim) */
+  int64_t n_experts;  /* E */
+  int topk;
+  int score_func;
+  float gate_temp;
+  int norm_topk_prob;
+  float route_scale;
+  float swiglu_limit;
+  int flags;
+} dsv41_moe_config;
+
+size_t dsv41_moe_decode_workspace_size(const dsv41_moe_config *cfg, int64_t T);
+/* The routed experts alone for given routing (mlx_lm SwitchGLU as called at
+ * deepseek_v41_mlx/moe.py:109, i.e. MoE.experts(xf, indices)): indices int32
+ * [T, topk] -> y f32 [T, topk, D], unweighted.  Same workspace size query. */
+int dsv41_moe_experts(const dsv41_moe_config *cfg, const dsv41_moe_weights *w, const void *x,
+                      int64_t T, const int32_t *indices, float *y, void *workspace,
+                      size_t workspace_bytes, void *stream);
+int dsv41_moe_decode(const dsv41_moe_config *cfg, const dsv41_moe_weights *w, const void *x,
+                     int64_t T, int out_dtype, void *y, float *weights_out,
+                     int32_t *indices_out, void *workspace, size_t workspace_bytes,
+                     void *stream);
+
+/* ---- a15: engram hasher (deepseek_v41_mlx/engram.py:154-180; upstream
+ * docs/reference/engram.py NgramHashState.forward).  input_ids int64 [B, L];
+ * token_map int64 [V]; ids_cache int64 [B, max_seq], positions
+ * [start_pos, start_pos+L) are written in place; multipliers int64 [nL, G];
+ * primes int64 [nL, G-1, H]; offsets int64 [nL, (G-1)*H].
+ * out int64 [B, L, nL, (G-1)*H].  Input ids outside [0, V) are an error
+ * reported through dsv41_device_status bit 1 and hash to row 0. */
+int dsv41_engram_hash(const int64_t *input_ids, int64_t B, int64_t L, int64_t start_pos,
+                      const int64_t *token_map, int64_t vocab, int64_t *ids_cache,
+                      int64_t max_seq, const int64_t *multipliers, const int64_t *primes,
+                      const int64_t *offsets, int n_layers, int max_ngram, int n_heads,
+                      int64_t pad_id, int64_t *out, void *stream);
+
+/* ---- a16: engram row gather (deepseek_v41_mlx/engram.py:197-203; upstream
+ * ParallelEngramEmbedding.forward docs/reference/model.py:312-325).
+ * table u8 [rows, d] e4m3 + scale u8 [rows, d/block]; idx int64 [n_idx]
+ * (row ids; rows outside [row_lo, row_lo + rows) read as zero rows, which is
+ * the row-sharded form with row_lo = rank * rows_per_rank).
+ *   gather_rows: out f32/bf16 [n_idx, d]  (= EngramEmbedding output)
+ *   gather_sum : out f32/bf16 [n_tok, d], out[t] = fp32 sum over the
+ *                n_per_tok rows idx[t*n_per_tok + h] in h order. */
+int dsv41_engram_gather_rows(const uint8_t *table, const uint8_t *scale, int64_t rows,
+                             int64_t row_lo, int64_t d, int64_t block, const int64_t *idx,
+                             int64_t n_idx, int out_dtype, void *out, void *stream);
+int dsv41_engram_gather_sum(const uint8_t *table, const uint8_t *scale, int64_t rows,
+                            int64_t row_lo, int64_t d, int64_t block, const int64_t *idx,
+                            int64_t n_tok, int n_per_tok, int out_dtype, void *out,
+                            void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DSV41Q_H */

@@ -1,0 +1,129 @@
+"""Engram hash and row gather vs the reference goldens and the oracle: bit-exact."""
+
+from __future__ import annotations
+
+import types
+
+import numpy as np
+import pytest
+import torch
+
+import deepseek_v41_mlx_b200 as q
+from conftest import bits_equal, golden
+from oracle import engram as OE
+
+pytestmark = pytest.mark.gpu
+
+
+def _d(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def _args_from_golden(g):
+    return types.SimpleNamespace(
+        engram_layer_ids=tuple(int(v) for v in g["layer_ids"]),
+        engram_num_embeddings=tuple(int(v) for v in g["num_embeddings"]),
+        engram_max_ngram_size=int(g["max_ngram"]), engram_vocab_size=int(g["vocab_size"]),
+        engram_n_heads=int(g["n_heads"]), engram_pad_id=2,
+        engram_compressed_vocab_size=int(g["token_map_max"]) + 1)
+
+
+def _token_map(g):
+    """The real map restricted to the ids the fixture uses, plus one unused id that
+    carries the largest compressed id (the compressed-vocab size check)."""
+    tm = np.zeros(int(g["token_map_len"]), dtype=np.int64)
+    tm[g["sample_ids"]] = g["token_map_sample"]
+    spare = np.setdiff1d(np.arange(len(tm)), g["sample_ids"])[0]
+    tm[spare] = int(g["token_map_max"])
+    return tm
+
+
+def test_hash_golden_release_config(cuda):
+    """Release layout (layers 1 and 14, 16M vocab, 8 heads) and the real token map,
+    two chunks through one id cache."""
+    g = golden("engram_hash.npz")
+    tm = _token_map(g)
+    args = _args_from_golden(g)
+    h = q.engram.EngramHasher(args, tm)
+    cache = torch.zeros(g["cache"].shape, dtype=torch.int64, device="cuda")
+    ids, L1 = g["ids"], int(g["L1"])
+    h1 = h(_d(ids[:, :L1]), 0, cache)
+    h2 = h(_d(ids[:, L1:]), L1, cache)
+    assert np.array_equal(h1.cpu().numpy(), g["h1"])
+    assert np.array_equal(h2.cpu().numpy(), g["h2"])
+    assert np.array_equal(cache.cpu().numpy(), g["cache"])
+
+
+def test_hash_numpy_cache_written_back(cuda):
+    g = golden("engram_hash.npz")
+    tm = _token_map(g)
+    h = q.engram.EngramHasher(_args_from_golden(g), tm)
+    cache = np.zeros_like(g["cache"])
+    ids, L1 = g["ids"], int(g["L1"])
+    h(ids[:, :L1], 0, cache)
+    assert np.array_equal(cache[:, :L1], g["cache"][:, :L1])
+
+
+def test_hash_baseline_layout(cuda):
+    """config 5 layout: one layer, 24 primes from 4,000,000 (about 96M rows)."""
+    rng = np.random.default_rng(5)
+    primes, offsets = OE.build_layout(1, 4, 8, 4_000_000)
+    mult = OE.compute_hash_multipliers((1,), 4, 99092)
+    tm = np.arange(99092, dtype=np.int64)
+    args = types.SimpleNamespace(engram_layer_ids=(1,), engram_num_embeddings=(int(primes.sum()),),
+                                 engram_max_ngram_size=4, engram_vocab_size=4_000_000,
+                                 engram_n_heads=8, engram_pad_id=2,
+                                 engram_compressed_vocab_size=99092)
+    h = q.engram.EngramHasher(args, tm)
+    ids = rng.integers(0, 99092, size=(2, 700), dtype=np.int64)
+    cache = torch.zeros((2, 1024), dtype=torch.int64, device="cuda")
+    got = h(_d(ids), 0, cache).cpu().numpy()
+    cache_np = np.zeros((2, 1024), dtype=np.int64)
+    want = OE.engram_hash(ids, 0, cache_np, tm, mult, primes, offsets, 2, 4)
+    assert np.array_equal(got, want)
+    assert got.min() >= 0 and got.max() < primes.sum()
+
+
+def test_gather_rows_golden(cuda):
+    g = golden("engram_embed.npz")
+    emb = q.engram.EngramEmbedding(g["table"].shape[0], g["table"].shape[1], 32)
+    emb.weight, emb.scale = _d(g["table"]), _d(g["scale"])
+    got = emb(_d(g["idx"])).cpu().numpy()
+    assert bits_equal(got, g["out"])
+
+
+@pytest.mark.parametrize("d,block", [(256, 32), (1024, 1024), (512, 64)])
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_gather_sum(cuda, d, block, dtype):
+    rng = np.random.default_rng(d + block)
+    rows = 5000
+    table = rng.integers(0, 256, size=(rows, d), dtype=np.uint8)
+    table[(table & 0x7F) == 0x7F] = 0
+    scale = rng.integers(115, 128, size=(rows, d // block), dtype=np.uint8)
+    idx = rng.integers(0, rows, size=(37, 24))
+    emb = q.engram.EngramEmbedding(rows, d, block)
+    emb.weight, emb.scale = _d(table), _d(scale)
+    tdt = torch.float32 if dtype == "f32" else torch.bfloat16
+    got = emb.gather_sum(_d(idx), tdt)
+    want = OE.gather_sum(table, scale, idx, block, dtype)
+    got = got.cpu().numpy() if dtype == "f32" else got.view(torch.int16).cpu().numpy().view(np.uint16)
+    assert bits_equal(got, want)
+
+
+def test_gather_sharded_sums_to_full(cuda):
+    """row-sharded lookups (ids off the shard read zero rows) add up to the full lookup."""
+    rng = np.random.default_rng(8)
+    rows, d, block, ws = 4000, 256, 32, 4
+    table = rng.integers(0, 126, size=(rows, d), dtype=np.uint8)
+    scale = rng.integers(115, 128, size=(rows, d // block), dtype=np.uint8)
+    idx = _d(rng.integers(0, rows, size=(9, 24)))
+    full = q.engram.EngramEmbedding(rows, d, block)
+    full.weight, full.scale = _d(table), _d(scale)
+    ref = full(idx)
+    part = (rows + ws - 1) // ws
+    acc = torch.zeros_like(ref)
+    for r in range(ws):
+        e = q.engram.EngramEmbedding(part, d, block, row_lo=r * part)
+        e.weight, e.scale = _d(table[r * part:(r + 1) * part]), _d(scale[r * part:(r + 1) * part])
+        acc += e(idx)
+    assert torch.equal(acc, ref)

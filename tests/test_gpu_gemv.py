@@ -1,0 +1,122 @@
+"""Weight-decode GEMV kernels vs the oracle's dequant-then-matmul (float64).
+
+Tolerances (relative Frobenius): 1e-5 with fp32 output, 1e-2 with bf16 output.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import deepseek_v41_mlx_b200 as q
+from conftest import rel_fro
+from gen import affine_weight, bf16_acts, fp4_weight, fp8_weight
+from oracle import formats as F
+from oracle import linear as OL
+
+pytestmark = pytest.mark.gpu
+
+TOL_F32, TOL_BF16 = 1e-5, 1e-2
+
+
+def _d(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def _x(bits):
+    return _d(bits.view(np.int16)).view(torch.bfloat16)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 256, 512), (5, 200, 256), (8, 64, 128), (16, 130, 384),
+                                   (32, 512, 1024), (40, 96, 7168), (1, 4096, 7168)])
+def test_gemv_fp8_block(cuda, M, N, K):
+    rng = np.random.default_rng(M * 1000 + N)
+    w, s = fp8_weight(rng, N, K)
+    xb, xf = bf16_acts(rng, M, K)
+    want = OL.linear_fp8_block(xf, w, s)
+    got = q.linear.linear_fp8(_x(xb), _d(w), _d(s), out_dtype=torch.float32).cpu().numpy()
+    assert rel_fro(got, want) < TOL_F32
+    gotb = q.linear.linear_fp8(_x(xb), _d(w), _d(s)).float().cpu().numpy()
+    assert rel_fro(gotb, want) < TOL_BF16
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 256, 512), (3, 70, 256), (16, 64, 2048), (32, 128, 1024),
+                                   (33, 64, 512), (8, 2048, 7168)])
+def test_gemv_fp4(cuda, M, N, K):
+    rng = np.random.default_rng(M * 7 + K)
+    w, s = fp4_weight(rng, N, K)
+    xb, xf = bf16_acts(rng, M, K)
+    want = OL.linear_fp4(xf, w, s)
+    got = q.linear.linear_fp4(_x(xb), _d(w), _d(s), out_dtype=torch.float32).cpu().numpy()
+    assert rel_fro(got, want) < TOL_F32
+    gotb = q.linear.linear_fp4(_x(xb), _d(w), _d(s)).float().cpu().numpy()
+    assert rel_fro(gotb, want) < TOL_BF16
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("M,N,K", [(1, 128, 512), (16, 96, 1024), (7, 64, 256), (32, 64, 512)])
+def test_gemv_affine(cuda, bits, M, N, K):
+    rng = np.random.default_rng(bits * 100 + M)
+    wq, s, b = affine_weight(rng, N, K, bits)
+    xb, xf = bf16_acts(rng, M, K)
+    want = OL.linear_affine(xf, wq, s, b, bits)
+    ts = _d(s.view(np.int16)).view(torch.bfloat16)
+    tb = _d(b.view(np.int16)).view(torch.bfloat16)
+    got = q.linear.linear_affine(_x(xb), _d(wq.view(np.int32)), ts, tb, bits,
+                                 out_dtype=torch.float32).cpu().numpy()
+    assert rel_fro(got, want) < TOL_F32
+    gotb = q.linear.linear_affine(_x(xb), _d(wq.view(np.int32)), ts, tb, bits).float().cpu().numpy()
+    assert rel_fro(gotb, want) < TOL_BF16
+
+
+def test_gemv_affine_baseline_shape(cuda):
+    """config 4 weight [14336, 7168] 4-bit, M = 16, against the oracle on a row sample."""
+    rng = np.random.default_rng(4)
+    N, K, M = 14336, 7168, 16
+    wq, s, b = affine_weight(rng, N, K, 4)
+    xb, xf = bf16_acts(rng, M, K)
+    ts = _d(s.view(np.int16)).view(torch.bfloat16)
+    tb = _d(b.view(np.int16)).view(torch.bfloat16)
+    got = q.linear.linear_affine(_x(xb), _d(wq.view(np.int32)), ts, tb, 4,
+                                 out_dtype=torch.float32).cpu().numpy()
+    rows = rng.choice(N, 256, replace=False)
+    want = OL.linear_affine(xf, wq[rows], s[rows], b[rows], 4)
+    assert rel_fro(got[:, rows], want) < TOL_F32
+
+
+def test_gemv_repeat_is_deterministic(cuda):
+    """split-K partial sums are reduced in a fixed order: identical bits on repeat."""
+    rng = np.random.default_rng(9)
+    w, s = fp8_weight(rng, 4096, 7168)
+    xb, _ = bf16_acts(rng, 1, 7168)
+    a = q.linear.linear_fp8(_x(xb), _d(w), _d(s), out_dtype=torch.float32)
+    b = q.linear.linear_fp8(_x(xb), _d(w), _d(s), out_dtype=torch.float32)
+    assert torch.equal(a, b)
+
+
+def test_gemv_extreme_scales_exact(cuda):
+    """ue8m0 scales over the whole exponent range stay exact (scale folded in fp32)."""
+    rng = np.random.default_rng(11)
+    N, K = 64, 256
+    w, _ = fp4_weight(rng, N, K)
+    s = rng.integers(1, 200, size=(N, K // 32), dtype=np.uint8)
+    xb, xf = bf16_acts(rng, 2, K)
+    want = OL.linear_fp4(xf, w, s)
+    got = q.linear.linear_fp4(_x(xb), _d(w), _d(s), out_dtype=torch.float32).cpu().numpy()
+    assert rel_fro(got, want) < TOL_F32
+
+
+def test_gemv_large_activations(cuda):
+    """per-row power-of-two activation scaling keeps huge / tiny rows exact."""
+    rng = np.random.default_rng(12)
+    N, K = 128, 512
+    w, s = fp8_weight(rng, N, K)
+    xb, xf = bf16_acts(rng, 3, K)
+    xf = xf * np.array([[1e30], [1e-30], [1.0]], dtype=np.float32)
+    xb = F.f32_to_bf16_bits(xf)
+    xf = F.bf16_bits_to_f32(xb)
+    want = OL.linear_fp8_block(xf, w, s)
+    got = q.linear.linear_fp8(_x(xb), _d(w), _d(s), out_dtype=torch.float32).cpu().numpy()
+    for r in range(3):
+        assert rel_fro(got[r], want[r]) < TOL_F32
