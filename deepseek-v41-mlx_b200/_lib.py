@@ -54,6 +54,9 @@ PROTOTYPES = {
     "dsv41_get_last_error": (C.c_char_p, []),
     "dsv41_abi_version": (_I, []),
     "dsv41_device_status": (_I, [_P, _U32P]),
+    "dsv41_prof_enable": (_I, [_I]),
+    "dsv41_prof_reset": (_I, []),
+    "dsv41_prof_report": (_I, [C.c_char_p, _SZ]),
     "dsv41_e8m0_to_float": (_I, [_P, _I64, _P, _P]),
     "dsv41_dequant_fp8_block": (_I, [_P, _P, _I64, _I64, _I, _P, _P]),
     "dsv41_unpack_fp4": (_I, [_P, _I64, _I64, _P, _P]),
@@ -163,6 +166,22 @@ def u8(t):
     if t.element_size() == 1:
         return t.view(tt.uint8)
     raise ValueError(f"expected a 1-byte dtype, got {t.dtype}")
+
+
+def prof_enable(on: bool = True):
+    load().dsv41_prof_enable(1 if on else 0)
+    load().dsv41_prof_reset()
+
+
+def prof_report() -> dict:
+    """{kernel name: (launches, total_ms)} for launches since prof_enable."""
+    buf = C.create_string_buffer(1 << 16)
+    call("dsv41_prof_report", buf, len(buf))
+    out = {}
+    for line in buf.value.decode().splitlines():
+        name, n, ms = line.split()
+        out[name] = (int(n), float(ms))
+    return out
 
 
 def workspace(nbytes: int, device):

@@ -256,6 +256,35 @@ static inline int make_tmap_2d(CUtensorMap *m, const void *base, CUtensorMapData
   return DSV41_OK;
 }
 
+// ------------------------------------------------------------------ host: launch timing
+// Optional per-kernel timing with CUDA events recorded on the launching stream
+// around each hot kernel (enabled by dsv41_prof_enable; off by default).
+struct ProfRec {
+  const char *name;
+  cudaEvent_t a, b;
+};
+static constexpr int PROF_CAP = 4096;
+static ProfRec g_prof[PROF_CAP];
+static int g_prof_n = 0;
+static bool g_prof_on = false;
+
+struct ProfScope {
+  int slot = -1;
+  cudaStream_t st;
+  ProfScope(const char *name, cudaStream_t s) : st(s) {
+    if (!g_prof_on || g_prof_n >= PROF_CAP) return;
+    slot = g_prof_n++;
+    ProfRec &r = g_prof[slot];
+    r.name = name;
+    if (!r.a) cudaEventCreate(&r.a);
+    if (!r.b) cudaEventCreate(&r.b);
+    cudaEventRecord(r.a, st);
+  }
+  ~ProfScope() {
+    if (slot >= 0) cudaEventRecord(g_prof[slot].b, st);
+  }
+};
+
 static inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 static inline size_t align_up(size_t a, size_t b) { return (a + b - 1) / b * b; }
 

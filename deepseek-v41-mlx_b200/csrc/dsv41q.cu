@@ -29,6 +29,50 @@ extern "C" int dsv41_device_status(void *stream, uint32_t *flags_out) {
   return cuda_status(e, "dsv41_device_status");
 }
 
+// ======================================================================= profiling
+
+extern "C" int dsv41_prof_enable(int on) {
+  g_prof_on = on != 0;
+  return DSV41_OK;
+}
+
+extern "C" int dsv41_prof_reset(void) {
+  g_prof_n = 0;
+  return DSV41_OK;
+}
+
+extern "C" int dsv41_prof_report(char *buf, size_t cap) {
+  DSV41_REQUIRE(buf && cap > 0, DSV41_ERR_BAD_ARG, "NULL buffer");
+  // aggregate per name: launches and total milliseconds
+  const char *names[64];
+  int count[64];
+  double total[64];
+  int nn = 0;
+  for (int i = 0; i < g_prof_n; ++i) {
+    cudaError_t e = cudaEventSynchronize(g_prof[i].b);
+    if (e != cudaSuccess) return cuda_status(e, "prof sync");
+    float ms = 0.0f;
+    e = cudaEventElapsedTime(&ms, g_prof[i].a, g_prof[i].b);
+    if (e != cudaSuccess) return cuda_status(e, "prof elapsed");
+    int j = 0;
+    while (j < nn && strcmp(names[j], g_prof[i].name) != 0) ++j;
+    if (j == nn) {
+      if (nn == 64) continue;
+      names[nn] = g_prof[i].name;
+      count[nn] = 0;
+      total[nn] = 0.0;
+      ++nn;
+    }
+    count[j] += 1;
+    total[j] += ms;
+  }
+  size_t off = 0;
+  buf[0] = 0;
+  for (int j = 0; j < nn && off < cap; ++j)
+    off += snprintf(buf + off, cap - off, "%s %d %.6f\n", names[j], count[j], total[j]);
+  return DSV41_OK;
+}
+
 // ======================================================================= decode
 
 extern "C" int dsv41_e8m0_to_float(const uint8_t *scale, int64_t n, float *out, void *stream) {
@@ -182,7 +226,7 @@ struct WsCarve {
 constexpr int QG_MAX_SPLIT = 16;
 
 template <int WF, int NMAT, int NT>
-int qgemv_launch(const CUtensorMap &w0, const CUtensorMap &w1, const CUtensorMap &x8,
+int qgemv_launch(const char *name, const CUtensorMap &w0, const CUtensorMap &w1, const CUtensorMap &x8,
                  const CUtensorMap &x16, const CUtensorMap &x32, const QParams &p, int max_items,
                  cudaStream_t st) {
   using Cfg = QCfg<WF, NMAT, NT>;
@@ -198,6 +242,7 @@ int qgemv_launch(const CUtensorMap &w0, const CUtensorMap &w1, const CUtensorMap
   int grid = 2 * num_sms();
   if (max_items < grid) grid = max_items;
   if (grid < 1) grid = 1;
+  ProfScope prof(name, st);
   k_qgemv<WF, NMAT, NT><<<grid, QG_THREADS, Cfg::SMEM, st>>>(w0, w1, x8, x16, x32, p);
   DSV41_CHECK_LAUNCH("qgemv");
   return DSV41_OK;
@@ -275,9 +320,10 @@ int gemv_common(const void *x, int64_t M, int64_t K, const void *w, int64_t w_ro
 
   constexpr bool AFF = WF == WF_AFF4 || WF == WF_AFF8;
   const int perm = WF == WF_AFF4 ? 4 : (WF == WF_AFF8 ? 8 : 0);
+  { ProfScope prof("qx_prep", st);
   k_qx_prep<<<unsigned(M), 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16 *>(x), M, K,
                                           nullptr, nullptr, ws.x16, ws.xscale,
-                                          AFF ? ws.xsum : nullptr, perm);
+                                          AFF ? ws.xsum : nullptr, perm); }
   DSV41_CHECK_LAUNCH("qx_prep");
 
   CUtensorMap wm, xm[3];
@@ -312,9 +358,9 @@ int gemv_common(const void *x, int64_t M, int64_t K, const void *w, int64_t w_ro
     if (e != cudaSuccess) return cuda_status(e, "memset counters");
   }
   const int items = int(tiles * nch * p.nsplit);
-  if (M <= 8) return qgemv_launch<WF, 1, 1>(wm, wm, xm[0], xm[1], xm[2], p, items, st);
-  if (M <= 16) return qgemv_launch<WF, 1, 2>(wm, wm, xm[0], xm[1], xm[2], p, items, st);
-  return qgemv_launch<WF, 1, 4>(wm, wm, xm[0], xm[1], xm[2], p, items, st);
+  if (M <= 8) return qgemv_launch<WF, 1, 1>("qgemv_dense", wm, wm, xm[0], xm[1], xm[2], p, items, st);
+  if (M <= 16) return qgemv_launch<WF, 1, 2>("qgemv_dense", wm, wm, xm[0], xm[1], xm[2], p, items, st);
+  return qgemv_launch<WF, 1, 4>("qgemv_dense", wm, wm, xm[0], xm[1], xm[2], p, items, st);
 }
 
 }  // namespace
@@ -378,11 +424,13 @@ static int route_impl(const void *x, int64_t T, int64_t D, const void *gate_w, c
                       cudaStream_t st) {
   const int nks = router_nks(T, D, E);
   const int64_t warps = ceil_div(E, 16) * ceil_div(T, 8) * nks;
+  { ProfScope prof("router_scores", st);
   k_router_scores<<<unsigned(ceil_div(warps * 32, 128)), 128, 0, st>>>(
       reinterpret_cast<const __nv_bfloat16 *>(x), T, D,
-      reinterpret_cast<const __nv_bfloat16 *>(gate_w), E, nks, partial);
+      reinterpret_cast<const __nv_bfloat16 *>(gate_w), E, nks, partial); }
   DSV41_CHECK_LAUNCH("router_scores");
   const int threads = int(ceil_div(E, 32) * 32);
+  ProfScope prof("router_select", st);
   k_router_select<<<unsigned(T), threads, 0, st>>>(partial, nks, T, E, bias, topk, score_func,
                                                    gate_temp, norm_topk_prob, route_scale, weights,
                                                    indices);
@@ -524,12 +572,14 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
   const int round = (cfg->flags & DSV41_MOE_ROUND_BF16) ? 1 : 0;
   int rc;
   // plan
-  k_moe_plan<<<1, 1024, 3 * d.E * sizeof(int), st>>>(idx, T, cfg->topk, d.E, ws.plan);
+  { ProfScope prof("moe_plan", st);
+  k_moe_plan<<<1, 1024, 3 * d.E * sizeof(int), st>>>(idx, T, cfg->topk, d.E, ws.plan); }
   DSV41_CHECK_LAUNCH("moe_plan");
   // activations gathered per pair
+  { ProfScope prof("qx_prep_gather", st);
   k_qx_prep<<<unsigned(d.Pmax), 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16 *>(x), T, d.D,
                                                 ws.plan.pair_tok, ws.plan.counts + 2, ws.x16g,
-                                                ws.xsg, nullptr, 0);
+                                                ws.xsg, nullptr, 0); }
   DSV41_CHECK_LAUNCH("qx_prep gathered");
 
   CUtensorMap m_w1, m_w3, m_w2, xg[3], hx[3];
@@ -565,7 +615,7 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
       cudaError_t e = cudaMemsetAsync(ws.cnt_gu, 0, sizeof(int) * d.Cmax * d.tiles_gu, st);
       if (e != cudaSuccess) return cuda_status(e, "memset");
     }
-    rc = qgemv_launch<WF_FP4, 2, 2>(m_w1, m_w3, xg[0], xg[1], xg[2], p,
+    rc = qgemv_launch<WF_FP4, 2, 2>("moe_expert_gate_up_fp4", m_w1, m_w3, xg[0], xg[1], xg[2], p,
                                      int(d.Cmax * d.tiles_gu * p.nsplit), st);
     if (rc) return rc;
   }
@@ -592,14 +642,15 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
       cudaError_t e = cudaMemsetAsync(ws.cnt_dn, 0, sizeof(int) * d.Cmax * d.tiles_dn, st);
       if (e != cudaSuccess) return cuda_status(e, "memset");
     }
-    rc = qgemv_launch<WF_FP4, 1, 4>(m_w2, m_w2, hx[0], hx[1], hx[2], p,
+    rc = qgemv_launch<WF_FP4, 1, 4>("moe_expert_down_fp4", m_w2, m_w2, hx[0], hx[1], hx[2], p,
                                      int(d.Cmax * d.tiles_dn * p.nsplit), st);
     if (rc) return rc;
   }
   if (!shared) return DSV41_OK;
   // shared expert (fp8 32x32): gate/up -> Hs -> down -> Ys
+  { ProfScope prof("qx_prep", st);
   k_qx_prep<<<unsigned(T), 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16 *>(x), T, d.D,
-                                          nullptr, nullptr, ws.x16, ws.xs, nullptr, 0);
+                                          nullptr, nullptr, ws.x16, ws.xs, nullptr, 0); }
   DSV41_CHECK_LAUNCH("qx_prep shared");
   CUtensorMap m_s1, m_s3, m_s2, xs[3], hs[3];
   if ((rc = weight_map(&m_s1, W->sw1, d.I, d.D))) return rc;
@@ -633,7 +684,7 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
       cudaError_t e = cudaMemsetAsync(ws.cnt_sgu, 0, sizeof(int) * nch * d.tiles_gu, st);
       if (e != cudaSuccess) return cuda_status(e, "memset");
     }
-    rc = qgemv_launch<WF_FP8B, 2, 4>(m_s1, m_s3, xs[0], xs[1], xs[2], p,
+    rc = qgemv_launch<WF_FP8B, 2, 4>("moe_shared_gate_up_fp8", m_s1, m_s3, xs[0], xs[1], xs[2], p,
                                       int(nch * d.tiles_gu * p.nsplit), st);
     if (rc) return rc;
   }
@@ -663,7 +714,7 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
       cudaError_t e = cudaMemsetAsync(ws.cnt_sdn, 0, sizeof(int) * nch * d.tiles_dn, st);
       if (e != cudaSuccess) return cuda_status(e, "memset");
     }
-    rc = qgemv_launch<WF_FP8B, 1, 4>(m_s2, m_s2, hs[0], hs[1], hs[2], p,
+    rc = qgemv_launch<WF_FP8B, 1, 4>("moe_shared_down_fp8", m_s2, m_s2, hs[0], hs[1], hs[2], p,
                                       int(nch * d.tiles_dn * p.nsplit), st);
     if (rc) return rc;
   }
@@ -712,6 +763,7 @@ extern "C" int dsv41_moe_decode(const dsv41_moe_config *cfg, const dsv41_moe_wei
   rc = moe_experts_impl(cfg, W, x, d, ws, idx, ws.Y, shared, st);
   if (rc) return rc;
   const int64_t n = T * d.D;
+  ProfScope prof("moe_combine", st);
   if (out_dtype == DSV41_F32)
     k_moe_combine<float><<<grid_for(n), 256, 0, st>>>(ws.Y, shared ? ws.Ys : nullptr, wts, T,
                                                       cfg->topk, d.D, (float *)y);
@@ -789,6 +841,7 @@ extern "C" int dsv41_engram_gather_sum(const uint8_t *table, const uint8_t *scal
   DSV41_REQUIRE(aligned(table, 8), DSV41_ERR_MISALIGNED, "table must be 8-byte aligned");
   const unsigned blocks = unsigned(ceil_div(n_tok * 32, 256));
   cudaStream_t st = STREAM(stream);
+  ProfScope prof("engram_gather_sum", st);
 #define GS(T, DPL)                                                                           \
   k_engram_gather_sum<T, DPL><<<blocks, 256, 0, st>>>(table, scale, rows, row_lo, block, idx, \
                                                       n_tok, n_per_tok, (T *)out)

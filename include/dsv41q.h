@@ -72,6 +72,14 @@ int dsv41_abi_version(void);
  * (bit 0: a bounded wait ran out).  Synchronises `stream`. */
 int dsv41_device_status(void *stream, uint32_t *flags_out);
 
+/* ---- launch timing (no reference counterpart; the reference times with
+ * ad-hoc time.time(), scripts/ppl_large.py:81-84).  When enabled, every hot
+ * kernel launch is bracketed by CUDA events on its stream; report() waits for
+ * them and writes one line per kernel name: "<name> <launches> <total_ms>". */
+int dsv41_prof_enable(int on);
+int dsv41_prof_reset(void);
+int dsv41_prof_report(char *buf, size_t cap);
+
 /* ---- a1..a7: release-format decode (bit-exact) --------------------------
  * e8m0_to_float    replaces deepseek_v41_mlx/dequant.py:33-36
  * dequant_fp8      replaces deepseek_v41_mlx/dequant.py:45-50 (+ _expand_blocks :39-42)
