@@ -8,6 +8,8 @@
 #include "router.cuh"
 #include "moe.cuh"
 
+#include <mutex>
+
 using namespace dsv41;
 
 #define STREAM(s) (reinterpret_cast<cudaStream_t>(s))
@@ -857,4 +859,124 @@ extern "C" int dsv41_engram_gather_sum(const uint8_t *table, const uint8_t *scal
 #undef GS
   DSV41_CHECK_LAUNCH("engram_gather_sum");
   return DSV41_OK;
+}
+
+// ======================================================================= allocation-free GEMV
+//
+// A second entry point for the fp8 32x32 GEMV for callers that cannot hand the
+// library any device memory and must not have it call cudaMalloc: hosts whose
+// device memory is owned up front by their own pool or arena (cudaMalloc behind
+// their back breaks their accounting and can fail once the pool has reserved the
+// GPU), and FFI callers that can pass data pointers but have no allocator for a
+// workspace.  Its scratch (activations as f16, split-K partial sums, split-K
+// tickets) lives in the file-scope array below, which every GPU that loads this
+// library holds until the process exits.
+//
+// Limits: 1 <= M <= 32, K % 32 == 0, M * K <= 262,144, N <= 16,384; larger
+// shapes are rejected with DSV41_ERR_UNSUPPORTED (use dsv41_gemv_fp8_block with a
+// workspace instead).
+//
+// The first call on a device looks up the array's device address for that device
+// (cudaGetSymbolAddress, with that device current); make that first call before
+// any stream capture.  All calls on a device share the one array and it keeps the
+// previous call's contents: the tickets are cleared on every call, and calls whose
+// kernels overlap on the GPU (different streams, no ordering between them) race on
+// the array and give wrong results -- order them on one stream.
+#define DSV41_NOALLOC_SCRATCH_BYTES (4u << 20)
+static __device__ __align__(256) unsigned char g_noalloc_scratch[DSV41_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+void *g_noalloc_ptr[64] = {nullptr};
+std::mutex g_noalloc_mu;
+
+int noalloc_scratch_ptr(void **out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
+  DSV41_REQUIRE(dev >= 0 && dev < 64, DSV41_ERR_UNSUPPORTED, "device index %d >= 64", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void *p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);   // device `dev` is current
+    if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(noalloc scratch)");
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return DSV41_OK;
+}
+
+template <int NT>
+int noalloc_gemv_launch(const CUtensorMap &wm, const CUtensorMap (&xm)[3], QParams &p,
+                        int tiles, cudaStream_t st) {
+  return qgemv_launch<WF_FP8B, 1, NT>("qgemv_dense_noalloc", wm, wm, xm[0], xm[1], xm[2], p,
+                                       tiles * p.nsplit, st);
+}
+
+}  // namespace
+
+extern "C" int dsv41_gemv_fp8_block_noalloc(const void *x, int64_t M, int64_t K, const uint8_t *w,
+                                            const uint8_t *s, int64_t N, int out_dtype, void *y,
+                                            void *stream) {
+  DSV41_REQUIRE(out_dtype == DSV41_F32 || out_dtype == DSV41_BF16, DSV41_ERR_BAD_DTYPE,
+                "out_dtype must be F32 or BF16");
+  DSV41_REQUIRE(K > 0 && K % 32 == 0, DSV41_ERR_BAD_SHAPE, "K must be a positive multiple of 32");
+  DSV41_REQUIRE(M >= 1 && M <= 32 && M * K <= 262144 && N >= 1 && N <= 16384,
+                DSV41_ERR_UNSUPPORTED,
+                "gemv_fp8_block_noalloc: needs 1 <= M <= 32, M*K <= 262144, 1 <= N <= 16384 "
+                "(got M=%lld K=%lld N=%lld); use dsv41_gemv_fp8_block with a workspace",
+                (long long)M, (long long)K, (long long)N);
+  DSV41_REQUIRE(x && w && s && y, DSV41_ERR_BAD_ARG, "NULL pointer");
+  cudaStream_t st = STREAM(stream);
+  void *base = nullptr;
+  int rc = noalloc_scratch_ptr(&base);
+  if (rc) return rc;
+
+  const int NT = M <= 8 ? 1 : (M <= 16 ? 2 : 4);
+  const int64_t tiles = ceil_div(N, QG_ROWS);
+  WsCarve wc{reinterpret_cast<uint8_t *>(base), DSV41_NOALLOC_SCRATCH_BYTES, 0};
+  __half *x16 = wc.take<__half>(M * K);
+  float *xscale = wc.take<float>(32);
+  int *counters = wc.take<int>(256);
+  wc.off = align_up(wc.off, 256);
+  float *partial = reinterpret_cast<float *>(wc.base + wc.off);
+  const size_t frag_bytes = (size_t)32 * QG_CW * NT * 4 * sizeof(float);   // per tile and split
+  const int64_t cap_splits = (int64_t)((DSV41_NOALLOC_SCRATCH_BYTES - wc.off) / (frag_bytes * tiles));
+  DSV41_REQUIRE(wc.ok && cap_splits >= 1, DSV41_ERR_UNSUPPORTED, "shape exceeds the scratch array");
+
+  QParams p{};
+  p.scale[0] = s;
+  p.scale[1] = s;
+  p.N = N;
+  p.K = K;
+  p.sld = ceil_div(K, 32);
+  p.tiles = int(tiles);
+  p.kstages = int(ceil_div(K, Fmt<WF_FP8B>::KS));
+  p.nsplit = pick_nsplit(tiles, p.kstages);
+  if (p.nsplit > cap_splits) p.nsplit = int(cap_splits);
+  p.xscale = xscale;
+  p.chunks = nullptr;
+  p.nchunks_host = 1;
+  p.dense_m = int(M);
+  p.epi = out_dtype == DSV41_F32 ? EPI_STORE_F32 : EPI_STORE_BF16;
+  p.out = y;
+  p.ldo = N;
+  p.partial = partial;
+  p.counters = counters;
+  // the array keeps the last call's contents: tickets must start at zero
+  cudaError_t e = cudaMemsetAsync(counters, 0, sizeof(int) * 256, st);
+  if (e != cudaSuccess) return cuda_status(e, "clear noalloc tickets");
+
+  {
+    ProfScope prof("qx_prep", st);
+    k_qx_prep<<<unsigned(M), 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16 *>(x), M, K,
+                                            nullptr, nullptr, x16, xscale, nullptr, 0);
+  }
+  DSV41_CHECK_LAUNCH("qx_prep (noalloc)");
+  CUtensorMap wm, xm[3];
+  if ((rc = weight_map(&wm, w, N, K))) return rc;
+  if ((rc = make_x_maps(xm, x16, M, K))) return rc;
+  if (NT == 1) return noalloc_gemv_launch<1>(wm, xm, p, int(tiles), st);
+  if (NT == 2) return noalloc_gemv_launch<2>(wm, xm, p, int(tiles), st);
+  return noalloc_gemv_launch<4>(wm, xm, p, int(tiles), st);
 }

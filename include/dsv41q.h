@@ -134,6 +134,17 @@ int dsv41_gemv_fp8_block(const void *x, int64_t M, int64_t K, const uint8_t *w,
 int dsv41_gemv_fp4(const void *x, int64_t M, int64_t K, const uint8_t *w, const uint8_t *s,
                    int64_t N, int out_dtype, void *y, void *workspace, size_t workspace_bytes,
                    void *stream);
+/* The same fp8 GEMV for callers that cannot give the library device memory and
+ * must not have it allocate: hosts whose GPU memory is owned up front by their own
+ * pool, and FFI callers with no device allocator for a workspace.  No counterpart
+ * in the reference (it has no allocation-free entry point).  Scratch is a 4 MiB
+ * array inside the library, held by every GPU that loads it until exit; limits
+ * 1 <= M <= 32, M*K <= 262144, N <= 16384 (else DSV41_ERR_UNSUPPORTED).  The first
+ * call on a device looks up that array's address and should come before any
+ * stream capture; calls that overlap on the GPU race on the shared array. */
+int dsv41_gemv_fp8_block_noalloc(const void *x, int64_t M, int64_t K, const uint8_t *w,
+                                 const uint8_t *s, int64_t N, int out_dtype, void *y,
+                                 void *stream);
 /* affine: bits 4 or 8, group 64; scales/biases bf16 [N, K/64] */
 int dsv41_gemv_affine(const void *x, int64_t M, int64_t K, const uint32_t *wq,
                       const void *scales, const void *biases, int bits, int64_t N,
