@@ -241,11 +241,22 @@ int qgemv_launch(const char *name, const CUtensorMap &w0, const CUtensorMap &w1,
     if (e != cudaSuccess) return cuda_status(e, "qgemv smem attribute");
     attr_set[dev] = true;
   }
-  int grid = 2 * num_sms();
+  int grid = QG_MIN_CTAS * num_sms();
   if (max_items < grid) grid = max_items;
   if (grid < 1) grid = 1;
+  // vector scale loads when every stage is full and scale rows are NG-aligned
+  QParams pv = p;
+  constexpr int NG = Fmt<WF>::NG;
+  bool sv = (p.K % Fmt<WF>::KS == 0) && (p.sld % NG == 0);
+  if (WF == WF_FP4)
+    sv = sv && aligned(p.scale[0], 8) && aligned(p.scale[NMAT - 1], 8);
+  else if (WF == WF_FP8B)
+    sv = sv && aligned(p.scale[0], 4) && aligned(p.scale[NMAT - 1], 4);
+  else
+    sv = sv && aligned(p.aff_s, 2 * NG) && aligned(p.aff_b, 2 * NG);
+  pv.svec = sv ? 1 : 0;
   ProfScope prof(name, st);
-  k_qgemv<WF, NMAT, NT><<<grid, QG_THREADS, Cfg::SMEM, st>>>(w0, w1, x8, x16, x32, p);
+  k_qgemv<WF, NMAT, NT><<<grid, QG_THREADS, Cfg::SMEM, st>>>(w0, w1, x8, x16, x32, pv);
   DSV41_CHECK_LAUNCH("qgemv");
   return DSV41_OK;
 }
@@ -267,7 +278,7 @@ int weight_map(CUtensorMap *m, const void *w, int64_t rows, int64_t row_bytes) {
 }
 
 int pick_nsplit(int64_t base_items, int kstages) {
-  const int64_t target = 2 * (int64_t)num_sms();
+  const int64_t target = QG_MIN_CTAS * (int64_t)num_sms();
   int64_t ns = (target + base_items - 1) / base_items;
   int64_t cap = kstages / 2;
   if (cap < 1) cap = 1;
@@ -495,7 +506,7 @@ MoeDims moe_dims(const dsv41_moe_config *c, int64_t T) {
   d.P = T * c->topk;
   const int64_t act = d.P < d.E ? d.P : d.E;
   d.Pmax = d.P + 3 * act;
-  d.Cmax = ceil_div(d.P, MOE_PAIRS_PER_CHUNK) + act;
+  d.Cmax = ceil_div(d.P, MOE_DN_CHUNK) + act;   // the down list is the longer one
   d.Tp = ceil_div(T, 4) * 4;
   d.tiles_gu = ceil_div(d.I, QG_ROWS);
   d.tiles_dn = ceil_div(d.D, QG_ROWS);
@@ -575,7 +586,7 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
   int rc;
   // plan
   { ProfScope prof("moe_plan", st);
-  k_moe_plan<<<1, 1024, 3 * d.E * sizeof(int), st>>>(idx, T, cfg->topk, d.E, ws.plan); }
+  k_moe_plan<<<1, 1024, 4 * d.E * sizeof(int), st>>>(idx, T, cfg->topk, d.E, ws.plan); }
   DSV41_CHECK_LAUNCH("moe_plan");
   // activations gathered per pair
   { ProfScope prof("qx_prep_gather", st);
@@ -617,7 +628,7 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
       cudaError_t e = cudaMemsetAsync(ws.cnt_gu, 0, sizeof(int) * d.Cmax * d.tiles_gu, st);
       if (e != cudaSuccess) return cuda_status(e, "memset");
     }
-    rc = qgemv_launch<WF_FP4, 2, 2>("moe_expert_gate_up_fp4", m_w1, m_w3, xg[0], xg[1], xg[2], p,
+    rc = qgemv_launch<WF_FP4, 2, 1>("moe_expert_gate_up_fp4", m_w1, m_w3, xg[0], xg[1], xg[2], p,
                                      int(d.Cmax * d.tiles_gu * p.nsplit), st);
     if (rc) return rc;
   }
@@ -644,7 +655,7 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
       cudaError_t e = cudaMemsetAsync(ws.cnt_dn, 0, sizeof(int) * d.Cmax * d.tiles_dn, st);
       if (e != cudaSuccess) return cuda_status(e, "memset");
     }
-    rc = qgemv_launch<WF_FP4, 1, 4>("moe_expert_down_fp4", m_w2, m_w2, hx[0], hx[1], hx[2], p,
+    rc = qgemv_launch<WF_FP4, 1, 1>("moe_expert_down_fp4", m_w2, m_w2, hx[0], hx[1], hx[2], p,
                                      int(d.Cmax * d.tiles_dn * p.nsplit), st);
     if (rc) return rc;
   }

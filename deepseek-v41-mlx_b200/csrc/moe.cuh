@@ -21,7 +21,10 @@ struct MoePlan {
   int *counts;          // [0] n_gu, [1] n_dn, [2] n_pairs_padded, [3] n_sgu, [4] n_sdn
 };
 
-constexpr int MOE_PAIRS_PER_CHUNK = 16;
+// Pairs per chunk: one n8 tile of activation rows for gate/up (8 pairs), and for
+// down 8 H rows = 4 pairs (hi/lo halves).  Experts with more pairs get more chunks.
+constexpr int MOE_GU_CHUNK = 8;
+constexpr int MOE_DN_CHUNK = 4;
 
 // One CTA of 1024 threads.  Deterministic: a pair's rank inside its expert is
 // the number of earlier pairs (row-major over [T, k]) routed to the same expert.
@@ -30,7 +33,8 @@ __global__ void __launch_bounds__(1024) k_moe_plan(const int32_t *__restrict__ i
   extern __shared__ int sh[];
   int *cnt = sh;            // [E]
   int *poff = sh + E;       // [E] padded pair offset
-  int *coff = sh + 2 * E;   // [E] chunk offset
+  int *coff = sh + 2 * E;   // [E] gate/up chunk offset
+  int *doff = sh + 3 * E;   // [E] down chunk offset
   const int64_t P = T * topk;
   for (int64_t e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
   __syncthreads();
@@ -41,15 +45,17 @@ __global__ void __launch_bounds__(1024) k_moe_plan(const int32_t *__restrict__ i
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    int po = 0, co = 0;
+    int po = 0, co = 0, dn = 0;
     for (int64_t e = 0; e < E; ++e) {
       poff[e] = po;
       coff[e] = co;
+      doff[e] = dn;
       po += (cnt[e] + 3) & ~3;
-      co += (cnt[e] + MOE_PAIRS_PER_CHUNK - 1) / MOE_PAIRS_PER_CHUNK;
+      co += (cnt[e] + MOE_GU_CHUNK - 1) / MOE_GU_CHUNK;
+      dn += (cnt[e] + MOE_DN_CHUNK - 1) / MOE_DN_CHUNK;
     }
     plan.counts[0] = co;
-    plan.counts[1] = co;
+    plan.counts[1] = dn;
     plan.counts[2] = po;
     const int sgu = int((T + 31) / 32), sdn = int((T + 15) / 16);
     plan.counts[3] = sgu;
@@ -66,12 +72,15 @@ __global__ void __launch_bounds__(1024) k_moe_plan(const int32_t *__restrict__ i
   for (int64_t e = threadIdx.x; e < E; e += blockDim.x) {
     const int n = cnt[e];
     if (n == 0) continue;
-    const int nch = (n + MOE_PAIRS_PER_CHUNK - 1) / MOE_PAIRS_PER_CHUNK;
-    for (int c = 0; c < nch; ++c) {
-      const int q0 = poff[e] + c * MOE_PAIRS_PER_CHUNK;
-      const int np = min(MOE_PAIRS_PER_CHUNK, n - c * MOE_PAIRS_PER_CHUNK);
+    for (int c = 0; c * MOE_GU_CHUNK < n; ++c) {
+      const int q0 = poff[e] + c * MOE_GU_CHUNK;
+      const int np = min(MOE_GU_CHUNK, n - c * MOE_GU_CHUNK);
       plan.gu_chunks[coff[e] + c] = QChunk{int(e), q0, np, q0};
-      plan.dn_chunks[coff[e] + c] = QChunk{int(e), 2 * q0, 8 * ((np + 3) / 4), q0};
+    }
+    for (int c = 0; c * MOE_DN_CHUNK < n; ++c) {
+      const int q0 = poff[e] + c * MOE_DN_CHUNK;   // multiple of 4: H rows 2*q0 ..
+      const int np = min(MOE_DN_CHUNK, n - c * MOE_DN_CHUNK);
+      plan.dn_chunks[doff[e] + c] = QChunk{int(e), 2 * q0, 8 * ((np + 3) / 4), q0};
     }
     for (int q = poff[e] + n; q < poff[e] + ((n + 3) & ~3); ++q) {
       plan.pair_tok[q] = -1;

@@ -7,10 +7,13 @@
 //   WF_AFF4 / WF_AFF8 : MLX affine codes, bf16 scale/bias per (row, 64 k)
 // The weight bytes are the HBM stream this kernel is bounded by.
 //
-// Structure (one CTA = 4 consumer warps + 1 producer warp, persistent):
-//   * the producer warp streams 64-row x 128-byte weight tiles and the matching
-//     activation tiles into a STAGES-deep shared-memory ring with 2D TMA
-//     (128-byte swizzle, no multicast), signalling mbarriers with tx counts;
+// Structure (one CTA = 4 consumer warps + 1 producer warp, persistent, 3 CTAs/SM):
+//   * producer lane 0 streams 64-row x 128-byte weight tiles and the matching
+//     activation tiles into a shared-memory ring with 2D TMA (128-byte swizzle,
+//     no multicast), signalling mbarriers with tx counts; the other producer lanes
+//     load the stage's ue8m0 / bf16 scale operands one stage ahead, convert them
+//     to fp32 once per CTA and store them next to the tile (the consumers would
+//     otherwise each convert the same scale four times);
 //   * each consumer warp owns 16 weight rows; per 32/64-k scale group it decodes
 //     its share of the tile in registers straight to exact f16 (cvt.rn.f16x2.
 //     e2m1x2 / e4m3x2, or the 0x6400 magic for affine codes), runs
@@ -27,6 +30,9 @@
 // expert's tokens) x 64-row tiles x K splits.  K splits write fp32 fragments to a
 // workspace and the last CTA of a tile (atomic ticket) sums them in split order,
 // so results are deterministic.
+//
+// A ue8m0 scale byte of 0 (2^-127) is applied as 0 here: the group's decoded
+// weights are then below 6 * 2^-127 in magnitude.
 #pragma once
 #include "common.cuh"
 
@@ -44,7 +50,8 @@ template <> struct Fmt<WF_AFF8> { static constexpr int KS = 128, GK = 64, NG = 2
 constexpr int QG_CW = 4;                   // consumer warps
 constexpr int QG_ROWS = 16 * QG_CW;        // weight rows per tile
 constexpr int QG_THREADS = 32 * (QG_CW + 1);
-constexpr int QG_STAGES = 4;
+constexpr int QG_MIN_CTAS = 3;             // CTAs per SM the shared memory is sized for
+constexpr int QG_SMEM_BUDGET = 72 * 1024;  // stage ring bytes per CTA
 
 // x-row chunk descriptor (device list for MoE, implicit for dense)
 struct QChunk {
@@ -60,9 +67,10 @@ struct QParams {
   const uint16_t *aff_b;       // affine bf16 biases
   int64_t N, K;
   int64_t sld;                 // scale row stride in elements
+  int svec;                    // scale rows are NG-aligned and K % KS == 0: vector loads
   int tiles;                   // ceil(N / QG_ROWS)
   int nsplit;
-  int kstages;                 // K / KS
+  int kstages;                 // ceil(K / KS)
   const float *xscale;         // per x row multiplier (power of two), or null
   const float *xsum;           // affine: [xrows, K/64] sums of the f16 x values
   const QChunk *chunks;        // null -> dense
@@ -115,6 +123,25 @@ __device__ __forceinline__ uint4 lds128(uint32_t a) {
                : "r"(a));
   return v;
 }
+__device__ __forceinline__ float4 lds128f(uint32_t a) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(a));
+  return v;
+}
+__device__ __forceinline__ float2 lds64f(uint32_t a) {
+  float2 v;
+  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ void sts128f(uint32_t a, float x, float y, float z, float w) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(a), "f"(x), "f"(y), "f"(z), "f"(w)
+               : "memory");
+}
+__device__ __forceinline__ void sts64f(uint32_t a, float x, float y) {
+  asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(a), "f"(x), "f"(y) : "memory");
+}
 
 // affine magic decode: f16x2 (1024 + q) - 1024 = exact q
 __device__ __forceinline__ uint32_t aff_pair(uint32_t bits) {
@@ -124,15 +151,30 @@ __device__ __forceinline__ uint32_t aff_pair(uint32_t bits) {
   return *reinterpret_cast<uint32_t *>(&h);
 }
 
+// ue8m0 byte (in the low 8 bits) -> 2^(b-127), with b = 0 applied as 0
+__device__ __forceinline__ float e8m0_fast(uint32_t b) { return __uint_as_float((b & 0xFFu) << 23); }
+
 template <int WF, int NMAT, int NT>
 struct QCfg {
   static constexpr int KS = Fmt<WF>::KS;
+  static constexpr int NG = Fmt<WF>::NG;
+  static constexpr bool AFF = (WF == WF_AFF4 || WF == WF_AFF8);
   static constexpr int NBOX = KS / 64;                       // x boxes per stage
   static constexpr int W_BYTES = QG_ROWS * 128;              // per matrix per stage
   static constexpr int XBOX_BYTES = NT * 8 * 128;            // max rows
-  static constexpr int STAGE_BYTES = NMAT * W_BYTES + NBOX * XBOX_BYTES;
-  static constexpr int SMEM = QG_STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int TILE_BYTES = NMAT * W_BYTES + NBOX * XBOX_BYTES;   // 1024-multiple
+  // fp32 scale operands per stage
+  static constexpr int SC_FLOATS =
+      WF == WF_FP4 ? NMAT * QG_ROWS * NG
+                   : (WF == WF_FP8B ? NMAT * 2 * NG : 2 * QG_ROWS * NG + NT * 8 * NG);
+  static constexpr int SC_BYTES = (SC_FLOATS * 4 + 127) / 128 * 128;
+  static constexpr int STAGES_RAW = QG_SMEM_BUDGET / (TILE_BYTES + SC_BYTES);
+  static constexpr int STAGES = STAGES_RAW < 2 ? 2 : (STAGES_RAW > 8 ? 8 : STAGES_RAW);
+  static constexpr int SMEM = STAGES * (TILE_BYTES + SC_BYTES) + 1024 /*align*/ + 256 /*barriers*/;
   static constexpr int FRAG = NMAT * NT * 4;                 // fp32 per consumer thread
+  // scale rows each producer lane converts per stage
+  static constexpr int PRODUCER_ITEMS =
+      WF == WF_FP4 ? NMAT * QG_ROWS / 32 : (WF == WF_FP8B ? 1 : 3);
 };
 
 __device__ __forceinline__ void decode_chunk(const QParams &p, int item, int &chunk, int &tile,
@@ -152,27 +194,173 @@ __device__ __forceinline__ void decode_chunk(const QParams &p, int item, int &ch
   }
 }
 
+// ------------------------------------------------------------------ producer scale staging
+// Raw scale words one producer lane fetches for one stage (registers), then
+// converts to fp32 into the stage's scale area.
+template <int WF, int NMAT, int NT>
+struct ScaleRaw {
+  using C = QCfg<WF, NMAT, NT>;
+  uint32_t w[C::PRODUCER_ITEMS][C::AFF ? 4 : (C::NG / 4 > 0 ? C::NG / 4 : 1)];
+};
+
+template <int WF, int NMAT, int NT>
+__device__ __forceinline__ void scales_fetch(const QParams &p, const QChunk &c, int64_t nbase, int ks,
+                                             int lane, ScaleRaw<WF, NMAT, NT> &r) {
+  using C = QCfg<WF, NMAT, NT>;
+  constexpr int NG = C::NG;
+  constexpr int GK = Fmt<WF>::GK;
+  if constexpr (WF == WF_FP4) {
+    // lane handles (mat, row) = items j: idx = lane + 32 j over NMAT x 64 rows
+#pragma unroll
+    for (int j = 0; j < C::PRODUCER_ITEMS; ++j) {
+      const int idx = lane + 32 * j, m = idx / QG_ROWS, row = idx % QG_ROWS;
+      const bool ok = nbase + row < p.N;
+      const uint8_t *sp = p.scale[m] + ((int64_t)c.mat * p.N + nbase + row) * p.sld + (int64_t)ks * NG;
+      if (p.svec) {
+        const uint2 v = ok ? __ldg(reinterpret_cast<const uint2 *>(sp)) : make_uint2(0, 0);
+        r.w[j][0] = v.x;
+        r.w[j][1] = v.y;
+      } else {
+        uint32_t v0 = 0, v1 = 0;
+#pragma unroll
+        for (int q = 0; q < NG; ++q) {
+          const bool in = ok && (int64_t)(ks * NG + q) * GK < p.K;
+          const uint32_t b = in ? __ldg(sp + q) : 0u;
+          if (q < 4) v0 |= b << (8 * q);
+          else v1 |= b << (8 * (q - 4));
+        }
+        r.w[j][0] = v0;
+        r.w[j][1] = v1;
+      }
+    }
+  } else if constexpr (WF == WF_FP8B) {
+    // lanes 0 .. 2*NMAT-1: (mat, row block) -> NG = 4 bytes
+    if (lane < 2 * NMAT) {
+      const int m = lane >> 1, rbl = lane & 1;
+      const int64_t rb = (int64_t)c.mat * ((p.N + 31) / 32) + ((nbase >> 5) + rbl);
+      const bool ok = nbase + 32 * rbl < p.N;
+      const uint8_t *sp = p.scale[m] + rb * p.sld + (int64_t)ks * NG;
+      uint32_t v = 0;
+      if (ok && p.svec) {
+        v = __ldg(reinterpret_cast<const uint32_t *>(sp));
+      } else if (ok) {
+#pragma unroll
+        for (int q = 0; q < NG; ++q)
+          if ((int64_t)(ks * NG + q) * GK < p.K) v |= uint32_t(__ldg(sp + q)) << (8 * q);
+      }
+      r.w[0][0] = v;
+    }
+  } else {
+    // rows lane, lane + 32: NG bf16 scales and biases; item 2: x sums for x row `lane`
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int row = lane + 32 * j;
+      const bool ok = nbase + row < p.N;
+      const int64_t o = ((int64_t)c.mat * p.N + nbase + row) * p.sld + (int64_t)ks * NG;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) r.w[j][q] = 0;
+      if (ok) {
+        // NG bf16 -> NG/2 words each for s and b (NG = 4: 2 + 2 words, NG = 2: 1 + 1)
+        if (p.svec) {
+          if (NG == 4) {
+            const uint2 s = __ldg(reinterpret_cast<const uint2 *>(p.aff_s + o));
+            const uint2 b = __ldg(reinterpret_cast<const uint2 *>(p.aff_b + o));
+            r.w[j][0] = s.x; r.w[j][1] = s.y; r.w[j][2] = b.x; r.w[j][3] = b.y;
+          } else {
+            r.w[j][0] = __ldg(reinterpret_cast<const uint32_t *>(p.aff_s + o));
+            r.w[j][2] = __ldg(reinterpret_cast<const uint32_t *>(p.aff_b + o));
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < NG; ++q) {
+            if ((int64_t)(ks * NG + q) * GK >= p.K) continue;
+            r.w[j][q >> 1] |= uint32_t(__ldg(p.aff_s + o + q)) << (16 * (q & 1));
+            r.w[j][2 + (q >> 1)] |= uint32_t(__ldg(p.aff_b + o + q)) << (16 * (q & 1));
+          }
+        }
+      }
+    }
+    // x sums: x row slot `lane` (< NT*8), NG floats kept as raw bits
+#pragma unroll
+    for (int q = 0; q < 4; ++q) r.w[2][q] = 0;
+    if (lane < NT * 8 && lane < c.ntok) {
+      const float *xp = p.xsum + (int64_t)(c.xrow + lane) * (p.K / 64) + (int64_t)ks * NG;
+#pragma unroll
+      for (int q = 0; q < NG; ++q)
+        if ((int64_t)(ks * NG + q) * GK < p.K) r.w[2][q] = __float_as_uint(__ldg(xp + q));
+    }
+  }
+}
+
+template <int WF, int NMAT, int NT>
+__device__ __forceinline__ void scales_store(uint32_t sc_base, int lane, const ScaleRaw<WF, NMAT, NT> &r) {
+  using C = QCfg<WF, NMAT, NT>;
+  constexpr int NG = C::NG;
+  if constexpr (WF == WF_FP4) {
+#pragma unroll
+    for (int j = 0; j < C::PRODUCER_ITEMS; ++j) {
+      const int idx = lane + 32 * j;   // = m * 64 + row
+      const uint32_t a = sc_base + idx * NG * 4;
+      const uint32_t v0 = r.w[j][0], v1 = r.w[j][1];
+      sts128f(a, e8m0_fast(v0), e8m0_fast(v0 >> 8), e8m0_fast(v0 >> 16), e8m0_fast(v0 >> 24));
+      sts128f(a + 16, e8m0_fast(v1), e8m0_fast(v1 >> 8), e8m0_fast(v1 >> 16), e8m0_fast(v1 >> 24));
+    }
+  } else if constexpr (WF == WF_FP8B) {
+    if (lane < 2 * NMAT) {
+      const uint32_t v = r.w[0][0];
+      sts128f(sc_base + lane * 16, e8m0_fast(v), e8m0_fast(v >> 8), e8m0_fast(v >> 16),
+              e8m0_fast(v >> 24));
+    }
+  } else {
+    // layout: s[64][NG], b[64][NG], xs[NT*8][NG]
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int row = lane + 32 * j;
+      const uint32_t as = sc_base + row * NG * 4, ab = sc_base + (QG_ROWS + row) * NG * 4;
+      if (NG == 4) {
+        sts128f(as, bf_bits2f(uint16_t(r.w[j][0])), bf_bits2f(uint16_t(r.w[j][0] >> 16)),
+                bf_bits2f(uint16_t(r.w[j][1])), bf_bits2f(uint16_t(r.w[j][1] >> 16)));
+        sts128f(ab, bf_bits2f(uint16_t(r.w[j][2])), bf_bits2f(uint16_t(r.w[j][2] >> 16)),
+                bf_bits2f(uint16_t(r.w[j][3])), bf_bits2f(uint16_t(r.w[j][3] >> 16)));
+      } else {
+        sts64f(as, bf_bits2f(uint16_t(r.w[j][0])), bf_bits2f(uint16_t(r.w[j][0] >> 16)));
+        sts64f(ab, bf_bits2f(uint16_t(r.w[j][2])), bf_bits2f(uint16_t(r.w[j][2] >> 16)));
+      }
+    }
+    if (lane < NT * 8) {
+      const uint32_t ax = sc_base + (2 * QG_ROWS + lane) * NG * 4;
+      if (NG == 4)
+        sts128f(ax, __uint_as_float(r.w[2][0]), __uint_as_float(r.w[2][1]),
+                __uint_as_float(r.w[2][2]), __uint_as_float(r.w[2][3]));
+      else
+        sts64f(ax, __uint_as_float(r.w[2][0]), __uint_as_float(r.w[2][1]));
+    }
+  }
+}
+
 // ------------------------------------------------------------------ the kernel
 template <int WF, int NMAT, int NT>
-__global__ void __launch_bounds__(QG_THREADS, 2)
+__global__ void __launch_bounds__(QG_THREADS, QG_MIN_CTAS)
     k_qgemv(const __grid_constant__ CUtensorMap wmap0, const __grid_constant__ CUtensorMap wmap1,
             const __grid_constant__ CUtensorMap xmap8, const __grid_constant__ CUtensorMap xmap16,
             const __grid_constant__ CUtensorMap xmap32, const QParams p) {
   using C = QCfg<WF, NMAT, NT>;
-  constexpr int KS = C::KS;
+  constexpr int KS = C::KS, NG = C::NG, ST = C::STAGES;
+  constexpr bool AFF = C::AFF;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~uintptr_t(1023));
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + QG_STAGES * C::STAGE_BYTES);
-  uint64_t *empty = full + QG_STAGES;
+  uint8_t *sc_ring = smem + ST * C::TILE_BYTES;                      // ST x SC_BYTES
+  uint64_t *full = reinterpret_cast<uint64_t *>(sc_ring + ST * C::SC_BYTES);
+  uint64_t *empty = full + ST;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   const int nchunks = p.chunks ? *p.nchunks_dev : p.nchunks_host;
   const int nitems = nchunks * p.tiles * p.nsplit;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < QG_STAGES; ++s) {
-      mbar_init(&full[s], 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&full[s], 33);     // TMA tx arrival + one scale-store arrival per producer lane
       mbar_init(&empty[s], QG_CW);
     }
     fence_barrier_init();
@@ -180,28 +368,37 @@ __global__ void __launch_bounds__(QG_THREADS, 2)
   __syncthreads();
 
   if (warp == QG_CW) {
-    // ---------------------------------------------------------------- producer
+    // ---------------------------------------------------------------- producer warp
     if (lane == 0) {
       prefetch_tmap(&wmap0);
       if (NMAT == 2) prefetch_tmap(&wmap1);
-      const uint64_t pol_w = l2_policy_evict_first();
-      const uint64_t pol_x = l2_policy_evict_last();
-      uint32_t it = 0;
-      for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
-        int chunk, tile, split;
-        QChunk c;
-        decode_chunk(p, item, chunk, tile, split, c);
-        const int kb = int((int64_t)p.kstages * split / p.nsplit);
-        const int ke = int((int64_t)p.kstages * (split + 1) / p.nsplit);
-        const int xr = c.ntok <= 8 ? 8 : (c.ntok <= 16 ? 16 : 32);
-        const CUtensorMap *xm = xr == 8 ? &xmap8 : (xr == 16 ? &xmap16 : &xmap32);
-        const uint32_t bytes = NMAT * C::W_BYTES + C::NBOX * xr * 128;
-        const int32_t wrow = int32_t(c.mat * p.N + (int64_t)tile * QG_ROWS);
-        for (int ks = kb; ks < ke; ++ks, ++it) {
-          const int slot = it % QG_STAGES;
-          const uint32_t ph = (it / QG_STAGES) & 1;
-          if (!mbar_wait(&empty[slot], ph ^ 1)) return;
-          uint8_t *st = smem + slot * C::STAGE_BYTES;
+    }
+    const uint64_t pol_w = l2_policy_evict_first();
+    const uint64_t pol_x = l2_policy_evict_last();
+    uint32_t it = 0;
+    ScaleRaw<WF, NMAT, NT> raw;
+    bool have_raw = false;
+    for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
+      int chunk, tile, split;
+      QChunk c;
+      decode_chunk(p, item, chunk, tile, split, c);
+      const int kb = int((int64_t)p.kstages * split / p.nsplit);
+      const int ke = int((int64_t)p.kstages * (split + 1) / p.nsplit);
+      const int xr = c.ntok <= 8 ? 8 : (c.ntok <= 16 ? 16 : 32);
+      const CUtensorMap *xm = xr == 8 ? &xmap8 : (xr == 16 ? &xmap16 : &xmap32);
+      const uint32_t bytes = NMAT * C::W_BYTES + C::NBOX * xr * 128;
+      const int64_t nbase = (int64_t)tile * QG_ROWS;
+      const int32_t wrow = int32_t(c.mat * p.N + nbase);
+      for (int ks = kb; ks < ke; ++ks, ++it) {
+        const int slot = it % ST;
+        const uint32_t ph = (it / ST) & 1;
+        if (!have_raw) scales_fetch<WF, NMAT, NT>(p, c, nbase, ks, lane, raw);
+        bool ok = true;
+        if (lane == 0) ok = mbar_wait(&empty[slot], ph ^ 1);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) return;
+        uint8_t *st = smem + slot * C::TILE_BYTES;
+        if (lane == 0) {
           mbar_arrive_expect_tx(&full[slot], bytes);
           tma_load_2d(st, &wmap0, &full[slot], ks * 128, wrow, pol_w);
           if (NMAT == 2) tma_load_2d(st + C::W_BYTES, &wmap1, &full[slot], ks * 128, wrow, pol_w);
@@ -210,14 +407,21 @@ __global__ void __launch_bounds__(QG_THREADS, 2)
             tma_load_2d(st + NMAT * C::W_BYTES + b * C::XBOX_BYTES, xm, &full[slot],
                         ks * KS + b * 64, c.xrow, pol_x);
         }
+        scales_store<WF, NMAT, NT>(smem_u32(sc_ring + slot * C::SC_BYTES), lane, raw);
+        // fetch the next stage's scales now (same item) so the loads overlap the wait
+        if (ks + 1 < ke) {
+          scales_fetch<WF, NMAT, NT>(p, c, nbase, ks + 1, lane, raw);
+          have_raw = true;
+        } else {
+          have_raw = false;
+        }
+        mbar_arrive(&full[slot]);      // every lane: its scale stores are in
       }
     }
     return;
   }
 
   // ------------------------------------------------------------------ consumers
-  constexpr int NG = Fmt<WF>::NG;
-  constexpr bool AFF = (WF == WF_AFF4 || WF == WF_AFF8);
   const int g = lane >> 2, t = lane & 3;
   const int ra = wrow_perm<WF>(g);                // smem row (mod 8) of mma rows g, g+8
   const int rowA = warp * 16 + ra;                // tile rows rowA, rowA + 8
@@ -232,11 +436,7 @@ __global__ void __launch_bounds__(QG_THREADS, 2)
     const int kb = int((int64_t)p.kstages * split / p.nsplit);
     const int ke = int((int64_t)p.kstages * (split + 1) / p.nsplit);
     const int64_t nbase = (int64_t)tile * QG_ROWS;              // row within the matrix
-    const int64_t grow0 = (int64_t)c.mat * p.N + nbase + rowA;  // stacked row of mma row g
     const int ntiles_x = (c.ntok + 7) / 8;                      // active n8 tiles
-    const bool rok[2] = {nbase + rowA < p.N, nbase + rowA + 8 < p.N};
-    const int64_t fp8_rb = (int64_t)c.mat * ((p.N + 31) / 32) + ((nbase + warp * 16) >> 5);
-    const bool fp8_ok = nbase + warp * 16 < p.N;
 
     float acc[NMAT][NT][4];
 #pragma unroll
@@ -246,89 +446,49 @@ __global__ void __launch_bounds__(QG_THREADS, 2)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[m][n][i] = 0.0f;
 
-    // per-stage scale operands, loaded one stage ahead (registers double buffer)
-    uint32_t sraw[NMAT][2][NG];    // fp4/fp8: e8m0 byte; affine: bf16 bits (scale)
-    uint32_t braw[2][NG];          // affine: bf16 bits (bias)
-    float xsn[NT][2][NG];          // affine: sums of x over the group per column
-    auto load_scales = [&](int ks, uint32_t (&so)[NMAT][2][NG], uint32_t (&bo)[2][NG],
-                           float (&xo)[NT][2][NG]) {
-      if constexpr (WF == WF_FP4) {
-#pragma unroll
-        for (int m = 0; m < NMAT; ++m)
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const uint8_t *sp = p.scale[m] + (grow0 + 8 * h) * p.sld + (int64_t)ks * NG;
-#pragma unroll
-            for (int q = 0; q < NG; ++q) so[m][h][q] = rok[h] ? __ldg(sp + q) : 0u;
-          }
-      } else if constexpr (WF == WF_FP8B) {
-#pragma unroll
-        for (int m = 0; m < NMAT; ++m) {
-          const uint8_t *sp = p.scale[m] + fp8_rb * p.sld + (int64_t)ks * NG;
-#pragma unroll
-          for (int q = 0; q < NG; ++q) {
-            so[m][0][q] = fp8_ok ? __ldg(sp + q) : 0u;
-            so[m][1][q] = so[m][0][q];
-          }
-        }
-      } else {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int64_t o = (grow0 + 8 * h) * p.sld + (int64_t)ks * NG;
-#pragma unroll
-          for (int q = 0; q < NG; ++q) {
-            so[0][h][q] = rok[h] ? __ldg(p.aff_s + o + q) : 0u;
-            bo[h][q] = rok[h] ? __ldg(p.aff_b + o + q) : 0u;
-          }
-        }
-#pragma unroll
-        for (int n = 0; n < NT; ++n)
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const int slotx = n * 8 + cs[j];
-            const bool ok = slotx < c.ntok;
-            const float *xp = p.xsum + (int64_t)(c.xrow + slotx) * (p.K / 64) + (int64_t)ks * NG;
-#pragma unroll
-            for (int q = 0; q < NG; ++q) xo[n][j][q] = ok ? __ldg(xp + q) : 0.0f;
-          }
-      }
-    };
-    if (kb < ke) load_scales(kb, sraw, braw, xsn);
-
     for (int ks = kb; ks < ke; ++ks, ++it) {
-      const int slot = it % QG_STAGES;
-      const uint32_t ph = (it / QG_STAGES) & 1;
-      float sc[NMAT][2][NG];
-      float bi[2][NG];
-      float xs[NT][2][NG];
-#pragma unroll
-      for (int m = 0; m < NMAT; ++m)
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-#pragma unroll
-          for (int q = 0; q < NG; ++q)
-            sc[m][h][q] = AFF ? bf_bits2f(uint16_t(sraw[m][h][q])) : e8m0f(sraw[m][h][q]);
-      if constexpr (AFF) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-#pragma unroll
-          for (int q = 0; q < NG; ++q) bi[h][q] = bf_bits2f(uint16_t(braw[h][q]));
-#pragma unroll
-        for (int n = 0; n < NT; ++n)
-#pragma unroll
-          for (int j = 0; j < 2; ++j)
-#pragma unroll
-            for (int q = 0; q < NG; ++q) xs[n][j][q] = xsn[n][j][q];
-      }
-      if (ks + 1 < ke) load_scales(ks + 1, sraw, braw, xsn);   // prefetch next stage
-
+      const int slot = it % ST;
+      const uint32_t ph = (it / ST) & 1;
       if (!mbar_wait(&full[slot], ph)) return;
-      const uint32_t st = smem_u32(smem + slot * C::STAGE_BYTES);
+      const uint32_t st = smem_u32(smem + slot * C::TILE_BYTES);
       const uint32_t xst = st + NMAT * C::W_BYTES;
+      const uint32_t scb = smem_u32(sc_ring + slot * C::SC_BYTES);
 
 #pragma unroll
       for (int grp = 0; grp < NG; ++grp) {
         constexpr int STEPS = Fmt<WF>::GK / 16;
+        // ---- this group's scale operands (fp32, staged by the producer) ----
+        float sc[NMAT][2];
+        float bi[2];
+        float xs[NT][2];
+        if constexpr (WF == WF_FP4) {
+#pragma unroll
+          for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const uint32_t a = scb + ((m * QG_ROWS + rowA + 8 * h) * NG + grp) * 4;
+              sc[m][h] = __uint_as_float(lds32(a));
+            }
+        } else if constexpr (WF == WF_FP8B) {
+#pragma unroll
+          for (int m = 0; m < NMAT; ++m) {
+            const float v = __uint_as_float(lds32(scb + ((m * 2 + (warp >> 1)) * NG + grp) * 4));
+            sc[m][0] = v;
+            sc[m][1] = v;
+          }
+        } else {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            sc[0][h] = __uint_as_float(lds32(scb + ((rowA + 8 * h) * NG + grp) * 4));
+            bi[h] = __uint_as_float(lds32(scb + ((QG_ROWS + rowA + 8 * h) * NG + grp) * 4));
+          }
+#pragma unroll
+          for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+              xs[n][j] = __uint_as_float(lds32(scb + ((2 * QG_ROWS + n * 8 + cs[j]) * NG + grp) * 4));
+        }
+        // ---- A fragments: [mat][step][4 regs] ----
         uint32_t a[NMAT][STEPS][4];
 #pragma unroll
         for (int m = 0; m < NMAT; ++m) {
@@ -388,6 +548,7 @@ __global__ void __launch_bounds__(QG_THREADS, 2)
             }
           }
         }
+        // ---- B fragments and MMA per n8 tile ----
 #pragma unroll
         for (int n = 0; n < NT; ++n) {
           if (n >= ntiles_x) break;
@@ -412,15 +573,15 @@ __global__ void __launch_bounds__(QG_THREADS, 2)
             for (int s2 = 0; s2 < STEPS; ++s2)
               mma_f16(d, a[m][s2][0], a[m][s2][1], a[m][s2][2], a[m][s2][3], b[s2][0], b[s2][1]);
             // fold the group scale (and the affine bias times the group's x sum)
-            acc[m][n][0] = __fmaf_rn(d[0], sc[m][0][grp], acc[m][n][0]);
-            acc[m][n][1] = __fmaf_rn(d[1], sc[m][0][grp], acc[m][n][1]);
-            acc[m][n][2] = __fmaf_rn(d[2], sc[m][1][grp], acc[m][n][2]);
-            acc[m][n][3] = __fmaf_rn(d[3], sc[m][1][grp], acc[m][n][3]);
+            acc[m][n][0] = __fmaf_rn(d[0], sc[m][0], acc[m][n][0]);
+            acc[m][n][1] = __fmaf_rn(d[1], sc[m][0], acc[m][n][1]);
+            acc[m][n][2] = __fmaf_rn(d[2], sc[m][1], acc[m][n][2]);
+            acc[m][n][3] = __fmaf_rn(d[3], sc[m][1], acc[m][n][3]);
             if constexpr (AFF) {
-              acc[m][n][0] = __fmaf_rn(bi[0][grp], xs[n][0][grp], acc[m][n][0]);
-              acc[m][n][1] = __fmaf_rn(bi[0][grp], xs[n][1][grp], acc[m][n][1]);
-              acc[m][n][2] = __fmaf_rn(bi[1][grp], xs[n][0][grp], acc[m][n][2]);
-              acc[m][n][3] = __fmaf_rn(bi[1][grp], xs[n][1][grp], acc[m][n][3]);
+              acc[m][n][0] = __fmaf_rn(bi[0], xs[n][0], acc[m][n][0]);
+              acc[m][n][1] = __fmaf_rn(bi[0], xs[n][1], acc[m][n][1]);
+              acc[m][n][2] = __fmaf_rn(bi[1], xs[n][0], acc[m][n][2]);
+              acc[m][n][3] = __fmaf_rn(bi[1], xs[n][1], acc[m][n][3]);
             }
           }
         }
