@@ -277,15 +277,27 @@ int weight_map(CUtensorMap *m, const void *w, int64_t rows, int64_t row_bytes) {
                       (uint64_t)row_bytes, 128, QG_ROWS);
 }
 
+// K splits per tile: the smallest split count whose items fill the resident CTA
+// slots in whole waves at >= 85% (items / (waves * slots)), else the best one;
+// splits keep >= 4 K stages each.
 int pick_nsplit(int64_t base_items, int kstages) {
-  const int64_t target = QG_MIN_CTAS * (int64_t)num_sms();
-  int64_t ns = (target + base_items - 1) / base_items;
-  int64_t cap = kstages / 2;
+  const int64_t slots = QG_MIN_CTAS * (int64_t)num_sms();
+  int64_t cap = kstages / 4;
   if (cap < 1) cap = 1;
-  if (ns > cap) ns = cap;
-  if (ns > QG_MAX_SPLIT) ns = QG_MAX_SPLIT;
-  if (ns < 1) ns = 1;
-  return int(ns);
+  if (cap > QG_MAX_SPLIT) cap = QG_MAX_SPLIT;
+  int64_t best = 1;
+  double best_eff = -1.0;
+  for (int64_t ns = 1; ns <= cap; ++ns) {
+    const int64_t items = base_items * ns;
+    const int64_t waves = (items + slots - 1) / slots;
+    const double eff = double(items) / double(waves * slots);
+    if (eff >= 0.85) return int(ns);
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      best = ns;
+    }
+  }
+  return int(best);
 }
 
 struct GemvWs {
@@ -361,6 +373,7 @@ int gemv_common(const void *x, int64_t M, int64_t K, const void *w, int64_t w_ro
   p.chunks = nullptr;
   p.nchunks_host = int(nch);
   p.dense_m = int(M);
+  p.dense_rows = 32;
   p.epi = out_dtype == DSV41_F32 ? EPI_STORE_F32 : EPI_STORE_BF16;
   p.out = y;
   p.ldo = N;
@@ -537,12 +550,13 @@ MoeWs moe_carve(const MoeDims &d, void *base, size_t cap) {
   const size_t frag2 = 32 * QG_CW * 2 * 4 * 4, frag4 = 32 * QG_CW * 4 * 4;  // NMAT*NT*4 floats
   w.part_gu = wc.take<float>(d.Cmax * d.tiles_gu * QG_MAX_SPLIT * frag2);
   w.part_dn = wc.take<float>(d.Cmax * d.tiles_dn * QG_MAX_SPLIT * frag4);
-  w.part_sgu = wc.take<float>(ceil_div(d.T, 32) * d.tiles_gu * QG_MAX_SPLIT * 32 * QG_CW * 2 * 4 * 4);
-  w.part_sdn = wc.take<float>(ceil_div(d.T, 16) * d.tiles_dn * QG_MAX_SPLIT * frag4);
+  // shared expert: at most ceil(T/8) gate/up and ceil(T/4) down chunks, <= 2*4*4 floats each
+  w.part_sgu = wc.take<float>(ceil_div(d.T, 8) * d.tiles_gu * QG_MAX_SPLIT * 32 * QG_CW * 2 * 4 * 4);
+  w.part_sdn = wc.take<float>(ceil_div(d.T, 4) * d.tiles_dn * QG_MAX_SPLIT * frag4);
   w.cnt_gu = wc.take<int>(d.Cmax * d.tiles_gu);
   w.cnt_dn = wc.take<int>(d.Cmax * d.tiles_dn);
-  w.cnt_sgu = wc.take<int>(ceil_div(d.T, 32) * d.tiles_gu);
-  w.cnt_sdn = wc.take<int>(ceil_div(d.T, 16) * d.tiles_dn);
+  w.cnt_sgu = wc.take<int>(ceil_div(d.T, 8) * d.tiles_gu);
+  w.cnt_sdn = wc.take<int>(ceil_div(d.T, 4) * d.tiles_dn);
   w.used = wc.off + 256;
   w.ok = wc.ok;
   return w;
@@ -576,11 +590,36 @@ int moe_check(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, int64_t T
   return DSV41_OK;
 }
 
-// Routed experts (SwitchGLU) for given indices -> Y[t*k + j, :] fp32, and the
-// shared expert -> Ys when `shared`.
+// Per (host thread, device) side stream and events used to run the shared
+// expert concurrently with the routed experts (fork / join on the caller's stream,
+// which also works while the caller's stream is being captured into a graph).
+struct SideStream {
+  cudaStream_t s = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+static thread_local SideStream g_side[64];
+
+int side_stream(SideStream **out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
+  DSV41_REQUIRE(dev >= 0 && dev < 64, DSV41_ERR_UNSUPPORTED, "device index %d >= 64", dev);
+  SideStream &s = g_side[dev];
+  if (!s.s) {
+    e = cudaStreamCreateWithFlags(&s.s, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s.fork, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s.join, cudaEventDisableTiming);
+    if (e != cudaSuccess) return cuda_status(e, "side stream");
+  }
+  *out = &s;
+  return DSV41_OK;
+}
+
+// Routed experts (SwitchGLU) for given indices -> Y[t*k + j, :] fp32 on `st`, and
+// the shared expert -> Ys on `st_shared` when `shared`.
 int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, const void *x,
                      const MoeDims &d, MoeWs &ws, const int32_t *idx, float *Y, bool shared,
-                     cudaStream_t st) {
+                     cudaStream_t st, cudaStream_t st_shared) {
   const int64_t T = d.T;
   const int round = (cfg->flags & DSV41_MOE_ROUND_BF16) ? 1 : 0;
   int rc;
@@ -660,7 +699,8 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
     if (rc) return rc;
   }
   if (!shared) return DSV41_OK;
-  // shared expert (fp8 32x32): gate/up -> Hs -> down -> Ys
+  // shared expert (fp8 32x32): gate/up -> Hs -> down -> Ys, on its own stream
+  st = st_shared;
   { ProfScope prof("qx_prep", st);
   k_qx_prep<<<unsigned(T), 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16 *>(x), T, d.D,
                                           nullptr, nullptr, ws.x16, ws.xs, nullptr, 0); }
@@ -671,6 +711,9 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
   if ((rc = weight_map(&m_s2, W->sw2, d.D, d.I))) return rc;
   if ((rc = make_x_maps(xs, ws.x16, d.T, d.D))) return rc;
   if ((rc = make_x_maps(hs, ws.Hs, 2 * d.Tp, d.I))) return rc;
+  // The shared expert's chunks depend only on T (dense chunk mode), so it never
+  // reads the routed plan and can run concurrently with it.
+  const int nts = T <= 8 ? 1 : (T <= 16 ? 2 : 4);     // n8 tiles per chunk
   {
     QParams p{};
     p.scale[0] = W->ss1;
@@ -680,11 +723,14 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
     p.sld = ceil_div(d.D, 32);
     p.tiles = int(d.tiles_gu);
     p.kstages = int(ceil_div(d.D, Fmt<WF_FP8B>::KS));
-    const int64_t nch = ceil_div(T, 32);
+    const int64_t nch = ceil_div(T, 8 * nts);
     p.nsplit = pick_nsplit(nch * d.tiles_gu, p.kstages);
     p.xscale = ws.xs;
-    p.chunks = ws.plan.sgu_chunks;
-    p.nchunks_dev = ws.plan.counts + 3;
+    p.chunks = nullptr;
+    p.nchunks_host = int(nch);
+    p.dense_m = int(T);
+    p.dense_rows = 8 * nts;
+    p.dense_down = 0;
     p.epi = EPI_SWIGLU;
     p.out = ws.Hs;
     p.ldo = d.I;
@@ -697,8 +743,13 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
       cudaError_t e = cudaMemsetAsync(ws.cnt_sgu, 0, sizeof(int) * nch * d.tiles_gu, st);
       if (e != cudaSuccess) return cuda_status(e, "memset");
     }
-    rc = qgemv_launch<WF_FP8B, 2, 4>("moe_shared_gate_up_fp8", m_s1, m_s3, xs[0], xs[1], xs[2], p,
-                                      int(nch * d.tiles_gu * p.nsplit), st);
+    const int items = int(nch * d.tiles_gu * p.nsplit);
+    if (nts == 1)
+      rc = qgemv_launch<WF_FP8B, 2, 1>("moe_shared_gate_up_fp8", m_s1, m_s3, xs[0], xs[1], xs[2], p, items, st);
+    else if (nts == 2)
+      rc = qgemv_launch<WF_FP8B, 2, 2>("moe_shared_gate_up_fp8", m_s1, m_s3, xs[0], xs[1], xs[2], p, items, st);
+    else
+      rc = qgemv_launch<WF_FP8B, 2, 4>("moe_shared_gate_up_fp8", m_s1, m_s3, xs[0], xs[1], xs[2], p, items, st);
     if (rc) return rc;
   }
   {
@@ -710,11 +761,14 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
     p.sld = ceil_div(d.I, 32);
     p.tiles = int(d.tiles_dn);
     p.kstages = int(ceil_div(d.I, Fmt<WF_FP8B>::KS));
-    const int64_t nch = ceil_div(T, 16);
+    const int64_t nch = ceil_div(T, 4 * nts);          // 8*nts H rows = 4*nts tokens
     p.nsplit = pick_nsplit(nch * d.tiles_dn, p.kstages);
     p.xscale = nullptr;
-    p.chunks = ws.plan.sdn_chunks;
-    p.nchunks_dev = ws.plan.counts + 4;
+    p.chunks = nullptr;
+    p.nchunks_host = int(nch);
+    p.dense_m = int(T);
+    p.dense_rows = 8 * nts;
+    p.dense_down = 1;
     p.epi = EPI_DOWN;
     p.out = ws.Ys;
     p.ldo = d.D;
@@ -727,8 +781,13 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
       cudaError_t e = cudaMemsetAsync(ws.cnt_sdn, 0, sizeof(int) * nch * d.tiles_dn, st);
       if (e != cudaSuccess) return cuda_status(e, "memset");
     }
-    rc = qgemv_launch<WF_FP8B, 1, 4>("moe_shared_down_fp8", m_s2, m_s2, hs[0], hs[1], hs[2], p,
-                                      int(nch * d.tiles_dn * p.nsplit), st);
+    const int items = int(nch * d.tiles_dn * p.nsplit);
+    if (nts == 1)
+      rc = qgemv_launch<WF_FP8B, 1, 1>("moe_shared_down_fp8", m_s2, m_s2, hs[0], hs[1], hs[2], p, items, st);
+    else if (nts == 2)
+      rc = qgemv_launch<WF_FP8B, 1, 2>("moe_shared_down_fp8", m_s2, m_s2, hs[0], hs[1], hs[2], p, items, st);
+    else
+      rc = qgemv_launch<WF_FP8B, 1, 4>("moe_shared_down_fp8", m_s2, m_s2, hs[0], hs[1], hs[2], p, items, st);
     if (rc) return rc;
   }
   return DSV41_OK;
@@ -747,7 +806,7 @@ extern "C" int dsv41_moe_experts(const dsv41_moe_config *cfg, const dsv41_moe_we
   MoeWs ws = moe_carve(d, workspace, workspace_bytes);
   DSV41_REQUIRE(ws.ok && ws.used <= workspace_bytes, DSV41_ERR_WORKSPACE,
                 "workspace too small: need %zu bytes", ws.used);
-  return moe_experts_impl(cfg, W, x, d, ws, indices, y, false, STREAM(stream));
+  return moe_experts_impl(cfg, W, x, d, ws, indices, y, false, STREAM(stream), STREAM(stream));
 }
 
 extern "C" int dsv41_moe_decode(const dsv41_moe_config *cfg, const dsv41_moe_weights *W,
@@ -770,11 +829,26 @@ extern "C" int dsv41_moe_decode(const dsv41_moe_config *cfg, const dsv41_moe_wei
   cudaStream_t st = STREAM(stream);
   float *wts = weights_out ? weights_out : ws.w;
   int32_t *idx = indices_out ? indices_out : ws.idx;
+  // the shared expert does not depend on routing: fork it onto the side stream
+  SideStream *side = nullptr;
+  cudaStream_t st_shared = st;
+  if (shared) {
+    if ((rc = side_stream(&side))) return rc;
+    cudaError_t e = cudaEventRecord(side->fork, st);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(side->s, side->fork, 0);
+    if (e != cudaSuccess) return cuda_status(e, "fork shared expert");
+    st_shared = side->s;
+  }
   rc = route_impl(x, T, d.D, W->gate_w, W->gate_bias, d.E, cfg->topk, cfg->score_func,
                   cfg->gate_temp, cfg->norm_topk_prob, cfg->route_scale, wts, idx, ws.rpart, st);
   if (rc) return rc;
-  rc = moe_experts_impl(cfg, W, x, d, ws, idx, ws.Y, shared, st);
+  rc = moe_experts_impl(cfg, W, x, d, ws, idx, ws.Y, shared, st, st_shared);
   if (rc) return rc;
+  if (shared) {
+    cudaError_t e = cudaEventRecord(side->join, side->s);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(st, side->join, 0);
+    if (e != cudaSuccess) return cuda_status(e, "join shared expert");
+  }
   const int64_t n = T * d.D;
   ProfScope prof("moe_combine", st);
   if (out_dtype == DSV41_F32)
@@ -969,6 +1043,7 @@ extern "C" int dsv41_gemv_fp8_block_noalloc(const void *x, int64_t M, int64_t K,
   p.chunks = nullptr;
   p.nchunks_host = 1;
   p.dense_m = int(M);
+  p.dense_rows = 32;
   p.epi = out_dtype == DSV41_F32 ? EPI_STORE_F32 : EPI_STORE_BF16;
   p.out = y;
   p.ldo = N;

@@ -26,8 +26,9 @@ struct MoePlan {
 constexpr int MOE_GU_CHUNK = 8;
 constexpr int MOE_DN_CHUNK = 4;
 
-// One CTA of 1024 threads.  Deterministic: a pair's rank inside its expert is
-// the number of earlier pairs (row-major over [T, k]) routed to the same expert.
+// One CTA of 1024 threads (E <= 1024).  Deterministic: a pair's rank inside its
+// expert is the number of earlier pairs (row-major over [T, k]) routed to the same
+// expert.  Offsets come from block-wide exclusive scans over the experts.
 __global__ void __launch_bounds__(1024) k_moe_plan(const int32_t *__restrict__ indices, int64_t T,
                                                    int topk, int64_t E, MoePlan plan) {
   extern __shared__ int sh[];
@@ -35,52 +36,73 @@ __global__ void __launch_bounds__(1024) k_moe_plan(const int32_t *__restrict__ i
   int *poff = sh + E;       // [E] padded pair offset
   int *coff = sh + 2 * E;   // [E] gate/up chunk offset
   int *doff = sh + 3 * E;   // [E] down chunk offset
+  __shared__ int wtot[3][32];
   const int64_t P = T * topk;
-  for (int64_t e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+  const int e = threadIdx.x, lane = e & 31, wid = e >> 5;
+  if (e < E) cnt[e] = 0;
   __syncthreads();
   for (int64_t p = threadIdx.x; p < P; p += blockDim.x) {
-    const int e = indices[p];
-    if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+    const int ex = indices[p];
+    if (ex >= 0 && ex < E) atomicAdd(&cnt[ex], 1);
     else dev_flag(DSV41_DEVST_BAD_INDEX);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int po = 0, co = 0, dn = 0;
-    for (int64_t e = 0; e < E; ++e) {
-      poff[e] = po;
-      coff[e] = co;
-      doff[e] = dn;
-      po += (cnt[e] + 3) & ~3;
-      co += (cnt[e] + MOE_GU_CHUNK - 1) / MOE_GU_CHUNK;
-      dn += (cnt[e] + MOE_DN_CHUNK - 1) / MOE_DN_CHUNK;
+  const int n = e < E ? cnt[e] : 0;
+  int v[3] = {(n + 3) & ~3, (n + MOE_GU_CHUNK - 1) / MOE_GU_CHUNK,
+              (n + MOE_DN_CHUNK - 1) / MOE_DN_CHUNK};
+  int inc[3] = {v[0], v[1], v[2]};
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      const int u = __shfl_up_sync(0xffffffffu, inc[k], o);
+      if (lane >= o) inc[k] += u;
     }
-    plan.counts[0] = co;
-    plan.counts[1] = dn;
-    plan.counts[2] = po;
-    const int sgu = int((T + 31) / 32), sdn = int((T + 15) / 16);
-    plan.counts[3] = sgu;
-    plan.counts[4] = sdn;
-    for (int c = 0; c < sgu; ++c)
-      plan.sgu_chunks[c] = QChunk{0, 32 * c, int(T - 32 * c < 32 ? T - 32 * c : 32), 32 * c};
-    for (int c = 0; c < sdn; ++c) {
-      const int nt = int(T - 16 * c < 16 ? T - 16 * c : 16);
-      plan.sdn_chunks[c] = QChunk{0, 32 * c, 8 * ((nt + 3) / 4), 16 * c};
+  }
+  if (lane == 31) {
+#pragma unroll
+    for (int k = 0; k < 3; ++k) wtot[k][wid] = inc[k];
+  }
+  __syncthreads();
+  if (wid == 0) {
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      const int nw = blockDim.x >> 5;
+      int t = lane < nw ? wtot[k][lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, t, o);
+        if (lane >= o) t += u;
+      }
+      wtot[k][lane] = t;                       // inclusive prefix over warps
     }
   }
   __syncthreads();
+  int excl[3];
+#pragma unroll
+  for (int k = 0; k < 3; ++k) excl[k] = inc[k] - v[k] + (wid > 0 ? wtot[k][wid - 1] : 0);
+  if (e < E) {
+    poff[e] = excl[0];
+    coff[e] = excl[1];
+    doff[e] = excl[2];
+  }
+  if (e == blockDim.x - 1) {
+    plan.counts[0] = excl[1] + v[1];
+    plan.counts[1] = excl[2] + v[2];
+    plan.counts[2] = excl[0] + v[0];
+  }
+  __syncthreads();
   // chunks and padding slots, one thread per expert
-  for (int64_t e = threadIdx.x; e < E; e += blockDim.x) {
-    const int n = cnt[e];
-    if (n == 0) continue;
+  if (e < E && n > 0) {
     for (int c = 0; c * MOE_GU_CHUNK < n; ++c) {
       const int q0 = poff[e] + c * MOE_GU_CHUNK;
       const int np = min(MOE_GU_CHUNK, n - c * MOE_GU_CHUNK);
-      plan.gu_chunks[coff[e] + c] = QChunk{int(e), q0, np, q0};
+      plan.gu_chunks[coff[e] + c] = QChunk{e, q0, np, q0};
     }
     for (int c = 0; c * MOE_DN_CHUNK < n; ++c) {
       const int q0 = poff[e] + c * MOE_DN_CHUNK;   // multiple of 4: H rows 2*q0 ..
       const int np = min(MOE_DN_CHUNK, n - c * MOE_DN_CHUNK);
-      plan.dn_chunks[doff[e] + c] = QChunk{int(e), 2 * q0, 8 * ((np + 3) / 4), q0};
+      plan.dn_chunks[doff[e] + c] = QChunk{e, 2 * q0, 8 * ((np + 3) / 4), q0};
     }
     for (int q = poff[e] + n; q < poff[e] + ((n + 3) & ~3); ++q) {
       plan.pair_tok[q] = -1;
@@ -89,11 +111,11 @@ __global__ void __launch_bounds__(1024) k_moe_plan(const int32_t *__restrict__ i
   }
   // pair placement
   for (int64_t p = threadIdx.x; p < P; p += blockDim.x) {
-    const int e = indices[p];
-    if (e < 0 || e >= E) continue;
+    const int ex = indices[p];
+    if (ex < 0 || ex >= E) continue;
     int rank = 0;
-    for (int64_t p2 = 0; p2 < p; ++p2) rank += (indices[p2] == e);
-    const int q = poff[e] + rank;
+    for (int64_t p2 = 0; p2 < p; ++p2) rank += (indices[p2] == ex);
+    const int q = poff[ex] + rank;
     plan.pair_tok[q] = int(p / topk);
     plan.pair_row[q] = int(p);
   }

@@ -76,7 +76,9 @@ struct QParams {
   const QChunk *chunks;        // null -> dense
   const int *nchunks_dev;
   int nchunks_host;            // dense: number of chunks
-  int dense_m;                 // dense: total x rows
+  int dense_m;                 // dense: total x rows (tokens for dense_down)
+  int dense_rows;              // dense: x rows per chunk (NT*8)
+  int dense_down;              // dense: x rows are hi/lo H rows of dense_rows/2 tokens
   int epi;
   void *out;
   int64_t ldo;
@@ -186,11 +188,20 @@ __device__ __forceinline__ void decode_chunk(const QParams &p, int item, int &ch
   split = rem % p.nsplit;
   if (p.chunks) {
     c = p.chunks[chunk];
-  } else {
+  } else if (!p.dense_down) {
     c.mat = 0;
-    c.xrow = chunk * 32;  // dense chunks are 32 rows apart (NT <= 4)
-    c.ntok = min(32, p.dense_m - c.xrow);
+    c.xrow = chunk * p.dense_rows;
+    c.ntok = min(p.dense_rows, p.dense_m - c.xrow);
     c.orow = c.xrow;
+  } else {
+    // H rows of tokens q0 .. q0 + dense_rows/2: hi/lo halves in blocks of 4 tokens
+    const int per = p.dense_rows / 2;
+    const int q0 = chunk * per;
+    const int nt = min(per, p.dense_m - q0);
+    c.mat = 0;
+    c.xrow = 2 * q0;
+    c.ntok = 8 * ((nt + 3) / 4);
+    c.orow = q0;
   }
 }
 
@@ -621,10 +632,11 @@ __global__ void __launch_bounds__(QG_THREADS, QG_MIN_CTAS)
         for (int n = 0; n < NT; ++n)
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
+            const float *src = p.partial + (int64_t)tile_id * p.nsplit * (CT * C::FRAG) +
+                               ((m * NT + n) * 4 + i) * CT + ctid;
             float v = 0.0f;
-            for (int sp = 0; sp < p.nsplit; ++sp)
-              v += __ldcg(p.partial + ((int64_t)tile_id * p.nsplit + sp) * (CT * C::FRAG) +
-                          ((m * NT + n) * 4 + i) * CT + ctid);
+#pragma unroll 8
+            for (int sp = 0; sp < p.nsplit; ++sp) v += __ldcg(src + (int64_t)sp * (CT * C::FRAG));
             acc[m][n][i] = v;
           }
     }
@@ -700,21 +712,30 @@ __global__ void __launch_bounds__(QG_THREADS, QG_MIN_CTAS)
 // of the scaled values.  bf16 values are exact in f16 within 2^29 of the row max;
 // smaller ones keep an absolute error below 2^-39 of the max.  perm selects the
 // per-16 k order the affine decode expects (0 none, 4 aff4, 8 aff8).
-// One CTA (256 threads) per row; optional gather: row r reads x[gather[r]].
-__global__ void k_qx_prep(const __nv_bfloat16 *__restrict__ x, int64_t M, int64_t K,
-                          const int32_t *__restrict__ gather, const int *__restrict__ nrows_dev,
-                          __half *__restrict__ xq, float *__restrict__ xscale,
-                          float *__restrict__ xsum, int perm) {
+// One CTA (256 threads) per row, 16-byte vectors (K % 8 == 0); optional gather:
+// row r reads x[gather[r]] (-1 = zero row).
+__global__ void __launch_bounds__(256) k_qx_prep(const __nv_bfloat16 *__restrict__ x, int64_t M,
+                                                 int64_t K, const int32_t *__restrict__ gather,
+                                                 const int *__restrict__ nrows_dev,
+                                                 __half *__restrict__ xq, float *__restrict__ xscale,
+                                                 float *__restrict__ xsum, int perm) {
   const int64_t r = blockIdx.x;
   const int64_t nrows = nrows_dev ? *nrows_dev : M;
   if (r >= nrows) return;
-  int64_t src = gather ? gather[r] : r;
+  const int64_t src = gather ? gather[r] : r;
   __shared__ float red[8];
-  __shared__ float s_scale;
+  __shared__ float s_inv;
+  const int64_t nv = K / 8;
+  const uint4 *xv = reinterpret_cast<const uint4 *>(x + (src >= 0 ? src : 0) * K);
   float amax = 0.0f;
   if (src >= 0) {
-    const __nv_bfloat16 *xr = x + src * K;
-    for (int64_t k = threadIdx.x; k < K; k += blockDim.x) amax = fmaxf(amax, fabsf(__bfloat162float(xr[k])));
+    for (int64_t i = threadIdx.x; i < nv; i += blockDim.x) {
+      const uint4 v = __ldg(xv + i);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        amax = fmaxf(amax, fmaxf(fabsf(bf_bits2f(uint16_t(w[j]))), fabsf(bf_bits2f(uint16_t(w[j] >> 16)))));
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -726,35 +747,48 @@ __global__ void k_qx_prep(const __nv_bfloat16 *__restrict__ x, int64_t M, int64_
     int E = 0;
     if (m > 0.0f && m < INFINITY) E = int((__float_as_uint(m) >> 23) & 0xFF) - 127 - 14;
     if (E < -126) E = -126;
-    s_scale = ldexpf(1.0f, E);
-    xscale[r] = s_scale;
+    xscale[r] = ldexpf(1.0f, E);
+    s_inv = ldexpf(1.0f, -E);                      // exact power of two
   }
   __syncthreads();
-  const float inv = 1.0f / s_scale;  // exact power of two
-  for (int64_t k = threadIdx.x; k < K; k += blockDim.x) {
-    const float v = src >= 0 ? __bfloat162float(x[src * K + k]) : 0.0f;
-    int64_t dk = k;
-    if (perm == 4) {  // aff4 order per 16: [0,4,1,5,2,6,3,7, 8,12,9,13,10,14,11,15]
-      const int64_t b16 = k & ~int64_t(15), w = k & 15, half8 = w & 8, i = w & 7;
-      dk = b16 + half8 + ((i & 3) << 1) + (i >> 2);
-    } else if (perm == 8) {  // aff8 order per 4: [0,2,1,3]
-      const int64_t b4 = k & ~int64_t(3), i = k & 3;
-      dk = b4 + ((i & 1) << 1) + (i >> 1);
-    }
-    xq[r * K + dk] = __float2half_rn(v * inv);
-  }
-  if (xsum) {
-    // per-64 sums of the scaled f16 values, in fp32 (one warp per group)
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    for (int64_t gi = wid; gi < K / 64; gi += (blockDim.x >> 5)) {
-      float s = 0.0f;
-      for (int j = lane; j < 64; j += 32) {
-        const float v = src >= 0 ? __bfloat162float(x[src * K + gi * 64 + j]) : 0.0f;
-        s += __half2float(__float2half_rn(v * inv));
-      }
+  const float inv = s_inv;
+  uint4 *qv = reinterpret_cast<uint4 *>(xq + r * K);
+  for (int64_t i = threadIdx.x; i < nv; i += blockDim.x) {
+    float f[8];
+    if (src >= 0) {
+      const uint4 v = __ldg(xv + i);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if (lane == 0) xsum[r * (K / 64) + gi] = s;
+      for (int j = 0; j < 4; ++j) {
+        f[2 * j] = bf_bits2f(uint16_t(w[j])) * inv;
+        f[2 * j + 1] = bf_bits2f(uint16_t(w[j] >> 16)) * inv;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[j] = 0.0f;
+    }
+    __half h[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      // destination position inside the 8-vector for the affine k orders:
+      // aff4: [0,4,1,5,2,6,3,7] per 8 (the 16-k block order is per half), aff8: [0,2,1,3] per 4
+      int dj = j;
+      if (perm == 4) dj = ((j & 3) << 1) | (j >> 2);
+      else if (perm == 8) dj = (j & 4) | ((j & 1) << 1) | ((j >> 1) & 1);
+      h[dj] = __float2half_rn(f[j]);
+    }
+    qv[i] = *reinterpret_cast<uint4 *>(h);
+    if (xsum) {
+      // per-64 sums of the f16 values: vectors 8g .. 8g+7 form group g (8 lanes)
+      float s = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s += __half2float(h[j]);
+      // the 8 lanes of a group are active together (K % 64 == 0); a warp may be partial
+      const unsigned gmask = 0xFFu << (threadIdx.x & 24);
+      s += __shfl_xor_sync(gmask, s, 1);
+      s += __shfl_xor_sync(gmask, s, 2);
+      s += __shfl_xor_sync(gmask, s, 4);
+      if ((threadIdx.x & 7) == 0) xsum[r * (K / 64) + i / 8] = s;
     }
   }
 }

@@ -126,9 +126,17 @@ class SharedExpert:
 
 
 class MoE:
-    """moe.py:96-112 (decode path: up to 4096 tokens per call)."""
+    """moe.py:96-112 (decode path: up to 4096 tokens per call).
 
-    def __init__(self, args, round_bf16: bool = True):
+    With ``cuda_graph=True`` (default) each (tokens, output dtype, device) shape is
+    captured once into a CUDA graph (router, plan, expert kernels, shared expert
+    on a forked stream, combine) and replayed; the graph owns its input/output
+    buffers and workspace and is rebuilt if any weight tensor is replaced.
+    Outputs are fresh tensors (copies of the graph's buffers), as the reference's
+    functional API returns new arrays.
+    """
+
+    def __init__(self, args, round_bf16: bool = True, cuda_graph: bool = True):
         self.args = args
         self.dim = args.dim
         self.gate = Gate(args)
@@ -137,7 +145,58 @@ class MoE:
         self.experts._owner = self
         self.shared_experts = SharedExpert(args.dim, args.moe_inter_dim, args.swiglu_limit)
         self.round_bf16 = round_bf16
+        self.cuda_graph = cuda_graph
         self._ws = None
+        self._graphs = {}
+        self._graph_sig = None
+
+    def _sig(self):
+        e, s = self.experts, self.shared_experts
+        objs = (self.gate.weight, self.gate.bias, e.gate_proj.weight, e.gate_proj.scales,
+                e.up_proj.weight, e.up_proj.scales, e.down_proj.weight, e.down_proj.scales,
+                s.w1.weight, s.w1.scales, s.w3.weight, s.w3.scales, s.w2.weight, s.w2.scales)
+        return tuple((id(o), o.data_ptr() if hasattr(o, "data_ptr") else 0) for o in objs)
+
+    def _decode_into(self, xf, y, weights, indices, W, ws):
+        T = xf.shape[0]
+        cfg = self._cfg()
+        L.call("dsv41_moe_decode", C.byref(cfg), C.byref(W), L.ptr(xf), T, L.dtype_code(y.dtype),
+               L.ptr(y), L.ptr(weights), L.ptr(indices), L.ptr(ws), ws.numel(), L.stream_of(xf))
+
+    def _graph_call(self, xf, odt):
+        t = _torch()
+        sig = self._sig()
+        if sig != self._graph_sig:
+            self._graphs = {}
+            self._graph_sig = sig
+        T = xf.shape[0]
+        key = (T, odt, xf.device)
+        ent = self._graphs.get(key)
+        if ent is None:
+            k = self.args.n_activated_experts
+            sx = t.empty_like(xf)
+            sy = t.empty((T, self.dim), dtype=odt, device=xf.device)
+            sw = t.empty((T, k), dtype=t.float32, device=xf.device)
+            si = t.empty((T, k), dtype=t.int32, device=xf.device)
+            cfg = self._cfg()
+            ws = L.workspace(L.load().dsv41_moe_decode_workspace_size(C.byref(cfg), T), xf.device)
+            W = self._weights()
+            keep = list(self._keep)
+            sx.copy_(xf)
+            side = t.cuda.Stream(device=xf.device)
+            side.wait_stream(t.cuda.current_stream(xf.device))
+            with t.cuda.stream(side):                      # warm-up outside capture
+                self._decode_into(sx, sy, sw, si, W, ws)
+            t.cuda.current_stream(xf.device).wait_stream(side)
+            g = t.cuda.CUDAGraph()
+            with t.cuda.graph(g):
+                self._decode_into(sx, sy, sw, si, W, ws)
+            ent = (g, sx, sy, sw, si, ws, W, keep)
+            self._graphs[key] = ent
+        g, sx, sy, sw, si = ent[:5]
+        sx.copy_(xf)
+        g.replay()
+        return sy.clone(), sw.clone(), si.clone()
 
     # -- plumbing --------------------------------------------------------------
     def _cfg(self, flags=0):
@@ -198,6 +257,11 @@ class MoE:
         shape = xt.shape
         xf = xt.to(t.bfloat16).reshape(-1, self.dim)
         T = xf.shape[0]
+        odt = out_dtype or (t.float32 if xt.dtype == t.float32 else t.bfloat16)
+        if self.cuda_graph and not t.cuda.is_current_stream_capturing():
+            y, weights, indices = self._graph_call(xf, odt)
+            y = y.reshape(shape)
+            return (y, weights, indices) if with_routing else y
         cfg = self._cfg()
         W = self._weights()
         odt = out_dtype or (t.float32 if xt.dtype == t.float32 else t.bfloat16)
