@@ -237,6 +237,11 @@ def run_ours(args):
 
     # active experts per step (for the algorithmic byte count), outside timing
     active = []
+    if world > 1:
+        layer.track = True                       # this rank's local experts per step
+        for x in xs[:4]:
+            layer.forward(x)                     # collective: every rank runs the same count
+        layer.track = False
     for x in xs[:4]:
         _, _, idx = (layer.full_routing(x) if world > 1 else fwd(x, with_routing=True))
         active.append(len(torch.unique(idx)))

@@ -1,0 +1,216 @@
+"""Expert parallelism for the MoE layer over torch.distributed (NCCL on GPUs).
+
+Upstream shards experts by rank (rank r owns experts [r*E/ws, (r+1)*E/ws),
+docs/reference/model.py:854-867) but lets every rank see every token and sums
+the partial outputs with an fp32 all_reduce (model.py:895-902).  Here each rank
+keeps its own tokens and only the (token, expert) pairs travel:
+
+1. route locally (router weights are replicated);
+2. dispatch: pairs are ordered by owning rank, the per-rank counts are exchanged
+   with one all_to_all, then the bf16 token rows and the owner-local expert ids
+   move with all_to_all_single;
+3. the owner runs its experts on the received rows (the fused decode kernels,
+   each received row being one pair);
+4. combine: the fp32 expert outputs return with the mirror all_to_all_single and
+   are summed per token in top-k order with the routing weights, then the shared
+   expert (computed locally) is added -- the same order of fp32 operations as the
+   single-GPU layer.
+
+The exchange logic is plain torch and runs with gloo on CPU (tests) or NCCL on
+GPUs; the expert computation is a callable so the CPU tests can inject a torch
+reference while the GPU path calls libdsv41q.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+
+from . import _lib as L
+
+
+def owner_of(indices, experts_per_rank: int):
+    return indices // experts_per_rank
+
+
+def plan_dispatch(indices, world: int, experts_per_rank: int):
+    """indices int [T, k] -> (order, send_counts) with pairs ordered by owner rank
+    (stable, row-major over [T, k])."""
+    t = L.torch()
+    flat = indices.reshape(-1).to(t.int64)
+    owner = owner_of(flat, experts_per_rank)
+    order = t.argsort(owner * flat.numel() + t.arange(flat.numel(), device=flat.device))
+    counts = t.bincount(owner, minlength=world)
+    return order, counts
+
+
+def exchange_counts(dist, send_counts, group=None):
+    t = L.torch()
+    recv = t.empty_like(send_counts)
+    dist.all_to_all_single(recv, send_counts, group=group)
+    return recv
+
+
+def dispatch(dist, x, indices, world, experts_per_rank, group=None):
+    """-> (recv_rows [R, D], recv_local_expert [R], order, send_counts, recv_counts)."""
+    t = L.torch()
+    D = x.shape[-1]
+    k = indices.shape[-1]
+    order, send_counts = plan_dispatch(indices, world, experts_per_rank)
+    recv_counts = exchange_counts(dist, send_counts, group)
+    tok = order // k
+    send_rows = x.reshape(-1, D).index_select(0, tok).contiguous()
+    send_exp = (indices.reshape(-1).to(t.int64).index_select(0, order) % experts_per_rank).to(t.int32)
+    sc = send_counts.tolist()
+    rc = recv_counts.tolist()
+    R = int(sum(rc))
+    recv_rows = t.empty((R, D), dtype=x.dtype, device=x.device)
+    recv_exp = t.empty((R,), dtype=t.int32, device=x.device)
+    dist.all_to_all_single(recv_rows, send_rows, rc, sc, group=group)
+    dist.all_to_all_single(recv_exp, send_exp, rc, sc, group=group)
+    return recv_rows, recv_exp, order, sc, rc
+
+
+def combine(dist, y_recv, order, send_counts, recv_counts, T, k, group=None):
+    """Return the owners' fp32 outputs to their pairs: -> Y [T, k, D] (unweighted)."""
+    t = L.torch()
+    D = y_recv.shape[-1]
+    back = t.empty((sum(send_counts), D), dtype=y_recv.dtype, device=y_recv.device)
+    dist.all_to_all_single(back, y_recv.contiguous(), send_counts, recv_counts, group=group)
+    Y = t.empty((T * k, D), dtype=y_recv.dtype, device=y_recv.device)
+    Y.index_copy_(0, order, back)
+    return Y.reshape(T, k, D)
+
+
+def weighted_sum(Y, weights, shared=None):
+    """sum_j w[t, j] * Y[t, j] in j order (fp32), + shared: the single-GPU combine."""
+    t = L.torch()
+    acc = t.zeros(Y.shape[0], Y.shape[2], dtype=t.float32, device=Y.device)
+    for j in range(Y.shape[1]):
+        acc = acc + Y[:, j].float() * weights[:, j:j + 1].float()
+    if shared is not None:
+        acc = acc + shared.float()
+    return acc
+
+
+class EPMoE:
+    """MoE layer with routed experts sharded over the process group.
+
+    ``local`` is a single-GPU ``moe.MoE`` holding this rank's experts (ids
+    renumbered 0 .. E/ws-1) plus the replicated router and shared expert.
+    """
+
+    def __init__(self, local, world: int, rank: int, n_experts: int, group=None):
+        import torch.distributed as dist
+        self.dist = dist
+        self.local = local
+        self.world, self.rank = world, rank
+        self.E = n_experts
+        self.epr = n_experts // world
+        self.group = group
+        self.local_active = []
+        self.track = False
+
+    # ---------------------------------------------------------------- GPU path
+    @classmethod
+    def random_init(cls, q, torch, dev, rank, world, E, D, I, topk, seed=0):
+        """Random weights of the release layout; the router and shared expert are the
+        same on every rank (same seed), each rank draws only its own experts."""
+        import types
+        if E % world:
+            raise ValueError(f"{E} experts do not split over {world} ranks")
+        g = torch.Generator(device=dev).manual_seed(seed)
+        args = types.SimpleNamespace(n_activated_experts=topk, score_func="sqrtsoftplus",
+                                     gate_temp=1.0, norm_topk_prob=True, route_scale=1.5,
+                                     n_routed_experts=E // world, dim=D, moe_inter_dim=I,
+                                     swiglu_limit=10.0)
+        m = q.moe.MoE(args, round_bf16=True, cuda_graph=False)
+        gate_w = (torch.randn(E, D, device=dev, generator=g) * D ** -0.5).to(torch.bfloat16)
+        gate_b = torch.randn(E, device=dev, generator=g) * 0.01
+        for key, (n, k) in (("1", (I, D)), ("3", (I, D)), ("2", (D, I))):
+            w = torch.randint(0, 256, (n, k), dtype=torch.uint8, device=dev, generator=g)
+            w[(w & 0x7F) == 0x7F] = 0
+            pr = getattr(m.shared_experts, "w" + key)
+            pr.weight = w
+            pr.scales = torch.randint(118, 128, (n // 32, k // 32), dtype=torch.uint8, device=dev,
+                                      generator=g)
+        gl = torch.Generator(device=dev).manual_seed(seed + 1000 + rank)
+        epr = E // world
+        for name, (n, k) in (("gate_proj", (I, D)), ("up_proj", (I, D)), ("down_proj", (D, I))):
+            pr = getattr(m.experts, name)
+            pr.weight = torch.randint(0, 256, (epr, n, k // 2), dtype=torch.uint8, device=dev,
+                                      generator=gl)
+            pr.scales = torch.randint(120, 129, (epr, n, k // 32), dtype=torch.uint8, device=dev,
+                                      generator=gl)
+        ep = cls(m, world, rank, E)
+        ep.gate_w, ep.gate_b = gate_w, gate_b
+        ep.topk = topk
+        return ep
+
+    def route(self, xf):
+        """Replicated router over all E experts (moe.py:58-74)."""
+        t = L.torch()
+        T, D = xf.shape
+        k = self.topk
+        w = t.empty((T, k), dtype=t.float32, device=xf.device)
+        idx = t.empty((T, k), dtype=t.int32, device=xf.device)
+        ws = L.workspace(L.load().dsv41_moe_route_workspace_size(T, D, self.E), xf.device)
+        L.call("dsv41_moe_route", L.ptr(xf), T, D, L.ptr(self.gate_w), L.ptr(self.gate_b), self.E, k,
+               0, 1.0, 1, 1.5, L.ptr(w), L.ptr(idx), L.ptr(ws), ws.numel(), L.stream_of(xf))
+        return w, idx
+
+    def full_routing(self, x):
+        xf = x.reshape(-1, x.shape[-1]).to(L.torch().bfloat16)
+        w, idx = self.route(xf)
+        return None, w, idx
+
+    @property
+    def local_active_mean(self):
+        return sum(self.local_active) / max(len(self.local_active), 1)
+
+    def _local_experts(self, rows, local_ids):
+        """Owner side: each received row is one pair -> fp32 [R, D] via dsv41_moe_experts."""
+        t = L.torch()
+        m = self.local
+        R = rows.shape[0]
+        if R == 0:
+            return t.empty((0, m.dim), dtype=t.float32, device=rows.device)
+        a = m.args
+        cfg = L.MoeConfig(dim=a.dim, inter=a.moe_inter_dim, n_experts=a.n_routed_experts, topk=1,
+                          score_func=0, gate_temp=1.0, norm_topk_prob=1, route_scale=1.0,
+                          swiglu_limit=float(a.swiglu_limit),
+                          flags=(L.MOE_ROUND_BF16 if m.round_bf16 else 0) | L.MOE_NO_SHARED)
+        W = m._weights()
+        y = t.empty((R, 1, m.dim), dtype=t.float32, device=rows.device)
+        ws = L.workspace(L.load().dsv41_moe_decode_workspace_size(C.byref(cfg), R), rows.device)
+        ids = local_ids.reshape(R, 1).contiguous()
+        L.call("dsv41_moe_experts", C.byref(cfg), C.byref(W), L.ptr(rows), R, L.ptr(ids), L.ptr(y),
+               L.ptr(ws), ws.numel(), L.stream_of(rows))
+        return y[:, 0]
+
+    def _shared(self, xf):
+        """Shared expert on this rank's tokens (port numerics: bf16 intermediates)."""
+        t = L.torch()
+        from .linear import linear_fp8
+        s = self.local.shared_experts
+        g = linear_fp8(xf, s.w1.weight, s.w1.scales).float()
+        u = linear_fp8(xf, s.w3.weight, s.w3.scales).float()
+        lim = s.limit
+        u = t.clamp(u, -lim, lim)
+        g = t.clamp(g, max=lim)
+        h = (t.nn.functional.silu(g) * u).to(t.bfloat16)
+        return linear_fp8(h, s.w2.weight, s.w2.scales, out_dtype=t.bfloat16).float()
+
+    def forward(self, x, expert_fn=None, with_routing=False):
+        t = L.torch()
+        xf = x.reshape(-1, x.shape[-1]).to(t.bfloat16)
+        T = xf.shape[0]
+        w, idx = self.route(xf)
+        rows, ids, order, sc, rc = dispatch(self.dist, xf, idx, self.world, self.epr, self.group)
+        if self.track:
+            self.local_active.append(int(t.unique(ids).numel()))
+        fn = expert_fn or self._local_experts
+        y_recv = fn(rows, ids)
+        Y = combine(self.dist, y_recv, order, sc, rc, T, self.topk, self.group)
+        out = weighted_sum(Y, w, self._shared(xf)).to(x.dtype if x.dtype != t.float32 else t.float32)
+        out = out.reshape(x.shape)
+        return (out, w, idx) if with_routing else out
