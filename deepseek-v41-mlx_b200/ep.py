@@ -135,6 +135,9 @@ class EPMoE:
                                       generator=g)
         gl = torch.Generator(device=dev).manual_seed(seed + 1000 + rank)
         epr = E // world
+        # the local layer's own router is not used (routing is over all E experts)
+        m.gate.weight = gate_w[rank * epr:(rank + 1) * epr].contiguous()
+        m.gate.bias = gate_b[rank * epr:(rank + 1) * epr].contiguous()
         for name, (n, k) in (("gate_proj", (I, D)), ("up_proj", (I, D)), ("down_proj", (D, I))):
             pr = getattr(m.experts, name)
             pr.weight = torch.randint(0, 256, (epr, n, k // 2), dtype=torch.uint8, device=dev,
