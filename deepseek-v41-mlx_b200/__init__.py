@@ -18,7 +18,7 @@ __all__ = ["dequant", "moe", "engram", "linear", "act_quant", "DSV41Error", "lib
 
 def __getattr__(name):
     # submodules load lazily so that importing the package never touches CUDA
-    if name in ("dequant", "moe", "engram", "linear", "act_quant"):
+    if name in ("dequant", "moe", "engram", "linear", "act_quant", "gemm", "ep"):
         import importlib
         return importlib.import_module(f"{__name__}.{name}")
     raise AttributeError(name)

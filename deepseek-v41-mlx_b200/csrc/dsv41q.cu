@@ -7,6 +7,8 @@
 #include "qgemv.cuh"
 #include "router.cuh"
 #include "moe.cuh"
+#include "bsgemm.cuh"
+#include "prefill.cuh"
 
 #include <mutex>
 
@@ -858,6 +860,378 @@ extern "C" int dsv41_moe_decode(const dsv41_moe_config *cfg, const dsv41_moe_wei
     k_moe_combine<__nv_bfloat16><<<grid_for(n), 256, 0, st>>>(
         ws.Y, shared ? ws.Ys : nullptr, wts, T, cfg->topk, d.D, (__nv_bfloat16 *)y);
   DSV41_CHECK_LAUNCH("moe_combine");
+  return DSV41_OK;
+}
+
+// ======================================================================= block-scaled GEMM
+
+namespace {
+
+// Weight tensor map: fp4 codes as 16U4_ALIGN16B (the padded one-byte-per-code smem form
+// the f8f6f4 MMA reads) or fp8 bytes; box {128 K, box_rows}.
+int bs_wmap(CUtensorMap *m, const uint8_t *w, int wfmt, int64_t rows, int64_t K, uint32_t box_rows) {
+  if (wfmt == BS_W_FP4) {
+    DSV41_REQUIRE(aligned(w, 32), DSV41_ERR_MISALIGNED, "fp4 weights must be 32-byte aligned");
+    return make_tmap_2d(m, w, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, (uint64_t)K, (uint64_t)rows,
+                        (uint64_t)(K / 2), 128, box_rows);
+  }
+  return make_tmap_2d(m, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)K, (uint64_t)rows,
+                      (uint64_t)K, 128, box_rows);
+}
+
+int bs_xmaps(CUtensorMap (&m)[4], const uint8_t *x, int64_t rows, int64_t K) {
+  for (int i = 0; i < 4; ++i) {
+    int rc = make_tmap_2d(&m[i], x, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)K,
+                          (uint64_t)(rows < 1 ? 1 : rows), (uint64_t)K, 128, 32u << i);
+    if (rc) return rc;
+  }
+  return DSV41_OK;
+}
+
+template <int WF, int EPI>
+int bs_launch(const char *name, const BsMaps &maps, const BsArgs &a, int grid, cudaStream_t st) {
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(k_bsgemm<WF, EPI>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, BS_SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_status(e, "bsgemm smem attribute");
+    attr_set[dev] = true;
+  }
+  if (grid < 1) return DSV41_OK;
+  ProfScope prof(name, st);
+  k_bsgemm<WF, EPI><<<grid, BS_THREADS, BS_SMEM_BYTES, st>>>(maps, a);
+  DSV41_CHECK_LAUNCH(name);
+  return DSV41_OK;
+}
+
+BsScale bs_scale(const uint8_t *p, int64_t ld, int rshift, int kblock, int64_t rows) {
+  BsScale s;
+  s.p = p;
+  s.ld = ld;
+  s.rshift = rshift;
+  s.kshift = kblock == 128 ? 2 : 0;
+  s.rows = rows;
+  return s;
+}
+
+BsArgs bs_args_dense(int64_t K, int64_t N, int64_t M, int n_per_tile) {
+  BsArgs a;
+  memset(&a, 0, sizeof(a));
+  a.nkb = int(K / BS_BK);
+  a.a_rows = int(N);
+  a.dense_nt = int(ceil_div(M, BS_BN));
+  a.dense_tiles = int(N / n_per_tile) * a.dense_nt;
+  a.dense_rows = int(M);
+  return a;
+}
+
+int bs_grid(int tiles) { return tiles < num_sms() ? tiles : num_sms(); }
+
+// C[M, N] = A[M, K] . B[N, K]^T with fp8 A and fp8 / fp4 B (wfmt), ue8m0 scales.
+int bs_dense(int wfmt, const uint8_t *a, const uint8_t *a_s, int a_blk, const uint8_t *b,
+             const uint8_t *b_s, int b_rshift, int b_blk, int64_t M, int64_t N, int64_t K,
+             void *c, int c_dtype, cudaStream_t st) {
+  DSV41_REQUIRE(M >= 0 && N > 0 && K > 0 && N % 128 == 0 && K % 128 == 0, DSV41_ERR_BAD_SHAPE,
+                "N and K must be positive multiples of 128");
+  DSV41_REQUIRE(M <= (int64_t(1) << 30) && N < (int64_t(1) << 31),
+                DSV41_ERR_BAD_SHAPE, "M or N too large");
+  DSV41_REQUIRE(c_dtype == DSV41_F32 || c_dtype == DSV41_BF16, DSV41_ERR_BAD_DTYPE,
+                "output must be F32 or BF16");
+  if (M == 0) return DSV41_OK;
+  DSV41_REQUIRE(a && a_s && b && b_s && c, DSV41_ERR_BAD_ARG, "NULL pointer");
+  DSV41_REQUIRE(aligned(a, 16) && aligned(c, 16) && aligned(a_s, 4) && aligned(b_s, 4),
+                DSV41_ERR_MISALIGNED, "a/c must be 16-byte and scales 4-byte aligned");
+  BsMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  int rc = bs_wmap(&maps.w, b, wfmt, N, K, 128);
+  if (!rc) rc = bs_xmaps(maps.x, a, M, K);
+  if (rc) return rc;
+  BsArgs g = bs_args_dense(K, N, M, BS_BM);
+  g.sw = bs_scale(b_s, K / b_blk, b_rshift, b_blk, N);
+  g.sx = bs_scale(a_s, K / a_blk, 0, a_blk, M);
+  g.out = c;
+  g.ldo = N;
+  const int grid = bs_grid(g.dense_tiles);
+  if (wfmt == BS_W_FP4)
+    return c_dtype == DSV41_F32 ? bs_launch<BS_W_FP4, BS_EPI_F32>("fp4_gemm", maps, g, grid, st)
+                                : bs_launch<BS_W_FP4, BS_EPI_BF16>("fp4_gemm", maps, g, grid, st);
+  return c_dtype == DSV41_F32 ? bs_launch<BS_W_FP8, BS_EPI_F32>("fp8_gemm", maps, g, grid, st)
+                              : bs_launch<BS_W_FP8, BS_EPI_BF16>("fp8_gemm", maps, g, grid, st);
+}
+
+}  // namespace
+
+extern "C" int dsv41_fp8_gemm(const uint8_t *a, const uint8_t *a_s, const uint8_t *b,
+                              const uint8_t *b_s, int64_t M, int64_t N, int64_t K, int block_size,
+                              void *c, int c_dtype, void *stream) {
+  DSV41_REQUIRE(block_size == 32 || block_size == 128, DSV41_ERR_BAD_ARG,
+                "block_size must be 32 or 128");
+  return bs_dense(BS_W_FP8, a, a_s, block_size, b, b_s, block_size == 32 ? 5 : 7, block_size, M,
+                  N, K, c, c_dtype, STREAM(stream));
+}
+
+extern "C" int dsv41_fp4_gemm(const uint8_t *a, const uint8_t *a_s, const uint8_t *b,
+                              const uint8_t *b_s, int64_t M, int64_t N, int64_t K,
+                              int act_block_size, void *c, int c_dtype, void *stream) {
+  DSV41_REQUIRE(act_block_size == 32 || act_block_size == 128, DSV41_ERR_BAD_ARG,
+                "act_block_size must be 32 or 128");
+  return bs_dense(BS_W_FP4, a, a_s, act_block_size, b, b_s, 0, 32, M, N, K, c, c_dtype,
+                  STREAM(stream));
+}
+
+// ======================================================================= MoE prefill
+
+namespace {
+
+struct PfDims {
+  int64_t T, D, I, E, P, nchunks, tiles_gu_cap, tiles_dn_cap;
+  int k;
+};
+
+PfDims pf_dims(const dsv41_moe_config *cfg, int64_t T) {
+  PfDims d;
+  d.T = T;
+  d.D = cfg->dim;
+  d.I = cfg->inter;
+  d.E = cfg->n_experts;
+  d.k = cfg->topk;
+  d.P = T * cfg->topk;
+  d.nchunks = ceil_div(d.P, PF_CHUNK);
+  const int64_t groups_cap = d.P / PF_TILE_ROWS + d.E + 1;
+  d.tiles_gu_cap = (d.I / 64) * groups_cap;
+  d.tiles_dn_cap = (d.D / BS_BM) * groups_cap;
+  return d;
+}
+
+struct PfWs {
+  float *w;
+  int32_t *idx;
+  float *rpart;
+  uint8_t *xq, *xs, *xpq, *xps, *hq, *hs, *shq, *shs;
+  __nv_bfloat16 *yp, *ysh;
+  int *chunk_cnt;
+  PfPlan plan;
+};
+
+size_t pf_carve(const PfDims &d, bool route, bool shared, uint8_t *base, size_t cap, PfWs *ws) {
+  WsCarve c{base, cap, 0};
+  PfWs w;
+  memset(&w, 0, sizeof(w));
+  if (route) {
+    w.w = c.take<float>(d.P);
+    w.idx = c.take<int32_t>(d.P);
+    w.rpart = c.take<float>(dsv41_moe_route_workspace_size(d.T, d.D, d.E) / sizeof(float));
+  }
+  w.xq = c.take<uint8_t>(d.T * d.D);
+  w.xs = c.take<uint8_t>(d.T * d.D / 32);
+  w.xpq = c.take<uint8_t>(d.P * d.D);
+  w.xps = c.take<uint8_t>(d.P * d.D / 32);
+  w.hq = c.take<uint8_t>(d.P * d.I);
+  w.hs = c.take<uint8_t>(d.P * d.I / 32);
+  w.yp = c.take<__nv_bfloat16>(d.P * d.D);
+  if (shared) {
+    w.shq = c.take<uint8_t>(d.T * d.I);
+    w.shs = c.take<uint8_t>(d.T * d.I / 32);
+    w.ysh = c.take<__nv_bfloat16>(d.T * d.D);
+  }
+  w.chunk_cnt = c.take<int>(d.nchunks * d.E);
+  w.plan.chunk_base = w.chunk_cnt;
+  w.plan.grp_off = c.take<int>(d.E);
+  w.plan.grp_cnt = c.take<int>(d.E);
+  w.plan.pair_tok = c.take<int>(d.P);
+  w.plan.pair_w = c.take<float>(d.P);
+  w.plan.slot_pos = c.take<int>(d.P);
+  w.plan.tiles_gu = c.take<int4>(d.tiles_gu_cap);
+  w.plan.tiles_dn = c.take<int4>(d.tiles_dn_cap);
+  w.plan.ntiles = c.take<int>(2);
+  if (ws) *ws = w;
+  return c.off + 256;
+}
+
+int pf_check(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, int64_t T, bool shared) {
+  DSV41_REQUIRE(cfg && W, DSV41_ERR_BAD_ARG, "NULL config/weights");
+  int rc = route_check(T, cfg->dim, cfg->n_experts, cfg->topk, cfg->score_func);
+  if (rc) return rc;
+  DSV41_REQUIRE(cfg->dim % 128 == 0 && cfg->inter % 128 == 0, DSV41_ERR_BAD_SHAPE,
+                "prefill needs dim and inter to be multiples of 128");
+  DSV41_REQUIRE(cfg->topk <= 8, DSV41_ERR_UNSUPPORTED, "prefill supports topk <= 8");
+  DSV41_REQUIRE(T * cfg->topk < (int64_t(1) << 30) && cfg->n_experts * cfg->dim < (int64_t(1) << 31),
+                DSV41_ERR_BAD_SHAPE, "too many pairs or expert rows");
+  if (T == 0) return DSV41_OK;
+  DSV41_REQUIRE(W->w1 && W->s1 && W->w3 && W->s3 && W->w2 && W->s2, DSV41_ERR_BAD_ARG,
+                "NULL expert pointer");
+  DSV41_REQUIRE(aligned(W->s1, 4) && aligned(W->s3, 4) && aligned(W->s2, 4), DSV41_ERR_MISALIGNED,
+                "expert scales must be 4-byte aligned");
+  DSV41_REQUIRE(!shared || (W->sw1 && W->ss1 && W->sw3 && W->ss3 && W->sw2 && W->ss2),
+                DSV41_ERR_BAD_ARG, "NULL shared-expert pointer");
+  DSV41_REQUIRE(!shared || (aligned(W->ss1, 4) && aligned(W->ss3, 4) && aligned(W->ss2, 4) &&
+                            aligned(W->sw1, 16) && aligned(W->sw3, 16) && aligned(W->sw2, 16)),
+                DSV41_ERR_MISALIGNED, "shared-expert weights/scales misaligned");
+  return DSV41_OK;
+}
+
+}  // namespace
+
+extern "C" size_t dsv41_moe_prefill_workspace_size(const dsv41_moe_config *cfg, int64_t T,
+                                                   int with_routing) {
+  if (!cfg || T <= 0) return 256;
+  const bool shared = (cfg->flags & DSV41_MOE_NO_SHARED) == 0;
+  return pf_carve(pf_dims(cfg, T), with_routing == 0, shared, nullptr, ~size_t(0) >> 1, nullptr);
+}
+
+extern "C" int dsv41_moe_prefill(const dsv41_moe_config *cfg, const dsv41_moe_weights *W,
+                                 const void *x, int64_t T, const float *route_weights,
+                                 const int32_t *route_indices, int out_dtype, void *y,
+                                 void *workspace, size_t workspace_bytes, void *stream) {
+  const bool shared = cfg && (cfg->flags & DSV41_MOE_NO_SHARED) == 0;
+  int rc = pf_check(cfg, W, T, shared);
+  if (rc) return rc;
+  if (T == 0) return DSV41_OK;
+  DSV41_REQUIRE(out_dtype == DSV41_F32 || out_dtype == DSV41_BF16, DSV41_ERR_BAD_DTYPE,
+                "output must be F32 or BF16");
+  DSV41_REQUIRE(x && y && aligned(x, 16) && aligned(y, 16), DSV41_ERR_MISALIGNED,
+                "x and y must be 16-byte aligned");
+  const bool route = route_indices == nullptr;
+  DSV41_REQUIRE(!route || W->gate_w, DSV41_ERR_BAD_ARG, "NULL gate weight");
+  const PfDims d = pf_dims(cfg, T);
+  PfWs ws;
+  const size_t need = pf_carve(d, route, shared, reinterpret_cast<uint8_t *>(workspace),
+                               workspace_bytes, &ws);
+  DSV41_REQUIRE(workspace && workspace_bytes >= need, DSV41_ERR_WORKSPACE,
+                "workspace too small (%zu < %zu)", workspace_bytes, need);
+  cudaStream_t st = STREAM(stream);
+  const float *rw = route_weights;
+  const int32_t *ri = route_indices;
+  if (route) {
+    DSV41_REQUIRE(aligned(W->gate_w, 16), DSV41_ERR_MISALIGNED, "gate_w must be 16-byte aligned");
+    rc = route_impl(x, T, d.D, W->gate_w, W->gate_bias, d.E, d.k, cfg->score_func,
+                    cfg->gate_temp, cfg->norm_topk_prob, cfg->route_scale, ws.w, ws.idx, ws.rpart,
+                    st);
+    if (rc) return rc;
+    rw = ws.w;
+    ri = ws.idx;
+  }
+  // act_quant(x, 32, ue8m0) once per token
+  {
+    const int64_t warps = d.T * (d.D / 32);
+    ProfScope prof("pf_act_quant", st);
+    k_act_quant<1><<<unsigned((warps * 32 + 255) / 256), 256, 0, st>>>(
+        reinterpret_cast<const __nv_bfloat16 *>(x), d.T, d.D, 1, ws.xq, ws.xs, 1, nullptr);
+    DSV41_CHECK_LAUNCH("pf_act_quant");
+  }
+  // stable sort of the (token, slot) pairs by expert + tile lists
+  {
+    ProfScope prof("pf_plan", st);
+    const size_t sm = size_t(16) * d.E * sizeof(int);
+    if (sm > 48 * 1024) {
+      cudaFuncSetAttribute(k_pf_count, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+      cudaFuncSetAttribute(k_pf_place, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+    }
+    k_pf_count<<<unsigned(d.nchunks), PF_CHUNK, sm, st>>>(ri, d.P, int(d.E), ws.chunk_cnt);
+    DSV41_CHECK_LAUNCH("pf_count");
+    k_pf_scan<<<1, 1024, 0, st>>>(ws.chunk_cnt, int(d.nchunks), int(d.E), int(d.I / 64),
+                                  int(d.D / BS_BM), ws.plan);
+    DSV41_CHECK_LAUNCH("pf_scan");
+    k_pf_place<<<unsigned(d.nchunks), PF_CHUNK, sm, st>>>(ri, rw, d.P, d.k, int(d.E), ws.plan);
+    DSV41_CHECK_LAUNCH("pf_place");
+  }
+  {
+    ProfScope prof("pf_gather", st);
+    k_pf_gather<<<unsigned(ceil_div(d.P * 32, 256)), 256, 0, st>>>(ws.xq, ws.xs, ws.plan.pair_tok,
+                                                                   d.P, d.D, ws.xpq, ws.xps);
+    DSV41_CHECK_LAUNCH("pf_gather");
+  }
+  const int grid = num_sms();
+  // routed gate/up: SwiGLU * routing weight, bf16, act_quant -> hq/hs
+  {
+    BsMaps maps;
+    memset(&maps, 0, sizeof(maps));
+    rc = bs_wmap(&maps.w, W->w1, BS_W_FP4, d.E * d.I, d.D, 64);
+    if (!rc) rc = bs_wmap(&maps.w2, W->w3, BS_W_FP4, d.E * d.I, d.D, 64);
+    if (!rc) rc = bs_xmaps(maps.x, ws.xpq, d.P, d.D);
+    if (rc) return rc;
+    BsArgs a;
+    memset(&a, 0, sizeof(a));
+    a.nkb = int(d.D / BS_BK);
+    a.a_rows = int(d.I);
+    a.sw = bs_scale(W->s1, d.D / 32, 0, 32, d.E * d.I);
+    a.sw2 = bs_scale(W->s3, d.D / 32, 0, 32, d.E * d.I);
+    a.sx = bs_scale(ws.xps, d.D / 32, 0, 32, d.P);
+    a.tiles = ws.plan.tiles_gu;
+    a.ntiles = ws.plan.ntiles;
+    a.pw = ws.plan.pair_w;
+    a.hq = ws.hq;
+    a.hs = ws.hs;
+    a.ldh = d.I;
+    a.limit = cfg->swiglu_limit;
+    rc = bs_launch<BS_W_FP4, BS_EPI_SWIGLU>("pf_gate_up_fp4", maps, a, grid, st);
+    if (rc) return rc;
+  }
+  // routed down -> yp (bf16 per pair)
+  {
+    BsMaps maps;
+    memset(&maps, 0, sizeof(maps));
+    rc = bs_wmap(&maps.w, W->w2, BS_W_FP4, d.E * d.D, d.I, 128);
+    if (!rc) rc = bs_xmaps(maps.x, ws.hq, d.P, d.I);
+    if (rc) return rc;
+    BsArgs a;
+    memset(&a, 0, sizeof(a));
+    a.nkb = int(d.I / BS_BK);
+    a.a_rows = int(d.D);
+    a.sw = bs_scale(W->s2, d.I / 32, 0, 32, d.E * d.D);
+    a.sx = bs_scale(ws.hs, d.I / 32, 0, 32, d.P);
+    a.tiles = ws.plan.tiles_dn;
+    a.ntiles = ws.plan.ntiles + 1;
+    a.out = ws.yp;
+    a.ldo = d.D;
+    rc = bs_launch<BS_W_FP4, BS_EPI_BF16>("pf_down_fp4", maps, a, grid, st);
+    if (rc) return rc;
+  }
+  if (shared) {
+    BsMaps maps;
+    memset(&maps, 0, sizeof(maps));
+    rc = bs_wmap(&maps.w, W->sw1, BS_W_FP8, d.I, d.D, 64);
+    if (!rc) rc = bs_wmap(&maps.w2, W->sw3, BS_W_FP8, d.I, d.D, 64);
+    if (!rc) rc = bs_xmaps(maps.x, ws.xq, d.T, d.D);
+    if (rc) return rc;
+    BsArgs a = bs_args_dense(d.D, d.I, d.T, 64);
+    a.sw = bs_scale(W->ss1, d.D / 32, 5, 32, d.I);
+    a.sw2 = bs_scale(W->ss3, d.D / 32, 5, 32, d.I);
+    a.sx = bs_scale(ws.xs, d.D / 32, 0, 32, d.T);
+    a.hq = ws.shq;
+    a.hs = ws.shs;
+    a.ldh = d.I;
+    a.limit = cfg->swiglu_limit;
+    rc = bs_launch<BS_W_FP8, BS_EPI_SWIGLU>("pf_shared_gate_up_fp8", maps, a,
+                                            bs_grid(a.dense_tiles), st);
+    if (rc) return rc;
+    BsMaps m2;
+    memset(&m2, 0, sizeof(m2));
+    rc = bs_wmap(&m2.w, W->sw2, BS_W_FP8, d.D, d.I, 128);
+    if (!rc) rc = bs_xmaps(m2.x, ws.shq, d.T, d.I);
+    if (rc) return rc;
+    BsArgs b = bs_args_dense(d.I, d.D, d.T, BS_BM);
+    b.sw = bs_scale(W->ss2, d.I / 32, 5, 32, d.D);
+    b.sx = bs_scale(ws.shs, d.I / 32, 0, 32, d.T);
+    b.out = ws.ysh;
+    b.ldo = d.D;
+    rc = bs_launch<BS_W_FP8, BS_EPI_BF16>("pf_shared_down_fp8", m2, b, bs_grid(b.dense_tiles), st);
+    if (rc) return rc;
+  }
+  {
+    const int64_t n = d.T * (d.D / 8);
+    ProfScope prof("pf_combine", st);
+    if (out_dtype == DSV41_F32)
+      k_pf_combine<float><<<unsigned(ceil_div(n, 256)), 256, 0, st>>>(
+          ws.yp, shared ? ws.ysh : nullptr, ri, ws.plan.slot_pos, d.T, d.k, d.D, (float *)y);
+    else
+      k_pf_combine<__nv_bfloat16><<<unsigned(ceil_div(n, 256)), 256, 0, st>>>(
+          ws.yp, shared ? ws.ysh : nullptr, ri, ws.plan.slot_pos, d.T, d.k, d.D,
+          (__nv_bfloat16 *)y);
+    DSV41_CHECK_LAUNCH("pf_combine");
+  }
   return DSV41_OK;
 }
 

@@ -1,0 +1,229 @@
+// prefill.cuh -- MoE prefill bookkeeping around the block-scaled grouped GEMM.
+//
+// Upstream MoE.forward (docs/reference/model.py:889-904) loops over experts and runs each
+// expert on the tokens routed to it.  Here the (token, slot) pairs are sorted by expert
+// once (a stable counting sort: pairs keep row-major [T, k] order inside an expert), the
+// fp8 activation rows are gathered into that order, the grouped GEMMs walk per-expert
+// tiles, and the combine sums every token's expert outputs in ascending expert order
+// (the order of upstream's loop) before adding the shared expert.
+#pragma once
+#include "common.cuh"
+
+namespace dsv41 {
+
+constexpr int PF_CHUNK = 512;       // pairs per counting block (16 warps)
+constexpr int PF_TILE_ROWS = 256;   // activation rows per GEMM tile
+
+struct PfPlan {
+  int *chunk_base;     // [nchunks, E]: pairs of expert e in earlier chunks
+  int *grp_off;        // [E] first sorted position of expert e
+  int *grp_cnt;        // [E]
+  int *pair_tok;       // [P] token of sorted pair
+  float *pair_w;       // [P] routing weight of sorted pair
+  int *slot_pos;       // [T*k] sorted position of pair (t, j)
+  int4 *tiles_gu;      // gate/up tiles {expert, m-tile, first row, rows}
+  int4 *tiles_dn;      // down tiles
+  int *ntiles;         // [0] gate/up, [1] down
+};
+
+__global__ void __launch_bounds__(PF_CHUNK) k_pf_count(const int32_t *__restrict__ idx, int64_t P,
+                                                       int E, int *__restrict__ chunk_cnt) {
+  extern __shared__ int wh[];   // [16][E]
+  const int warp = threadIdx.x >> 5;
+  for (int i = threadIdx.x; i < 16 * E; i += PF_CHUNK) wh[i] = 0;
+  __syncthreads();
+  const int64_t p = int64_t(blockIdx.x) * PF_CHUNK + threadIdx.x;
+  if (p < P) {
+    const int e = idx[p];
+    if (e >= 0 && e < E) atomicAdd(&wh[warp * E + e], 1);
+    else dev_flag(DSV41_DEVST_BAD_INDEX);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += PF_CHUNK) {
+    int s = 0;
+#pragma unroll
+    for (int w = 0; w < 16; ++w) s += wh[w * E + e];
+    chunk_cnt[int64_t(blockIdx.x) * E + e] = s;
+  }
+}
+
+// Exclusive block-wide scan of three values per thread (1024 threads).
+__device__ __forceinline__ void block_scan3(int (&v)[3], int (&excl)[3], int (&total)[3]) {
+  __shared__ int wt[3][32];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  int inc[3] = {v[0], v[1], v[2]};
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      const int u = __shfl_up_sync(0xffffffffu, inc[k], o);
+      if (lane >= o) inc[k] += u;
+    }
+  }
+  if (lane == 31) {
+#pragma unroll
+    for (int k = 0; k < 3; ++k) wt[k][wid] = inc[k];
+  }
+  __syncthreads();
+  if (wid == 0) {
+    const int nw = blockDim.x >> 5;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      int t = lane < nw ? wt[k][lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, t, o);
+        if (lane >= o) t += u;
+      }
+      wt[k][lane] = t;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    excl[k] = inc[k] - v[k] + (wid > 0 ? wt[k][wid - 1] : 0);
+    total[k] = wt[k][(blockDim.x >> 5) - 1];
+  }
+}
+
+// One CTA of 1024 threads, one expert per thread (E <= 1024).
+__global__ void __launch_bounds__(1024) k_pf_scan(int *__restrict__ chunk_cnt, int nchunks, int E,
+                                                  int mt_gu, int mt_dn, PfPlan plan) {
+  const int e = threadIdx.x;
+  int run = 0;
+  if (e < E) {
+    for (int c = 0; c < nchunks; ++c) {
+      const int v = chunk_cnt[int64_t(c) * E + e];
+      chunk_cnt[int64_t(c) * E + e] = run;
+      run += v;
+    }
+  }
+  const int nnt = (run + PF_TILE_ROWS - 1) / PF_TILE_ROWS;
+  int v[3] = {run, nnt * mt_gu, nnt * mt_dn}, excl[3], tot[3];
+  block_scan3(v, excl, tot);
+  if (e < E) {
+    plan.grp_off[e] = excl[0];
+    plan.grp_cnt[e] = run;
+    for (int mt = 0; mt < mt_gu; ++mt)
+      for (int nt = 0; nt < nnt; ++nt)
+        plan.tiles_gu[excl[1] + mt * nnt + nt] =
+            make_int4(e, mt, excl[0] + nt * PF_TILE_ROWS, min(PF_TILE_ROWS, run - nt * PF_TILE_ROWS));
+    for (int mt = 0; mt < mt_dn; ++mt)
+      for (int nt = 0; nt < nnt; ++nt)
+        plan.tiles_dn[excl[2] + mt * nnt + nt] =
+            make_int4(e, mt, excl[0] + nt * PF_TILE_ROWS, min(PF_TILE_ROWS, run - nt * PF_TILE_ROWS));
+  }
+  if (threadIdx.x == 0) {
+    plan.ntiles[0] = tot[1];
+    plan.ntiles[1] = tot[2];
+  }
+}
+
+// Stable placement: rank inside the chunk from per-warp counts and warp-level matching.
+__global__ void __launch_bounds__(PF_CHUNK) k_pf_place(const int32_t *__restrict__ idx,
+                                                       const float *__restrict__ w, int64_t P,
+                                                       int topk, int E, PfPlan plan) {
+  extern __shared__ int wh[];   // [16][E]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < 16 * E; i += PF_CHUNK) wh[i] = 0;
+  __syncthreads();
+  const int64_t p = int64_t(blockIdx.x) * PF_CHUNK + threadIdx.x;
+  int e = -1;
+  if (p < P) {
+    e = idx[p];
+    if (e < 0 || e >= E) e = -1;
+  }
+  if (p < P && e < 0) plan.slot_pos[p] = -1;   // skipped by the combine
+  const unsigned peers = __match_any_sync(0xffffffffu, e);
+  const int rank = __popc(peers & ((1u << lane) - 1u));
+  if (e >= 0 && rank == 0) wh[warp * E + e] = __popc(peers);
+  __syncthreads();
+  if (e >= 0) {
+    int before = 0;
+    for (int w2 = 0; w2 < warp; ++w2) before += wh[w2 * E + e];
+    const int pos = plan.grp_off[e] + plan.chunk_base[int64_t(blockIdx.x) * E + e] + before + rank;
+    plan.pair_tok[pos] = int(p / topk);
+    plan.pair_w[pos] = w ? w[p] : 1.0f;
+    plan.slot_pos[p] = pos;
+  }
+}
+
+// dst row r = src row tok[r] for the fp8 codes (K bytes) and their ue8m0 scales (K/32).
+__global__ void k_pf_gather(const uint8_t *__restrict__ xq, const uint8_t *__restrict__ xs,
+                            const int *__restrict__ tok, int64_t R, int64_t K,
+                            uint8_t *__restrict__ dq, uint8_t *__restrict__ ds) {
+  const int64_t r = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (r >= R) return;
+  const int64_t t = tok[r];
+  const uint4 *src = reinterpret_cast<const uint4 *>(xq + t * K);
+  uint4 *dst = reinterpret_cast<uint4 *>(dq + r * K);
+  for (int64_t i = lane; i < K / 16; i += 32) dst[i] = __ldg(src + i);
+  const uint32_t *ss = reinterpret_cast<const uint32_t *>(xs + t * (K / 32));
+  uint32_t *sd = reinterpret_cast<uint32_t *>(ds + r * (K / 32));
+  for (int64_t i = lane; i < K / 128; i += 32) sd[i] = __ldg(ss + i);
+}
+
+// out[t, :] = sum over the token's experts in ascending id order of Yp[pos] (bf16), then
+// + Ys[t, :] (bf16, may be null); fp32 arithmetic.  8 columns per thread.
+template <typename TO>
+__global__ void k_pf_combine(const __nv_bfloat16 *__restrict__ Yp, const __nv_bfloat16 *__restrict__ Ys,
+                             const int32_t *__restrict__ idx, const int *__restrict__ slot_pos,
+                             int64_t T, int topk, int64_t D, TO *__restrict__ out) {
+  const int64_t groups = D / 8;
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= T * groups) return;
+  const int64_t t = i / groups, c0 = (i % groups) * 8;
+  int ids[8], pos[8];
+  for (int j = 0; j < topk; ++j) {
+    ids[j] = idx[t * topk + j];
+    pos[j] = slot_pos[t * topk + j];
+  }
+  for (int a = 1; a < topk; ++a) {       // insertion sort by expert id
+    const int ki = ids[a], kp = pos[a];
+    int b = a - 1;
+    while (b >= 0 && ids[b] > ki) {
+      ids[b + 1] = ids[b];
+      pos[b + 1] = pos[b];
+      --b;
+    }
+    ids[b + 1] = ki;
+    pos[b + 1] = kp;
+  }
+  float acc[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) acc[c] = 0.0f;
+  for (int j = 0; j < topk; ++j) {
+    if (pos[j] < 0) continue;
+    const uint4 v = *reinterpret_cast<const uint4 *>(Yp + int64_t(pos[j]) * D + c0);
+    const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      acc[2 * c] = __fadd_rn(acc[2 * c], bf_bits2f(uint16_t(wv[c] & 0xFFFF)));
+      acc[2 * c + 1] = __fadd_rn(acc[2 * c + 1], bf_bits2f(uint16_t(wv[c] >> 16)));
+    }
+  }
+  if (Ys) {
+    const uint4 v = *reinterpret_cast<const uint4 *>(Ys + t * D + c0);
+    const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      acc[2 * c] = __fadd_rn(acc[2 * c], bf_bits2f(uint16_t(wv[c] & 0xFFFF)));
+      acc[2 * c + 1] = __fadd_rn(acc[2 * c + 1], bf_bits2f(uint16_t(wv[c] >> 16)));
+    }
+  }
+  if constexpr (sizeof(TO) == 4) {
+    float4 *o = reinterpret_cast<float4 *>(out + t * D + c0);
+    o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+  } else {
+    uint4 o;
+    o.x = uint32_t(f2bf_bits(acc[0])) | (uint32_t(f2bf_bits(acc[1])) << 16);
+    o.y = uint32_t(f2bf_bits(acc[2])) | (uint32_t(f2bf_bits(acc[3])) << 16);
+    o.z = uint32_t(f2bf_bits(acc[4])) | (uint32_t(f2bf_bits(acc[5])) << 16);
+    o.w = uint32_t(f2bf_bits(acc[6])) | (uint32_t(f2bf_bits(acc[7])) << 16);
+    *reinterpret_cast<uint4 *>(out + t * D + c0) = o;
+  }
+}
+
+}  // namespace dsv41

@@ -274,3 +274,31 @@ class MoE:
                L.ptr(y), L.ptr(weights), L.ptr(indices), L.ptr(ws), ws.numel(), L.stream_of(xf))
         y = y.reshape(shape)
         return (y, weights, indices) if with_routing else y
+
+    # -- prefill, upstream a8 numerics ---------------------------------------
+    def prefill_a8(self, x, weights=None, indices=None, out_dtype=None):
+        """The layer as upstream runs it (docs/reference/model.py:889-904): every
+        linear in a8 form (act_quant + block-scaled GEMM, bf16 outputs), routed
+        experts as grouped GEMMs on tcgen05 block-scaled MMA.  Routing is computed
+        by the router unless ``weights``/``indices`` [T, topk] are given."""
+        t = _torch()
+        xt = L.cuda_tensor(x, "x")
+        shape = xt.shape
+        xf = xt.to(t.bfloat16).reshape(-1, self.dim).contiguous()
+        T = xf.shape[0]
+        odt = out_dtype or (t.float32 if xt.dtype == t.float32 else t.bfloat16)
+        se = self.shared_experts
+        has_shared = se is not None and se.w1.weight is not None
+        cfg = self._cfg(0 if has_shared else L.MOE_NO_SHARED)
+        W = self._weights()
+        given = indices is not None
+        if given:
+            idx = L.cuda_tensor(indices, "indices").to(t.int32).reshape(T, -1).contiguous()
+            wts = L.cuda_tensor(weights, "weights").float().reshape(T, -1).contiguous()
+        need = L.load().dsv41_moe_prefill_workspace_size(C.byref(cfg), T, 1 if given else 0)
+        ws = L.workspace(need, xf.device)
+        y = t.empty((T, self.dim), dtype=odt, device=xf.device)
+        L.call("dsv41_moe_prefill", C.byref(cfg), C.byref(W), L.ptr(xf), T,
+               L.ptr(wts) if given else None, L.ptr(idx) if given else None, L.dtype_code(odt),
+               L.ptr(y), L.ptr(ws), ws.numel(), L.stream_of(xf))
+        return y.reshape(shape)

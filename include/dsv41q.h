@@ -208,6 +208,37 @@ int dsv41_moe_decode(const dsv41_moe_config *cfg, const dsv41_moe_weights *w, co
                      int32_t *indices_out, void *workspace, size_t workspace_bytes,
                      void *stream);
 
+/* ---- a13: upstream fp8_gemm / fp4_gemm (docs/reference/kernel.py:277-308 and
+ * :562-591) on tcgen05 block-scaled MMA (kind::mxf8f6f4, fp32
+ * accumulation in TMEM).  C[M, N] = A[M, K] . B[N, K]^T with
+ *   a   fp8 e4m3 [M, K], a_s ue8m0 bytes [M, K / block] (act_quant output);
+ *   b   fp8_gemm: fp8 e4m3 [N, K], b_s ue8m0 [ceil(N/block), K/block] (block 32 or 128);
+ *       fp4_gemm: fp4 e2m1 packed two per byte [N, K/2] (low nibble = even k),
+ *                 b_s ue8m0 [N, K/32]; act_block_size 32 or 128 for a_s;
+ *   c   [M, N] F32 or BF16 (upstream returns torch's default dtype).
+ * N and K must be multiples of 128; a and c 16-byte aligned, scales 4-byte aligned.
+ * Only ue8m0 scales: upstream's float32-scale variant has no block-scaled MMA form. */
+int dsv41_fp8_gemm(const uint8_t *a, const uint8_t *a_s, const uint8_t *b, const uint8_t *b_s,
+                   int64_t M, int64_t N, int64_t K, int block_size, void *c, int c_dtype,
+                   void *stream);
+int dsv41_fp4_gemm(const uint8_t *a, const uint8_t *a_s, const uint8_t *b, const uint8_t *b_s,
+                   int64_t M, int64_t N, int64_t K, int act_block_size, void *c, int c_dtype,
+                   void *stream);
+
+/* ---- MoE prefill, a8 numerics (docs/reference/model.py:889-904 with Expert.forward
+ * :841-851 and linear() :181-207): act_quant(x, 32, ue8m0), per-expert fp4 gate/up on the
+ * block-scaled grouped GEMM, clamped SwiGLU x routing weight -> bf16 -> act_quant, fp4
+ * down -> bf16 per (token, expert), summed in ascending expert order, + the fp8 shared
+ * expert (same a8 form).  Routing is either given (route_weights f32 [T, topk],
+ * route_indices int32 [T, topk]) or computed with the router of dsv41_moe_route when
+ * route_indices is NULL.  dim and inter must be multiples of 128, topk <= 8.
+ * with_routing = 1 when the caller passes routing (smaller workspace). */
+size_t dsv41_moe_prefill_workspace_size(const dsv41_moe_config *cfg, int64_t T, int with_routing);
+int dsv41_moe_prefill(const dsv41_moe_config *cfg, const dsv41_moe_weights *w, const void *x,
+                      int64_t T, const float *route_weights, const int32_t *route_indices,
+                      int out_dtype, void *y, void *workspace, size_t workspace_bytes,
+                      void *stream);
+
 /* ---- a15: engram hasher (deepseek_v41_mlx/engram.py:154-180; upstream
  * docs/reference/engram.py NgramHashState.forward).  input_ids int64 [B, L];
  * token_map int64 [V]; ids_cache int64 [B, max_seq], positions

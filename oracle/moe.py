@@ -155,12 +155,16 @@ def moe_forward(x, p, cfg, round_bf16_io=True, with_shared=True, acc=np.float64,
     return y, w, idx
 
 
-def moe_forward_upstream_a8(x, p, cfg):
+def moe_forward_upstream_a8(x, p, cfg, routing=None, with_shared=True):
     """docs/reference/model.py:889-904 with fp4 experts and fp8 shared expert, a8
-    linears (act_quant + block-scaled GEMM), bf16 linear outputs."""
+    linears (act_quant + block-scaled GEMM), bf16 linear outputs.  ``routing``
+    = (weights, indices) replaces the router (e.g. a synthetic skewed routing)."""
     T, D = x.shape
-    w, idx, _ = gate(x, p["gate_w"], p.get("gate_bias"), cfg["topk"], cfg["score_func"],
-                     cfg["gate_temp"], cfg["norm_topk_prob"], cfg["route_scale"])
+    if routing is None:
+        w, idx, _ = gate(x, p["gate_w"], p.get("gate_bias"), cfg["topk"], cfg["score_func"],
+                         cfg["gate_temp"], cfg["norm_topk_prob"], cfg["route_scale"])
+    else:
+        w, idx = (np.asarray(a) for a in routing)
     L = cfg["swiglu_limit"]
     y = np.zeros((T, D), dtype=np.float32)
     xq = act_dequant(round_bf16(x))
@@ -178,6 +182,8 @@ def moe_forward_upstream_a8(x, p, cfg):
         h = round_bf16(h * w[t_sel, j_sel][:, None])
         ye = round_bf16(_mm(act_dequant(h), W2, np.float64))
         np.add.at(y, t_sel, ye)
+    if not with_shared:
+        return y.astype(np.float32), w, idx
     W1 = dequant_fp8(p["sw1"], p["ss1"], "f32")
     W3 = dequant_fp8(p["sw3"], p["ss3"], "f32")
     W2 = dequant_fp8(p["sw2"], p["ss2"], "f32")
