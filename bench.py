@@ -158,6 +158,60 @@ def make_moe(q, torch, device, seed=0, n_local=None):
     return m
 
 
+def zipf_routing(torch, dev, x, gate_w, T, seed=7, s=1.1):
+    """BASELINE.json configs[2] routing: per token, top-6 expert ids drawn without
+    replacement from Zipf(s) over a seeded permutation of the experts (Gumbel-top-k on
+    log p_zipf); weights = the router's unbiased sqrt-softplus scores at those ids,
+    normalised and scaled by route_scale 1.5."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    perm = torch.randperm(E, device=dev, generator=g)
+    logp = torch.empty(E, device=dev)
+    logp[perm] = -s * torch.log(torch.arange(1, E + 1, device=dev, dtype=torch.float32))
+    u = torch.rand(T, E, device=dev, generator=g).clamp_(1e-30, 1.0)
+    idx = (logp[None, :] - torch.log(-torch.log(u))).topk(TOPK, dim=-1).indices
+    scores = torch.sqrt(torch.nn.functional.softplus(x.float() @ gate_w.float().T))
+    w = scores.gather(1, idx)
+    w = w / (w.sum(-1, keepdim=True) + 1e-20) * 1.5
+    return w.contiguous(), idx.to(torch.int32).contiguous()
+
+
+def prefill_measurement(q, torch, dev, layer, flush, stream, peaks, K, W, T=8192):
+    """d3: the layer at prefill in a8 numerics (upstream linear()), T=8192, Zipf routing."""
+    hbm_peak, bf16_peak, peak_src = peaks
+    g = torch.Generator(device=dev).manual_seed(4321)
+    x = torch.randn(T, D, device=dev, generator=g).to(torch.bfloat16)
+    w, idx = zipf_routing(torch, dev, x, layer.gate.weight, T)
+    counts = torch.bincount(idx.reshape(-1).long(), minlength=E)
+    fn = lambda i: layer.prefill_a8(x, weights=w, indices=idx)
+    ms = timed_steps(torch, fn, K, W, flush, stream)
+    st = statistics.median(ms)
+    q._lib.prof_enable(True)
+    fn(0)
+    torch.cuda.synchronize()
+    prof = q._lib.prof_report()
+    q._lib.prof_enable(False)
+    f_routed = 2.0 * T * TOPK * 3 * I * D
+    f_shared = 2.0 * 3 * T * I * D
+    fp8_peak = 2.0 * bf16_peak          # f8f6f4 rate = twice the bf16 rate
+    kern = {k: round(v[1] / v[0], 4) for k, v in prof.items()}
+    gu, dn = kern.get("pf_gate_up_fp4"), kern.get("pf_down_fp4")
+    routed_ms = (gu or 0) + (dn or 0)
+    active = int((counts > 0).sum())
+    wbytes = active * BYTES_PER_EXPERT
+    return {
+        "tok_s": round(T / (st / 1e3), 1), "ms": round(st, 4), "tokens": T,
+        "tflops_layer": round((f_routed + f_shared) / (st / 1e3) / 1e12, 1),
+        "routed_gemm_tflops": round(f_routed / (routed_ms / 1e3) / 1e12, 1) if routed_ms else None,
+        "routed_gemm_frac_fp8_peak": round(f_routed / (routed_ms / 1e3) / 1e12 / fp8_peak, 4)
+        if routed_ms else None,
+        "routed_weight_gbs": round(wbytes / (routed_ms / 1e3) / 1e9, 1) if routed_ms else None,
+        "fp8_peak_tflops": fp8_peak, "peak_source": peak_src + " 2x bf16_tflops",
+        "kernel_ms": kern, "experts_active": active, "pairs_max_expert": int(counts.max()),
+        "pairs_min_expert": int(counts.min()),
+        "routing": "Zipf(1.1) Gumbel-top-6 over a seeded expert permutation; router-score weights",
+    }
+
+
 def timed_steps(torch, fn, K, W, flush, stream):
     """W warm-up calls, then K calls each between CUDA events; returns per-step ms."""
     for i in range(W):
@@ -293,6 +347,8 @@ def run_ours(args):
     sub = {}
     if world == 1 and not args.no_sub:
         sub = sub_measurements(q, torch, dev, layer, flush, stream, hbm_peak, max(3, K // 2), W)
+        sub["moe_prefill_T8192_a8"] = prefill_measurement(
+            q, torch, dev, layer, flush, stream, (hbm_peak, bf16_peak, peak_src), max(3, K // 4), W)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -491,10 +547,25 @@ def main():
     ap.add_argument("--ref-sample", type=int, default=2, help="routed experts per reference step")
     ap.add_argument("--experts", type=int, default=384,
                     help="routed experts (384 = BASELINE; smaller only for ncu captures)")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="only the T=8192 a8 prefill measurement (one JSON line)")
+    ap.add_argument("--prefill-tokens", type=int, default=8192)
     args = ap.parse_args()
     global E, ROUTER_BYTES
     E = args.experts
     ROUTER_BYTES = E * D * 2
+    if args.prefill_only:
+        import torch
+        q = _package()
+        dev = torch.device("cuda", 0)
+        layer = make_moe(q, torch, dev)
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        with Clocks(0) as clk:
+            r = prefill_measurement(q, torch, dev, layer, flush, torch.cuda.current_stream(),
+                                    _peaks(), args.steps, args.warmup, T=args.prefill_tokens)
+        r["clocks"] = clk.summary()
+        print(json.dumps(r))
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

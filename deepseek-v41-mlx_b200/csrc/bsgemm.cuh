@@ -3,28 +3,32 @@
 // Computes D[n, p] = sum_k W[n, k] * X[p, k] with ue8m0 scales per 32 (or 128) along K on
 // both operands, i.e. upstream fp8_gemm / fp4_gemm (docs/reference/kernel.py:207-307,
 // :478-591) with the weights as the MMA's A operand (M = 128 weight rows per tile) and the
-// fp8 activations as the B operand (N = up to 256 activation rows per tile):
+// fp8 activations as the B operand (N = up to 224 activation rows per tile):
 //
 //   tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale, scale_vec 1X (one ue8m0 per 32 K)
 //   A = fp4 e2m1 (TMA 16U4_ALIGN16B: 16 codes + 8 pad bytes per 16-byte smem chunk) or
-//       fp8 e4m3; B = fp8 e4m3; fp32 accumulator in TMEM (256 columns).
+//       fp8 e4m3; B = fp8 e4m3; fp32 accumulators in TMEM, double-buffered (2 x 224
+//       columns) so that a tile's epilogue overlaps the next tile's MMAs.
 //
 // One persistent CTA per SM walks a tile list (grouped: one tile = (group, 128 weight rows,
-// <= 256 activation rows); the MMA's N shrinks to the tile's rows rounded up to 16, so
+// <= 224 activation rows); the MMA's N shrinks to the tile's rows rounded up to 16, so
 // ragged expert groups cost what they use).  Warp roles, 192 threads:
 //   warp 0     TMA producer: A/B tiles (128B swizzle) into a 4-stage ring; its 32 lanes
-//              stage the scale words into the 32x16-byte layout tcgen05.cp wants
-//              (byte l*16 + c*4 + b = scale of row 32c+l, K-block b), fence the async proxy
-//              and arrive (full barrier count 33 = expect_tx arrive + 32 lanes);
+//              copy the scale words (4-byte cp.async, completion tracked by the stage's
+//              mbarrier) into the 32x16-byte layout tcgen05.cp wants (byte l*16 + c*4 + b =
+//              scale of row 32c+l, K-block b); full barrier count 33 = expect_tx arrive +
+//              32 lane arrivals;
 //   warp 1     TMEM allocator + MMA issuer (lane 0): per stage copy SFA/SFB smem -> TMEM,
 //              4 MMAs of K=32 (sf_id = K-block), commit -> empty[stage];
-//              after a tile, commit -> acc_full;
+//              after a tile, commit -> acc_full[buffer];
 //   warps 2-5  epilogue: tcgen05.ld 32 lanes x 32 columns, transpose through shared memory,
 //              vector stores.  Store mode writes fp32/bf16 rows; SwiGLU mode pairs the gate
-//              and up halves of the tile (A = 64 gate rows + 64 up rows), applies the clamped
-//              SwiGLU, the routing weight and bf16 rounding, then act_quant's per-32 fp8
-//              quantization of h (the down projection's input) -- upstream Expert.forward
-//              (docs/reference/model.py:841-851) with linear() in a8 form (:181-207).
+//              and up halves of the tile (A = 64 gate rows + 64 up rows; warps q and q+2
+//              hold the same features), applies the clamped SwiGLU (CUDA's __expf and
+//              __fdividef), the routing weight and bf16 rounding, then act_quant's per-32
+//              fp8 quantization of h (the down projection's input) -- upstream
+//              Expert.forward (docs/reference/model.py:841-851) with linear() in a8 form
+//              (:181-207).
 //
 // Every wait is bounded (2 s); on expiry the device status flag is raised and the CTA
 // drains its own copies and MMAs before freeing TMEM.  No multicast anywhere.
@@ -34,23 +38,49 @@
 
 namespace dsv41 {
 
-constexpr int BS_BM = 128, BS_BN = 256, BS_BK = 128, BS_STAGES = 4;
-constexpr int BS_A_BYTES = BS_BM * BS_BK;      // 16 KB: fp8, or fp4 padded to one byte/code
-constexpr int BS_B_BYTES = BS_BN * BS_BK;      // 32 KB
-constexpr int BS_SFA_BYTES = 512, BS_SFB_BYTES = 1024;
+constexpr int BS_BM = 128, BS_BK = 128, BS_BN = 224, BS_BN_NARROW = 64;
+constexpr int BS_THREADS = 192;
 constexpr int BS_EPI_LD = 36;                  // floats per row of a transposition tile
 constexpr int BS_EPI_BYTES = 32 * BS_EPI_LD * 4;
-constexpr int BS_OFF_A = 0;
-constexpr int BS_OFF_B = BS_OFF_A + BS_STAGES * BS_A_BYTES;
-constexpr int BS_OFF_SFA = BS_OFF_B + BS_STAGES * BS_B_BYTES;
-constexpr int BS_OFF_SFB = BS_OFF_SFA + BS_STAGES * BS_SFA_BYTES;
-constexpr int BS_OFF_EPI = BS_OFF_SFB + BS_STAGES * BS_SFB_BYTES;
-constexpr int BS_OFF_BAR = BS_OFF_EPI + 4 * BS_EPI_BYTES;
-constexpr int BS_SMEM_BYTES = BS_OFF_BAR + 256 + 1024;   // + barriers + alignment slack
-constexpr int BS_THREADS = 192;
-constexpr uint32_t BS_TMEM_COLS = 512;
-constexpr uint32_t BS_SF_COL0 = 256;           // SF slot s: SFA at 256+16s (4), SFB at +4 (8)
-static_assert(BS_SMEM_BYTES <= 232448, "bsgemm shared memory");
+constexpr int BS_RING = 4;                     // tile-ring slots (producer -> MMA, epilogue)
+
+// Two shapes of the same pipeline.  Wide: up to 224 activation rows per tile, 4 stages of
+// 128 K (16 KB of weights + 28 KB of activations) -- the compute-bound shape.  Narrow: up to
+// 64 rows, 4 stages of 256 K (32 + 16 KB): the tiles of lightly routed experts only stream
+// weights, and a stage that carries two 128-wide K blocks halves the waits and commits the
+// single MMA-issuing thread spends per weight byte.
+template <bool NARROW>
+struct BsCfg {
+  static constexpr int BN = NARROW ? BS_BN_NARROW : BS_BN;
+  static constexpr int STAGES = 4;
+  static constexpr int KSUB = NARROW ? 2 : 1;            // 128-wide K blocks per stage
+  static constexpr int NBOX = NARROW ? 2 : 4;            // activation boxes 32/64(/128/224)
+  static constexpr int SFB_CHUNKS = NARROW ? 4 : 8;      // 32-row scale chunks staged
+  static constexpr int A_SUB = BS_BM * BS_BK;            // fp8, or fp4 padded to a byte/code
+  static constexpr int B_SUB = BN * BS_BK;
+  static constexpr int SFB_SUB = SFB_CHUNKS * 128;
+  static constexpr int A_BYTES = KSUB * A_SUB;
+  static constexpr int B_BYTES = KSUB * B_SUB;
+  static constexpr int SFA_BYTES = KSUB * 512;
+  static constexpr int SFB_BYTES = KSUB * SFB_SUB;
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
+  static constexpr int OFF_SFA = OFF_B + STAGES * B_BYTES;
+  static constexpr int OFF_SFB = OFF_SFA + STAGES * SFA_BYTES;
+  static constexpr int OFF_EPI = OFF_SFB + STAGES * SFB_BYTES;
+  static constexpr int OFF_RING = OFF_EPI + 4 * BS_EPI_BYTES;
+  static constexpr int OFF_BAR = OFF_RING + BS_RING * 16;
+  static constexpr int SMEM = OFF_BAR + 512 + 1024;     // + barriers + alignment slack
+  static constexpr uint32_t TMEM_COLS = NARROW ? 256 : 512;
+  static constexpr uint32_t ACC_COLS = BN;               // accumulator b at column b * BN
+  static constexpr uint32_t SF_COL0 = 2 * BN;            // SF slot s at SF_COL0 + 16 s
+  static constexpr uint32_t SFA_COLS = 4 * KSUB;         // then SFB: 4 columns per atom
+  static constexpr uint32_t SFB_ATOMS = SFB_CHUNKS / 4;
+  static_assert(SFA_COLS + 4 * KSUB * SFB_ATOMS <= 16, "SF slot");
+  static_assert(SF_COL0 + 16 * STAGES <= TMEM_COLS, "TMEM columns");
+  static_assert(B_SUB % 1024 == 0 && A_SUB % 1024 == 0, "swizzle atoms");
+  static_assert(SMEM <= 232448, "shared memory");
+};
 
 enum { BS_W_FP4 = 0, BS_W_FP8 = 1 };
 enum { BS_EPI_F32 = 0, BS_EPI_BF16 = 1, BS_EPI_SWIGLU = 2 };
@@ -67,15 +97,17 @@ struct BsScale {
 };
 
 struct BsArgs {
-  int nkb;             // K / 128
+  int nkb;             // K / 128 (the launcher divides by the stage's K blocks)
   int a_rows;          // weight rows of one group (N; I in SwiGLU mode)
   BsScale sw, sw2;     // weight scales (sw2: up projection in SwiGLU mode)
   BsScale sx;          // activation scales
   const int4 *tiles;   // grouped: {group, m-tile, first activation row, rows}; null = dense
   const int *ntiles;   // grouped tile count (device)
-  int dense_tiles, dense_nt, dense_rows;
+  int *next_tile;      // grouped: work counter (zeroed before the launch), tiles taken in order
+  int dense_tiles, dense_nt, dense_bn, dense_rows;
   void *out;           // store mode: out[p * ldo + n]
   int64_t ldo;
+  int sf_async;        // 1: every scale operand is per-32 (cp.async staging)
   const float *pw;     // SwiGLU: per-row routing weight (null = none)
   uint8_t *hq;         // SwiGLU: fp8 h [rows, ldh]
   uint8_t *hs;         // SwiGLU: ue8m0 scales of h [rows, ldh / 32]
@@ -86,7 +118,7 @@ struct BsArgs {
 struct BsMaps {
   CUtensorMap w;       // weights, box {128 K, 128 rows} (64 rows in SwiGLU mode)
   CUtensorMap w2;      // up-projection weights (SwiGLU mode)
-  CUtensorMap x[4];    // activations, box {128 K, 32 << i rows}
+  CUtensorMap x[4];    // activations, box {128 K, bs_box_rows(i)}
 };
 
 // ------------------------------------------------------------------ tcgen05 wrappers
@@ -145,6 +177,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+// 4-byte asynchronous copy global -> shared; src_bytes 0 fills zeros.
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+// Arrive on `bar` (counted in its expected arrivals) once this thread's cp.asyncs landed.
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t *bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
 __device__ __forceinline__ uint64_t l2_policy_evict_normal() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
@@ -169,6 +211,13 @@ __device__ __forceinline__ uint32_t idesc_mx(uint32_t a_fmt, uint32_t n, uint32_
   return (a_fmt << 7) | ((n >> 3) << 17) | (1u << 23) | (8u << 24) | (sf_id << 29) | (sf_id << 4);
 }
 
+// cp.async of the 4 per-32 scales of (row, K stage kb) to shared address dst.
+__device__ __forceinline__ void bs_scale_copy(const BsScale &s, int64_t row, int kb, uint32_t dst) {
+  const bool ok = row < s.rows;
+  const uint8_t *p = ok ? s.p + (row >> s.rshift) * s.ld + 4 * kb : s.p;
+  cp_async4(dst, p, ok ? 4u : 0u);
+}
+
 __device__ __forceinline__ uint32_t bs_scale_word(const BsScale &s, int64_t row, int kb) {
   if (row >= s.rows) return 0x7F7F7F7Fu;   // 1.0: rows past the operand feed discarded columns
   const uint8_t *p = s.p + (row >> s.rshift) * s.ld;
@@ -176,20 +225,21 @@ __device__ __forceinline__ uint32_t bs_scale_word(const BsScale &s, int64_t row,
   return uint32_t(__ldg(p + kb)) * 0x01010101u;
 }
 
-__device__ __forceinline__ int4 bs_tile(const BsArgs &a, int t) {
-  if (a.tiles) return a.tiles[t];
+__device__ __forceinline__ int4 bs_dense_tile(const BsArgs &a, int t) {
   const int nt = t % a.dense_nt, mt = t / a.dense_nt;
-  const int row0 = nt * BS_BN;
-  return make_int4(0, mt, row0, min(BS_BN, a.dense_rows - row0));
+  const int row0 = nt * a.dense_bn;
+  return make_int4(0, mt, row0, min(a.dense_bn, a.dense_rows - row0));
 }
 
+template <int BN>
 __device__ __forceinline__ int bs_nmma(int nrows) {
   const int n = (nrows + 15) & ~15;
-  return n < 16 ? 16 : (n > BS_BN ? BS_BN : n);
+  return n < 16 ? 16 : (n > BN ? BN : n);
 }
-__device__ __forceinline__ int bs_box(int nmma) {   // activation box index: 32 << i rows
+__device__ __forceinline__ int bs_box(int nmma) {   // activation box index
   return nmma <= 32 ? 0 : nmma <= 64 ? 1 : nmma <= 128 ? 2 : 3;
 }
+__host__ __device__ constexpr uint32_t bs_box_rows(int i) { return i < 3 ? 32u << i : uint32_t(BS_BN); }
 
 // Bounded wait taken by all 32 lanes; the warp agrees on the outcome.
 __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity) {
@@ -197,47 +247,55 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity) {
   return __all_sync(0xffffffffu, ok);
 }
 
-template <int WFMT, int EPI>
+template <int WFMT, int EPI, bool NARROW>
 __global__ void __launch_bounds__(BS_THREADS, 1)
     k_bsgemm(const __grid_constant__ BsMaps maps, const BsArgs args) {
+  using Cfg = BsCfg<NARROW>;
+  constexpr int S = Cfg::STAGES;
   extern __shared__ uint8_t bs_raw[];
   const uint32_t raw_s = smem_u32(bs_raw);
   uint8_t *smem = bs_raw + ((1024u - (raw_s & 1023u)) & 1023u);
   const uint32_t sbase = smem_u32(smem);
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + BS_OFF_BAR);
-  uint64_t *full = bars;                    // [4] count 33
-  uint64_t *empty = bars + 4;               // [4] count 1 (tcgen05.commit)
-  uint64_t *acc_full = bars + 8;            // count 1 (tcgen05.commit)
-  uint64_t *acc_empty = bars + 9;           // count 4 (epilogue warps)
-  uint64_t *xfull = bars + 10;              // [2] count 32 (SwiGLU pair exchange)
-  uint64_t *xempty = bars + 12;             // [2] count 32
-  uint64_t *mma_done = bars + 14;           // count 1
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 16);
+  int4 *ring = reinterpret_cast<int4 *>(smem + Cfg::OFF_RING);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Cfg::OFF_BAR);
+  uint64_t *full = bars;                    // [S] count 33
+  uint64_t *empty = bars + S;               // [S] count 1 (tcgen05.commit)
+  uint64_t *acc_full = bars + 2 * S;        // [2] count 1 (tcgen05.commit)
+  uint64_t *acc_empty = acc_full + 2;       // [2] count 4 (epilogue warps)
+  uint64_t *xfull = acc_full + 4;           // [2] count 64 (SwiGLU pair exchange)
+  uint64_t *xempty = acc_full + 6;          // [2] count 64
+  uint64_t *tfull = acc_full + 8;           // [BS_RING] count 1 (producer)
+  uint64_t *tempty = tfull + BS_RING;       // [BS_RING] count 5 (MMA + 4 epilogue warps)
+  uint64_t *mma_done = tempty + BS_RING;    // count 1
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < BS_STAGES; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 33);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 4);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&xfull[i], 32);
-      mbar_init(&xempty[i], 32);
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);
+      mbar_init(&xfull[i], 64);
+      mbar_init(&xempty[i], 64);
+    }
+    for (int i = 0; i < BS_RING; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 5);
     }
     mbar_init(mma_done, 1);
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, BS_TMEM_COLS);
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int ntiles = args.tiles ? *args.ntiles : args.dense_tiles;
   const int nkb = args.nkb;
   constexpr uint32_t W_TX = WFMT == BS_W_FP4 ? BS_BM * BS_BK / 2 : BS_BM * BS_BK;
 
@@ -246,107 +304,158 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
     if (lane == 0) {
       prefetch_tmap(&maps.w);
       if (EPI == BS_EPI_SWIGLU) prefetch_tmap(&maps.w2);
-      for (int i = 0; i < 4; ++i) prefetch_tmap(&maps.x[i]);
+      for (int i = 0; i < Cfg::NBOX; ++i) prefetch_tmap(&maps.x[i]);
     }
-    const uint64_t pol_w = l2_policy_evict_normal();
-    const uint64_t pol_x = l2_policy_evict_last();
+    // narrow tiles read their weights once; activation rows are reused by the m-tiles of
+    // their expert, which the tile order keeps close together in time
+    const uint64_t pol_w = NARROW ? l2_policy_evict_first() : l2_policy_evict_normal();
+    const uint64_t pol_x = l2_policy_evict_normal();
+    const int ntiles = args.tiles ? *args.ntiles : args.dense_tiles;
     int it = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-      const int4 tl = bs_tile(args, t);
-      const int nmma = bs_nmma(tl.w), bi = bs_box(nmma);
-      const uint32_t x_tx = uint32_t(32 << bi) * BS_BK;
+    for (int ti = 0; ok; ++ti) {
+      // next tile -> ring slot (an end marker when the work runs out)
+      const int slot = ti % BS_RING;
+      if (!warp_wait(&tempty[slot], (uint32_t(ti / BS_RING) & 1u) ^ 1u)) break;
+      int4 tl = make_int4(-1, 0, 0, 0);
+      if (lane == 0) {
+        const int t = args.tiles ? atomicAdd(args.next_tile, 1) : int(blockIdx.x) + ti * int(gridDim.x);
+        if (t < ntiles) tl = args.tiles ? args.tiles[t] : bs_dense_tile(args, t);
+        ring[slot] = tl;
+        mbar_arrive(&tfull[slot]);
+      }
+      tl.x = __shfl_sync(0xffffffffu, tl.x, 0);
+      tl.y = __shfl_sync(0xffffffffu, tl.y, 0);
+      tl.z = __shfl_sync(0xffffffffu, tl.z, 0);
+      tl.w = __shfl_sync(0xffffffffu, tl.w, 0);
+      if (tl.x < 0) break;
+      const int nmma = bs_nmma<Cfg::BN>(tl.w), bi = bs_box(nmma);
+      const uint32_t x_tx = bs_box_rows(bi) * BS_BK;
       const int64_t wrow0 = int64_t(tl.x) * args.a_rows +
                             int64_t(tl.y) * (EPI == BS_EPI_SWIGLU ? 64 : BS_BM);
       for (int kb = 0; kb < nkb; ++kb, ++it) {
-        const int s = it % BS_STAGES;
-        const uint32_t ph = uint32_t(it / BS_STAGES) & 1u;
+        const int s = it % S;
+        const uint32_t ph = uint32_t(it / S) & 1u;
         if (!warp_wait(&empty[s], ph ^ 1u)) {
           ok = false;
           break;
         }
-        uint8_t *sa = smem + BS_OFF_A + s * BS_A_BYTES;
-        uint8_t *sb = smem + BS_OFF_B + s * BS_B_BYTES;
+        uint8_t *sa = smem + Cfg::OFF_A + s * Cfg::A_BYTES;
+        uint8_t *sb = smem + Cfg::OFF_B + s * Cfg::B_BYTES;
         if (lane == 0) {
-          mbar_arrive_expect_tx(&full[s], W_TX + x_tx);
-          if (EPI == BS_EPI_SWIGLU) {
-            tma_load_2d(sa, &maps.w, &full[s], kb * BS_BK, int32_t(wrow0), pol_w);
-            tma_load_2d(sa + BS_A_BYTES / 2, &maps.w2, &full[s], kb * BS_BK, int32_t(wrow0), pol_w);
-          } else {
-            tma_load_2d(sa, &maps.w, &full[s], kb * BS_BK, int32_t(wrow0), pol_w);
+          mbar_arrive_expect_tx(&full[s], uint32_t(Cfg::KSUB) * (W_TX + x_tx));
+#pragma unroll
+          for (int ks = 0; ks < Cfg::KSUB; ++ks) {
+            const int kx = (kb * Cfg::KSUB + ks) * BS_BK;
+            uint8_t *a = sa + ks * Cfg::A_SUB;
+            tma_load_2d(a, &maps.w, &full[s], kx, int32_t(wrow0), pol_w);
+            if (EPI == BS_EPI_SWIGLU)
+              tma_load_2d(a + Cfg::A_SUB / 2, &maps.w2, &full[s], kx, int32_t(wrow0), pol_w);
+            tma_load_2d(sb + ks * Cfg::B_SUB, &maps.x[bi], &full[s], kx, tl.z, pol_x);
           }
-          tma_load_2d(sb, &maps.x[bi], &full[s], kb * BS_BK, tl.z, pol_x);
         }
         // scale words -> tcgen05.cp layout (row 32c + l at byte l*16 + c*4)
-        uint4 va;
-        uint32_t *vw = reinterpret_cast<uint32_t *>(&va);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          if (EPI == BS_EPI_SWIGLU)
-            vw[c] = c < 2 ? bs_scale_word(args.sw, wrow0 + 32 * c + lane, kb)
-                          : bs_scale_word(args.sw2, wrow0 + 32 * (c - 2) + lane, kb);
-          else
-            vw[c] = bs_scale_word(args.sw, wrow0 + 32 * c + lane, kb);
+        for (int ks = 0; ks < Cfg::KSUB; ++ks) {
+          const int kq = kb * Cfg::KSUB + ks;
+          const uint32_t sfa = sbase + Cfg::OFF_SFA + s * Cfg::SFA_BYTES + ks * 512 + lane * 16;
+          const uint32_t sfb = sbase + Cfg::OFF_SFB + s * Cfg::SFB_BYTES + ks * Cfg::SFB_SUB +
+                               lane * 16;
+          if (args.sf_async) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              if (EPI == BS_EPI_SWIGLU && c >= 2)
+                bs_scale_copy(args.sw2, wrow0 + 32 * (c - 2) + lane, kq, sfa + 4 * c);
+              else
+                bs_scale_copy(args.sw, wrow0 + 32 * c + lane, kq, sfa + 4 * c);
+            }
+#pragma unroll
+            for (int c = 0; c < Cfg::SFB_CHUNKS; ++c)
+              bs_scale_copy(args.sx, int64_t(tl.z) + 32 * c + lane, kq,
+                            sfb + (c >> 2) * 512 + 4 * (c & 3));
+          } else {
+            uint4 va;
+            uint32_t *vw = reinterpret_cast<uint32_t *>(&va);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              if (EPI == BS_EPI_SWIGLU && c >= 2)
+                vw[c] = bs_scale_word(args.sw2, wrow0 + 32 * (c - 2) + lane, kq);
+              else
+                vw[c] = bs_scale_word(args.sw, wrow0 + 32 * c + lane, kq);
+            }
+            *reinterpret_cast<uint4 *>(smem + (sfa - sbase)) = va;
+#pragma unroll
+            for (int h = 0; h < Cfg::SFB_ATOMS; ++h) {
+              uint4 vb;
+              uint32_t *bw = reinterpret_cast<uint32_t *>(&vb);
+#pragma unroll
+              for (int c = 0; c < 4; ++c)
+                bw[c] = bs_scale_word(args.sx, int64_t(tl.z) + 32 * (4 * h + c) + lane, kq);
+              *reinterpret_cast<uint4 *>(smem + (sfb - sbase) + h * 512) = vb;
+            }
+          }
         }
-        *reinterpret_cast<uint4 *>(smem + BS_OFF_SFA + s * BS_SFA_BYTES + lane * 16) = va;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          uint4 vb;
-          uint32_t *bw = reinterpret_cast<uint32_t *>(&vb);
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-            bw[c] = bs_scale_word(args.sx, int64_t(tl.z) + 32 * (4 * h + c) + lane, kb);
-          *reinterpret_cast<uint4 *>(smem + BS_OFF_SFB + s * BS_SFB_BYTES + h * 512 + lane * 16) = vb;
+        if (args.sf_async) {
+          cp_async_arrive_noinc(&full[s]);
+        } else {
+          fence_proxy_async_smem();
+          mbar_arrive(&full[s]);
         }
-        fence_proxy_async_smem();
-        mbar_arrive(&full[s]);
       }
     }
     // every copy this warp issued has landed before the CTA can finish
-    for (int j = it - BS_STAGES < 0 ? 0 : it - BS_STAGES; j < it; ++j)
-      mbar_wait(&full[j % BS_STAGES], uint32_t(j / BS_STAGES) & 1u);
+    for (int j = it - S < 0 ? 0 : it - S; j < it; ++j)
+      mbar_wait(&full[j % S], uint32_t(j / S) & 1u);
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      int it = 0, tc = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++tc) {
-        const int4 tl = bs_tile(args, t);
-        const int nmma = bs_nmma(tl.w);
-        if (!mbar_wait(acc_empty, (uint32_t(tc) & 1u) ^ 1u)) {
-          ok = false;
-          break;
-        }
+      int it = 0;
+      for (int ti = 0;; ++ti) {
+        const int slot = ti % BS_RING;
+        if (!mbar_wait(&tfull[slot], uint32_t(ti / BS_RING) & 1u)) break;
+        const int4 tl = ring[slot];
+        if (tl.x < 0) break;
+        const int nmma = bs_nmma<Cfg::BN>(tl.w);
+        const int ab = ti & 1;
+        if (!mbar_wait(&acc_empty[ab], (uint32_t(ti >> 1) & 1u) ^ 1u)) break;
         tc_fence_after();
+        const uint32_t tacc = tmem + uint32_t(ab) * Cfg::ACC_COLS;
+        bool ok = true;
         for (int kb = 0; kb < nkb; ++kb, ++it) {
-          const int s = it % BS_STAGES;
-          const uint32_t ph = uint32_t(it / BS_STAGES) & 1u;
+          const int s = it % S;
+          const uint32_t ph = uint32_t(it / S) & 1u;
           if (!mbar_wait(&full[s], ph)) {
             ok = false;
             break;
           }
+          fence_proxy_async_smem();   // scale words written by cp.async -> tcgen05.cp reads
           tc_fence_after();
-          const uint32_t t_sfa = tmem + BS_SF_COL0 + 16u * s;
-          const uint32_t t_sfb = t_sfa + 4u;
-          const uint32_t s_sfa = sbase + BS_OFF_SFA + s * BS_SFA_BYTES;
-          const uint32_t s_sfb = sbase + BS_OFF_SFB + s * BS_SFB_BYTES;
-          tc_cp_sf(t_sfa, sdesc_sf(s_sfa));
-          tc_cp_sf(t_sfb, sdesc_sf(s_sfb));
-          if (nmma > 128) tc_cp_sf(t_sfb + 4u, sdesc_sf(s_sfb + 512u));
-          const uint64_t da = sdesc_sw128(sbase + BS_OFF_A + s * BS_A_BYTES);
-          const uint64_t db = sdesc_sw128(sbase + BS_OFF_B + s * BS_B_BYTES);
+          const uint32_t t_sfa = tmem + Cfg::SF_COL0 + 16u * s;
+          const uint32_t t_sfb = t_sfa + Cfg::SFA_COLS;
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            // +32 bytes along K inside the swizzle atom = +2 in the descriptor's address field
-            tc_mma_mx(tmem, da + uint64_t(2 * k), db + uint64_t(2 * k),
-                      idesc_mx(WFMT == BS_W_FP4 ? 5u : 0u, uint32_t(nmma), uint32_t(k)),
-                      t_sfa | (uint32_t(k) << 30), t_sfb | (uint32_t(k) << 30),
-                      (kb | k) != 0 ? 1u : 0u);
+          for (int ks = 0; ks < Cfg::KSUB; ++ks) {
+            const uint32_t ta = t_sfa + 4u * ks, tb = t_sfb + 4u * Cfg::SFB_ATOMS * ks;
+            const uint32_t s_sfa = sbase + Cfg::OFF_SFA + s * Cfg::SFA_BYTES + ks * 512;
+            const uint32_t s_sfb = sbase + Cfg::OFF_SFB + s * Cfg::SFB_BYTES + ks * Cfg::SFB_SUB;
+            tc_cp_sf(ta, sdesc_sf(s_sfa));
+            tc_cp_sf(tb, sdesc_sf(s_sfb));
+            if (Cfg::SFB_ATOMS > 1 && nmma > 128) tc_cp_sf(tb + 4u, sdesc_sf(s_sfb + 512u));
+            const uint64_t da = sdesc_sw128(sbase + Cfg::OFF_A + s * Cfg::A_BYTES + ks * Cfg::A_SUB);
+            const uint64_t db = sdesc_sw128(sbase + Cfg::OFF_B + s * Cfg::B_BYTES + ks * Cfg::B_SUB);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              // +32 bytes along K inside the swizzle atom = +2 in the descriptor's address field
+              tc_mma_mx(tacc, da + uint64_t(2 * k), db + uint64_t(2 * k),
+                        idesc_mx(WFMT == BS_W_FP4 ? 5u : 0u, uint32_t(nmma), uint32_t(k)),
+                        ta | (uint32_t(k) << 30), tb | (uint32_t(k) << 30),
+                        (kb | ks | k) != 0 ? 1u : 0u);
+            }
           }
           tc_commit(&empty[s]);
         }
         if (!ok) break;
-        tc_commit(acc_full);
+        tc_commit(&acc_full[ab]);
+        mbar_arrive(&tempty[slot]);
       }
       tc_commit(mma_done);
       mbar_wait(mma_done, 0);
@@ -355,14 +464,18 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;                 // TMEM lane quadrant of this warp
-    float *tp = reinterpret_cast<float *>(smem + BS_OFF_EPI + q * BS_EPI_BYTES);
-    int tc = 0, xc = 0;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tc) {
-      const int4 tl = bs_tile(args, t);
-      const int nmma = bs_nmma(tl.w);
-      if (!warp_wait(acc_full, uint32_t(tc) & 1u)) break;
+    float *tp = reinterpret_cast<float *>(smem + Cfg::OFF_EPI + q * BS_EPI_BYTES);
+    int xc = 0;
+    for (int ti = 0;; ++ti) {
+      const int slot = ti % BS_RING;
+      if (!warp_wait(&tfull[slot], uint32_t(ti / BS_RING) & 1u)) break;
+      const int4 tl = ring[slot];
+      if (tl.x < 0) break;
+      const int nmma = bs_nmma<Cfg::BN>(tl.w);
+      const int ab = ti & 1;
+      if (!warp_wait(&acc_full[ab], uint32_t(ti >> 1) & 1u)) break;
       tc_fence_after();
-      const uint32_t tq = tmem + (uint32_t(32 * q) << 16);
+      const uint32_t tq = tmem + (uint32_t(32 * q) << 16) + uint32_t(ab) * Cfg::ACC_COLS;
       bool ok = true;
       for (int cc = 0; cc * 32 < nmma && ok; ++cc) {
         uint32_t r[32];
@@ -398,79 +511,88 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
           }
           __syncwarp();
         } else {
-          const int pr = q & 1;
+          // SwiGLU pair: warp q (gate rows 32q..) and warp q+2 (the same up rows) both park
+          // their chunk transposed in shared memory, then each finishes 16 of the 32 rows:
+          // lane l takes row 16*half + l/2 and features (l&1)*16 .. +15 of the pair's 32.
+          const int pr = q & 1, half = q >> 1;
           const uint32_t xph = uint32_t(xc) & 1u;
           const float L = args.limit;
-          if (q >= 2) {
-            // up half: bf16-round, clamp, hand to the gate warp of the same rows
-            if (!warp_wait(&xempty[pr], xph ^ 1u)) {
-              ok = false;
-              break;
+          if (!warp_wait(&xempty[pr], xph ^ 1u)) {
+            ok = false;
+            break;
+          }
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float v = round_bf16f(__uint_as_float(r[j]));
+            if (L > 0.0f) v = half ? fminf(fmaxf(v, -L), L) : fminf(v, L);
+            tp[j * BS_EPI_LD + lane] = v;
+          }
+          mbar_arrive(&xfull[pr]);
+          if (!warp_wait(&xfull[pr], xph)) {
+            ok = false;
+            break;
+          }
+          const int jt = 16 * half + (lane >> 1), fh = lane & 1;
+          const float *tg = reinterpret_cast<const float *>(smem + Cfg::OFF_EPI + pr * BS_EPI_BYTES) +
+                            jt * BS_EPI_LD + fh * 16;
+          const float *tu = reinterpret_cast<const float *>(smem + Cfg::OFF_EPI +
+                                                            (pr + 2) * BS_EPI_BYTES) +
+                            jt * BS_EPI_LD + fh * 16;
+          const bool jlive = cc * 32 + jt < tl.w;
+          const int64_t pj = int64_t(tl.z) + cc * 32 + jt;
+          const float w = (args.pw && jlive) ? args.pw[pj] : 1.0f;
+          float h[16];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float4 g4 = reinterpret_cast<const float4 *>(tg)[i];
+            const float4 u4 = reinterpret_cast<const float4 *>(tu)[i];
+            const float gg[4] = {g4.x, g4.y, g4.z, g4.w}, uu[4] = {u4.x, u4.y, u4.z, u4.w};
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+              const float sg = __fdividef(gg[b], 1.0f + __expf(-gg[b]));
+              float v = sg * uu[b];
+              if (args.pw) v = v * w;
+              h[4 * i + b] = round_bf16f(v);
             }
+          }
+          mbar_arrive(&xempty[pr]);
+          // act_quant of the 32 features of row pj (docs/reference/kernel.py:40-95): the two
+          // lanes of a row combine their amax; the scale is a power of two, so x / s is the
+          // exact product x * (1 / s)
+          float amax = 0.0f;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              float u = round_bf16f(__uint_as_float(r[j]));
-              if (L > 0.0f) u = fminf(fmaxf(u, -L), L);
-              tp[j * BS_EPI_LD + lane] = u;
+          for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(h[i]));
+          amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+          amax = fmaxf(amax, 1e-4f);
+          const float sc = pow2_ceil_log2(__fmul_rn(amax, 1.0f / 448.0f));
+          const float inv = __uint_as_float((254u << 23) - __float_as_uint(sc));
+          uint32_t wq[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint32_t wv = 0;
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+              const float y = fminf(fmaxf(__fmul_rn(h[4 * i + b], inv), -448.0f), 448.0f);
+              wv |= uint32_t(f32_to_e4m3_sat(y)) << (8 * b);
             }
-            mbar_arrive(&xfull[pr]);
-          } else {
-            if (!warp_wait(&xfull[pr], xph)) {
-              ok = false;
-              break;
-            }
-            const float *ub = reinterpret_cast<const float *>(smem + BS_OFF_EPI +
-                                                              (q + 2) * BS_EPI_BYTES);
-            const float wl = (args.pw && live) ? args.pw[p_lane] : 1.0f;
-            float h[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              float g = round_bf16f(__uint_as_float(r[j]));
-              if (L > 0.0f) g = fminf(g, L);
-              const float u = ub[j * BS_EPI_LD + lane];
-              const float sg = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
-              float v = __fmul_rn(sg, u);
-              if (args.pw) v = __fmul_rn(v, __shfl_sync(0xffffffffu, wl, j));
-              h[j] = round_bf16f(v);
-            }
-            mbar_arrive(&xempty[pr]);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) tp[j * BS_EPI_LD + lane] = h[j];
-            __syncwarp();
-            if (live) {
-              // act_quant of 32 features of row p_lane (docs/reference/kernel.py:40-95)
-              const float *row = tp + lane * BS_EPI_LD;
-              float amax = 0.0f;
-#pragma unroll
-              for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(row[i]));
-              amax = fmaxf(amax, 1e-4f);
-              const float sc = pow2_ceil_log2(__fmul_rn(amax, 1.0f / 448.0f));
-              uint32_t wq[8];
-#pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                uint32_t w = 0;
-#pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                  const float y = fminf(fmaxf(__fdiv_rn(row[4 * i + b], sc), -448.0f), 448.0f);
-                  w |= uint32_t(f32_to_e4m3_sat(y)) << (8 * b);
-                }
-                wq[i] = w;
-              }
-              const int64_t f0 = int64_t(tl.y) * 64 + 32 * q;
-              uint4 *dst = reinterpret_cast<uint4 *>(args.hq + p_lane * args.ldh + f0);
-              dst[0] = make_uint4(wq[0], wq[1], wq[2], wq[3]);
-              dst[1] = make_uint4(wq[4], wq[5], wq[6], wq[7]);
-              args.hs[p_lane * (args.ldh / 32) + f0 / 32] =
-                  uint8_t((__float_as_uint(sc) >> 23) & 0xFF);
-            }
-            __syncwarp();
+            wq[i] = wv;
+          }
+          if (jlive) {
+            const int64_t f0 = int64_t(tl.y) * 64 + 32 * pr;
+            *reinterpret_cast<uint4 *>(args.hq + pj * args.ldh + f0 + fh * 16) =
+                make_uint4(wq[0], wq[1], wq[2], wq[3]);
+            if (fh == 0)
+              args.hs[pj * (args.ldh / 32) + f0 / 32] = uint8_t((__float_as_uint(sc) >> 23) & 0xFF);
           }
           ++xc;
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty);
+      if (lane == 0) {
+        mbar_arrive(&acc_empty[ab]);
+        mbar_arrive(&tempty[slot]);
+      }
       if (!ok) break;
     }
   }
@@ -478,7 +600,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, BS_TMEM_COLS);
+    tmem_dealloc(tmem, Cfg::TMEM_COLS);
   }
 }
 

@@ -879,31 +879,73 @@ int bs_wmap(CUtensorMap *m, const uint8_t *w, int wfmt, int64_t rows, int64_t K,
                       (uint64_t)K, 128, box_rows);
 }
 
+static_assert(PF_TILE_ROWS == BS_BN, "prefill tiles are GEMM tiles");
+
 int bs_xmaps(CUtensorMap (&m)[4], const uint8_t *x, int64_t rows, int64_t K) {
   for (int i = 0; i < 4; ++i) {
     int rc = make_tmap_2d(&m[i], x, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)K,
-                          (uint64_t)(rows < 1 ? 1 : rows), (uint64_t)K, 128, 32u << i);
+                          (uint64_t)(rows < 1 ? 1 : rows), (uint64_t)K, 128, bs_box_rows(i));
     if (rc) return rc;
   }
   return DSV41_OK;
 }
 
-template <int WF, int EPI>
+template <int WF, int EPI, bool NARROW>
 int bs_launch(const char *name, const BsMaps &maps, const BsArgs &a, int grid, cudaStream_t st) {
+  using Cfg = BsCfg<NARROW>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(k_bsgemm<WF, EPI>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, BS_SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(k_bsgemm<WF, EPI, NARROW>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
     if (e != cudaSuccess) return cuda_status(e, "bsgemm smem attribute");
     attr_set[dev] = true;
   }
   if (grid < 1) return DSV41_OK;
+  BsArgs g = a;
+  g.sf_async = (a.sw.kshift == 0 && a.sx.kshift == 0 &&
+                (EPI != BS_EPI_SWIGLU || a.sw2.kshift == 0)) ? 1 : 0;
+  g.nkb = a.nkb / Cfg::KSUB;
   ProfScope prof(name, st);
-  k_bsgemm<WF, EPI><<<grid, BS_THREADS, BS_SMEM_BYTES, st>>>(maps, a);
+  k_bsgemm<WF, EPI, NARROW><<<grid, BS_THREADS, Cfg::SMEM, st>>>(maps, g);
   DSV41_CHECK_LAUNCH(name);
   return DSV41_OK;
+}
+
+int bs_grid(int tiles) { return tiles < num_sms() ? tiles : num_sms(); }
+
+// Dense problem: static tiles of 128 weight rows (64 + 64 in SwiGLU mode) x BN activation
+// rows, the narrow shape when all activation rows fit one narrow tile.
+template <int WF, int EPI>
+int bs_dense_launch(const char *name, const BsMaps &maps, BsArgs a, int64_t N, int64_t M,
+                    cudaStream_t st) {
+  const bool narrow = M <= BS_BN_NARROW && a.nkb % BsCfg<true>::KSUB == 0;
+  a.dense_bn = narrow ? BS_BN_NARROW : BS_BN;
+  a.dense_nt = int(ceil_div(M, a.dense_bn));
+  a.dense_tiles = int(N / (EPI == BS_EPI_SWIGLU ? 64 : BS_BM)) * a.dense_nt;
+  a.dense_rows = int(M);
+  a.tiles = nullptr;
+  const int grid = bs_grid(a.dense_tiles);
+  return narrow ? bs_launch<WF, EPI, true>(name, maps, a, grid, st)
+                : bs_launch<WF, EPI, false>(name, maps, a, grid, st);
+}
+
+// Grouped problem: the wide tile list, then the narrow one, each taken from a work counter.
+template <int WF, int EPI>
+int bs_grouped_launch(const char *name_w, const char *name_n, const BsMaps &maps, BsArgs a,
+                      const PfPlan &plan, int list, cudaStream_t st) {
+  a.tiles = plan.tiles[list];
+  a.ntiles = plan.ntiles + list;
+  a.next_tile = plan.next_tile + list;
+  int rc = bs_launch<WF, EPI, false>(name_w, maps, a, num_sms(), st);
+  if (rc) return rc;
+  a.tiles = plan.tiles[list + 1];
+  a.ntiles = plan.ntiles + list + 1;
+  a.next_tile = plan.next_tile + list + 1;
+  if (a.nkb % BsCfg<true>::KSUB != 0)   // K not a multiple of the narrow stage: wide shape
+    return bs_launch<WF, EPI, false>(name_n, maps, a, num_sms(), st);
+  return bs_launch<WF, EPI, true>(name_n, maps, a, num_sms(), st);
 }
 
 BsScale bs_scale(const uint8_t *p, int64_t ld, int rshift, int kblock, int64_t rows) {
@@ -916,18 +958,13 @@ BsScale bs_scale(const uint8_t *p, int64_t ld, int rshift, int kblock, int64_t r
   return s;
 }
 
-BsArgs bs_args_dense(int64_t K, int64_t N, int64_t M, int n_per_tile) {
+BsArgs bs_args(int64_t K, int64_t a_rows) {
   BsArgs a;
   memset(&a, 0, sizeof(a));
   a.nkb = int(K / BS_BK);
-  a.a_rows = int(N);
-  a.dense_nt = int(ceil_div(M, BS_BN));
-  a.dense_tiles = int(N / n_per_tile) * a.dense_nt;
-  a.dense_rows = int(M);
+  a.a_rows = int(a_rows);
   return a;
 }
-
-int bs_grid(int tiles) { return tiles < num_sms() ? tiles : num_sms(); }
 
 // C[M, N] = A[M, K] . B[N, K]^T with fp8 A and fp8 / fp4 B (wfmt), ue8m0 scales.
 int bs_dense(int wfmt, const uint8_t *a, const uint8_t *a_s, int a_blk, const uint8_t *b,
@@ -948,17 +985,16 @@ int bs_dense(int wfmt, const uint8_t *a, const uint8_t *a_s, int a_blk, const ui
   int rc = bs_wmap(&maps.w, b, wfmt, N, K, 128);
   if (!rc) rc = bs_xmaps(maps.x, a, M, K);
   if (rc) return rc;
-  BsArgs g = bs_args_dense(K, N, M, BS_BM);
+  BsArgs g = bs_args(K, N);
   g.sw = bs_scale(b_s, K / b_blk, b_rshift, b_blk, N);
   g.sx = bs_scale(a_s, K / a_blk, 0, a_blk, M);
   g.out = c;
   g.ldo = N;
-  const int grid = bs_grid(g.dense_tiles);
   if (wfmt == BS_W_FP4)
-    return c_dtype == DSV41_F32 ? bs_launch<BS_W_FP4, BS_EPI_F32>("fp4_gemm", maps, g, grid, st)
-                                : bs_launch<BS_W_FP4, BS_EPI_BF16>("fp4_gemm", maps, g, grid, st);
-  return c_dtype == DSV41_F32 ? bs_launch<BS_W_FP8, BS_EPI_F32>("fp8_gemm", maps, g, grid, st)
-                              : bs_launch<BS_W_FP8, BS_EPI_BF16>("fp8_gemm", maps, g, grid, st);
+    return c_dtype == DSV41_F32 ? bs_dense_launch<BS_W_FP4, BS_EPI_F32>("fp4_gemm", maps, g, N, M, st)
+                                : bs_dense_launch<BS_W_FP4, BS_EPI_BF16>("fp4_gemm", maps, g, N, M, st);
+  return c_dtype == DSV41_F32 ? bs_dense_launch<BS_W_FP8, BS_EPI_F32>("fp8_gemm", maps, g, N, M, st)
+                              : bs_dense_launch<BS_W_FP8, BS_EPI_BF16>("fp8_gemm", maps, g, N, M, st);
 }
 
 }  // namespace
@@ -986,7 +1022,7 @@ extern "C" int dsv41_fp4_gemm(const uint8_t *a, const uint8_t *a_s, const uint8_
 namespace {
 
 struct PfDims {
-  int64_t T, D, I, E, P, nchunks, tiles_gu_cap, tiles_dn_cap;
+  int64_t T, D, I, E, P, nchunks, cap_w, cap_n;
   int k;
 };
 
@@ -999,9 +1035,8 @@ PfDims pf_dims(const dsv41_moe_config *cfg, int64_t T) {
   d.k = cfg->topk;
   d.P = T * cfg->topk;
   d.nchunks = ceil_div(d.P, PF_CHUNK);
-  const int64_t groups_cap = d.P / PF_TILE_ROWS + d.E + 1;
-  d.tiles_gu_cap = (d.I / 64) * groups_cap;
-  d.tiles_dn_cap = (d.D / BS_BM) * groups_cap;
+  d.cap_w = d.P / PF_TILE_ROWS + d.E + 1;       // row tiles of all experts, per m-tile
+  d.cap_n = d.E;
   return d;
 }
 
@@ -1043,9 +1078,13 @@ size_t pf_carve(const PfDims &d, bool route, bool shared, uint8_t *base, size_t 
   w.plan.pair_tok = c.take<int>(d.P);
   w.plan.pair_w = c.take<float>(d.P);
   w.plan.slot_pos = c.take<int>(d.P);
-  w.plan.tiles_gu = c.take<int4>(d.tiles_gu_cap);
-  w.plan.tiles_dn = c.take<int4>(d.tiles_dn_cap);
-  w.plan.ntiles = c.take<int>(2);
+  const int64_t mts[2] = {d.I / 64, d.D / BS_BM};
+  for (int pj = 0; pj < 2; ++pj) {
+    w.plan.tiles[2 * pj] = c.take<int4>(mts[pj] * d.cap_w);
+    w.plan.tiles[2 * pj + 1] = c.take<int4>(mts[pj] * d.cap_n);
+  }
+  w.plan.ntiles = c.take<int>(4);
+  w.plan.next_tile = c.take<int>(4);
   if (ws) *ws = w;
   return c.off + 256;
 }
@@ -1143,7 +1182,6 @@ extern "C" int dsv41_moe_prefill(const dsv41_moe_config *cfg, const dsv41_moe_we
                                                                    d.P, d.D, ws.xpq, ws.xps);
     DSV41_CHECK_LAUNCH("pf_gather");
   }
-  const int grid = num_sms();
   // routed gate/up: SwiGLU * routing weight, bf16, act_quant -> hq/hs
   {
     BsMaps maps;
@@ -1159,14 +1197,13 @@ extern "C" int dsv41_moe_prefill(const dsv41_moe_config *cfg, const dsv41_moe_we
     a.sw = bs_scale(W->s1, d.D / 32, 0, 32, d.E * d.I);
     a.sw2 = bs_scale(W->s3, d.D / 32, 0, 32, d.E * d.I);
     a.sx = bs_scale(ws.xps, d.D / 32, 0, 32, d.P);
-    a.tiles = ws.plan.tiles_gu;
-    a.ntiles = ws.plan.ntiles;
     a.pw = ws.plan.pair_w;
     a.hq = ws.hq;
     a.hs = ws.hs;
     a.ldh = d.I;
     a.limit = cfg->swiglu_limit;
-    rc = bs_launch<BS_W_FP4, BS_EPI_SWIGLU>("pf_gate_up_fp4", maps, a, grid, st);
+    rc = bs_grouped_launch<BS_W_FP4, BS_EPI_SWIGLU>("pf_gate_up_fp4", "pf_gate_up_fp4_narrow",
+                                                    maps, a, ws.plan, 0, st);
     if (rc) return rc;
   }
   // routed down -> yp (bf16 per pair)
@@ -1182,11 +1219,10 @@ extern "C" int dsv41_moe_prefill(const dsv41_moe_config *cfg, const dsv41_moe_we
     a.a_rows = int(d.D);
     a.sw = bs_scale(W->s2, d.I / 32, 0, 32, d.E * d.D);
     a.sx = bs_scale(ws.hs, d.I / 32, 0, 32, d.P);
-    a.tiles = ws.plan.tiles_dn;
-    a.ntiles = ws.plan.ntiles + 1;
     a.out = ws.yp;
     a.ldo = d.D;
-    rc = bs_launch<BS_W_FP4, BS_EPI_BF16>("pf_down_fp4", maps, a, grid, st);
+    rc = bs_grouped_launch<BS_W_FP4, BS_EPI_BF16>("pf_down_fp4", "pf_down_fp4_narrow", maps, a,
+                                                  ws.plan, 2, st);
     if (rc) return rc;
   }
   if (shared) {
@@ -1196,7 +1232,7 @@ extern "C" int dsv41_moe_prefill(const dsv41_moe_config *cfg, const dsv41_moe_we
     if (!rc) rc = bs_wmap(&maps.w2, W->sw3, BS_W_FP8, d.I, d.D, 64);
     if (!rc) rc = bs_xmaps(maps.x, ws.xq, d.T, d.D);
     if (rc) return rc;
-    BsArgs a = bs_args_dense(d.D, d.I, d.T, 64);
+    BsArgs a = bs_args(d.D, d.I);
     a.sw = bs_scale(W->ss1, d.D / 32, 5, 32, d.I);
     a.sw2 = bs_scale(W->ss3, d.D / 32, 5, 32, d.I);
     a.sx = bs_scale(ws.xs, d.D / 32, 0, 32, d.T);
@@ -1204,20 +1240,19 @@ extern "C" int dsv41_moe_prefill(const dsv41_moe_config *cfg, const dsv41_moe_we
     a.hs = ws.shs;
     a.ldh = d.I;
     a.limit = cfg->swiglu_limit;
-    rc = bs_launch<BS_W_FP8, BS_EPI_SWIGLU>("pf_shared_gate_up_fp8", maps, a,
-                                            bs_grid(a.dense_tiles), st);
+    rc = bs_dense_launch<BS_W_FP8, BS_EPI_SWIGLU>("pf_shared_gate_up_fp8", maps, a, d.I, d.T, st);
     if (rc) return rc;
     BsMaps m2;
     memset(&m2, 0, sizeof(m2));
     rc = bs_wmap(&m2.w, W->sw2, BS_W_FP8, d.D, d.I, 128);
     if (!rc) rc = bs_xmaps(m2.x, ws.shq, d.T, d.I);
     if (rc) return rc;
-    BsArgs b = bs_args_dense(d.I, d.D, d.T, BS_BM);
+    BsArgs b = bs_args(d.I, d.D);
     b.sw = bs_scale(W->ss2, d.I / 32, 5, 32, d.D);
     b.sx = bs_scale(ws.shs, d.I / 32, 0, 32, d.T);
     b.out = ws.ysh;
     b.ldo = d.D;
-    rc = bs_launch<BS_W_FP8, BS_EPI_BF16>("pf_shared_down_fp8", m2, b, bs_grid(b.dense_tiles), st);
+    rc = bs_dense_launch<BS_W_FP8, BS_EPI_BF16>("pf_shared_down_fp8", m2, b, d.D, d.T, st);
     if (rc) return rc;
   }
   {

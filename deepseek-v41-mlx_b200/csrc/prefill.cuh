@@ -12,7 +12,7 @@
 namespace dsv41 {
 
 constexpr int PF_CHUNK = 512;       // pairs per counting block (16 warps)
-constexpr int PF_TILE_ROWS = 256;   // activation rows per GEMM tile
+constexpr int PF_TILE_ROWS = 224;   // activation rows per GEMM tile (the GEMM's N)
 
 struct PfPlan {
   int *chunk_base;     // [nchunks, E]: pairs of expert e in earlier chunks
@@ -21,10 +21,14 @@ struct PfPlan {
   int *pair_tok;       // [P] token of sorted pair
   float *pair_w;       // [P] routing weight of sorted pair
   int *slot_pos;       // [T*k] sorted position of pair (t, j)
-  int4 *tiles_gu;      // gate/up tiles {expert, m-tile, first row, rows}
-  int4 *tiles_dn;      // down tiles
-  int *ntiles;         // [0] gate/up, [1] down
+  int4 *tiles[4];      // {expert, m-tile, first row, rows}: gate/up wide, gate/up narrow,
+                       // down wide, down narrow
+  int *ntiles;         // [4] tile counts of the four lists
+  int *next_tile;      // [4] work counters of the four launches (zeroed here)
 };
+
+// Tiles with at most this many rows (after rounding up to 16) go to the narrow GEMM shape.
+constexpr int PF_NARROW_ROWS = 64;
 
 __global__ void __launch_bounds__(PF_CHUNK) k_pf_count(const int32_t *__restrict__ idx, int64_t P,
                                                        int E, int *__restrict__ chunk_cnt) {
@@ -86,7 +90,10 @@ __device__ __forceinline__ void block_scan3(int (&v)[3], int (&excl)[3], int (&t
   }
 }
 
-// One CTA of 1024 threads, one expert per thread (E <= 1024).
+// One CTA of 1024 threads, one expert per thread (E <= 1024).  An expert with n pairs has
+// ceil(n / 224) row tiles; its last tile is narrow when it holds <= 64 rows.  Each list is
+// ordered expert-major, then m-tile, then row tile, so tiles that share weights or
+// activations are taken close together.
 __global__ void __launch_bounds__(1024) k_pf_scan(int *__restrict__ chunk_cnt, int nchunks, int E,
                                                   int mt_gu, int mt_dn, PfPlan plan) {
   const int e = threadIdx.x;
@@ -99,23 +106,33 @@ __global__ void __launch_bounds__(1024) k_pf_scan(int *__restrict__ chunk_cnt, i
     }
   }
   const int nnt = (run + PF_TILE_ROWS - 1) / PF_TILE_ROWS;
-  int v[3] = {run, nnt * mt_gu, nnt * mt_dn}, excl[3], tot[3];
+  const int tail = run - (nnt - 1) * PF_TILE_ROWS;
+  const int nnar = (nnt > 0 && ((tail + 15) & ~15) <= PF_NARROW_ROWS) ? 1 : 0;
+  const int nwide = nnt - nnar;
+  int v[3] = {run, nwide, nnar}, excl[3], tot[3];
   block_scan3(v, excl, tot);
   if (e < E) {
     plan.grp_off[e] = excl[0];
     plan.grp_cnt[e] = run;
-    for (int mt = 0; mt < mt_gu; ++mt)
-      for (int nt = 0; nt < nnt; ++nt)
-        plan.tiles_gu[excl[1] + mt * nnt + nt] =
-            make_int4(e, mt, excl[0] + nt * PF_TILE_ROWS, min(PF_TILE_ROWS, run - nt * PF_TILE_ROWS));
-    for (int mt = 0; mt < mt_dn; ++mt)
-      for (int nt = 0; nt < nnt; ++nt)
-        plan.tiles_dn[excl[2] + mt * nnt + nt] =
-            make_int4(e, mt, excl[0] + nt * PF_TILE_ROWS, min(PF_TILE_ROWS, run - nt * PF_TILE_ROWS));
+    const int mts[2] = {mt_gu, mt_dn};
+    for (int pj = 0; pj < 2; ++pj) {
+      const int mt_n = mts[pj];
+      int4 *tw = plan.tiles[2 * pj] + int64_t(excl[1]) * mt_n;
+      int4 *tn = plan.tiles[2 * pj + 1] + int64_t(excl[2]) * mt_n;
+      for (int mt = 0; mt < mt_n; ++mt) {
+        for (int j = 0; j < nwide; ++j)
+          tw[mt * nwide + j] = make_int4(e, mt, excl[0] + j * PF_TILE_ROWS,
+                                         min(PF_TILE_ROWS, run - j * PF_TILE_ROWS));
+        if (nnar) tn[mt] = make_int4(e, mt, excl[0] + nwide * PF_TILE_ROWS, tail);
+      }
+    }
   }
   if (threadIdx.x == 0) {
-    plan.ntiles[0] = tot[1];
-    plan.ntiles[1] = tot[2];
+    plan.ntiles[0] = tot[1] * mt_gu;
+    plan.ntiles[1] = tot[2] * mt_gu;
+    plan.ntiles[2] = tot[1] * mt_dn;
+    plan.ntiles[3] = tot[2] * mt_dn;
+    for (int i = 0; i < 4; ++i) plan.next_tile[i] = 0;
   }
 }
 
