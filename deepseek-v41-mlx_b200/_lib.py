@@ -79,9 +79,11 @@ PROTOTYPES = {
                               _P, _P, _SZ, _P]),
     "dsv41_fp8_gemm": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I, _P, _I, _P]),
     "dsv41_fp4_gemm": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I, _P, _I, _P]),
-    "dsv41_moe_prefill_workspace_size": (_SZ, [C.POINTER(MoeConfig), _I64, _I]),
-    "dsv41_moe_prefill": (_I, [C.POINTER(MoeConfig), C.POINTER(MoeWeights), _P, _I64, _P, _P, _I,
-                               _P, _P, _SZ, _P]),
+    "dsv41_moe_prefill_pack_size": (_SZ, [C.POINTER(MoeConfig)]),
+    "dsv41_moe_prefill_pack": (_I, [C.POINTER(MoeConfig), C.POINTER(MoeWeights), _P, _SZ, _P]),
+    "dsv41_moe_prefill_workspace_size": (_SZ, [C.POINTER(MoeConfig), _I64, _I, _I]),
+    "dsv41_moe_prefill": (_I, [C.POINTER(MoeConfig), C.POINTER(MoeWeights), _P, _P, _I64, _P, _P,
+                               _I, _P, _P, _SZ, _P]),
     "dsv41_engram_hash": (_I, [_P, _I64, _I64, _I64, _P, _I64, _P, _I64, _P, _P, _P, _I, _I, _I,
                                _I64, _P, _P]),
     "dsv41_engram_gather_rows": (_I, [_P, _P, _I64, _I64, _I64, _I64, _P, _I64, _I, _P, _P]),

@@ -101,13 +101,21 @@ struct BsArgs {
   int a_rows;          // weight rows of one group (N; I in SwiGLU mode)
   BsScale sw, sw2;     // weight scales (sw2: up projection in SwiGLU mode)
   BsScale sx;          // activation scales
-  const int4 *tiles;   // grouped: {group, m-tile, first activation row, rows}; null = dense
+  const int4 *tiles;   // grouped: {group, m-tile, first activation row, rows | row tile << 8};
+                       // null = dense
   const int *ntiles;   // grouped tile count (device)
   int *next_tile;      // grouped: work counter (zeroed before the launch), tiles taken in order
   int dense_tiles, dense_nt, dense_bn, dense_rows;
   void *out;           // store mode: out[p * ldo + n]
   int64_t ldo;
-  int sf_async;        // 1: every scale operand is per-32 (cp.async staging)
+  int sf_async;        // 1: every staged scale operand is per-32 (cp.async staging)
+  int nkq;             // K / 128 (scale-atom addressing)
+  int mtiles;          // m-tiles per group (weight-atom addressing)
+  const uint8_t *sfa_atoms;  // weight scales as tcgen05.cp atoms [group][m-tile][K/128][512]
+                             // (null: staged from sw / sw2)
+  const uint8_t *sfb_atoms;  // activation scales as atoms [row tile][K/128][2][512]
+                             // (null: staged from sx)
+  uint8_t *hs_atoms;   // SwiGLU: write h's scales as atoms [row tile][ldh/128][2][512]
   const float *pw;     // SwiGLU: per-row routing weight (null = none)
   uint8_t *hq;         // SwiGLU: fp8 h [rows, ldh]
   uint8_t *hs;         // SwiGLU: ue8m0 scales of h [rows, ldh / 32]
@@ -182,6 +190,19 @@ __device__ __forceinline__ void cp_async4(uint32_t dst, const void *src, uint32_
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
                : "memory");
 }
+// Bulk copy global -> shared (16-byte aligned, size a multiple of 16), completes on `bar`.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes,
+                                          uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+// Byte offset of row r (of a <= 256-row tile), 32-wide K block j, in a tile's scale atoms
+// [K/128][2][512]: atom (r / 128) of K stage j / 4, lane r % 32, column (r / 32) % 4, byte j % 4.
+__host__ __device__ __forceinline__ int64_t sf_atom_off(int r, int j) {
+  return int64_t(j >> 2) * 1024 + (r >> 7) * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4 + (j & 3);
+}
 // Arrive on `bar` (counted in its expected arrivals) once this thread's cp.asyncs landed.
 __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t *bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
@@ -228,7 +249,7 @@ __device__ __forceinline__ uint32_t bs_scale_word(const BsScale &s, int64_t row,
 __device__ __forceinline__ int4 bs_dense_tile(const BsArgs &a, int t) {
   const int nt = t % a.dense_nt, mt = t / a.dense_nt;
   const int row0 = nt * a.dense_bn;
-  return make_int4(0, mt, row0, min(a.dense_bn, a.dense_rows - row0));
+  return make_int4(0, mt, row0, min(a.dense_bn, a.dense_rows - row0) | (nt << 8));
 }
 
 template <int BN>
@@ -258,7 +279,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
   const uint32_t sbase = smem_u32(smem);
   int4 *ring = reinterpret_cast<int4 *>(smem + Cfg::OFF_RING);
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Cfg::OFF_BAR);
-  uint64_t *full = bars;                    // [S] count 33
+  uint64_t *full = bars;                    // [S] count 33 (1 when all scales are atoms)
   uint64_t *empty = bars + S;               // [S] count 1 (tcgen05.commit)
   uint64_t *acc_full = bars + 2 * S;        // [2] count 1 (tcgen05.commit)
   uint64_t *acc_empty = acc_full + 2;       // [2] count 4 (epilogue warps)
@@ -271,8 +292,9 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
+    const bool lanes = !(args.sfa_atoms && args.sfb_atoms);   // some scales staged by lanes
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 33);
+      mbar_init(&full[s], lanes ? 33 : 1);
       mbar_init(&empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -329,8 +351,12 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
       tl.z = __shfl_sync(0xffffffffu, tl.z, 0);
       tl.w = __shfl_sync(0xffffffffu, tl.w, 0);
       if (tl.x < 0) break;
-      const int nmma = bs_nmma<Cfg::BN>(tl.w), bi = bs_box(nmma);
+      const int nrows = tl.w & 0xFF, rtile = tl.w >> 8;
+      const int nmma = bs_nmma<Cfg::BN>(nrows), bi = bs_box(nmma);
       const uint32_t x_tx = bs_box_rows(bi) * BS_BK;
+      const uint32_t sfb_ks = (NARROW || nmma <= 128) ? 512u : 1024u;   // atom bytes per K stage
+      const uint32_t sf_tx = (args.sfa_atoms ? 512u * Cfg::KSUB : 0u) +
+                             (args.sfb_atoms ? sfb_ks * Cfg::KSUB : 0u);
       const int64_t wrow0 = int64_t(tl.x) * args.a_rows +
                             int64_t(tl.y) * (EPI == BS_EPI_SWIGLU ? 64 : BS_BM);
       for (int kb = 0; kb < nkb; ++kb, ++it) {
@@ -343,7 +369,19 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
         uint8_t *sa = smem + Cfg::OFF_A + s * Cfg::A_BYTES;
         uint8_t *sb = smem + Cfg::OFF_B + s * Cfg::B_BYTES;
         if (lane == 0) {
-          mbar_arrive_expect_tx(&full[s], uint32_t(Cfg::KSUB) * (W_TX + x_tx));
+          mbar_arrive_expect_tx(&full[s], uint32_t(Cfg::KSUB) * (W_TX + x_tx) + sf_tx);
+          if (args.sfa_atoms)
+            bulk_load(sbase + Cfg::OFF_SFA + s * Cfg::SFA_BYTES,
+                      args.sfa_atoms + ((int64_t(tl.x) * args.mtiles + tl.y) * args.nkq +
+                                        kb * Cfg::KSUB) * 512,
+                      512u * Cfg::KSUB, &full[s]);
+          if (args.sfb_atoms) {
+#pragma unroll
+            for (int ks = 0; ks < Cfg::KSUB; ++ks)
+              bulk_load(sbase + Cfg::OFF_SFB + s * Cfg::SFB_BYTES + ks * Cfg::SFB_SUB,
+                        args.sfb_atoms + (int64_t(rtile) * args.nkq + kb * Cfg::KSUB + ks) * 1024,
+                        sfb_ks, &full[s]);
+          }
 #pragma unroll
           for (int ks = 0; ks < Cfg::KSUB; ++ks) {
             const int kx = (kb * Cfg::KSUB + ks) * BS_BK;
@@ -362,30 +400,36 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
           const uint32_t sfb = sbase + Cfg::OFF_SFB + s * Cfg::SFB_BYTES + ks * Cfg::SFB_SUB +
                                lane * 16;
           if (args.sf_async) {
+            if (!args.sfa_atoms) {
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              if (EPI == BS_EPI_SWIGLU && c >= 2)
-                bs_scale_copy(args.sw2, wrow0 + 32 * (c - 2) + lane, kq, sfa + 4 * c);
-              else
-                bs_scale_copy(args.sw, wrow0 + 32 * c + lane, kq, sfa + 4 * c);
+              for (int c = 0; c < 4; ++c) {
+                if (EPI == BS_EPI_SWIGLU && c >= 2)
+                  bs_scale_copy(args.sw2, wrow0 + 32 * (c - 2) + lane, kq, sfa + 4 * c);
+                else
+                  bs_scale_copy(args.sw, wrow0 + 32 * c + lane, kq, sfa + 4 * c);
+              }
             }
+            if (!args.sfb_atoms) {
 #pragma unroll
-            for (int c = 0; c < Cfg::SFB_CHUNKS; ++c)
-              bs_scale_copy(args.sx, int64_t(tl.z) + 32 * c + lane, kq,
-                            sfb + (c >> 2) * 512 + 4 * (c & 3));
+              for (int c = 0; c < Cfg::SFB_CHUNKS; ++c)
+                bs_scale_copy(args.sx, int64_t(tl.z) + 32 * c + lane, kq,
+                              sfb + (c >> 2) * 512 + 4 * (c & 3));
+            }
           } else {
             uint4 va;
             uint32_t *vw = reinterpret_cast<uint32_t *>(&va);
+            if (!args.sfa_atoms) {
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              if (EPI == BS_EPI_SWIGLU && c >= 2)
-                vw[c] = bs_scale_word(args.sw2, wrow0 + 32 * (c - 2) + lane, kq);
-              else
-                vw[c] = bs_scale_word(args.sw, wrow0 + 32 * c + lane, kq);
+              for (int c = 0; c < 4; ++c) {
+                if (EPI == BS_EPI_SWIGLU && c >= 2)
+                  vw[c] = bs_scale_word(args.sw2, wrow0 + 32 * (c - 2) + lane, kq);
+                else
+                  vw[c] = bs_scale_word(args.sw, wrow0 + 32 * c + lane, kq);
+              }
+              *reinterpret_cast<uint4 *>(smem + (sfa - sbase)) = va;
             }
-            *reinterpret_cast<uint4 *>(smem + (sfa - sbase)) = va;
 #pragma unroll
-            for (int h = 0; h < Cfg::SFB_ATOMS; ++h) {
+            for (int h = 0; h < (args.sfb_atoms ? 0 : Cfg::SFB_ATOMS); ++h) {
               uint4 vb;
               uint32_t *bw = reinterpret_cast<uint32_t *>(&vb);
 #pragma unroll
@@ -395,7 +439,9 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
             }
           }
         }
-        if (args.sf_async) {
+        if (args.sfa_atoms && args.sfb_atoms) {
+          // every scale arrives by bulk copy: lane 0's expect_tx is the only arrival
+        } else if (args.sf_async) {
           cp_async_arrive_noinc(&full[s]);
         } else {
           fence_proxy_async_smem();
@@ -415,7 +461,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
         if (!mbar_wait(&tfull[slot], uint32_t(ti / BS_RING) & 1u)) break;
         const int4 tl = ring[slot];
         if (tl.x < 0) break;
-        const int nmma = bs_nmma<Cfg::BN>(tl.w);
+        const int nmma = bs_nmma<Cfg::BN>(tl.w & 0xFF);
         const int ab = ti & 1;
         if (!mbar_wait(&acc_empty[ab], (uint32_t(ti >> 1) & 1u) ^ 1u)) break;
         tc_fence_after();
@@ -471,7 +517,8 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
       if (!warp_wait(&tfull[slot], uint32_t(ti / BS_RING) & 1u)) break;
       const int4 tl = ring[slot];
       if (tl.x < 0) break;
-      const int nmma = bs_nmma<Cfg::BN>(tl.w);
+      const int nrows = tl.w & 0xFF, rtile = tl.w >> 8;
+      const int nmma = bs_nmma<Cfg::BN>(nrows);
       const int ab = ti & 1;
       if (!warp_wait(&acc_full[ab], uint32_t(ti >> 1) & 1u)) break;
       tc_fence_after();
@@ -481,7 +528,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
         uint32_t r[32];
         tmem_ld32(tq + uint32_t(cc * 32), r);
         const int64_t p_lane = int64_t(tl.z) + cc * 32 + lane;   // this lane's row after transpose
-        const bool live = cc * 32 + lane < tl.w;
+        const bool live = cc * 32 + lane < nrows;
         if constexpr (EPI != BS_EPI_SWIGLU) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) tp[j * BS_EPI_LD + lane] = __uint_as_float(r[j]);
@@ -538,7 +585,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
           const float *tu = reinterpret_cast<const float *>(smem + Cfg::OFF_EPI +
                                                             (pr + 2) * BS_EPI_BYTES) +
                             jt * BS_EPI_LD + fh * 16;
-          const bool jlive = cc * 32 + jt < tl.w;
+          const bool jlive = cc * 32 + jt < nrows;
           const int64_t pj = int64_t(tl.z) + cc * 32 + jt;
           const float w = (args.pw && jlive) ? args.pw[pj] : 1.0f;
           float h[16];
@@ -581,8 +628,14 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
             const int64_t f0 = int64_t(tl.y) * 64 + 32 * pr;
             *reinterpret_cast<uint4 *>(args.hq + pj * args.ldh + f0 + fh * 16) =
                 make_uint4(wq[0], wq[1], wq[2], wq[3]);
-            if (fh == 0)
-              args.hs[pj * (args.ldh / 32) + f0 / 32] = uint8_t((__float_as_uint(sc) >> 23) & 0xFF);
+            if (fh == 0) {
+              const uint8_t e8 = uint8_t((__float_as_uint(sc) >> 23) & 0xFF);
+              if (args.hs_atoms)
+                args.hs_atoms[int64_t(rtile) * (args.ldh / 128) * 1024 +
+                              sf_atom_off(cc * 32 + jt, int(f0 / 32))] = e8;
+              else
+                args.hs[pj * (args.ldh / 32) + f0 / 32] = e8;
+            }
           }
           ++xc;
         }

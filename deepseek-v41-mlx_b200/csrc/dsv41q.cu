@@ -1022,9 +1022,17 @@ extern "C" int dsv41_fp4_gemm(const uint8_t *a, const uint8_t *a_s, const uint8_
 namespace {
 
 struct PfDims {
-  int64_t T, D, I, E, P, nchunks, cap_w, cap_n;
+  int64_t T, D, I, E, P, nchunks, cap_w, cap_n, cap_rt;
   int k;
 };
+
+// Packed weight scales (tcgen05.cp atoms, see k_pack_sfw): gate/up paired, then down.
+size_t pf_packed_gu_bytes(const dsv41_moe_config *c) {
+  return size_t(c->n_experts) * (c->inter / 64) * (c->dim / 128) * 512;
+}
+size_t pf_packed_bytes(const dsv41_moe_config *c) {
+  return pf_packed_gu_bytes(c) + size_t(c->n_experts) * (c->dim / 128) * (c->inter / 128) * 512;
+}
 
 PfDims pf_dims(const dsv41_moe_config *cfg, int64_t T) {
   PfDims d;
@@ -1037,6 +1045,7 @@ PfDims pf_dims(const dsv41_moe_config *cfg, int64_t T) {
   d.nchunks = ceil_div(d.P, PF_CHUNK);
   d.cap_w = d.P / PF_TILE_ROWS + d.E + 1;       // row tiles of all experts, per m-tile
   d.cap_n = d.E;
+  d.cap_rt = d.cap_w;
   return d;
 }
 
@@ -1044,13 +1053,16 @@ struct PfWs {
   float *w;
   int32_t *idx;
   float *rpart;
-  uint8_t *xq, *xs, *xpq, *xps, *hq, *hs, *shq, *shs;
+  uint8_t *xq, *xs, *xpq, *hq, *shq, *shs;
+  uint8_t *sfx_gu, *sfx_dn;   // activation scale atoms of the row tiles (gate/up, down inputs)
+  uint8_t *packed;            // weight scale atoms when the caller passes none
   __nv_bfloat16 *yp, *ysh;
   int *chunk_cnt;
   PfPlan plan;
 };
 
-size_t pf_carve(const PfDims &d, bool route, bool shared, uint8_t *base, size_t cap, PfWs *ws) {
+size_t pf_carve(const dsv41_moe_config *cfg, const PfDims &d, bool route, bool shared,
+                bool pack, uint8_t *base, size_t cap, PfWs *ws) {
   WsCarve c{base, cap, 0};
   PfWs w;
   memset(&w, 0, sizeof(w));
@@ -1062,10 +1074,11 @@ size_t pf_carve(const PfDims &d, bool route, bool shared, uint8_t *base, size_t 
   w.xq = c.take<uint8_t>(d.T * d.D);
   w.xs = c.take<uint8_t>(d.T * d.D / 32);
   w.xpq = c.take<uint8_t>(d.P * d.D);
-  w.xps = c.take<uint8_t>(d.P * d.D / 32);
   w.hq = c.take<uint8_t>(d.P * d.I);
-  w.hs = c.take<uint8_t>(d.P * d.I / 32);
+  w.sfx_gu = c.take<uint8_t>(d.cap_rt * (d.D / 128) * 1024);
+  w.sfx_dn = c.take<uint8_t>(d.cap_rt * (d.I / 128) * 1024);
   w.yp = c.take<__nv_bfloat16>(d.P * d.D);
+  if (pack) w.packed = c.take<uint8_t>(pf_packed_bytes(cfg));
   if (shared) {
     w.shq = c.take<uint8_t>(d.T * d.I);
     w.shs = c.take<uint8_t>(d.T * d.I / 32);
@@ -1074,10 +1087,11 @@ size_t pf_carve(const PfDims &d, bool route, bool shared, uint8_t *base, size_t 
   w.chunk_cnt = c.take<int>(d.nchunks * d.E);
   w.plan.chunk_base = w.chunk_cnt;
   w.plan.grp_off = c.take<int>(d.E);
-  w.plan.grp_cnt = c.take<int>(d.E);
+  w.plan.grp_rt0 = c.take<int>(d.E);
   w.plan.pair_tok = c.take<int>(d.P);
   w.plan.pair_w = c.take<float>(d.P);
   w.plan.slot_pos = c.take<int>(d.P);
+  w.plan.row_tile = c.take<int>(d.P);
   const int64_t mts[2] = {d.I / 64, d.D / BS_BM};
   for (int pj = 0; pj < 2; ++pj) {
     w.plan.tiles[2 * pj] = c.take<int4>(mts[pj] * d.cap_w);
@@ -1113,21 +1127,52 @@ int pf_check(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, int64_t T,
 
 }  // namespace
 
+namespace {
+int pf_pack(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, uint8_t *out,
+            cudaStream_t st) {
+  const int64_t E = cfg->n_experts, D = cfg->dim, I = cfg->inter;
+  ProfScope prof("pf_pack_scales", st);
+  k_pack_sfw<<<unsigned(4 * num_sms()), 256, 0, st>>>(W->s1, W->s3, E, I, D, 1, out);
+  DSV41_CHECK_LAUNCH("pack gate/up scales");
+  k_pack_sfw<<<unsigned(4 * num_sms()), 256, 0, st>>>(W->s2, nullptr, E, D, I, 0,
+                                                      out + pf_packed_gu_bytes(cfg));
+  DSV41_CHECK_LAUNCH("pack down scales");
+  return DSV41_OK;
+}
+}  // namespace
+
+extern "C" size_t dsv41_moe_prefill_pack_size(const dsv41_moe_config *cfg) {
+  return cfg ? pf_packed_bytes(cfg) : 0;
+}
+
+extern "C" int dsv41_moe_prefill_pack(const dsv41_moe_config *cfg, const dsv41_moe_weights *W,
+                                      void *packed, size_t packed_bytes, void *stream) {
+  int rc = pf_check(cfg, W, 1, false);
+  if (rc) return rc;
+  DSV41_REQUIRE(packed && packed_bytes >= pf_packed_bytes(cfg) && aligned(packed, 16),
+                DSV41_ERR_WORKSPACE, "packed buffer too small or misaligned");
+  return pf_pack(cfg, W, reinterpret_cast<uint8_t *>(packed), STREAM(stream));
+}
+
 extern "C" size_t dsv41_moe_prefill_workspace_size(const dsv41_moe_config *cfg, int64_t T,
-                                                   int with_routing) {
+                                                   int with_routing, int with_packed) {
   if (!cfg || T <= 0) return 256;
   const bool shared = (cfg->flags & DSV41_MOE_NO_SHARED) == 0;
-  return pf_carve(pf_dims(cfg, T), with_routing == 0, shared, nullptr, ~size_t(0) >> 1, nullptr);
+  return pf_carve(cfg, pf_dims(cfg, T), with_routing == 0, shared, with_packed == 0, nullptr,
+                  ~size_t(0) >> 1, nullptr);
 }
 
 extern "C" int dsv41_moe_prefill(const dsv41_moe_config *cfg, const dsv41_moe_weights *W,
-                                 const void *x, int64_t T, const float *route_weights,
-                                 const int32_t *route_indices, int out_dtype, void *y,
-                                 void *workspace, size_t workspace_bytes, void *stream) {
+                                 const void *packed_scales, const void *x, int64_t T,
+                                 const float *route_weights, const int32_t *route_indices,
+                                 int out_dtype, void *y, void *workspace, size_t workspace_bytes,
+                                 void *stream) {
   const bool shared = cfg && (cfg->flags & DSV41_MOE_NO_SHARED) == 0;
   int rc = pf_check(cfg, W, T, shared);
   if (rc) return rc;
   if (T == 0) return DSV41_OK;
+  DSV41_REQUIRE(!packed_scales || aligned(packed_scales, 16), DSV41_ERR_MISALIGNED,
+                "packed scales must be 16-byte aligned");
   DSV41_REQUIRE(out_dtype == DSV41_F32 || out_dtype == DSV41_BF16, DSV41_ERR_BAD_DTYPE,
                 "output must be F32 or BF16");
   DSV41_REQUIRE(x && y && aligned(x, 16) && aligned(y, 16), DSV41_ERR_MISALIGNED,
@@ -1136,8 +1181,8 @@ extern "C" int dsv41_moe_prefill(const dsv41_moe_config *cfg, const dsv41_moe_we
   DSV41_REQUIRE(!route || W->gate_w, DSV41_ERR_BAD_ARG, "NULL gate weight");
   const PfDims d = pf_dims(cfg, T);
   PfWs ws;
-  const size_t need = pf_carve(d, route, shared, reinterpret_cast<uint8_t *>(workspace),
-                               workspace_bytes, &ws);
+  const size_t need = pf_carve(cfg, d, route, shared, packed_scales == nullptr,
+                               reinterpret_cast<uint8_t *>(workspace), workspace_bytes, &ws);
   DSV41_REQUIRE(workspace && workspace_bytes >= need, DSV41_ERR_WORKSPACE,
                 "workspace too small (%zu < %zu)", workspace_bytes, need);
   cudaStream_t st = STREAM(stream);
@@ -1151,6 +1196,12 @@ extern "C" int dsv41_moe_prefill(const dsv41_moe_config *cfg, const dsv41_moe_we
     if (rc) return rc;
     rw = ws.w;
     ri = ws.idx;
+  }
+  const uint8_t *packed = reinterpret_cast<const uint8_t *>(packed_scales);
+  if (!packed) {
+    rc = pf_pack(cfg, W, ws.packed, st);
+    if (rc) return rc;
+    packed = ws.packed;
   }
   // act_quant(x, 32, ue8m0) once per token
   {
@@ -1178,8 +1229,8 @@ extern "C" int dsv41_moe_prefill(const dsv41_moe_config *cfg, const dsv41_moe_we
   }
   {
     ProfScope prof("pf_gather", st);
-    k_pf_gather<<<unsigned(ceil_div(d.P * 32, 256)), 256, 0, st>>>(ws.xq, ws.xs, ws.plan.pair_tok,
-                                                                   d.P, d.D, ws.xpq, ws.xps);
+    k_pf_gather<<<unsigned(ceil_div(d.P * 32, 256)), 256, 0, st>>>(
+        ws.xq, ws.xs, ws.plan.pair_tok, ws.plan.row_tile, d.P, d.D, ws.xpq, ws.sfx_gu);
     DSV41_CHECK_LAUNCH("pf_gather");
   }
   // routed gate/up: SwiGLU * routing weight, bf16, act_quant -> hq/hs
@@ -1196,10 +1247,13 @@ extern "C" int dsv41_moe_prefill(const dsv41_moe_config *cfg, const dsv41_moe_we
     a.a_rows = int(d.I);
     a.sw = bs_scale(W->s1, d.D / 32, 0, 32, d.E * d.I);
     a.sw2 = bs_scale(W->s3, d.D / 32, 0, 32, d.E * d.I);
-    a.sx = bs_scale(ws.xps, d.D / 32, 0, 32, d.P);
+    a.nkq = int(d.D / 128);
+    a.mtiles = int(d.I / 64);
+    a.sfa_atoms = packed;
+    a.sfb_atoms = ws.sfx_gu;
     a.pw = ws.plan.pair_w;
     a.hq = ws.hq;
-    a.hs = ws.hs;
+    a.hs_atoms = ws.sfx_dn;
     a.ldh = d.I;
     a.limit = cfg->swiglu_limit;
     rc = bs_grouped_launch<BS_W_FP4, BS_EPI_SWIGLU>("pf_gate_up_fp4", "pf_gate_up_fp4_narrow",
@@ -1217,8 +1271,10 @@ extern "C" int dsv41_moe_prefill(const dsv41_moe_config *cfg, const dsv41_moe_we
     memset(&a, 0, sizeof(a));
     a.nkb = int(d.I / BS_BK);
     a.a_rows = int(d.D);
-    a.sw = bs_scale(W->s2, d.I / 32, 0, 32, d.E * d.D);
-    a.sx = bs_scale(ws.hs, d.I / 32, 0, 32, d.P);
+    a.nkq = int(d.I / 128);
+    a.mtiles = int(d.D / BS_BM);
+    a.sfa_atoms = packed + pf_packed_gu_bytes(cfg);
+    a.sfb_atoms = ws.sfx_dn;
     a.out = ws.yp;
     a.ldo = d.D;
     rc = bs_grouped_launch<BS_W_FP4, BS_EPI_BF16>("pf_down_fp4", "pf_down_fp4_narrow", maps, a,

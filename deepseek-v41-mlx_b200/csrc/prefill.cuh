@@ -7,6 +7,7 @@
 // tiles, and the combine sums every token's expert outputs in ascending expert order
 // (the order of upstream's loop) before adding the shared expert.
 #pragma once
+#include "bsgemm.cuh"
 #include "common.cuh"
 
 namespace dsv41 {
@@ -17,12 +18,13 @@ constexpr int PF_TILE_ROWS = 224;   // activation rows per GEMM tile (the GEMM's
 struct PfPlan {
   int *chunk_base;     // [nchunks, E]: pairs of expert e in earlier chunks
   int *grp_off;        // [E] first sorted position of expert e
-  int *grp_cnt;        // [E]
+  int *grp_rt0;        // [E] first row tile of expert e (tiles of <= 224 rows, numbered in order)
   int *pair_tok;       // [P] token of sorted pair
   float *pair_w;       // [P] routing weight of sorted pair
   int *slot_pos;       // [T*k] sorted position of pair (t, j)
-  int4 *tiles[4];      // {expert, m-tile, first row, rows}: gate/up wide, gate/up narrow,
-                       // down wide, down narrow
+  int *row_tile;       // [P] (row tile << 8) | row within the tile, of sorted pair
+  int4 *tiles[4];      // {expert, m-tile, first row, rows | row tile << 8}: gate/up wide,
+                       // gate/up narrow, down wide, down narrow
   int *ntiles;         // [4] tile counts of the four lists
   int *next_tile;      // [4] work counters of the four launches (zeroed here)
 };
@@ -111,9 +113,11 @@ __global__ void __launch_bounds__(1024) k_pf_scan(int *__restrict__ chunk_cnt, i
   const int nwide = nnt - nnar;
   int v[3] = {run, nwide, nnar}, excl[3], tot[3];
   block_scan3(v, excl, tot);
+  // row tiles are numbered expert by expert: expert e owns [rt0, rt0 + nnt)
+  const int rt0 = excl[1] + excl[2];
   if (e < E) {
     plan.grp_off[e] = excl[0];
-    plan.grp_cnt[e] = run;
+    plan.grp_rt0[e] = rt0;
     const int mts[2] = {mt_gu, mt_dn};
     for (int pj = 0; pj < 2; ++pj) {
       const int mt_n = mts[pj];
@@ -122,8 +126,10 @@ __global__ void __launch_bounds__(1024) k_pf_scan(int *__restrict__ chunk_cnt, i
       for (int mt = 0; mt < mt_n; ++mt) {
         for (int j = 0; j < nwide; ++j)
           tw[mt * nwide + j] = make_int4(e, mt, excl[0] + j * PF_TILE_ROWS,
-                                         min(PF_TILE_ROWS, run - j * PF_TILE_ROWS));
-        if (nnar) tn[mt] = make_int4(e, mt, excl[0] + nwide * PF_TILE_ROWS, tail);
+                                         min(PF_TILE_ROWS, run - j * PF_TILE_ROWS) |
+                                             ((rt0 + j) << 8));
+        if (nnar)
+          tn[mt] = make_int4(e, mt, excl[0] + nwide * PF_TILE_ROWS, tail | ((rt0 + nwide) << 8));
       }
     }
   }
@@ -158,17 +164,21 @@ __global__ void __launch_bounds__(PF_CHUNK) k_pf_place(const int32_t *__restrict
   if (e >= 0) {
     int before = 0;
     for (int w2 = 0; w2 < warp; ++w2) before += wh[w2 * E + e];
-    const int pos = plan.grp_off[e] + plan.chunk_base[int64_t(blockIdx.x) * E + e] + before + rank;
+    const int in_e = plan.chunk_base[int64_t(blockIdx.x) * E + e] + before + rank;
+    const int pos = plan.grp_off[e] + in_e;
     plan.pair_tok[pos] = int(p / topk);
     plan.pair_w[pos] = w ? w[p] : 1.0f;
     plan.slot_pos[p] = pos;
+    plan.row_tile[pos] = ((plan.grp_rt0[e] + in_e / PF_TILE_ROWS) << 8) | (in_e % PF_TILE_ROWS);
   }
 }
 
-// dst row r = src row tok[r] for the fp8 codes (K bytes) and their ue8m0 scales (K/32).
+// dst row r = src row tok[r] for the fp8 codes (K bytes); the row's ue8m0 scales (K/32) go
+// to its row tile's scale atoms (the tcgen05.cp layout the GEMM bulk-copies per K stage).
 __global__ void k_pf_gather(const uint8_t *__restrict__ xq, const uint8_t *__restrict__ xs,
-                            const int *__restrict__ tok, int64_t R, int64_t K,
-                            uint8_t *__restrict__ dq, uint8_t *__restrict__ ds) {
+                            const int *__restrict__ tok, const int *__restrict__ row_tile,
+                            int64_t R, int64_t K, uint8_t *__restrict__ dq,
+                            uint8_t *__restrict__ datoms) {
   const int64_t r = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (r >= R) return;
@@ -176,9 +186,36 @@ __global__ void k_pf_gather(const uint8_t *__restrict__ xq, const uint8_t *__res
   const uint4 *src = reinterpret_cast<const uint4 *>(xq + t * K);
   uint4 *dst = reinterpret_cast<uint4 *>(dq + r * K);
   for (int64_t i = lane; i < K / 16; i += 32) dst[i] = __ldg(src + i);
+  const int rt = row_tile[r] >> 8, lr = row_tile[r] & 0xFF;
   const uint32_t *ss = reinterpret_cast<const uint32_t *>(xs + t * (K / 32));
-  uint32_t *sd = reinterpret_cast<uint32_t *>(ds + r * (K / 32));
-  for (int64_t i = lane; i < K / 128; i += 32) sd[i] = __ldg(ss + i);
+  uint8_t *base = datoms + int64_t(rt) * (K / 128) * 1024;
+  for (int64_t i = lane; i < K / 128; i += 32)   // 4 scales (one K stage) per word
+    *reinterpret_cast<uint32_t *>(base + sf_atom_off(lr, int(4 * i))) = __ldg(ss + i);
+}
+
+// Weight scales -> tcgen05.cp atoms, once per weight set.  One thread per (atom, lane):
+// a 16-byte row of atom (g, mt, kq) holds the 4 per-32 scales of K stage kq for rows
+// 32c + l, c = 0..3, of the tile.  paired: the tile is 64 rows of s (c = 0, 1) and the
+// same 64 rows of s2 (c = 2, 3) -- the gate/up pairing of the SwiGLU GEMM.
+__global__ void k_pack_sfw(const uint8_t *__restrict__ sc, const uint8_t *__restrict__ sc2,
+                           int64_t groups, int64_t rows, int64_t K, int paired,
+                           uint8_t *__restrict__ out) {
+  const int64_t nkq = K / 128, mt_rows = paired ? 64 : 128, mtiles = rows / mt_rows;
+  const int64_t n = groups * mtiles * nkq * 32;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int l = int(i & 31);
+    const int64_t atom = i >> 5;
+    const int64_t kq = atom % nkq, mt = (atom / nkq) % mtiles, g = atom / (nkq * mtiles);
+    uint32_t w[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint8_t *src = (paired && c >= 2) ? sc2 : sc;
+      const int64_t row = g * rows + mt * mt_rows + 32 * (paired ? (c & 1) : c) + l;
+      w[c] = __ldg(reinterpret_cast<const uint32_t *>(src + row * (K / 32) + 4 * kq));
+    }
+    *reinterpret_cast<uint4 *>(out + atom * 512 + l * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
 }
 
 // out[t, :] = sum over the token's experts in ascending id order of Yp[pos] (bf16), then

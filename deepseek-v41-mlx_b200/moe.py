@@ -295,10 +295,24 @@ class MoE:
         if given:
             idx = L.cuda_tensor(indices, "indices").to(t.int32).reshape(T, -1).contiguous()
             wts = L.cuda_tensor(weights, "weights").float().reshape(T, -1).contiguous()
-        need = L.load().dsv41_moe_prefill_workspace_size(C.byref(cfg), T, 1 if given else 0)
+        packed = self._packed_scales(cfg, W, xf.device)
+        need = L.load().dsv41_moe_prefill_workspace_size(C.byref(cfg), T, 1 if given else 0, 1)
         ws = L.workspace(need, xf.device)
         y = t.empty((T, self.dim), dtype=odt, device=xf.device)
-        L.call("dsv41_moe_prefill", C.byref(cfg), C.byref(W), L.ptr(xf), T,
+        L.call("dsv41_moe_prefill", C.byref(cfg), C.byref(W), L.ptr(packed), L.ptr(xf), T,
                L.ptr(wts) if given else None, L.ptr(idx) if given else None, L.dtype_code(odt),
                L.ptr(y), L.ptr(ws), ws.numel(), L.stream_of(xf))
         return y.reshape(shape)
+
+    def _packed_scales(self, cfg, W, device):
+        """Expert scales in the tensor-core layout, rebuilt when a scale tensor changes."""
+        e = self.experts
+        srcs = [L.cuda_tensor(p.scales) for p in (e.gate_proj, e.up_proj, e.down_proj)]
+        key = tuple((s.data_ptr(), s._version, tuple(s.shape)) for s in srcs)
+        if getattr(self, "_pack_key", None) != key:
+            n = L.load().dsv41_moe_prefill_pack_size(C.byref(cfg))
+            self._pack = L.workspace(n, device)
+            L.call("dsv41_moe_prefill_pack", C.byref(cfg), C.byref(W), L.ptr(self._pack), n,
+                   L.stream_of(self._pack))
+            self._pack_key = key
+        return self._pack

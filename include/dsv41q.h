@@ -232,12 +232,22 @@ int dsv41_fp4_gemm(const uint8_t *a, const uint8_t *a_s, const uint8_t *b, const
  * expert (same a8 form).  Routing is either given (route_weights f32 [T, topk],
  * route_indices int32 [T, topk]) or computed with the router of dsv41_moe_route when
  * route_indices is NULL.  dim and inter must be multiples of 128, topk <= 8.
- * with_routing = 1 when the caller passes routing (smaller workspace). */
-size_t dsv41_moe_prefill_workspace_size(const dsv41_moe_config *cfg, int64_t T, int with_routing);
-int dsv41_moe_prefill(const dsv41_moe_config *cfg, const dsv41_moe_weights *w, const void *x,
-                      int64_t T, const float *route_weights, const int32_t *route_indices,
-                      int out_dtype, void *y, void *workspace, size_t workspace_bytes,
-                      void *stream);
+ *
+ * packed_scales: the expert scales rearranged once by dsv41_moe_prefill_pack into the
+ * layout the tensor cores read (dsv41_moe_prefill_pack_size bytes, 16-byte aligned); valid
+ * while the expert scales are unchanged.  NULL: they are packed into the workspace on
+ * every call.  No reference counterpart (the reference dequantizes per call).
+ * Workspace query: with_routing = 1 when routing is passed, with_packed = 1 when
+ * packed_scales is passed. */
+size_t dsv41_moe_prefill_pack_size(const dsv41_moe_config *cfg);
+int dsv41_moe_prefill_pack(const dsv41_moe_config *cfg, const dsv41_moe_weights *w, void *packed,
+                           size_t packed_bytes, void *stream);
+size_t dsv41_moe_prefill_workspace_size(const dsv41_moe_config *cfg, int64_t T, int with_routing,
+                                        int with_packed);
+int dsv41_moe_prefill(const dsv41_moe_config *cfg, const dsv41_moe_weights *w,
+                      const void *packed_scales, const void *x, int64_t T,
+                      const float *route_weights, const int32_t *route_indices, int out_dtype,
+                      void *y, void *workspace, size_t workspace_bytes, void *stream);
 
 /* ---- a15: engram hasher (deepseek_v41_mlx/engram.py:154-180; upstream
  * docs/reference/engram.py NgramHashState.forward).  input_ids int64 [B, L];
