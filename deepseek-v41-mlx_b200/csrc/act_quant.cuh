@@ -66,4 +66,66 @@ __global__ void k_act_quant(const __nv_bfloat16 *__restrict__ x, int64_t M, int6
   }
 }
 
+// Vectorized form of k_act_quant (same arithmetic): 8 elements per thread from one 16-byte
+// load; a block of 8*G elements is G adjacent lanes combining their amax by shuffles.
+// When s_atoms is set (G == 4, ue8m0 bytes) the scales are also written as tcgen05.cp atoms
+// of 224-row tiles (row m -> tile m / 224), the layout the block-scaled GEMM bulk-copies.
+template <int G>
+__global__ void k_act_quant_v8(const __nv_bfloat16 *__restrict__ x, int64_t M, int64_t K,
+                               int round_scale, uint8_t *__restrict__ q, void *__restrict__ s,
+                               int s_u8, __nv_bfloat16 *__restrict__ deq,
+                               uint8_t *__restrict__ s_atoms, int tile_rows) {
+  const int64_t nthr = M * (K / 8);
+  const int64_t tid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if ((tid & ~int64_t(31)) >= nthr) return;   // whole warps only: the shuffles below
+  const bool valid = tid < nthr;
+  float v[8];
+  float amax = 0.0f;
+  if (valid) {
+    const uint4 raw = *reinterpret_cast<const uint4 *>(x + tid * 8);
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[2 * i] = bf_bits2f(uint16_t(w[i] & 0xFFFF));
+      v[2 * i + 1] = bf_bits2f(uint16_t(w[i] >> 16));
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  }
+#pragma unroll
+  for (int o = 1; o < G; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if (!valid) return;
+  amax = fmaxf(amax, 1e-4f);
+  const float sc = round_scale ? pow2_ceil_log2(__fmul_rn(amax, 1.0f / 448.0f))
+                               : __fdiv_rn(amax, 448.0f);
+  uint32_t c[2] = {0u, 0u};
+  uint32_t dq[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float r = __fdiv_rn(v[i], sc);
+    const float y = isnan(r) ? r : fminf(fmaxf(r, -448.0f), 448.0f);   // torch clamp keeps NaN
+    const uint8_t code = f32_to_e4m3_sat(y);
+    c[i >> 2] |= uint32_t(code) << (8 * (i & 3));
+    if (deq) {
+      const float back = h2f2(e4m3x2_to_f16x2(code)).x;
+      dq[i >> 1] |= uint32_t(f2bf_bits(__fmul_rn(back, sc))) << (16 * (i & 1));
+    }
+  }
+  *reinterpret_cast<uint2 *>(q + tid * 8) = make_uint2(c[0], c[1]);
+  if (deq) *reinterpret_cast<uint4 *>(deq + tid * 8) = make_uint4(dq[0], dq[1], dq[2], dq[3]);
+  if ((tid % G) == 0) {
+    const int64_t e0 = tid * 8, m = e0 / K, blk = (e0 % K) / (8 * G), nblk = K / (8 * G);
+    if (s_u8) {
+      const uint8_t e8 = uint8_t((__float_as_uint(sc) >> 23) & 0xFF);
+      reinterpret_cast<uint8_t *>(s)[m * nblk + blk] = e8;
+      if (s_atoms)
+        s_atoms[(m / tile_rows) * (K / 128) * 1024 +
+                (int64_t(blk) >> 2) * 1024 + ((m % tile_rows) >> 7) * 512 +
+                ((m % tile_rows) & 31) * 16 + (((m % tile_rows) >> 5) & 3) * 4 + (blk & 3)] = e8;
+    } else {
+      reinterpret_cast<float *>(s)[m * nblk + blk] = sc;
+    }
+  }
+}
+
 }  // namespace dsv41

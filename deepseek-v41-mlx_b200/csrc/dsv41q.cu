@@ -203,9 +203,21 @@ extern "C" int dsv41_act_quant_fp8(const void *x, int64_t M, int64_t K, int bloc
   const __nv_bfloat16 *xb = reinterpret_cast<const __nv_bfloat16 *>(x);
   __nv_bfloat16 *dq = reinterpret_cast<__nv_bfloat16 *>(deq_out);
   const int su8 = s_dtype == DSV41_U8;
-  if (block == 32) k_act_quant<1><<<blocks, 256, 0, st>>>(xb, M, K, round_scale, q, s, su8, dq);
-  else if (block == 64) k_act_quant<2><<<blocks, 256, 0, st>>>(xb, M, K, round_scale, q, s, su8, dq);
-  else k_act_quant<4><<<blocks, 256, 0, st>>>(xb, M, K, round_scale, q, s, su8, dq);
+  if (aligned(x, 16) && aligned(q, 8) && (!dq || aligned(dq, 16))) {
+    const unsigned vb = unsigned(ceil_div(M * (K / 8), 256));
+    if (block == 32)
+      k_act_quant_v8<4><<<vb, 256, 0, st>>>(xb, M, K, round_scale, q, s, su8, dq, nullptr, 1);
+    else if (block == 64)
+      k_act_quant_v8<8><<<vb, 256, 0, st>>>(xb, M, K, round_scale, q, s, su8, dq, nullptr, 1);
+    else
+      k_act_quant_v8<16><<<vb, 256, 0, st>>>(xb, M, K, round_scale, q, s, su8, dq, nullptr, 1);
+  } else if (block == 32) {
+    k_act_quant<1><<<blocks, 256, 0, st>>>(xb, M, K, round_scale, q, s, su8, dq);
+  } else if (block == 64) {
+    k_act_quant<2><<<blocks, 256, 0, st>>>(xb, M, K, round_scale, q, s, su8, dq);
+  } else {
+    k_act_quant<4><<<blocks, 256, 0, st>>>(xb, M, K, round_scale, q, s, su8, dq);
+  }
   DSV41_CHECK_LAUNCH("act_quant_fp8");
   return DSV41_OK;
 }
@@ -1030,8 +1042,16 @@ struct PfDims {
 size_t pf_packed_gu_bytes(const dsv41_moe_config *c) {
   return size_t(c->n_experts) * (c->inter / 64) * (c->dim / 128) * 512;
 }
+size_t pf_packed_dn_bytes(const dsv41_moe_config *c) {
+  return size_t(c->n_experts) * (c->dim / 128) * (c->inter / 128) * 512;
+}
+// shared expert (one group), packed after the routed experts when its weights are given
+size_t pf_packed_sh_off(const dsv41_moe_config *c) {
+  return pf_packed_gu_bytes(c) + pf_packed_dn_bytes(c);
+}
 size_t pf_packed_bytes(const dsv41_moe_config *c) {
-  return pf_packed_gu_bytes(c) + size_t(c->n_experts) * (c->dim / 128) * (c->inter / 128) * 512;
+  return pf_packed_sh_off(c) + size_t(c->inter / 64) * (c->dim / 128) * 512 +
+         size_t(c->dim / 128) * (c->inter / 128) * 512;
 }
 
 PfDims pf_dims(const dsv41_moe_config *cfg, int64_t T) {
@@ -1053,8 +1073,9 @@ struct PfWs {
   float *w;
   int32_t *idx;
   float *rpart;
-  uint8_t *xq, *xs, *xpq, *hq, *shq, *shs;
+  uint8_t *xq, *xs, *xpq, *hq, *shq;
   uint8_t *sfx_gu, *sfx_dn;   // activation scale atoms of the row tiles (gate/up, down inputs)
+  uint8_t *sfx_sh, *sfh_sh;   // the same for the shared expert's dense row tiles
   uint8_t *packed;            // weight scale atoms when the caller passes none
   __nv_bfloat16 *yp, *ysh;
   int *chunk_cnt;
@@ -1080,8 +1101,10 @@ size_t pf_carve(const dsv41_moe_config *cfg, const PfDims &d, bool route, bool s
   w.yp = c.take<__nv_bfloat16>(d.P * d.D);
   if (pack) w.packed = c.take<uint8_t>(pf_packed_bytes(cfg));
   if (shared) {
+    const int64_t rts = ceil_div(d.T, BS_BN);
     w.shq = c.take<uint8_t>(d.T * d.I);
-    w.shs = c.take<uint8_t>(d.T * d.I / 32);
+    w.sfx_sh = c.take<uint8_t>(rts * (d.D / 128) * 1024);
+    w.sfh_sh = c.take<uint8_t>(rts * (d.I / 128) * 1024);
     w.ysh = c.take<__nv_bfloat16>(d.T * d.D);
   }
   w.chunk_cnt = c.take<int>(d.nchunks * d.E);
@@ -1132,11 +1155,19 @@ int pf_pack(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, uint8_t *ou
             cudaStream_t st) {
   const int64_t E = cfg->n_experts, D = cfg->dim, I = cfg->inter;
   ProfScope prof("pf_pack_scales", st);
-  k_pack_sfw<<<unsigned(4 * num_sms()), 256, 0, st>>>(W->s1, W->s3, E, I, D, 1, out);
+  k_pack_sfw<<<unsigned(4 * num_sms()), 256, 0, st>>>(W->s1, W->s3, E, I, D, 1, 0, out);
   DSV41_CHECK_LAUNCH("pack gate/up scales");
-  k_pack_sfw<<<unsigned(4 * num_sms()), 256, 0, st>>>(W->s2, nullptr, E, D, I, 0,
+  k_pack_sfw<<<unsigned(4 * num_sms()), 256, 0, st>>>(W->s2, nullptr, E, D, I, 0, 0,
                                                       out + pf_packed_gu_bytes(cfg));
   DSV41_CHECK_LAUNCH("pack down scales");
+  if (W->ss1 && W->ss3 && W->ss2) {   // fp8 shared expert: one ue8m0 per 32x32 block
+    uint8_t *sh = out + pf_packed_sh_off(cfg);
+    k_pack_sfw<<<unsigned(num_sms()), 256, 0, st>>>(W->ss1, W->ss3, 1, I, D, 1, 5, sh);
+    DSV41_CHECK_LAUNCH("pack shared gate/up scales");
+    k_pack_sfw<<<unsigned(num_sms()), 256, 0, st>>>(W->ss2, nullptr, 1, D, I, 0, 5,
+                                                    sh + size_t(I / 64) * (D / 128) * 512);
+    DSV41_CHECK_LAUNCH("pack shared down scales");
+  }
   return DSV41_OK;
 }
 }  // namespace
@@ -1203,12 +1234,12 @@ extern "C" int dsv41_moe_prefill(const dsv41_moe_config *cfg, const dsv41_moe_we
     if (rc) return rc;
     packed = ws.packed;
   }
-  // act_quant(x, 32, ue8m0) once per token
+  // act_quant(x, 32, ue8m0) once per token (+ scale atoms of the shared expert's row tiles)
   {
-    const int64_t warps = d.T * (d.D / 32);
     ProfScope prof("pf_act_quant", st);
-    k_act_quant<1><<<unsigned((warps * 32 + 255) / 256), 256, 0, st>>>(
-        reinterpret_cast<const __nv_bfloat16 *>(x), d.T, d.D, 1, ws.xq, ws.xs, 1, nullptr);
+    k_act_quant_v8<4><<<unsigned(ceil_div(d.T * (d.D / 8), 256)), 256, 0, st>>>(
+        reinterpret_cast<const __nv_bfloat16 *>(x), d.T, d.D, 1, ws.xq, ws.xs, 1, nullptr,
+        shared ? ws.sfx_sh : nullptr, BS_BN);
     DSV41_CHECK_LAUNCH("pf_act_quant");
   }
   // stable sort of the (token, slot) pairs by expert + tile lists
@@ -1289,11 +1320,12 @@ extern "C" int dsv41_moe_prefill(const dsv41_moe_config *cfg, const dsv41_moe_we
     if (!rc) rc = bs_xmaps(maps.x, ws.xq, d.T, d.D);
     if (rc) return rc;
     BsArgs a = bs_args(d.D, d.I);
-    a.sw = bs_scale(W->ss1, d.D / 32, 5, 32, d.I);
-    a.sw2 = bs_scale(W->ss3, d.D / 32, 5, 32, d.I);
-    a.sx = bs_scale(ws.xs, d.D / 32, 0, 32, d.T);
+    a.nkq = int(d.D / 128);
+    a.mtiles = int(d.I / 64);
+    a.sfa_atoms = packed + pf_packed_sh_off(cfg);
+    a.sfb_atoms = ws.sfx_sh;
     a.hq = ws.shq;
-    a.hs = ws.shs;
+    a.hs_atoms = ws.sfh_sh;
     a.ldh = d.I;
     a.limit = cfg->swiglu_limit;
     rc = bs_dense_launch<BS_W_FP8, BS_EPI_SWIGLU>("pf_shared_gate_up_fp8", maps, a, d.I, d.T, st);
@@ -1304,8 +1336,10 @@ extern "C" int dsv41_moe_prefill(const dsv41_moe_config *cfg, const dsv41_moe_we
     if (!rc) rc = bs_xmaps(m2.x, ws.shq, d.T, d.I);
     if (rc) return rc;
     BsArgs b = bs_args(d.I, d.D);
-    b.sw = bs_scale(W->ss2, d.I / 32, 5, 32, d.D);
-    b.sx = bs_scale(ws.shs, d.I / 32, 0, 32, d.T);
+    b.nkq = int(d.I / 128);
+    b.mtiles = int(d.D / BS_BM);
+    b.sfa_atoms = packed + pf_packed_sh_off(cfg) + size_t(d.I / 64) * (d.D / 128) * 512;
+    b.sfb_atoms = ws.sfh_sh;
     b.out = ws.ysh;
     b.ldo = d.D;
     rc = bs_dense_launch<BS_W_FP8, BS_EPI_BF16>("pf_shared_down_fp8", m2, b, d.D, d.T, st);

@@ -193,12 +193,13 @@ __global__ void k_pf_gather(const uint8_t *__restrict__ xq, const uint8_t *__res
     *reinterpret_cast<uint32_t *>(base + sf_atom_off(lr, int(4 * i))) = __ldg(ss + i);
 }
 
-// Weight scales -> tcgen05.cp atoms, once per weight set.  One thread per (atom, lane):
+// Weight scales -> tcgen05.cp atoms, once per weight set.  Scale row of weight row r is
+// r >> rshift (0: per-row fp4 scales; 5: fp8 32x32 blocks).  One thread per (atom, lane):
 // a 16-byte row of atom (g, mt, kq) holds the 4 per-32 scales of K stage kq for rows
 // 32c + l, c = 0..3, of the tile.  paired: the tile is 64 rows of s (c = 0, 1) and the
 // same 64 rows of s2 (c = 2, 3) -- the gate/up pairing of the SwiGLU GEMM.
 __global__ void k_pack_sfw(const uint8_t *__restrict__ sc, const uint8_t *__restrict__ sc2,
-                           int64_t groups, int64_t rows, int64_t K, int paired,
+                           int64_t groups, int64_t rows, int64_t K, int paired, int rshift,
                            uint8_t *__restrict__ out) {
   const int64_t nkq = K / 128, mt_rows = paired ? 64 : 128, mtiles = rows / mt_rows;
   const int64_t n = groups * mtiles * nkq * 32;
@@ -212,7 +213,7 @@ __global__ void k_pack_sfw(const uint8_t *__restrict__ sc, const uint8_t *__rest
     for (int c = 0; c < 4; ++c) {
       const uint8_t *src = (paired && c >= 2) ? sc2 : sc;
       const int64_t row = g * rows + mt * mt_rows + 32 * (paired ? (c & 1) : c) + l;
-      w[c] = __ldg(reinterpret_cast<const uint32_t *>(src + row * (K / 32) + 4 * kq));
+      w[c] = __ldg(reinterpret_cast<const uint32_t *>(src + (row >> rshift) * (K / 32) + 4 * kq));
     }
     *reinterpret_cast<uint4 *>(out + atom * 512 + l * 16) = make_uint4(w[0], w[1], w[2], w[3]);
   }
