@@ -77,6 +77,7 @@ PROTOTYPES = {
                                _SZ, _P]),
     "dsv41_moe_decode": (_I, [C.POINTER(MoeConfig), C.POINTER(MoeWeights), _P, _I64, _I, _P, _P,
                               _P, _P, _SZ, _P]),
+    "dsv41_qmm_affine": (_I, [_P, _I64, _I64, _P, _P, _P, _I, _I64, _I, _P, _P]),
     "dsv41_fp8_gemm": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I, _P, _I, _P]),
     "dsv41_fp4_gemm": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I, _P, _I, _P]),
     "dsv41_moe_prefill_pack_size": (_SZ, [C.POINTER(MoeConfig)]),

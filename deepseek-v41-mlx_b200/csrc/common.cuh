@@ -234,11 +234,12 @@ static inline int get_encoder() {
   return DSV41_OK;
 }
 
-// 2D byte/u16 tensor map with 128-byte swizzle.  inner = elements per row,
+// 2D tensor map, 128-byte swizzle unless told otherwise.  inner = elements per row,
 // outer = rows, row_bytes = stride, box = {box_inner, box_outer}.
 static inline int make_tmap_2d(CUtensorMap *m, const void *base, CUtensorMapDataType dt,
                                uint64_t inner, uint64_t outer, uint64_t row_bytes,
-                               uint32_t box_inner, uint32_t box_outer) {
+                               uint32_t box_inner, uint32_t box_outer,
+                               CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
   int st = get_encoder();
   if (st) return st;
   if (!aligned(base, 16) || (row_bytes % 16) != 0)
@@ -249,7 +250,7 @@ static inline int make_tmap_2d(CUtensorMap *m, const void *base, CUtensorMapData
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = g_encode_tiled(m, dt, 2, const_cast<void *>(base), dims, strides, box, estr,
-                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(DSV41_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);

@@ -9,6 +9,7 @@
 #include "moe.cuh"
 #include "bsgemm.cuh"
 #include "prefill.cuh"
+#include "aqgemm.cuh"
 
 #include <mutex>
 
@@ -1027,6 +1028,62 @@ extern "C" int dsv41_fp4_gemm(const uint8_t *a, const uint8_t *a_s, const uint8_
                 "act_block_size must be 32 or 128");
   return bs_dense(BS_W_FP4, a, a_s, act_block_size, b, b_s, 0, 32, M, N, K, c, c_dtype,
                   STREAM(stream));
+}
+
+// ======================================================================= affine prefill GEMM
+
+extern "C" int dsv41_qmm_affine(const void *x, int64_t M, int64_t K, const uint32_t *wq,
+                                const void *scales, const void *biases, int bits, int64_t N,
+                                int out_dtype, void *y, void *stream) {
+  DSV41_REQUIRE(bits == 4 || bits == 8, DSV41_ERR_UNSUPPORTED, "bits must be 4 or 8");
+  DSV41_REQUIRE(M >= 0 && K > 0 && N > 0 && K % AQ_BK == 0 && N % AQ_BM == 0,
+                DSV41_ERR_BAD_SHAPE, "K must be a multiple of 64 and N of 128");
+  DSV41_REQUIRE(M < (int64_t(1) << 31) && N < (int64_t(1) << 31), DSV41_ERR_BAD_SHAPE,
+                "shape too large");
+  DSV41_REQUIRE(out_dtype == DSV41_F32 || out_dtype == DSV41_BF16, DSV41_ERR_BAD_DTYPE,
+                "out_dtype must be F32 or BF16");
+  if (M == 0) return DSV41_OK;
+  DSV41_REQUIRE(x && wq && scales && biases && y, DSV41_ERR_BAD_ARG, "NULL pointer");
+  DSV41_REQUIRE(aligned(x, 16) && aligned(wq, 16) && aligned(y, 16) && aligned(scales, 2) &&
+                    aligned(biases, 2),
+                DSV41_ERR_MISALIGNED, "x, wq and y must be 16-byte aligned");
+  AqMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  const uint64_t row_bytes = uint64_t(K) * bits / 8;
+  int rc = make_tmap_2d(&maps.w, wq, CU_TENSOR_MAP_DATA_TYPE_UINT8, row_bytes, uint64_t(N),
+                        row_bytes, AQ_BK * bits / 8, AQ_BM, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!rc)
+    rc = make_tmap_2d(&maps.x, x, CU_TENSOR_MAP_DATA_TYPE_UINT16, uint64_t(K), uint64_t(M),
+                      uint64_t(K) * 2, AQ_BK, AQ_BN);
+  if (rc) return rc;
+  AqArgs a;
+  memset(&a, 0, sizeof(a));
+  a.nkb = int(K / AQ_BK);
+  a.M = M;
+  a.N = N;
+  a.scale = reinterpret_cast<const uint16_t *>(scales);
+  a.bias = reinterpret_cast<const uint16_t *>(biases);
+  a.nt = int(ceil_div(M, AQ_BN));
+  a.tiles = int(N / AQ_BM) * a.nt;
+  a.out = y;
+  a.ldo = N;
+  cudaStream_t st = STREAM(stream);
+  const int grid = a.tiles < num_sms() ? a.tiles : num_sms();
+  static bool attr_set[64][4] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int v = (bits == 8 ? 2 : 0) + (out_dtype == DSV41_F32 ? 1 : 0);
+  auto kern = bits == 4 ? (out_dtype == DSV41_F32 ? k_aqgemm<4, BS_EPI_F32> : k_aqgemm<4, BS_EPI_BF16>)
+                        : (out_dtype == DSV41_F32 ? k_aqgemm<8, BS_EPI_F32> : k_aqgemm<8, BS_EPI_BF16>);
+  if (dev >= 0 && dev < 64 && !attr_set[dev][v]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, AQ_SMEM);
+    if (e != cudaSuccess) return cuda_status(e, "aqgemm smem attribute");
+    attr_set[dev][v] = true;
+  }
+  ProfScope prof("qmm_affine", st);
+  kern<<<grid, AQ_THREADS, AQ_SMEM, st>>>(maps, a);
+  DSV41_CHECK_LAUNCH("qmm_affine");
+  return DSV41_OK;
 }
 
 // ======================================================================= MoE prefill

@@ -67,6 +67,10 @@ def linear_fp4(x, weight, scale, out_dtype=None):
     return y.reshape(tuple(xt.shape[:-1]) + (N,))
 
 
+# Above this many activation rows the affine product runs on the tensor cores.
+QMM_MIN_ROWS = 64
+
+
 def linear_affine(x, wq, scales, biases, bits=4, group_size=64, out_dtype=None):
     t = L.torch()
     if group_size != 64:
@@ -82,9 +86,14 @@ def linear_affine(x, wq, scales, biases, bits=4, group_size=64, out_dtype=None):
         raise ValueError("affine weight must be [N, K*bits/32] u32 with scales [N, K/64]")
     M = xf.shape[0]
     y = t.empty((M, N), dtype=odt, device=xf.device)
-    ws = _ws(L.load().dsv41_gemv_workspace_size(M, N, K), xf.device)
-    L.call("dsv41_gemv_affine", L.ptr(xf), M, K, L.ptr(w), L.ptr(s), L.ptr(b), bits, N,
-           L.dtype_code(odt), L.ptr(y), L.ptr(ws), ws.numel(), L.stream_of(xf))
+    if M > QMM_MIN_ROWS and N % 128 == 0 and bits in (4, 8):
+        # prefill sizes: tensor-core GEMM on weights dequantized to bf16 (MLX's qmm form)
+        L.call("dsv41_qmm_affine", L.ptr(xf), M, K, L.ptr(w), L.ptr(s), L.ptr(b), bits, N,
+               L.dtype_code(odt), L.ptr(y), L.stream_of(xf))
+    else:
+        ws = _ws(L.load().dsv41_gemv_workspace_size(M, N, K), xf.device)
+        L.call("dsv41_gemv_affine", L.ptr(xf), M, K, L.ptr(w), L.ptr(s), L.ptr(b), bits, N,
+               L.dtype_code(odt), L.ptr(y), L.ptr(ws), ws.numel(), L.stream_of(xf))
     return y.reshape(tuple(xt.shape[:-1]) + (N,))
 
 

@@ -208,6 +208,17 @@ int dsv41_moe_decode(const dsv41_moe_config *cfg, const dsv41_moe_weights *w, co
                      int32_t *indices_out, void *workspace, size_t workspace_bytes,
                      void *stream);
 
+/* ---- a14 at prefill sizes: MLX affine quantized matmul (mx.quantized_matmul behind
+ * nn.QuantizedLinear, deepseek_v41_mlx/load.py:124-131) on tcgen05 kind::f16.
+ * y[M, N] = x[M, K] . W^T, W = bf16(fma_f32(scale, q, bias)) per group of 64 -- the weights
+ * dequantized to the activation dtype as MLX's quantized matmul does for bf16 inputs.
+ * x bf16 [M, K]; wq u32 [N, K*bits/32] (little-endian row bit stream); scales, biases bf16
+ * [N, K/64]; bits 4 or 8; K % 64 == 0, N % 128 == 0; out F32 or BF16.  For decode sizes use
+ * dsv41_gemv_affine (exact affine arithmetic, no weight rounding). */
+int dsv41_qmm_affine(const void *x, int64_t M, int64_t K, const uint32_t *wq, const void *scales,
+                     const void *biases, int bits, int64_t N, int out_dtype, void *y,
+                     void *stream);
+
 /* ---- a13: upstream fp8_gemm / fp4_gemm (docs/reference/kernel.py:277-308 and
  * :562-591) on tcgen05 block-scaled MMA (kind::mxf8f6f4, fp32
  * accumulation in TMEM).  C[M, N] = A[M, K] . B[N, K]^T with

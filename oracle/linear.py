@@ -18,7 +18,8 @@ from __future__ import annotations
 import numpy as np
 
 from . import act_quant as AQ
-from .formats import E4M3, affine_qmm_reference, dequant_fp4, dequant_fp8
+from .formats import (E4M3, affine_qmm_reference, bf16_bits_to_f32, dequant_affine,
+                      dequant_fp4, dequant_fp8)
 
 
 def _mm(x: np.ndarray, w: np.ndarray, acc=np.float64) -> np.ndarray:
@@ -38,6 +39,14 @@ def linear_fp4(x, w_packed, s_u8, acc=np.float64):
 def linear_affine(x, wq, scales, biases, bits, group=64, sb_dtype="bf16"):
     """mx.quantized_matmul form (see formats.affine_qmm_reference)."""
     return affine_qmm_reference(x, wq, scales, biases, bits, group, sb_dtype).astype(np.float32)
+
+
+def linear_affine_bf16w(x, wq, scales, biases, bits, group=64):
+    """The quantized matmul with the weights dequantized to bf16 first (mx.dequantize,
+    then a bf16 matmul -- the form MLX's quantized matmul evaluates for bf16 inputs),
+    float64 accumulation, float32 out."""
+    w = bf16_bits_to_f32(dequant_affine(wq, scales, biases, bits, group, np.asarray(x).shape[-1]))
+    return _mm(x, w)
 
 
 def act_dequant(x, block=32):
