@@ -1,22 +1,24 @@
 // aqgemm.cuh -- MLX affine quantized matmul at prefill sizes on the 5th-generation tensor
 // cores (tcgen05.mma kind::f16, bf16 x bf16 -> fp32 in TMEM).
 //
-// y[m, n] = sum_k x[m, k] * w[n, k], w[n, k] = bf16(fma_f32(scale[n, k/64], q[n, k],
-// bias[n, k/64])) with q the 4- or 8-bit code of the little-endian row bit stream
+// y[m, n] = sum_k x[m, k] * w[n, k], w[n, k] = bf16(scale[n, k/64] * q[n, k] + bias[n, k/64])
+// (8-bit codes: fp32 fma then bf16; 4-bit codes: one fused bf16x2 fma, i.e. a single
+// rounding) with q the 4- or 8-bit code of the little-endian row bit stream
 // (mx.quantized_matmul behind nn.QuantizedLinear, deepseek_v41_mlx/load.py:124-131; the
 // layout written by deepseek_v41_mlx/convert.py:156-175).  The weights are dequantized to
 // bf16 once per tile in shared memory -- the form MLX's own quantized matmul computes for
 // bf16 activations -- and multiplied by the bf16 activations as they are, no conversion.
 //
-// One persistent CTA per SM, 320 threads:
+// One persistent CTA per SM, 448 threads:
 //   warp 0     TMA producer: packed codes (128 rows x 64 k, no swizzle) and activations
 //              (256 rows x 64 k bf16, 128-byte swizzle) into a 3-stage ring;
 //   warp 1     TMEM allocator + MMA issuer: 4 MMAs of K=16 per stage, M=128, N=256;
 //   warps 2-5  epilogue: tcgen05.ld, transpose through shared memory, 16-byte stores;
-//   warps 6-9  decoders: thread t owns weight row t of the tile; per stage it expands the
-//              row's 64 codes with the group's scale and bias into one 128-byte row of the
-//              swizzled bf16 A tile (the layout TMA's 128-byte swizzle would give), then
-//              fences the async proxy; the MMA waits for all four warps.
+//   warps 6-13 decoders: two threads per weight row of the tile, each expanding 32 of the
+//              row's 64 codes with the group's scale and bias into half of one 128-byte row
+//              of the swizzled bf16 A tile (the layout TMA's 128-byte swizzle would give),
+//              then fencing the async proxy; the MMA waits for all eight warps (two decoder
+//              warps per SM sub-partition, so one hides the other's latency).
 // Accumulators are double-buffered (2 x 256 TMEM columns).  Every wait is bounded.
 #pragma once
 #include "bsgemm.cuh"
@@ -24,7 +26,8 @@
 namespace dsv41 {
 
 constexpr int AQ_BM = 128, AQ_BN = 256, AQ_BK = 64, AQ_STAGES = 3;
-constexpr int AQ_THREADS = 320;
+constexpr int AQ_THREADS = 448;
+constexpr int AQ_DEC_WARPS = 8;
 constexpr int AQ_A_BYTES = AQ_BM * AQ_BK * 2;          // bf16 weights, 16 KB
 constexpr int AQ_B_BYTES = AQ_BN * AQ_BK * 2;          // bf16 activations, 32 KB
 constexpr int AQ_RAW_BYTES = AQ_BM * AQ_BK;            // codes (8-bit; 4-bit uses half)
@@ -77,7 +80,7 @@ __global__ void __launch_bounds__(AQ_THREADS, 1)
   const uint32_t sbase = smem_u32(smem);
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + AQ_OFF_BAR);
   uint64_t *full = bars;                 // [S] count 1 (+ tx): codes and activations landed
-  uint64_t *afull = bars + S;            // [S] count 4: decoded A tile written
+  uint64_t *afull = bars + S;            // [S] count 8: decoded A tile written
   uint64_t *empty = bars + 2 * S;        // [S] count 1 (tcgen05.commit)
   uint64_t *acc_full = bars + 3 * S;     // [2] count 1
   uint64_t *acc_empty = acc_full + 2;    // [2] count 4
@@ -88,7 +91,7 @@ __global__ void __launch_bounds__(AQ_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&afull[s], 4);
+      mbar_init(&afull[s], AQ_DEC_WARPS);
       mbar_init(&empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -218,29 +221,32 @@ __global__ void __launch_bounds__(AQ_THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ decoders
-    const int row = (warp - 6) * 32 + lane;            // tile row owned by this thread
+    const int dt = (warp - 6) * 32 + lane;             // 0 .. 255
+    const int row = dt >> 1, half = dt & 1;             // tile row, k half (32 codes)
+    constexpr uint32_t HALF_BYTES = RAW_ROW / 2;        // 16 (4-bit) or 32 (8-bit)
     int it = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < args.tiles && ok; t += gridDim.x) {
       const int mt = t / args.nt;
-      const int64_t grow = int64_t(mt) * AQ_BM + row;   // weight row (N < 2^31, N % 128 == 0)
+      const int64_t grow = int64_t(mt) * AQ_BM + row;   // weight row (N % 128 == 0)
       const uint16_t *sp = args.scale + grow * nkb;
       const uint16_t *bp = args.bias + grow * nkb;
-      float sc = bf_bits2f(__ldg(sp)), bi = bf_bits2f(__ldg(bp));
+      uint16_t sc_b = __ldg(sp), bi_b = __ldg(bp);
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const int s = it % S;
         // next group's scale and bias while this one decodes
-        const float sc_n = kb + 1 < nkb ? bf_bits2f(__ldg(sp + kb + 1)) : 0.0f;
-        const float bi_n = kb + 1 < nkb ? bf_bits2f(__ldg(bp + kb + 1)) : 0.0f;
+        const uint16_t sc_nb = kb + 1 < nkb ? __ldg(sp + kb + 1) : uint16_t(0);
+        const uint16_t bi_nb = kb + 1 < nkb ? __ldg(bp + kb + 1) : uint16_t(0);
+        const float sc = bf_bits2f(sc_b), bi = bf_bits2f(bi_b);
         if (!warp_wait(&full[s], uint32_t(it / S) & 1u)) {
           ok = false;
           break;
         }
-        const uint4 *src = reinterpret_cast<const uint4 *>(smem + AQ_OFF_RAW + s * AQ_RAW_BYTES +
-                                                           row * RAW_ROW);
-        uint32_t code[RAW_ROW / 4];
+        const uint4 *src = reinterpret_cast<const uint4 *>(
+            smem + AQ_OFF_RAW + s * AQ_RAW_BYTES + row * RAW_ROW + half * HALF_BYTES);
+        uint32_t code[HALF_BYTES / 4];
 #pragma unroll
-        for (int i = 0; i < int(RAW_ROW / 16); ++i) {
+        for (int i = 0; i < int(HALF_BYTES / 16); ++i) {
           const uint4 v = src[i];
           code[4 * i] = v.x;
           code[4 * i + 1] = v.y;
@@ -248,34 +254,47 @@ __global__ void __launch_bounds__(AQ_THREADS, 1)
           code[4 * i + 3] = v.w;
         }
         uint8_t *arow = smem + AQ_OFF_A + s * AQ_A_BYTES + (row >> 3) * 1024 + (row & 7) * 128;
+        // bf16x2 forms of the scale and bias, and 128 (the code magic's offset)
+        const uint32_t s2u = uint32_t(sc_b) | (uint32_t(sc_b) << 16);
+        const uint32_t b2u = uint32_t(bi_b) | (uint32_t(bi_b) << 16);
+        const __nv_bfloat162 s2 = *reinterpret_cast<const __nv_bfloat162 *>(&s2u);
+        const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162 *>(&b2u);
+        const uint32_t m2u = 0x43004300u;
+        const __nv_bfloat162 m2 = *reinterpret_cast<const __nv_bfloat162 *>(&m2u);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {       // 16-byte chunk c = k 8c .. 8c+7
+        for (int cl = 0; cl < 4; ++cl) {    // local chunk: k 8cl .. 8cl+7 of this half
           uint32_t wv[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const int k0 = 8 * c + 2 * e;
-            uint32_t q0, q1;
+            const int k0 = 8 * cl + 2 * e;
             if (BITS == 4) {
-              q0 = (code[k0 >> 3] >> (4 * (k0 & 7))) & 0xFu;
-              q1 = (code[(k0 + 1) >> 3] >> (4 * ((k0 + 1) & 7))) & 0xFu;
+              // codes k0, k0+1 are the two nibbles of one byte: bf16 pair (128 + q) exactly,
+              // minus 128, then one fused fma.rn.bf16x2 -- round(s*q + b) to bf16 once
+              const uint32_t t = code[k0 >> 3] >> (4 * (k0 & 7));
+              const uint32_t pu = (t & 0xFu) | ((t << 12) & 0xF0000u) | 0x43004300u;
+              const __nv_bfloat162 q2 = __hsub2(*reinterpret_cast<const __nv_bfloat162 *>(&pu), m2);
+              const __nv_bfloat162 h2 = __hfma2(s2, q2, b2);
+              wv[e] = *reinterpret_cast<const uint32_t *>(&h2);
             } else {
-              q0 = (code[k0 >> 2] >> (8 * (k0 & 3))) & 0xFFu;
-              q1 = (code[(k0 + 1) >> 2] >> (8 * ((k0 + 1) & 3))) & 0xFFu;
+              const uint32_t q0 = (code[k0 >> 2] >> (8 * (k0 & 3))) & 0xFFu;
+              const uint32_t q1 = (code[k0 >> 2] >> (8 * ((k0 + 1) & 3))) & 0xFFu;
+              // exact integer -> float (2^23 + q - 2^23), the affine fma in fp32, then bf16
+              const float f0 = __uint_as_float(0x4B000000u | q0) - 8388608.0f;
+              const float f1 = __uint_as_float(0x4B000000u | q1) - 8388608.0f;
+              const __nv_bfloat162 h2 = __floats2bfloat162_rn(__fmaf_rn(sc, f0, bi),
+                                                              __fmaf_rn(sc, f1, bi));
+              wv[e] = *reinterpret_cast<const uint32_t *>(&h2);
             }
-            // exact integer -> float (2^23 + q - 2^23), then the affine fma in fp32
-            const float f0 = __uint_as_float(0x4B000000u | q0) - 8388608.0f;
-            const float f1 = __uint_as_float(0x4B000000u | q1) - 8388608.0f;
-            wv[e] = uint32_t(f2bf_bits(__fmaf_rn(sc, f0, bi))) |
-                    (uint32_t(f2bf_bits(__fmaf_rn(sc, f1, bi))) << 16);
           }
+          const int c = 4 * half + cl;      // chunk of the 128-byte row
           *reinterpret_cast<uint4 *>(arow + ((c ^ (row & 7)) << 4)) =
               make_uint4(wv[0], wv[1], wv[2], wv[3]);
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&afull[s]);
-        sc = sc_n;
-        bi = bi_n;
+        sc_b = sc_nb;
+        bi_b = bi_nb;
       }
     }
   }
