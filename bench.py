@@ -429,6 +429,7 @@ def sub_measurements(q, torch, dev, layer, flush, stream, hbm_peak, K, W):
         out[f"gemv_fp8_block_M{M}"] = {"ms": round(st, 5), "gbs": round(byts / st / 1e6, 1),
                                        "frac_hbm": round(byts / st / 1e6 / hbm_peak, 4)}
     del ws, ss
+    out.update(affine_prefill_measurement(q, torch, dev, flush, stream, K, W))
     # d4: MLX affine [14336, 7168], 4 and 8 bit
     N, Kd = 14336, 7168
     for bits in (4, 8):
@@ -448,6 +449,29 @@ def sub_measurements(q, torch, dev, layer, flush, stream, hbm_peak, K, W):
             byts = N * Kd * bits // 8 + 2 * N * (Kd // 64) * 2 + M * Kd * 2 + M * N * 2
             out[f"gemv_affine{bits}_M{M}"] = {"ms": round(st, 5), "gbs": round(byts / st / 1e6, 1),
                                               "frac_hbm": round(byts / st / 1e6 / hbm_peak, 4)}
+        del wq, sc, bi
+    return out
+
+
+def affine_prefill_measurement(q, torch, dev, flush, stream, K, W, M=4096):
+    """d4 at prefill: MLX affine [14336, 7168] 4- and 8-bit, M = 4096 activation rows, on the
+    tensor cores (weights dequantized to bf16 per tile); TFLOP/s against the bf16 peak."""
+    _, bf16_peak, peak_src = _peaks()
+    N, Kd = 14336, 7168
+    g = torch.Generator(device=dev).manual_seed(77)
+    x = torch.randn(M, Kd, device=dev, generator=g).to(torch.bfloat16)
+    out = {}
+    for bits in (4, 8):
+        wq = torch.randint(-2 ** 31, 2 ** 31 - 1, (N, Kd * bits // 32), dtype=torch.int32,
+                           device=dev, generator=g)
+        sc = (torch.rand(N, Kd // 64, device=dev, generator=g) * 0.019 + 0.001).to(torch.bfloat16)
+        bi = (torch.randn(N, Kd // 64, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+        ms = statistics.median(timed_steps(
+            torch, lambda i: q.linear.linear_affine(x, wq, sc, bi, bits), K, W, flush, stream))
+        tf = 2.0 * M * N * Kd / (ms / 1e3) / 1e12
+        out[f"qmm_affine{bits}_M{M}"] = {"ms": round(ms, 4), "tflops": round(tf, 1),
+                                         "frac_bf16_peak": round(tf / bf16_peak, 4),
+                                         "peak_source": peak_src + " bf16_tflops"}
         del wq, sc, bi
     return out
 
@@ -550,6 +574,8 @@ def main():
     ap.add_argument("--prefill-only", action="store_true",
                     help="only the T=8192 a8 prefill measurement (one JSON line)")
     ap.add_argument("--prefill-tokens", type=int, default=8192)
+    ap.add_argument("--affine-only", action="store_true",
+                    help="only the M=4096 affine tensor-core measurement (one JSON line)")
     args = ap.parse_args()
     global E, ROUTER_BYTES
     E = args.experts
@@ -563,6 +589,17 @@ def main():
         with Clocks(0) as clk:
             r = prefill_measurement(q, torch, dev, layer, flush, torch.cuda.current_stream(),
                                     _peaks(), args.steps, args.warmup, T=args.prefill_tokens)
+        r["clocks"] = clk.summary()
+        print(json.dumps(r))
+        return
+    if args.affine_only:
+        import torch
+        q = _package()
+        dev = torch.device("cuda", 0)
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        with Clocks(0) as clk:
+            r = affine_prefill_measurement(q, torch, dev, flush, torch.cuda.current_stream(),
+                                           args.steps, args.warmup)
         r["clocks"] = clk.summary()
         print(json.dumps(r))
         return
