@@ -95,13 +95,27 @@ __device__ __forceinline__ void block_scan3(int (&v)[3], int (&excl)[3], int (&t
 // One CTA of 1024 threads, one expert per thread (E <= 1024).  An expert with n pairs has
 // ceil(n / 224) row tiles; its last tile is narrow when it holds <= 64 rows.  Each list is
 // ordered expert-major, then m-tile, then row tile, so tiles that share weights or
-// activations are taken close together.
+// activations are taken close together.  The tile records are written by one warp per
+// expert, its lanes striding over the expert's tiles.
 __global__ void __launch_bounds__(1024) k_pf_scan(int *__restrict__ chunk_cnt, int nchunks, int E,
                                                   int mt_gu, int mt_dn, PfPlan plan) {
+  __shared__ int s_off[1024], s_rt0[1024], s_wide[1024], s_nar[1024], s_run[1024];
+  __shared__ int s_excl_w[1024], s_excl_n[1024];
   const int e = threadIdx.x;
   int run = 0;
   if (e < E) {
-    for (int c = 0; c < nchunks; ++c) {
+    int c = 0;
+    for (; c + 8 <= nchunks; c += 8) {   // 8 independent loads in flight
+      int v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = chunk_cnt[int64_t(c + u) * E + e];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        chunk_cnt[int64_t(c + u) * E + e] = run;
+        run += v[u];
+      }
+    }
+    for (; c < nchunks; ++c) {
       const int v = chunk_cnt[int64_t(c) * E + e];
       chunk_cnt[int64_t(c) * E + e] = run;
       run += v;
@@ -118,20 +132,13 @@ __global__ void __launch_bounds__(1024) k_pf_scan(int *__restrict__ chunk_cnt, i
   if (e < E) {
     plan.grp_off[e] = excl[0];
     plan.grp_rt0[e] = rt0;
-    const int mts[2] = {mt_gu, mt_dn};
-    for (int pj = 0; pj < 2; ++pj) {
-      const int mt_n = mts[pj];
-      int4 *tw = plan.tiles[2 * pj] + int64_t(excl[1]) * mt_n;
-      int4 *tn = plan.tiles[2 * pj + 1] + int64_t(excl[2]) * mt_n;
-      for (int mt = 0; mt < mt_n; ++mt) {
-        for (int j = 0; j < nwide; ++j)
-          tw[mt * nwide + j] = make_int4(e, mt, excl[0] + j * PF_TILE_ROWS,
-                                         min(PF_TILE_ROWS, run - j * PF_TILE_ROWS) |
-                                             ((rt0 + j) << 8));
-        if (nnar)
-          tn[mt] = make_int4(e, mt, excl[0] + nwide * PF_TILE_ROWS, tail | ((rt0 + nwide) << 8));
-      }
-    }
+    s_off[e] = excl[0];
+    s_rt0[e] = rt0;
+    s_wide[e] = nwide;
+    s_nar[e] = nnar;
+    s_run[e] = run;
+    s_excl_w[e] = excl[1];
+    s_excl_n[e] = excl[2];
   }
   if (threadIdx.x == 0) {
     plan.ntiles[0] = tot[1] * mt_gu;
@@ -139,6 +146,27 @@ __global__ void __launch_bounds__(1024) k_pf_scan(int *__restrict__ chunk_cnt, i
     plan.ntiles[2] = tot[1] * mt_dn;
     plan.ntiles[3] = tot[2] * mt_dn;
     for (int i = 0; i < 4; ++i) plan.next_tile[i] = 0;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int ee = warp; ee < E; ee += blockDim.x >> 5) {
+    const int nw = s_wide[ee], rn = s_run[ee], off = s_off[ee], r0 = s_rt0[ee];
+    const int mts[2] = {mt_gu, mt_dn};
+    for (int pj = 0; pj < 2; ++pj) {
+      const int mt_n = mts[pj];
+      int4 *tw = plan.tiles[2 * pj] + int64_t(s_excl_w[ee]) * mt_n;
+      for (int i = lane; i < mt_n * nw; i += 32) {
+        const int mt = i / nw, j = i % nw;
+        tw[i] = make_int4(ee, mt, off + j * PF_TILE_ROWS,
+                          min(PF_TILE_ROWS, rn - j * PF_TILE_ROWS) | ((r0 + j) << 8));
+      }
+      if (s_nar[ee]) {
+        int4 *tn = plan.tiles[2 * pj + 1] + int64_t(s_excl_n[ee]) * mt_n;
+        for (int mt = lane; mt < mt_n; mt += 32)
+          tn[mt] = make_int4(ee, mt, off + nw * PF_TILE_ROWS,
+                             (rn - nw * PF_TILE_ROWS) | ((r0 + nw) << 8));
+      }
+    }
   }
 }
 
