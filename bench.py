@@ -349,6 +349,7 @@ def run_ours(args):
         sub = sub_measurements(q, torch, dev, layer, flush, stream, hbm_peak, max(3, K // 2), W)
         sub["moe_prefill_T8192_a8"] = prefill_measurement(
             q, torch, dev, layer, flush, stream, (hbm_peak, bf16_peak, peak_src), max(3, K // 4), W)
+        sub.update(engram_measurement(q, torch, dev, flush, stream, max(3, K // 2), W))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -476,6 +477,59 @@ def affine_prefill_measurement(q, torch, dev, flush, stream, K, W, M=4096):
     return out
 
 
+def engram_measurement(q, torch, dev, flush, stream, K, W):
+    """d5: engram table fp8 e4m3 [96,000,xxx x 1024] (one ue8m0 per row, [115, 127]) built on
+    the device, 24 rows per token (2/3/4-gram x 8 heads, one layer, primes from 4,000,000)
+    hashed from uniform compressed ids in [0, 99092); a step = hash + gather + dequant + fp32
+    sum -> bf16 [T, 1024].  Bytes per token: 24 x (1024 + 1) read + 2048 written."""
+    import types
+    import numpy as np
+    hbm_peak, _, peak_src = _peaks()
+    args = types.SimpleNamespace(engram_layer_ids=(1,), engram_max_ngram_size=4,
+                                 engram_vocab_size=4_000_000, engram_n_heads=8, engram_pad_id=2,
+                                 engram_compressed_vocab_size=99092)
+    primes, _ = q.engram.build_layout(args)
+    rows, d = int(primes.sum()), 1024
+    args.engram_num_embeddings = (rows,)
+    hasher = q.engram.EngramHasher(args, np.arange(99092, dtype=np.int64), device=dev)
+    g = torch.Generator(device=dev).manual_seed(55)
+    table = torch.empty((rows, d), dtype=torch.uint8, device=dev)
+    for r0 in range(0, rows, 1 << 20):          # 1 GB at a time: uniform over non-NaN codes
+        c = table[r0:r0 + (1 << 20)]
+        c.random_(0, 254, generator=g)
+        c += (c >= 127).to(torch.uint8)
+    scale = torch.randint(115, 128, (rows, 1), dtype=torch.uint8, device=dev, generator=g)
+    emb = q.engram.EngramEmbedding(rows, d, block=d)
+    emb.weight, emb.scale = table, scale
+    out = {}
+    for T in (1, 8192):
+        start = 100 if T == 1 else 0
+        ids = [torch.randint(0, 99092, (1, T), dtype=torch.int64, device=dev, generator=g)
+               for _ in range(8)]
+        cache = torch.randint(0, 99092, (1, start + T + 8), dtype=torch.int64, device=dev,
+                              generator=g)
+
+        def step(i, T=T, start=start):
+            idx = hasher(ids[i % 8], start, cache)
+            return emb.gather_sum(idx.reshape(T, -1))
+
+        # the step replayed from CUDA graphs (one per input batch): device time, no host gaps
+        gr = graphed(torch, [lambda c=c: step(c) for c in range(8)])
+        ms = statistics.median(timed_steps(torch, lambda i: gr[i % 8].replay(), K, W, flush,
+                                           stream))
+        ms_host = statistics.median(timed_steps(torch, step, K, W, flush, stream))
+        byts = T * (24 * (d + 1) + 2 * d)
+        out[f"engram_T{T}"] = {"ms": round(ms, 4), "ms_eager": round(ms_host, 4),
+                               "tok_s": round(T / (ms / 1e3), 1),
+                               "gbs": round(byts / (ms / 1e3) / 1e9, 1),
+                               "frac_hbm": round(byts / (ms / 1e3) / 1e9 / hbm_peak, 4),
+                               "table_rows": rows, "table_gb": round(rows * (d + 1) / 1e9, 1),
+                               "peak_source": peak_src + " hbm_gbs"}
+    del table, scale, emb
+    torch.cuda.empty_cache()
+    return out
+
+
 # ---------------------------------------------------------------- CPU baseline --
 
 def cpu_baseline(seconds=15.0, sample_experts=None):
@@ -576,6 +630,8 @@ def main():
     ap.add_argument("--prefill-tokens", type=int, default=8192)
     ap.add_argument("--affine-only", action="store_true",
                     help="only the M=4096 affine tensor-core measurement (one JSON line)")
+    ap.add_argument("--engram-only", action="store_true",
+                    help="only the engram d5 measurement (one JSON line)")
     args = ap.parse_args()
     global E, ROUTER_BYTES
     E = args.experts
@@ -589,6 +645,17 @@ def main():
         with Clocks(0) as clk:
             r = prefill_measurement(q, torch, dev, layer, flush, torch.cuda.current_stream(),
                                     _peaks(), args.steps, args.warmup, T=args.prefill_tokens)
+        r["clocks"] = clk.summary()
+        print(json.dumps(r))
+        return
+    if args.engram_only:
+        import torch
+        q = _package()
+        dev = torch.device("cuda", 0)
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        with Clocks(0) as clk:
+            r = engram_measurement(q, torch, dev, flush, torch.cuda.current_stream(),
+                                   args.steps, args.warmup)
         r["clocks"] = clk.summary()
         print(json.dumps(r))
         return

@@ -1439,7 +1439,9 @@ extern "C" int dsv41_engram_hash(const int64_t *input_ids, int64_t B, int64_t L,
                                                                  max_seq);
   DSV41_CHECK_LAUNCH("engram_compress");
   const int64_t n2 = B * L * n_layers;
-  k_engram_hash<<<unsigned(ceil_div(n2, 128)), 128, 0, st>>>(B, L, start_pos, ids_cache, max_seq,
+  const size_t hash_smem = sizeof(uint64_t) * size_t(n_layers) * (max_ngram - 1) * n_heads;
+  DSV41_REQUIRE(hash_smem <= 48 * 1024, DSV41_ERR_UNSUPPORTED, "too many hash primes");
+  k_engram_hash<<<unsigned(ceil_div(n2, 128)), 128, hash_smem, st>>>(B, L, start_pos, ids_cache, max_seq,
                                                              multipliers, primes, offsets,
                                                              n_layers, max_ngram, n_heads, pad_id,
                                                              out);
@@ -1481,21 +1483,22 @@ extern "C" int dsv41_engram_gather_sum(const uint8_t *table, const uint8_t *scal
                 "out_dtype must be F32 or BF16");
   if (n_tok == 0) return DSV41_OK;
   DSV41_REQUIRE(table && scale && idx && out, DSV41_ERR_BAD_ARG, "NULL pointer");
-  DSV41_REQUIRE(aligned(table, 8), DSV41_ERR_MISALIGNED, "table must be 8-byte aligned");
-  const unsigned blocks = unsigned(ceil_div(n_tok * 32, 256));
+  DSV41_REQUIRE(aligned(table, 8) && aligned(out, 16), DSV41_ERR_MISALIGNED,
+                "table must be 8-byte and out 16-byte aligned");
   cudaStream_t st = STREAM(stream);
   ProfScope prof("engram_gather_sum", st);
-#define GS(T, DPL)                                                                           \
-  k_engram_gather_sum<T, DPL><<<blocks, 256, 0, st>>>(table, scale, rows, row_lo, block, idx, \
+  // a warp covers 256 columns (d = 256) or 512 (d = 512, 1024)
+  const int ch = d == 256 ? 1 : 2;
+  const unsigned blocks = unsigned(ceil_div(n_tok * (d / (256 * ch)) * 32, 256));
+#define GS(T, CHV)                                                                           \
+  k_engram_gather_sum<T, CHV><<<blocks, 256, 0, st>>>(table, scale, rows, row_lo, d, block, idx, \
                                                       n_tok, n_per_tok, (T *)out)
   if (out_dtype == DSV41_F32) {
-    if (d == 256) GS(float, 8);
-    else if (d == 512) GS(float, 16);
-    else GS(float, 32);
+    if (ch == 1) GS(float, 1);
+    else GS(float, 2);
   } else {
-    if (d == 256) GS(__nv_bfloat16, 8);
-    else if (d == 512) GS(__nv_bfloat16, 16);
-    else GS(__nv_bfloat16, 32);
+    if (ch == 1) GS(__nv_bfloat16, 1);
+    else GS(__nv_bfloat16, 2);
   }
 #undef GS
   DSV41_CHECK_LAUNCH("engram_gather_sum");

@@ -32,12 +32,22 @@ __global__ void k_engram_compress(const int64_t *__restrict__ ids, int64_t B, in
   cache[b * max_seq + start + l] = token_map[id];
 }
 
-// step 2: hashes; one thread per (b, l, layer)
+// step 2: hashes; one thread per (b, l, layer).  x % p by Barrett reduction: with
+// m = floor((2^64 - 1) / p), q = hi64(x * m) is floor(x / p) or one less, so one
+// conditional subtraction gives the exact remainder (x < 2^63, p < 2^63).  The block
+// computes the m of every prime once into shared memory.
 __global__ void k_engram_hash(int64_t B, int64_t L, int64_t start,
                               const int64_t *__restrict__ cache, int64_t max_seq,
                               const int64_t *__restrict__ mult, const int64_t *__restrict__ primes,
                               const int64_t *__restrict__ offsets, int nL, int G, int H,
                               int64_t pad_id, int64_t *__restrict__ out) {
+  extern __shared__ uint64_t s_recip[];   // [nL * (G - 1) * H]
+  const int np = nL * (G - 1) * H;
+  for (int k = threadIdx.x; k < np; k += blockDim.x) {
+    const uint64_t pk = uint64_t(primes[k]);
+    s_recip[k] = pk > 1 ? ~0ull / pk : 0ull;
+  }
+  __syncthreads();
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (i >= B * L * nL) return;
   const int layer = int(i % nL);
@@ -55,11 +65,36 @@ __global__ void k_engram_hash(int64_t B, int64_t L, int64_t start,
     const int64_t prod = tok * mrow[shift];
     rolling = shift == 0 ? prod : (rolling ^ prod);
     if (shift >= 1) {
-      const int64_t *pr = primes + ((int64_t)layer * (G - 1) + (shift - 1)) * H;
+      const int base = (layer * (G - 1) + (shift - 1)) * H;
       const int64_t *of = offsets + (int64_t)layer * cols + (shift - 1) * H;
-      for (int h = 0; h < H; ++h) o[(shift - 1) * H + h] = rolling % pr[h] + of[h];
+      const uint64_t x = uint64_t(rolling);
+      for (int h = 0; h < H; ++h) {
+        const uint64_t p = uint64_t(primes[base + h]);
+        uint64_t r;
+        if (p > 1) {
+          r = x - __umul64hi(x, s_recip[base + h]) * p;
+          if (r >= p) r -= p;
+        } else {
+          r = 0;
+        }
+        o[(shift - 1) * H + h] = int64_t(r) + of[h];
+      }
     }
   }
+}
+
+// 8 consecutive outputs from one 16-byte (bf16) or 32-byte (fp32) store.
+__device__ __forceinline__ void store8(float *p, const float *v) {
+  reinterpret_cast<float4 *>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+  reinterpret_cast<float4 *>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+__device__ __forceinline__ void store8(__nv_bfloat16 *p, const float *v) {
+  uint4 o;
+  o.x = uint32_t(f2bf_bits(v[0])) | (uint32_t(f2bf_bits(v[1])) << 16);
+  o.y = uint32_t(f2bf_bits(v[2])) | (uint32_t(f2bf_bits(v[3])) << 16);
+  o.z = uint32_t(f2bf_bits(v[4])) | (uint32_t(f2bf_bits(v[5])) << 16);
+  o.w = uint32_t(f2bf_bits(v[6])) | (uint32_t(f2bf_bits(v[7])) << 16);
+  *reinterpret_cast<uint4 *>(p) = o;
 }
 
 template <typename T> __device__ __forceinline__ void store_out(T *p, float v);
@@ -81,6 +116,7 @@ __global__ void k_engram_gather_rows(const uint8_t *__restrict__ table,
   const int64_t local = idx[warp] - row_lo;
   const bool in = local >= 0 && local < rows;
   const int64_t sb = d / block;
+  const int blk = int(block);                 // <= d, so 32-bit index arithmetic
   T *o = out + warp * d;
   for (int64_t c = lane * 8; c < d; c += 256) {
     float f[8];
@@ -91,7 +127,7 @@ __global__ void k_engram_gather_rows(const uint8_t *__restrict__ table,
       e4m3x4_to_f16x4(uint32_t(v >> 32), h[2], h[3]);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float sc = e8m0f(scale[local * sb + (c + j) / block]);
+        const float sc = e8m0f(scale[local * sb + (int(c) + j) / blk]);
         const float2 p = h2f2(h[j >> 1]);
         f[j] = __fmul_rn((j & 1) ? p.y : p.x, sc);
       }
@@ -104,63 +140,64 @@ __global__ void k_engram_gather_rows(const uint8_t *__restrict__ table,
   }
 }
 
-// One warp per token; D_PER_LANE = d / 32 values per lane (d = 32 * D_PER_LANE,
-// D_PER_LANE % 8 == 0); rows summed in column order, fp32.
-template <typename T, int D_PER_LANE>
+// Warps per token = d / (256 * CH): a warp covers 256 * CH columns, its lanes 8-column
+// chunks at c*256 + lane*8 (coalesced 256-byte spans); rows summed in column order, fp32,
+// 8 rows in flight per warp, table rows streamed (read once, not kept in L1/L2).
+template <typename T, int CH>
 __global__ void __launch_bounds__(256) k_engram_gather_sum(
     const uint8_t *__restrict__ table, const uint8_t *__restrict__ scale, int64_t rows,
-    int64_t row_lo, int64_t block, const int64_t *__restrict__ idx, int64_t n_tok, int n_per_tok,
-    T *__restrict__ out) {
-  constexpr int64_t D = 32 * D_PER_LANE;
-  constexpr int CH = D_PER_LANE / 8;  // 8-byte chunks per lane per row
-  const int64_t tok = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    int64_t row_lo, int64_t D, int64_t block, const int64_t *__restrict__ idx, int64_t n_tok,
+    int n_per_tok, T *__restrict__ out) {
+  const int64_t gw = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
+  const int wpt = int(D / (256 * CH));
+  const int64_t tok = gw / wpt;
   if (tok >= n_tok) return;
+  const int64_t col0 = (gw % wpt) * 256 * CH;
   const int64_t sb = D / block;
-  float acc[D_PER_LANE];
+  // the scale column of each of this lane's chunks (8 | block keeps a chunk in one block)
+  int soff[CH];
 #pragma unroll
-  for (int j = 0; j < D_PER_LANE; ++j) acc[j] = 0.0f;
+  for (int c = 0; c < CH; ++c) soff[c] = int(col0 + c * 256 + lane * 8) / int(block);
+  float acc[8 * CH];
+#pragma unroll
+  for (int j = 0; j < 8 * CH; ++j) acc[j] = 0.0f;
   const int64_t *ti = idx + tok * n_per_tok;
-  // lane owns columns [c*256 + lane*8, +8) for c in [0, CH): coalesced 256-byte spans
-  for (int h = 0; h < n_per_tok; h += 4) {
-    uint64_t v[4][CH];
-    float sc[4][CH];
-    bool in[4];
+  for (int h = 0; h < n_per_tok; h += 8) {
+    uint64_t v[8][CH];
+    bool in[8];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < 8; ++u) {
       const int hh = h + u;
       const int64_t local = hh < n_per_tok ? ti[hh] - row_lo : -1;
       in[u] = hh < n_per_tok && local >= 0 && local < rows;
 #pragma unroll
-      for (int c = 0; c < CH; ++c) {
-        const int64_t col = c * 256 + lane * 8;
-        v[u][c] = in[u] ? __ldg(reinterpret_cast<const unsigned long long *>(table + local * D + col))
+      for (int c = 0; c < CH; ++c)
+        v[u][c] = in[u] ? __ldcs(reinterpret_cast<const unsigned long long *>(
+                              table + local * D + col0 + c * 256 + lane * 8))
                         : 0ull;
-        sc[u][c] = in[u] ? e8m0f(scale[local * sb + col / block]) : 0.0f;
-      }
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < 8; ++u) {
       if (!in[u]) continue;
+      const int64_t local = ti[h + u] - row_lo;
 #pragma unroll
       for (int c = 0; c < CH; ++c) {
-        uint32_t hh[4];
-        e4m3x4_to_f16x4(uint32_t(v[u][c]), hh[0], hh[1]);
-        e4m3x4_to_f16x4(uint32_t(v[u][c] >> 32), hh[2], hh[3]);
+        const float s = e8m0f(scale[local * sb + soff[c]]);
+        uint32_t hq[4];
+        e4m3x4_to_f16x4(uint32_t(v[u][c]), hq[0], hq[1]);
+        e4m3x4_to_f16x4(uint32_t(v[u][c] >> 32), hq[2], hq[3]);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float2 p = h2f2(hh[j >> 1]);
-          // block >= 8 and 8 | block keep the 8 columns in one scale block
-          acc[c * 8 + j] = __fadd_rn(acc[c * 8 + j], __fmul_rn((j & 1) ? p.y : p.x, sc[u][c]));
+          const float2 p = h2f2(hq[j >> 1]);
+          acc[c * 8 + j] = __fadd_rn(acc[c * 8 + j], __fmul_rn((j & 1) ? p.y : p.x, s));
         }
       }
     }
   }
-  T *o = out + tok * D;
+  T *o = out + tok * D + col0;
 #pragma unroll
-  for (int c = 0; c < CH; ++c)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) store_out<T>(o + c * 256 + lane * 8 + j, acc[c * 8 + j]);
+  for (int c = 0; c < CH; ++c) store8(o + c * 256 + lane * 8, acc + c * 8);
 }
 
 }  // namespace dsv41
