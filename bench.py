@@ -530,6 +530,54 @@ def engram_measurement(q, torch, dev, flush, stream, K, W):
     return out
 
 
+def run_prefill_ep(args):
+    """d3 over NCCL: each rank prefills its own T tokens (weak scaling) with E / ws experts;
+    the step is timed with CUDA events per rank, max over ranks."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    from importlib import import_module
+    q = _package()
+    ep = import_module("deepseek_v41_mlx_b200.ep")
+    world = int(os.environ["WORLD_SIZE"])
+    rank = int(os.environ["RANK"])
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=180))
+    T = args.prefill_tokens
+    layer = ep.EPMoE.random_init(q, torch, dev, rank, world, E, D, I, TOPK)
+    g = torch.Generator(device=dev).manual_seed(4321 + rank)
+    x = torch.randn(T, D, device=dev, generator=g).to(torch.bfloat16)
+    w, idx = zipf_routing(torch, dev, x, layer.gate_w, T, seed=7 + rank)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    fn = lambda i: layer.forward_prefill(x, weights=w, indices=idx)
+    for i in range(args.warmup):
+        fn(i)
+    torch.cuda.synchronize()
+    dist.barrier()
+    with Clocks(local) as clk:
+        ms = timed_steps(torch, fn, args.steps, 0, flush, stream)
+        dist.barrier()
+        torch.cuda.synchronize()
+    st = torch.tensor([statistics.median(ms)], device=dev)
+    dist.all_reduce(st, op=dist.ReduceOp.MAX)
+    layer.track = True
+    fn(0)
+    layer.track = False
+    loc = torch.tensor([float(layer.local_active[-1])], device=dev)
+    dist.barrier()
+    dist.destroy_process_group()
+    if rank == 0:
+        step = float(st.item())
+        print(json.dumps({"metric": "MoE-layer prefill tok/s (a8, EP)", "tok_s": round(T * world / (step / 1e3), 1),
+                          "ms": round(step, 4), "n_gpus": world, "tokens_per_gpu": T,
+                          "parallelism": "ep%d" % world, "experts_per_gpu": E // world,
+                          "scaling": "weak", "clocks": clk.summary(),
+                          "routing": "Zipf(1.1) per rank (seed 7 + rank)"}))
+
+
 # ---------------------------------------------------------------- CPU baseline --
 
 def cpu_baseline(seconds=15.0, sample_experts=None):
@@ -636,6 +684,9 @@ def main():
     global E, ROUTER_BYTES
     E = args.experts
     ROUTER_BYTES = E * D * 2
+    if args.prefill_only and int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        run_prefill_ep(args)
+        return
     if args.prefill_only:
         import torch
         q = _package()

@@ -1183,7 +1183,8 @@ size_t pf_carve(const dsv41_moe_config *cfg, const PfDims &d, bool route, bool s
   return c.off + 256;
 }
 
-int pf_check(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, int64_t T, bool shared) {
+int pf_check(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, int64_t T, bool shared,
+             bool routed = true) {
   DSV41_REQUIRE(cfg && W, DSV41_ERR_BAD_ARG, "NULL config/weights");
   int rc = route_check(T, cfg->dim, cfg->n_experts, cfg->topk, cfg->score_func);
   if (rc) return rc;
@@ -1193,10 +1194,11 @@ int pf_check(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, int64_t T,
   DSV41_REQUIRE(T * cfg->topk < (int64_t(1) << 30) && cfg->n_experts * cfg->dim < (int64_t(1) << 31),
                 DSV41_ERR_BAD_SHAPE, "too many pairs or expert rows");
   if (T == 0) return DSV41_OK;
-  DSV41_REQUIRE(W->w1 && W->s1 && W->w3 && W->s3 && W->w2 && W->s2, DSV41_ERR_BAD_ARG,
-                "NULL expert pointer");
-  DSV41_REQUIRE(aligned(W->s1, 4) && aligned(W->s3, 4) && aligned(W->s2, 4), DSV41_ERR_MISALIGNED,
-                "expert scales must be 4-byte aligned");
+  DSV41_REQUIRE(!routed || (W->w1 && W->s1 && W->w3 && W->s3 && W->w2 && W->s2),
+                DSV41_ERR_BAD_ARG, "NULL expert pointer");
+  DSV41_REQUIRE(!routed || (aligned(W->s1, 4) && aligned(W->s3, 4) && aligned(W->s2, 4)),
+                DSV41_ERR_MISALIGNED, "expert scales must be 4-byte aligned");
+  DSV41_REQUIRE(shared || routed, DSV41_ERR_BAD_ARG, "neither routed nor shared experts");
   DSV41_REQUIRE(!shared || (W->sw1 && W->ss1 && W->sw3 && W->ss3 && W->sw2 && W->ss2),
                 DSV41_ERR_BAD_ARG, "NULL shared-expert pointer");
   DSV41_REQUIRE(!shared || (aligned(W->ss1, 4) && aligned(W->ss3, 4) && aligned(W->ss2, 4) &&
@@ -1212,11 +1214,13 @@ int pf_pack(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, uint8_t *ou
             cudaStream_t st) {
   const int64_t E = cfg->n_experts, D = cfg->dim, I = cfg->inter;
   ProfScope prof("pf_pack_scales", st);
-  k_pack_sfw<<<unsigned(4 * num_sms()), 256, 0, st>>>(W->s1, W->s3, E, I, D, 1, 0, out);
-  DSV41_CHECK_LAUNCH("pack gate/up scales");
-  k_pack_sfw<<<unsigned(4 * num_sms()), 256, 0, st>>>(W->s2, nullptr, E, D, I, 0, 0,
-                                                      out + pf_packed_gu_bytes(cfg));
-  DSV41_CHECK_LAUNCH("pack down scales");
+  if (W->s1 && W->s3 && W->s2) {
+    k_pack_sfw<<<unsigned(4 * num_sms()), 256, 0, st>>>(W->s1, W->s3, E, I, D, 1, 0, out);
+    DSV41_CHECK_LAUNCH("pack gate/up scales");
+    k_pack_sfw<<<unsigned(4 * num_sms()), 256, 0, st>>>(W->s2, nullptr, E, D, I, 0, 0,
+                                                        out + pf_packed_gu_bytes(cfg));
+    DSV41_CHECK_LAUNCH("pack down scales");
+  }
   if (W->ss1 && W->ss3 && W->ss2) {   // fp8 shared expert: one ue8m0 per 32x32 block
     uint8_t *sh = out + pf_packed_sh_off(cfg);
     k_pack_sfw<<<unsigned(num_sms()), 256, 0, st>>>(W->ss1, W->ss3, 1, I, D, 1, 5, sh);
@@ -1242,12 +1246,25 @@ extern "C" int dsv41_moe_prefill_pack(const dsv41_moe_config *cfg, const dsv41_m
   return pf_pack(cfg, W, reinterpret_cast<uint8_t *>(packed), STREAM(stream));
 }
 
+namespace {
+// shared-only calls carry no (token, expert) pairs
+PfDims pf_dims_for(const dsv41_moe_config *cfg, int64_t T) {
+  PfDims d = pf_dims(cfg, T);
+  if (cfg->flags & DSV41_MOE_SHARED_ONLY) {
+    d.P = 0;
+    d.nchunks = 0;
+  }
+  return d;
+}
+}  // namespace
+
 extern "C" size_t dsv41_moe_prefill_workspace_size(const dsv41_moe_config *cfg, int64_t T,
                                                    int with_routing, int with_packed) {
   if (!cfg || T <= 0) return 256;
   const bool shared = (cfg->flags & DSV41_MOE_NO_SHARED) == 0;
-  return pf_carve(cfg, pf_dims(cfg, T), with_routing == 0, shared, with_packed == 0, nullptr,
-                  ~size_t(0) >> 1, nullptr);
+  const bool routed = (cfg->flags & DSV41_MOE_SHARED_ONLY) == 0;
+  return pf_carve(cfg, pf_dims_for(cfg, T), routed && with_routing == 0, shared,
+                  with_packed == 0, nullptr, ~size_t(0) >> 1, nullptr);
 }
 
 extern "C" int dsv41_moe_prefill(const dsv41_moe_config *cfg, const dsv41_moe_weights *W,
@@ -1256,7 +1273,8 @@ extern "C" int dsv41_moe_prefill(const dsv41_moe_config *cfg, const dsv41_moe_we
                                  int out_dtype, void *y, void *workspace, size_t workspace_bytes,
                                  void *stream) {
   const bool shared = cfg && (cfg->flags & DSV41_MOE_NO_SHARED) == 0;
-  int rc = pf_check(cfg, W, T, shared);
+  const bool routed = cfg && (cfg->flags & DSV41_MOE_SHARED_ONLY) == 0;
+  int rc = pf_check(cfg, W, T, shared, routed);
   if (rc) return rc;
   if (T == 0) return DSV41_OK;
   DSV41_REQUIRE(!packed_scales || aligned(packed_scales, 16), DSV41_ERR_MISALIGNED,
@@ -1265,9 +1283,9 @@ extern "C" int dsv41_moe_prefill(const dsv41_moe_config *cfg, const dsv41_moe_we
                 "output must be F32 or BF16");
   DSV41_REQUIRE(x && y && aligned(x, 16) && aligned(y, 16), DSV41_ERR_MISALIGNED,
                 "x and y must be 16-byte aligned");
-  const bool route = route_indices == nullptr;
+  const bool route = routed && route_indices == nullptr;
   DSV41_REQUIRE(!route || W->gate_w, DSV41_ERR_BAD_ARG, "NULL gate weight");
-  const PfDims d = pf_dims(cfg, T);
+  const PfDims d = pf_dims_for(cfg, T);
   PfWs ws;
   const size_t need = pf_carve(cfg, d, route, shared, packed_scales == nullptr,
                                reinterpret_cast<uint8_t *>(workspace), workspace_bytes, &ws);
@@ -1299,75 +1317,77 @@ extern "C" int dsv41_moe_prefill(const dsv41_moe_config *cfg, const dsv41_moe_we
         shared ? ws.sfx_sh : nullptr, BS_BN);
     DSV41_CHECK_LAUNCH("pf_act_quant");
   }
-  // stable sort of the (token, slot) pairs by expert + tile lists
-  {
-    ProfScope prof("pf_plan", st);
-    const size_t sm = size_t(16) * d.E * sizeof(int);
-    if (sm > 48 * 1024) {
-      cudaFuncSetAttribute(k_pf_count, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
-      cudaFuncSetAttribute(k_pf_place, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+  if (routed) {
+    // stable sort of the (token, slot) pairs by expert + tile lists
+    {
+      ProfScope prof("pf_plan", st);
+      const size_t sm = size_t(16) * d.E * sizeof(int);
+      if (sm > 48 * 1024) {
+        cudaFuncSetAttribute(k_pf_count, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+        cudaFuncSetAttribute(k_pf_place, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+      }
+      k_pf_count<<<unsigned(d.nchunks), PF_CHUNK, sm, st>>>(ri, d.P, int(d.E), ws.chunk_cnt);
+      DSV41_CHECK_LAUNCH("pf_count");
+      k_pf_scan<<<1, 1024, 0, st>>>(ws.chunk_cnt, int(d.nchunks), int(d.E), int(d.I / 64),
+                                    int(d.D / BS_BM), ws.plan);
+      DSV41_CHECK_LAUNCH("pf_scan");
+      k_pf_place<<<unsigned(d.nchunks), PF_CHUNK, sm, st>>>(ri, rw, d.P, d.k, int(d.E), ws.plan);
+      DSV41_CHECK_LAUNCH("pf_place");
     }
-    k_pf_count<<<unsigned(d.nchunks), PF_CHUNK, sm, st>>>(ri, d.P, int(d.E), ws.chunk_cnt);
-    DSV41_CHECK_LAUNCH("pf_count");
-    k_pf_scan<<<1, 1024, 0, st>>>(ws.chunk_cnt, int(d.nchunks), int(d.E), int(d.I / 64),
-                                  int(d.D / BS_BM), ws.plan);
-    DSV41_CHECK_LAUNCH("pf_scan");
-    k_pf_place<<<unsigned(d.nchunks), PF_CHUNK, sm, st>>>(ri, rw, d.P, d.k, int(d.E), ws.plan);
-    DSV41_CHECK_LAUNCH("pf_place");
-  }
-  {
-    ProfScope prof("pf_gather", st);
-    k_pf_gather<<<unsigned(ceil_div(d.P * 32, 256)), 256, 0, st>>>(
-        ws.xq, ws.xs, ws.plan.pair_tok, ws.plan.row_tile, d.P, d.D, ws.xpq, ws.sfx_gu);
-    DSV41_CHECK_LAUNCH("pf_gather");
-  }
-  // routed gate/up: SwiGLU * routing weight, bf16, act_quant -> hq/hs
-  {
-    BsMaps maps;
-    memset(&maps, 0, sizeof(maps));
-    rc = bs_wmap(&maps.w, W->w1, BS_W_FP4, d.E * d.I, d.D, 64);
-    if (!rc) rc = bs_wmap(&maps.w2, W->w3, BS_W_FP4, d.E * d.I, d.D, 64);
-    if (!rc) rc = bs_xmaps(maps.x, ws.xpq, d.P, d.D);
-    if (rc) return rc;
-    BsArgs a;
-    memset(&a, 0, sizeof(a));
-    a.nkb = int(d.D / BS_BK);
-    a.a_rows = int(d.I);
-    a.sw = bs_scale(W->s1, d.D / 32, 0, 32, d.E * d.I);
-    a.sw2 = bs_scale(W->s3, d.D / 32, 0, 32, d.E * d.I);
-    a.nkq = int(d.D / 128);
-    a.mtiles = int(d.I / 64);
-    a.sfa_atoms = packed;
-    a.sfb_atoms = ws.sfx_gu;
-    a.pw = ws.plan.pair_w;
-    a.hq = ws.hq;
-    a.hs_atoms = ws.sfx_dn;
-    a.ldh = d.I;
-    a.limit = cfg->swiglu_limit;
-    rc = bs_grouped_launch<BS_W_FP4, BS_EPI_SWIGLU>("pf_gate_up_fp4", "pf_gate_up_fp4_narrow",
-                                                    maps, a, ws.plan, 0, st);
-    if (rc) return rc;
-  }
-  // routed down -> yp (bf16 per pair)
-  {
-    BsMaps maps;
-    memset(&maps, 0, sizeof(maps));
-    rc = bs_wmap(&maps.w, W->w2, BS_W_FP4, d.E * d.D, d.I, 128);
-    if (!rc) rc = bs_xmaps(maps.x, ws.hq, d.P, d.I);
-    if (rc) return rc;
-    BsArgs a;
-    memset(&a, 0, sizeof(a));
-    a.nkb = int(d.I / BS_BK);
-    a.a_rows = int(d.D);
-    a.nkq = int(d.I / 128);
-    a.mtiles = int(d.D / BS_BM);
-    a.sfa_atoms = packed + pf_packed_gu_bytes(cfg);
-    a.sfb_atoms = ws.sfx_dn;
-    a.out = ws.yp;
-    a.ldo = d.D;
-    rc = bs_grouped_launch<BS_W_FP4, BS_EPI_BF16>("pf_down_fp4", "pf_down_fp4_narrow", maps, a,
-                                                  ws.plan, 2, st);
-    if (rc) return rc;
+    {
+      ProfScope prof("pf_gather", st);
+      k_pf_gather<<<unsigned(ceil_div(d.P * 32, 256)), 256, 0, st>>>(
+          ws.xq, ws.xs, ws.plan.pair_tok, ws.plan.row_tile, d.P, d.D, ws.xpq, ws.sfx_gu);
+      DSV41_CHECK_LAUNCH("pf_gather");
+    }
+    // routed gate/up: SwiGLU * routing weight, bf16, act_quant -> hq/hs
+    {
+      BsMaps maps;
+      memset(&maps, 0, sizeof(maps));
+      rc = bs_wmap(&maps.w, W->w1, BS_W_FP4, d.E * d.I, d.D, 64);
+      if (!rc) rc = bs_wmap(&maps.w2, W->w3, BS_W_FP4, d.E * d.I, d.D, 64);
+      if (!rc) rc = bs_xmaps(maps.x, ws.xpq, d.P, d.D);
+      if (rc) return rc;
+      BsArgs a;
+      memset(&a, 0, sizeof(a));
+      a.nkb = int(d.D / BS_BK);
+      a.a_rows = int(d.I);
+      a.sw = bs_scale(W->s1, d.D / 32, 0, 32, d.E * d.I);
+      a.sw2 = bs_scale(W->s3, d.D / 32, 0, 32, d.E * d.I);
+      a.nkq = int(d.D / 128);
+      a.mtiles = int(d.I / 64);
+      a.sfa_atoms = packed;
+      a.sfb_atoms = ws.sfx_gu;
+      a.pw = ws.plan.pair_w;
+      a.hq = ws.hq;
+      a.hs_atoms = ws.sfx_dn;
+      a.ldh = d.I;
+      a.limit = cfg->swiglu_limit;
+      rc = bs_grouped_launch<BS_W_FP4, BS_EPI_SWIGLU>("pf_gate_up_fp4", "pf_gate_up_fp4_narrow",
+                                                      maps, a, ws.plan, 0, st);
+      if (rc) return rc;
+    }
+    // routed down -> yp (bf16 per pair)
+    {
+      BsMaps maps;
+      memset(&maps, 0, sizeof(maps));
+      rc = bs_wmap(&maps.w, W->w2, BS_W_FP4, d.E * d.D, d.I, 128);
+      if (!rc) rc = bs_xmaps(maps.x, ws.hq, d.P, d.I);
+      if (rc) return rc;
+      BsArgs a;
+      memset(&a, 0, sizeof(a));
+      a.nkb = int(d.I / BS_BK);
+      a.a_rows = int(d.D);
+      a.nkq = int(d.I / 128);
+      a.mtiles = int(d.D / BS_BM);
+      a.sfa_atoms = packed + pf_packed_gu_bytes(cfg);
+      a.sfb_atoms = ws.sfx_dn;
+      a.out = ws.yp;
+      a.ldo = d.D;
+      rc = bs_grouped_launch<BS_W_FP4, BS_EPI_BF16>("pf_down_fp4", "pf_down_fp4_narrow", maps, a,
+                                                    ws.plan, 2, st);
+      if (rc) return rc;
+    }
   }
   if (shared) {
     BsMaps maps;
@@ -1407,10 +1427,11 @@ extern "C" int dsv41_moe_prefill(const dsv41_moe_config *cfg, const dsv41_moe_we
     ProfScope prof("pf_combine", st);
     if (out_dtype == DSV41_F32)
       k_pf_combine<float><<<unsigned(ceil_div(n, 256)), 256, 0, st>>>(
-          ws.yp, shared ? ws.ysh : nullptr, ri, ws.plan.slot_pos, d.T, d.k, d.D, (float *)y);
+          ws.yp, shared ? ws.ysh : nullptr, ri, ws.plan.slot_pos, d.T, routed ? d.k : 0, d.D,
+          (float *)y);
     else
       k_pf_combine<__nv_bfloat16><<<unsigned(ceil_div(n, 256)), 256, 0, st>>>(
-          ws.yp, shared ? ws.ysh : nullptr, ri, ws.plan.slot_pos, d.T, d.k, d.D,
+          ws.yp, shared ? ws.ysh : nullptr, ri, ws.plan.slot_pos, d.T, routed ? d.k : 0, d.D,
           (__nv_bfloat16 *)y);
     DSV41_CHECK_LAUNCH("pf_combine");
   }

@@ -50,8 +50,9 @@ def exchange_counts(dist, send_counts, group=None):
     return recv
 
 
-def dispatch(dist, x, indices, world, experts_per_rank, group=None):
-    """-> (recv_rows [R, D], recv_local_expert [R], order, send_counts, recv_counts)."""
+def dispatch(dist, x, indices, world, experts_per_rank, group=None, weights=None):
+    """-> (recv_rows [R, D], recv_local_expert [R], order, send_counts, recv_counts) and, when
+    ``weights`` [T, k] is given, the pairs' routing weights recv_w [R] last."""
     t = L.torch()
     D = x.shape[-1]
     k = indices.shape[-1]
@@ -67,7 +68,12 @@ def dispatch(dist, x, indices, world, experts_per_rank, group=None):
     recv_exp = t.empty((R,), dtype=t.int32, device=x.device)
     dist.all_to_all_single(recv_rows, send_rows, rc, sc, group=group)
     dist.all_to_all_single(recv_exp, send_exp, rc, sc, group=group)
-    return recv_rows, recv_exp, order, sc, rc
+    if weights is None:
+        return recv_rows, recv_exp, order, sc, rc
+    send_w = weights.reshape(-1).float().index_select(0, order).contiguous()
+    recv_w = t.empty((R,), dtype=t.float32, device=x.device)
+    dist.all_to_all_single(recv_w, send_w, rc, sc, group=group)
+    return recv_rows, recv_exp, order, sc, rc, recv_w
 
 
 def combine(dist, y_recv, order, send_counts, recv_counts, T, k, group=None):
@@ -79,6 +85,20 @@ def combine(dist, y_recv, order, send_counts, recv_counts, T, k, group=None):
     Y = t.empty((T * k, D), dtype=y_recv.dtype, device=y_recv.device)
     Y.index_copy_(0, order, back)
     return Y.reshape(T, k, D)
+
+
+def ascending_sum(Y, indices, shared=None):
+    """sum over j of Y[t, j] in ascending expert-id order (fp32), then + shared: the order of
+    upstream's expert loop (docs/reference/model.py:895-900) and of the single-GPU prefill."""
+    t = L.torch()
+    order = t.argsort(indices.to(t.int64), dim=1, stable=True)
+    Ys = t.take_along_dim(Y, order[:, :, None], dim=1)
+    acc = t.zeros(Y.shape[0], Y.shape[2], dtype=t.float32, device=Y.device)
+    for j in range(Y.shape[1]):
+        acc = acc + Ys[:, j].float()
+    if shared is not None:
+        acc = acc + shared.float()
+    return acc
 
 
 def weighted_sum(Y, weights, shared=None):
@@ -202,6 +222,40 @@ class EPMoE:
         g = t.clamp(g, max=lim)
         h = (t.nn.functional.silu(g) * u).to(t.bfloat16)
         return linear_fp8(h, s.w2.weight, s.w2.scales, out_dtype=t.bfloat16).float()
+
+    # ---------------------------------------------------------------- prefill (a8)
+    def _local_prefill(self, rows, local_ids, recv_w):
+        """Owner side: each received row is one pair; its routing weight scales h before
+        the down projection (upstream Expert.forward) -> bf16 [R, D]."""
+        t = L.torch()
+        R = rows.shape[0]
+        if R == 0:
+            return t.empty((0, self.local.dim), dtype=t.bfloat16, device=rows.device)
+        return self.local.prefill_a8(rows, weights=recv_w.reshape(R, 1),
+                                     indices=local_ids.reshape(R, 1), out_dtype=t.bfloat16,
+                                     topk=1, shared=False)
+
+    def forward_prefill(self, x, weights=None, indices=None, out_dtype=None, expert_fn=None):
+        """The MoE layer at prefill (a8 numerics) with experts sharded over the group: pairs
+        travel to their owner with their routing weight, come back as bf16 expert outputs
+        and are summed per token in ascending expert order, then the shared expert (run on
+        this rank's tokens) is added -- the same fp32 operations as one GPU."""
+        t = L.torch()
+        xf = x.reshape(-1, x.shape[-1]).to(t.bfloat16).contiguous()
+        T = xf.shape[0]
+        if indices is None:
+            w, idx = self.route(xf)
+        else:
+            w, idx = weights.float().contiguous(), indices.to(t.int32).contiguous()
+        rows, ids, order, sc, rc, recv_w = dispatch(self.dist, xf, idx, self.world, self.epr,
+                                                    self.group, weights=w)
+        if self.track:
+            self.local_active.append(int(t.unique(ids).numel()))
+        y_recv = (expert_fn or self._local_prefill)(rows, ids, recv_w)
+        Y = combine(self.dist, y_recv, order, sc, rc, T, self.topk, self.group)
+        sh = self.local.prefill_a8(xf, out_dtype=t.float32, routed=False)
+        out = ascending_sum(Y, idx, sh)
+        return out.to(out_dtype or (t.float32 if x.dtype == t.float32 else t.bfloat16))
 
     def forward(self, x, expert_fn=None, with_routing=False):
         t = L.torch()

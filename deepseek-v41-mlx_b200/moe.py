@@ -276,11 +276,15 @@ class MoE:
         return (y, weights, indices) if with_routing else y
 
     # -- prefill, upstream a8 numerics ---------------------------------------
-    def prefill_a8(self, x, weights=None, indices=None, out_dtype=None):
+    def prefill_a8(self, x, weights=None, indices=None, out_dtype=None, topk=None,
+                   shared=True, routed=True):
         """The layer as upstream runs it (docs/reference/model.py:889-904): every
         linear in a8 form (act_quant + block-scaled GEMM, bf16 outputs), routed
         experts as grouped GEMMs on tcgen05 block-scaled MMA.  Routing is computed
-        by the router unless ``weights``/``indices`` [T, topk] are given."""
+        by the router unless ``weights``/``indices`` [T, topk] are given.
+        ``routed=False``: the shared expert alone; ``shared=False``: the routed
+        experts alone; ``topk`` overrides the config (1 = every row is one pair, the
+        owner side of expert parallelism)."""
         t = _torch()
         xt = L.cuda_tensor(x, "x")
         shape = xt.shape
@@ -288,26 +292,33 @@ class MoE:
         T = xf.shape[0]
         odt = out_dtype or (t.float32 if xt.dtype == t.float32 else t.bfloat16)
         se = self.shared_experts
-        has_shared = se is not None and se.w1.weight is not None
-        cfg = self._cfg(0 if has_shared else L.MOE_NO_SHARED)
+        has_shared = shared and se is not None and se.w1.weight is not None
+        flags = (0 if has_shared else L.MOE_NO_SHARED) | (0 if routed else L.MOE_SHARED_ONLY)
+        cfg = self._cfg(flags)
+        if topk is not None:
+            cfg.topk = int(topk)
         W = self._weights()
-        given = indices is not None
-        if given:
+        given = indices is not None or not routed
+        if indices is not None:
             idx = L.cuda_tensor(indices, "indices").to(t.int32).reshape(T, -1).contiguous()
             wts = L.cuda_tensor(weights, "weights").float().reshape(T, -1).contiguous()
         packed = self._packed_scales(cfg, W, xf.device)
         need = L.load().dsv41_moe_prefill_workspace_size(C.byref(cfg), T, 1 if given else 0, 1)
         ws = L.workspace(need, xf.device)
         y = t.empty((T, self.dim), dtype=odt, device=xf.device)
+        has_idx = indices is not None
         L.call("dsv41_moe_prefill", C.byref(cfg), C.byref(W), L.ptr(packed), L.ptr(xf), T,
-               L.ptr(wts) if given else None, L.ptr(idx) if given else None, L.dtype_code(odt),
-               L.ptr(y), L.ptr(ws), ws.numel(), L.stream_of(xf))
+               L.ptr(wts) if has_idx else None, L.ptr(idx) if has_idx else None,
+               L.dtype_code(odt), L.ptr(y), L.ptr(ws), ws.numel(), L.stream_of(xf))
         return y.reshape(shape)
 
     def _packed_scales(self, cfg, W, device):
         """Expert scales in the tensor-core layout, rebuilt when a scale tensor changes."""
-        e = self.experts
-        srcs = [L.cuda_tensor(p.scales) for p in (e.gate_proj, e.up_proj, e.down_proj)]
+        e, se = self.experts, self.shared_experts
+        projs = [p for p in (e.gate_proj, e.up_proj, e.down_proj) if p.scales is not None]
+        if se is not None:
+            projs += [p for p in (se.w1, se.w3, se.w2) if p.scales is not None]
+        srcs = [L.cuda_tensor(p.scales) for p in projs]
         key = tuple((s.data_ptr(), s._version, tuple(s.shape)) for s in srcs)
         if getattr(self, "_pack_key", None) != key:
             n = L.load().dsv41_moe_prefill_pack_size(C.byref(cfg))

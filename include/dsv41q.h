@@ -64,6 +64,9 @@ extern "C" {
 #define DSV41_MOE_ROUND_BF16 1
 /* Skip the shared expert (output = routed experts only). */
 #define DSV41_MOE_NO_SHARED 2
+/* dsv41_moe_prefill only: the shared expert alone (no routing, no routed experts) -- the
+ * source-rank half of expert-parallel prefill. */
+#define DSV41_MOE_SHARED_ONLY 4
 
 /* ---- library ------------------------------------------------------------ */
 const char *dsv41_get_last_error(void);

@@ -75,6 +75,76 @@ def _worker(rank, world, port, out_q):
         dist.destroy_process_group()
 
 
+def _prefill_reference(W, x, idx, w, shared):
+    """Per pair bf16(w * (x W_e^T)), summed per token in ascending expert order, + shared."""
+    Y = torch.stack([torch.stack([((x[t] @ W[idx[t, j]].T) * w[t, j]).to(torch.bfloat16)
+                                  for j in range(K)]) for t in range(T)])
+    import importlib
+    ep = importlib.import_module("deepseek_v41_mlx_b200.ep")
+    return ep.ascending_sum(Y, idx, shared)
+
+
+def _prefill_worker(rank, world, port, out_q):
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path.insert(0, here)
+    import conftest  # noqa: F401
+    import importlib
+    ep = importlib.import_module("deepseek_v41_mlx_b200.ep")
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        W, xs, idx, wts = _problem(1)
+        epr = E // world
+        x, ind, w = xs[rank], idx[rank], wts[rank]
+        shared = torch.randn(T, D, generator=torch.Generator().manual_seed(7 + rank))
+
+        def experts(rows, local_ids, recv_w):
+            out = torch.empty(rows.shape[0], D, dtype=torch.bfloat16)
+            for i in range(rows.shape[0]):
+                out[i] = ((rows[i] @ W[rank * epr + int(local_ids[i])].T) * recv_w[i]).to(
+                    torch.bfloat16)
+            return out
+
+        rows, ids, order, sc, rc, recv_w = ep.dispatch(dist, x, ind, world, epr, weights=w)
+        assert recv_w.shape[0] == rows.shape[0]
+        Y = ep.combine(dist, experts(rows, ids, recv_w), order, sc, rc, T, K)
+        got = ep.ascending_sum(Y, ind, shared)
+        want = _prefill_reference(W, x, ind, w, shared)
+        out_q.put((rank, bool(torch.equal(got, want)), float((got - want).abs().max())))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_ep_prefill_weights_travel_gloo(world):
+    """Prefill form: routing weights travel with the pairs, outputs return as bf16 and are
+    summed in ascending expert order -- exactly the single-process result."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_prefill_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, same, err in res:
+        assert same, f"rank {rank}: max err {err}"
+
+
+def test_ascending_sum_order():
+    import importlib
+    import conftest  # noqa: F401
+    ep = importlib.import_module("deepseek_v41_mlx_b200.ep")
+    Y = torch.tensor([[[1.0], [1e8], [-1e8]]])          # fp32 order matters
+    idx = torch.tensor([[7, 2, 5]])                      # ascending: 2, 5, 7
+    got = ep.ascending_sum(Y, idx)
+    assert float(got[0, 0]) == float((torch.tensor(0.0) + 1e8 - 1e8) + 1.0)
+
+
 @pytest.mark.parametrize("world", [2, 3])
 def test_ep_dispatch_combine_gloo(world):
     ctx = mp.get_context("spawn")
