@@ -1134,13 +1134,16 @@ struct PfWs {
   uint8_t *sfx_gu, *sfx_dn;   // activation scale atoms of the row tiles (gate/up, down inputs)
   uint8_t *sfx_sh, *sfh_sh;   // the same for the shared expert's dense row tiles
   uint8_t *packed;            // weight scale atoms when the caller passes none
+  int32_t *ep_ids;            // expert-parallel owner: local expert of each received row
+  float *ep_w;                // ... and its routing weight
   __nv_bfloat16 *yp, *ysh;
   int *chunk_cnt;
   PfPlan plan;
 };
 
 size_t pf_carve(const dsv41_moe_config *cfg, const PfDims &d, bool route, bool shared,
-                bool pack, uint8_t *base, size_t cap, PfWs *ws) {
+                bool pack, uint8_t *base, size_t cap, PfWs *ws, bool quant_x = true,
+                bool ep_owner = false) {
   WsCarve c{base, cap, 0};
   PfWs w;
   memset(&w, 0, sizeof(w));
@@ -1149,8 +1152,14 @@ size_t pf_carve(const dsv41_moe_config *cfg, const PfDims &d, bool route, bool s
     w.idx = c.take<int32_t>(d.P);
     w.rpart = c.take<float>(dsv41_moe_route_workspace_size(d.T, d.D, d.E) / sizeof(float));
   }
-  w.xq = c.take<uint8_t>(d.T * d.D);
-  w.xs = c.take<uint8_t>(d.T * d.D / 32);
+  if (quant_x) {
+    w.xq = c.take<uint8_t>(d.T * d.D);
+    w.xs = c.take<uint8_t>(d.T * d.D / 32);
+  }
+  if (ep_owner) {
+    w.ep_ids = c.take<int32_t>(d.P);
+    w.ep_w = c.take<float>(d.P);
+  }
   w.xpq = c.take<uint8_t>(d.P * d.D);
   w.hq = c.take<uint8_t>(d.P * d.I);
   w.sfx_gu = c.take<uint8_t>(d.cap_rt * (d.D / 128) * 1024);
@@ -1247,6 +1256,91 @@ extern "C" int dsv41_moe_prefill_pack(const dsv41_moe_config *cfg, const dsv41_m
 }
 
 namespace {
+// The routed experts of the prefill: stable sort of the pairs by expert, gather of the fp8
+// rows (xq rows qld bytes apart, their scales xs rows sld bytes apart) into expert order
+// with row-tile scale atoms, grouped gate/up (SwiGLU x weight -> act_quant) and down GEMMs
+// -> ws.yp (bf16, sorted order).  Shared by the one-GPU layer and the expert-parallel owner.
+int pf_routed(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, const uint8_t *packed,
+              const PfDims &d, PfWs &ws, const uint8_t *xq, int64_t qld, const uint8_t *xs,
+              int64_t sld, const int32_t *ri, const float *rw, cudaStream_t st) {
+  int rc = DSV41_OK;
+  // stable sort of the (token, slot) pairs by expert + tile lists
+  {
+    ProfScope prof("pf_plan", st);
+    const size_t sm = size_t(16) * d.E * sizeof(int);
+    if (sm > 48 * 1024) {
+      cudaFuncSetAttribute(k_pf_count, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+      cudaFuncSetAttribute(k_pf_place, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+    }
+    k_pf_count<<<unsigned(d.nchunks), PF_CHUNK, sm, st>>>(ri, d.P, int(d.E), ws.chunk_cnt);
+    DSV41_CHECK_LAUNCH("pf_count");
+    k_pf_scan<<<1, 1024, 0, st>>>(ws.chunk_cnt, int(d.nchunks), int(d.E), int(d.I / 64),
+                                  int(d.D / BS_BM), ws.plan);
+    DSV41_CHECK_LAUNCH("pf_scan");
+    k_pf_place<<<unsigned(d.nchunks), PF_CHUNK, sm, st>>>(ri, rw, d.P, d.k, int(d.E), ws.plan);
+    DSV41_CHECK_LAUNCH("pf_place");
+  }
+  {
+    ProfScope prof("pf_gather", st);
+    k_pf_gather<<<unsigned(ceil_div(d.P * 32, 256)), 256, 0, st>>>(
+        xq, xs, qld, sld, ws.plan.pair_tok, ws.plan.row_tile, d.P, d.D, ws.xpq,
+        ws.sfx_gu);
+    DSV41_CHECK_LAUNCH("pf_gather");
+  }
+  // routed gate/up: SwiGLU * routing weight, bf16, act_quant -> hq/hs
+  {
+    BsMaps maps;
+    memset(&maps, 0, sizeof(maps));
+    rc = bs_wmap(&maps.w, W->w1, BS_W_FP4, d.E * d.I, d.D, 64);
+    if (!rc) rc = bs_wmap(&maps.w2, W->w3, BS_W_FP4, d.E * d.I, d.D, 64);
+    if (!rc) rc = bs_xmaps(maps.x, ws.xpq, d.P, d.D);
+    if (rc) return rc;
+    BsArgs a;
+    memset(&a, 0, sizeof(a));
+    a.nkb = int(d.D / BS_BK);
+    a.a_rows = int(d.I);
+    a.sw = bs_scale(W->s1, d.D / 32, 0, 32, d.E * d.I);
+    a.sw2 = bs_scale(W->s3, d.D / 32, 0, 32, d.E * d.I);
+    a.nkq = int(d.D / 128);
+    a.mtiles = int(d.I / 64);
+    a.sfa_atoms = packed;
+    a.sfb_atoms = ws.sfx_gu;
+    a.pw = ws.plan.pair_w;
+    a.hq = ws.hq;
+    a.hs_atoms = ws.sfx_dn;
+    a.ldh = d.I;
+    a.limit = cfg->swiglu_limit;
+    rc = bs_grouped_launch<BS_W_FP4, BS_EPI_SWIGLU>("pf_gate_up_fp4", "pf_gate_up_fp4_narrow",
+                                                    maps, a, ws.plan, 0, st);
+    if (rc) return rc;
+  }
+  // routed down -> yp (bf16 per pair)
+  {
+    BsMaps maps;
+    memset(&maps, 0, sizeof(maps));
+    rc = bs_wmap(&maps.w, W->w2, BS_W_FP4, d.E * d.D, d.I, 128);
+    if (!rc) rc = bs_xmaps(maps.x, ws.hq, d.P, d.I);
+    if (rc) return rc;
+    BsArgs a;
+    memset(&a, 0, sizeof(a));
+    a.nkb = int(d.I / BS_BK);
+    a.a_rows = int(d.D);
+    a.nkq = int(d.I / 128);
+    a.mtiles = int(d.D / BS_BM);
+    a.sfa_atoms = packed + pf_packed_gu_bytes(cfg);
+    a.sfb_atoms = ws.sfx_dn;
+    a.out = ws.yp;
+    a.ldo = d.D;
+    rc = bs_grouped_launch<BS_W_FP4, BS_EPI_BF16>("pf_down_fp4", "pf_down_fp4_narrow", maps, a,
+                                                  ws.plan, 2, st);
+    if (rc) return rc;
+  }
+
+  return DSV41_OK;
+}
+}  // namespace
+
+namespace {
 // shared-only calls carry no (token, expert) pairs
 PfDims pf_dims_for(const dsv41_moe_config *cfg, int64_t T) {
   PfDims d = pf_dims(cfg, T);
@@ -1318,76 +1412,8 @@ extern "C" int dsv41_moe_prefill(const dsv41_moe_config *cfg, const dsv41_moe_we
     DSV41_CHECK_LAUNCH("pf_act_quant");
   }
   if (routed) {
-    // stable sort of the (token, slot) pairs by expert + tile lists
-    {
-      ProfScope prof("pf_plan", st);
-      const size_t sm = size_t(16) * d.E * sizeof(int);
-      if (sm > 48 * 1024) {
-        cudaFuncSetAttribute(k_pf_count, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
-        cudaFuncSetAttribute(k_pf_place, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
-      }
-      k_pf_count<<<unsigned(d.nchunks), PF_CHUNK, sm, st>>>(ri, d.P, int(d.E), ws.chunk_cnt);
-      DSV41_CHECK_LAUNCH("pf_count");
-      k_pf_scan<<<1, 1024, 0, st>>>(ws.chunk_cnt, int(d.nchunks), int(d.E), int(d.I / 64),
-                                    int(d.D / BS_BM), ws.plan);
-      DSV41_CHECK_LAUNCH("pf_scan");
-      k_pf_place<<<unsigned(d.nchunks), PF_CHUNK, sm, st>>>(ri, rw, d.P, d.k, int(d.E), ws.plan);
-      DSV41_CHECK_LAUNCH("pf_place");
-    }
-    {
-      ProfScope prof("pf_gather", st);
-      k_pf_gather<<<unsigned(ceil_div(d.P * 32, 256)), 256, 0, st>>>(
-          ws.xq, ws.xs, ws.plan.pair_tok, ws.plan.row_tile, d.P, d.D, ws.xpq, ws.sfx_gu);
-      DSV41_CHECK_LAUNCH("pf_gather");
-    }
-    // routed gate/up: SwiGLU * routing weight, bf16, act_quant -> hq/hs
-    {
-      BsMaps maps;
-      memset(&maps, 0, sizeof(maps));
-      rc = bs_wmap(&maps.w, W->w1, BS_W_FP4, d.E * d.I, d.D, 64);
-      if (!rc) rc = bs_wmap(&maps.w2, W->w3, BS_W_FP4, d.E * d.I, d.D, 64);
-      if (!rc) rc = bs_xmaps(maps.x, ws.xpq, d.P, d.D);
-      if (rc) return rc;
-      BsArgs a;
-      memset(&a, 0, sizeof(a));
-      a.nkb = int(d.D / BS_BK);
-      a.a_rows = int(d.I);
-      a.sw = bs_scale(W->s1, d.D / 32, 0, 32, d.E * d.I);
-      a.sw2 = bs_scale(W->s3, d.D / 32, 0, 32, d.E * d.I);
-      a.nkq = int(d.D / 128);
-      a.mtiles = int(d.I / 64);
-      a.sfa_atoms = packed;
-      a.sfb_atoms = ws.sfx_gu;
-      a.pw = ws.plan.pair_w;
-      a.hq = ws.hq;
-      a.hs_atoms = ws.sfx_dn;
-      a.ldh = d.I;
-      a.limit = cfg->swiglu_limit;
-      rc = bs_grouped_launch<BS_W_FP4, BS_EPI_SWIGLU>("pf_gate_up_fp4", "pf_gate_up_fp4_narrow",
-                                                      maps, a, ws.plan, 0, st);
-      if (rc) return rc;
-    }
-    // routed down -> yp (bf16 per pair)
-    {
-      BsMaps maps;
-      memset(&maps, 0, sizeof(maps));
-      rc = bs_wmap(&maps.w, W->w2, BS_W_FP4, d.E * d.D, d.I, 128);
-      if (!rc) rc = bs_xmaps(maps.x, ws.hq, d.P, d.I);
-      if (rc) return rc;
-      BsArgs a;
-      memset(&a, 0, sizeof(a));
-      a.nkb = int(d.I / BS_BK);
-      a.a_rows = int(d.D);
-      a.nkq = int(d.I / 128);
-      a.mtiles = int(d.D / BS_BM);
-      a.sfa_atoms = packed + pf_packed_gu_bytes(cfg);
-      a.sfb_atoms = ws.sfx_dn;
-      a.out = ws.yp;
-      a.ldo = d.D;
-      rc = bs_grouped_launch<BS_W_FP4, BS_EPI_BF16>("pf_down_fp4", "pf_down_fp4_narrow", maps, a,
-                                                    ws.plan, 2, st);
-      if (rc) return rc;
-    }
+    rc = pf_routed(cfg, W, packed, d, ws, ws.xq, d.D, ws.xs, d.D / 32, ri, rw, st);
+    if (rc) return rc;
   }
   if (shared) {
     BsMaps maps;
@@ -1435,6 +1461,169 @@ extern "C" int dsv41_moe_prefill(const dsv41_moe_config *cfg, const dsv41_moe_we
           (__nv_bfloat16 *)y);
     DSV41_CHECK_LAUNCH("pf_combine");
   }
+  return DSV41_OK;
+}
+
+// ======================================================================= expert-parallel prefill
+
+namespace {
+PfDims ep_owner_dims(const dsv41_moe_config *cfg, int64_t R) {
+  dsv41_moe_config c = *cfg;
+  c.topk = 1;
+  return pf_dims(&c, R);
+}
+}  // namespace
+
+extern "C" size_t dsv41_moe_ep_row_bytes(int64_t dim) { return size_t(ep_row_bytes(dim)); }
+
+extern "C" size_t dsv41_moe_ep_pack_workspace_size(const dsv41_moe_config *cfg, int64_t T) {
+  if (!cfg || T <= 0) return 256;
+  const PfDims d = pf_dims(cfg, T);
+  WsCarve c{nullptr, ~size_t(0) >> 1, 0};
+  c.take<uint8_t>(d.T * d.D);
+  c.take<uint8_t>(d.T * d.D / 32);
+  c.take<int>(d.nchunks * d.E);
+  c.take<int>(d.E);
+  c.take<int>(d.E);
+  c.take<int>(d.P);
+  c.take<float>(d.P);
+  c.take<int>(d.P);
+  c.take<int>(d.P);
+  c.take<int>(8);
+  return c.off + 256;
+}
+
+extern "C" int dsv41_moe_ep_pack(const dsv41_moe_config *cfg, const void *x, int64_t T,
+                                 const float *route_weights, const int32_t *route_indices,
+                                 int world, void *send_rows, int64_t *send_counts,
+                                 int32_t *slot_pos, void *workspace, size_t workspace_bytes,
+                                 void *stream) {
+  DSV41_REQUIRE(cfg, DSV41_ERR_BAD_ARG, "NULL config");
+  int rc = route_check(T, cfg->dim, cfg->n_experts, cfg->topk, cfg->score_func);
+  if (rc) return rc;
+  DSV41_REQUIRE(world >= 1 && world <= 1024 && cfg->n_experts % world == 0, DSV41_ERR_BAD_SHAPE,
+                "experts must split evenly over the ranks");
+  DSV41_REQUIRE(cfg->dim % 128 == 0 && cfg->topk <= 8, DSV41_ERR_BAD_SHAPE,
+                "dim must be a multiple of 128, topk <= 8");
+  if (T == 0) return DSV41_OK;
+  DSV41_REQUIRE(x && route_weights && route_indices && send_rows && send_counts && slot_pos,
+                DSV41_ERR_BAD_ARG, "NULL pointer");
+  DSV41_REQUIRE(aligned(x, 16) && aligned(send_rows, 16), DSV41_ERR_MISALIGNED,
+                "x and send_rows must be 16-byte aligned");
+  DSV41_REQUIRE(workspace && workspace_bytes >= dsv41_moe_ep_pack_workspace_size(cfg, T),
+                DSV41_ERR_WORKSPACE, "workspace too small");
+  const PfDims d = pf_dims(cfg, T);
+  WsCarve c{reinterpret_cast<uint8_t *>(workspace), workspace_bytes, 0};
+  uint8_t *xq = c.take<uint8_t>(d.T * d.D);
+  uint8_t *xs = c.take<uint8_t>(d.T * d.D / 32);
+  PfPlan plan;
+  memset(&plan, 0, sizeof(plan));
+  plan.chunk_base = c.take<int>(d.nchunks * d.E);
+  plan.grp_off = c.take<int>(d.E);
+  plan.grp_rt0 = c.take<int>(d.E);
+  plan.pair_tok = c.take<int>(d.P);
+  plan.pair_w = c.take<float>(d.P);
+  plan.pair_exp = c.take<int>(d.P);
+  plan.row_tile = c.take<int>(d.P);
+  plan.ntiles = c.take<int>(4);
+  plan.next_tile = c.take<int>(4);
+  plan.slot_pos = slot_pos;
+  cudaStream_t st = STREAM(stream);
+  ProfScope prof("ep_pack", st);
+  k_act_quant_v8<4><<<unsigned(ceil_div(d.T * (d.D / 8), 256)), 256, 0, st>>>(
+      reinterpret_cast<const __nv_bfloat16 *>(x), d.T, d.D, 1, xq, xs, 1, nullptr, nullptr, 1);
+  DSV41_CHECK_LAUNCH("ep_act_quant");
+  const size_t sm = size_t(16) * d.E * sizeof(int);
+  if (sm > 48 * 1024) {
+    cudaFuncSetAttribute(k_pf_count, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+    cudaFuncSetAttribute(k_pf_place, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+  }
+  k_pf_count<<<unsigned(d.nchunks), PF_CHUNK, sm, st>>>(route_indices, d.P, int(d.E), plan.chunk_base);
+  DSV41_CHECK_LAUNCH("ep_count");
+  k_pf_scan<<<1, 1024, 0, st>>>(plan.chunk_base, int(d.nchunks), int(d.E), 0, 0, plan);
+  DSV41_CHECK_LAUNCH("ep_scan");
+  k_pf_place<<<unsigned(d.nchunks), PF_CHUNK, sm, st>>>(route_indices, route_weights, d.P, d.k,
+                                                       int(d.E), plan);
+  DSV41_CHECK_LAUNCH("ep_place");
+  k_ep_pack<<<unsigned(ceil_div(d.P * 32, 256)), 256, 0, st>>>(
+      xq, xs, plan.pair_tok, plan.pair_exp, plan.pair_w, d.P, d.D, int(d.E / world),
+      reinterpret_cast<uint8_t *>(send_rows));
+  DSV41_CHECK_LAUNCH("ep_pack_rows");
+  k_ep_counts<<<1, 1024, 0, st>>>(plan.grp_off, int(d.E), int(d.E / world), d.P, world, send_counts);
+  DSV41_CHECK_LAUNCH("ep_counts");
+  return DSV41_OK;
+}
+
+extern "C" size_t dsv41_moe_ep_experts_workspace_size(const dsv41_moe_config *cfg, int64_t R,
+                                                      int with_packed) {
+  if (!cfg || R <= 0) return 256;
+  return pf_carve(cfg, ep_owner_dims(cfg, R), false, false, with_packed == 0, nullptr,
+                  ~size_t(0) >> 1, nullptr, false, true);
+}
+
+extern "C" int dsv41_moe_ep_experts(const dsv41_moe_config *cfg, const dsv41_moe_weights *W,
+                                    const void *packed_scales, const void *recv_rows, int64_t R,
+                                    void *y, void *workspace, size_t workspace_bytes,
+                                    void *stream) {
+  int rc = pf_check(cfg, W, R, false, true);
+  if (rc) return rc;
+  if (R == 0) return DSV41_OK;
+  DSV41_REQUIRE(recv_rows && y && aligned(recv_rows, 16) && aligned(y, 16), DSV41_ERR_MISALIGNED,
+                "rows and y must be 16-byte aligned");
+  DSV41_REQUIRE(!packed_scales || aligned(packed_scales, 16), DSV41_ERR_MISALIGNED,
+                "packed scales must be 16-byte aligned");
+  const PfDims d = ep_owner_dims(cfg, R);
+  PfWs ws;
+  const size_t need = pf_carve(cfg, d, false, false, packed_scales == nullptr,
+                               reinterpret_cast<uint8_t *>(workspace), workspace_bytes, &ws,
+                               false, true);
+  DSV41_REQUIRE(workspace && workspace_bytes >= need, DSV41_ERR_WORKSPACE,
+                "workspace too small (%zu < %zu)", workspace_bytes, need);
+  cudaStream_t st = STREAM(stream);
+  const uint8_t *packed = reinterpret_cast<const uint8_t *>(packed_scales);
+  if (!packed) {
+    rc = pf_pack(cfg, W, ws.packed, st);
+    if (rc) return rc;
+    packed = ws.packed;
+  }
+  const uint8_t *rows = reinterpret_cast<const uint8_t *>(recv_rows);
+  const int64_t rb = ep_row_bytes(d.D);
+  k_ep_unpack<<<unsigned(ceil_div(R, 256)), 256, 0, st>>>(rows, R, d.D, ws.ep_ids, ws.ep_w);
+  DSV41_CHECK_LAUNCH("ep_unpack");
+  rc = pf_routed(cfg, W, packed, d, ws, rows, rb, rows + d.D, rb, ws.ep_ids, ws.ep_w, st);
+  if (rc) return rc;
+  // back to arrival order: y[r] = yp[position of r] (one pair per row, bf16)
+  const int64_t n = R * (d.D / 8);
+  ProfScope prof("ep_unsort", st);
+  k_pf_combine<__nv_bfloat16><<<unsigned(ceil_div(n, 256)), 256, 0, st>>>(
+      ws.yp, nullptr, ws.ep_ids, ws.plan.slot_pos, R, 1, d.D, (__nv_bfloat16 *)y);
+  DSV41_CHECK_LAUNCH("ep_unsort");
+  return DSV41_OK;
+}
+
+extern "C" int dsv41_moe_ep_combine(const void *back, const int32_t *slot_pos,
+                                    const int32_t *route_indices, const void *shared, int64_t T,
+                                    int topk, int64_t D, int out_dtype, void *y, void *stream) {
+  DSV41_REQUIRE(T >= 0 && topk >= 1 && topk <= 8 && D > 0 && D % 8 == 0, DSV41_ERR_BAD_SHAPE,
+                "bad shape");
+  DSV41_REQUIRE(out_dtype == DSV41_F32 || out_dtype == DSV41_BF16, DSV41_ERR_BAD_DTYPE,
+                "output must be F32 or BF16");
+  if (T == 0) return DSV41_OK;
+  DSV41_REQUIRE(back && slot_pos && route_indices && y, DSV41_ERR_BAD_ARG, "NULL pointer");
+  DSV41_REQUIRE(aligned(back, 16) && aligned(y, 16) && (!shared || aligned(shared, 16)),
+                DSV41_ERR_MISALIGNED, "buffers must be 16-byte aligned");
+  cudaStream_t st = STREAM(stream);
+  const int64_t n = T * (D / 8);
+  ProfScope prof("ep_combine", st);
+  const __nv_bfloat16 *bk = reinterpret_cast<const __nv_bfloat16 *>(back);
+  const __nv_bfloat16 *sh = reinterpret_cast<const __nv_bfloat16 *>(shared);
+  if (out_dtype == DSV41_F32)
+    k_pf_combine<float><<<unsigned(ceil_div(n, 256)), 256, 0, st>>>(bk, sh, route_indices,
+                                                                    slot_pos, T, topk, D, (float *)y);
+  else
+    k_pf_combine<__nv_bfloat16><<<unsigned(ceil_div(n, 256)), 256, 0, st>>>(
+        bk, sh, route_indices, slot_pos, T, topk, D, (__nv_bfloat16 *)y);
+  DSV41_CHECK_LAUNCH("ep_combine");
   return DSV41_OK;
 }
 

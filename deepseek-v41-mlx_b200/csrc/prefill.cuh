@@ -22,6 +22,7 @@ struct PfPlan {
   int *pair_tok;       // [P] token of sorted pair
   float *pair_w;       // [P] routing weight of sorted pair
   int *slot_pos;       // [T*k] sorted position of pair (t, j)
+  int *pair_exp;       // [P] expert of sorted pair (written when non-null)
   int *row_tile;       // [P] (row tile << 8) | row within the tile, of sorted pair
   int4 *tiles[4];      // {expert, m-tile, first row, rows | row tile << 8}: gate/up wide,
                        // gate/up narrow, down wide, down narrow
@@ -196,6 +197,7 @@ __global__ void __launch_bounds__(PF_CHUNK) k_pf_place(const int32_t *__restrict
     const int pos = plan.grp_off[e] + in_e;
     plan.pair_tok[pos] = int(p / topk);
     plan.pair_w[pos] = w ? w[p] : 1.0f;
+    if (plan.pair_exp) plan.pair_exp[pos] = e;
     plan.slot_pos[p] = pos;
     plan.row_tile[pos] = ((plan.grp_rt0[e] + in_e / PF_TILE_ROWS) << 8) | (in_e % PF_TILE_ROWS);
   }
@@ -203,22 +205,71 @@ __global__ void __launch_bounds__(PF_CHUNK) k_pf_place(const int32_t *__restrict
 
 // dst row r = src row tok[r] for the fp8 codes (K bytes); the row's ue8m0 scales (K/32) go
 // to its row tile's scale atoms (the tcgen05.cp layout the GEMM bulk-copies per K stage).
+// xq / xs rows are qld / sld bytes apart (K and K/32 for act_quant's output; the packed
+// row size for rows received by an expert-parallel owner).
 __global__ void k_pf_gather(const uint8_t *__restrict__ xq, const uint8_t *__restrict__ xs,
-                            const int *__restrict__ tok, const int *__restrict__ row_tile,
-                            int64_t R, int64_t K, uint8_t *__restrict__ dq,
-                            uint8_t *__restrict__ datoms) {
+                            int64_t qld, int64_t sld, const int *__restrict__ tok,
+                            const int *__restrict__ row_tile, int64_t R, int64_t K,
+                            uint8_t *__restrict__ dq, uint8_t *__restrict__ datoms) {
   const int64_t r = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (r >= R) return;
   const int64_t t = tok[r];
-  const uint4 *src = reinterpret_cast<const uint4 *>(xq + t * K);
+  const uint4 *src = reinterpret_cast<const uint4 *>(xq + t * qld);
   uint4 *dst = reinterpret_cast<uint4 *>(dq + r * K);
   for (int64_t i = lane; i < K / 16; i += 32) dst[i] = __ldg(src + i);
   const int rt = row_tile[r] >> 8, lr = row_tile[r] & 0xFF;
-  const uint32_t *ss = reinterpret_cast<const uint32_t *>(xs + t * (K / 32));
+  const uint32_t *ss = reinterpret_cast<const uint32_t *>(xs + t * sld);
   uint8_t *base = datoms + int64_t(rt) * (K / 128) * 1024;
   for (int64_t i = lane; i < K / 128; i += 32)   // 4 scales (one K stage) per word
     *reinterpret_cast<uint32_t *>(base + sf_atom_off(lr, int(4 * i))) = __ldg(ss + i);
+}
+
+// Expert parallelism.  A pair travels as one packed row: the token's fp8 codes (K bytes),
+// their ue8m0 scales (K/32), the owner-local expert id (int32) and the routing weight (f32),
+// padded to 16 bytes.  Source side: rows in expert-sorted order (so grouped by owner).
+__host__ __device__ constexpr int64_t ep_row_bytes(int64_t K) {
+  return (K + K / 32 + 8 + 15) / 16 * 16;
+}
+
+__global__ void k_ep_pack(const uint8_t *__restrict__ xq, const uint8_t *__restrict__ xs,
+                          const int *__restrict__ pair_tok, const int *__restrict__ pair_exp,
+                          const float *__restrict__ pair_w, int64_t P, int64_t K, int epr,
+                          uint8_t *__restrict__ rows) {
+  const int64_t r = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (r >= P) return;
+  const int64_t t = pair_tok[r], rb = ep_row_bytes(K);
+  uint8_t *row = rows + r * rb;
+  const uint4 *src = reinterpret_cast<const uint4 *>(xq + t * K);
+  for (int64_t i = lane; i < K / 16; i += 32) reinterpret_cast<uint4 *>(row)[i] = __ldg(src + i);
+  const uint32_t *ss = reinterpret_cast<const uint32_t *>(xs + t * (K / 32));
+  for (int64_t i = lane; i < K / 128; i += 32)
+    reinterpret_cast<uint32_t *>(row + K)[i] = __ldg(ss + i);
+  if (lane == 0) {
+    reinterpret_cast<int32_t *>(row + K + K / 32)[0] = pair_exp[r] % epr;
+    reinterpret_cast<float *>(row + K + K / 32)[1] = pair_w[r];
+  }
+}
+
+// Pairs per owner rank from the expert offsets: owner r holds experts [r*epr, (r+1)*epr).
+__global__ void k_ep_counts(const int *__restrict__ grp_off, int E, int epr, int64_t P,
+                            int world, int64_t *__restrict__ counts) {
+  const int r = threadIdx.x;
+  if (r >= world) return;
+  const int64_t lo = grp_off[r * epr];
+  const int64_t hi = (r + 1) * epr < E ? grp_off[(r + 1) * epr] : P;
+  counts[r] = hi - lo;
+}
+
+// Owner side: the expert id and routing weight of each received row.
+__global__ void k_ep_unpack(const uint8_t *__restrict__ rows, int64_t R, int64_t K,
+                            int32_t *__restrict__ ids, float *__restrict__ w) {
+  const int64_t r = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (r >= R) return;
+  const uint8_t *tail = rows + r * ep_row_bytes(K) + K + K / 32;
+  ids[r] = reinterpret_cast<const int32_t *>(tail)[0];
+  w[r] = reinterpret_cast<const float *>(tail)[1];
 }
 
 // Weight scales -> tcgen05.cp atoms, once per weight set.  Scale row of weight row r is

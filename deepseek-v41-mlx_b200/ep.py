@@ -224,38 +224,69 @@ class EPMoE:
         return linear_fp8(h, s.w2.weight, s.w2.scales, out_dtype=t.bfloat16).float()
 
     # ---------------------------------------------------------------- prefill (a8)
-    def _local_prefill(self, rows, local_ids, recv_w):
-        """Owner side: each received row is one pair; its routing weight scales h before
-        the down projection (upstream Expert.forward) -> bf16 [R, D]."""
+    def forward_prefill(self, x, weights=None, indices=None, out_dtype=None):
+        """The MoE layer at prefill (a8 numerics) with experts sharded over the group.  Each
+        pair travels once as a packed fp8 row (codes, ue8m0 scales, owner-local expert,
+        routing weight); owners run the grouped GEMMs and return bf16 rows; the source sums
+        them per token in ascending expert order and adds the shared expert, which runs on
+        a side stream during the exchange -- the same fp32 operations as one GPU."""
         t = L.torch()
-        R = rows.shape[0]
-        if R == 0:
-            return t.empty((0, self.local.dim), dtype=t.bfloat16, device=rows.device)
-        return self.local.prefill_a8(rows, weights=recv_w.reshape(R, 1),
-                                     indices=local_ids.reshape(R, 1), out_dtype=t.bfloat16,
-                                     topk=1, shared=False)
-
-    def forward_prefill(self, x, weights=None, indices=None, out_dtype=None, expert_fn=None):
-        """The MoE layer at prefill (a8 numerics) with experts sharded over the group: pairs
-        travel to their owner with their routing weight, come back as bf16 expert outputs
-        and are summed per token in ascending expert order, then the shared expert (run on
-        this rank's tokens) is added -- the same fp32 operations as one GPU."""
-        t = L.torch()
+        lib = L.load()
         xf = x.reshape(-1, x.shape[-1]).to(t.bfloat16).contiguous()
-        T = xf.shape[0]
+        T, D = xf.shape
+        k = self.topk
         if indices is None:
             w, idx = self.route(xf)
         else:
             w, idx = weights.float().contiguous(), indices.to(t.int32).contiguous()
-        rows, ids, order, sc, rc, recv_w = dispatch(self.dist, xf, idx, self.world, self.epr,
-                                                    self.group, weights=w)
+        dev = xf.device
+        main = t.cuda.current_stream(dev)
+        m = self.local
+        lcfg = m._cfg(L.MOE_NO_SHARED)
+        lcfg.topk = 1
+        W = m._weights()
+        packed = m._packed_scales(lcfg, W, dev)   # (re)packed on this stream, before the fork
+        # shared expert on its own stream, overlapping the exchange and the routed experts
+        if not hasattr(self, "_side"):
+            self._side = t.cuda.Stream(device=dev)
+        self._side.wait_stream(main)
+        with t.cuda.stream(self._side):
+            sh = m.prefill_a8(xf, out_dtype=t.bfloat16, routed=False)
+        # pack the pairs by owner
+        gcfg = m._cfg(L.MOE_NO_SHARED)
+        gcfg.n_experts = self.E
+        gcfg.topk = k
+        P = T * k
+        rb = lib.dsv41_moe_ep_row_bytes(D)
+        send = t.empty((P, rb), dtype=t.uint8, device=dev)
+        counts = t.empty((self.world,), dtype=t.int64, device=dev)
+        slot_pos = t.empty((P,), dtype=t.int32, device=dev)
+        ws = L.workspace(lib.dsv41_moe_ep_pack_workspace_size(C.byref(gcfg), T), dev)
+        L.call("dsv41_moe_ep_pack", C.byref(gcfg), L.ptr(xf), T, L.ptr(w), L.ptr(idx),
+               self.world, L.ptr(send), L.ptr(counts), L.ptr(slot_pos), L.ptr(ws), ws.numel(),
+               L.stream_of(xf))
+        recv_counts = exchange_counts(self.dist, counts, self.group)
+        sc, rc = counts.tolist(), recv_counts.tolist()
+        R = int(sum(rc))
+        recv = t.empty((R, rb), dtype=t.uint8, device=dev)
+        self.dist.all_to_all_single(recv, send, rc, sc, group=self.group)
+        # owner: this rank's experts on the received rows
+        y_recv = t.empty((R, D), dtype=t.bfloat16, device=dev)
+        if R:
+            ws2 = L.workspace(lib.dsv41_moe_ep_experts_workspace_size(C.byref(lcfg), R, 1), dev)
+            L.call("dsv41_moe_ep_experts", C.byref(lcfg), C.byref(W), L.ptr(packed), L.ptr(recv),
+                   R, L.ptr(y_recv), L.ptr(ws2), ws2.numel(), L.stream_of(xf))
         if self.track:
-            self.local_active.append(int(t.unique(ids).numel()))
-        y_recv = (expert_fn or self._local_prefill)(rows, ids, recv_w)
-        Y = combine(self.dist, y_recv, order, sc, rc, T, self.topk, self.group)
-        sh = self.local.prefill_a8(xf, out_dtype=t.float32, routed=False)
-        out = ascending_sum(Y, idx, sh)
-        return out.to(out_dtype or (t.float32 if x.dtype == t.float32 else t.bfloat16))
+            self.local_active.append(R)
+        back = t.empty((P, D), dtype=t.bfloat16, device=dev)
+        self.dist.all_to_all_single(back, y_recv, sc, rc, group=self.group)
+        main.wait_stream(self._side)
+        sh.record_stream(main)
+        odt = out_dtype or (t.float32 if x.dtype == t.float32 else t.bfloat16)
+        out = t.empty((T, D), dtype=odt, device=dev)
+        L.call("dsv41_moe_ep_combine", L.ptr(back), L.ptr(slot_pos), L.ptr(idx), L.ptr(sh), T, k,
+               D, L.dtype_code(odt), L.ptr(out), L.stream_of(xf))
+        return out.reshape(tuple(x.shape[:-1]) + (D,))
 
     def forward(self, x, expert_fn=None, with_routing=False):
         t = L.torch()

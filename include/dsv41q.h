@@ -263,6 +263,29 @@ int dsv41_moe_prefill(const dsv41_moe_config *cfg, const dsv41_moe_weights *w,
                       const float *route_weights, const int32_t *route_indices, int out_dtype,
                       void *y, void *workspace, size_t workspace_bytes, void *stream);
 
+/* ---- (e) expert-parallel prefill (replaces upstream's replicate + fp32 all_reduce,
+ * docs/reference/model.py:854-904).  Source rank: dsv41_moe_ep_pack quantizes its tokens
+ * (act_quant), sorts the (token, slot) pairs by global expert (hence by owner rank) and packs
+ * each pair as one row of dsv41_moe_ep_row_bytes(dim) bytes -- fp8 codes, ue8m0 scales,
+ * owner-local expert id (int32), routing weight (f32) -- plus int64 send_counts[world] and
+ * int32 slot_pos[T*topk] (row of pair (t, j)).  The caller exchanges the rows (all-to-all);
+ * the owner runs dsv41_moe_ep_experts (cfg with its local expert count) -> bf16 [R, dim]
+ * in arrival order; after the mirror exchange, dsv41_moe_ep_combine sums each token's rows
+ * in ascending expert order and adds the shared expert (bf16 [T, dim], may be NULL). */
+size_t dsv41_moe_ep_row_bytes(int64_t dim);
+size_t dsv41_moe_ep_pack_workspace_size(const dsv41_moe_config *cfg, int64_t T);
+int dsv41_moe_ep_pack(const dsv41_moe_config *cfg, const void *x, int64_t T,
+                      const float *route_weights, const int32_t *route_indices, int world,
+                      void *send_rows, int64_t *send_counts, int32_t *slot_pos, void *workspace,
+                      size_t workspace_bytes, void *stream);
+size_t dsv41_moe_ep_experts_workspace_size(const dsv41_moe_config *cfg, int64_t R, int with_packed);
+int dsv41_moe_ep_experts(const dsv41_moe_config *cfg, const dsv41_moe_weights *w,
+                         const void *packed_scales, const void *recv_rows, int64_t R, void *y,
+                         void *workspace, size_t workspace_bytes, void *stream);
+int dsv41_moe_ep_combine(const void *back, const int32_t *slot_pos, const int32_t *route_indices,
+                         const void *shared, int64_t T, int topk, int64_t dim, int out_dtype,
+                         void *y, void *stream);
+
 /* ---- a15: engram hasher (deepseek_v41_mlx/engram.py:154-180; upstream
  * docs/reference/engram.py NgramHashState.forward).  input_ids int64 [B, L];
  * token_map int64 [V]; ids_cache int64 [B, max_seq], positions
