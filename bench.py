@@ -427,8 +427,16 @@ def sub_measurements(q, torch, dev, layer, flush, stream, hbm_peak, K, W):
         ms = timed_steps(torch, lambda i: gr[i % copies].replay(), K * 4, W, flush, stream)
         st = sum(ms) / len(ms)
         byts = N * Kd + (N // 32) * (Kd // 32) + M * Kd * 2 + M * N * 2
+        # the same GEMV over the 10 weight copies back to back in one graph (a decode step
+        # runs many such products in a row): time per GEMV
+        chain = graphed(torch, [lambda: [q.linear.linear_fp8(x, ws[c], ss[c]) for c in range(copies)]])[0]
+        msc = timed_steps(torch, lambda i: chain.replay(), K, W, flush, stream)
+        stc = sum(msc) / len(msc) / copies
         out[f"gemv_fp8_block_M{M}"] = {"ms": round(st, 5), "gbs": round(byts / st / 1e6, 1),
-                                       "frac_hbm": round(byts / st / 1e6 / hbm_peak, 4)}
+                                       "frac_hbm": round(byts / st / 1e6 / hbm_peak, 4),
+                                       "chained_ms": round(stc, 5),
+                                       "chained_gbs": round(byts / stc / 1e6, 1),
+                                       "chained_frac_hbm": round(byts / stc / 1e6 / hbm_peak, 4)}
     del ws, ss
     out.update(affine_prefill_measurement(q, torch, dev, flush, stream, K, W))
     # d4: MLX affine [14336, 7168], 4 and 8 bit

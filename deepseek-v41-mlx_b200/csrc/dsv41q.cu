@@ -271,7 +271,9 @@ int qgemv_launch(const char *name, const CUtensorMap &w0, const CUtensorMap &w1,
     sv = sv && aligned(p.aff_s, 2 * NG) && aligned(p.aff_b, 2 * NG);
   pv.svec = sv ? 1 : 0;
   ProfScope prof(name, st);
-  k_qgemv<WF, NMAT, NT><<<grid, QG_THREADS, Cfg::SMEM, st>>>(w0, w1, x8, x16, x32, pv);
+  DSV41_LAUNCH(launch_pdl(k_qgemv<WF, NMAT, NT>, dim3(grid), dim3(QG_THREADS), Cfg::SMEM, st, w0,
+                          w1, x8, x16, x32, pv),
+               "qgemv");
   DSV41_CHECK_LAUNCH("qgemv");
   return DSV41_OK;
 }
@@ -361,9 +363,11 @@ int gemv_common(const void *x, int64_t M, int64_t K, const void *w, int64_t w_ro
   constexpr bool AFF = WF == WF_AFF4 || WF == WF_AFF8;
   const int perm = WF == WF_AFF4 ? 4 : (WF == WF_AFF8 ? 8 : 0);
   { ProfScope prof("qx_prep", st);
-  k_qx_prep<<<unsigned(M), 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16 *>(x), M, K,
-                                          nullptr, nullptr, ws.x16, ws.xscale,
-                                          AFF ? ws.xsum : nullptr, perm); }
+  DSV41_LAUNCH(launch_pdl(k_qx_prep, dim3(unsigned(M)), dim3(256), 0, st,
+                          reinterpret_cast<const __nv_bfloat16 *>(x), M, K,
+                          static_cast<const int32_t *>(nullptr), static_cast<const int *>(nullptr),
+                          ws.x16, ws.xscale, AFF ? ws.xsum : static_cast<float *>(nullptr), perm),
+               "qx_prep"); }
   DSV41_CHECK_LAUNCH("qx_prep");
 
   CUtensorMap wm, xm[3];
@@ -466,15 +470,17 @@ static int route_impl(const void *x, int64_t T, int64_t D, const void *gate_w, c
   const int nks = router_nks(T, D, E);
   const int64_t warps = ceil_div(E, 16) * ceil_div(T, 8) * nks;
   { ProfScope prof("router_scores", st);
-  k_router_scores<<<unsigned(ceil_div(warps * 32, 128)), 128, 0, st>>>(
-      reinterpret_cast<const __nv_bfloat16 *>(x), T, D,
-      reinterpret_cast<const __nv_bfloat16 *>(gate_w), E, nks, partial); }
+  DSV41_LAUNCH(launch_pdl(k_router_scores, dim3(unsigned(ceil_div(warps * 32, 128))), dim3(128), 0,
+                          st, reinterpret_cast<const __nv_bfloat16 *>(x), T, D,
+                          reinterpret_cast<const __nv_bfloat16 *>(gate_w), E, nks, partial),
+               "router_scores"); }
   DSV41_CHECK_LAUNCH("router_scores");
   const int threads = int(ceil_div(E, 32) * 32);
   ProfScope prof("router_select", st);
-  k_router_select<<<unsigned(T), threads, 0, st>>>(partial, nks, T, E, bias, topk, score_func,
-                                                   gate_temp, norm_topk_prob, route_scale, weights,
-                                                   indices);
+  DSV41_LAUNCH(launch_pdl(k_router_select, dim3(unsigned(T)), dim3(threads), 0, st,
+                          static_cast<const float *>(partial), nks, T, E, bias, topk, score_func,
+                          gate_temp, norm_topk_prob, route_scale, weights, indices),
+               "router_select");
   DSV41_CHECK_LAUNCH("router_select");
   return DSV41_OK;
 }
@@ -640,13 +646,18 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
   int rc;
   // plan
   { ProfScope prof("moe_plan", st);
-  k_moe_plan<<<1, 1024, 4 * d.E * sizeof(int), st>>>(idx, T, cfg->topk, d.E, ws.plan); }
+  DSV41_LAUNCH(launch_pdl(k_moe_plan, dim3(1), dim3(1024), 4 * d.E * sizeof(int), st,
+                          static_cast<const int32_t *>(idx), T, cfg->topk, d.E, ws.plan),
+               "moe_plan"); }
   DSV41_CHECK_LAUNCH("moe_plan");
   // activations gathered per pair
   { ProfScope prof("qx_prep_gather", st);
-  k_qx_prep<<<unsigned(d.Pmax), 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16 *>(x), T, d.D,
-                                                ws.plan.pair_tok, ws.plan.counts + 2, ws.x16g,
-                                                ws.xsg, nullptr, 0); }
+  DSV41_LAUNCH(launch_pdl(k_qx_prep, dim3(unsigned(d.Pmax)), dim3(256), 0, st,
+                          reinterpret_cast<const __nv_bfloat16 *>(x), T, d.D,
+                          static_cast<const int32_t *>(ws.plan.pair_tok),
+                          static_cast<const int *>(ws.plan.counts + 2), ws.x16g, ws.xsg,
+                          static_cast<float *>(nullptr), 0),
+               "qx_prep gathered"); }
   DSV41_CHECK_LAUNCH("qx_prep gathered");
 
   CUtensorMap m_w1, m_w3, m_w2, xg[3], hx[3];
@@ -717,8 +728,11 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
   // shared expert (fp8 32x32): gate/up -> Hs -> down -> Ys, on its own stream
   st = st_shared;
   { ProfScope prof("qx_prep", st);
-  k_qx_prep<<<unsigned(T), 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16 *>(x), T, d.D,
-                                          nullptr, nullptr, ws.x16, ws.xs, nullptr, 0); }
+  DSV41_LAUNCH(launch_pdl(k_qx_prep, dim3(unsigned(T)), dim3(256), 0, st,
+                          reinterpret_cast<const __nv_bfloat16 *>(x), T, d.D,
+                          static_cast<const int32_t *>(nullptr), static_cast<const int *>(nullptr),
+                          ws.x16, ws.xs, static_cast<float *>(nullptr), 0),
+               "qx_prep shared"); }
   DSV41_CHECK_LAUNCH("qx_prep shared");
   CUtensorMap m_s1, m_s3, m_s2, xs[3], hs[3];
   if ((rc = weight_map(&m_s1, W->sw1, d.I, d.D))) return rc;
@@ -867,11 +881,18 @@ extern "C" int dsv41_moe_decode(const dsv41_moe_config *cfg, const dsv41_moe_wei
   const int64_t n = T * d.D;
   ProfScope prof("moe_combine", st);
   if (out_dtype == DSV41_F32)
-    k_moe_combine<float><<<grid_for(n), 256, 0, st>>>(ws.Y, shared ? ws.Ys : nullptr, wts, T,
-                                                      cfg->topk, d.D, (float *)y);
+    DSV41_LAUNCH(launch_pdl(k_moe_combine<float>, dim3(grid_for(n)), dim3(256), 0, st,
+                            static_cast<const float *>(ws.Y),
+                            static_cast<const float *>(shared ? ws.Ys : nullptr),
+                            static_cast<const float *>(wts), T, cfg->topk, d.D, (float *)y),
+                 "moe_combine");
   else
-    k_moe_combine<__nv_bfloat16><<<grid_for(n), 256, 0, st>>>(
-        ws.Y, shared ? ws.Ys : nullptr, wts, T, cfg->topk, d.D, (__nv_bfloat16 *)y);
+    DSV41_LAUNCH(launch_pdl(k_moe_combine<__nv_bfloat16>, dim3(grid_for(n)), dim3(256), 0, st,
+                            static_cast<const float *>(ws.Y),
+                            static_cast<const float *>(shared ? ws.Ys : nullptr),
+                            static_cast<const float *>(wts), T, cfg->topk, d.D,
+                            (__nv_bfloat16 *)y),
+                 "moe_combine");
   DSV41_CHECK_LAUNCH("moe_combine");
   return DSV41_OK;
 }

@@ -31,6 +31,8 @@ constexpr int MOE_DN_CHUNK = 4;
 // expert.  Offsets come from block-wide exclusive scans over the experts.
 __global__ void __launch_bounds__(1024) k_moe_plan(const int32_t *__restrict__ indices, int64_t T,
                                                    int topk, int64_t E, MoePlan plan) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ int sh[];
   int *cnt = sh;            // [E]
   int *poff = sh + E;       // [E] padded pair offset
@@ -126,6 +128,8 @@ template <typename TO>
 __global__ void k_moe_combine(const float *__restrict__ Y, const float *__restrict__ Ys,
                               const float *__restrict__ w, int64_t T, int topk, int64_t D,
                               TO *__restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < T * D;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t t = i / D, n = i % D;

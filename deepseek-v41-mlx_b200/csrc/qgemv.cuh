@@ -366,17 +366,20 @@ __global__ void __launch_bounds__(QG_THREADS, QG_MIN_CTAS)
   uint64_t *empty = full + ST;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  const int nchunks = p.chunks ? *p.nchunks_dev : p.nchunks_host;
-  const int nitems = nchunks * p.tiles * p.nsplit;
-
   if (threadIdx.x == 0) {
     for (int s = 0; s < ST; ++s) {
       mbar_init(&full[s], 33);     // TMA tx arrival + one scale-store arrival per producer lane
       mbar_init(&empty[s], QG_CW);
     }
     fence_barrier_init();
+    prefetch_tmap(&wmap0);
+    if (NMAT == 2) prefetch_tmap(&wmap1);
   }
   __syncthreads();
+  pdl_wait();       // the plan, activations and split-K state come from earlier kernels
+  pdl_trigger();
+  const int nchunks = p.chunks ? *p.nchunks_dev : p.nchunks_host;
+  const int nitems = nchunks * p.tiles * p.nsplit;
 
   if (warp == QG_CW) {
     // ---------------------------------------------------------------- producer warp
@@ -719,6 +722,8 @@ __global__ void __launch_bounds__(256) k_qx_prep(const __nv_bfloat16 *__restrict
                                                  const int *__restrict__ nrows_dev,
                                                  __half *__restrict__ xq, float *__restrict__ xscale,
                                                  float *__restrict__ xsum, int perm) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t r = blockIdx.x;
   const int64_t nrows = nrows_dev ? *nrows_dev : M;
   if (r >= nrows) return;

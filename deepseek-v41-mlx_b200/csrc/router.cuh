@@ -20,6 +20,8 @@ __global__ void __launch_bounds__(128) k_router_scores(const __nv_bfloat16 *__re
                                                        const __nv_bfloat16 *__restrict__ w,
                                                        int64_t E, int nks,
                                                        float *__restrict__ partial) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t gw = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int64_t etiles = (E + 15) / 16, ttiles = (T + 7) / 8;
@@ -94,6 +96,8 @@ __global__ void k_router_select(const float *__restrict__ partial, int nks, int6
                                 const float *__restrict__ bias, int topk, int score_func,
                                 float gate_temp, int norm_topk_prob, float route_scale,
                                 float *__restrict__ weights, int32_t *__restrict__ indices) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[32];
   __shared__ ArgMax redm[32];
   __shared__ float sel_score[64];
