@@ -586,6 +586,81 @@ def run_prefill_ep(args):
                           "routing": "Zipf(1.1) per rank (seed 7 + rank)"}))
 
 
+def run_engram_ep(args):
+    """d5 row-sharded over NCCL (upstream ParallelEngramEmbedding layout): rank r holds rows
+    [r * part, (r + 1) * part) of the 96M-row table; every rank hashes the same T tokens (the
+    tensor-parallel setting upstream runs in), the owners send the raw rows each token slice
+    needs (one all-to-all), slices are summed in head order and all-gathered.  Total work is
+    fixed as ranks are added ("strong"); a step is timed with CUDA events per rank, max over
+    ranks."""
+    import datetime
+    import types
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    q = _package()
+    world = int(os.environ["WORLD_SIZE"])
+    rank = int(os.environ["RANK"])
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=180))
+    hbm_peak, _, peak_src = _peaks()
+    eargs = types.SimpleNamespace(engram_layer_ids=(1,), engram_max_ngram_size=4,
+                                  engram_vocab_size=4_000_000, engram_n_heads=8, engram_pad_id=2,
+                                  engram_compressed_vocab_size=99092)
+    primes, _ = q.engram.build_layout(eargs)
+    rows, d = int(primes.sum()), 1024
+    eargs.engram_num_embeddings = (rows,)
+    hasher = q.engram.EngramHasher(eargs, np.arange(99092, dtype=np.int64), device=dev)
+    emb = q.engram.ParallelEngramEmbedding(rows, d, block=d)
+    g = torch.Generator(device=dev).manual_seed(55 + rank)
+    table = torch.empty((emb.part, d), dtype=torch.uint8, device=dev)
+    for r0 in range(0, emb.part, 1 << 20):
+        c = table[r0:r0 + (1 << 20)]
+        c.random_(0, 254, generator=g)
+        c += (c >= 127).to(torch.uint8)
+    emb.weight = table
+    emb.scale = torch.randint(115, 128, (emb.part, 1), dtype=torch.uint8, device=dev, generator=g)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    res = {}
+    gi = torch.Generator(device=dev).manual_seed(77)          # same ids on every rank
+    for T in (1, 8192):
+        start = 100 if T == 1 else 0
+        ids = [torch.randint(0, 99092, (1, T), dtype=torch.int64, device=dev, generator=gi)
+               for _ in range(8)]
+        cache = torch.randint(0, 99092, (1, start + T + 8), dtype=torch.int64, device=dev,
+                              generator=gi)
+
+        def step(i, T=T, start=start):
+            idx = hasher(ids[i % 8], start, cache)
+            return emb.gather_sum(idx.reshape(T, -1))
+
+        for i in range(args.warmup):
+            step(i)
+        torch.cuda.synchronize()
+        dist.barrier()
+        with Clocks(local) as clk:
+            ms = timed_steps(torch, step, args.steps, 0, flush, stream)
+            dist.barrier()
+            torch.cuda.synchronize()
+        st = torch.tensor([statistics.median(ms)], device=dev)
+        dist.all_reduce(st, op=dist.ReduceOp.MAX)
+        step_ms = float(st.item())
+        byts = T * (24 * (d + 1) + 2 * d)
+        res[f"engram_T{T}"] = {"ms": round(step_ms, 4), "tok_s": round(T / (step_ms / 1e3), 1),
+                               "gbs_per_gpu": round(byts / world / (step_ms / 1e3) / 1e9, 1),
+                               "clocks": clk.summary()}
+    dist.barrier()
+    dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps({"metric": "engram hash + gather-sum tok/s (row-sharded table)",
+                          "n_gpus": world, "parallelism": "rows%d" % world, "scaling": "strong",
+                          "table_rows": rows, "rows_per_gpu": emb.part,
+                          "peak_source": peak_src + " hbm_gbs", "hbm_peak": hbm_peak, **res}))
+
+
 # ---------------------------------------------------------------- CPU baseline --
 
 def cpu_baseline(seconds=15.0, sample_experts=None):
@@ -706,6 +781,9 @@ def main():
                                     _peaks(), args.steps, args.warmup, T=args.prefill_tokens)
         r["clocks"] = clk.summary()
         print(json.dumps(r))
+        return
+    if args.engram_only and int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        run_engram_ep(args)
         return
     if args.engram_only:
         import torch

@@ -1694,18 +1694,20 @@ extern "C" int dsv41_engram_gather_rows(const uint8_t *table, const uint8_t *sca
   const unsigned blocks = unsigned(ceil_div(n_idx * 32, 256));
   if (out_dtype == DSV41_F32)
     k_engram_gather_rows<float><<<blocks, 256, 0, STREAM(stream)>>>(
-        table, scale, rows, row_lo, d, block, idx, n_idx, (float *)out);
+        table, scale, rows, row_lo, d, block, d, d / block, idx, n_idx, (float *)out);
   else
     k_engram_gather_rows<__nv_bfloat16><<<blocks, 256, 0, STREAM(stream)>>>(
-        table, scale, rows, row_lo, d, block, idx, n_idx, (__nv_bfloat16 *)out);
+        table, scale, rows, row_lo, d, block, d, d / block, idx, n_idx, (__nv_bfloat16 *)out);
   DSV41_CHECK_LAUNCH("engram_gather_rows");
   return DSV41_OK;
 }
 
-extern "C" int dsv41_engram_gather_sum(const uint8_t *table, const uint8_t *scale, int64_t rows,
-                                       int64_t row_lo, int64_t d, int64_t block,
-                                       const int64_t *idx, int64_t n_tok, int n_per_tok,
-                                       int out_dtype, void *out, void *stream) {
+// fp32 sum of n_per_tok rows per token (engram_gather_sum) over a table with row strides
+// tld / sld bytes: a plain table (d, d / block) or packed rows received from their owners.
+static int engram_sum_launch(const uint8_t *table, const uint8_t *scale, int64_t rows,
+                             int64_t row_lo, int64_t d, int64_t block, int64_t tld, int64_t sld,
+                             const int64_t *idx, int64_t n_tok, int n_per_tok, int out_dtype,
+                             void *out, cudaStream_t st) {
   DSV41_REQUIRE(d == 256 || d == 512 || d == 1024, DSV41_ERR_UNSUPPORTED,
                 "gather_sum supports d in {256, 512, 1024}");
   DSV41_REQUIRE(block >= 8 && block % 8 == 0 && d % block == 0 && rows >= 0 && n_per_tok >= 1,
@@ -1714,16 +1716,15 @@ extern "C" int dsv41_engram_gather_sum(const uint8_t *table, const uint8_t *scal
                 "out_dtype must be F32 or BF16");
   if (n_tok == 0) return DSV41_OK;
   DSV41_REQUIRE(table && scale && idx && out, DSV41_ERR_BAD_ARG, "NULL pointer");
-  DSV41_REQUIRE(aligned(table, 8) && aligned(out, 16), DSV41_ERR_MISALIGNED,
-                "table must be 8-byte and out 16-byte aligned");
-  cudaStream_t st = STREAM(stream);
+  DSV41_REQUIRE(aligned(table, 8) && tld % 8 == 0 && aligned(out, 16), DSV41_ERR_MISALIGNED,
+                "table rows must be 8-byte and out 16-byte aligned");
   ProfScope prof("engram_gather_sum", st);
   // a warp covers 256 columns (d = 256) or 512 (d = 512, 1024)
   const int ch = d == 256 ? 1 : 2;
   const unsigned blocks = unsigned(ceil_div(n_tok * (d / (256 * ch)) * 32, 256));
-#define GS(T, CHV)                                                                           \
-  k_engram_gather_sum<T, CHV><<<blocks, 256, 0, st>>>(table, scale, rows, row_lo, d, block, idx, \
-                                                      n_tok, n_per_tok, (T *)out)
+#define GS(T, CHV)                                                                             \
+  k_engram_gather_sum<T, CHV><<<blocks, 256, 0, st>>>(table, scale, rows, row_lo, d, block, tld, \
+                                                      sld, idx, n_tok, n_per_tok, (T *)out)
   if (out_dtype == DSV41_F32) {
     if (ch == 1) GS(float, 1);
     else GS(float, 2);
@@ -1733,6 +1734,79 @@ extern "C" int dsv41_engram_gather_sum(const uint8_t *table, const uint8_t *scal
   }
 #undef GS
   DSV41_CHECK_LAUNCH("engram_gather_sum");
+  return DSV41_OK;
+}
+
+extern "C" int dsv41_engram_gather_sum(const uint8_t *table, const uint8_t *scale, int64_t rows,
+                                       int64_t row_lo, int64_t d, int64_t block,
+                                       const int64_t *idx, int64_t n_tok, int n_per_tok,
+                                       int out_dtype, void *out, void *stream) {
+  DSV41_REQUIRE(block > 0, DSV41_ERR_BAD_SHAPE, "block must be positive");
+  return engram_sum_launch(table, scale, rows, row_lo, d, block, d, d / block, idx, n_tok,
+                           n_per_tok, out_dtype, out, STREAM(stream));
+}
+
+// ---- row-sharded table: raw rows travel from their owners to the ranks that sum them
+extern "C" size_t dsv41_engram_row_bytes(int64_t d, int64_t block) {
+  if (d <= 0 || block <= 0) return 0;
+  return size_t(align_up(size_t(d + d / block), 16));
+}
+
+extern "C" int dsv41_engram_pack_rows(const uint8_t *table, const uint8_t *scale, int64_t rows,
+                                      int64_t row_lo, int64_t d, int64_t block,
+                                      const int64_t *idx, int64_t n, void *out_rows,
+                                      void *stream) {
+  DSV41_REQUIRE(rows >= 0 && d > 0 && block > 0 && d % block == 0 && d % 16 == 0 && n >= 0,
+                DSV41_ERR_BAD_SHAPE, "need block | d and 16 | d");
+  if (n == 0) return DSV41_OK;
+  DSV41_REQUIRE(table && scale && idx && out_rows, DSV41_ERR_BAD_ARG, "NULL pointer");
+  DSV41_REQUIRE(aligned(table, 16) && aligned(out_rows, 16), DSV41_ERR_MISALIGNED,
+                "table and out_rows must be 16-byte aligned");
+  cudaStream_t st = STREAM(stream);
+  ProfScope prof("engram_pack_rows", st);
+  k_engram_pack_rows<<<unsigned(ceil_div(n * 32, 256)), 256, 0, st>>>(
+      table, scale, rows, row_lo, d, block, idx, n, (uint8_t *)out_rows,
+      int64_t(dsv41_engram_row_bytes(d, block)));
+  DSV41_CHECK_LAUNCH("engram_pack_rows");
+  return DSV41_OK;
+}
+
+extern "C" int dsv41_engram_sum_rows(const void *packed, int64_t n_rows, int64_t d, int64_t block,
+                                     const int64_t *pos, int64_t n_tok, int n_per_tok,
+                                     int out_dtype, void *out, void *stream) {
+  DSV41_REQUIRE(d > 0 && block > 0 && d % block == 0, DSV41_ERR_BAD_SHAPE, "need block | d");
+  const int64_t rb = int64_t(dsv41_engram_row_bytes(d, block));
+  DSV41_REQUIRE(packed || n_rows == 0, DSV41_ERR_BAD_ARG, "NULL packed rows");
+  const uint8_t *p = static_cast<const uint8_t *>(packed);
+  // every position must name a received row or be negative; a NULL buffer with no rows
+  // still needs a valid address for the (never read) scale pointer
+  alignas(16) static const uint8_t dummy[16] = {0};
+  if (!p) p = dummy;
+  return engram_sum_launch(p, p + d, n_rows, 0, d, block, rb, rb, pos, n_tok, n_per_tok,
+                           out_dtype, out, STREAM(stream));
+}
+
+extern "C" int dsv41_engram_dequant_rows(const void *packed, int64_t n_rows, int64_t d,
+                                         int64_t block, const int64_t *pos, int64_t n,
+                                         int out_dtype, void *out, void *stream) {
+  DSV41_REQUIRE(d > 0 && block > 0 && d % block == 0 && d % 8 == 0 && block % 8 == 0 && n >= 0,
+                DSV41_ERR_BAD_SHAPE, "need block | d, 8 | d, 8 | block");
+  DSV41_REQUIRE(out_dtype == DSV41_F32 || out_dtype == DSV41_BF16, DSV41_ERR_BAD_DTYPE,
+                "out_dtype must be F32 or BF16");
+  if (n == 0) return DSV41_OK;
+  DSV41_REQUIRE(pos && out && (packed || n_rows == 0), DSV41_ERR_BAD_ARG, "NULL pointer");
+  const int64_t rb = int64_t(dsv41_engram_row_bytes(d, block));
+  alignas(16) static const uint8_t dummy[16] = {0};
+  const uint8_t *p = packed ? static_cast<const uint8_t *>(packed) : dummy;
+  const unsigned blocks = unsigned(ceil_div(n * 32, 256));
+  cudaStream_t st = STREAM(stream);
+  if (out_dtype == DSV41_F32)
+    k_engram_gather_rows<float><<<blocks, 256, 0, st>>>(p, p + d, n_rows, 0, d, block, rb, rb,
+                                                        pos, n, (float *)out);
+  else
+    k_engram_gather_rows<__nv_bfloat16><<<blocks, 256, 0, st>>>(p, p + d, n_rows, 0, d, block, rb,
+                                                                rb, pos, n, (__nv_bfloat16 *)out);
+  DSV41_CHECK_LAUNCH("engram_dequant_rows");
   return DSV41_OK;
 }
 

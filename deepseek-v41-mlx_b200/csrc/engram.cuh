@@ -103,31 +103,32 @@ template <> __device__ __forceinline__ void store_out<__nv_bfloat16>(__nv_bfloat
   *p = __float2bfloat16_rn(v);
 }
 
-// One warp per gathered row; each lane decodes 8-byte chunks.  d % 8 == 0.
+// One warp per gathered row; each lane decodes 8-byte chunks.  d % 8 == 0.  tld / sld:
+// table / scale row strides in bytes (d and d / block for a plain table; the packed row
+// size for rows received from their owners, whose scale bytes follow the codes).
 template <typename T>
 __global__ void k_engram_gather_rows(const uint8_t *__restrict__ table,
                                      const uint8_t *__restrict__ scale, int64_t rows,
-                                     int64_t row_lo, int64_t d, int64_t block,
-                                     const int64_t *__restrict__ idx, int64_t n_idx,
+                                     int64_t row_lo, int64_t d, int64_t block, int64_t tld,
+                                     int64_t sld, const int64_t *__restrict__ idx, int64_t n_idx,
                                      T *__restrict__ out) {
   const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= n_idx) return;
   const int64_t local = idx[warp] - row_lo;
   const bool in = local >= 0 && local < rows;
-  const int64_t sb = d / block;
   const int blk = int(block);                 // <= d, so 32-bit index arithmetic
   T *o = out + warp * d;
   for (int64_t c = lane * 8; c < d; c += 256) {
     float f[8];
     if (in) {
-      const uint64_t v = __ldg(reinterpret_cast<const unsigned long long *>(table + local * d + c));
+      const uint64_t v = __ldg(reinterpret_cast<const unsigned long long *>(table + local * tld + c));
       uint32_t h[4];
       e4m3x4_to_f16x4(uint32_t(v), h[0], h[1]);
       e4m3x4_to_f16x4(uint32_t(v >> 32), h[2], h[3]);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float sc = e8m0f(scale[local * sb + (int(c) + j) / blk]);
+        const float sc = e8m0f(scale[local * sld + (int(c) + j) / blk]);
         const float2 p = h2f2(h[j >> 1]);
         f[j] = __fmul_rn((j & 1) ? p.y : p.x, sc);
       }
@@ -146,15 +147,14 @@ __global__ void k_engram_gather_rows(const uint8_t *__restrict__ table,
 template <typename T, int CH>
 __global__ void __launch_bounds__(256) k_engram_gather_sum(
     const uint8_t *__restrict__ table, const uint8_t *__restrict__ scale, int64_t rows,
-    int64_t row_lo, int64_t D, int64_t block, const int64_t *__restrict__ idx, int64_t n_tok,
-    int n_per_tok, T *__restrict__ out) {
+    int64_t row_lo, int64_t D, int64_t block, int64_t tld, int64_t sld,
+    const int64_t *__restrict__ idx, int64_t n_tok, int n_per_tok, T *__restrict__ out) {
   const int64_t gw = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int wpt = int(D / (256 * CH));
   const int64_t tok = gw / wpt;
   if (tok >= n_tok) return;
   const int64_t col0 = (gw % wpt) * 256 * CH;
-  const int64_t sb = D / block;
   // the scale column of each of this lane's chunks (8 | block keeps a chunk in one block)
   int soff[CH];
 #pragma unroll
@@ -174,7 +174,7 @@ __global__ void __launch_bounds__(256) k_engram_gather_sum(
 #pragma unroll
       for (int c = 0; c < CH; ++c)
         v[u][c] = in[u] ? __ldcs(reinterpret_cast<const unsigned long long *>(
-                              table + local * D + col0 + c * 256 + lane * 8))
+                              table + local * tld + col0 + c * 256 + lane * 8))
                         : 0ull;
     }
 #pragma unroll
@@ -183,7 +183,7 @@ __global__ void __launch_bounds__(256) k_engram_gather_sum(
       const int64_t local = ti[h + u] - row_lo;
 #pragma unroll
       for (int c = 0; c < CH; ++c) {
-        const float s = e8m0f(scale[local * sb + soff[c]]);
+        const float s = e8m0f(scale[local * sld + soff[c]]);
         uint32_t hq[4];
         e4m3x4_to_f16x4(uint32_t(v[u][c]), hq[0], hq[1]);
         e4m3x4_to_f16x4(uint32_t(v[u][c] >> 32), hq[2], hq[3]);
@@ -198,6 +198,29 @@ __global__ void __launch_bounds__(256) k_engram_gather_sum(
   T *o = out + tok * D + col0;
 #pragma unroll
   for (int c = 0; c < CH; ++c) store8(o + c * 256 + lane * 8, acc + c * 8);
+}
+
+// Row-sharded tables: the owner of rows [row_lo, row_lo + rows) copies the raw rows
+// idx[i] (global ids, all owned) into packed rows of rb bytes -- D code bytes, then the
+// D / block scale bytes, zero padding to rb (a multiple of 16) -- for the ranks whose
+// tokens need them.  One warp per row, 16-byte copies; rows not owned are zero.
+__global__ void __launch_bounds__(256) k_engram_pack_rows(
+    const uint8_t *__restrict__ table, const uint8_t *__restrict__ scale, int64_t rows,
+    int64_t row_lo, int64_t D, int64_t block, const int64_t *__restrict__ idx, int64_t n,
+    uint8_t *__restrict__ out, int64_t rb) {
+  const int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (i >= n) return;
+  const int64_t local = idx[i] - row_lo;
+  const bool in = local >= 0 && local < rows;
+  uint8_t *o = out + i * rb;
+  for (int64_t c = lane * 16; c < D; c += 512) {
+    const uint4 v = in ? __ldcs(reinterpret_cast<const uint4 *>(table + local * D + c))
+                       : make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<uint4 *>(o + c) = v;
+  }
+  const int64_t sb = D / block;
+  for (int64_t b = lane; b < rb - D; b += 32) o[D + b] = (in && b < sb) ? scale[local * sb + b] : 0;
 }
 
 }  // namespace dsv41

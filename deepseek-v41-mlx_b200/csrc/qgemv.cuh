@@ -605,22 +605,31 @@ __global__ void __launch_bounds__(QG_THREADS, QG_MIN_CTAS)
     }
 
     // ---------------------------------------------------------------- split-K fixup
+    // Each split stores its fragment as float4s ([tile][split][thread][FRAG]); after the
+    // CTA barrier one thread's acq_rel ticket both publishes the CTA's stores (release is
+    // cumulative over the barrier) and, for the last split, acquires every other split's.
+    // The last split then sums the fragments in split order, all of a split's vectors in
+    // flight at once -- the same fp32 additions, in the same order, for every launch.
     if (p.nsplit > 1) {
       const int tile_id = chunk * p.tiles + tile;
       const int ctid = threadIdx.x;                        // 0 .. 32*QG_CW-1
       constexpr int CT = 32 * QG_CW;
-      float *mine = p.partial + ((int64_t)tile_id * p.nsplit + split) * (CT * C::FRAG);
+      constexpr int NV = NMAT * NT;                        // float4s per thread
+      float4 *base = reinterpret_cast<float4 *>(p.partial) + (int64_t)tile_id * p.nsplit * (CT * NV);
+      float4 *mine = base + (int64_t)split * (CT * NV) + ctid * NV;
 #pragma unroll
       for (int m = 0; m < NMAT; ++m)
 #pragma unroll
         for (int n = 0; n < NT; ++n)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) __stcg(mine + ((m * NT + n) * 4 + i) * CT + ctid, acc[m][n][i]);
-      __threadfence();
+          __stcg(mine + m * NT + n, make_float4(acc[m][n][0], acc[m][n][1], acc[m][n][2], acc[m][n][3]));
       asm volatile("bar.sync 1, %0;" ::"n"(CT) : "memory");
       __shared__ int s_last;
       if (ctid == 0) {
-        const int prev = atomicAdd(&p.counters[tile_id], 1);
+        int prev;
+        asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;"
+                     : "=r"(prev)
+                     : "l"(p.counters + tile_id)
+                     : "memory");
         s_last = (prev == p.nsplit - 1);
         if (s_last) p.counters[tile_id] = 0;               // ready for the next call
       }
@@ -628,20 +637,32 @@ __global__ void __launch_bounds__(QG_THREADS, QG_MIN_CTAS)
       const int last = s_last;
       asm volatile("bar.sync 1, %0;" ::"n"(CT) : "memory");  // s_last reused next item
       if (!last) continue;
-      __threadfence();
+      float4 v[NV];
+#pragma unroll
+      for (int k = 0; k < NV; ++k) v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 *src = base + ctid * NV;
+#pragma unroll 4
+      for (int sp = 0; sp < p.nsplit; ++sp) {
+        float4 t[NV];
+#pragma unroll
+        for (int k = 0; k < NV; ++k) t[k] = __ldcg(src + (int64_t)sp * (CT * NV) + k);
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+          v[k].x += t[k].x;
+          v[k].y += t[k].y;
+          v[k].z += t[k].z;
+          v[k].w += t[k].w;
+        }
+      }
 #pragma unroll
       for (int m = 0; m < NMAT; ++m)
 #pragma unroll
-        for (int n = 0; n < NT; ++n)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float *src = p.partial + (int64_t)tile_id * p.nsplit * (CT * C::FRAG) +
-                               ((m * NT + n) * 4 + i) * CT + ctid;
-            float v = 0.0f;
-#pragma unroll 8
-            for (int sp = 0; sp < p.nsplit; ++sp) v += __ldcg(src + (int64_t)sp * (CT * C::FRAG));
-            acc[m][n][i] = v;
-          }
+        for (int n = 0; n < NT; ++n) {
+          acc[m][n][0] = v[m * NT + n].x;
+          acc[m][n][1] = v[m * NT + n].y;
+          acc[m][n][2] = v[m * NT + n].z;
+          acc[m][n][3] = v[m * NT + n].w;
+        }
     }
 
     // ---------------------------------------------------------------- epilogue

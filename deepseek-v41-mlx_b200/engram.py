@@ -12,6 +12,11 @@
   outside [row_lo, row_lo + rows) give zero rows.
 * ``QuantizedEngramEmbedding`` is the MLX affine table (engram.py:206-223).
 * ``gather_sum`` is the summed form used by the benchmark configuration.
+* ``ParallelEngramEmbedding(num, dim, block)`` is upstream's row-sharded table
+  (docs/reference/model.py:296-325) over a torch.distributed process group: each
+  rank keeps ceil(num / world) rows, the raw rows a token needs travel from their
+  owners to the rank that handles the token (one all-to-all), and the results are
+  all-gathered -- bit-identical to one GPU, unlike a sum of partial sums.
 """
 
 from __future__ import annotations
@@ -171,4 +176,133 @@ class QuantizedEngramEmbedding:
         s = L.cuda_tensor(self.scales).index_select(0, idx)
         b = L.cuda_tensor(self.biases).index_select(0, idx)
         out = dequantize_affine(w, s, b, self.group_size, self.bits, t.float32)
+        return out.reshape(tuple(indices.shape) + (self.dim,))
+
+
+class _CudaRowOps:
+    """The device half of ParallelEngramEmbedding: libdsv41q's row pack / sum / dequant."""
+
+    def row_bytes(self, d, block):
+        return int(L.load().dsv41_engram_row_bytes(d, block))
+
+    def pack_rows(self, weight, scale, row_lo, d, block, ids):
+        t = L.torch()
+        rb = self.row_bytes(d, block)
+        out = t.empty((ids.numel(), rb), dtype=t.uint8, device=ids.device)
+        L.call("dsv41_engram_pack_rows", L.ptr(weight), L.ptr(scale), weight.shape[0], row_lo, d,
+               block, L.ptr(ids), ids.numel(), L.ptr(out), L.stream_of(ids))
+        return out
+
+    def sum_rows(self, recv, pos, d, block, out):
+        n_tok, n = pos.shape
+        L.call("dsv41_engram_sum_rows", L.ptr(recv) if recv.numel() else None, recv.shape[0], d,
+               block, L.ptr(pos), n_tok, n, L.dtype_code(out.dtype), L.ptr(out), L.stream_of(out))
+
+    def dequant_rows(self, recv, pos, d, block, out):
+        L.call("dsv41_engram_dequant_rows", L.ptr(recv) if recv.numel() else None, recv.shape[0],
+               d, block, L.ptr(pos), pos.numel(), L.dtype_code(out.dtype), L.ptr(out),
+               L.stream_of(out))
+
+
+class ParallelEngramEmbedding:
+    """Upstream ParallelEngramEmbedding (docs/reference/model.py:296-325) over a process group.
+
+    Rank r holds rows [r * part, (r + 1) * part) of the table, part = ceil(num / world)
+    (``weight`` u8 e4m3 [part, dim], ``scale`` u8 ue8m0 [part, dim / block]).  The indices
+    are the same on every rank (the hasher runs everywhere), so every rank can tell, with
+    no request message, which of its rows each token needs.  Rank r handles tokens
+    [r * per, (r + 1) * per): the owners pack the raw rows those tokens need, one
+    all_to_all_single delivers them, rank r dequantizes (``__call__``) or sums them per
+    token in head order (``gather_sum``), and all_gather_into_tensor gives every rank the
+    whole result.  Upstream's masked lookup + all_reduce gives the same rows; this moves
+    the fp8 rows once instead of reducing bf16 rows over all ranks.
+    """
+
+    def __init__(self, num_embeddings: int, dim: int, block: int = 32, rank=None, world=None,
+                 group=None, ops=None):
+        import torch.distributed as dist
+        self.dist = dist
+        self.group = group
+        init = dist.is_available() and dist.is_initialized()
+        self.world = world if world is not None else (dist.get_world_size(group) if init else 1)
+        self.rank = rank if rank is not None else (dist.get_rank(group) if init else 0)
+        self.num_embeddings, self.dim, self.block = num_embeddings, dim, block
+        self.part = -(-num_embeddings // self.world)
+        self.row_lo = self.rank * self.part
+        self.weight = None
+        self.scale = None
+        self.ops = ops if ops is not None else _CudaRowOps()
+
+    def plan(self, idx2):
+        """idx2 int64 [T, H] (same on every rank) -> the exchange for this rank.
+
+        send_ids: global row ids this rank owns, in (token, head) order, grouped by the
+        handling rank; recv_pos[(t - t0) * H + h]: row of (t, h) in the receive buffer
+        (grouped by owner rank, (token, head) order inside a group)."""
+        t = L.torch()
+        T, H = idx2.shape
+        ws, r = self.world, self.rank
+        dev = idx2.device
+        per = max(1, -(-T // ws))
+        owner = t.div(idx2.reshape(-1), self.part, rounding_mode="floor").clamp_(0, ws - 1)
+        tok = t.arange(T, device=dev).repeat_interleave(H)
+        mine = (owner == r).nonzero(as_tuple=True)[0]
+        send_ids = idx2.reshape(-1)[mine].contiguous()
+        send_counts = t.bincount(t.div(tok[mine], per, rounding_mode="floor"), minlength=ws)
+        t0 = min(T, r * per)
+        t1 = min(T, t0 + per)
+        my = owner[t0 * H:t1 * H]
+        order = t.sort(my, stable=True).indices
+        recv_pos = t.empty_like(order)
+        recv_pos[order] = t.arange(order.numel(), device=dev)
+        recv_counts = t.bincount(my, minlength=ws)
+        counts = t.cat([send_counts, recv_counts]).tolist()          # one host sync
+        return {"T": T, "H": H, "per": per, "t0": t0, "t1": t1, "send_ids": send_ids,
+                "send_counts": counts[:ws], "recv_counts": counts[ws:],
+                "recv_pos": recv_pos.reshape(t1 - t0, H)}
+
+    def _exchange(self, idx2):
+        t = L.torch()
+        plan = self.plan(idx2)
+        rb = self.ops.row_bytes(self.dim, self.block)
+        send = self.ops.pack_rows(self.weight, self.scale, self.row_lo, self.dim, self.block,
+                                  plan["send_ids"])
+        recv = t.empty((sum(plan["recv_counts"]), rb), dtype=t.uint8, device=idx2.device)
+        self.dist.all_to_all_single(recv.reshape(-1), send.reshape(-1),
+                                    [c * rb for c in plan["recv_counts"]],
+                                    [c * rb for c in plan["send_counts"]], group=self.group)
+        return plan, recv
+
+    def _gather_all(self, part_out, n_total):
+        t = L.torch()
+        full = t.empty((part_out.shape[0] * self.world,) + tuple(part_out.shape[1:]),
+                       dtype=part_out.dtype, device=part_out.device)
+        self.dist.all_gather_into_tensor(full, part_out, group=self.group)
+        return full[:n_total]
+
+    def gather_sum(self, indices, out_dtype=None):
+        """indices [..., H] -> [..., dim]: each token's H rows summed in head order (fp32)."""
+        t = L.torch()
+        idx2 = indices.reshape(-1, indices.shape[-1]).to(t.int64)
+        plan, recv = self._exchange(idx2)
+        odt = out_dtype or t.bfloat16
+        part_out = t.zeros((plan["per"], self.dim), dtype=odt, device=idx2.device)
+        n_my = plan["t1"] - plan["t0"]
+        if n_my:
+            self.ops.sum_rows(recv, plan["recv_pos"], self.dim, self.block, part_out[:n_my])
+        out = self._gather_all(part_out, plan["T"])
+        return out.reshape(tuple(indices.shape[:-1]) + (self.dim,))
+
+    def __call__(self, indices, out_dtype=None):
+        """indices [...] -> [..., dim] rows (bf16 as upstream returns them)."""
+        t = L.torch()
+        idx2 = indices.reshape(-1, 1).to(t.int64)
+        plan, recv = self._exchange(idx2)
+        odt = out_dtype or t.bfloat16
+        part_out = t.zeros((plan["per"], self.dim), dtype=odt, device=idx2.device)
+        n_my = plan["t1"] - plan["t0"]
+        if n_my:
+            self.ops.dequant_rows(recv, plan["recv_pos"].reshape(-1), self.dim, self.block,
+                                  part_out[:n_my])
+        out = self._gather_all(part_out, plan["T"])
         return out.reshape(tuple(indices.shape) + (self.dim,))

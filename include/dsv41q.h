@@ -315,6 +315,27 @@ int dsv41_engram_gather_sum(const uint8_t *table, const uint8_t *scale, int64_t 
                             int64_t n_tok, int n_per_tok, int out_dtype, void *out,
                             void *stream);
 
+/* ---- (e) row-sharded engram table (replaces upstream ParallelEngramEmbedding.forward,
+ * docs/reference/model.py:312-325: zero-masked local lookup + all_reduce of the rows).
+ * Rank r owns rows [r*part, (r+1)*part) of the table; the hashes are known on every rank.
+ * Each rank sums the rows of one slice of the tokens: the owners copy the raw rows that
+ * slice needs (dsv41_engram_pack_rows, packed rows of dsv41_engram_row_bytes(d, block)
+ * bytes: d e4m3 codes, d/block ue8m0 bytes, zero padding to 16), the caller exchanges
+ * them (all-to-all), and the slice's rank sums them per token in head order
+ * (dsv41_engram_sum_rows, = dsv41_engram_gather_sum on the received rows; pos[t*n + h] is
+ * the received row of (t, h), negative = skipped) or dequantizes them one by one
+ * (dsv41_engram_dequant_rows, = dsv41_engram_gather_rows).  Bit-identical to one GPU. */
+size_t dsv41_engram_row_bytes(int64_t d, int64_t block);
+int dsv41_engram_pack_rows(const uint8_t *table, const uint8_t *scale, int64_t rows,
+                           int64_t row_lo, int64_t d, int64_t block, const int64_t *idx, int64_t n,
+                           void *out_rows, void *stream);
+int dsv41_engram_sum_rows(const void *packed, int64_t n_rows, int64_t d, int64_t block,
+                          const int64_t *pos, int64_t n_tok, int n_per_tok, int out_dtype,
+                          void *out, void *stream);
+int dsv41_engram_dequant_rows(const void *packed, int64_t n_rows, int64_t d, int64_t block,
+                              const int64_t *pos, int64_t n, int out_dtype, void *out,
+                              void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -127,3 +127,44 @@ def test_gather_sharded_sums_to_full(cuda):
         e.weight, e.scale = _d(table[r * part:(r + 1) * part]), _d(scale[r * part:(r + 1) * part])
         acc += e(idx)
     assert torch.equal(acc, ref)
+
+
+@pytest.mark.parametrize("d,block", [(1024, 32), (256, 1024 // 4), (512, 64)])
+def test_packed_rows_match_table_lookup(cuda, d, block):
+    """The row-sharded exchange's device half: rows packed by their owners (in any order),
+    then summed / dequantized through positions, equal the plain table lookups bit for bit."""
+    rng = np.random.default_rng(d + 3 * block)
+    rows, T, H = 3000, 41, 24
+    table = rng.integers(0, 256, size=(rows, d), dtype=np.uint8)
+    table[(table & 0x7F) == 0x7F] = 0
+    scale = rng.integers(112, 130, size=(rows, d // block), dtype=np.uint8)
+    idx = _d(rng.integers(0, rows, size=(T, H)))
+    emb = q.engram.EngramEmbedding(rows, d, block)
+    emb.weight, emb.scale = _d(table), _d(scale)
+    ops = q.engram._CudaRowOps()
+    perm = torch.from_numpy(rng.permutation(T * H)).cuda()
+    ids = idx.reshape(-1)[perm].contiguous()                  # rows in shuffled order
+    packed = ops.pack_rows(emb.weight, emb.scale, 0, d, block, ids)
+    assert packed.shape == (T * H, ops.row_bytes(d, block))
+    pos = torch.empty_like(perm)
+    pos[perm] = torch.arange(T * H, device="cuda")            # (t, h) -> packed row
+    for dt in (torch.float32, torch.bfloat16):
+        out = torch.empty(T, d, dtype=dt, device="cuda")
+        ops.sum_rows(packed, pos.reshape(T, H), d, block, out)
+        assert torch.equal(out, emb.gather_sum(idx, dt))
+        rows_out = torch.empty(T * H, d, dtype=dt, device="cuda")
+        ops.dequant_rows(packed, pos, d, block, rows_out)
+        assert torch.equal(rows_out, emb(idx, dt).reshape(T * H, d))
+
+
+def test_packed_rows_off_shard_are_zero(cuda):
+    """An owner asked for a row it does not hold packs zeros (codes and scale)."""
+    rng = np.random.default_rng(5)
+    rows, d, block = 100, 256, 32
+    table = _d(rng.integers(1, 126, size=(rows, d), dtype=np.uint8))
+    scale = _d(rng.integers(115, 128, size=(rows, d // block), dtype=np.uint8))
+    ops = q.engram._CudaRowOps()
+    ids = torch.tensor([1000, 1001, 1099, 1100, 999], dtype=torch.int64, device="cuda")
+    packed = ops.pack_rows(table, scale, 1000, d, block, ids)
+    assert torch.equal(packed[0, :d], table[0]) and torch.equal(packed[2, d:d + d // block], scale[99])
+    assert int(packed[3].abs().sum()) == 0 and int(packed[4].abs().sum()) == 0
