@@ -22,7 +22,7 @@ OK, BAD_SHAPE, BAD_DTYPE, MISALIGNED, CUDA_ERR, NCCL_ERR, TIMEOUT, BAD_ARG, UNSU
     WORKSPACE = range(10)
 F32, BF16, F16, U8 = 0, 1, 2, 3
 SCORE_FUNCS = {"sqrtsoftplus": 0, "sigmoid": 1, "softmax": 2}
-MOE_ROUND_BF16, MOE_NO_SHARED, MOE_SHARED_ONLY = 1, 2, 4
+MOE_ROUND_BF16, MOE_NO_SHARED, MOE_SHARED_ONLY, MOE_PACKED_SCALES = 1, 2, 4, 8
 
 
 class DSV41Error(RuntimeError):
@@ -73,6 +73,8 @@ PROTOTYPES = {
     "dsv41_moe_route": (_I, [_P, _I64, _I64, _P, _P, _I64, _I, _I, _F, _I, _F, _P, _P, _P, _SZ,
                              _P]),
     "dsv41_moe_decode_workspace_size": (_SZ, [C.POINTER(MoeConfig), _I64]),
+    "dsv41_moe_decode_pack_size": (_SZ, [C.POINTER(MoeConfig)]),
+    "dsv41_moe_decode_pack": (_I, [C.POINTER(MoeConfig), C.POINTER(MoeWeights), _P, _SZ, _P]),
     "dsv41_moe_experts": (_I, [C.POINTER(MoeConfig), C.POINTER(MoeWeights), _P, _I64, _P, _P, _P,
                                _SZ, _P]),
     "dsv41_moe_decode": (_I, [C.POINTER(MoeConfig), C.POINTER(MoeWeights), _P, _I64, _I, _P, _P,

@@ -606,6 +606,12 @@ int moe_check(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, int64_t T
   if (T == 0) return DSV41_OK;
   DSV41_REQUIRE(W->w1 && W->s1 && W->w3 && W->s3 && W->w2 && W->s2, DSV41_ERR_BAD_ARG,
                 "NULL expert pointer");
+  if (cfg->flags & DSV41_MOE_PACKED_SCALES) {
+    DSV41_REQUIRE(cfg->dim % 256 == 0 && cfg->inter % 256 == 0, DSV41_ERR_BAD_SHAPE,
+                  "decode-packed scales need dim and inter to be multiples of 256");
+    DSV41_REQUIRE(aligned(W->s1, 16) && aligned(W->s3, 16) && aligned(W->s2, 16),
+                  DSV41_ERR_MISALIGNED, "decode-packed scales must be 16-byte aligned");
+  }
   DSV41_REQUIRE(!shared || (W->sw1 && W->ss1 && W->sw3 && W->ss3 && W->sw2 && W->ss2),
                 DSV41_ERR_BAD_ARG, "NULL shared-expert pointer");
   return DSV41_OK;
@@ -689,6 +695,7 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
     p.round_h = 0;
     p.partial = ws.part_gu;
     p.counters = ws.cnt_gu;
+    p.spack = (cfg->flags & DSV41_MOE_PACKED_SCALES) ? 1 : 0;
     if (p.nsplit > 1) {
       cudaError_t e = cudaMemsetAsync(ws.cnt_gu, 0, sizeof(int) * d.Cmax * d.tiles_gu, st);
       if (e != cudaSuccess) return cuda_status(e, "memset");
@@ -716,6 +723,7 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
     p.pair_row = ws.plan.pair_row;
     p.partial = ws.part_dn;
     p.counters = ws.cnt_dn;
+    p.spack = (cfg->flags & DSV41_MOE_PACKED_SCALES) ? 1 : 0;
     if (p.nsplit > 1) {
       cudaError_t e = cudaMemsetAsync(ws.cnt_dn, 0, sizeof(int) * d.Cmax * d.tiles_dn, st);
       if (e != cudaSuccess) return cuda_status(e, "memset");
@@ -1216,6 +1224,8 @@ size_t pf_carve(const dsv41_moe_config *cfg, const PfDims &d, bool route, bool s
 int pf_check(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, int64_t T, bool shared,
              bool routed = true) {
   DSV41_REQUIRE(cfg && W, DSV41_ERR_BAD_ARG, "NULL config/weights");
+  DSV41_REQUIRE((cfg->flags & DSV41_MOE_PACKED_SCALES) == 0, DSV41_ERR_BAD_ARG,
+                "prefill reads the expert scales in their release layout (no decode-packed scales)");
   int rc = route_check(T, cfg->dim, cfg->n_experts, cfg->topk, cfg->score_func);
   if (rc) return rc;
   DSV41_REQUIRE(cfg->dim % 128 == 0 && cfg->inter % 128 == 0, DSV41_ERR_BAD_SHAPE,
@@ -1262,6 +1272,40 @@ int pf_pack(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, uint8_t *ou
   return DSV41_OK;
 }
 }  // namespace
+
+// ---- decode-packed expert scales (DSV41_MOE_PACKED_SCALES): s1, s3, s2 rearranged by
+// k_pack_decode_sf, stored back to back [s1 | s3 | s2] with the release sizes.
+extern "C" size_t dsv41_moe_decode_pack_size(const dsv41_moe_config *cfg) {
+  if (!cfg || cfg->dim <= 0 || cfg->inter <= 0 || cfg->n_experts <= 0) return 0;
+  const size_t gu = size_t(cfg->n_experts) * cfg->inter * (cfg->dim / 32);
+  const size_t dn = size_t(cfg->n_experts) * cfg->dim * (cfg->inter / 32);
+  return 2 * gu + dn;
+}
+
+extern "C" int dsv41_moe_decode_pack(const dsv41_moe_config *cfg, const dsv41_moe_weights *W,
+                                     void *packed, size_t packed_bytes, void *stream) {
+  DSV41_REQUIRE(cfg && W, DSV41_ERR_BAD_ARG, "NULL config/weights");
+  DSV41_REQUIRE(cfg->dim > 0 && cfg->inter > 0 && cfg->n_experts > 0 && cfg->dim % 256 == 0 &&
+                    cfg->inter % 256 == 0,
+                DSV41_ERR_BAD_SHAPE, "decode-packed scales need dim and inter multiples of 256");
+  DSV41_REQUIRE(W->s1 && W->s3 && W->s2 && packed, DSV41_ERR_BAD_ARG, "NULL pointer");
+  DSV41_REQUIRE(packed_bytes >= dsv41_moe_decode_pack_size(cfg), DSV41_ERR_BAD_ARG,
+                "packed buffer too small (%zu < %zu)", packed_bytes, dsv41_moe_decode_pack_size(cfg));
+  DSV41_REQUIRE(aligned(packed, 16) && aligned(W->s1, 8) && aligned(W->s3, 8) && aligned(W->s2, 8),
+                DSV41_ERR_MISALIGNED, "packed must be 16-byte and scales 8-byte aligned");
+  cudaStream_t st = STREAM(stream);
+  const int64_t E = cfg->n_experts, D = cfg->dim, I = cfg->inter;
+  uint8_t *o = static_cast<uint8_t *>(packed);
+  const size_t gu = size_t(E) * I * (D / 32);
+  const struct { const uint8_t *src; int64_t rows, G; uint8_t *dst; } jobs[3] = {
+      {W->s1, E * I, D / 32, o}, {W->s3, E * I, D / 32, o + gu}, {W->s2, E * D, I / 32, o + 2 * gu}};
+  for (const auto &j : jobs) {
+    const int64_t n = j.rows * (j.G / 8);
+    k_pack_decode_sf<<<unsigned(ceil_div(n, 256)), 256, 0, st>>>(j.src, j.rows, j.G, j.dst);
+    DSV41_CHECK_LAUNCH("pack_decode_sf");
+  }
+  return DSV41_OK;
+}
 
 extern "C" size_t dsv41_moe_prefill_pack_size(const dsv41_moe_config *cfg) {
   return cfg ? pf_packed_bytes(cfg) : 0;

@@ -10,11 +10,11 @@
 // Structure (one CTA = 4 consumer warps + 1 producer warp, persistent, 3 CTAs/SM):
 //   * producer lane 0 streams 64-row x 128-byte weight tiles and the matching
 //     activation tiles into a shared-memory ring with 2D TMA (128-byte swizzle,
-//     no multicast), signalling mbarriers with tx counts; the other producer lanes
-//     load the stage's ue8m0 / bf16 scale operands one stage ahead, convert them
-//     to fp32 once per CTA and store them next to the tile (the consumers would
-//     otherwise each convert the same scale four times);
-//   * each consumer warp owns 16 weight rows; per 32/64-k scale group it decodes
+//     no multicast), signalling mbarriers with tx counts; every producer lane
+//     copies its share of the stage's raw ue8m0 / bf16 scale bytes with cp.async,
+//     whose completion arrives on the same mbarrier (no wait in the producer);
+//   * each consumer warp owns 16 weight rows; it reads its rows' raw scale words once
+//     per stage and, per 32/64-k scale group, turns the group's byte into fp32 and decodes
 //     its share of the tile in registers straight to exact f16 (cvt.rn.f16x2.
 //     e2m1x2 / e4m3x2, or the 0x6400 magic for affine codes), runs
 //     mma.sync m16n8k16 f16 x f16 -> f32 against the activations, and folds the
@@ -68,6 +68,8 @@ struct QParams {
   int64_t N, K;
   int64_t sld;                 // scale row stride in elements
   int svec;                    // scale rows are NG-aligned and K % KS == 0: vector loads
+  int spack;                   // FP4: scales in the decode-packed layout (k_pack_decode_sf):
+                               // one 512-byte block [64 rows][8 groups] per (row tile, stage)
   int tiles;                   // ceil(N / QG_ROWS)
   int nsplit;
   int kstages;                 // ceil(K / KS)
@@ -165,11 +167,14 @@ struct QCfg {
   static constexpr int W_BYTES = QG_ROWS * 128;              // per matrix per stage
   static constexpr int XBOX_BYTES = NT * 8 * 128;            // max rows
   static constexpr int TILE_BYTES = NMAT * W_BYTES + NBOX * XBOX_BYTES;   // 1024-multiple
-  // fp32 scale operands per stage
-  static constexpr int SC_FLOATS =
-      WF == WF_FP4 ? NMAT * QG_ROWS * NG
-                   : (WF == WF_FP8B ? NMAT * 2 * NG : 2 * QG_ROWS * NG + NT * 8 * NG);
-  static constexpr int SC_BYTES = (SC_FLOATS * 4 + 127) / 128 * 128;
+  // raw scale operands per stage, as stored in memory:
+  //   FP4  u8 [NMAT * 64 rows][NG]            FP8B u8 [NMAT * 2 row blocks][NG]
+  //   AFF  bf16 s [64][NG] at 0, bf16 b [64][NG] at B_OFF, fp32 x sums [NT * 8][NG] at X_OFF
+  static constexpr int B_OFF = QG_ROWS * NG * 2;
+  static constexpr int X_OFF = 2 * QG_ROWS * NG * 2;
+  static constexpr int SC_RAW =
+      WF == WF_FP4 ? NMAT * QG_ROWS * NG : (WF == WF_FP8B ? NMAT * 2 * NG : X_OFF + NT * 8 * NG * 4);
+  static constexpr int SC_BYTES = (SC_RAW + 127) / 128 * 128;
   static constexpr int STAGES_RAW = QG_SMEM_BUDGET / (TILE_BYTES + SC_BYTES);
   static constexpr int STAGES = STAGES_RAW < 2 ? 2 : (STAGES_RAW > 8 ? 8 : STAGES_RAW);
   static constexpr int SMEM = STAGES * (TILE_BYTES + SC_BYTES) + 1024 /*align*/ + 256 /*barriers*/;
@@ -303,50 +308,113 @@ __device__ __forceinline__ void scales_fetch(const QParams &p, const QChunk &c, 
   }
 }
 
+__device__ __forceinline__ void sts32(uint32_t a, uint32_t v) {
+  asm volatile("st.shared.b32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ void sts64(uint32_t a, uint32_t x, uint32_t y) {
+  asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(a), "r"(x), "r"(y) : "memory");
+}
+__device__ __forceinline__ void sts128(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w)
+               : "memory");
+}
+// cp.async of N (4, 8 or 16) bytes; ok = false fills zeros and reads nothing
+template <int N>
+__device__ __forceinline__ void qg_cp_async(uint32_t dst, const void *src, bool ok) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], %2, %3;" ::"r"(dst), "l"(src), "n"(N),
+               "r"(ok ? N : 0)
+               : "memory");
+}
+// arrive on `bar` once every cp.async this thread issued so far has landed
+__device__ __forceinline__ void qg_cp_arrive(uint64_t *bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void qg_cp_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// bulk copy global -> shared (16-byte aligned, size a multiple of 16), completes on `bar`
+__device__ __forceinline__ void qg_bulk_load(uint32_t dst, const void *src, uint32_t bytes,
+                                             uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Ragged shapes: store the synchronously fetched words in the raw layout.
 template <int WF, int NMAT, int NT>
-__device__ __forceinline__ void scales_store(uint32_t sc_base, int lane, const ScaleRaw<WF, NMAT, NT> &r) {
+__device__ __forceinline__ void scales_raw_store(uint32_t scb, int lane, const ScaleRaw<WF, NMAT, NT> &r) {
+  using C = QCfg<WF, NMAT, NT>;
+  constexpr int NG = C::NG;
+  if constexpr (WF == WF_FP4) {
+#pragma unroll
+    for (int j = 0; j < C::PRODUCER_ITEMS; ++j) sts64(scb + (lane + 32 * j) * 8, r.w[j][0], r.w[j][1]);
+  } else if constexpr (WF == WF_FP8B) {
+    if (lane < 2 * NMAT) sts32(scb + lane * 4, r.w[0][0]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int row = lane + 32 * j;
+      if (NG == 4) {
+        sts64(scb + row * 8, r.w[j][0], r.w[j][1]);
+        sts64(scb + C::B_OFF + row * 8, r.w[j][2], r.w[j][3]);
+      } else {
+        sts32(scb + row * 4, r.w[j][0]);
+        sts32(scb + C::B_OFF + row * 4, r.w[j][2]);
+      }
+    }
+    if (lane < NT * 8) {
+      if (NG == 4) sts128(scb + C::X_OFF + lane * 16, r.w[2][0], r.w[2][1], r.w[2][2], r.w[2][3]);
+      else sts64(scb + C::X_OFF + lane * 8, r.w[2][0], r.w[2][1]);
+    }
+  }
+}
+
+// Vector shapes: the same bytes by cp.async (rows past N and x rows past the chunk are
+// zero-filled); the caller then arrives on the stage's full barrier through qg_cp_arrive.
+template <int WF, int NMAT, int NT>
+__device__ __forceinline__ void scales_issue(const QParams &p, const QChunk &c, int64_t nbase, int ks,
+                                             int lane, uint32_t scb) {
   using C = QCfg<WF, NMAT, NT>;
   constexpr int NG = C::NG;
   if constexpr (WF == WF_FP4) {
 #pragma unroll
     for (int j = 0; j < C::PRODUCER_ITEMS; ++j) {
-      const int idx = lane + 32 * j;   // = m * 64 + row
-      const uint32_t a = sc_base + idx * NG * 4;
-      const uint32_t v0 = r.w[j][0], v1 = r.w[j][1];
-      sts128f(a, e8m0_fast(v0), e8m0_fast(v0 >> 8), e8m0_fast(v0 >> 16), e8m0_fast(v0 >> 24));
-      sts128f(a + 16, e8m0_fast(v1), e8m0_fast(v1 >> 8), e8m0_fast(v1 >> 16), e8m0_fast(v1 >> 24));
+      const int idx = lane + 32 * j, m = idx / QG_ROWS, row = idx % QG_ROWS;
+      const bool ok = nbase + row < p.N;
+      const uint8_t *sp =
+          p.scale[m] + (ok ? ((int64_t)c.mat * p.N + nbase + row) * p.sld + (int64_t)ks * NG : 0);
+      qg_cp_async<8>(scb + idx * 8, sp, ok);
     }
   } else if constexpr (WF == WF_FP8B) {
     if (lane < 2 * NMAT) {
-      const uint32_t v = r.w[0][0];
-      sts128f(sc_base + lane * 16, e8m0_fast(v), e8m0_fast(v >> 8), e8m0_fast(v >> 16),
-              e8m0_fast(v >> 24));
+      const int m = lane >> 1, rbl = lane & 1;
+      const bool ok = nbase + 32 * rbl < p.N;
+      const int64_t rb = (int64_t)c.mat * ((p.N + 31) / 32) + ((nbase >> 5) + rbl);
+      qg_cp_async<4>(scb + lane * 4, p.scale[m] + (ok ? rb * p.sld + (int64_t)ks * NG : 0), ok);
     }
   } else {
-    // layout: s[64][NG], b[64][NG], xs[NT*8][NG]
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       const int row = lane + 32 * j;
-      const uint32_t as = sc_base + row * NG * 4, ab = sc_base + (QG_ROWS + row) * NG * 4;
-      if (NG == 4) {
-        sts128f(as, bf_bits2f(uint16_t(r.w[j][0])), bf_bits2f(uint16_t(r.w[j][0] >> 16)),
-                bf_bits2f(uint16_t(r.w[j][1])), bf_bits2f(uint16_t(r.w[j][1] >> 16)));
-        sts128f(ab, bf_bits2f(uint16_t(r.w[j][2])), bf_bits2f(uint16_t(r.w[j][2] >> 16)),
-                bf_bits2f(uint16_t(r.w[j][3])), bf_bits2f(uint16_t(r.w[j][3] >> 16)));
-      } else {
-        sts64f(as, bf_bits2f(uint16_t(r.w[j][0])), bf_bits2f(uint16_t(r.w[j][0] >> 16)));
-        sts64f(ab, bf_bits2f(uint16_t(r.w[j][2])), bf_bits2f(uint16_t(r.w[j][2] >> 16)));
-      }
+      const bool ok = nbase + row < p.N;
+      const int64_t o = ok ? ((int64_t)c.mat * p.N + nbase + row) * p.sld + (int64_t)ks * NG : 0;
+      qg_cp_async<NG * 2>(scb + row * NG * 2, p.aff_s + o, ok);
+      qg_cp_async<NG * 2>(scb + C::B_OFF + row * NG * 2, p.aff_b + o, ok);
     }
     if (lane < NT * 8) {
-      const uint32_t ax = sc_base + (2 * QG_ROWS + lane) * NG * 4;
-      if (NG == 4)
-        sts128f(ax, __uint_as_float(r.w[2][0]), __uint_as_float(r.w[2][1]),
-                __uint_as_float(r.w[2][2]), __uint_as_float(r.w[2][3]));
-      else
-        sts64f(ax, __uint_as_float(r.w[2][0]), __uint_as_float(r.w[2][1]));
+      const bool ok = lane < c.ntok;
+      const float *xp = p.xsum + (ok ? (int64_t)(c.xrow + lane) * (p.K / 64) + (int64_t)ks * NG : 0);
+      qg_cp_async<NG * 4>(scb + C::X_OFF + lane * NG * 4, xp, ok);
     }
   }
+}
+
+// ue8m0 byte j of a raw word -> fp32 (2^(b-127); b = 0 gives 0)
+__device__ __forceinline__ float e8m0_byte(uint32_t w, int j) {
+  return __uint_as_float(((w >> (8 * j)) & 0xFFu) << 23);
+}
+// bf16 half j of a raw word -> fp32
+__device__ __forceinline__ float bf16_half(uint32_t w, int j) {
+  return __uint_as_float(j ? (w & 0xFFFF0000u) : (w << 16));
 }
 
 // ------------------------------------------------------------------ the kernel
@@ -390,8 +458,7 @@ __global__ void __launch_bounds__(QG_THREADS, QG_MIN_CTAS)
     const uint64_t pol_w = l2_policy_evict_first();
     const uint64_t pol_x = l2_policy_evict_last();
     uint32_t it = 0;
-    ScaleRaw<WF, NMAT, NT> raw;
-    bool have_raw = false;
+    const uint32_t sc0 = smem_u32(sc_ring);
     for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
       int chunk, tile, split;
       QChunk c;
@@ -406,14 +473,25 @@ __global__ void __launch_bounds__(QG_THREADS, QG_MIN_CTAS)
       for (int ks = kb; ks < ke; ++ks, ++it) {
         const int slot = it % ST;
         const uint32_t ph = (it / ST) & 1;
-        if (!have_raw) scales_fetch<WF, NMAT, NT>(p, c, nbase, ks, lane, raw);
         bool ok = true;
         if (lane == 0) ok = mbar_wait(&empty[slot], ph ^ 1);
         ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) return;
+        if (!ok) {
+          qg_cp_wait_all();      // no copy may land after the CTA is gone
+          return;
+        }
         uint8_t *st = smem + slot * C::TILE_BYTES;
+        const uint32_t scb = sc0 + slot * C::SC_BYTES;
+        const bool packed = WF == WF_FP4 && p.spack;
         if (lane == 0) {
-          mbar_arrive_expect_tx(&full[slot], bytes);
+          mbar_arrive_expect_tx(&full[slot], bytes + (packed ? NMAT * QG_ROWS * 8 : 0));
+          if (WF == WF_FP4 && packed) {
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m)
+              qg_bulk_load(scb + m * QG_ROWS * 8,
+                           p.scale[m] + (((int64_t)c.mat * p.tiles + tile) * p.kstages + ks) * (QG_ROWS * 8),
+                           QG_ROWS * 8, &full[slot]);
+          }
           tma_load_2d(st, &wmap0, &full[slot], ks * 128, wrow, pol_w);
           if (NMAT == 2) tma_load_2d(st + C::W_BYTES, &wmap1, &full[slot], ks * 128, wrow, pol_w);
 #pragma unroll
@@ -421,17 +499,20 @@ __global__ void __launch_bounds__(QG_THREADS, QG_MIN_CTAS)
             tma_load_2d(st + NMAT * C::W_BYTES + b * C::XBOX_BYTES, xm, &full[slot],
                         ks * KS + b * 64, c.xrow, pol_x);
         }
-        scales_store<WF, NMAT, NT>(smem_u32(sc_ring + slot * C::SC_BYTES), lane, raw);
-        // fetch the next stage's scales now (same item) so the loads overlap the wait
-        if (ks + 1 < ke) {
-          scales_fetch<WF, NMAT, NT>(p, c, nbase, ks + 1, lane, raw);
-          have_raw = true;
+        if (packed) {
+          mbar_arrive(&full[slot]);        // the scales came with the stage's bulk copies
+        } else if (p.svec) {
+          scales_issue<WF, NMAT, NT>(p, c, nbase, ks, lane, scb);
+          qg_cp_arrive(&full[slot]);       // every lane: arrives when its copies land
         } else {
-          have_raw = false;
+          ScaleRaw<WF, NMAT, NT> raw;
+          scales_fetch<WF, NMAT, NT>(p, c, nbase, ks, lane, raw);
+          scales_raw_store<WF, NMAT, NT>(scb, lane, raw);
+          mbar_arrive(&full[slot]);        // every lane: its scale stores are in
         }
-        mbar_arrive(&full[slot]);      // every lane: its scale stores are in
       }
     }
+    qg_cp_wait_all();
     return;
   }
 
@@ -468,10 +549,41 @@ __global__ void __launch_bounds__(QG_THREADS, QG_MIN_CTAS)
       const uint32_t xst = st + NMAT * C::W_BYTES;
       const uint32_t scb = smem_u32(sc_ring + slot * C::SC_BYTES);
 
+      // this stage's raw scale words for my rows (one vector load per row)
+      uint32_t rs[NMAT][2][2];        // FP4: [mat][h] 8 bytes; FP8B: [mat] 4 bytes; AFF: s [h]
+      uint32_t rb[2][2];              // AFF: biases [h]
+      if constexpr (WF == WF_FP4) {
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint2 v = lds64(scb + (m * QG_ROWS + rowA + 8 * h) * 8);
+            rs[m][h][0] = v.x;
+            rs[m][h][1] = v.y;
+          }
+      } else if constexpr (WF == WF_FP8B) {
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m) rs[m][0][0] = lds32(scb + (m * 2 + (warp >> 1)) * 4);
+      } else {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t r = rowA + 8 * h;
+          if (NG == 4) {
+            const uint2 sv = lds64(scb + r * 8), bv = lds64(scb + C::B_OFF + r * 8);
+            rs[0][h][0] = sv.x; rs[0][h][1] = sv.y;
+            rb[h][0] = bv.x; rb[h][1] = bv.y;
+          } else {
+            rs[0][h][0] = lds32(scb + r * 4);
+            rb[h][0] = lds32(scb + C::B_OFF + r * 4);
+            rs[0][h][1] = 0u;
+            rb[h][1] = 0u;
+          }
+        }
+      }
 #pragma unroll
       for (int grp = 0; grp < NG; ++grp) {
         constexpr int STEPS = Fmt<WF>::GK / 16;
-        // ---- this group's scale operands (fp32, staged by the producer) ----
+        // ---- this group's scale operands ----
         float sc[NMAT][2];
         float bi[2];
         float xs[NT][2];
@@ -479,28 +591,25 @@ __global__ void __launch_bounds__(QG_THREADS, QG_MIN_CTAS)
 #pragma unroll
           for (int m = 0; m < NMAT; ++m)
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const uint32_t a = scb + ((m * QG_ROWS + rowA + 8 * h) * NG + grp) * 4;
-              sc[m][h] = __uint_as_float(lds32(a));
-            }
+            for (int h = 0; h < 2; ++h) sc[m][h] = e8m0_byte(rs[m][h][grp >> 2], grp & 3);
         } else if constexpr (WF == WF_FP8B) {
 #pragma unroll
           for (int m = 0; m < NMAT; ++m) {
-            const float v = __uint_as_float(lds32(scb + ((m * 2 + (warp >> 1)) * NG + grp) * 4));
+            const float v = e8m0_byte(rs[m][0][0], grp);
             sc[m][0] = v;
             sc[m][1] = v;
           }
         } else {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            sc[0][h] = __uint_as_float(lds32(scb + ((rowA + 8 * h) * NG + grp) * 4));
-            bi[h] = __uint_as_float(lds32(scb + ((QG_ROWS + rowA + 8 * h) * NG + grp) * 4));
+            sc[0][h] = bf16_half(rs[0][h][grp >> 1], grp & 1);
+            bi[h] = bf16_half(rb[h][grp >> 1], grp & 1);
           }
 #pragma unroll
           for (int n = 0; n < NT; ++n)
 #pragma unroll
             for (int j = 0; j < 2; ++j)
-              xs[n][j] = __uint_as_float(lds32(scb + ((2 * QG_ROWS + n * 8 + cs[j]) * NG + grp) * 4));
+              xs[n][j] = __uint_as_float(lds32(scb + C::X_OFF + ((n * 8 + cs[j]) * NG + grp) * 4));
         }
         // ---- A fragments: [mat][step][4 regs] ----
         uint32_t a[NMAT][STEPS][4];
@@ -817,6 +926,23 @@ __global__ void __launch_bounds__(256) k_qx_prep(const __nv_bfloat16 *__restrict
       if ((threadIdx.x & 7) == 0) xsum[r * (K / 64) + i / 8] = s;
     }
   }
+}
+
+// ------------------------------------------------------------------ decode scale pack
+// FP4 expert scales u8 [rows, G] (G = K / 32 groups per row, rows % 64 == 0, G % 8 == 0) ->
+// [rows / 64 tiles][G / 8 stages][64 rows][8 groups]: the scales one decode stage of one
+// 64-row tile needs are one contiguous 512-byte block (one bulk copy, whole lines), where the
+// row-major layout costs a separate 8-byte request per row and stage.  One thread per block
+// row (8 bytes).
+__global__ void __launch_bounds__(256) k_pack_decode_sf(const uint8_t *__restrict__ src, int64_t rows,
+                                                        int64_t G, uint8_t *__restrict__ dst) {
+  const int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;   // (tile, stage, r)
+  const int64_t nst = G / 8;
+  if (u >= rows * nst) return;
+  const int64_t r = u % QG_ROWS, ts = u / QG_ROWS;
+  const int64_t tile = ts / nst, stg = ts % nst;
+  const uint2 v = __ldg(reinterpret_cast<const uint2 *>(src + (tile * QG_ROWS + r) * G + stg * 8));
+  reinterpret_cast<uint2 *>(dst)[u] = v;
 }
 
 }  // namespace dsv41

@@ -197,12 +197,8 @@ class EPMoE:
         R = rows.shape[0]
         if R == 0:
             return t.empty((0, m.dim), dtype=t.float32, device=rows.device)
-        a = m.args
-        cfg = L.MoeConfig(dim=a.dim, inter=a.moe_inter_dim, n_experts=a.n_routed_experts, topk=1,
-                          score_func=0, gate_temp=1.0, norm_topk_prob=1, route_scale=1.0,
-                          swiglu_limit=float(a.swiglu_limit),
-                          flags=(L.MOE_ROUND_BF16 if m.round_bf16 else 0) | L.MOE_NO_SHARED)
-        W = m._weights()
+        cfg, W = m._decode_args(L.MOE_NO_SHARED)      # decode-packed scales when they apply
+        cfg.topk = 1                                   # every received row is one pair
         y = t.empty((R, 1, m.dim), dtype=t.float32, device=rows.device)
         ws = L.workspace(L.load().dsv41_moe_decode_workspace_size(C.byref(cfg), R), rows.device)
         ids = local_ids.reshape(R, 1).contiguous()

@@ -131,12 +131,19 @@ class MoE:
     With ``cuda_graph=True`` (default) each (tokens, output dtype, device) shape is
     captured once into a CUDA graph (router, plan, expert kernels, shared expert
     on a forked stream, combine) and replayed; the graph owns its input/output
-    buffers and workspace and is rebuilt if any weight tensor is replaced.
+    buffers and workspace and is rebuilt if any weight tensor is replaced or modified.
     Outputs are fresh tensors (copies of the graph's buffers), as the reference's
     functional API returns new arrays.
+
+    With ``pack_decode_scales=True`` (default, when dim and moe_inter_dim are
+    multiples of 256) the routed experts' ue8m0 scales are rearranged once into the
+    decode-packed layout (``dsv41_moe_decode_pack``: one contiguous block per 64-row
+    tile and K stage) and rebuilt when a scale tensor changes; the decode kernels then
+    fetch each stage's scales with one bulk copy.
     """
 
-    def __init__(self, args, round_bf16: bool = True, cuda_graph: bool = True):
+    def __init__(self, args, round_bf16: bool = True, cuda_graph: bool = True,
+                 pack_decode_scales: bool = True):
         self.args = args
         self.dim = args.dim
         self.gate = Gate(args)
@@ -146,6 +153,9 @@ class MoE:
         self.shared_experts = SharedExpert(args.dim, args.moe_inter_dim, args.swiglu_limit)
         self.round_bf16 = round_bf16
         self.cuda_graph = cuda_graph
+        self.pack_decode_scales = pack_decode_scales
+        self._dpack = None
+        self._dpack_key = None
         self._ws = None
         self._graphs = {}
         self._graph_sig = None
@@ -155,11 +165,11 @@ class MoE:
         objs = (self.gate.weight, self.gate.bias, e.gate_proj.weight, e.gate_proj.scales,
                 e.up_proj.weight, e.up_proj.scales, e.down_proj.weight, e.down_proj.scales,
                 s.w1.weight, s.w1.scales, s.w3.weight, s.w3.scales, s.w2.weight, s.w2.scales)
-        return tuple((id(o), o.data_ptr() if hasattr(o, "data_ptr") else 0) for o in objs)
+        return tuple((id(o), o.data_ptr() if hasattr(o, "data_ptr") else 0,
+                      getattr(o, "_version", 0)) for o in objs)
 
-    def _decode_into(self, xf, y, weights, indices, W, ws):
+    def _decode_into(self, xf, y, weights, indices, W, ws, cfg):
         T = xf.shape[0]
-        cfg = self._cfg()
         L.call("dsv41_moe_decode", C.byref(cfg), C.byref(W), L.ptr(xf), T, L.dtype_code(y.dtype),
                L.ptr(y), L.ptr(weights), L.ptr(indices), L.ptr(ws), ws.numel(), L.stream_of(xf))
 
@@ -178,20 +188,19 @@ class MoE:
             sy = t.empty((T, self.dim), dtype=odt, device=xf.device)
             sw = t.empty((T, k), dtype=t.float32, device=xf.device)
             si = t.empty((T, k), dtype=t.int32, device=xf.device)
-            cfg = self._cfg()
+            cfg, W = self._decode_args()
             ws = L.workspace(L.load().dsv41_moe_decode_workspace_size(C.byref(cfg), T), xf.device)
-            W = self._weights()
             keep = list(self._keep)
             sx.copy_(xf)
             side = t.cuda.Stream(device=xf.device)
             side.wait_stream(t.cuda.current_stream(xf.device))
             with t.cuda.stream(side):                      # warm-up outside capture
-                self._decode_into(sx, sy, sw, si, W, ws)
+                self._decode_into(sx, sy, sw, si, W, ws, cfg)
             t.cuda.current_stream(xf.device).wait_stream(side)
             g = t.cuda.CUDAGraph()
             with t.cuda.graph(g):
-                self._decode_into(sx, sy, sw, si, W, ws)
-            ent = (g, sx, sy, sw, si, ws, W, keep)
+                self._decode_into(sx, sy, sw, si, W, ws, cfg)
+            ent = (g, sx, sy, sw, si, ws, W, keep, cfg)
             self._graphs[key] = ent
         g, sx, sy, sw, si = ent[:5]
         sx.copy_(xf)
@@ -231,6 +240,39 @@ class MoE:
             sw3=p(s.w3.weight, L.u8), ss3=p(s.w3.scales, L.u8),
             sw2=p(s.w2.weight, L.u8), ss2=p(s.w2.scales, L.u8))
 
+    def _decode_pack(self, cfg, W):
+        """The routed experts' scales in the decode-packed layout, or None when the shapes
+        do not allow it (dim and inter must be multiples of 256)."""
+        a = self.args
+        e = self.experts
+        if (not self.pack_decode_scales or a.dim % 256 or a.moe_inter_dim % 256
+                or e.gate_proj.scales is None):
+            return None
+        srcs = [L.cuda_tensor(p.scales) for p in (e.gate_proj, e.up_proj, e.down_proj)]
+        key = tuple((s.data_ptr(), s._version, tuple(s.shape)) for s in srcs)
+        if self._dpack_key != key:
+            n = L.load().dsv41_moe_decode_pack_size(C.byref(cfg))
+            buf = L.workspace(n, srcs[0].device)
+            L.call("dsv41_moe_decode_pack", C.byref(cfg), C.byref(W), L.ptr(buf), n,
+                   L.stream_of(buf))
+            self._dpack, self._dpack_key = buf, key
+        return self._dpack
+
+    def _decode_args(self, flags=0):
+        """(config, weights) for the decode entries, with the decode-packed scales when
+        they apply."""
+        cfg = self._cfg(flags)
+        W = self._weights()
+        pk = self._decode_pack(cfg, W)
+        if pk is not None:
+            a = self.args
+            gu = a.n_routed_experts * a.moe_inter_dim * (a.dim // 32)
+            base = L.ptr(pk)
+            W.s1, W.s3, W.s2 = base, base + gu, base + 2 * gu
+            cfg.flags |= L.MOE_PACKED_SCALES
+            self._keep.append(pk)
+        return cfg, W
+
     def _workspace(self, cfg, T, device):
         need = L.load().dsv41_moe_decode_workspace_size(C.byref(cfg), T)
         if self._ws is None or self._ws.numel() < need or self._ws.device != device:
@@ -243,8 +285,7 @@ class MoE:
         xf = xt.reshape(-1, self.dim)
         idx = L.cuda_tensor(indices, "indices").to(t.int32).reshape(xf.shape[0], -1)
         T, k = idx.shape
-        cfg = self._cfg(L.MOE_NO_SHARED)
-        W = self._weights()
+        cfg, W = self._decode_args(L.MOE_NO_SHARED)
         y = t.empty((T, k, self.dim), dtype=t.float32, device=xf.device)
         ws = self._workspace(cfg, T, xf.device)
         L.call("dsv41_moe_experts", C.byref(cfg), C.byref(W), L.ptr(xf), T, L.ptr(idx), L.ptr(y),
@@ -262,9 +303,7 @@ class MoE:
             y, weights, indices = self._graph_call(xf, odt)
             y = y.reshape(shape)
             return (y, weights, indices) if with_routing else y
-        cfg = self._cfg()
-        W = self._weights()
-        odt = out_dtype or (t.float32 if xt.dtype == t.float32 else t.bfloat16)
+        cfg, W = self._decode_args()
         y = t.empty((T, self.dim), dtype=odt, device=xf.device)
         k = self.args.n_activated_experts
         weights = t.empty((T, k), dtype=t.float32, device=xf.device)

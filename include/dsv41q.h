@@ -67,6 +67,11 @@ extern "C" {
 /* dsv41_moe_prefill only: the shared expert alone (no routing, no routed experts) -- the
  * source-rank half of expert-parallel prefill. */
 #define DSV41_MOE_SHARED_ONLY 4
+/* Decode entries (dsv41_moe_decode, dsv41_moe_experts): w->s1, s3, s2 point into the
+ * decode-packed scales written by dsv41_moe_decode_pack (s1 at offset 0, s3 at
+ * E*I*(D/32), s2 at 2*E*I*(D/32) bytes) instead of the release layout.  Needs dim and inter
+ * multiples of 256 and 16-byte aligned pointers.  Rejected by the prefill entries. */
+#define DSV41_MOE_PACKED_SCALES 8
 
 /* ---- library ------------------------------------------------------------ */
 const char *dsv41_get_last_error(void);
@@ -199,6 +204,15 @@ typedef struct dsv41_moe_config {
   int flags;
 } dsv41_moe_config;
 
+/* Decode-packed expert scales (no reference counterpart; the release layout is kept as the
+ * input): for each of s1, s3 ([E*I, D/32]) and s2 ([E*D, I/32]) the bytes one decode stage of
+ * one 64-row tile reads -- 64 rows x 8 groups of 32 -- become one contiguous 512-byte block
+ * ([rows/64][K/256][64][8]), fetched by a single bulk copy instead of an 8-byte request per row.
+ * packed: dsv41_moe_decode_pack_size(cfg) bytes, 16-byte aligned; valid while the scales are
+ * unchanged. */
+size_t dsv41_moe_decode_pack_size(const dsv41_moe_config *cfg);
+int dsv41_moe_decode_pack(const dsv41_moe_config *cfg, const dsv41_moe_weights *w, void *packed,
+                          size_t packed_bytes, void *stream);
 size_t dsv41_moe_decode_workspace_size(const dsv41_moe_config *cfg, int64_t T);
 /* The routed experts alone for given routing (mlx_lm SwitchGLU as called at
  * deepseek_v41_mlx/moe.py:109, i.e. MoE.experts(xf, indices)): indices int32

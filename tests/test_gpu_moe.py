@@ -225,3 +225,43 @@ def test_moe_decode_capi_workspace_reuse(cuda):
     st = C.c_uint32(0)
     L.call("dsv41_device_status", torch.cuda.current_stream().cuda_stream, C.byref(st))
     assert st.value == 0
+
+
+@pytest.mark.parametrize("T", [1, 7, 40])
+def test_moe_decode_packed_scales_identical(cuda, T):
+    """Decode with the routed scales in the decode-packed layout (one contiguous block per
+    64-row tile and stage) gives the same bits as the release layout, graph and direct."""
+    rng = np.random.default_rng(300 + T)
+    E, D, I, k = 12, 512, 256, 4
+    p = moe_params(rng, E, D, I)
+    args = _args(E, D, I, k)
+    xb, _ = bf16_acts(rng, T, D)
+    outs = []
+    for pack in (False, True):
+        for graph in (False, True):
+            m = _moe(p, args, round_bf16=True)
+            m.pack_decode_scales, m.cuda_graph = pack, graph
+            y, w, idx = m(_bf(xb), with_routing=True, out_dtype=torch.float32)
+            ye = m.experts(_bf(xb), idx)
+            outs.append((y, w, idx, ye))
+            assert (m._dpack is not None) == pack
+    for y, w, idx, ye in outs[1:]:
+        assert torch.equal(y, outs[0][0]) and torch.equal(idx, outs[0][2])
+        assert torch.equal(ye, outs[0][3])
+
+
+def test_moe_decode_pack_rejected_by_prefill(cuda):
+    """The prefill entries read the release layout and refuse the packed-scales flag."""
+    rng = np.random.default_rng(4)
+    E, D, I, k = 8, 256, 256, 2
+    p = moe_params(rng, E, D, I)
+    m = _moe(p, _args(E, D, I, k), round_bf16=True)
+    cfg, W = m._decode_args()
+    assert cfg.flags & L.MOE_PACKED_SCALES
+    x = torch.zeros(4, D, dtype=torch.bfloat16, device="cuda")
+    y = torch.empty(4, D, dtype=torch.float32, device="cuda")
+    ws = L.workspace(L.load().dsv41_moe_prefill_workspace_size(C.byref(cfg), 4, 0, 0), "cuda")
+    st = L.load().dsv41_moe_prefill(C.byref(cfg), C.byref(W), None, L.ptr(x), 4, None, None,
+                                    L.dtype_code(torch.float32), L.ptr(y), L.ptr(ws), ws.numel(),
+                                    L.stream_of(x))
+    assert st != 0
