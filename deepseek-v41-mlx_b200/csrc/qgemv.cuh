@@ -110,34 +110,24 @@ template <int WF> __device__ __forceinline__ int xcol_perm(int c) {
   return (WF == WF_AFF4 || WF == WF_AFF8) ? c : rhoB(c);
 }
 
+// Shared-memory reads of the stage data as plain C++ loads from the dynamic shared array
+// (every extern __shared__ array names its base), so the compiler may overlap one scale
+// group's loads with the previous group's MMAs; the mbarrier wait before a stage and the
+// arrive after it carry "memory" clobbers, so no load crosses either.
+extern __shared__ __align__(1024) uint8_t qg_dyn_smem[];
+__device__ __forceinline__ const uint8_t *qg_sptr(uint32_t a) {
+  return qg_dyn_smem + (a - static_cast<uint32_t>(__cvta_generic_to_shared(qg_dyn_smem)));
+}
 __device__ __forceinline__ uint32_t lds32(uint32_t a) {
-  uint32_t v;
-  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(a));
-  return v;
+  return *reinterpret_cast<const uint32_t *>(qg_sptr(a));
 }
-__device__ __forceinline__ uint2 lds64(uint32_t a) {
-  uint2 v;
-  asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
-  return v;
-}
-__device__ __forceinline__ uint4 lds128(uint32_t a) {
-  uint4 v;
-  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "r"(a));
-  return v;
-}
+__device__ __forceinline__ uint2 lds64(uint32_t a) { return *reinterpret_cast<const uint2 *>(qg_sptr(a)); }
+__device__ __forceinline__ uint4 lds128(uint32_t a) { return *reinterpret_cast<const uint4 *>(qg_sptr(a)); }
 __device__ __forceinline__ float4 lds128f(uint32_t a) {
-  float4 v;
-  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(a));
-  return v;
+  return *reinterpret_cast<const float4 *>(qg_sptr(a));
 }
 __device__ __forceinline__ float2 lds64f(uint32_t a) {
-  float2 v;
-  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(a));
-  return v;
+  return *reinterpret_cast<const float2 *>(qg_sptr(a));
 }
 __device__ __forceinline__ void sts128f(uint32_t a, float x, float y, float z, float w) {
   asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(a), "f"(x), "f"(y), "f"(z), "f"(w)
@@ -184,15 +174,18 @@ struct QCfg {
       WF == WF_FP4 ? NMAT * QG_ROWS / 32 : (WF == WF_FP8B ? 1 : 3);
 };
 
+// Work item -> (chunk, row tile, K split) and the chunk's descriptor.  In list form the
+// descriptor comes from `pre`, which the caller loaded one item ahead (chunk_prefetch), so
+// no item waits on a dependent global load before its first stage.
 __device__ __forceinline__ void decode_chunk(const QParams &p, int item, int &chunk, int &tile,
-                                             int &split, QChunk &c) {
+                                             int &split, QChunk &c, const QChunk &pre) {
   const int per_chunk = p.tiles * p.nsplit;
   chunk = item / per_chunk;
   const int rem = item % per_chunk;
   tile = rem / p.nsplit;
   split = rem % p.nsplit;
   if (p.chunks) {
-    c = p.chunks[chunk];
+    c = pre;
   } else if (!p.dense_down) {
     c.mat = 0;
     c.xrow = chunk * p.dense_rows;
@@ -208,6 +201,10 @@ __device__ __forceinline__ void decode_chunk(const QParams &p, int item, int &ch
     c.ntok = 8 * ((nt + 3) / 4);
     c.orow = q0;
   }
+}
+
+__device__ __forceinline__ void chunk_prefetch(const QParams &p, int item, int nitems, QChunk &pre) {
+  if (p.chunks && item < nitems) pre = p.chunks[item / (p.tiles * p.nsplit)];
 }
 
 // ------------------------------------------------------------------ producer scale staging
@@ -459,10 +456,13 @@ __global__ void __launch_bounds__(QG_THREADS, QG_MIN_CTAS)
     const uint64_t pol_x = l2_policy_evict_last();
     uint32_t it = 0;
     const uint32_t sc0 = smem_u32(sc_ring);
+    QChunk pre{};
+    chunk_prefetch(p, blockIdx.x, nitems, pre);
     for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
       int chunk, tile, split;
       QChunk c;
-      decode_chunk(p, item, chunk, tile, split, c);
+      decode_chunk(p, item, chunk, tile, split, c, pre);
+      chunk_prefetch(p, item + gridDim.x, nitems, pre);      // used by the next item
       const int kb = int((int64_t)p.kstages * split / p.nsplit);
       const int ke = int((int64_t)p.kstages * (split + 1) / p.nsplit);
       const int xr = c.ntok <= 8 ? 8 : (c.ntok <= 16 ? 16 : 32);
@@ -524,15 +524,17 @@ __global__ void __launch_bounds__(QG_THREADS, QG_MIN_CTAS)
   const int cs[2] = {xcol_perm<WF>(2 * t), xcol_perm<WF>(2 * t + 1)};  // slots of my columns
   uint32_t it = 0;
 
+  QChunk pre{};
+  chunk_prefetch(p, blockIdx.x, nitems, pre);
   for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
     int chunk, tile, split;
     QChunk c;
-    decode_chunk(p, item, chunk, tile, split, c);
+    decode_chunk(p, item, chunk, tile, split, c, pre);
+    chunk_prefetch(p, item + gridDim.x, nitems, pre);        // used by the next item
     const int kb = int((int64_t)p.kstages * split / p.nsplit);
     const int ke = int((int64_t)p.kstages * (split + 1) / p.nsplit);
     const int64_t nbase = (int64_t)tile * QG_ROWS;              // row within the matrix
     const int ntiles_x = (c.ntok + 7) / 8;                      // active n8 tiles
-
     float acc[NMAT][NT][4];
 #pragma unroll
     for (int m = 0; m < NMAT; ++m)
@@ -796,17 +798,19 @@ __global__ void __launch_bounds__(QG_THREADS, QG_MIN_CTAS)
         }
         continue;
       }
+      if (p.epi == EPI_SWIGLU) {
+        // the four outputs (j, h) of this thread are computed together, branch-free, so
+        // their exp / divide chains overlap; only the stores are predicated.  silu uses
+        // the fast exp and divide (a few ulp; for g below about -88 the quotient is -0).
+        float hv[2][2];
+        bool ok[2][2];
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int slotx = n * 8 + cs[j];
-        if (slotx >= c.ntok) continue;
-        const float xsc = p.xscale ? p.xscale[c.xrow + slotx] : 1.0f;
+        for (int j = 0; j < 2; ++j)
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int64_t nn = nbase + rowA + 8 * h;
-          if (nn >= p.N) continue;
-          const int i = 2 * h + j;
-          if (p.epi == EPI_SWIGLU) {
+          for (int h = 0; h < 2; ++h) {
+            const int i = 2 * h + j;
+            ok[j][h] = (n * 8 + cs[j] < c.ntok) && (nbase + rowA + 8 * h < p.N);
+            const float xsc = (p.xscale && n * 8 + cs[j] < c.ntok) ? p.xscale[c.xrow + n * 8 + cs[j]] : 1.0f;
             float gv = acc[0][n][i] * xsc, uv = acc[NMAT - 1][n][i] * xsc;
             if (p.round_gu) {
               gv = round_bf16f(gv);
@@ -816,23 +820,42 @@ __global__ void __launch_bounds__(QG_THREADS, QG_MIN_CTAS)
               uv = fminf(fmaxf(uv, -p.limit), p.limit);
               gv = fminf(gv, p.limit);
             }
-            float hv = __fdiv_rn(gv, 1.0f + expf(-gv)) * uv;
-            if (p.round_h) hv = round_bf16f(hv);
-            const __half hi = __float2half_rn(hv);
-            const __half lo = __float2half_rn(hv - __half2float(hi));
-            const int q = c.xrow + slotx;                 // pair (or token) index
-            __half *H = reinterpret_cast<__half *>(p.out);
-            const int64_t hr = 8 * (q >> 2) + (q & 3);
+            float v = __fdividef(gv, 1.0f + __expf(-gv)) * uv;
+            if (p.round_h) v = round_bf16f(v);
+            hv[j][h] = v;
+          }
+        __half *H = reinterpret_cast<__half *>(p.out);
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int q = c.xrow + n * 8 + cs[j];               // pair (or token) index
+          const int64_t hr = 8 * (q >> 2) + (q & 3);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            if (!ok[j][h]) continue;
+            const int64_t nn = nbase + rowA + 8 * h;
+            const __half hi = __float2half_rn(hv[j][h]);
+            const __half lo = __float2half_rn(hv[j][h] - __half2float(hi));
             H[hr * p.ldo + nn] = hi;
             H[(hr + 4) * p.ldo + nn] = lo;
-          } else {
-            const float v = acc[0][n][i] * xsc;
-            const int64_t o = (int64_t)(c.orow + slotx) * p.ldo + nn;
-            if (p.epi == EPI_STORE_F32)
-              reinterpret_cast<float *>(p.out)[o] = v;
-            else
-              reinterpret_cast<__nv_bfloat16 *>(p.out)[o] = __float2bfloat16_rn(v);
           }
+        }
+        continue;
+      }
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int slotx = n * 8 + cs[j];
+        if (slotx >= c.ntok) continue;
+        const float xsc = p.xscale ? p.xscale[c.xrow + slotx] : 1.0f;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int64_t nn = nbase + rowA + 8 * h;
+          if (nn >= p.N) continue;
+          const float v = acc[0][n][2 * h + j] * xsc;
+          const int64_t o = (int64_t)(c.orow + slotx) * p.ldo + nn;
+          if (p.epi == EPI_STORE_F32)
+            reinterpret_cast<float *>(p.out)[o] = v;
+          else
+            reinterpret_cast<__nv_bfloat16 *>(p.out)[o] = __float2bfloat16_rn(v);
         }
       }
     }
