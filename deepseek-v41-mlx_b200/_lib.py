@@ -57,6 +57,8 @@ PROTOTYPES = {
     "dsv41_prof_enable": (_I, [_I]),
     "dsv41_prof_reset": (_I, []),
     "dsv41_prof_report": (_I, [C.c_char_p, _SZ]),
+    "dsv41_prof_select": (_I, [C.c_char_p]),
+    "dsv41_prof_launches": (C.c_longlong, []),
     "dsv41_e8m0_to_float": (_I, [_P, _I64, _P, _P]),
     "dsv41_dequant_fp8_block": (_I, [_P, _P, _I64, _I64, _I, _P, _P]),
     "dsv41_unpack_fp4": (_I, [_P, _I64, _I64, _P, _P]),
@@ -194,6 +196,16 @@ def u8(t):
 def prof_enable(on: bool = True):
     load().dsv41_prof_enable(1 if on else 0)
     load().dsv41_prof_reset()
+
+
+def prof_select(names=None):
+    """Time only the named kernels (an iterable of names; None = all of them)."""
+    load().dsv41_prof_select(",".join(names).encode() if names else None)
+
+
+def prof_launches() -> int:
+    """Kernel launches counted since prof_enable, timed or not."""
+    return int(load().dsv41_prof_launches())
 
 
 def prof_report() -> dict:

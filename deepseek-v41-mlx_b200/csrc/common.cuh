@@ -312,22 +312,46 @@ static constexpr int PROF_CAP = 4096;
 static ProfRec g_prof[PROF_CAP];
 static int g_prof_n = 0;
 static bool g_prof_on = false;
+static char g_prof_sel[512] = "";   // comma-separated kernel names to time; empty = all
+static long long g_prof_launches = 0;
+
+// whether `name` is one of the comma-separated names in g_prof_sel (or the list is empty)
+static inline bool prof_selected(const char *name) {
+  if (!g_prof_sel[0]) return true;
+  const size_t n = strlen(name);
+  for (const char *p = g_prof_sel; *p;) {
+    const char *e = strchr(p, ',');
+    const size_t len = e ? size_t(e - p) : strlen(p);
+    if (len == n && strncmp(p, name, n) == 0) return true;
+    if (!e) break;
+    p = e + 1;
+  }
+  return false;
+}
 
 struct ProfScope {
   int slot = -1;
   cudaStream_t st;
   ProfScope(const char *name, cudaStream_t s) : st(s) {
-    if (!g_prof_on || g_prof_n >= PROF_CAP) return;
+    if (!g_prof_on) return;
+    ++g_prof_launches;
+    if (g_prof_n >= PROF_CAP || !prof_selected(name)) return;
     slot = g_prof_n++;
     ProfRec &r = g_prof[slot];
     r.name = name;
     if (!r.a) cudaEventCreate(&r.a);
     if (!r.b) cudaEventCreate(&r.b);
-    cudaEventRecord(r.a, st);
+    // while the stream is being captured, the records become event nodes of the graph
+    // (recorded at every replay of it); otherwise plain stream records
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(st, &cs);
+    flags = cs == cudaStreamCaptureStatusActive ? cudaEventRecordExternal : cudaEventRecordDefault;
+    cudaEventRecordWithFlags(r.a, st, flags);
   }
   ~ProfScope() {
-    if (slot >= 0) cudaEventRecord(g_prof[slot].b, st);
+    if (slot >= 0) cudaEventRecordWithFlags(g_prof[slot].b, st, flags);
   }
+  unsigned flags = cudaEventRecordDefault;
 };
 
 static inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }

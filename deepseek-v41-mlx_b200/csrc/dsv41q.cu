@@ -43,8 +43,20 @@ extern "C" int dsv41_prof_enable(int on) {
 
 extern "C" int dsv41_prof_reset(void) {
   g_prof_n = 0;
+  g_prof_launches = 0;
   return DSV41_OK;
 }
+
+extern "C" int dsv41_prof_select(const char *names) {
+  const size_t n = names ? strlen(names) : 0;
+  DSV41_REQUIRE(n < sizeof(g_prof_sel), DSV41_ERR_BAD_ARG, "name list longer than %zu bytes",
+                sizeof(g_prof_sel) - 1);
+  if (n) memcpy(g_prof_sel, names, n);
+  g_prof_sel[n] = 0;
+  return DSV41_OK;
+}
+
+extern "C" long long dsv41_prof_launches(void) { return g_prof_launches; }
 
 extern "C" int dsv41_prof_report(char *buf, size_t cap) {
   DSV41_REQUIRE(buf && cap > 0, DSV41_ERR_BAD_ARG, "NULL buffer");

@@ -87,6 +87,11 @@ int dsv41_device_status(void *stream, uint32_t *flags_out);
 int dsv41_prof_enable(int on);
 int dsv41_prof_reset(void);
 int dsv41_prof_report(char *buf, size_t cap);
+/* Time only the kernels named in the comma-separated list (NULL or "" = all), so that a
+ * timed region carries events around its dominant kernel alone; every launch is still
+ * counted (dsv41_prof_launches, since the last reset). */
+int dsv41_prof_select(const char *names);
+long long dsv41_prof_launches(void);
 
 /* ---- a1..a7: release-format decode (bit-exact) --------------------------
  * e8m0_to_float    replaces deepseek_v41_mlx/dequant.py:33-36
