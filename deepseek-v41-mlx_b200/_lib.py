@@ -76,6 +76,14 @@ PROTOTYPES = {
                              _P]),
     "dsv41_moe_decode_workspace_size": (_SZ, [C.POINTER(MoeConfig), _I64]),
     "dsv41_moe_decode_pack_size": (_SZ, [C.POINTER(MoeConfig)]),
+    "dsv41_ep_create": (_I, [_I, _I, _I64, _I, _I64, C.POINTER(_P)]),
+    "dsv41_ep_handle_bytes": (_SZ, []),
+    "dsv41_ep_handle": (_I, [_P, _P]),
+    "dsv41_ep_connect": (_I, [_P, _P]),
+    "dsv41_ep_destroy": (_I, [_P]),
+    "dsv41_moe_ep_decode_workspace_size": (_SZ, [C.POINTER(MoeConfig), _P, _I64]),
+    "dsv41_moe_ep_decode": (_I, [C.POINTER(MoeConfig), C.POINTER(MoeWeights), _P, _P, _I64, _I,
+                                 _P, _P, _P, _P, _SZ, _P]),
     "dsv41_moe_decode_pack": (_I, [C.POINTER(MoeConfig), C.POINTER(MoeWeights), _P, _SZ, _P]),
     "dsv41_moe_experts": (_I, [C.POINTER(MoeConfig), C.POINTER(MoeWeights), _P, _I64, _P, _P, _P,
                                _SZ, _P]),

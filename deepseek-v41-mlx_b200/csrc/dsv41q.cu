@@ -9,6 +9,7 @@
 #include "moe.cuh"
 #include "bsgemm.cuh"
 #include "prefill.cuh"
+#include "ep_decode.cuh"
 #include "aqgemm.cuh"
 
 #include <mutex>
@@ -658,10 +659,11 @@ int side_stream(SideStream **out) {
 // the shared expert -> Ys on `st_shared` when `shared`.
 int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, const void *x,
                      const MoeDims &d, MoeWs &ws, const int32_t *idx, float *Y, bool shared,
-                     cudaStream_t st, cudaStream_t st_shared) {
+                     cudaStream_t st, cudaStream_t st_shared, bool routed = true) {
   const int64_t T = d.T;
   const int round = (cfg->flags & DSV41_MOE_ROUND_BF16) ? 1 : 0;
   int rc;
+  if (routed) {
   // plan
   { ProfScope prof("moe_plan", st);
   DSV41_LAUNCH(launch_pdl(k_moe_plan, dim3(1), dim3(1024), 4 * d.E * sizeof(int), st,
@@ -744,6 +746,7 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
                                      int(d.Cmax * d.tiles_dn * p.nsplit), st);
     if (rc) return rc;
   }
+  }  // routed
   if (!shared) return DSV41_OK;
   // shared expert (fp8 32x32): gate/up -> Hs -> down -> Ys, on its own stream
   st = st_shared;
@@ -914,6 +917,242 @@ extern "C" int dsv41_moe_decode(const dsv41_moe_config *cfg, const dsv41_moe_wei
                             (__nv_bfloat16 *)y),
                  "moe_combine");
   DSV41_CHECK_LAUNCH("moe_combine");
+  return DSV41_OK;
+}
+
+// ======================================================================= EP decode (peer memory)
+
+struct dsv41_ep_ctx {
+  int world = 0, rank = 0, topk = 0;
+  int64_t max_tokens = 0, dim = 0;
+  int device = 0;
+  EpLayout L{};
+  uint8_t *buf = nullptr;                 // this rank's buffer (peers map it)
+  EpPeers peers{};                        // every rank's buffer as seen from this GPU
+  bool opened[EP_MAX_RANKS] = {false};
+  unsigned long long *dseq = nullptr;     // step counter
+  unsigned *done = nullptr;               // [2][world] CTA completion counters
+  bool connected = false;
+};
+
+extern "C" int dsv41_ep_create(int world, int rank, int64_t max_tokens, int topk, int64_t dim,
+                               dsv41_ep_ctx **out) {
+  DSV41_REQUIRE(out, DSV41_ERR_BAD_ARG, "NULL output");
+  *out = nullptr;
+  DSV41_REQUIRE(world >= 1 && world <= EP_MAX_RANKS && rank >= 0 && rank < world,
+                DSV41_ERR_BAD_ARG, "need 1 <= world <= %d and 0 <= rank < world", EP_MAX_RANKS);
+  DSV41_REQUIRE(max_tokens >= 1 && topk >= 1 && topk <= 16 && max_tokens * topk <= 8192 &&
+                    dim > 0 && dim % 8 == 0,
+                DSV41_ERR_UNSUPPORTED, "EP decode needs max_tokens*topk <= 8192 and 8 | dim");
+  auto *c = new dsv41_ep_ctx();
+  c->world = world;
+  c->rank = rank;
+  c->topk = topk;
+  c->max_tokens = max_tokens;
+  c->dim = dim;
+  cudaGetDevice(&c->device);
+  c->L = ep_layout(world, max_tokens * topk, dim);
+  cudaError_t e = cudaMalloc(&c->buf, c->L.total);
+  if (e == cudaSuccess) e = cudaMemset(c->buf, 0, c->L.total);
+  if (e == cudaSuccess) e = cudaMalloc(&c->dseq, sizeof(unsigned long long));
+  if (e == cudaSuccess) e = cudaMemset(c->dseq, 0, sizeof(unsigned long long));
+  if (e == cudaSuccess) e = cudaMalloc(&c->done, sizeof(unsigned) * 2 * world);
+  if (e == cudaSuccess) e = cudaMemset(c->done, 0, sizeof(unsigned) * 2 * world);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    cudaFree(c->buf);
+    cudaFree(c->dseq);
+    cudaFree(c->done);
+    delete c;
+    return cuda_status(e, "EP buffers");
+  }
+  c->peers.base[rank] = c->buf;
+  *out = c;
+  return DSV41_OK;
+}
+
+extern "C" size_t dsv41_ep_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+extern "C" int dsv41_ep_handle(const dsv41_ep_ctx *c, void *handle_out) {
+  DSV41_REQUIRE(c && handle_out, DSV41_ERR_BAD_ARG, "NULL pointer");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, c->buf);
+  if (e != cudaSuccess) return cuda_status(e, "cudaIpcGetMemHandle");
+  memcpy(handle_out, &h, sizeof(h));
+  return DSV41_OK;
+}
+
+extern "C" int dsv41_ep_connect(dsv41_ep_ctx *c, const void *handles) {
+  DSV41_REQUIRE(c && handles, DSV41_ERR_BAD_ARG, "NULL pointer");
+  DSV41_REQUIRE(!c->connected, DSV41_ERR_BAD_ARG, "already connected");
+  const uint8_t *hb = static_cast<const uint8_t *>(handles);
+  for (int r = 0; r < c->world; ++r) {
+    if (r == c->rank) continue;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, hb + r * sizeof(h), sizeof(h));
+    void *p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_status(e, "cudaIpcOpenMemHandle (rank %d)");
+    c->peers.base[r] = static_cast<uint8_t *>(p);
+    c->opened[r] = true;
+  }
+  c->connected = true;
+  return DSV41_OK;
+}
+
+extern "C" int dsv41_ep_destroy(dsv41_ep_ctx *c) {
+  if (!c) return DSV41_OK;
+  cudaDeviceSynchronize();
+  for (int r = 0; r < c->world; ++r)
+    if (c->opened[r]) cudaIpcCloseMemHandle(c->peers.base[r]);
+  cudaFree(c->buf);
+  cudaFree(c->dseq);
+  cudaFree(c->done);
+  delete c;
+  return DSV41_OK;
+}
+
+namespace {
+
+// The owner runs its experts on ws*C received rows (padding rows skipped), one pair each.
+MoeDims ep_owner_dims_decode(const dsv41_moe_config *cfg, const dsv41_ep_ctx *c) {
+  dsv41_moe_config lc = *cfg;
+  lc.n_experts = cfg->n_experts / c->world;
+  lc.topk = 1;
+  return moe_dims(&lc, int64_t(c->world) * c->L.C);
+}
+
+size_t ep_decode_ws_bytes(const dsv41_moe_config *cfg, const dsv41_ep_ctx *c, int64_t T) {
+  const MoeDims dl = moe_dims(cfg, T < 1 ? 1 : T), dw = ep_owner_dims_decode(cfg, c);
+  const size_t a = moe_carve(dl, nullptr, ~size_t(0)).used;
+  const size_t b = moe_carve(dw, nullptr, ~size_t(0)).used;
+  return align_up(a, 256) + align_up(b, 256) + align_up(size_t(dw.T) * 4, 256) +
+         align_up(size_t(c->max_tokens) * c->topk * 4, 256) + 256;
+}
+
+}  // namespace
+
+extern "C" size_t dsv41_moe_ep_decode_workspace_size(const dsv41_moe_config *cfg,
+                                                     const dsv41_ep_ctx *ctx, int64_t T) {
+  if (!cfg || !ctx || cfg->n_experts % ctx->world) return 0;
+  return ep_decode_ws_bytes(cfg, ctx, T);
+}
+
+extern "C" int dsv41_moe_ep_decode(const dsv41_moe_config *cfg, const dsv41_moe_weights *W,
+                                   dsv41_ep_ctx *c, const void *x, int64_t T, int out_dtype,
+                                   void *y, float *weights_out, int32_t *indices_out,
+                                   void *workspace, size_t workspace_bytes, void *stream) {
+  DSV41_REQUIRE(cfg && W && c, DSV41_ERR_BAD_ARG, "NULL config/weights/context");
+  DSV41_REQUIRE(c->connected, DSV41_ERR_BAD_ARG, "EP context is not connected");
+  DSV41_REQUIRE(cfg->topk == c->topk && cfg->dim == c->dim && cfg->n_experts % c->world == 0,
+                DSV41_ERR_BAD_SHAPE, "config does not match the EP context");
+  DSV41_REQUIRE(T >= 0 && T <= c->max_tokens, DSV41_ERR_UNSUPPORTED,
+                "T = %lld exceeds the context's max_tokens %lld", (long long)T,
+                (long long)c->max_tokens);
+  const bool shared = !(cfg->flags & DSV41_MOE_NO_SHARED);
+  dsv41_moe_config lc = *cfg;                 // this rank's experts
+  lc.n_experts = cfg->n_experts / c->world;
+  lc.topk = 1;
+  int rc = moe_check(&lc, W, 1, shared);
+  if (rc) return rc;
+  rc = route_check(T < 1 ? 1 : T, cfg->dim, cfg->n_experts, cfg->topk, cfg->score_func);
+  if (rc) return rc;
+  DSV41_REQUIRE(out_dtype == DSV41_F32 || out_dtype == DSV41_BF16, DSV41_ERR_BAD_DTYPE,
+                "out_dtype must be F32 or BF16");
+  DSV41_REQUIRE((x && y) || T == 0, DSV41_ERR_BAD_ARG, "NULL pointer");
+  DSV41_REQUIRE(W->gate_w, DSV41_ERR_BAD_ARG, "NULL router weight");
+  DSV41_REQUIRE(!x || (aligned(x, 16) && aligned(W->gate_w, 16)), DSV41_ERR_MISALIGNED,
+                "x and gate_w must be 16-byte aligned");
+  const size_t need = ep_decode_ws_bytes(cfg, c, T);
+  DSV41_REQUIRE(workspace && workspace_bytes >= need, DSV41_ERR_WORKSPACE,
+                "workspace too small: need %zu bytes", need);
+  cudaStream_t st = STREAM(stream);
+  const MoeDims dl = moe_dims(cfg, T < 1 ? 1 : T), dw = ep_owner_dims_decode(cfg, c);
+  WsCarve wc{static_cast<uint8_t *>(workspace), workspace_bytes, 0};
+  uint8_t *ws_loc = wc.take<uint8_t>(moe_carve(dl, nullptr, ~size_t(0)).used);
+  uint8_t *ws_own = wc.take<uint8_t>(moe_carve(dw, nullptr, ~size_t(0)).used);
+  int32_t *ids = wc.take<int32_t>(dw.T);
+  int32_t *slot_pos = wc.take<int32_t>(c->max_tokens * c->topk);
+  DSV41_REQUIRE(wc.ok, DSV41_ERR_WORKSPACE, "workspace too small");
+  MoeWs wl = moe_carve(dl, ws_loc, ~size_t(0));
+  MoeWs wo = moe_carve(dw, ws_own, ~size_t(0));
+  float *wts = weights_out ? weights_out : wl.w;
+  int32_t *idx = indices_out ? indices_out : wl.idx;
+  const EpLayout &L = c->L;
+  const int epr = int(cfg->n_experts / c->world);
+
+  // shared expert of this rank's tokens, on the side stream
+  SideStream *side = nullptr;
+  const bool do_shared = shared && T > 0;
+  if (do_shared) {
+    if ((rc = side_stream(&side))) return rc;
+    cudaError_t e = cudaEventRecord(side->fork, st);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(side->s, side->fork, 0);
+    if (e != cudaSuccess) return cuda_status(e, "fork shared expert");
+    rc = moe_experts_impl(cfg, W, x, dl, wl, nullptr, nullptr, true, side->s, side->s, false);
+    if (rc) return rc;
+  }
+  if (T > 0) {
+    rc = route_impl(x, T, cfg->dim, W->gate_w, W->gate_bias, cfg->n_experts, cfg->topk,
+                    cfg->score_func, cfg->gate_temp, cfg->norm_topk_prob, cfg->route_scale, wts,
+                    idx, wl.rpart, st);
+    if (rc) return rc;
+  }
+  // dispatch: rows into the owners' receive buffers
+  const int P = int(T * cfg->topk);
+  {
+    ProfScope prof("ep_dispatch", st);
+    const unsigned nb = unsigned(std::max<int64_t>(1, std::min<int64_t>(16, ceil_div(P, c->world))));
+    k_ep_dispatch<<<dim3(c->world, nb), 256, P * sizeof(int), st>>>(
+        static_cast<const __nv_bfloat16 *>(x), idx, int(T), cfg->topk, epr, c->rank, L, c->peers,
+        c->dseq, slot_pos, c->done);
+    DSV41_CHECK_LAUNCH("ep_dispatch");
+  }
+  {
+    ProfScope prof("ep_wait", st);
+    k_ep_wait<<<1, 64, 0, st>>>(c->buf, L, 0, c->dseq);
+  }
+  DSV41_CHECK_LAUNCH("ep_wait dispatch");
+  // owner: experts on the received rows
+  {
+    ProfScope prof("ep_ids", st);
+    k_ep_ids<<<unsigned(ceil_div(dw.T, 256)), 256, 0, st>>>(c->buf, L, ids);
+  }
+  DSV41_CHECK_LAUNCH("ep_ids");
+  float *Yr = wo.Y;
+  rc = moe_experts_impl(&lc, W, c->buf + L.rows, dw, wo, ids, Yr, false, st, st, true);
+  if (rc) return rc;
+  {
+    ProfScope prof("ep_return", st);
+    const unsigned nb = unsigned(std::max<int64_t>(1, std::min<int64_t>(16, ceil_div(L.C, 4))));
+    k_ep_return<<<dim3(c->world, nb), 256, 0, st>>>(Yr, c->buf, c->rank, L, c->peers, c->dseq,
+                                                     c->done + c->world);
+    DSV41_CHECK_LAUNCH("ep_return");
+  }
+  {
+    ProfScope prof("ep_wait", st);
+    k_ep_wait<<<1, 64, 0, st>>>(c->buf, L, 1, c->dseq);
+  }
+  DSV41_CHECK_LAUNCH("ep_wait return");
+  if (do_shared) {
+    cudaError_t e = cudaEventRecord(side->join, side->s);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(st, side->join, 0);
+    if (e != cudaSuccess) return cuda_status(e, "join shared expert");
+  }
+  {
+    ProfScope prof("ep_combine", st);
+    const int64_t n = T * cfg->dim;
+    const unsigned g = n > 0 ? grid_for(n) : 1;
+    const float *Ys = do_shared ? wl.Ys : nullptr;
+    if (out_dtype == DSV41_F32)
+      k_ep_combine_decode<float><<<g, 256, 0, st>>>(c->buf, L, slot_pos, wts, Ys, T, cfg->topk,
+                                                    static_cast<float *>(y), c->dseq);
+    else
+      k_ep_combine_decode<__nv_bfloat16><<<g, 256, 0, st>>>(c->buf, L, slot_pos, wts, Ys, T,
+                                                            cfg->topk,
+                                                            static_cast<__nv_bfloat16 *>(y), c->dseq);
+    DSV41_CHECK_LAUNCH("ep_combine");
+  }
   return DSV41_OK;
 }
 

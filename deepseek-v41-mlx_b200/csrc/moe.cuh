@@ -46,7 +46,7 @@ __global__ void __launch_bounds__(1024) k_moe_plan(const int32_t *__restrict__ i
   for (int64_t p = threadIdx.x; p < P; p += blockDim.x) {
     const int ex = indices[p];
     if (ex >= 0 && ex < E) atomicAdd(&cnt[ex], 1);
-    else dev_flag(DSV41_DEVST_BAD_INDEX);
+    else if (ex >= E) dev_flag(DSV41_DEVST_BAD_INDEX);   // negative: a padding row, skipped
   }
   __syncthreads();
   const int n = e < E ? cnt[e] : 0;

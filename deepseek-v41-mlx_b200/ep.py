@@ -119,7 +119,8 @@ class EPMoE:
     renumbered 0 .. E/ws-1) plus the replicated router and shared expert.
     """
 
-    def __init__(self, local, world: int, rank: int, n_experts: int, group=None):
+    def __init__(self, local, world: int, rank: int, n_experts: int, group=None,
+                 max_tokens: int = 256, p2p: bool = True):
         import torch.distributed as dist
         self.dist = dist
         self.local = local
@@ -129,6 +130,10 @@ class EPMoE:
         self.group = group
         self.local_active = []
         self.track = False
+        self.max_tokens = max_tokens      # decode tokens per rank and call (peer-memory path)
+        self.p2p = p2p
+        self._ctx = None
+        self._ws = None
 
     # ---------------------------------------------------------------- GPU path
     @classmethod
@@ -284,10 +289,71 @@ class EPMoE:
                D, L.dtype_code(odt), L.ptr(out), L.stream_of(xf))
         return out.reshape(tuple(x.shape[:-1]) + (D,))
 
+    # ---------------------------------------------------------------- decode over peer memory
+    def _ensure_ctx(self, dev):
+        """This rank's exchange buffer, with every peer's buffer mapped (collective: every rank
+        calls it once, on the first decode step)."""
+        if self._ctx is not None:
+            return self._ctx
+        t = L.torch()
+        lib = L.load()
+        ctx = C.c_void_p()
+        L.call("dsv41_ep_create", self.world, self.rank, self.max_tokens, self.topk,
+               self.local.dim, C.byref(ctx))
+        nb = int(lib.dsv41_ep_handle_bytes())
+        h = (C.c_uint8 * nb)()
+        L.call("dsv41_ep_handle", ctx, C.cast(h, C.c_void_p))
+        mine = t.tensor(list(bytes(h)), dtype=t.uint8, device=dev)
+        every = t.empty(nb * self.world, dtype=t.uint8, device=dev)
+        self.dist.all_gather_into_tensor(every, mine, group=self.group)
+        hb = (C.c_uint8 * (nb * self.world)).from_buffer_copy(bytes(every.cpu().numpy().tobytes()))
+        L.call("dsv41_ep_connect", ctx, C.cast(hb, C.c_void_p))
+        self.dist.barrier(group=self.group)            # every peer mapped before any step
+        self._ctx = ctx
+        return ctx
+
+    def close(self):
+        """Unmap the peers and free the exchange buffer (collective)."""
+        if self._ctx is not None:
+            L.torch().cuda.synchronize()
+            self.dist.barrier(group=self.group)
+            L.call("dsv41_ep_destroy", self._ctx)
+            self._ctx = None
+
+    def _forward_p2p(self, xf, odt):
+        """One decode step: dsv41_moe_ep_decode (pairs to their owners and back through
+        NVLink peer stores, no host synchronisation)."""
+        t = L.torch()
+        lib = L.load()
+        T, D = xf.shape
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens exceed max_tokens={self.max_tokens} of the EP buffers")
+        ctx = self._ensure_ctx(xf.device)
+        m = self.local
+        cfg, W = m._decode_args()                      # shared + this rank's experts
+        cfg.n_experts = self.E
+        W.gate_w, W.gate_bias = L.ptr(self.gate_w), L.ptr(self.gate_b)
+        need = int(lib.dsv41_moe_ep_decode_workspace_size(C.byref(cfg), ctx, T))
+        if self._ws is None or self._ws.numel() < need or self._ws.device != xf.device:
+            self._ws = L.workspace(need, xf.device)
+        k = self.topk
+        y = t.empty((T, D), dtype=odt, device=xf.device)
+        w = t.empty((T, k), dtype=t.float32, device=xf.device)
+        idx = t.empty((T, k), dtype=t.int32, device=xf.device)
+        L.call("dsv41_moe_ep_decode", C.byref(cfg), C.byref(W), ctx, L.ptr(xf) if T else None, T,
+               L.dtype_code(odt), L.ptr(y) if T else None, L.ptr(w) if T else None,
+               L.ptr(idx) if T else None, L.ptr(self._ws), self._ws.numel(), L.stream_of(xf))
+        return y, w, idx
+
     def forward(self, x, expert_fn=None, with_routing=False):
         t = L.torch()
-        xf = x.reshape(-1, x.shape[-1]).to(t.bfloat16)
+        xf = x.reshape(-1, x.shape[-1]).to(t.bfloat16).contiguous()
         T = xf.shape[0]
+        if expert_fn is None and not self.track and self.p2p and xf.is_cuda:
+            odt = t.float32 if x.dtype == t.float32 else t.bfloat16
+            y, w, idx = self._forward_p2p(xf, odt)
+            out = y.reshape(x.shape)
+            return (out, w, idx) if with_routing else out
         w, idx = self.route(xf)
         rows, ids, order, sc, rc = dispatch(self.dist, xf, idx, self.world, self.epr, self.group)
         if self.track:

@@ -305,6 +305,34 @@ int dsv41_moe_ep_combine(const void *back, const int32_t *slot_pos, const int32_
                          const void *shared, int64_t T, int topk, int64_t dim, int out_dtype,
                          void *y, void *stream);
 
+/* ---- (e) expert-parallel decode over NVLink peer memory (replaces upstream's replicate +
+ * fp32 all_reduce, docs/reference/model.py:854-904, at decode).  One context per rank:
+ * dsv41_ep_create allocates this rank's exchange buffer (rows it receives, outputs it gets
+ * back, step flags); every rank exports its IPC handle (dsv41_ep_handle,
+ * dsv41_ep_handle_bytes() bytes), the caller gathers them in rank order (e.g. an
+ * all_gather) and each rank maps its peers' buffers with dsv41_ep_connect.  One MoE decode
+ * step is then dsv41_moe_ep_decode on every rank (a collective: all ranks call it the same
+ * number of times, T may differ per rank): route the rank's own tokens with the replicated
+ * router, write each (token, expert) row into the owning rank's buffer, run this rank's
+ * experts (cfg->n_experts / world of them, w holding only those, renumbered from 0) on the
+ * rows it received, write the fp32 outputs back into the sources' buffers, and sum each
+ * token's outputs in top-k order with the shared expert -- the same fp32 operations as
+ * dsv41_moe_decode on one GPU.  No host synchronisation; waits for peers are bounded (on
+ * expiry the device status bit 0 is raised).  cfg->n_experts is the total expert count. */
+typedef struct dsv41_ep_ctx dsv41_ep_ctx;
+int dsv41_ep_create(int world, int rank, int64_t max_tokens, int topk, int64_t dim,
+                    dsv41_ep_ctx **out);
+size_t dsv41_ep_handle_bytes(void);
+int dsv41_ep_handle(const dsv41_ep_ctx *ctx, void *handle_out);
+int dsv41_ep_connect(dsv41_ep_ctx *ctx, const void *handles);
+int dsv41_ep_destroy(dsv41_ep_ctx *ctx);
+size_t dsv41_moe_ep_decode_workspace_size(const dsv41_moe_config *cfg, const dsv41_ep_ctx *ctx,
+                                          int64_t T);
+int dsv41_moe_ep_decode(const dsv41_moe_config *cfg, const dsv41_moe_weights *w,
+                        dsv41_ep_ctx *ctx, const void *x, int64_t T, int out_dtype, void *y,
+                        float *weights_out, int32_t *indices_out, void *workspace,
+                        size_t workspace_bytes, void *stream);
+
 /* ---- a15: engram hasher (deepseek_v41_mlx/engram.py:154-180; upstream
  * docs/reference/engram.py NgramHashState.forward).  input_ids int64 [B, L];
  * token_map int64 [V]; ids_cache int64 [B, max_seq], positions
