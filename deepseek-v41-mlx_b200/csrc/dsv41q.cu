@@ -659,7 +659,8 @@ int side_stream(SideStream **out) {
 // the shared expert -> Ys on `st_shared` when `shared`.
 int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, const void *x,
                      const MoeDims &d, MoeWs &ws, const int32_t *idx, float *Y, bool shared,
-                     cudaStream_t st, cudaStream_t st_shared, bool routed = true) {
+                     cudaStream_t st, cudaStream_t st_shared, bool routed = true,
+                     const int32_t *tok_map = nullptr) {
   const int64_t T = d.T;
   const int round = (cfg->flags & DSV41_MOE_ROUND_BF16) ? 1 : 0;
   int rc;
@@ -667,7 +668,7 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
   // plan
   { ProfScope prof("moe_plan", st);
   DSV41_LAUNCH(launch_pdl(k_moe_plan, dim3(1), dim3(1024), 4 * d.E * sizeof(int), st,
-                          static_cast<const int32_t *>(idx), T, cfg->topk, d.E, ws.plan),
+                          static_cast<const int32_t *>(idx), T, cfg->topk, d.E, ws.plan, tok_map),
                "moe_plan"); }
   DSV41_CHECK_LAUNCH("moe_plan");
   // activations gathered per pair
@@ -1026,7 +1027,7 @@ size_t ep_decode_ws_bytes(const dsv41_moe_config *cfg, const dsv41_ep_ctx *c, in
   const MoeDims dl = moe_dims(cfg, T < 1 ? 1 : T), dw = ep_owner_dims_decode(cfg, c);
   const size_t a = moe_carve(dl, nullptr, ~size_t(0)).used;
   const size_t b = moe_carve(dw, nullptr, ~size_t(0)).used;
-  return align_up(a, 256) + align_up(b, 256) + align_up(size_t(dw.T) * 4, 256) +
+  return align_up(a, 256) + align_up(b, 256) + 2 * align_up(size_t(dw.T) * 4, 256) +
          align_up(size_t(c->max_tokens) * c->topk * 4, 256) + 256;
 }
 
@@ -1072,6 +1073,7 @@ extern "C" int dsv41_moe_ep_decode(const dsv41_moe_config *cfg, const dsv41_moe_
   uint8_t *ws_loc = wc.take<uint8_t>(moe_carve(dl, nullptr, ~size_t(0)).used);
   uint8_t *ws_own = wc.take<uint8_t>(moe_carve(dw, nullptr, ~size_t(0)).used);
   int32_t *ids = wc.take<int32_t>(dw.T);
+  int32_t *rowmap = wc.take<int32_t>(dw.T);
   int32_t *slot_pos = wc.take<int32_t>(c->max_tokens * c->topk);
   DSV41_REQUIRE(wc.ok, DSV41_ERR_WORKSPACE, "workspace too small");
   MoeWs wl = moe_carve(dl, ws_loc, ~size_t(0));
@@ -1116,11 +1118,11 @@ extern "C" int dsv41_moe_ep_decode(const dsv41_moe_config *cfg, const dsv41_moe_
   // owner: experts on the received rows
   {
     ProfScope prof("ep_ids", st);
-    k_ep_ids<<<unsigned(ceil_div(dw.T, 256)), 256, 0, st>>>(c->buf, L, ids);
+    k_ep_ids<<<unsigned(ceil_div(dw.T, 256)), 256, 0, st>>>(c->buf, L, ids, rowmap);
   }
   DSV41_CHECK_LAUNCH("ep_ids");
   float *Yr = wo.Y;
-  rc = moe_experts_impl(&lc, W, c->buf + L.rows, dw, wo, ids, Yr, false, st, st, true);
+  rc = moe_experts_impl(&lc, W, c->buf + L.rows, dw, wo, ids, Yr, false, st, st, true, rowmap);
   if (rc) return rc;
   {
     ProfScope prof("ep_return", st);

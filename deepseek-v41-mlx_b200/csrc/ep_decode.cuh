@@ -164,27 +164,50 @@ __global__ void k_ep_wait(const uint8_t *own, EpLayout L, int which,
   dev_flag(DSV41_DEVST_TIMEOUT);
 }
 
-// Owner side: expert id per received row, -1 past each source's count (padding, skipped).
-__global__ void k_ep_ids(const uint8_t *own, EpLayout L, int32_t *__restrict__ ids) {
-  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (i >= L.ws * L.C) return;
-  const int s = int(i / L.C);
-  const int n = reinterpret_cast<const int32_t *>(own + L.cnt)[s];
-  ids[i] = (i % L.C) < n ? reinterpret_cast<const int32_t *>(own + L.meta)[i] : -1;
+// Received rows of source s, before it: the rows of sources 0 .. s-1 (compact order).
+__device__ __forceinline__ int ep_rows_before(const uint8_t *own, const EpLayout &L, int s) {
+  const int32_t *cnt = reinterpret_cast<const int32_t *>(own + L.cnt);
+  int b = 0;
+  for (int r = 0; r < s; ++r) b += cnt[r];
+  return b;
 }
 
-// Owner side.  grid (ws sources, nb), 256 threads: the fp32 outputs of source s's rows go
-// back into source s's return buffer at [this rank][i].
+// Owner side: the received rows listed compactly, source by source -- ids[j] the owner-local
+// expert of the j-th valid row and rowmap[j] its row in the receive buffer; -1 ids after
+// the last valid row (padding, skipped), so the plan's ranking only scans real pairs.
+__global__ void k_ep_ids(const uint8_t *own, EpLayout L, int32_t *__restrict__ ids,
+                         int32_t *__restrict__ rowmap) {
+  const int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (j >= L.ws * L.C) return;
+  const int32_t *cnt = reinterpret_cast<const int32_t *>(own + L.cnt);
+  int64_t before = 0;
+  for (int s = 0; s < L.ws; ++s) {
+    const int n = cnt[s];
+    if (j < before + n) {
+      const int64_t row = s * L.C + (j - before);
+      ids[j] = reinterpret_cast<const int32_t *>(own + L.meta)[row];
+      rowmap[j] = int32_t(row);
+      return;
+    }
+    before += n;
+  }
+  ids[j] = -1;
+  rowmap[j] = 0;
+}
+
+// Owner side.  grid (ws sources, nb), 256 threads: the fp32 outputs of source s's rows
+// (compact rows before(s) + i) go back into source s's return buffer at [this rank][i].
 __global__ void __launch_bounds__(256) k_ep_return(
     const float *__restrict__ Y, const uint8_t *own, int rank, EpLayout L, EpPeers peers,
     const unsigned long long *__restrict__ dseq, unsigned *__restrict__ done) {
   const int s = blockIdx.x, b = blockIdx.y, nb = gridDim.y;
   const int n = reinterpret_cast<const int32_t *>(own + L.cnt)[s];
+  const int64_t y0 = ep_rows_before(own, L, s);       // Y rows are in compact order
   uint8_t *dst = peers.base[s];
   const unsigned long long seq = *dseq + 1;
   float *back = reinterpret_cast<float *>(dst + L.back) + (int64_t)rank * L.C * L.D;
   for (int i = b; i < n; i += nb)
-    cta_copy16(back + (int64_t)i * L.D, Y + ((int64_t)s * L.C + i) * L.D, L.D * 4);
+    cta_copy16(back + (int64_t)i * L.D, Y + (y0 + i) * L.D, L.D * 4);
   ep_publish(done, s, nb,
              reinterpret_cast<unsigned long long *>(dst + L.flags) + L.ws + rank, seq);
 }

@@ -29,8 +29,11 @@ constexpr int MOE_DN_CHUNK = 4;
 // One CTA of 1024 threads (E <= 1024).  Deterministic: a pair's rank inside its
 // expert is the number of earlier pairs (row-major over [T, k]) routed to the same
 // expert.  Offsets come from block-wide exclusive scans over the experts.
+// tok_map (optional): the activation row of pair p's token, instead of p / topk (expert-
+// parallel owners list their received rows compactly, valid rows first).
 __global__ void __launch_bounds__(1024) k_moe_plan(const int32_t *__restrict__ indices, int64_t T,
-                                                   int topk, int64_t E, MoePlan plan) {
+                                                   int topk, int64_t E, MoePlan plan,
+                                                   const int32_t *__restrict__ tok_map) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ int sh[];
@@ -118,7 +121,7 @@ __global__ void __launch_bounds__(1024) k_moe_plan(const int32_t *__restrict__ i
     int rank = 0;
     for (int64_t p2 = 0; p2 < p; ++p2) rank += (indices[p2] == ex);
     const int q = poff[ex] + rank;
-    plan.pair_tok[q] = int(p / topk);
+    plan.pair_tok[q] = tok_map ? tok_map[p] : int(p / topk);
     plan.pair_row[q] = int(p);
   }
 }
