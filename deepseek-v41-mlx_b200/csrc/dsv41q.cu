@@ -462,7 +462,7 @@ extern "C" int dsv41_gemv_affine(const void *x, int64_t M, int64_t K, const uint
 namespace {
 int router_nks(int64_t T, int64_t K, int64_t E) {
   const int64_t base = ceil_div(E, 16) * ceil_div(T, 8);
-  const int64_t target = 4 * (int64_t)num_sms();
+  const int64_t target = 8 * (int64_t)num_sms();
   int64_t want = ceil_div(target, base);
   const int64_t k32 = K / 32;
   int64_t best = 1;
@@ -989,11 +989,9 @@ extern "C" int dsv41_ep_connect(dsv41_ep_ctx *c, const void *handles) {
   const uint8_t *hb = static_cast<const uint8_t *>(handles);
   for (int r = 0; r < c->world; ++r) {
     if (r == c->rank) continue;
-    cudaIpcMemHandle_t h;
-    memcpy(&h, hb + r * sizeof(h), sizeof(h));
     void *p = nullptr;
-    cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
-    if (e != cudaSuccess) return cuda_status(e, "cudaIpcOpenMemHandle (rank %d)");
+    const int rc = dsv41_ipc_import(hb + r * sizeof(cudaIpcMemHandle_t), &p);
+    if (rc) return rc;
     c->peers.base[r] = static_cast<uint8_t *>(p);
     c->opened[r] = true;
   }
@@ -1005,7 +1003,7 @@ extern "C" int dsv41_ep_destroy(dsv41_ep_ctx *c) {
   if (!c) return DSV41_OK;
   cudaDeviceSynchronize();
   for (int r = 0; r < c->world; ++r)
-    if (c->opened[r]) cudaIpcCloseMemHandle(c->peers.base[r]);
+    if (c->opened[r]) dsv41_ipc_close(c->peers.base[r]);
   cudaFree(c->buf);
   cudaFree(c->dseq);
   cudaFree(c->done);
@@ -2041,6 +2039,117 @@ extern "C" int dsv41_engram_gather_sum(const uint8_t *table, const uint8_t *scal
   DSV41_REQUIRE(block > 0, DSV41_ERR_BAD_SHAPE, "block must be positive");
   return engram_sum_launch(table, scale, rows, row_lo, d, block, d, d / block, idx, n_tok,
                            n_per_tok, out_dtype, out, STREAM(stream));
+}
+
+// ---- CUDA IPC of a caller's allocation (any pointer inside it): the handle names the whole
+// allocation, the offset locates the pointer in it.
+static PFN_cuMemGetAddressRange_v3020 g_addr_range = nullptr;
+
+extern "C" int dsv41_ipc_export(const void *ptr, void *handle_out, int64_t *offset_out) {
+  DSV41_REQUIRE(ptr && handle_out && offset_out, DSV41_ERR_BAD_ARG, "NULL pointer");
+  if (!g_addr_range) {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q);
+    DSV41_REQUIRE(e == cudaSuccess && fn && q == cudaDriverEntryPointSuccess, DSV41_ERR_CUDA,
+                  "cuMemGetAddressRange unavailable");
+    g_addr_range = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  CUresult r = g_addr_range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr));
+  DSV41_REQUIRE(r == CUDA_SUCCESS, DSV41_ERR_CUDA, "cuMemGetAddressRange failed (%d)", (int)r);
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void *>(base));
+  if (e != cudaSuccess) return cuda_status(e, "cudaIpcGetMemHandle");
+  memcpy(handle_out, &h, sizeof(h));
+  *offset_out = int64_t(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return DSV41_OK;
+}
+
+// A handle is opened once per process and device; later imports of the same handle share the
+// mapping (reference-counted), the last close unmaps it.
+struct IpcMapping {
+  int device;
+  cudaIpcMemHandle_t handle;
+  void *base;
+  int refs;
+};
+static IpcMapping g_ipc[256];
+static int g_ipc_n = 0;
+static std::mutex g_ipc_mu;
+
+extern "C" int dsv41_ipc_import(const void *handle, void **base_out) {
+  DSV41_REQUIRE(handle && base_out, DSV41_ERR_BAD_ARG, "NULL pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(g_ipc_mu);
+  for (int i = 0; i < g_ipc_n; ++i)
+    if (g_ipc[i].refs > 0 && g_ipc[i].device == dev && !memcmp(&g_ipc[i].handle, &h, sizeof(h))) {
+      ++g_ipc[i].refs;
+      *base_out = g_ipc[i].base;
+      return DSV41_OK;
+    }
+  int slot = -1;
+  for (int i = 0; i < g_ipc_n && slot < 0; ++i)
+    if (g_ipc[i].refs == 0) slot = i;
+  if (slot < 0) {
+    DSV41_REQUIRE(g_ipc_n < 256, DSV41_ERR_UNSUPPORTED, "more than 256 peer mappings");
+    slot = g_ipc_n++;
+  }
+  cudaError_t e = cudaIpcOpenMemHandle(base_out, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_status(e, "cudaIpcOpenMemHandle");
+  g_ipc[slot] = IpcMapping{dev, h, *base_out, 1};
+  return DSV41_OK;
+}
+
+extern "C" int dsv41_ipc_close(void *base) {
+  DSV41_REQUIRE(base, DSV41_ERR_BAD_ARG, "NULL pointer");
+  std::lock_guard<std::mutex> lock(g_ipc_mu);
+  for (int i = 0; i < g_ipc_n; ++i)
+    if (g_ipc[i].refs > 0 && g_ipc[i].base == base) {
+      if (--g_ipc[i].refs == 0) return cuda_status(cudaIpcCloseMemHandle(base), "cudaIpcCloseMemHandle");
+      return DSV41_OK;
+    }
+  return set_error(DSV41_ERR_BAD_ARG, "not a mapping made by dsv41_ipc_import");
+}
+
+extern "C" int dsv41_engram_gather_sum_peers(const uint64_t *tables, const uint64_t *scales, int nsh,
+                                             int64_t rows, int64_t total, int64_t d, int64_t block,
+                                             const int64_t *idx, int64_t n_tok, int n_per_tok,
+                                             int out_dtype, void *out, void *stream) {
+  DSV41_REQUIRE(d == 256 || d == 512 || d == 1024, DSV41_ERR_UNSUPPORTED,
+                "gather_sum supports d in {256, 512, 1024}");
+  DSV41_REQUIRE(nsh >= 1 && rows >= 1 && total >= 0 && total <= rows * nsh && block >= 8 &&
+                    block % 8 == 0 && d % block == 0 && n_per_tok >= 1,
+                DSV41_ERR_BAD_SHAPE, "need shards, 8 | block and block | d");
+  DSV41_REQUIRE(out_dtype == DSV41_F32 || out_dtype == DSV41_BF16, DSV41_ERR_BAD_DTYPE,
+                "out_dtype must be F32 or BF16");
+  if (n_tok == 0) return DSV41_OK;
+  DSV41_REQUIRE(tables && scales && idx && out, DSV41_ERR_BAD_ARG, "NULL pointer");
+  DSV41_REQUIRE(aligned(out, 16), DSV41_ERR_MISALIGNED, "out must be 16-byte aligned");
+  cudaStream_t st = STREAM(stream);
+  ProfScope prof("engram_gather_sum_peers", st);
+  const int ch = d == 256 ? 1 : 2;
+  const unsigned blocks = unsigned(ceil_div(n_tok * (d / (256 * ch)) * 32, 256));
+  const auto *tabs = reinterpret_cast<const uint8_t *const *>(tables);
+  const auto *scs = reinterpret_cast<const uint8_t *const *>(scales);
+#define GSP(T, CHV)                                                                             \
+  k_engram_gather_sum<T, CHV, true><<<blocks, 256, 0, st>>>(nullptr, nullptr, rows, 0, d, block, d, \
+                                                            d / block, idx, n_tok, n_per_tok,       \
+                                                            (T *)out, tabs, scs, nsh, total)
+  if (out_dtype == DSV41_F32) {
+    if (ch == 1) GSP(float, 1);
+    else GSP(float, 2);
+  } else {
+    if (ch == 1) GSP(__nv_bfloat16, 1);
+    else GSP(__nv_bfloat16, 2);
+  }
+#undef GSP
+  DSV41_CHECK_LAUNCH("engram_gather_sum_peers");
+  return DSV41_OK;
 }
 
 // ---- row-sharded table: raw rows travel from their owners to the ranks that sum them

@@ -144,11 +144,18 @@ __global__ void k_engram_gather_rows(const uint8_t *__restrict__ table,
 // Warps per token = d / (256 * CH): a warp covers 256 * CH columns, its lanes 8-column
 // chunks at c*256 + lane*8 (coalesced 256-byte spans); rows summed in column order, fp32,
 // 8 rows in flight per warp, table rows streamed (read once, not kept in L1/L2).
-template <typename T, int CH>
+// PEERS: the table is sharded over ranks by rows (rank r holds rows [r*rows, (r+1)*rows),
+// `rows` = the shard size); row id's codes and scales are read from shard id / rows through
+// the pointer arrays tabs / scs (other ranks' shards mapped into this process: peer loads
+// over NVLink); ids at or past `total` (the table's rows) read as zero rows; table / scale /
+// row_lo unused.
+template <typename T, int CH, bool PEERS = false>
 __global__ void __launch_bounds__(256) k_engram_gather_sum(
     const uint8_t *__restrict__ table, const uint8_t *__restrict__ scale, int64_t rows,
     int64_t row_lo, int64_t D, int64_t block, int64_t tld, int64_t sld,
-    const int64_t *__restrict__ idx, int64_t n_tok, int n_per_tok, T *__restrict__ out) {
+    const int64_t *__restrict__ idx, int64_t n_tok, int n_per_tok, T *__restrict__ out,
+    const uint8_t *const *__restrict__ tabs = nullptr,
+    const uint8_t *const *__restrict__ scs = nullptr, int nsh = 0, int64_t total = 0) {
   const int64_t gw = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int wpt = int(D / (256 * CH));
@@ -166,24 +173,34 @@ __global__ void __launch_bounds__(256) k_engram_gather_sum(
   for (int h = 0; h < n_per_tok; h += 8) {
     uint64_t v[8][CH];
     bool in[8];
+    const uint8_t *rt[8], *rs[8];         // this row's codes and scales
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int hh = h + u;
-      const int64_t local = hh < n_per_tok ? ti[hh] - row_lo : -1;
-      in[u] = hh < n_per_tok && local >= 0 && local < rows;
+      const int64_t id = hh < n_per_tok ? ti[hh] : -1;
+      if (PEERS) {
+        const int64_t sh = id >= 0 ? id / rows : -1, local = id - sh * rows;
+        in[u] = id >= 0 && id < total && sh < nsh;   // the last shard may be shorter
+        rt[u] = in[u] ? tabs[sh] + local * tld : table;
+        rs[u] = in[u] ? scs[sh] + local * sld : scale;
+      } else {
+        const int64_t local = id - row_lo;
+        in[u] = hh < n_per_tok && local >= 0 && local < rows;
+        rt[u] = table + local * tld;
+        rs[u] = scale + local * sld;
+      }
 #pragma unroll
       for (int c = 0; c < CH; ++c)
         v[u][c] = in[u] ? __ldcs(reinterpret_cast<const unsigned long long *>(
-                              table + local * tld + col0 + c * 256 + lane * 8))
+                              rt[u] + col0 + c * 256 + lane * 8))
                         : 0ull;
     }
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       if (!in[u]) continue;
-      const int64_t local = ti[h + u] - row_lo;
 #pragma unroll
       for (int c = 0; c < CH; ++c) {
-        const float s = e8m0f(scale[local * sld + soff[c]]);
+        const float s = e8m0f(rs[u][soff[c]]);
         uint32_t hq[4];
         e4m3x4_to_f16x4(uint32_t(v[u][c]), hq[0], hq[1]);
         e4m3x4_to_f16x4(uint32_t(v[u][c] >> 32), hq[2], hq[3]);

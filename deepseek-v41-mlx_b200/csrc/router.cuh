@@ -36,6 +36,7 @@ __global__ void __launch_bounds__(128) k_router_scores(const __nv_bfloat16 *__re
   const __nv_bfloat16 *w1 = w + (e0 + g + 8) * K + kbeg + 8 * t;
   const __nv_bfloat16 *xx = x + (t0 + g) * K + kbeg + 8 * t;
   float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
   for (int64_t k = 0; k < klen; k += 64) {
     uint4 a0[2], a1[2], b[2];
 #pragma unroll
@@ -107,7 +108,8 @@ __global__ void k_router_select(const float *__restrict__ partial, int nks, int6
   const bool valid = e < E;
   float s = 0.0f;
   if (valid) {
-    for (int ks = 0; ks < nks; ++ks) s += partial[((int64_t)ks * T + tok) * E + e];
+#pragma unroll 16
+    for (int ks = 0; ks < nks; ++ks) s += partial[((int64_t)ks * T + tok) * E + e];   // loads in flight, adds in order
     s = __fdiv_rn(s, gate_temp);
   }
   float score;

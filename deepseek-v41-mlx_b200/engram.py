@@ -21,6 +21,8 @@
 
 from __future__ import annotations
 
+import ctypes as C
+
 import numpy as np
 
 from . import _lib as L
@@ -232,6 +234,8 @@ class ParallelEngramEmbedding:
         self.weight = None
         self.scale = None
         self.ops = ops if ops is not None else _CudaRowOps()
+        self.peers = ops is None          # CUDA shards: read peers' rows in place (NVLink)
+        self._peer = None                 # (table ptrs, scale ptrs, mapped bases, key)
 
     def plan(self, idx2):
         """idx2 int64 [T, H] (same on every rank) -> the exchange for this rank.
@@ -280,10 +284,86 @@ class ParallelEngramEmbedding:
         self.dist.all_gather_into_tensor(full, part_out, group=self.group)
         return full[:n_total]
 
+    # ------------------------------------------------------------ peer-memory form
+    def _map_peers(self, dev):
+        """Map every rank's shard (codes and scales) into this process (collective, once; call
+        remap() after replacing ``weight`` / ``scale``)."""
+        t = L.torch()
+        lib = L.load()
+        w = L.u8(L.cuda_tensor(self.weight, "weight"))
+        sc = L.u8(L.cuda_tensor(self.scale, "scale"))
+        key = (w.data_ptr(), sc.data_ptr())
+        if self._peer is not None and self._peer[3] == key:
+            return self._peer
+        need = max(0, min(self.part, self.num_embeddings - self.rank * self.part))
+        if w.shape[0] < need or sc.shape[0] < need:
+            raise ValueError(f"shard has {w.shape[0]} rows, expected {need} (of {self.part})")
+        nb = int(lib.dsv41_ep_handle_bytes())
+        rec = []
+        for a in (w, sc):
+            h = (C.c_uint8 * nb)()
+            off = C.c_int64(0)
+            L.call("dsv41_ipc_export", L.ptr(a), C.cast(h, C.c_void_p), C.byref(off))
+            rec.append(bytes(h) + int(off.value).to_bytes(8, "little"))
+        mine = t.tensor(list(rec[0] + rec[1]), dtype=t.uint8, device=dev)
+        every = t.empty(mine.numel() * self.world, dtype=t.uint8, device=dev)
+        self.dist.all_gather_into_tensor(every, mine, group=self.group)
+        allb = bytes(every.cpu().numpy().tobytes())
+        per = len(rec[0])
+        opened = {}                       # handle bytes -> mapped base (one import each)
+        ptrs = [[], []]
+        for r in range(self.world):
+            for j, a in enumerate((w, sc)):
+                blob = allb[(2 * r + j) * per:(2 * r + j + 1) * per]
+                if r == self.rank:
+                    ptrs[j].append(a.data_ptr())
+                    continue
+                hnd, off = blob[:nb], int.from_bytes(blob[nb:], "little")
+                if hnd not in opened:
+                    base = C.c_void_p()
+                    hb = (C.c_uint8 * nb).from_buffer_copy(hnd)
+                    L.call("dsv41_ipc_import", C.cast(hb, C.c_void_p), C.byref(base))
+                    opened[hnd] = base.value
+                ptrs[j].append(opened[hnd] + off)
+        tabs = t.tensor(ptrs[0], dtype=t.int64, device=dev)
+        scs = t.tensor(ptrs[1], dtype=t.int64, device=dev)
+        self.dist.barrier(group=self.group)
+        self._peer = (tabs, scs, list(opened.values()), key, w, sc)
+        return self._peer
+
+    def remap(self):
+        """Unmap the peers' shards (collective); the next lookup maps them again."""
+        if self._peer is not None:
+            L.torch().cuda.synchronize()
+            self.dist.barrier(group=self.group)
+            for base in self._peer[2]:
+                L.call("dsv41_ipc_close", base)
+            self._peer = None
+
+    def _peer_sum(self, idx2, odt):
+        """This rank's token slice summed from the shards in place, then all-gathered."""
+        t = L.torch()
+        tabs, scs = self._map_peers(idx2.device)[:2]
+        T, H = idx2.shape
+        per = max(1, -(-T // self.world))
+        t0 = min(T, self.rank * per)
+        t1 = min(T, t0 + per)
+        part_out = t.zeros((per, self.dim), dtype=odt, device=idx2.device)
+        if t1 > t0:
+            sl = idx2[t0:t1].contiguous()
+            L.call("dsv41_engram_gather_sum_peers", L.ptr(tabs), L.ptr(scs), self.world,
+                   self.part, self.num_embeddings, self.dim, self.block, L.ptr(sl), t1 - t0, H,
+                   L.dtype_code(odt),
+                   L.ptr(part_out), L.stream_of(sl))
+        return self._gather_all(part_out, T)
+
     def gather_sum(self, indices, out_dtype=None):
         """indices [..., H] -> [..., dim]: each token's H rows summed in head order (fp32)."""
         t = L.torch()
         idx2 = indices.reshape(-1, indices.shape[-1]).to(t.int64)
+        if self.peers and idx2.is_cuda and self.dim in (256, 512, 1024):
+            out = self._peer_sum(idx2, out_dtype or t.bfloat16)
+            return out.reshape(tuple(indices.shape[:-1]) + (self.dim,))
         plan, recv = self._exchange(idx2)
         odt = out_dtype or t.bfloat16
         part_out = t.zeros((plan["per"], self.dim), dtype=odt, device=idx2.device)
@@ -297,6 +377,9 @@ class ParallelEngramEmbedding:
         """indices [...] -> [..., dim] rows (bf16 as upstream returns them)."""
         t = L.torch()
         idx2 = indices.reshape(-1, 1).to(t.int64)
+        if self.peers and idx2.is_cuda and self.dim in (256, 512, 1024):
+            out = self._peer_sum(idx2, out_dtype or t.bfloat16)     # one row per "token"
+            return out.reshape(tuple(indices.shape) + (self.dim,))
         plan, recv = self._exchange(idx2)
         odt = out_dtype or t.bfloat16
         part_out = t.zeros((plan["per"], self.dim), dtype=odt, device=idx2.device)

@@ -383,6 +383,25 @@ int dsv41_engram_dequant_rows(const void *packed, int64_t n_rows, int64_t d, int
                               const int64_t *pos, int64_t n, int out_dtype, void *out,
                               void *stream);
 
+/* ---- (e) row-sharded engram table read in place through NVLink peer memory: every rank maps
+ * the other ranks' shards (CUDA IPC) once, then sums the rows of its own slice of the tokens
+ * reading each row from the GPU that holds it -- no row packing, no exchange of rows, no
+ * host synchronisation (the callers all-gather the slices).  tables / scales: device arrays
+ * of nsh pointers (uint64) to shard s's codes u8 [rows, d] and scales u8 [rows, d/block]
+ * (shard s holds global rows [s*rows, (s+1)*rows), the last one possibly fewer: ids at or past
+ * total, the table's row count, read as zero rows); otherwise as dsv41_engram_gather_sum.
+ * dsv41_ipc_export gives the IPC handle (dsv41_ep_handle_bytes() bytes) of the allocation
+ * holding ptr and ptr's offset in it; dsv41_ipc_import maps a peer's allocation (its base;
+ * add the offset), dsv41_ipc_close unmaps it.  Each allocation is imported once per process. */
+int dsv41_ipc_export(const void *ptr, void *handle_out, int64_t *offset_out);
+int dsv41_ipc_import(const void *handle, void **base_out);
+int dsv41_ipc_close(void *base);
+int dsv41_engram_gather_sum_peers(const uint64_t *tables, const uint64_t *scales, int nsh,
+                                  int64_t rows, int64_t total, int64_t d, int64_t block,
+                                  const int64_t *idx,
+                                  int64_t n_tok, int n_per_tok, int out_dtype, void *out,
+                                  void *stream);
+
 #ifdef __cplusplus
 }
 #endif
