@@ -100,7 +100,6 @@ __global__ void k_router_select(const float *__restrict__ partial, int nks, int6
   pdl_wait();
   pdl_trigger();
   __shared__ float red[32];
-  __shared__ ArgMax redm[32];
   __shared__ float sel_score[64];
   __shared__ int sel_idx[64];
   const int64_t tok = blockIdx.x;
@@ -127,26 +126,68 @@ __global__ void k_router_select(const float *__restrict__ partial, int nks, int6
   }
   float biased = valid ? score + (bias ? bias[e] : 0.0f) : -INFINITY;
   if (isnan(biased)) biased = -INFINITY;
-  for (int j = 0; j < topk; ++j) {
-    ArgMax a{biased, valid ? e : 0x7fffffff};
+  // 1) every warp picks its own top-min(k, 32) with shuffles only (descending biased score,
+  //    ties to the lower expert id) into the candidate pool
+  __shared__ float cand_v[1024];
+  __shared__ float cand_s[1024];
+  __shared__ int cand_i[1024];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int kw = topk < 32 ? topk : 32;
+  {
+    float bv = biased;
+    bool taken = false;
+    for (int j = 0; j < kw; ++j) {
+      ArgMax a{bv, (valid && !taken) ? e : 0x7fffffff};
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      ArgMax b{__shfl_xor_sync(0xffffffffu, a.v, o), __shfl_xor_sync(0xffffffffu, a.i, o)};
-      a = better(a, b);
+      for (int o = 16; o > 0; o >>= 1) {
+        ArgMax b{__shfl_xor_sync(0xffffffffu, a.v, o), __shfl_xor_sync(0xffffffffu, a.i, o)};
+        a = better(a, b);
+      }
+      const int src = a.i == 0x7fffffff ? 0 : a.i & 31;
+      const float sc = __shfl_sync(0xffffffffu, score, src);
+      if (lane == 0) {
+        cand_v[w * kw + j] = a.v;
+        cand_i[w * kw + j] = a.i;
+        cand_s[w * kw + j] = sc;
+      }
+      if (e == a.i) {                             // remove from the next rounds
+        bv = -INFINITY;
+        taken = true;
+      }
     }
-    const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    __syncthreads();
-    if ((threadIdx.x & 31) == 0) redm[w] = a;
-    __syncthreads();
-    ArgMax r = redm[0];
-    for (int i = 1; i < nw; ++i) r = better(r, redm[i]);
-    if (e == r.i) {
-      sel_idx[j] = e;
-      sel_score[j] = score;
-      biased = -INFINITY;  // remove from later rounds
-    }
-    __syncthreads();
   }
+  __syncthreads();
+  // 2) warp 0 merges the nw * kw candidates: topk rounds of argmax over the pool
+  if (w == 0) {
+    const int n = nw * kw;
+    for (int j = 0; j < topk; ++j) {
+      ArgMax a{-INFINITY, 0x7fffffff};
+      int at = -1;
+      for (int c = lane; c < n; c += 32) {
+        const ArgMax b{cand_v[c], cand_i[c]};
+        const ArgMax m = better(a, b);
+        if (m.i != a.i || m.v != a.v) at = c;
+        a = m;
+      }
+      int pos = at;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        ArgMax b{__shfl_xor_sync(0xffffffffu, a.v, o), __shfl_xor_sync(0xffffffffu, a.i, o)};
+        const int pb = __shfl_xor_sync(0xffffffffu, pos, o);
+        const ArgMax m = better(a, b);
+        if (m.i != a.i || m.v != a.v) pos = pb;
+        a = m;
+      }
+      if (lane == 0) {
+        sel_idx[j] = a.i;
+        sel_score[j] = cand_s[pos];
+        cand_v[pos] = -INFINITY;               // taken
+        cand_i[pos] = 0x7fffffff;
+      }
+      __syncwarp();
+    }
+  }
+  __syncthreads();
   if (threadIdx.x == 0) {
     float sum = 0.0f;
     for (int j = 0; j < topk; ++j) sum += sel_score[j];
