@@ -110,6 +110,7 @@ PROTOTYPES = {
     "dsv41_engram_gather_rows": (_I, [_P, _P, _I64, _I64, _I64, _I64, _P, _I64, _I, _P, _P]),
     "dsv41_engram_gather_sum": (_I, [_P, _P, _I64, _I64, _I64, _I64, _P, _I64, _I, _I, _P, _P]),
     "dsv41_engram_row_bytes": (_SZ, [_I64, _I64]),
+    "dsv41_engram_gate": (_I, [_P, _I, _P, _I, _P, _P, _P, _I64, _I, _I64, _F, _F, _P, _P]),
     "dsv41_ipc_export": (_I, [_P, _P, C.POINTER(_I64)]),
     "dsv41_ipc_import": (_I, [_P, C.POINTER(_P)]),
     "dsv41_ipc_close": (_I, [_P]),

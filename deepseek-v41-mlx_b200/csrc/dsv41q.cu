@@ -2152,6 +2152,35 @@ extern "C" int dsv41_engram_gather_sum_peers(const uint64_t *tables, const uint6
   return DSV41_OK;
 }
 
+extern "C" int dsv41_engram_gate(const void *x, int x_dtype, const void *kv, int kv_dtype,
+                                 const float *q_weight, const float *k_weight,
+                                 const uint8_t *token_mask, int64_t T, int hc, int64_t D,
+                                 float eps, float clamp, void *out, void *stream) {
+  DSV41_REQUIRE(T >= 0 && hc >= 1 && D >= 1, DSV41_ERR_BAD_SHAPE, "bad shape");
+  DSV41_REQUIRE((x_dtype == DSV41_F32 || x_dtype == DSV41_BF16) &&
+                    (kv_dtype == DSV41_F32 || kv_dtype == DSV41_BF16),
+                DSV41_ERR_BAD_DTYPE, "x / kv must be F32 or BF16");
+  if (T == 0) return DSV41_OK;
+  DSV41_REQUIRE(x && kv && q_weight && k_weight && out, DSV41_ERR_BAD_ARG, "NULL pointer");
+  cudaStream_t st = STREAM(stream);
+  ProfScope prof("engram_gate", st);
+  const unsigned grid = unsigned(T * hc);
+#define EG(TX, TKV)                                                                              \
+  k_engram_gate<TX, TKV><<<grid, 256, 0, st>>>(static_cast<const TX *>(x), static_cast<const TKV *>(kv), \
+                                               q_weight, k_weight, token_mask, hc, D, eps, clamp,  \
+                                               static_cast<TX *>(out))
+  if (x_dtype == DSV41_F32) {
+    if (kv_dtype == DSV41_F32) EG(float, float);
+    else EG(float, __nv_bfloat16);
+  } else {
+    if (kv_dtype == DSV41_F32) EG(__nv_bfloat16, float);
+    else EG(__nv_bfloat16, __nv_bfloat16);
+  }
+#undef EG
+  DSV41_CHECK_LAUNCH("engram_gate");
+  return DSV41_OK;
+}
+
 // ---- row-sharded table: raw rows travel from their owners to the ranks that sum them
 extern "C" size_t dsv41_engram_row_bytes(int64_t d, int64_t block) {
   if (d <= 0 || block <= 0) return 0;

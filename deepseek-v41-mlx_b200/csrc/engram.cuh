@@ -240,4 +240,80 @@ __global__ void __launch_bounds__(256) k_engram_pack_rows(
   for (int64_t b = lane; b < rb - D; b += 32) o[D + b] = (in && b < sb) ? scale[local * sb + b] : 0;
 }
 
+// ---- Engram gate (deepseek_v41_mlx/engram.py:245-264; upstream Engram.forward,
+// docs/reference/model.py:344-365), after kv = wkv(rows).  One CTA per (token t, hc copy c):
+//   rstd = rsqrt(mean(h^2) + eps) * rsqrt(mean(key^2) + eps)       (over dim, fp32)
+//   dot  = sum(h * q * k * key) * rstd / sqrt(dim)
+//   gate = sigmoid(sign(dot) * sqrt(max(|dot|, clamp)))            (0 where the mask is off)
+//   out  = h + gate * value                                        (rounded to out's type)
+// x, out [T, hc, D]; kv [T, (hc + 1) * D] = hc keys then the shared value.
+template <typename T> __device__ __forceinline__ float ld_f(const T *p);
+template <> __device__ __forceinline__ float ld_f<float>(const float *p) { return *p; }
+template <> __device__ __forceinline__ float ld_f<__nv_bfloat16>(const __nv_bfloat16 *p) {
+  return __bfloat162float(*p);
+}
+
+template <typename TX, typename TKV>
+__global__ void __launch_bounds__(256) k_engram_gate(const TX *__restrict__ x,
+                                                     const TKV *__restrict__ kv,
+                                                     const float *__restrict__ qw,
+                                                     const float *__restrict__ kw,
+                                                     const uint8_t *__restrict__ mask, int hc,
+                                                     int64_t D, float eps, float clamp,
+                                                     TX *__restrict__ out) {
+  const int64_t t = blockIdx.x / hc;
+  const int c = int(blockIdx.x % hc);
+  const TX *h = x + (t * hc + c) * D;
+  const TKV *key = kv + t * (hc + 1) * D + c * D;
+  const TKV *val = kv + t * (hc + 1) * D + (int64_t)hc * D;
+  const float *q = qw + (int64_t)c * D, *k = kw + (int64_t)c * D;
+  float shh = 0.0f, skk = 0.0f, sd = 0.0f;
+  for (int64_t j = threadIdx.x; j < D; j += blockDim.x) {
+    const float hv = ld_f(h + j), kv_ = ld_f(key + j);
+    shh = fmaf(hv, hv, shh);
+    skk = fmaf(kv_, kv_, skk);
+    sd = fmaf(hv * (q[j] * k[j]), kv_, sd);
+  }
+  __shared__ float red[3][8];
+  __shared__ float s_gate;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    shh += __shfl_xor_sync(0xffffffffu, shh, o);
+    skk += __shfl_xor_sync(0xffffffffu, skk, o);
+    sd += __shfl_xor_sync(0xffffffffu, sd, o);
+  }
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    red[0][w] = shh;
+    red[1][w] = skk;
+    red[2][w] = sd;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float a = 0.0f, b = 0.0f, d = 0.0f;
+    for (int i = 0; i < int(blockDim.x >> 5); ++i) {
+      a += red[0][i];
+      b += red[1][i];
+      d += red[2][i];
+    }
+    const float inv_d = 1.0f / float(D);
+    const float rstd = rsqrtf(a * inv_d + eps) * rsqrtf(b * inv_d + eps);
+    const float dot = d * rstd * rsqrtf(float(D));
+    const float mag = sqrtf(fmaxf(fabsf(dot), clamp));
+    float g = 1.0f / (1.0f + expf(dot < 0.0f ? mag : -mag));
+    if (mask && !mask[t]) g = 0.0f;
+    s_gate = g;
+  }
+  __syncthreads();
+  const float g = s_gate;
+  TX *o = out + (t * hc + c) * D;
+  for (int64_t j = threadIdx.x; j < D; j += blockDim.x) {
+    const float v = fmaf(g, ld_f(val + j), ld_f(h + j));
+    if constexpr (sizeof(TX) == 4)
+      o[j] = v;
+    else
+      o[j] = __float2bfloat16_rn(v);
+  }
+}
+
 }  // namespace dsv41

@@ -11,6 +11,10 @@
   row-sharded ParallelEngramEmbedding (docs/reference/model.py:296-325): ids
   outside [row_lo, row_lo + rows) give zero rows.
 * ``QuantizedEngramEmbedding`` is the MLX affine table (engram.py:206-223).
+* ``Engram(args, layer_hash_index)(x, hash_ids)`` is the gated write of the looked-up
+  rows into the hc-expanded stream (engram.py:225-264): rows -> ``wkv`` (any linear of
+  this package, e.g. ``linear.FP8Linear`` for the release's fp8 blocks) -> the fused gate
+  kernel ``dsv41_engram_gate``.
 * ``gather_sum`` is the summed form used by the benchmark configuration.
 * ``ParallelEngramEmbedding(num, dim, block)`` is upstream's row-sharded table
   (docs/reference/model.py:296-325) over a torch.distributed process group: each
@@ -389,3 +393,71 @@ class ParallelEngramEmbedding:
                                   part_out[:n_my])
         out = self._gather_all(part_out, plan["T"])
         return out.reshape(tuple(indices.shape) + (self.dim,))
+
+
+class Engram:
+    """engram.py:225-264 (upstream Engram, docs/reference/model.py:328-365): the n-gram rows,
+    projected by ``wkv`` to one key per hc copy plus a shared value, written into the
+    hc-expanded stream x [..., hc, dim] through a gate -- the normalised dot of the stream
+    with the key, signed square root, sigmoid.  ``wkv`` is a linear of this package
+    (``linear.FP8Linear`` for the release's fp8 32x32 blocks, ``linear.QuantizedLinear`` for
+    MLX affine); ``q_weight`` / ``k_weight`` [hc, dim] default to ones as in the reference."""
+
+    def __init__(self, args, layer_hash_index: int):
+        self.layer_hash_index = layer_hash_index
+        self.dim = args.dim
+        self.hc_mult = args.hc_mult
+        self.eps = float(args.norm_eps)
+        self.clamp_value = 1e-6
+        self.n_hash_cols = (args.engram_max_ngram_size - 1) * args.engram_n_heads
+        self.head_dim = args.engram_head_dim
+        self.embed = EngramEmbedding(args.engram_num_embeddings[layer_hash_index],
+                                     args.engram_head_dim, getattr(args, "engram_block", 32))
+        self.wkv = None
+        self.q_weight = None
+        self.k_weight = None
+
+    def _qk(self, device):
+        t = L.torch()
+        ones = t.ones((self.hc_mult, self.dim), dtype=t.float32, device=device)
+        q = ones if self.q_weight is None else L.cuda_tensor(self.q_weight).float().contiguous()
+        k = ones if self.k_weight is None else L.cuda_tensor(self.k_weight).float().contiguous()
+        return q, k
+
+    def gate(self, x, kv, token_mask=None):
+        """The gated write for a given kv [..., (hc + 1) * dim] (the step after wkv)."""
+        t = L.torch()
+        xt = L.cuda_tensor(x, "x")
+        if xt.dtype not in (t.float32, t.bfloat16):
+            xt = xt.to(t.bfloat16)
+        xt = xt.contiguous()
+        kvt = L.cuda_tensor(kv, "kv")
+        if kvt.dtype not in (t.float32, t.bfloat16):
+            kvt = kvt.float()
+        kvt = kvt.contiguous()
+        hc, D = self.hc_mult, self.dim
+        if tuple(xt.shape[-2:]) != (hc, D) or kvt.shape[-1] != (hc + 1) * D:
+            raise ValueError(f"x [..., {hc}, {D}] and kv [..., {(hc + 1) * D}] expected")
+        T = xt.numel() // (hc * D)
+        q, k = self._qk(xt.device)
+        m = None
+        if token_mask is not None:
+            m = L.cuda_tensor(token_mask, "token_mask").to(t.uint8).reshape(-1).contiguous()
+        out = t.empty_like(xt)
+        L.call("dsv41_engram_gate", L.ptr(xt), L.dtype_code(xt.dtype), L.ptr(kvt),
+               L.dtype_code(kvt.dtype), L.ptr(q), L.ptr(k), L.ptr(m) if m is not None else None,
+               T, hc, D, self.eps, self.clamp_value, L.ptr(out), L.stream_of(xt))
+        return out
+
+    def __call__(self, x, hash_ids, token_mask=None):
+        """x [B, L, hc, dim]; hash_ids [B, L, n_hash_cols] -> the updated stream, x's dtype."""
+        t = L.torch()
+        if self.wkv is None:
+            raise ValueError("Engram.wkv is not set")
+        xt = L.cuda_tensor(x, "x")
+        dt = xt.dtype if xt.dtype in (t.float32, t.bfloat16) else t.bfloat16
+        ids = L.cuda_tensor(hash_ids, "hash_ids").to(t.int64)
+        rows = self.embed(ids, dt)                                    # rows cast to x's dtype
+        rows = rows.reshape(-1, self.n_hash_cols * self.head_dim)
+        kv = self.wkv(rows, out_dtype=dt)                             # the linear's output dtype
+        return self.gate(xt, kv.reshape(tuple(xt.shape[:-2]) + (-1,)), token_mask)

@@ -383,6 +383,18 @@ int dsv41_engram_dequant_rows(const void *packed, int64_t n_rows, int64_t d, int
                               const int64_t *pos, int64_t n, int out_dtype, void *out,
                               void *stream);
 
+/* ---- Engram gate (deepseek_v41_mlx/engram.py:245-264; upstream Engram.forward,
+ * docs/reference/model.py:344-365), applied after kv = wkv(rows):
+ * x, out [T, hc, D] of x_dtype (F32 or BF16; out takes x's type); kv [T, (hc+1)*D] of kv_dtype
+ * (hc keys, then the shared value); q_weight, k_weight f32 [hc, D]; token_mask u8 [T] or NULL
+ * (upstream's mask: 0 closes the gate).  Per (token, hc copy): rstd = rsqrt(mean(h^2)+eps) *
+ * rsqrt(mean(key^2)+eps), dot = sum(h*q*k*key)*rstd/sqrt(D), gate = sigmoid(sign(dot) *
+ * sqrt(max(|dot|, clamp))), out = h + gate*value.  fp32 arithmetic. */
+int dsv41_engram_gate(const void *x, int x_dtype, const void *kv, int kv_dtype,
+                      const float *q_weight, const float *k_weight, const uint8_t *token_mask,
+                      int64_t T, int hc, int64_t D, float eps, float clamp, void *out,
+                      void *stream);
+
 /* ---- (e) row-sharded engram table read in place through NVLink peer memory: every rank maps
  * the other ranks' shards (CUDA IPC) once, then sums the rows of its own slice of the tokens
  * reading each row from the GPU that holds it -- no row packing, no exchange of rows, no

@@ -13,6 +13,10 @@ and the upstream row-sharded lookup ParallelEngramEmbedding.forward
 (docs/reference/model.py:312-325): ids outside the shard read zero rows.
 The gather-sum form sums the per-token rows in
 hash-column order in fp32.
+  Engram.__call__              engram.py:245-264 kv = wkv(rows); per (token, hc copy)
+                                                 normalised dot of the stream with the key,
+                                                 signed-sqrt sigmoid gate, h + gate * value
+(upstream Engram.forward, docs/reference/model.py:344-365, adds the token mask).
 """
 
 from __future__ import annotations
@@ -114,3 +118,29 @@ def gather_sum(table, scale, idx, block, out_dtype="bf16", row_lo=0):
     for h in range(rows.shape[1]):
         acc = (acc + rows[:, h]).astype(np.float32)
     return to_dtype(acc, out_dtype)
+
+
+def engram_gate(x, kv, q_weight, k_weight, eps, clamp=1e-6, token_mask=None):
+    """Engram.__call__ after the wkv projection (engram.py:248-264), fp32.
+
+    x [..., hc, dim]; kv [..., (hc + 1) * dim] (hc keys, then the shared value);
+    q_weight, k_weight [hc, dim].  rstd = rsqrt(mean(h^2) + eps) * rsqrt(mean(key^2) + eps)
+    per (token, hc copy); dot = sum(h * (q*k) * key) * rstd / sqrt(dim);
+    gate = sigmoid(sign(dot) * sqrt(max(|dot|, clamp))); out = h + gate * value.
+    token_mask [...] (upstream model.py:361-362): False closes the gate."""
+    x = np.asarray(x, dtype=np.float32)
+    kv = np.asarray(kv, dtype=np.float32)
+    hc, dim = x.shape[-2], x.shape[-1]
+    key = kv[..., :hc * dim].reshape(kv.shape[:-1] + (hc, dim))
+    value = kv[..., hc * dim:]
+    weight = (np.asarray(q_weight, np.float32) * np.asarray(k_weight, np.float32)).astype(np.float32)
+    ms_h = np.mean(np.square(x), axis=-1, dtype=np.float32)
+    ms_k = np.mean(np.square(key), axis=-1, dtype=np.float32)
+    rstd = (1.0 / np.sqrt(ms_h + np.float32(eps))) * (1.0 / np.sqrt(ms_k + np.float32(eps)))
+    dot = np.sum(x * weight * key, axis=-1, dtype=np.float32) * rstd.astype(np.float32) \
+        * np.float32(dim ** -0.5)
+    mag = np.sqrt(np.maximum(np.abs(dot), np.float32(clamp)))
+    gate = 1.0 / (1.0 + np.exp(-np.where(dot < 0, -mag, mag)))
+    if token_mask is not None:
+        gate = np.where(np.asarray(token_mask)[..., None], gate, 0.0)
+    return (x + gate.astype(np.float32)[..., None] * value[..., None, :]).astype(np.float32)

@@ -25,6 +25,7 @@ runs without MLX):
   (docs/reference/model.py:792-851) in fp32 on fp4-decoded weights, plus the
   upstream MoE.forward on a small config (world_size 1).
 * engram_embed.npz -- upstream ParallelEngramEmbedding.forward
+* engram_gate.npz -- upstream Engram.forward (gated write of the looked-up rows)
   (docs/reference/model.py:312-325), world_size 1.
 
 The fixtures are small (< 1 MB together) and committed; the GPU box never
@@ -268,6 +269,49 @@ def golden_engram_embed():
                         idx=idx.numpy(), out=out)
 
 
+def golden_engram_gate():
+    """upstream Engram.forward (docs/reference/model.py:344-365) in fp32 with the row lookup
+    replaced by fixed rows: kv = wkv(rows), the per-(token, hc copy) normalised gate and the
+    gated write, with and without a token mask.  Inputs are bf16-representable."""
+    import model as M
+    M.default_dtype = torch.float32
+    M.world_size, M.rank = 1, 0
+    rng = np.random.default_rng(31)
+    D, hc, hd, B, L = 64, 4, 16, 2, 5
+    layout = types.SimpleNamespace(layer_ids=(1,), num_embeddings=(100,), head_dim=hd,
+                                   max_ngram_size=4, n_heads=2)
+    cols = (layout.max_ngram_size - 1) * layout.n_heads
+    args = M.ModelArgs(dim=D, n_layers=1, hc_mult=hc, norm_eps=1e-6)
+    eg = M.Engram(args, 1, layout)
+
+    def bf(a):
+        return torch.from_numpy(a.astype(np.float32)).to(torch.bfloat16).float()
+
+    eg.wkv.weight.data.copy_(bf(rng.standard_normal(((hc + 1) * D, cols * hd)) / np.sqrt(cols * hd)))
+    eg.q_weight.data.copy_(bf(1.0 + 0.1 * rng.standard_normal((hc, D))))
+    eg.k_weight.data.copy_(bf(1.0 + 0.1 * rng.standard_normal((hc, D))))
+    rows = bf(rng.standard_normal((B, L, cols, hd)))
+
+    class Rows(torch.nn.Module):
+        def forward(self, ids):
+            return rows
+
+    eg._modules["embed"] = Rows()
+    x = bf(rng.standard_normal((B, L, hc, D)))
+    ids = torch.zeros((B, L, cols), dtype=torch.int64)
+    mask = torch.from_numpy(rng.random((B, L)) > 0.3)
+    with torch.no_grad():
+        kv = eg.wkv(rows.flatten(-2))
+        out = eg(x, ids)
+        out_m = eg(x, ids, mask)
+    np.savez_compressed(os.path.join(HERE, "engram_gate.npz"), x=x.numpy(), rows=rows.numpy(),
+                        wkv=eg.wkv.weight.detach().numpy(), kv=kv.numpy(),
+                        q_weight=eg.q_weight.detach().numpy(),
+                        k_weight=eg.k_weight.detach().numpy(), eps=eg.eps,
+                        clamp=eg.clamp_value, out=out.numpy(), mask=mask.numpy(),
+                        out_masked=out_m.numpy())
+
+
 def main():
     torch.set_default_dtype(torch.float32)
     ks = _setup_imports()
@@ -276,6 +320,7 @@ def main():
     golden_engram_hash()
     golden_router_expert()
     golden_engram_embed()
+    golden_engram_gate()
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

@@ -9,7 +9,7 @@ import pytest
 import torch
 
 import deepseek_v41_mlx_b200 as q
-from conftest import bits_equal, golden
+from conftest import bits_equal, golden, rel_fro
 from oracle import engram as OE
 
 pytestmark = pytest.mark.gpu
@@ -168,3 +168,55 @@ def test_packed_rows_off_shard_are_zero(cuda):
     packed = ops.pack_rows(table, scale, 1000, d, block, ids)
     assert torch.equal(packed[0, :d], table[0]) and torch.equal(packed[2, d:d + d // block], scale[99])
     assert int(packed[3].abs().sum()) == 0 and int(packed[4].abs().sum()) == 0
+
+
+def test_engram_gate_golden(cuda):
+    """The fused gate against upstream Engram.forward (fp32 stream and kv), with and without
+    the token mask."""
+    g = golden("engram_gate.npz")
+    args = types.SimpleNamespace(dim=g["x"].shape[-1], hc_mult=g["x"].shape[-2],
+                                 norm_eps=float(g["eps"]), engram_max_ngram_size=4,
+                                 engram_n_heads=2, engram_head_dim=16,
+                                 engram_num_embeddings=(100,))
+    eg = q.engram.Engram(args, 0)
+    eg.q_weight, eg.k_weight = _d(g["q_weight"]), _d(g["k_weight"])
+    x, kv = _d(g["x"]), _d(g["kv"])
+    got = eg.gate(x, kv).cpu().numpy()
+    np.testing.assert_allclose(got, g["out"], rtol=1e-5, atol=2e-6)
+    got = eg.gate(x, kv, token_mask=_d(g["mask"])).cpu().numpy()
+    np.testing.assert_allclose(got, g["out_masked"], rtol=1e-5, atol=2e-6)
+
+
+def test_engram_module_fp8_wkv(cuda):
+    """Rows gathered from an fp8 table -> bf16 -> release-format fp8 wkv -> gate, bf16 stream,
+    against the oracle chain (row gather, bf16 rounding, exact decode, float64 projection
+    rounded to bf16, the gate)."""
+    from gen import bf16_acts, fp8_weight
+    from oracle import formats as F
+    rng = np.random.default_rng(12)
+    rows_n, hd, heads, hc, D, B, Lq = 2000, 256, 2, 4, 256, 3, 7
+    cols = 3 * heads
+    args = types.SimpleNamespace(dim=D, hc_mult=hc, norm_eps=1e-6, engram_max_ngram_size=4,
+                                 engram_n_heads=heads, engram_head_dim=hd,
+                                 engram_num_embeddings=(rows_n,))
+    table = rng.integers(0, 126, size=(rows_n, hd), dtype=np.uint8)
+    scale = rng.integers(115, 124, size=(rows_n, hd // 32), dtype=np.uint8)
+    w, s = fp8_weight(rng, (hc + 1) * D, cols * hd, 112, 120)
+    qw = (1.0 + 0.1 * rng.standard_normal((hc, D))).astype(np.float32)
+    kw = (1.0 + 0.1 * rng.standard_normal((hc, D))).astype(np.float32)
+    xb, xf = bf16_acts(rng, B * Lq * hc, D)
+    ids = rng.integers(0, rows_n, size=(B, Lq, cols))
+    eg = q.engram.Engram(args, 0)
+    eg.embed.weight, eg.embed.scale = _d(table), _d(scale)
+    eg.wkv = q.linear.FP8Linear(_d(w), _d(s))
+    eg.q_weight, eg.k_weight = _d(qw), _d(kw)
+    x = _d(xb.view(np.int16)).view(torch.bfloat16).reshape(B, Lq, hc, D)
+    got = eg(x, _d(ids)).float().cpu().numpy()
+    # oracle chain
+    rows = OE.gather_rows(table, scale, ids.reshape(-1), 32).reshape(B * Lq, cols * hd)
+    rows = F.bf16_bits_to_f32(F.f32_to_bf16_bits(rows.astype(np.float32)))
+    wd = F.dequant_fp8(w, s, "f32").astype(np.float64)
+    kv = (rows.astype(np.float64) @ wd.T).astype(np.float32)
+    kv = F.bf16_bits_to_f32(F.f32_to_bf16_bits(kv))
+    want = OE.engram_gate(xf.reshape(B * Lq, hc, D), kv, qw, kw, 1e-6)
+    assert rel_fro(got.reshape(B * Lq, hc, D), want) < 1e-2

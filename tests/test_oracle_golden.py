@@ -197,3 +197,18 @@ def test_moe_layer_golden_exact_mode():
     assert rel_fro(y, g["y_moe"]) < 1e-5
     yb, _, _ = OM.moe_forward(g["x"], p, cfg, round_bf16_io=True)
     assert rel_fro(yb, g["y_moe"]) < 1e-2
+
+
+def test_engram_gate_golden():
+    """The gate restatement against upstream Engram.forward (fp32, with and without the
+    token mask) on the same kv."""
+    g = golden("engram_gate.npz")
+    got = OE.engram_gate(g["x"], g["kv"], g["q_weight"], g["k_weight"], float(g["eps"]),
+                         float(g["clamp"]))
+    np.testing.assert_allclose(got, g["out"], rtol=1e-5, atol=1e-6)
+    got = OE.engram_gate(g["x"], g["kv"], g["q_weight"], g["k_weight"], float(g["eps"]),
+                         float(g["clamp"]), token_mask=g["mask"])
+    np.testing.assert_allclose(got, g["out_masked"], rtol=1e-5, atol=1e-6)
+    # kv is the rows' projection
+    rows = g["rows"].reshape(g["rows"].shape[:-2] + (-1,))
+    np.testing.assert_allclose(rows @ g["wkv"].T, g["kv"], rtol=1e-5, atol=1e-5)
