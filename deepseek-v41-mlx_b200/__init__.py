@@ -13,12 +13,13 @@ from __future__ import annotations
 from . import _lib  # noqa: F401
 from ._lib import DSV41Error, lib_path  # noqa: F401
 
-__all__ = ["dequant", "moe", "engram", "linear", "act_quant", "DSV41Error", "lib_path"]
+__all__ = ["dequant", "moe", "engram", "linear", "act_quant", "gemm", "ep", "release",
+           "DSV41Error", "lib_path"]
 
 
 def __getattr__(name):
     # submodules load lazily so that importing the package never touches CUDA
-    if name in ("dequant", "moe", "engram", "linear", "act_quant", "gemm", "ep"):
+    if name in ("dequant", "moe", "engram", "linear", "act_quant", "gemm", "ep", "release"):
         import importlib
         return importlib.import_module(f"{__name__}.{name}")
     raise AttributeError(name)
