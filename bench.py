@@ -527,14 +527,17 @@ def engram_measurement(q, torch, dev, flush, stream, K, W):
     args.engram_num_embeddings = (rows,)
     hasher = q.engram.EngramHasher(args, np.arange(99092, dtype=np.int64), device=dev)
     g = torch.Generator(device=dev).manual_seed(55)
-    table = torch.empty((rows, d), dtype=torch.uint8, device=dev)
-    for r0 in range(0, rows, 1 << 20):          # 1 GB at a time: uniform over non-NaN codes
-        c = table[r0:r0 + (1 << 20)]
+    # the table stored packed (EngramEmbedding.pack: codes then the row's scale, 1040 bytes a
+    # row), generated in place: uniform over non-NaN codes, scales in [115, 127]
+    rb = int(q._lib.load().dsv41_engram_row_bytes(d, d))
+    table = torch.zeros((rows, rb), dtype=torch.uint8, device=dev)
+    for r0 in range(0, rows, 1 << 20):          # 1 GB at a time
+        c = table[r0:r0 + (1 << 20), :d]
         c.random_(0, 254, generator=g)
         c += (c >= 127).to(torch.uint8)
-    scale = torch.randint(115, 128, (rows, 1), dtype=torch.uint8, device=dev, generator=g)
+        table[r0:r0 + (1 << 20), d].random_(115, 128, generator=g)
     emb = q.engram.EngramEmbedding(rows, d, block=d)
-    emb.weight, emb.scale = table, scale
+    emb.packed = table
     out = {}
     for T in (1, 8192):
         start = 100 if T == 1 else 0
@@ -557,9 +560,10 @@ def engram_measurement(q, torch, dev, flush, stream, K, W):
                                "tok_s": round(T / (ms / 1e3), 1),
                                "gbs": round(byts / (ms / 1e3) / 1e9, 1),
                                "frac_hbm": round(byts / (ms / 1e3) / 1e9 / hbm_peak, 4),
-                               "table_rows": rows, "table_gb": round(rows * (d + 1) / 1e9, 1),
+                               "table_rows": rows, "table_gb": round(rows * rb / 1e9, 1),
+                               "table_layout": "packed rows (codes + scale, %d B)" % rb,
                                "peak_source": peak_src + " hbm_gbs"}
-    del table, scale, emb
+    del table, emb
     torch.cuda.empty_cache()
     return out
 

@@ -2194,7 +2194,8 @@ extern "C" int dsv41_engram_pack_rows(const uint8_t *table, const uint8_t *scale
   DSV41_REQUIRE(rows >= 0 && d > 0 && block > 0 && d % block == 0 && d % 16 == 0 && n >= 0,
                 DSV41_ERR_BAD_SHAPE, "need block | d and 16 | d");
   if (n == 0) return DSV41_OK;
-  DSV41_REQUIRE(table && scale && idx && out_rows, DSV41_ERR_BAD_ARG, "NULL pointer");
+  DSV41_REQUIRE(table && scale && out_rows, DSV41_ERR_BAD_ARG, "NULL pointer");
+  DSV41_REQUIRE(idx || n <= rows, DSV41_ERR_BAD_SHAPE, "without idx, n must be <= rows");
   DSV41_REQUIRE(aligned(table, 16) && aligned(out_rows, 16), DSV41_ERR_MISALIGNED,
                 "table and out_rows must be 16-byte aligned");
   cudaStream_t st = STREAM(stream);

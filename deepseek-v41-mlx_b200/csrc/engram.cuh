@@ -220,7 +220,9 @@ __global__ void __launch_bounds__(256) k_engram_gather_sum(
 // Row-sharded tables: the owner of rows [row_lo, row_lo + rows) copies the raw rows
 // idx[i] (global ids, all owned) into packed rows of rb bytes -- D code bytes, then the
 // D / block scale bytes, zero padding to rb (a multiple of 16) -- for the ranks whose
-// tokens need them.  One warp per row, 16-byte copies; rows not owned are zero.
+// tokens need them.  One warp per row, 16-byte copies; rows not owned are zero.  Without
+// idx, rows 0 .. n-1 of the table in order: a whole table repacked so that a lookup reads
+// one contiguous row (codes and scales) instead of two places.
 __global__ void __launch_bounds__(256) k_engram_pack_rows(
     const uint8_t *__restrict__ table, const uint8_t *__restrict__ scale, int64_t rows,
     int64_t row_lo, int64_t D, int64_t block, const int64_t *__restrict__ idx, int64_t n,
@@ -228,7 +230,7 @@ __global__ void __launch_bounds__(256) k_engram_pack_rows(
   const int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (i >= n) return;
-  const int64_t local = idx[i] - row_lo;
+  const int64_t local = idx ? idx[i] - row_lo : i;   // no list: the table's rows in order
   const bool in = local >= 0 && local < rows;
   uint8_t *o = out + i * rb;
   for (int64_t c = lane * 16; c < D; c += 512) {

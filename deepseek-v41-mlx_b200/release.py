@@ -151,11 +151,27 @@ def load_moe(ckpt, layer: int, args=None, device="cuda", rank: int = 0, world: i
     return e
 
 
+def _packed_table(ckpt, prefix, rows, hd, block, device, chunk=1 << 20):
+    """The table read in row chunks and stored packed (codes then scales a row) on the device:
+    the unpacked table is never whole on the device."""
+    t = L.torch()
+    rb = int(L.load().dsv41_engram_row_bytes(hd, block))
+    out = t.empty((rows, rb), dtype=t.uint8, device=device)
+    for r0 in range(0, rows, chunk):
+        r1 = min(rows, r0 + chunk)
+        w = ckpt.get(f"{prefix}.embed.weight", device, rows=(r0, r1))
+        s = ckpt.get(f"{prefix}.embed.scale", device, rows=(r0, r1))
+        L.call("dsv41_engram_pack_rows", L.ptr(w), L.ptr(s), r1 - r0, 0, hd, block, None, r1 - r0,
+               L.ptr(out) + r0 * rb, L.stream_of(w))
+    return out
+
+
 def load_engram(ckpt, layer_id: int, args=None, device="cuda", rank: int = 0, world: int = 1,
-                group=None):
+                group=None, packed: bool = True):
     """``layers.{layer_id}.engram`` -> ``engram.Engram``: the fp8 row table (this rank's rows
     only when world > 1, as a ``ParallelEngramEmbedding``), the fp8 ``wkv`` projection and the
-    gate weights."""
+    gate weights.  ``packed`` (one GPU): the table is stored as packed rows (see
+    ``EngramEmbedding.pack``), built chunk by chunk while reading."""
     from . import engram as G
     from .linear import FP8Linear
     t = L.torch()
@@ -168,8 +184,11 @@ def load_engram(ckpt, layer_id: int, args=None, device="cuda", rank: int = 0, wo
     block = hd // ckpt.get(f"{prefix}.embed.scale", "cpu", rows=(0, 1)).shape[-1]
     if world == 1:
         emb = G.EngramEmbedding(rows, hd, block)
-        emb.weight = ckpt.get(f"{prefix}.embed.weight", device)
-        emb.scale = ckpt.get(f"{prefix}.embed.scale", device)
+        if packed and str(device).startswith("cuda"):
+            emb.packed = _packed_table(ckpt, prefix, rows, hd, block, device)
+        else:
+            emb.weight = ckpt.get(f"{prefix}.embed.weight", device)
+            emb.scale = ckpt.get(f"{prefix}.embed.scale", device)
     else:
         emb = G.ParallelEngramEmbedding(rows, hd, block, rank=rank, world=world, group=group)
         r0 = min(rows, rank * emb.part)

@@ -371,7 +371,10 @@ int dsv41_engram_gather_sum(const uint8_t *table, const uint8_t *scale, int64_t 
  * them (all-to-all), and the slice's rank sums them per token in head order
  * (dsv41_engram_sum_rows, = dsv41_engram_gather_sum on the received rows; pos[t*n + h] is
  * the received row of (t, h), negative = skipped) or dequantizes them one by one
- * (dsv41_engram_dequant_rows, = dsv41_engram_gather_rows).  Bit-identical to one GPU. */
+ * (dsv41_engram_dequant_rows, = dsv41_engram_gather_rows).  Bit-identical to one GPU.
+ * dsv41_engram_pack_rows with idx = NULL repacks rows 0 .. n-1 of a table in order: a
+ * table stored that way (1040 bytes a row at d = 1024) is read with dsv41_engram_sum_rows /
+ * dsv41_engram_dequant_rows with pos = the row ids -- one contiguous read a row. */
 size_t dsv41_engram_row_bytes(int64_t d, int64_t block);
 int dsv41_engram_pack_rows(const uint8_t *table, const uint8_t *scale, int64_t rows,
                            int64_t row_lo, int64_t d, int64_t block, const int64_t *idx, int64_t n,

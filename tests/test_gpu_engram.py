@@ -220,3 +220,26 @@ def test_engram_module_fp8_wkv(cuda):
     kv = F.bf16_bits_to_f32(F.f32_to_bf16_bits(kv))
     want = OE.engram_gate(xf.reshape(B * Lq, hc, D), kv, qw, kw, 1e-6)
     assert rel_fro(got.reshape(B * Lq, hc, D), want) < 1e-2
+
+
+@pytest.mark.parametrize("d,block,row_lo", [(1024, 1024, 0), (256, 32, 0), (512, 64, 700)])
+def test_packed_table_lookups_identical(cuda, d, block, row_lo):
+    """A table stored as packed rows (EngramEmbedding.pack) gives the same bits as the codes
+    and scales stored apart, for the summed and the per-row lookups; ids outside this shard
+    read zero rows either way."""
+    rng = np.random.default_rng(d + row_lo)
+    rows, T, H = 3000, 29, 24
+    table = rng.integers(0, 256, size=(rows, d), dtype=np.uint8)
+    table[(table & 0x7F) == 0x7F] = 0
+    scale = rng.integers(112, 130, size=(rows, d // block), dtype=np.uint8)
+    idx = _d(rng.integers(row_lo - 50, row_lo + rows + 50, size=(T, H)))
+    a = q.engram.EngramEmbedding(rows, d, block, row_lo=row_lo)
+    a.weight, a.scale = _d(table), _d(scale)
+    b = q.engram.EngramEmbedding(rows, d, block, row_lo=row_lo)
+    b.weight, b.scale = _d(table), _d(scale)
+    b.pack()
+    assert b.weight is None and b.packed.shape[0] == rows
+    for dt in (torch.float32, torch.bfloat16):
+        if d in (256, 512, 1024):
+            assert torch.equal(a.gather_sum(idx, dt), b.gather_sum(idx, dt))
+        assert torch.equal(a(idx, dt), b(idx, dt))
