@@ -2014,20 +2014,15 @@ static int engram_sum_launch(const uint8_t *table, const uint8_t *scale, int64_t
   DSV41_REQUIRE(aligned(table, 8) && tld % 8 == 0 && aligned(out, 16), DSV41_ERR_MISALIGNED,
                 "table rows must be 8-byte and out 16-byte aligned");
   ProfScope prof("engram_gather_sum", st);
-  // a warp covers 256 columns (d = 256) or 512 (d = 512, 1024)
-  const int ch = d == 256 ? 1 : 2;
-  const unsigned blocks = unsigned(ceil_div(n_tok * (d / (256 * ch)) * 32, 256));
-#define GS(T, CHV)                                                                             \
-  k_engram_gather_sum<T, CHV><<<blocks, 256, 0, st>>>(table, scale, rows, row_lo, d, block, tld, \
-                                                      sld, idx, n_tok, n_per_tok, (T *)out)
-  if (out_dtype == DSV41_F32) {
-    if (ch == 1) GS(float, 1);
-    else GS(float, 2);
-  } else {
-    if (ch == 1) GS(__nv_bfloat16, 1);
-    else GS(__nv_bfloat16, 2);
-  }
-#undef GS
+  // a warp covers 256 columns
+  const unsigned blocks = unsigned(ceil_div(n_tok * (d / 256) * 32, 256));
+  if (out_dtype == DSV41_F32)
+    k_engram_gather_sum<float><<<blocks, 256, 0, st>>>(table, scale, rows, row_lo, d, block, tld,
+                                                       sld, idx, n_tok, n_per_tok, (float *)out);
+  else
+    k_engram_gather_sum<__nv_bfloat16><<<blocks, 256, 0, st>>>(
+        table, scale, rows, row_lo, d, block, tld, sld, idx, n_tok, n_per_tok,
+        (__nv_bfloat16 *)out);
   DSV41_CHECK_LAUNCH("engram_gather_sum");
   return DSV41_OK;
 }
@@ -2132,22 +2127,17 @@ extern "C" int dsv41_engram_gather_sum_peers(const uint64_t *tables, const uint6
   DSV41_REQUIRE(aligned(out, 16), DSV41_ERR_MISALIGNED, "out must be 16-byte aligned");
   cudaStream_t st = STREAM(stream);
   ProfScope prof("engram_gather_sum_peers", st);
-  const int ch = d == 256 ? 1 : 2;
-  const unsigned blocks = unsigned(ceil_div(n_tok * (d / (256 * ch)) * 32, 256));
+  const unsigned blocks = unsigned(ceil_div(n_tok * (d / 256) * 32, 256));
   const auto *tabs = reinterpret_cast<const uint8_t *const *>(tables);
   const auto *scs = reinterpret_cast<const uint8_t *const *>(scales);
-#define GSP(T, CHV)                                                                             \
-  k_engram_gather_sum<T, CHV, true><<<blocks, 256, 0, st>>>(nullptr, nullptr, rows, 0, d, block, d, \
-                                                            d / block, idx, n_tok, n_per_tok,       \
-                                                            (T *)out, tabs, scs, nsh, total)
-  if (out_dtype == DSV41_F32) {
-    if (ch == 1) GSP(float, 1);
-    else GSP(float, 2);
-  } else {
-    if (ch == 1) GSP(__nv_bfloat16, 1);
-    else GSP(__nv_bfloat16, 2);
-  }
-#undef GSP
+  if (out_dtype == DSV41_F32)
+    k_engram_gather_sum<float, true><<<blocks, 256, 0, st>>>(nullptr, nullptr, rows, 0, d, block,
+                                                             d, d / block, idx, n_tok, n_per_tok,
+                                                             (float *)out, tabs, scs, nsh, total);
+  else
+    k_engram_gather_sum<__nv_bfloat16, true><<<blocks, 256, 0, st>>>(
+        nullptr, nullptr, rows, 0, d, block, d, d / block, idx, n_tok, n_per_tok,
+        (__nv_bfloat16 *)out, tabs, scs, nsh, total);
   DSV41_CHECK_LAUNCH("engram_gather_sum_peers");
   return DSV41_OK;
 }

@@ -141,16 +141,18 @@ __global__ void k_engram_gather_rows(const uint8_t *__restrict__ table,
   }
 }
 
-// Warps per token = d / (256 * CH): a warp covers 256 * CH columns, its lanes 8-column
-// chunks at c*256 + lane*8 (coalesced 256-byte spans); rows summed in column order, fp32,
-// 8 rows in flight per warp, table rows streamed (read once, not kept in L1/L2).
+// Warps per token = d / 256: a warp covers 256 columns, its lanes 8-column chunks at
+// lane*8 (coalesced 256-byte spans); rows summed in column order, fp32, 8 rows in flight per
+// warp, table rows streamed (read once, not kept in L1/L2).  The token's ids are read once,
+// one per lane, and broadcast by shuffle, so a batch's row loads wait on no index load; each
+// row's scale byte is loaded with its codes.  64 registers: 4 CTAs (32 warps) an SM.
 // PEERS: the table is sharded over ranks by rows (rank r holds rows [r*rows, (r+1)*rows),
 // `rows` = the shard size); row id's codes and scales are read from shard id / rows through
 // the pointer arrays tabs / scs (other ranks' shards mapped into this process: peer loads
 // over NVLink); ids at or past `total` (the table's rows) read as zero rows; table / scale /
 // row_lo unused.
-template <typename T, int CH, bool PEERS = false>
-__global__ void __launch_bounds__(256) k_engram_gather_sum(
+template <typename T, bool PEERS = false>
+__global__ void __launch_bounds__(256, 4) k_engram_gather_sum(
     const uint8_t *__restrict__ table, const uint8_t *__restrict__ scale, int64_t rows,
     int64_t row_lo, int64_t D, int64_t block, int64_t tld, int64_t sld,
     const int64_t *__restrict__ idx, int64_t n_tok, int n_per_tok, T *__restrict__ out,
@@ -158,63 +160,57 @@ __global__ void __launch_bounds__(256) k_engram_gather_sum(
     const uint8_t *const *__restrict__ scs = nullptr, int nsh = 0, int64_t total = 0) {
   const int64_t gw = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  const int wpt = int(D / (256 * CH));
+  const int wpt = int(D / 256);
   const int64_t tok = gw / wpt;
   if (tok >= n_tok) return;
-  const int64_t col0 = (gw % wpt) * 256 * CH;
-  // the scale column of each of this lane's chunks (8 | block keeps a chunk in one block)
-  int soff[CH];
+  const int64_t col = (gw % wpt) * 256 + lane * 8;
+  const int soff = int(col / block);            // 8 | block keeps a chunk in one scale block
+  float acc[8];
 #pragma unroll
-  for (int c = 0; c < CH; ++c) soff[c] = int(col0 + c * 256 + lane * 8) / int(block);
-  float acc[8 * CH];
-#pragma unroll
-  for (int j = 0; j < 8 * CH; ++j) acc[j] = 0.0f;
+  for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
   const int64_t *ti = idx + tok * n_per_tok;
-  for (int h = 0; h < n_per_tok; h += 8) {
-    uint64_t v[8][CH];
-    bool in[8];
-    const uint8_t *rt[8], *rs[8];         // this row's codes and scales
+  for (int h0 = 0; h0 < n_per_tok; h0 += 32) {
+    // lane l holds id h0 + l (-1 past the token's ids)
+    const int64_t mine = h0 + lane < n_per_tok ? ti[h0 + lane] : -1;
+    const int nh = min(32, n_per_tok - h0);
+    for (int h = 0; h < nh; h += 8) {             // h + u <= 31: every source lane exists
+      uint64_t v[8];
+      uint32_t sb[8];
+      bool in[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int hh = h + u;
-      const int64_t id = hh < n_per_tok ? ti[hh] : -1;
-      if (PEERS) {
-        const int64_t sh = id >= 0 ? id / rows : -1, local = id - sh * rows;
-        in[u] = id >= 0 && id < total && sh < nsh;   // the last shard may be shorter
-        rt[u] = in[u] ? tabs[sh] + local * tld : table;
-        rs[u] = in[u] ? scs[sh] + local * sld : scale;
-      } else {
-        const int64_t local = id - row_lo;
-        in[u] = hh < n_per_tok && local >= 0 && local < rows;
-        rt[u] = table + local * tld;
-        rs[u] = scale + local * sld;
+      for (int u = 0; u < 8; ++u) {
+        const int64_t id = __shfl_sync(0xffffffffu, mine, h + u);   // warp-uniform
+        const uint8_t *rt, *rs;                    // this row's codes and scales
+        if (PEERS) {
+          const int64_t sh = id >= 0 ? id / rows : -1, local = id - sh * rows;
+          in[u] = id >= 0 && id < total && sh < nsh;   // the last shard may be shorter
+          rt = in[u] ? tabs[sh] + local * tld : nullptr;
+          rs = in[u] ? scs[sh] + local * sld : nullptr;
+        } else {
+          const int64_t local = id - row_lo;
+          in[u] = id >= 0 && local >= 0 && local < rows;
+          rt = table + local * tld;
+          rs = scale + local * sld;
+        }
+        v[u] = in[u] ? __ldcs(reinterpret_cast<const unsigned long long *>(rt + col)) : 0ull;
+        sb[u] = in[u] ? uint32_t(rs[soff]) : 0u;
       }
 #pragma unroll
-      for (int c = 0; c < CH; ++c)
-        v[u][c] = in[u] ? __ldcs(reinterpret_cast<const unsigned long long *>(
-                              rt[u] + col0 + c * 256 + lane * 8))
-                        : 0ull;
-    }
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      if (!in[u]) continue;
-#pragma unroll
-      for (int c = 0; c < CH; ++c) {
-        const float s = e8m0f(rs[u][soff[c]]);
+      for (int u = 0; u < 8; ++u) {
+        if (!in[u]) continue;
+        const float s = e8m0f(uint8_t(sb[u]));
         uint32_t hq[4];
-        e4m3x4_to_f16x4(uint32_t(v[u][c]), hq[0], hq[1]);
-        e4m3x4_to_f16x4(uint32_t(v[u][c] >> 32), hq[2], hq[3]);
+        e4m3x4_to_f16x4(uint32_t(v[u]), hq[0], hq[1]);
+        e4m3x4_to_f16x4(uint32_t(v[u] >> 32), hq[2], hq[3]);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const float2 p = h2f2(hq[j >> 1]);
-          acc[c * 8 + j] = __fadd_rn(acc[c * 8 + j], __fmul_rn((j & 1) ? p.y : p.x, s));
+          acc[j] = __fadd_rn(acc[j], __fmul_rn((j & 1) ? p.y : p.x, s));
         }
       }
     }
   }
-  T *o = out + tok * D + col0;
-#pragma unroll
-  for (int c = 0; c < CH; ++c) store8(o + c * 256 + lane * 8, acc + c * 8);
+  store8(out + tok * D + col, acc);
 }
 
 // Row-sharded tables: the owner of rows [row_lo, row_lo + rows) copies the raw rows
