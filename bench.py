@@ -511,16 +511,17 @@ def affine_prefill_measurement(q, torch, dev, flush, stream, K, W, M=4096):
     return out
 
 
-def engram_measurement(q, torch, dev, flush, stream, K, W):
+def engram_measurement(q, torch, dev, flush, stream, K, W, vocab=4_000_000):
     """d5: engram table fp8 e4m3 [96,000,xxx x 1024] (one ue8m0 per row, [115, 127]) built on
     the device, 24 rows per token (2/3/4-gram x 8 heads, one layer, primes from 4,000,000)
     hashed from uniform compressed ids in [0, 99092); a step = hash + gather + dequant + fp32
-    sum -> bf16 [T, 1024].  Bytes per token: 24 x (1024 + 1) read + 2048 written."""
+    sum -> bf16 [T, 1024].  Bytes per token: 24 x (1024 + 1) read + 2048 written.  A smaller
+    ``vocab`` (engram_vocab_size) gives a table of about 24 x vocab rows, for ncu captures."""
     import types
     import numpy as np
     hbm_peak, _, peak_src = _peaks()
     args = types.SimpleNamespace(engram_layer_ids=(1,), engram_max_ngram_size=4,
-                                 engram_vocab_size=4_000_000, engram_n_heads=8, engram_pad_id=2,
+                                 engram_vocab_size=vocab, engram_n_heads=8, engram_pad_id=2,
                                  engram_compressed_vocab_size=99092)
     primes, _ = q.engram.build_layout(args)
     rows, d = int(primes.sum()), 1024
@@ -793,6 +794,9 @@ def main():
                     help="only the M=4096 affine tensor-core measurement (one JSON line)")
     ap.add_argument("--engram-only", action="store_true",
                     help="only the engram d5 measurement (one JSON line)")
+    ap.add_argument("--engram-vocab", type=int, default=4_000_000,
+                    help="engram_vocab_size of d5 (4,000,000 = BASELINE; smaller only for ncu "
+                         "captures)")
     args = ap.parse_args()
     global E, ROUTER_BYTES
     E = args.experts
@@ -822,7 +826,7 @@ def main():
         flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
         with Clocks(0) as clk:
             r = engram_measurement(q, torch, dev, flush, torch.cuda.current_stream(),
-                                   args.steps, args.warmup)
+                                   args.steps, args.warmup, args.engram_vocab)
         r["clocks"] = clk.summary()
         print(json.dumps(r))
         return
