@@ -22,7 +22,7 @@ OK, BAD_SHAPE, BAD_DTYPE, MISALIGNED, CUDA_ERR, NCCL_ERR, TIMEOUT, BAD_ARG, UNSU
     WORKSPACE = range(10)
 F32, BF16, F16, U8 = 0, 1, 2, 3
 SCORE_FUNCS = {"sqrtsoftplus": 0, "sigmoid": 1, "softmax": 2}
-MOE_ROUND_BF16, MOE_NO_SHARED, MOE_SHARED_ONLY, MOE_PACKED_SCALES = 1, 2, 4, 8
+MOE_ROUND_BF16, MOE_NO_SHARED, MOE_SHARED_ONLY, MOE_PACKED_SCALES, MOE_NO_ROWPAIR = 1, 2, 4, 8, 16
 
 
 class DSV41Error(RuntimeError):

@@ -117,6 +117,25 @@ __device__ __forceinline__ float2 h2f2(uint32_t h) {
   return __half22float2(v);
 }
 
+// Packed fp32 pairs (sm_100 f32x2 instructions): lane 0 in the low word.  Each lane is one
+// IEEE round-to-nearest multiply / add, no flush to zero -- the same bits as __fmul_rn /
+// __fadd_rn on the two lanes -- at one instruction for the pair.
+__device__ __forceinline__ uint64_t f32x2(float lo, float hi) {
+  return (uint64_t(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ uint64_t f32x2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f32x2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float f32x2_lo(uint64_t v) { return __uint_as_float(uint32_t(v)); }
+__device__ __forceinline__ float f32x2_hi(uint64_t v) { return __uint_as_float(uint32_t(v >> 32)); }
+
 __device__ __forceinline__ uint16_t f2bf_bits(float f) {
   __nv_bfloat16 b = __float2bfloat16_rn(f);
   return *reinterpret_cast<uint16_t *>(&b);

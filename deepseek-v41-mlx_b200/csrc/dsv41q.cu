@@ -726,9 +726,16 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
     p.N = d.D;
     p.K = d.I;
     p.sld = d.I / 32;
-    p.tiles = int(d.tiles_dn);
+    p.spack = (cfg->flags & DSV41_MOE_PACKED_SCALES) ? 1 : 0;
+    // Row pairs (two 64-row tiles of one expert per item, on the two-matrix kernel: the
+    // B fragments are shared and each warp runs two independent MMA chains) once the pair
+    // items fill a wave of CTAs; below that the single-tile kernel keeps more CTAs busy.
+    const int64_t pair_tiles = d.D / (2 * QG_ROWS);
+    p.rowpair = (p.spack && !(cfg->flags & DSV41_MOE_NO_ROWPAIR) && d.D % (2 * QG_ROWS) == 0 &&
+                 active * pair_tiles >= QG_MIN_CTAS * (int64_t)num_sms()) ? 1 : 0;
+    p.tiles = int(p.rowpair ? pair_tiles : d.tiles_dn);
     p.kstages = int(ceil_div(d.I, Fmt<WF_FP4>::KS));
-    p.nsplit = pick_nsplit(active * d.tiles_dn, p.kstages);
+    p.nsplit = pick_nsplit(active * p.tiles, p.kstages);
     p.xscale = nullptr;
     p.chunks = ws.plan.dn_chunks;
     p.nchunks_dev = ws.plan.counts + 1;
@@ -736,15 +743,18 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
     p.out = Y;
     p.ldo = d.D;
     p.pair_row = ws.plan.pair_row;
-    p.partial = ws.part_dn;
+    p.partial = ws.part_dn;       // a rowpair tile's fragments fill two tiles' room
     p.counters = ws.cnt_dn;
-    p.spack = (cfg->flags & DSV41_MOE_PACKED_SCALES) ? 1 : 0;
     if (p.nsplit > 1) {
       cudaError_t e = cudaMemsetAsync(ws.cnt_dn, 0, sizeof(int) * d.Cmax * d.tiles_dn, st);
       if (e != cudaSuccess) return cuda_status(e, "memset");
     }
-    rc = qgemv_launch<WF_FP4, 1, 1>("moe_expert_down_fp4", m_w2, m_w2, hx[0], hx[1], hx[2], p,
-                                     int(d.Cmax * d.tiles_dn * p.nsplit), st);
+    if (p.rowpair)
+      rc = qgemv_launch<WF_FP4, 2, 1>("moe_expert_down_fp4_pairs", m_w2, m_w2, hx[0], hx[1], hx[2], p,
+                                       int(d.Cmax * p.tiles * p.nsplit), st);
+    else
+      rc = qgemv_launch<WF_FP4, 1, 1>("moe_expert_down_fp4", m_w2, m_w2, hx[0], hx[1], hx[2], p,
+                                       int(d.Cmax * d.tiles_dn * p.nsplit), st);
     if (rc) return rc;
   }
   }  // routed

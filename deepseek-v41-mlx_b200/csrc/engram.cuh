@@ -165,9 +165,9 @@ __global__ void __launch_bounds__(256, 4) k_engram_gather_sum(
   if (tok >= n_tok) return;
   const int64_t col = (gw % wpt) * 256 + lane * 8;
   const int soff = int(col / block);            // 8 | block keeps a chunk in one scale block
-  float acc[8];
+  uint64_t acc2[4];                             // columns (2q, 2q + 1) as fp32 pairs
 #pragma unroll
-  for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+  for (int q = 0; q < 4; ++q) acc2[q] = 0ull;
   const int64_t *ti = idx + tok * n_per_tok;
   for (int h0 = 0; h0 < n_per_tok; h0 += 32) {
     // lane l holds id h0 + l (-1 past the token's ids)
@@ -199,16 +199,23 @@ __global__ void __launch_bounds__(256, 4) k_engram_gather_sum(
       for (int u = 0; u < 8; ++u) {
         if (!in[u]) continue;
         const float s = e8m0f(uint8_t(sb[u]));
+        const uint64_t s2 = f32x2(s, s);
         uint32_t hq[4];
         e4m3x4_to_f16x4(uint32_t(v[u]), hq[0], hq[1]);
         e4m3x4_to_f16x4(uint32_t(v[u] >> 32), hq[2], hq[3]);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float2 p = h2f2(hq[j >> 1]);
-          acc[j] = __fadd_rn(acc[j], __fmul_rn((j & 1) ? p.y : p.x, s));
+        for (int q = 0; q < 4; ++q) {           // rounded product, then rounded sum
+          const float2 p = h2f2(hq[q]);
+          acc2[q] = f32x2_add(acc2[q], f32x2_mul(f32x2(p.x, p.y), s2));
         }
       }
     }
+  }
+  float acc[8];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    acc[2 * q] = f32x2_lo(acc2[q]);
+    acc[2 * q + 1] = f32x2_hi(acc2[q]);
   }
   store8(out + tok * D + col, acc);
 }

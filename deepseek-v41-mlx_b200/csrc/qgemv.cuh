@@ -70,7 +70,10 @@ struct QParams {
   int svec;                    // scale rows are NG-aligned and K % KS == 0: vector loads
   int spack;                   // FP4: scales in the decode-packed layout (k_pack_decode_sf):
                                // one 512-byte block [64 rows][8 groups] per (row tile, stage)
-  int tiles;                   // ceil(N / QG_ROWS)
+  int tiles;                   // ceil(N / QG_ROWS); ceil(N / (2 * QG_ROWS)) with rowpair
+  int rowpair;                 // NMAT = 2 over ONE matrix: "matrix" m of tile t is the 64-row
+                               // tile 2t + m (wmap1 = wmap0, scale[1] = scale[0]); needs
+                               // spack, N % (2 * QG_ROWS) == 0 and EPI_DOWN
   int nsplit;
   int kstages;                 // ceil(K / KS)
   const float *xscale;         // per x row multiplier (power of two), or null
@@ -468,8 +471,11 @@ __global__ void __launch_bounds__(QG_THREADS, QG_MIN_CTAS)
       const int xr = c.ntok <= 8 ? 8 : (c.ntok <= 16 ? 16 : 32);
       const CUtensorMap *xm = xr == 8 ? &xmap8 : (xr == 16 ? &xmap16 : &xmap32);
       const uint32_t bytes = NMAT * C::W_BYTES + C::NBOX * xr * 128;
-      const int64_t nbase = (int64_t)tile * QG_ROWS;
+      const int64_t nbase = (int64_t)tile * QG_ROWS * (p.rowpair ? 2 : 1);
       const int32_t wrow = int32_t(c.mat * p.N + nbase);
+      const int32_t wrow1 = wrow + (p.rowpair ? QG_ROWS : 0);     // matrix 1's first row
+      // packed scale blocks are per 64-row tile: rowpair tile t holds tiles 2t and 2t + 1
+      const int64_t sblk = (int64_t)c.mat * p.tiles + tile;
       for (int ks = kb; ks < ke; ++ks, ++it) {
         const int slot = it % ST;
         const uint32_t ph = (it / ST) & 1;
@@ -487,13 +493,14 @@ __global__ void __launch_bounds__(QG_THREADS, QG_MIN_CTAS)
           mbar_arrive_expect_tx(&full[slot], bytes + (packed ? NMAT * QG_ROWS * 8 : 0));
           if (WF == WF_FP4 && packed) {
 #pragma unroll
-            for (int m = 0; m < NMAT; ++m)
-              qg_bulk_load(scb + m * QG_ROWS * 8,
-                           p.scale[m] + (((int64_t)c.mat * p.tiles + tile) * p.kstages + ks) * (QG_ROWS * 8),
+            for (int m = 0; m < NMAT; ++m) {
+              const int64_t blk = p.rowpair ? 2 * sblk + m : sblk;
+              qg_bulk_load(scb + m * QG_ROWS * 8, p.scale[m] + (blk * p.kstages + ks) * (QG_ROWS * 8),
                            QG_ROWS * 8, &full[slot]);
+            }
           }
           tma_load_2d(st, &wmap0, &full[slot], ks * 128, wrow, pol_w);
-          if (NMAT == 2) tma_load_2d(st + C::W_BYTES, &wmap1, &full[slot], ks * 128, wrow, pol_w);
+          if (NMAT == 2) tma_load_2d(st + C::W_BYTES, &wmap1, &full[slot], ks * 128, wrow1, pol_w);
 #pragma unroll
           for (int b = 0; b < C::NBOX; ++b)
             tma_load_2d(st + NMAT * C::W_BYTES + b * C::XBOX_BYTES, xm, &full[slot],
@@ -533,7 +540,7 @@ __global__ void __launch_bounds__(QG_THREADS, QG_MIN_CTAS)
     chunk_prefetch(p, item + gridDim.x, nitems, pre);        // used by the next item
     const int kb = int((int64_t)p.kstages * split / p.nsplit);
     const int ke = int((int64_t)p.kstages * (split + 1) / p.nsplit);
-    const int64_t nbase = (int64_t)tile * QG_ROWS;              // row within the matrix
+    const int64_t nbase = (int64_t)tile * QG_ROWS * (p.rowpair ? 2 : 1);   // row in the matrix
     const int ntiles_x = (c.ntok + 7) / 8;                      // active n8 tiles
     float acc[NMAT][NT][4];
 #pragma unroll
@@ -789,12 +796,16 @@ __global__ void __launch_bounds__(QG_THREADS, QG_MIN_CTAS)
         const int orow = p.pair_row ? p.pair_row[q] : (q < p.npairs ? q : -1);
         if (orow < 0) continue;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int64_t nn = nbase + rowA + 8 * h;
-          if (nn >= p.N) continue;
-          float v = acc[0][n][2 * h] + acc[0][n][2 * h + 1];
-          if (p.round_out) v = round_bf16f(v);
-          reinterpret_cast<float *>(p.out)[(int64_t)orow * p.ldo + nn] = v;
+        for (int m = 0; m < NMAT; ++m) {
+          if (m > 0 && !p.rowpair) break;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int64_t nn = nbase + m * QG_ROWS + rowA + 8 * h;
+            if (nn >= p.N) continue;
+            float v = acc[m][n][2 * h] + acc[m][n][2 * h + 1];
+            if (p.round_out) v = round_bf16f(v);
+            reinterpret_cast<float *>(p.out)[(int64_t)orow * p.ldo + nn] = v;
+          }
         }
         continue;
       }

@@ -139,11 +139,13 @@ class MoE:
     multiples of 256) the routed experts' ue8m0 scales are rearranged once into the
     decode-packed layout (``dsv41_moe_decode_pack``: one contiguous block per 64-row
     tile and K stage) and rebuilt when a scale tensor changes; the decode kernels then
-    fetch each stage's scales with one bulk copy.
+    fetch each stage's scales with one bulk copy.  With packed scales the routed down
+    projection runs two 64-row tiles of an expert per work item once those items fill a
+    wave of CTAs; ``row_pair_down=False`` keeps it on single tiles (same bits).
     """
 
     def __init__(self, args, round_bf16: bool = True, cuda_graph: bool = True,
-                 pack_decode_scales: bool = True):
+                 pack_decode_scales: bool = True, row_pair_down: bool = True):
         self.args = args
         self.dim = args.dim
         self.gate = Gate(args)
@@ -154,6 +156,7 @@ class MoE:
         self.round_bf16 = round_bf16
         self.cuda_graph = cuda_graph
         self.pack_decode_scales = pack_decode_scales
+        self.row_pair_down = row_pair_down
         self._dpack = None
         self._dpack_key = None
         self._ws = None
@@ -165,8 +168,9 @@ class MoE:
         objs = (self.gate.weight, self.gate.bias, e.gate_proj.weight, e.gate_proj.scales,
                 e.up_proj.weight, e.up_proj.scales, e.down_proj.weight, e.down_proj.scales,
                 s.w1.weight, s.w1.scales, s.w3.weight, s.w3.scales, s.w2.weight, s.w2.scales)
-        return tuple((id(o), o.data_ptr() if hasattr(o, "data_ptr") else 0,
-                      getattr(o, "_version", 0)) for o in objs)
+        return (self.pack_decode_scales, self.row_pair_down) + tuple(
+            (id(o), o.data_ptr() if hasattr(o, "data_ptr") else 0, getattr(o, "_version", 0))
+            for o in objs)
 
     def _decode_into(self, xf, y, weights, indices, W, ws, cfg):
         T = xf.shape[0]
@@ -214,7 +218,8 @@ class MoE:
                            topk=a.n_activated_experts, score_func=L.SCORE_FUNCS[a.score_func],
                            gate_temp=float(a.gate_temp), norm_topk_prob=int(a.norm_topk_prob),
                            route_scale=float(a.route_scale), swiglu_limit=float(a.swiglu_limit),
-                           flags=(L.MOE_ROUND_BF16 if self.round_bf16 else 0) | flags)
+                           flags=(L.MOE_ROUND_BF16 if self.round_bf16 else 0)
+                           | (0 if self.row_pair_down else L.MOE_NO_ROWPAIR) | flags)
 
     def _weights(self):
         t = _torch()

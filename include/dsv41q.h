@@ -72,6 +72,11 @@ extern "C" {
  * E*I*(D/32), s2 at 2*E*I*(D/32) bytes) instead of the release layout.  Needs dim and inter
  * multiples of 256 and 16-byte aligned pointers.  Rejected by the prefill entries. */
 #define DSV41_MOE_PACKED_SCALES 8
+/* With packed scales, dim % 128 == 0 and enough routed work to fill a wave of CTAs, the
+ * routed down projection runs two 64-row tiles of one expert per work item (shared
+ * activation fragments, two MMA chains per warp).  This flag keeps it on single 64-row
+ * tiles; both give the same bits whenever they pick the same K split. */
+#define DSV41_MOE_NO_ROWPAIR 16
 
 /* ---- library ------------------------------------------------------------ */
 const char *dsv41_get_last_error(void);

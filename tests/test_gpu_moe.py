@@ -265,3 +265,38 @@ def test_moe_decode_pack_rejected_by_prefill(cuda):
                                     L.dtype_code(torch.float32), L.ptr(y), L.ptr(ws), ws.numel(),
                                     L.stream_of(x))
     assert st != 0
+
+
+@pytest.mark.parametrize("T", [16, 40])
+def test_moe_decode_row_pair_down(cuda, T):
+    """Routed down projection on pairs of 64-row tiles (chosen once its items fill a wave of
+    CTAs: 64 experts x 2048 / 128 pairs here) gives the same bits as single tiles, direct and
+    graphed, and matches the oracle."""
+    rng = np.random.default_rng(500 + T)
+    E, D, I, k = 64, 2048, 256, 6
+    p = moe_params(rng, E, D, I)
+    args = _args(E, D, I, k)
+    xb, xf = bf16_acts(rng, T, D)
+    outs = []
+    for pair in (True, False):
+        for graph in (False, True):
+            m = _moe(p, args, round_bf16=False)
+            m.row_pair_down, m.cuda_graph = pair, graph
+            if not graph:
+                L.prof_enable(True)
+            y, w, idx = m(_bf(xb), with_routing=True, out_dtype=torch.float32)
+            ye = m.experts(_bf(xb), idx)
+            if not graph:
+                torch.cuda.synchronize()
+                names = set(L.prof_report())
+                L.prof_enable(False)
+                assert ("moe_expert_down_fp4_pairs" in names) == pair
+                assert ("moe_expert_down_fp4" in names) == (not pair)
+            outs.append((y, w, idx, ye))
+    for y, w, idx, ye in outs[1:]:
+        assert torch.equal(idx, outs[0][2]) and torch.equal(w, outs[0][1])
+        assert torch.equal(y, outs[0][0]) and torch.equal(ye, outs[0][3])
+    y, w, idx, _ = outs[0]
+    w, idx = w.cpu().numpy(), idx.cpu().numpy()
+    want, _, _ = OM.moe_forward(xf, p, _cfg(args), round_bf16_io=False, routing=(w, idx))
+    assert rel_fro(y.cpu().numpy(), want) < 1e-5
