@@ -177,7 +177,7 @@ class MoE:
         L.call("dsv41_moe_decode", C.byref(cfg), C.byref(W), L.ptr(xf), T, L.dtype_code(y.dtype),
                L.ptr(y), L.ptr(weights), L.ptr(indices), L.ptr(ws), ws.numel(), L.stream_of(xf))
 
-    def _graph_call(self, xf, odt):
+    def _graph_call(self, xf, odt, with_routing=True):
         t = _torch()
         sig = self._sig()
         if sig != self._graph_sig:
@@ -209,6 +209,8 @@ class MoE:
         g, sx, sy, sw, si = ent[:5]
         sx.copy_(xf)
         g.replay()
+        if not with_routing:
+            return sy.clone(), None, None
         return sy.clone(), sw.clone(), si.clone()
 
     # -- plumbing --------------------------------------------------------------
@@ -305,7 +307,7 @@ class MoE:
         T = xf.shape[0]
         odt = out_dtype or (t.float32 if xt.dtype == t.float32 else t.bfloat16)
         if self.cuda_graph and not t.cuda.is_current_stream_capturing():
-            y, weights, indices = self._graph_call(xf, odt)
+            y, weights, indices = self._graph_call(xf, odt, with_routing)
             y = y.reshape(shape)
             return (y, weights, indices) if with_routing else y
         cfg, W = self._decode_args()
