@@ -515,7 +515,8 @@ def engram_measurement(q, torch, dev, flush, stream, K, W, vocab=4_000_000):
     """d5: engram table fp8 e4m3 [96,000,xxx x 1024] (one ue8m0 per row, [115, 127]) built on
     the device, 24 rows per token (2/3/4-gram x 8 heads, one layer, primes from 4,000,000)
     hashed from uniform compressed ids in [0, 99092); a step = hash + gather + dequant + fp32
-    sum -> bf16 [T, 1024].  Bytes per token: 24 x (1024 + 1) read + 2048 written.  A smaller
+    sum -> bf16 [T, 1024] through EngramHasher.lookup_sum (one launch at T=1, the hasher then
+    the gather-sum above its fused_max_positions); ``ms_two_step`` always times the latter.  Bytes per token: 24 x (1024 + 1) read + 2048 written.  A smaller
     ``vocab`` (engram_vocab_size) gives a table of about 24 x vocab rows, for ncu captures."""
     import types
     import numpy as np
@@ -548,6 +549,10 @@ def engram_measurement(q, torch, dev, flush, stream, K, W, vocab=4_000_000):
                               generator=g)
 
         def step(i, T=T, start=start):
+            # hash + gather-sum (one launch up to EngramHasher.fused_max_positions positions)
+            return hasher.lookup_sum(emb, ids[i % 8], start, cache)
+
+        def step2(i, T=T, start=start):
             idx = hasher(ids[i % 8], start, cache)
             return emb.gather_sum(idx.reshape(T, -1))
 
@@ -556,8 +561,13 @@ def engram_measurement(q, torch, dev, flush, stream, K, W, vocab=4_000_000):
         ms = statistics.median(timed_steps(torch, lambda i: gr[i % 8].replay(), K, W, flush,
                                            stream))
         ms_host = statistics.median(timed_steps(torch, step, K, W, flush, stream))
+        gr2 = graphed(torch, [lambda c=c: step2(c) for c in range(8)])
+        ms2 = statistics.median(timed_steps(torch, lambda i: gr2[i % 8].replay(), K, W, flush,
+                                            stream))
+        del gr2
         byts = T * (24 * (d + 1) + 2 * d)
         out[f"engram_T{T}"] = {"ms": round(ms, 4), "ms_eager": round(ms_host, 4),
+                               "ms_two_step": round(ms2, 4),
                                "tok_s": round(T / (ms / 1e3), 1),
                                "gbs": round(byts / (ms / 1e3) / 1e9, 1),
                                "frac_hbm": round(byts / (ms / 1e3) / 1e9 / hbm_peak, 4),

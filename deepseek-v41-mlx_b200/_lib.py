@@ -107,6 +107,8 @@ PROTOTYPES = {
     "dsv41_moe_ep_combine": (_I, [_P, _P, _P, _P, _I64, _I, _I64, _I, _P, _P]),
     "dsv41_engram_hash": (_I, [_P, _I64, _I64, _I64, _P, _I64, _P, _I64, _P, _P, _P, _I, _I, _I,
                                _I64, _P, _P]),
+    "dsv41_engram_lookup_sum": (_I, [_P, _I64, _I64, _I64, _P, _I64, _P, _I64, _P, _P, _P, _P, _I,
+                                     _I, _I, _I, _I64, _P, _I64, _I64, _I64, _I64, _I, _P, _P]),
     "dsv41_engram_gather_rows": (_I, [_P, _P, _I64, _I64, _I64, _I64, _P, _I64, _I, _P, _P]),
     "dsv41_engram_gather_sum": (_I, [_P, _P, _I64, _I64, _I64, _I64, _P, _I64, _I, _I, _P, _P]),
     "dsv41_engram_row_bytes": (_SZ, [_I64, _I64]),

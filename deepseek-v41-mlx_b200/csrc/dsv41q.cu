@@ -1985,6 +1985,54 @@ extern "C" int dsv41_engram_hash(const int64_t *input_ids, int64_t B, int64_t L,
   return DSV41_OK;
 }
 
+extern "C" int dsv41_engram_lookup_sum(const int64_t *input_ids, int64_t B, int64_t L,
+                                       int64_t start_pos, const int64_t *token_map, int64_t vocab,
+                                       int64_t *ids_cache, int64_t max_seq,
+                                       const int64_t *multipliers, const int64_t *primes,
+                                       const int64_t *offsets, const uint64_t *reciprocals,
+                                       int n_layers, int layer, int max_ngram, int n_heads,
+                                       int64_t pad_id, const void *packed, int64_t n_rows, int64_t row_lo,
+                                       int64_t d, int64_t block, int out_dtype, void *out,
+                                       void *stream) {
+  DSV41_REQUIRE(B >= 0 && L >= 0 && start_pos >= 0 && start_pos + L <= max_seq,
+                DSV41_ERR_BAD_SHAPE, "positions [start_pos, start_pos+L) exceed the id cache");
+  DSV41_REQUIRE(n_layers >= 1 && layer >= 0 && layer < n_layers && max_ngram >= 2 &&
+                    n_heads >= 1 && vocab >= 1,
+                DSV41_ERR_BAD_ARG, "bad layout");
+  DSV41_REQUIRE((max_ngram - 1) * n_heads <= 32 && max_ngram <= ENGRAM_MAX_G,
+                DSV41_ERR_UNSUPPORTED,
+                "lookup_sum needs (max_ngram - 1) * n_heads <= 32 rows a position, max_ngram <= 8");
+  DSV41_REQUIRE(d == 256 || d == 512 || d == 1024, DSV41_ERR_UNSUPPORTED,
+                "lookup_sum supports d in {256, 512, 1024}");
+  DSV41_REQUIRE(block >= 8 && block % 8 == 0 && d % block == 0 && n_rows >= 0,
+                DSV41_ERR_BAD_SHAPE, "need 8 | block and block | d");
+  DSV41_REQUIRE(out_dtype == DSV41_F32 || out_dtype == DSV41_BF16, DSV41_ERR_BAD_DTYPE,
+                "out_dtype must be F32 or BF16");
+  if (B == 0 || L == 0) return DSV41_OK;
+  DSV41_REQUIRE(input_ids && token_map && ids_cache && multipliers && primes && offsets && out &&
+                    (packed || n_rows == 0),
+                DSV41_ERR_BAD_ARG, "NULL pointer");
+  DSV41_REQUIRE(aligned(packed, 16) && aligned(out, 16), DSV41_ERR_MISALIGNED,
+                "packed rows and out must be 16-byte aligned");
+  cudaStream_t st = STREAM(stream);
+  ProfScope prof("engram_lookup_sum", st);
+  const int G = max_ngram, H = n_heads, cols = (G - 1) * H;
+  const int64_t rb = int64_t(dsv41_engram_row_bytes(d, block));
+  const unsigned blocks = unsigned(ceil_div(B * L * (d / 256) * 32, 256));
+  const uint8_t *tab = static_cast<const uint8_t *>(packed);
+#define LS(T)                                                                                    \
+  k_engram_lookup_sum<T><<<blocks, 256, 0, st>>>(                                                \
+      input_ids, B, L, start_pos, token_map, vocab, ids_cache, max_seq, multipliers + layer * G, \
+      primes + (int64_t)layer * cols, offsets + (int64_t)layer * cols,                          \
+      reciprocals ? reciprocals + (int64_t)layer * cols : nullptr, G, H, pad_id, tab, n_rows,   \
+      row_lo, d, block, rb, (T *)out)
+  if (out_dtype == DSV41_F32) LS(float);
+  else LS(__nv_bfloat16);
+#undef LS
+  DSV41_CHECK_LAUNCH("engram_lookup_sum");
+  return DSV41_OK;
+}
+
 extern "C" int dsv41_engram_gather_rows(const uint8_t *table, const uint8_t *scale, int64_t rows,
                                         int64_t row_lo, int64_t d, int64_t block,
                                         const int64_t *idx, int64_t n_idx, int out_dtype,

@@ -141,6 +141,68 @@ __global__ void k_engram_gather_rows(const uint8_t *__restrict__ table,
   }
 }
 
+// Sums into acc2 (columns lane*8 .. +8 of the warp's 256, as fp32 pairs) the nh <= 32 rows
+// whose ids lane l holds in `mine` (-1 past the token's ids), in lane order: 8 rows in
+// flight, streaming loads, each row's scale byte loaded with its codes.  Ids are
+// warp-uniform after the shuffle; rows outside the table are skipped.
+template <bool PEERS>
+__device__ __forceinline__ void gs_rows(uint64_t (&acc2)[4], int64_t mine, int nh, int64_t col,
+                                        int soff, const uint8_t *__restrict__ table,
+                                        const uint8_t *__restrict__ scale, int64_t rows,
+                                        int64_t row_lo, int64_t tld, int64_t sld,
+                                        const uint8_t *const *__restrict__ tabs,
+                                        const uint8_t *const *__restrict__ scs, int nsh,
+                                        int64_t total) {
+  for (int h = 0; h < nh; h += 8) {               // h + u <= 31: every source lane exists
+    uint64_t v[8];
+    uint32_t sb[8];
+    bool in[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int64_t id = __shfl_sync(0xffffffffu, mine, h + u);   // warp-uniform
+      const uint8_t *rt, *rs;                    // this row's codes and scales
+      if (PEERS) {
+        const int64_t sh = id >= 0 ? id / rows : -1, local = id - sh * rows;
+        in[u] = id >= 0 && id < total && sh < nsh;   // the last shard may be shorter
+        rt = in[u] ? tabs[sh] + local * tld : nullptr;
+        rs = in[u] ? scs[sh] + local * sld : nullptr;
+      } else {
+        const int64_t local = id - row_lo;
+        in[u] = id >= 0 && local >= 0 && local < rows;
+        rt = table + local * tld;
+        rs = scale + local * sld;
+      }
+      v[u] = in[u] ? __ldcs(reinterpret_cast<const unsigned long long *>(rt + col)) : 0ull;
+      sb[u] = in[u] ? uint32_t(rs[soff]) : 0u;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      if (!in[u]) continue;
+      const float s = e8m0f(uint8_t(sb[u]));
+      const uint64_t s2 = f32x2(s, s);
+      uint32_t hq[4];
+      e4m3x4_to_f16x4(uint32_t(v[u]), hq[0], hq[1]);
+      e4m3x4_to_f16x4(uint32_t(v[u] >> 32), hq[2], hq[3]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {             // rounded product, then rounded sum
+        const float2 p = h2f2(hq[q]);
+        acc2[q] = f32x2_add(acc2[q], f32x2_mul(f32x2(p.x, p.y), s2));
+      }
+    }
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void gs_store(T *o, const uint64_t (&acc2)[4]) {
+  float acc[8];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    acc[2 * q] = f32x2_lo(acc2[q]);
+    acc[2 * q + 1] = f32x2_hi(acc2[q]);
+  }
+  store8(o, acc);
+}
+
 // Warps per token = d / 256: a warp covers 256 columns, its lanes 8-column chunks at
 // lane*8 (coalesced 256-byte spans); rows summed in column order, fp32, 8 rows in flight per
 // warp, table rows streamed (read once, not kept in L1/L2).  The token's ids are read once,
@@ -165,59 +227,92 @@ __global__ void __launch_bounds__(256, 4) k_engram_gather_sum(
   if (tok >= n_tok) return;
   const int64_t col = (gw % wpt) * 256 + lane * 8;
   const int soff = int(col / block);            // 8 | block keeps a chunk in one scale block
-  uint64_t acc2[4];                             // columns (2q, 2q + 1) as fp32 pairs
-#pragma unroll
-  for (int q = 0; q < 4; ++q) acc2[q] = 0ull;
+  uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};  // columns (2q, 2q + 1) as fp32 pairs
   const int64_t *ti = idx + tok * n_per_tok;
   for (int h0 = 0; h0 < n_per_tok; h0 += 32) {
     // lane l holds id h0 + l (-1 past the token's ids)
     const int64_t mine = h0 + lane < n_per_tok ? ti[h0 + lane] : -1;
-    const int nh = min(32, n_per_tok - h0);
-    for (int h = 0; h < nh; h += 8) {             // h + u <= 31: every source lane exists
-      uint64_t v[8];
-      uint32_t sb[8];
-      bool in[8];
+    gs_rows<PEERS>(acc2, mine, min(32, n_per_tok - h0), col, soff, table, scale, rows, row_lo,
+                   tld, sld, tabs, scs, nsh, total);
+  }
+  gs_store(out + tok * D + col, acc2);
+}
+
+// a15 + a16 in one pass: the (G-1)*H <= 32 row ids of each position of one hash layer
+// (k_engram_compress + k_engram_hash, same arithmetic) computed by the lanes that would have
+// loaded them, summed as rows of a packed table (codes then scale bytes, rb bytes a row).
+// Lane c < (G-1)*H hashes column c = (shift-1)*H + head: the compressed ids of positions
+// pos - s (s <= shift) come from input_ids through token_map inside this call's positions and
+// from the id cache before them (pad_id before position 0); the first warp of each position
+// writes that position's compressed id into the cache, as the hasher does.  The cache is read
+// only below start and written only from start on, so no position is both read and written.
+// recips[c] = floor((2^64 - 1) / prime[c]) (0 for prime <= 1) when given; otherwise each lane
+// divides for its own prime.  No shared memory and no barrier: a warp's hash loads (its
+// lookback unrolled, G <= ENGRAM_MAX_G) issue together and its row loads follow at once.
+constexpr int ENGRAM_MAX_G = 8;
+template <typename T>
+__global__ void __launch_bounds__(256, 4) k_engram_lookup_sum(
+    const int64_t *__restrict__ ids, int64_t B, int64_t L, int64_t start,
+    const int64_t *__restrict__ token_map, int64_t vocab, int64_t *__restrict__ cache,
+    int64_t max_seq, const int64_t *__restrict__ mult, const int64_t *__restrict__ primes,
+    const int64_t *__restrict__ offsets, const uint64_t *__restrict__ recips, int G, int H,
+    int64_t pad_id, const uint8_t *__restrict__ table, int64_t rows, int64_t row_lo, int64_t D,
+    int64_t block, int64_t rb, T *__restrict__ out) {
+  const int64_t gw = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int wpt = int(D / 256);
+  const int64_t tok = gw / wpt;
+  if (tok >= B * L) return;
+  const int cols = (G - 1) * H;
+  const int64_t b = tok / L, l = tok % L, pos = start + l;
+  const int64_t *bids = ids + b * L;
+  int64_t *bcache = cache + b * max_seq;
+  auto compressed = [&](int64_t q) -> int64_t {      // position q's compressed id, q <= pos
+    if (q < start) return bcache[q];
+    int64_t id = bids[q - start];
+    if (id < 0 || id >= vocab) {
+      dev_flag(DSV41_DEVST_BAD_INDEX);
+      id = 0;
+    }
+    return token_map[id];
+  };
+  int64_t mine = -1;
+  if (lane < cols) {
+    const int shift = lane / H + 1;
+    const uint64_t p = uint64_t(primes[lane]);
+    const int64_t off = offsets[lane];
+    int64_t tk[ENGRAM_MAX_G], mu[ENGRAM_MAX_G];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int64_t id = __shfl_sync(0xffffffffu, mine, h + u);   // warp-uniform
-        const uint8_t *rt, *rs;                    // this row's codes and scales
-        if (PEERS) {
-          const int64_t sh = id >= 0 ? id / rows : -1, local = id - sh * rows;
-          in[u] = id >= 0 && id < total && sh < nsh;   // the last shard may be shorter
-          rt = in[u] ? tabs[sh] + local * tld : nullptr;
-          rs = in[u] ? scs[sh] + local * sld : nullptr;
-        } else {
-          const int64_t local = id - row_lo;
-          in[u] = id >= 0 && local >= 0 && local < rows;
-          rt = table + local * tld;
-          rs = scale + local * sld;
-        }
-        v[u] = in[u] ? __ldcs(reinterpret_cast<const unsigned long long *>(rt + col)) : 0ull;
-        sb[u] = in[u] ? uint32_t(rs[soff]) : 0u;
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        if (!in[u]) continue;
-        const float s = e8m0f(uint8_t(sb[u]));
-        const uint64_t s2 = f32x2(s, s);
-        uint32_t hq[4];
-        e4m3x4_to_f16x4(uint32_t(v[u]), hq[0], hq[1]);
-        e4m3x4_to_f16x4(uint32_t(v[u] >> 32), hq[2], hq[3]);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {           // rounded product, then rounded sum
-          const float2 p = h2f2(hq[q]);
-          acc2[q] = f32x2_add(acc2[q], f32x2_mul(f32x2(p.x, p.y), s2));
-        }
+    for (int s = 0; s < ENGRAM_MAX_G; ++s) {
+      if (s <= shift) {
+        tk[s] = pos < s ? pad_id : compressed(pos - s);
+        mu[s] = mult[s];
       }
     }
-  }
-  float acc[8];
+    int64_t rolling = 0;
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    acc[2 * q] = f32x2_lo(acc2[q]);
-    acc[2 * q + 1] = f32x2_hi(acc2[q]);
+    for (int s = 0; s < ENGRAM_MAX_G; ++s) {
+      if (s <= shift) {
+        const int64_t prod = tk[s] * mu[s];
+        rolling = s == 0 ? prod : (rolling ^ prod);
+      }
+    }
+    const uint64_t x = uint64_t(rolling);
+    uint64_t r = 0;
+    if (p > 1) {
+      const uint64_t m = recips ? recips[lane] : ~0ull / p;
+      r = x - __umul64hi(x, m) * p;
+      if (r >= p) r -= p;
+    }
+    mine = int64_t(r) + off;
   }
-  store8(out + tok * D + col, acc);
+  if (gw % wpt == 0 && lane == 0) bcache[pos] = compressed(pos);
+  const int64_t col = (gw % wpt) * 256 + lane * 8;
+  const int soff = int(col / block);
+  uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
+  gs_rows<false>(acc2, mine, cols, col, soff, table, table + D, rows, row_lo, rb, rb, nullptr,
+                 nullptr, 0, 0);
+  gs_store(out + tok * D + col, acc2);
 }
 
 // Row-sharded tables: the owner of rows [row_lo, row_lo + rows) copies the raw rows

@@ -351,6 +351,26 @@ int dsv41_engram_hash(const int64_t *input_ids, int64_t B, int64_t L, int64_t st
                       const int64_t *offsets, int n_layers, int max_ngram, int n_heads,
                       int64_t pad_id, int64_t *out, void *stream);
 
+/* ---- a15 + a16 in one launch: hash layer `layer` of the dsv41_engram_hash layout and sum
+ * its (G-1)*H <= 32 rows a position from a packed table -- EngramHasher.__call__
+ * (deepseek_v41_mlx/engram.py:154-180) followed by EngramEmbedding.__call__ (:197-203) and
+ * the sum over the hashed rows (upstream Engram.forward's embedding sum,
+ * docs/reference/model.py:344-365), without writing the ids.  The id cache is updated as
+ * dsv41_engram_hash updates it.  packed: [n_rows, dsv41_engram_row_bytes(d, block)] rows
+ * (dsv41_engram_pack_rows with idx = NULL), holding table rows [row_lo, row_lo + n_rows);
+ * other ids read as zero rows.  reciprocals: NULL, or uint64 [nL, G-1, H] =
+ * floor((2^64 - 1) / prime) (0 where prime <= 1), computed once with the layout, which spares
+ * every launch a 64-bit division per prime.  Needs (G-1)*H <= 32 and G <= 8.
+ * out f32/bf16 [B, L, d], the same bits as dsv41_engram_hash then dsv41_engram_sum_rows. */
+int dsv41_engram_lookup_sum(const int64_t *input_ids, int64_t B, int64_t L, int64_t start_pos,
+                            const int64_t *token_map, int64_t vocab, int64_t *ids_cache,
+                            int64_t max_seq, const int64_t *multipliers, const int64_t *primes,
+                            const int64_t *offsets, const uint64_t *reciprocals, int n_layers,
+                            int layer, int max_ngram, int n_heads, int64_t pad_id,
+                            const void *packed, int64_t n_rows,
+                            int64_t row_lo, int64_t d, int64_t block, int out_dtype, void *out,
+                            void *stream);
+
 /* ---- a16: engram row gather (deepseek_v41_mlx/engram.py:197-203; upstream
  * ParallelEngramEmbedding.forward docs/reference/model.py:312-325).
  * table u8 [rows, d] e4m3 + scale u8 [rows, d/block]; idx int64 [n_idx]

@@ -243,3 +243,52 @@ def test_packed_table_lookups_identical(cuda, d, block, row_lo):
         if d in (256, 512, 1024):
             assert torch.equal(a.gather_sum(idx, dt), b.gather_sum(idx, dt))
         assert torch.equal(a(idx, dt), b(idx, dt))
+
+
+@pytest.mark.parametrize("d,block,shard", [(512, 64, False), (1024, 1024, True), (256, 32, False)])
+def test_lookup_sum_matches_hash_then_sum(cuda, d, block, shard):
+    """The fused hash + row sum (EngramHasher.lookup_sum, one launch) gives the same bits as
+    the hasher followed by gather_sum on its ids, for the second of two hash layers, through
+    one id cache over two chunks (pad positions at the start, cached ids after), B = 2, fp32
+    and bf16 out; the id cache ends the same.  shard: the table holds rows [300, n - 300)
+    only, so some ids read zero rows."""
+    rng = np.random.default_rng(d + block)
+    layer_ids, G, H, vocab = (1, 5), 4, 8, 2000
+    primes, offsets = OE.build_layout(len(layer_ids), G, H, vocab)
+    sums = primes.reshape(len(layer_ids), -1).sum(-1)
+    tm = rng.integers(0, 500, size=1200, dtype=np.int64)
+    tm[7] = 499
+    args = types.SimpleNamespace(engram_layer_ids=layer_ids,
+                                 engram_num_embeddings=tuple(int(v) for v in sums),
+                                 engram_max_ngram_size=G, engram_vocab_size=vocab,
+                                 engram_n_heads=H, engram_pad_id=2,
+                                 engram_compressed_vocab_size=500)
+    h = q.engram.EngramHasher(args, tm)
+    n = int(sums[1])
+    lo, hi = (300, n - 300) if shard else (0, n)
+    table = rng.integers(0, 256, size=(hi - lo, d), dtype=np.uint8)
+    table[(table & 0x7F) == 0x7F] = 0
+    scale = rng.integers(112, 130, size=(hi - lo, d // block), dtype=np.uint8)
+    emb = q.engram.EngramEmbedding(hi - lo, d, block, row_lo=lo)
+    emb.weight, emb.scale = _d(table), _d(scale)
+    emb.pack()
+    ids = rng.integers(0, 1200, size=(2, 37), dtype=np.int64)
+    L1 = 5
+    recips = h._dev["recips"]
+    for dt in (torch.float32, torch.bfloat16):
+        # given reciprocals, the kernel's own division (NULL reciprocals), the two-launch form
+        for given, fused_max in ((True, 4096), (False, 4096), (True, 0)):
+            h._dev["recips"] = recips if given else None
+            h.fused_max_positions = fused_max
+            ca = torch.zeros((2, 64), dtype=torch.int64, device="cuda")
+            cb = torch.zeros_like(ca)
+            for s0, s1 in ((0, L1), (L1, ids.shape[1])):
+                chunk = _d(ids[:, s0:s1])
+                got = h.lookup_sum(emb, chunk, s0, ca, layer=1, out_dtype=dt)
+                hid = h(chunk, s0, cb)
+                want = emb.gather_sum(hid[:, :, 1], dt)
+                assert got.shape == (2, s1 - s0, d)
+                assert torch.equal(got, want)
+                assert torch.equal(ca, cb)
+    h._dev["recips"] = recips
+    h.fused_max_positions = q.engram.EngramHasher.fused_max_positions
