@@ -307,7 +307,9 @@ class ParallelEngramEmbedding:
     all_to_all_single delivers them, rank r dequantizes (``__call__``) or sums them per
     token in head order (``gather_sum``), and all_gather_into_tensor gives every rank the
     whole result.  Upstream's masked lookup + all_reduce gives the same rows; this moves
-    the fp8 rows once instead of reducing bf16 rows over all ranks.
+    the fp8 rows once instead of reducing bf16 rows over all ranks.  On CUDA the shards are
+    read in place over NVLink instead (peer mappings); there, up to
+    ``replicate_max_tokens`` tokens every rank sums all of them and no collective runs.
     """
 
     def __init__(self, num_embeddings: int, dim: int, block: int = 32, rank=None, world=None,
@@ -430,11 +432,25 @@ class ParallelEngramEmbedding:
                 L.call("dsv41_ipc_close", base)
             self._peer = None
 
+    # Up to this many tokens a call, every rank sums all of them from the shards in place and
+    # no collective runs (a T=1 lookup is then a few NVLink row reads); above it each rank
+    # sums its slice of the tokens and the slices are all-gathered, so that no rank reads
+    # every row.  Same kernel, same rows, same order either way.
+    replicate_max_tokens = 64
+
     def _peer_sum(self, idx2, odt):
-        """This rank's token slice summed from the shards in place, then all-gathered."""
+        """The tokens summed from the shards in place: all of them on every rank (small T),
+        or this rank's slice, then all-gathered."""
         t = L.torch()
         tabs, scs = self._map_peers(idx2.device)[:2]
         T, H = idx2.shape
+        if T <= self.replicate_max_tokens:
+            out = t.empty((T, self.dim), dtype=odt, device=idx2.device)
+            sl = idx2.contiguous()
+            L.call("dsv41_engram_gather_sum_peers", L.ptr(tabs), L.ptr(scs), self.world,
+                   self.part, self.num_embeddings, self.dim, self.block, L.ptr(sl), T, H,
+                   L.dtype_code(odt), L.ptr(out), L.stream_of(sl))
+            return out
         per = max(1, -(-T // self.world))
         t0 = min(T, self.rank * per)
         t1 = min(T, t0 + per)
