@@ -675,8 +675,9 @@ def run_engram_ep(args):
                               generator=gi)
 
         def step(i, T=T, start=start):
-            idx = hasher(ids[i % 8], start, cache)
-            return emb.gather_sum(idx.reshape(T, -1))
+            # up to replicate_max_tokens one launch reading the peers' shards in place;
+            # above it the hasher, then the sliced gather-sum and its all-gather
+            return hasher.lookup_sum(emb, ids[i % 8], start, cache)
 
         for i in range(args.warmup):
             step(i)

@@ -109,6 +109,9 @@ PROTOTYPES = {
                                _I64, _P, _P]),
     "dsv41_engram_lookup_sum": (_I, [_P, _I64, _I64, _I64, _P, _I64, _P, _I64, _P, _P, _P, _P, _I,
                                      _I, _I, _I, _I64, _P, _I64, _I64, _I64, _I64, _I, _P, _P]),
+    "dsv41_engram_lookup_sum_peers": (_I, [_P, _I64, _I64, _I64, _P, _I64, _P, _I64, _P, _P, _P,
+                                           _P, _I, _I, _I, _I, _I64, _P, _P, _I, _I64, _I64,
+                                           _I64, _I64, _I, _P, _P]),
     "dsv41_engram_gather_rows": (_I, [_P, _P, _I64, _I64, _I64, _I64, _P, _I64, _I, _P, _P]),
     "dsv41_engram_gather_sum": (_I, [_P, _P, _I64, _I64, _I64, _I64, _P, _I64, _I, _I, _P, _P]),
     "dsv41_engram_row_bytes": (_SZ, [_I64, _I64]),

@@ -2024,12 +2024,58 @@ extern "C" int dsv41_engram_lookup_sum(const int64_t *input_ids, int64_t B, int6
   k_engram_lookup_sum<T><<<blocks, 256, 0, st>>>(                                                \
       input_ids, B, L, start_pos, token_map, vocab, ids_cache, max_seq, multipliers + layer * G, \
       primes + (int64_t)layer * cols, offsets + (int64_t)layer * cols,                          \
-      reciprocals ? reciprocals + (int64_t)layer * cols : nullptr, G, H, pad_id, tab, n_rows,   \
-      row_lo, d, block, rb, (T *)out)
+      reciprocals ? reciprocals + (int64_t)layer * cols : nullptr, G, H, pad_id, tab, tab + d,  \
+      n_rows, row_lo, d, block, rb, rb, (T *)out)
   if (out_dtype == DSV41_F32) LS(float);
   else LS(__nv_bfloat16);
 #undef LS
   DSV41_CHECK_LAUNCH("engram_lookup_sum");
+  return DSV41_OK;
+}
+
+extern "C" int dsv41_engram_lookup_sum_peers(
+    const int64_t *input_ids, int64_t B, int64_t L, int64_t start_pos, const int64_t *token_map,
+    int64_t vocab, int64_t *ids_cache, int64_t max_seq, const int64_t *multipliers,
+    const int64_t *primes, const int64_t *offsets, const uint64_t *reciprocals, int n_layers,
+    int layer, int max_ngram, int n_heads, int64_t pad_id, const uint64_t *tables,
+    const uint64_t *scales, int nsh, int64_t rows, int64_t total, int64_t d, int64_t block,
+    int out_dtype, void *out, void *stream) {
+  DSV41_REQUIRE(B >= 0 && L >= 0 && start_pos >= 0 && start_pos + L <= max_seq,
+                DSV41_ERR_BAD_SHAPE, "positions [start_pos, start_pos+L) exceed the id cache");
+  DSV41_REQUIRE(n_layers >= 1 && layer >= 0 && layer < n_layers && max_ngram >= 2 &&
+                    n_heads >= 1 && vocab >= 1,
+                DSV41_ERR_BAD_ARG, "bad layout");
+  DSV41_REQUIRE((max_ngram - 1) * n_heads <= 32 && max_ngram <= ENGRAM_MAX_G,
+                DSV41_ERR_UNSUPPORTED,
+                "lookup_sum needs (max_ngram - 1) * n_heads <= 32 rows a position, max_ngram <= 8");
+  DSV41_REQUIRE(d == 256 || d == 512 || d == 1024, DSV41_ERR_UNSUPPORTED,
+                "lookup_sum supports d in {256, 512, 1024}");
+  DSV41_REQUIRE(nsh >= 1 && rows >= 1 && total >= 0 && total <= rows * nsh && block >= 8 &&
+                    block % 8 == 0 && d % block == 0,
+                DSV41_ERR_BAD_SHAPE, "need shards, 8 | block and block | d");
+  DSV41_REQUIRE(out_dtype == DSV41_F32 || out_dtype == DSV41_BF16, DSV41_ERR_BAD_DTYPE,
+                "out_dtype must be F32 or BF16");
+  if (B == 0 || L == 0) return DSV41_OK;
+  DSV41_REQUIRE(input_ids && token_map && ids_cache && multipliers && primes && offsets && out &&
+                    tables && scales,
+                DSV41_ERR_BAD_ARG, "NULL pointer");
+  DSV41_REQUIRE(aligned(out, 16), DSV41_ERR_MISALIGNED, "out must be 16-byte aligned");
+  cudaStream_t st = STREAM(stream);
+  ProfScope prof("engram_lookup_sum_peers", st);
+  const int G = max_ngram, H = n_heads, cols = (G - 1) * H;
+  const unsigned blocks = unsigned(ceil_div(B * L * (d / 256) * 32, 256));
+  const auto *tabs = reinterpret_cast<const uint8_t *const *>(tables);
+  const auto *scs = reinterpret_cast<const uint8_t *const *>(scales);
+#define LSP(T)                                                                                   \
+  k_engram_lookup_sum<T, true><<<blocks, 256, 0, st>>>(                                          \
+      input_ids, B, L, start_pos, token_map, vocab, ids_cache, max_seq, multipliers + layer * G, \
+      primes + (int64_t)layer * cols, offsets + (int64_t)layer * cols,                          \
+      reciprocals ? reciprocals + (int64_t)layer * cols : nullptr, G, H, pad_id, nullptr,       \
+      nullptr, rows, 0, d, block, d, d / block, (T *)out, tabs, scs, nsh, total)
+  if (out_dtype == DSV41_F32) LSP(float);
+  else LSP(__nv_bfloat16);
+#undef LSP
+  DSV41_CHECK_LAUNCH("engram_lookup_sum_peers");
   return DSV41_OK;
 }
 

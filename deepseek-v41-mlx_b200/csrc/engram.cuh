@@ -249,15 +249,19 @@ __global__ void __launch_bounds__(256, 4) k_engram_gather_sum(
 // recips[c] = floor((2^64 - 1) / prime[c]) (0 for prime <= 1) when given; otherwise each lane
 // divides for its own prime.  No shared memory and no barrier: a warp's hash loads (its
 // lookback unrolled, G <= ENGRAM_MAX_G) issue together and its row loads follow at once.
+// PEERS: the rows come from row shards as in k_engram_gather_sum's PEERS mode (tabs / scs,
+// shard size `rows`, `total` rows in all); table / scale / row_lo unused.
 constexpr int ENGRAM_MAX_G = 8;
-template <typename T>
+template <typename T, bool PEERS = false>
 __global__ void __launch_bounds__(256, 4) k_engram_lookup_sum(
     const int64_t *__restrict__ ids, int64_t B, int64_t L, int64_t start,
     const int64_t *__restrict__ token_map, int64_t vocab, int64_t *__restrict__ cache,
     int64_t max_seq, const int64_t *__restrict__ mult, const int64_t *__restrict__ primes,
     const int64_t *__restrict__ offsets, const uint64_t *__restrict__ recips, int G, int H,
-    int64_t pad_id, const uint8_t *__restrict__ table, int64_t rows, int64_t row_lo, int64_t D,
-    int64_t block, int64_t rb, T *__restrict__ out) {
+    int64_t pad_id, const uint8_t *__restrict__ table, const uint8_t *__restrict__ scale,
+    int64_t rows, int64_t row_lo, int64_t D, int64_t block, int64_t tld, int64_t sld,
+    T *__restrict__ out, const uint8_t *const *__restrict__ tabs = nullptr,
+    const uint8_t *const *__restrict__ scs = nullptr, int nsh = 0, int64_t total = 0) {
   const int64_t gw = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int wpt = int(D / 256);
@@ -310,8 +314,8 @@ __global__ void __launch_bounds__(256, 4) k_engram_lookup_sum(
   const int64_t col = (gw % wpt) * 256 + lane * 8;
   const int soff = int(col / block);
   uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
-  gs_rows<false>(acc2, mine, cols, col, soff, table, table + D, rows, row_lo, rb, rb, nullptr,
-                 nullptr, 0, 0);
+  gs_rows<PEERS>(acc2, mine, cols, col, soff, table, scale, rows, row_lo, tld, sld, tabs, scs,
+                 nsh, total);
   gs_store(out + tok * D + col, acc2);
 }
 

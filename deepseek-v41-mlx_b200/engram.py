@@ -142,18 +142,32 @@ class EngramHasher:
     def lookup_sum(self, embedding, input_ids, start_pos: int, ids_cache, layer: int = 0,
                    out_dtype=None):
         """``embedding.gather_sum(self(input_ids, start_pos, ids_cache)[:, :, layer])``, the
-        same bits and the same id-cache update.  Up to ``fused_max_positions`` positions in
-        one launch (``dsv41_engram_lookup_sum``: the hashes are computed where the rows are
-        summed and never written).  ``embedding`` must hold packed rows
-        (``EngramEmbedding.pack``).  -> [B, L, dim]."""
+        same bits and the same id-cache update, in one launch where it pays: the hashes are
+        computed where the rows are summed and never written.
+          * ``EngramEmbedding`` with packed rows (``pack``): ``dsv41_engram_lookup_sum`` up to
+            ``fused_max_positions`` positions;
+          * ``ParallelEngramEmbedding`` reading its peers' shards in place:
+            ``dsv41_engram_lookup_sum_peers`` up to its ``replicate_max_tokens`` positions
+            (every rank sums every position; no collective);
+        otherwise the hasher and ``gather_sum`` run apart.  -> [B, L, dim]."""
         t = L.torch()
-        if embedding.packed is None:
-            raise ValueError("lookup_sum reads packed rows: call embedding.pack() first")
+        odt = out_dtype or t.bfloat16
         n_pos = int(np.prod(getattr(input_ids, "shape", np.shape(input_ids))))
-        if n_pos > self.fused_max_positions:
-            hid = self(input_ids, start_pos, ids_cache)
-            return embedding.gather_sum(hid[:, :, layer], out_dtype or t.bfloat16)
+        packed = getattr(embedding, "packed", None) is not None
+        peers = (isinstance(embedding, ParallelEngramEmbedding) and embedding.peers
+                 and embedding.dim in (256, 512, 1024))
+        if packed:
+            fused = n_pos <= self.fused_max_positions
+        elif peers:
+            fused = n_pos <= embedding.replicate_max_tokens
+        elif isinstance(embedding, EngramEmbedding):
+            raise ValueError("lookup_sum reads packed rows: call embedding.pack() first")
+        else:
+            fused = False
         dev = self._dev["token_map"].device
+        if not fused:
+            hid = self(input_ids, start_pos, ids_cache)
+            return embedding.gather_sum(hid[:, :, layer], odt)
         host_cache = isinstance(ids_cache, np.ndarray)
         cache = t.from_numpy(ids_cache).to(dev) if host_cache else L.cuda_tensor(ids_cache)
         if cache.dtype != t.int64:
@@ -163,14 +177,21 @@ class EngramHasher:
         B, Lq = ids.shape
         nL = len(self.args.engram_layer_ids)
         G, H = self.max_ngram, self.args.engram_n_heads
-        odt = out_dtype or t.bfloat16
         out = t.empty((B, Lq, embedding.dim), dtype=odt, device=dev)
-        pk = embedding.packed
-        L.call("dsv41_engram_lookup_sum", L.ptr(ids), B, Lq, int(start_pos),
-               L.ptr(self._dev["token_map"]), self.vocab, L.ptr(cache), cache.shape[1],
-               L.ptr(self._dev["mult"]), L.ptr(self._dev["primes"]), L.ptr(self._dev["offsets"]),
-               L.ptr(self._dev["recips"]), nL, int(layer), G, H, self.pad_id, L.ptr(pk), pk.shape[0], embedding.row_lo,
-               embedding.dim, embedding.block, L.dtype_code(odt), L.ptr(out), L.stream_of(out))
+        hash_args = (L.ptr(ids), B, Lq, int(start_pos), L.ptr(self._dev["token_map"]), self.vocab,
+                     L.ptr(cache), cache.shape[1], L.ptr(self._dev["mult"]),
+                     L.ptr(self._dev["primes"]), L.ptr(self._dev["offsets"]),
+                     L.ptr(self._dev["recips"]), nL, int(layer), G, H, self.pad_id)
+        if packed:
+            pk = embedding.packed
+            L.call("dsv41_engram_lookup_sum", *hash_args, L.ptr(pk), pk.shape[0],
+                   embedding.row_lo, embedding.dim, embedding.block, L.dtype_code(odt),
+                   L.ptr(out), L.stream_of(out))
+        else:
+            tabs, scs = embedding._map_peers(dev)[:2]
+            L.call("dsv41_engram_lookup_sum_peers", *hash_args, L.ptr(tabs), L.ptr(scs),
+                   embedding.world, embedding.part, embedding.num_embeddings, embedding.dim,
+                   embedding.block, L.dtype_code(odt), L.ptr(out), L.stream_of(out))
         if host_cache:
             ids_cache[...] = cache.cpu().numpy()
         elif cache.data_ptr() != L.as_tensor(ids_cache).data_ptr():

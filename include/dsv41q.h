@@ -441,6 +441,18 @@ int dsv41_engram_gather_sum_peers(const uint64_t *tables, const uint64_t *scales
                                   const int64_t *idx,
                                   int64_t n_tok, int n_per_tok, int out_dtype, void *out,
                                   void *stream);
+/* dsv41_engram_lookup_sum over the row shards: the hashing of dsv41_engram_lookup_sum (id
+ * cache updated the same way), the rows read from the shards as dsv41_engram_gather_sum_peers
+ * reads them.  The same bits as dsv41_engram_hash then dsv41_engram_gather_sum_peers. */
+int dsv41_engram_lookup_sum_peers(const int64_t *input_ids, int64_t B, int64_t L,
+                                  int64_t start_pos, const int64_t *token_map, int64_t vocab,
+                                  int64_t *ids_cache, int64_t max_seq,
+                                  const int64_t *multipliers, const int64_t *primes,
+                                  const int64_t *offsets, const uint64_t *reciprocals,
+                                  int n_layers, int layer, int max_ngram, int n_heads,
+                                  int64_t pad_id, const uint64_t *tables, const uint64_t *scales,
+                                  int nsh, int64_t rows, int64_t total, int64_t d, int64_t block,
+                                  int out_dtype, void *out, void *stream);
 
 #ifdef __cplusplus
 }
