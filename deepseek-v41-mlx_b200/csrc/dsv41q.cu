@@ -473,7 +473,9 @@ int router_nks(int64_t T, int64_t K, int64_t E) {
 }  // namespace
 
 extern "C" size_t dsv41_moe_route_workspace_size(int64_t T, int64_t D, int64_t E) {
-  return align_up((size_t)64 * T * E * 4, 256) + 256;
+  // the K-split partial scores of router_scores: router_nks(T, D, E) x T x E floats
+  const int64_t nks = (T > 0 && E > 0 && D >= 32) ? router_nks(T, D, E) : 1;
+  return align_up((size_t)nks * T * E * 4, 256) + 256;
 }
 
 static int route_impl(const void *x, int64_t T, int64_t D, const void *gate_w, const float *bias,
@@ -542,6 +544,11 @@ struct MoeWs {
 
 struct MoeDims {
   int64_t T, D, I, E, P, Pmax, Cmax, Tp, tiles_gu, tiles_dn;
+  // what the launches use: K-split counts (routed / shared gate/up and down, router), the
+  // row-pair down projection and its tiles; split-K partials are carved only where a count
+  // exceeds 1
+  int ns_gu, ns_dn, ns_sgu, ns_sdn, nks, rowpair;
+  int64_t tiles_dnx;
 };
 
 MoeDims moe_dims(const dsv41_moe_config *c, int64_t T) {
@@ -557,13 +564,29 @@ MoeDims moe_dims(const dsv41_moe_config *c, int64_t T) {
   d.Tp = ceil_div(T, 4) * 4;
   d.tiles_gu = ceil_div(d.I, QG_ROWS);
   d.tiles_dn = ceil_div(d.D, QG_ROWS);
+  // routed: gate/up over all active experts' tiles; down on row pairs (two 64-row tiles of an
+  // expert per item, on the two-matrix kernel) once the pair items fill a wave of CTAs,
+  // which needs packed scales and dim % 128 == 0 -- below that single tiles keep more CTAs
+  // streaming
+  d.ns_gu = pick_nsplit(act * d.tiles_gu, int(ceil_div(d.D, Fmt<WF_FP4>::KS)));
+  const int64_t pair_tiles = d.D / (2 * QG_ROWS);
+  d.rowpair = ((c->flags & DSV41_MOE_PACKED_SCALES) && !(c->flags & DSV41_MOE_NO_ROWPAIR) &&
+               d.D % (2 * QG_ROWS) == 0 &&
+               act * pair_tiles >= QG_MIN_CTAS * (int64_t)num_sms()) ? 1 : 0;
+  d.tiles_dnx = d.rowpair ? pair_tiles : d.tiles_dn;
+  d.ns_dn = pick_nsplit(act * d.tiles_dnx, int(ceil_div(d.I, Fmt<WF_FP4>::KS)));
+  // shared expert: dense chunks of nts n8 tiles
+  const int nts = T <= 8 ? 1 : (T <= 16 ? 2 : 4);
+  d.ns_sgu = pick_nsplit(ceil_div(T, 8 * nts) * d.tiles_gu, int(ceil_div(d.D, Fmt<WF_FP8B>::KS)));
+  d.ns_sdn = pick_nsplit(ceil_div(T, 4 * nts) * d.tiles_dn, int(ceil_div(d.I, Fmt<WF_FP8B>::KS)));
+  d.nks = T > 0 ? router_nks(T, d.D, d.E) : 1;
   return d;
 }
 
 MoeWs moe_carve(const MoeDims &d, void *base, size_t cap) {
   WsCarve wc{reinterpret_cast<uint8_t *>(base), cap, 0};
   MoeWs w;
-  w.rpart = wc.take<float>(64 * d.T * d.E);
+  w.rpart = wc.take<float>(int64_t(d.nks) * d.T * d.E);
   w.w = wc.take<float>(d.P);
   w.idx = wc.take<int32_t>(d.P);
   w.plan.pair_tok = wc.take<int32_t>(d.Pmax);
@@ -581,12 +604,18 @@ MoeWs moe_carve(const MoeDims &d, void *base, size_t cap) {
   w.Hs = wc.take<__half>(2 * d.Tp * d.I);
   w.Y = wc.take<float>(d.P * d.D);
   w.Ys = wc.take<float>(d.T * d.D);
-  const size_t frag2 = 32 * QG_CW * 2 * 4 * 4, frag4 = 32 * QG_CW * 4 * 4;  // NMAT*NT*4 floats
-  w.part_gu = wc.take<float>(d.Cmax * d.tiles_gu * QG_MAX_SPLIT * frag2);
-  w.part_dn = wc.take<float>(d.Cmax * d.tiles_dn * QG_MAX_SPLIT * frag4);
-  // shared expert: at most ceil(T/8) gate/up and ceil(T/4) down chunks, <= 2*4*4 floats each
-  w.part_sgu = wc.take<float>(ceil_div(d.T, 8) * d.tiles_gu * QG_MAX_SPLIT * 32 * QG_CW * 2 * 4 * 4);
-  w.part_sdn = wc.take<float>(ceil_div(d.T, 4) * d.tiles_dn * QG_MAX_SPLIT * frag4);
+  // split-K partials, [tile][split][thread][NMAT * NT * 4 floats], only where a launch splits:
+  // routed kernels NMAT * NT <= 2 x 1; shared gate/up ceil(T / 8nts) chunks of 2 x nts and
+  // down ceil(T / 4nts) chunks of 1 x nts (nts <= 4) are covered by ceil(T/8) x 32 and
+  // ceil(T/4) x 16 floats a thread
+  const size_t ct = 32 * QG_CW;
+  auto parts = [&](int64_t tiles, int ns, size_t floats) -> size_t {
+    return ns > 1 ? size_t(tiles) * size_t(ns) * ct * floats : 0;
+  };
+  w.part_gu = wc.take<float>(parts(d.Cmax * d.tiles_gu, d.ns_gu, 8));
+  w.part_dn = wc.take<float>(parts(d.Cmax * d.tiles_dnx, d.ns_dn, 8));
+  w.part_sgu = wc.take<float>(parts(ceil_div(d.T, 8) * d.tiles_gu, d.ns_sgu, 32));
+  w.part_sdn = wc.take<float>(parts(ceil_div(d.T, 4) * d.tiles_dn, d.ns_sdn, 16));
   w.cnt_gu = wc.take<int>(d.Cmax * d.tiles_gu);
   w.cnt_dn = wc.take<int>(d.Cmax * d.tiles_dn);
   w.cnt_sgu = wc.take<int>(ceil_div(d.T, 8) * d.tiles_gu);
@@ -698,7 +727,7 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
     p.sld = d.D / 32;
     p.tiles = int(d.tiles_gu);
     p.kstages = int(ceil_div(d.D, Fmt<WF_FP4>::KS));
-    p.nsplit = pick_nsplit(active * d.tiles_gu, p.kstages);
+    p.nsplit = d.ns_gu;
     p.xscale = ws.xsg;
     p.chunks = ws.plan.gu_chunks;
     p.nchunks_dev = ws.plan.counts + 0;
@@ -727,15 +756,12 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
     p.K = d.I;
     p.sld = d.I / 32;
     p.spack = (cfg->flags & DSV41_MOE_PACKED_SCALES) ? 1 : 0;
-    // Row pairs (two 64-row tiles of one expert per item, on the two-matrix kernel: the
-    // B fragments are shared and each warp runs two independent MMA chains) once the pair
-    // items fill a wave of CTAs; below that the single-tile kernel keeps more CTAs busy.
-    const int64_t pair_tiles = d.D / (2 * QG_ROWS);
-    p.rowpair = (p.spack && !(cfg->flags & DSV41_MOE_NO_ROWPAIR) && d.D % (2 * QG_ROWS) == 0 &&
-                 active * pair_tiles >= QG_MIN_CTAS * (int64_t)num_sms()) ? 1 : 0;
-    p.tiles = int(p.rowpair ? pair_tiles : d.tiles_dn);
+    // row pairs (two 64-row tiles of one expert per item, on the two-matrix kernel: the
+    // B fragments are shared and each warp runs two independent MMA chains), as moe_dims chose
+    p.rowpair = d.rowpair;
+    p.tiles = int(d.tiles_dnx);
     p.kstages = int(ceil_div(d.I, Fmt<WF_FP4>::KS));
-    p.nsplit = pick_nsplit(active * p.tiles, p.kstages);
+    p.nsplit = d.ns_dn;
     p.xscale = nullptr;
     p.chunks = ws.plan.dn_chunks;
     p.nchunks_dev = ws.plan.counts + 1;
@@ -787,7 +813,7 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
     p.tiles = int(d.tiles_gu);
     p.kstages = int(ceil_div(d.D, Fmt<WF_FP8B>::KS));
     const int64_t nch = ceil_div(T, 8 * nts);
-    p.nsplit = pick_nsplit(nch * d.tiles_gu, p.kstages);
+    p.nsplit = d.ns_sgu;
     p.xscale = ws.xs;
     p.chunks = nullptr;
     p.nchunks_host = int(nch);
@@ -825,7 +851,7 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
     p.tiles = int(d.tiles_dn);
     p.kstages = int(ceil_div(d.I, Fmt<WF_FP8B>::KS));
     const int64_t nch = ceil_div(T, 4 * nts);          // 8*nts H rows = 4*nts tokens
-    p.nsplit = pick_nsplit(nch * d.tiles_dn, p.kstages);
+    p.nsplit = d.ns_sdn;
     p.xscale = nullptr;
     p.chunks = nullptr;
     p.nchunks_host = int(nch);

@@ -114,15 +114,35 @@ __global__ void __launch_bounds__(1024) k_moe_plan(const int32_t *__restrict__ i
       plan.pair_row[q] = -1;
     }
   }
-  // pair placement
-  for (int64_t p = threadIdx.x; p < P; p += blockDim.x) {
-    const int ex = indices[p];
-    if (ex < 0 || ex >= E) continue;
+  // pair placement, stable (an expert's pairs in ascending p): pairs in chunks of the block;
+  // a pair's rank = its expert's pairs in earlier chunks and earlier warps of this chunk
+  // (a running count per expert, advanced warp by warp) + lower lanes of its own warp with
+  // the same expert (warp match).  Only the warps that hold pairs take a turn.
+  if (e < E) cnt[e] = 0;                       // reused as the running count
+  __syncthreads();
+  for (int64_t base = 0; base < P; base += blockDim.x) {
+    const int64_t p = base + threadIdx.x;
+    const int ex = p < P ? indices[p] : -1;
+    const bool valid = ex >= 0 && ex < E;
+    const unsigned grp = __match_any_sync(0xffffffffu, valid ? ex : -1);
+    const int lower = __popc(grp & ((1u << lane) - 1u));
+    const int64_t left = P - base;
+    const int nw = int((left < int64_t(blockDim.x) ? left : int64_t(blockDim.x)) + 31) >> 5;
     int rank = 0;
-    for (int64_t p2 = 0; p2 < p; ++p2) rank += (indices[p2] == ex);
-    const int q = poff[ex] + rank;
-    plan.pair_tok[q] = tok_map ? tok_map[p] : int(p / topk);
-    plan.pair_row[q] = int(p);
+    for (int w = 0; w < nw; ++w) {
+      if (wid == w) {
+        const int b = valid ? cnt[ex] : 0;
+        __syncwarp();
+        if (valid && lower == 0) cnt[ex] = b + __popc(grp);
+        rank = b + lower;
+      }
+      __syncthreads();
+    }
+    if (valid) {
+      const int q = poff[ex] + rank;
+      plan.pair_tok[q] = tok_map ? tok_map[p] : int(p / topk);
+      plan.pair_row[q] = int(p);
+    }
   }
 }
 
