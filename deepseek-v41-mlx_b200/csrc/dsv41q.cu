@@ -336,13 +336,24 @@ struct GemvWs {
   int *counters;
 };
 
+// split-K fragments of the dense GEMV: floats for tiles x chunks x the launch's split count
+// (the larger of the counts for 128- and 256-column K stages, the two stage widths of the
+// formats) x 128 threads x 16 (NMAT 1 x NT <= 4 x 4); none when neither splits
+size_t gemv_partial_floats(int64_t M, int64_t N, int64_t K) {
+  const int64_t tiles = ceil_div(N, QG_ROWS), nch = ceil_div(M, 32);
+  const int a = pick_nsplit(tiles * nch, int(ceil_div(K, 128)));
+  const int b = pick_nsplit(tiles * nch, int(ceil_div(K, 256)));
+  const int ns = a > b ? a : b;
+  return ns > 1 ? size_t(tiles) * nch * ns * 32 * QG_CW * 16 : 0;
+}
+
 size_t gemv_ws_bytes(int64_t M, int64_t N, int64_t K) {
   const int64_t tiles = ceil_div(N, QG_ROWS), nch = ceil_div(M, 32);
   size_t b = 0;
   b += align_up((size_t)M * K * 2, 256);
   b += align_up((size_t)M * 4, 256);
   b += align_up((size_t)M * ceil_div(K, 64) * 4, 256);
-  b += align_up((size_t)tiles * nch * QG_MAX_SPLIT * 32 * QG_CW * 16 * 4, 256);
+  b += align_up(gemv_partial_floats(M, N, K) * 4, 256);
   b += align_up((size_t)tiles * nch * 4, 256);
   return b + 256;
 }
@@ -369,7 +380,7 @@ int gemv_common(const void *x, int64_t M, int64_t K, const void *w, int64_t w_ro
   ws.x16 = wc.take<__half>(M * K);
   ws.xscale = wc.take<float>(M);
   ws.xsum = wc.take<float>(M * ceil_div(K, 64));
-  ws.partial = wc.take<float>((size_t)tiles * nch * QG_MAX_SPLIT * 32 * QG_CW * 16);
+  ws.partial = wc.take<float>(gemv_partial_floats(M, N, K));
   ws.counters = wc.take<int>(tiles * nch);
   DSV41_REQUIRE(wc.ok, DSV41_ERR_WORKSPACE, "workspace too small");
 
