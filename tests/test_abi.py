@@ -48,6 +48,23 @@ def test_host_side_validation_without_gpu():
     assert lib.dsv41_moe_decode_workspace_size(ctypes.byref(cfg), 64) > 64 * 6 * 7168 * 4
 
 
+def test_workspaces_stay_proportionate():
+    """Scratch is carved only for what the launches use: the split-K fragments of a launch
+    that does not split K take no room.  Guards the decode workspace of the BASELINE layer
+    (once 11 GB at T=64 and 172 GB at T=4096) and the dense GEMV's (once 3.8 GB at M=4096)."""
+    lib = L.load()
+    for flags in (1, 1 | L.MOE_PACKED_SCALES):
+        cfg = L.MoeConfig(dim=7168, inter=2048, n_experts=384, topk=6, score_func=0,
+                          gate_temp=1.0, norm_topk_prob=1, route_scale=1.5, swiglu_limit=10.0,
+                          flags=flags)
+        for T, cap in ((1, 64e6), (8, 128e6), (64, 512e6), (4096, 4e9)):
+            n = lib.dsv41_moe_decode_workspace_size(ctypes.byref(cfg), T)
+            assert T * 6 * 7168 * 4 < n < cap, (flags, T, n)
+    assert lib.dsv41_gemv_workspace_size(4096, 14336, 7168) < 128e6
+    assert lib.dsv41_gemv_workspace_size(1, 4096, 7168) < 16e6
+    assert lib.dsv41_moe_route_workspace_size(4096, 7168, 384) <= 4096 * 384 * 4 + 512
+
+
 def test_errors_map_to_python_exceptions():
     import pytest
     with pytest.raises(ValueError):
