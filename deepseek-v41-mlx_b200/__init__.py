@@ -13,13 +13,14 @@ from __future__ import annotations
 from . import _lib  # noqa: F401
 from ._lib import DSV41Error, lib_path  # noqa: F401
 
-__all__ = ["dequant", "moe", "engram", "linear", "act_quant", "gemm", "ep", "release",
+__all__ = ["dequant", "moe", "engram", "linear", "act_quant", "gemm", "ep", "release", "convert",
            "DSV41Error", "lib_path"]
 
 
 def __getattr__(name):
     # submodules load lazily so that importing the package never touches CUDA
-    if name in ("dequant", "moe", "engram", "linear", "act_quant", "gemm", "ep", "release"):
+    if name in ("dequant", "moe", "engram", "linear", "act_quant", "gemm", "ep", "release",
+                "convert"):
         import importlib
         return importlib.import_module(f"{__name__}.{name}")
     raise AttributeError(name)

@@ -65,6 +65,7 @@ PROTOTYPES = {
     "dsv41_dequant_fp4": (_I, [_P, _P, _I64, _I64, _I, _P, _P]),
     "dsv41_dequant_fp8_rows": (_I, [_P, _P, _I64, _I64, _I64, _P, _P]),
     "dsv41_dequant_affine": (_I, [_P, _P, _P, _I, _I64, _I64, _I, _I, _I, _P, _P]),
+    "dsv41_quantize_affine": (_I, [_P, _I, _I64, _I64, _I, _I, _P, _P, _P, _P]),
     "dsv41_act_quant_fp8": (_I, [_P, _I64, _I64, _I, _I, _P, _P, _I, _P, _P]),
     "dsv41_gemv_workspace_size": (_SZ, [_I64, _I64, _I64]),
     "dsv41_gemv_fp8_block": (_I, [_P, _I64, _I64, _P, _P, _I64, _I, _P, _P, _SZ, _P]),

@@ -10,6 +10,7 @@
 #include "bsgemm.cuh"
 #include "prefill.cuh"
 #include "ep_decode.cuh"
+#include "quantize.cuh"
 #include "aqgemm.cuh"
 
 #include <mutex>
@@ -199,6 +200,40 @@ extern "C" int dsv41_dequant_affine(const uint32_t *wq, const void *scales, cons
 }
 
 // ======================================================================= act_quant
+
+extern "C" int dsv41_quantize_affine(const void *w, int dtype, int64_t rows, int64_t cols,
+                                     int group, int bits, uint32_t *wq, void *scales,
+                                     void *biases, void *stream) {
+  DSV41_REQUIRE(dtype == DSV41_BF16 || dtype == DSV41_F32, DSV41_ERR_BAD_DTYPE,
+                "dtype must be BF16 or F32");
+  DSV41_REQUIRE(group == 32 || group == 64 || group == 128, DSV41_ERR_UNSUPPORTED,
+                "group must be 32, 64 or 128");
+  DSV41_REQUIRE(bits == 2 || bits == 4 || bits == 8, DSV41_ERR_UNSUPPORTED,
+                "bits must be 2, 4 or 8");
+  DSV41_REQUIRE(rows >= 0 && cols >= 0 && cols % group == 0, DSV41_ERR_BAD_SHAPE,
+                "cols must be a multiple of group");
+  if (rows == 0 || cols == 0) return DSV41_OK;
+  DSV41_REQUIRE(w && wq && scales && biases, DSV41_ERR_BAD_ARG, "NULL pointer");
+  cudaStream_t st = STREAM(stream);
+  ProfScope prof("quantize_affine", st);
+  const unsigned blocks = unsigned(ceil_div(rows * (cols / group) * 32, 256));
+#define QA(T, V)                                                                                 \
+  k_quantize_affine<T, V><<<blocks, 256, 0, st>>>(static_cast<const T *>(w), rows, cols, bits, \
+                                                  wq, static_cast<T *>(scales),                \
+                                                  static_cast<T *>(biases))
+  if (dtype == DSV41_BF16) {
+    if (group == 32) QA(__nv_bfloat16, 1);
+    else if (group == 64) QA(__nv_bfloat16, 2);
+    else QA(__nv_bfloat16, 4);
+  } else {
+    if (group == 32) QA(float, 1);
+    else if (group == 64) QA(float, 2);
+    else QA(float, 4);
+  }
+#undef QA
+  DSV41_CHECK_LAUNCH("quantize_affine");
+  return DSV41_OK;
+}
 
 extern "C" int dsv41_act_quant_fp8(const void *x, int64_t M, int64_t K, int block,
                                    int round_scale, uint8_t *q, void *s, int s_dtype,

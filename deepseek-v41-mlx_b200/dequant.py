@@ -121,3 +121,28 @@ def dequantize_affine(wq, scales, biases, group_size: int = 64, bits: int = 4, d
     L.call("dsv41_dequant_affine", L.ptr(w), L.ptr(s), L.ptr(b), L.dtype_code(s.dtype), rows, cols,
            bits, group_size, code, L.ptr(out), L.stream_of(w))
     return out
+
+
+def quantize_affine(w, group_size: int = 64, bits: int = 4):
+    """mx.quantize(w, group_size, bits) for the MLX affine layout, as the converter calls it
+    (convert.py:169, :188): w bf16 or fp32 [..., cols] -> (uint32 codes [..., cols*bits/32],
+    scales, biases [..., cols/group_size] in w's dtype).  Per group in fp32: the scale spans
+    max - min over 2^bits - 1 steps, signed toward the edge of larger magnitude, then set so
+    that the edge is a whole number of steps from zero (bias = that edge); codes round half
+    away from zero.  group_size 32 / 64 / 128, bits 2 / 4 / 8."""
+    t = _torch()
+    x = L.cuda_tensor(w, "w")
+    if x.dtype not in (t.bfloat16, t.float32):
+        x = x.to(t.float32)
+    x = x.contiguous()
+    cols = x.shape[-1]
+    if cols % group_size:
+        raise ValueError(f"the last dimension ({cols}) must be a multiple of group_size")
+    rows = x.numel() // cols if cols else 0
+    lead = tuple(x.shape[:-1])
+    wq = t.empty(lead + (cols * bits // 32,), dtype=t.uint32, device=x.device)
+    scales = t.empty(lead + (cols // group_size,), dtype=x.dtype, device=x.device)
+    biases = t.empty_like(scales)
+    L.call("dsv41_quantize_affine", L.ptr(x), L.dtype_code(x.dtype), rows, cols, group_size,
+           bits, L.ptr(wq), L.ptr(scales), L.ptr(biases), L.stream_of(x))
+    return wq, scales, biases

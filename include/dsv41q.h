@@ -127,6 +127,17 @@ int dsv41_dequant_fp8_rows(const uint8_t *w, const uint8_t *s, int64_t rows, int
 int dsv41_dequant_affine(const uint32_t *wq, const void *scales, const void *biases,
                          int sb_dtype, int64_t rows, int64_t cols, int bits, int group,
                          int out_dtype, void *out, void *stream);
+/* The inverse direction, mx.quantize as called by the converter
+ * (deepseek_v41_mlx/convert.py:169 quantize_tree, :188 quantize_engram_table): w
+ * [rows, cols] of dtype (BF16 or F32), cols % group == 0, group in {32, 64, 128},
+ * bits in {2, 4, 8} -> wq u32 [rows, cols*bits/32] in the layout above, scales and biases
+ * [rows, cols/group] of the same dtype.  Per group, in fp32: scale = max((max - min) /
+ * (2^bits - 1), 1e-7), signed toward the edge of larger magnitude; q0 = round(edge / scale);
+ * if q0 != 0 then scale = edge / q0 and bias = edge, else bias = 0; code = clamp(round((w -
+ * bias) / scale), 0, 2^bits - 1) (round half away from zero).  MLX's own numerics are not
+ * pinned by any reference test. */
+int dsv41_quantize_affine(const void *w, int dtype, int64_t rows, int64_t cols, int group,
+                          int bits, uint32_t *wq, void *scales, void *biases, void *stream);
 
 /* ---- a12: upstream act_quant (docs/reference/kernel.py:40-124,
  * mirrored by tests/kernel_stub.py:47-63).  x bf16 [M, K] (K % block == 0).

@@ -20,6 +20,13 @@ unpinned -- no reference test checks these numerics):
   affine_qmm_reference   y = sum_g scale_g * sum_{k in g} x_k q_k + bias_g * sum_{k in g} x_k
                          accumulated in float64 (the mx.quantized_matmul form,
                          which never materialises bf16 weights).
+  quantize_affine        mx.quantize as the converter calls it (convert.py:169, :188): per
+                         group in fp32, scale = max((max-min)/n, 1e-7) signed toward the
+                         larger-magnitude edge, q0 = round(edge/scale), scale = edge/q0 and
+                         bias = edge when q0 != 0 (else bias 0), codes = clamp(round((w-bias)
+                         /scale), 0, n); rounding half away from zero; scale and bias stored
+                         in the input's dtype.  MLX's published scheme as this build restates
+                         it -- parity unpinned like the rest of the affine format.
 """
 
 from __future__ import annotations
@@ -197,6 +204,34 @@ def dequant_affine(wq, scales, biases, bits: int, group: int, cols: int,
     b = np.repeat(sb_to_f32(biases, sb_dtype).astype(np.float64), group, axis=1)[:, :cols]
     v = (s * q + b).astype(np.float32)   # exact product, sum rounded once to f32
     return to_dtype(v, out_dtype)
+
+
+def _round_half_away(x: np.ndarray) -> np.ndarray:
+    """round() of fp32 values, half away from zero, exact (float64 holds x + 0.5 exactly)."""
+    x64 = np.asarray(x, dtype=np.float64)
+    return (np.sign(x64) * np.floor(np.abs(x64) + 0.5)).astype(np.float32)
+
+
+def quantize_affine(w: np.ndarray, group: int, bits: int, sb_dtype: str = "bf16"):
+    """mx.quantize(w, group_size=group, bits=bits) as restated in the module docstring:
+    fp32 w [rows, cols] -> (uint32 codes [rows, cols*bits/32], scales, biases [rows,
+    cols/group] in sb_dtype).  Every step is one IEEE fp32 operation, as the kernel does."""
+    w = np.asarray(w, dtype=np.float32)
+    rows, cols = w.shape
+    g = w.reshape(rows, cols // group, group)
+    hi, lo = g.max(-1), g.min(-1)
+    nb = np.float32((1 << bits) - 1)
+    scale = np.maximum((hi - lo) / nb, np.float32(1e-7)).astype(np.float32)
+    side = np.abs(lo) > np.abs(hi)
+    scale = np.where(side, scale, -scale).astype(np.float32)
+    edge = np.where(side, lo, hi).astype(np.float32)
+    q0 = _round_half_away(edge / scale)
+    nz = q0 != 0
+    scale = np.where(nz, edge / np.where(nz, q0, np.float32(1)), scale).astype(np.float32)
+    bias = np.where(nz, edge, np.float32(0)).astype(np.float32)
+    q = _round_half_away((g - bias[..., None]) / scale[..., None])
+    q = np.clip(q, 0, nb).astype(np.int64).reshape(rows, cols)
+    return pack_affine(q, bits), to_dtype(scale, sb_dtype), to_dtype(bias, sb_dtype)
 
 
 def affine_qmm_reference(x: np.ndarray, wq, scales, biases, bits: int, group: int,

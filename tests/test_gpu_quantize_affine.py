@@ -1,0 +1,74 @@
+"""MLX affine quantization on the GPU (mx.quantize as the converter calls it) vs the oracle's
+restatement: codes, scales and biases bit-identical.  Parity with MLX itself is unpinned
+(MLX is not in the reference tree and no reference test pins its quantizer)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import deepseek_v41_mlx_b200 as q
+from oracle import formats as F
+
+pytestmark = pytest.mark.gpu
+
+
+def _u32(t):
+    return t.view(torch.int32).cpu().numpy().view(np.uint32)
+
+
+def _u16(t):
+    return t.view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def _weights(rng, rows, cols, group):
+    w = (rng.standard_normal((rows, cols)) * rng.uniform(0.001, 3.0, (rows, 1))).astype(np.float32)
+    w[0, :group] = 0.0                                  # all zero
+    w[1, :group] = -0.3                                 # constant
+    w[2, :group] = np.abs(w[2, :group])                 # one-signed
+    w[3, group:2 * group] *= 1000.0                     # large
+    return w
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+@pytest.mark.parametrize("bits", [2, 4, 8])
+@pytest.mark.parametrize("group", [32, 64, 128])
+def test_quantize_affine_matches_oracle(cuda, dtype, bits, group):
+    rng = np.random.default_rng(bits * 100 + group + (dtype == "bf16"))
+    rows, cols = 37, 512
+    w = _weights(rng, rows, cols, group)
+    if dtype == "bf16":
+        w = F.round_bf16(w)
+        wt = torch.from_numpy(w).cuda().to(torch.bfloat16)
+    else:
+        wt = torch.from_numpy(w).cuda()
+    wq, s, b = q.dequant.quantize_affine(wt, group, bits)
+    owq, os_, ob = F.quantize_affine(w, group, bits, dtype)
+    assert wq.shape == (rows, cols * bits // 32) and s.dtype == wt.dtype
+    assert np.array_equal(_u32(wq), owq)
+    if dtype == "bf16":
+        assert np.array_equal(_u16(s), os_) and np.array_equal(_u16(b), ob)
+    else:
+        assert np.array_equal(s.cpu().numpy().view(np.uint32), os_.view(np.uint32))
+        assert np.array_equal(b.cpu().numpy().view(np.uint32), ob.view(np.uint32))
+    # the library's own dequantize reads what it wrote as the oracle's dequantize does
+    got = q.dequant.dequantize_affine(wq, s, b, group, bits, torch.float32).cpu().numpy()
+    want = F.dequant_affine(owq, os_, ob, bits, group, cols, dtype, "f32")
+    assert np.array_equal(got, want)
+
+
+def test_quantize_engram_table_matches_oracle(cuda):
+    """convert.quantize_engram_table: fp8 rows + ue8m0 -> fp32 -> bf16 -> affine, in row
+    chunks (here 100 rows, so the last chunk is short)."""
+    rng = np.random.default_rng(7)
+    rows, d, block, bits, group = 250, 256, 32, 4, 64
+    wu8 = rng.integers(0, 256, size=(rows, d), dtype=np.uint8)
+    wu8[(wu8 & 0x7F) == 0x7F] = 0
+    su8 = rng.integers(115, 128, size=(rows, d // block), dtype=np.uint8)
+    out = q.convert.quantize_engram_table(torch.from_numpy(wu8).cuda(),
+                                          torch.from_numpy(su8).cuda(), bits, group, step=100)
+    deq = F.round_bf16(F.dequant_fp8_rows(wu8, su8, block))
+    owq, os_, ob = F.quantize_affine(deq, group, bits, "bf16")
+    assert np.array_equal(_u32(out["weight"]), owq)
+    assert np.array_equal(_u16(out["scales"]), os_) and np.array_equal(_u16(out["biases"]), ob)
