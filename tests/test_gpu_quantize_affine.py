@@ -4,6 +4,8 @@ restatement: codes, scales and biases bit-identical.  Parity with MLX itself is 
 
 from __future__ import annotations
 
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -72,3 +74,39 @@ def test_quantize_engram_table_matches_oracle(cuda):
     owq, os_, ob = F.quantize_affine(deq, group, bits, "bf16")
     assert np.array_equal(_u32(out["weight"]), owq)
     assert np.array_equal(_u16(out["scales"]), os_) and np.array_equal(_u16(out["biases"]), ob)
+
+
+def test_release_group_sanitize_and_quantize(cuda, tmp_path):
+    """A synthetic release checkpoint through convert.sanitize_group (GPU decode, expert
+    stacking) and quantize_tree (experts at 4 bits, the rest at 8): decoded tensors and the
+    quantized triples equal the oracle's decode and quantizer."""
+    from safetensors.torch import load_file
+    import release_fixture as RF
+    path, a = RF.write(str(tmp_path / "ckpt"))
+    tensors = {}
+    for fn in sorted(os.listdir(path)):
+        if fn.endswith(".safetensors"):
+            tensors.update(load_file(os.path.join(path, fn)))
+    out = q.convert.sanitize_group(sorted(tensors), tensors)
+    p = a["moe"]
+    pre = f"layers.{RF.MOE_LAYER}.ffn"
+    for wn, proj in (("w1", "gate_proj"), ("w3", "up_proj"), ("w2", "down_proj")):
+        got = out[f"{pre}.experts.{proj}.weight"]
+        assert got.dtype == torch.bfloat16 and got.shape[0] == RF.E
+        want = np.stack([F.dequant_fp4(p[wn][e], p["s" + wn[1]][e], "bf16") for e in range(RF.E)])
+        assert np.array_equal(_u16(got), want)
+    got = out[f"{pre}.shared_experts.w1.weight"]
+    assert np.array_equal(_u16(got), F.dequant_fp8(p["sw1"], p["ss1"], "bf16"))
+    assert out[f"{pre}.gate.bias"].dtype == torch.float32
+    assert out[f"layers.{RF.ENGRAM_LAYER}.engram.embed.weight"].dtype == torch.uint8
+    qt, modules = q.convert.quantize_tree(out, 8, 4, 64)
+    base = f"{pre}.experts.gate_proj"
+    assert modules[base] == {"group_size": 64, "bits": 4}
+    assert modules[f"{pre}.shared_experts.w1"] == {"group_size": 64, "bits": 8}
+    assert f"{pre}.gate" not in modules
+    assert f"layers.{RF.ENGRAM_LAYER}.engram.embed" not in modules
+    w = F.bf16_bits_to_f32(_u16(out[f"{base}.weight"])).reshape(-1, RF.D)
+    owq, os_, ob = F.quantize_affine(w, 64, 4, "bf16")
+    assert np.array_equal(_u32(qt[f"{base}.weight"]).reshape(owq.shape), owq)
+    assert np.array_equal(_u16(qt[f"{base}.scales"]).reshape(os_.shape), os_)
+    assert np.array_equal(_u16(qt[f"{base}.biases"]).reshape(ob.shape), ob)
