@@ -130,3 +130,30 @@ def quantize_engram_table(weight_u8, scale_u8, bits: int, group_size: int, step:
         qw, qs, qb = D.quantize_affine(deq, group_size, bits)
         out_w[r0:r1], out_s[r0:r1], out_b[r0:r1] = qw, qs, qb
     return {"weight": out_w, "scales": out_s, "biases": out_b}
+
+
+def quantize_engram_table_from_checkpoint(ckpt, weight_name: str, bits: int, group_size: int,
+                                          step: int = 1 << 22):
+    """convert.py:199-226: a release engram table streamed off disk in row slices (never the
+    whole 98 GB tensor in host memory) into the MLX affine triple, on the GPU.  ``ckpt`` is a
+    ``release.Checkpoint``; ``weight_name`` the table's ``.weight`` (its ``.scale`` beside
+    it).  The same chunk arithmetic as ``quantize_engram_table`` (quantization is row-local),
+    so the result is identical to converting the table in one piece."""
+    t = L.torch()
+    sname = weight_name[:-len(".weight")] + ".scale"
+    first_w = ckpt.get(weight_name, "cuda", rows=(0, 1))
+    first_s = ckpt.get(sname, "cuda", rows=(0, 1))
+    d = first_w.shape[-1]
+    block = d // first_s.shape[-1]
+    with ckpt._open(ckpt.where[weight_name], framework="pt") as f:
+        rows = f.get_slice(weight_name).get_shape()[0]
+    out_w = t.empty((rows, d * bits // 32), dtype=t.uint32, device="cuda")
+    out_s = t.empty((rows, d // group_size), dtype=t.bfloat16, device="cuda")
+    out_b = t.empty_like(out_s)
+    for r0 in range(0, rows, step):
+        r1 = min(rows, r0 + step)
+        w = ckpt.get(weight_name, "cuda", rows=(r0, r1))
+        s = ckpt.get(sname, "cuda", rows=(r0, r1))
+        deq = D.dequant_fp8_rows(w, s, block).to(t.bfloat16)
+        out_w[r0:r1], out_s[r0:r1], out_b[r0:r1] = D.quantize_affine(deq, group_size, bits)
+    return {"weight": out_w, "scales": out_s, "biases": out_b}

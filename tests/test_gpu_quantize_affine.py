@@ -110,3 +110,19 @@ def test_release_group_sanitize_and_quantize(cuda, tmp_path):
     assert np.array_equal(_u32(qt[f"{base}.weight"]).reshape(owq.shape), owq)
     assert np.array_equal(_u16(qt[f"{base}.scales"]).reshape(os_.shape), os_)
     assert np.array_equal(_u16(qt[f"{base}.biases"]).reshape(ob.shape), ob)
+
+
+def test_engram_table_from_checkpoint_matches_in_memory(cuda, tmp_path):
+    """The release engram table streamed off disk in row slices (3 slices, the last short)
+    converts to the same triple as the table converted in memory."""
+    import release_fixture as RF
+    path, a = RF.write(str(tmp_path / "ckpt"))
+    ckpt = q.release.Checkpoint(path)
+    name = f"layers.{RF.ENGRAM_LAYER}.engram.embed.weight"
+    got = q.convert.quantize_engram_table_from_checkpoint(ckpt, name, 4, 64, step=400)
+    want = q.convert.quantize_engram_table(torch.from_numpy(a["table"]).cuda(),
+                                           torch.from_numpy(a["tscale"]).cuda(), 4, 64)
+    assert torch.equal(got["weight"].view(torch.int32), want["weight"].view(torch.int32))
+    for k in ("scales", "biases"):
+        assert torch.equal(got[k], want[k]), k
+    assert got["weight"].shape == (RF.ROWS, RF.HD * 4 // 32)
