@@ -485,6 +485,20 @@ def sub_measurements(q, torch, dev, layer, flush, stream, hbm_peak, K, W):
             out[f"gemv_affine{bits}_M{M}"] = {"ms": round(st, 5), "gbs": round(byts / st / 1e6, 1),
                                               "frac_hbm": round(byts / st / 1e6 / hbm_peak, 4)}
         del wq, sc, bi
+    # converter (next row 3): mx.quantize of a bf16 [14336, 7168] weight, groups of 64; two
+    # weight copies (> L2) rotated; bytes = bf16 in + codes + bf16 scales and biases out
+    ws_bf = [torch.randn(N, Kd, device=dev, generator=g).to(torch.bfloat16) for _ in range(2)]
+    for bits in (4, 8):
+        gr = graphed(torch, [lambda c=c: q.dequant.quantize_affine(ws_bf[c], 64, bits)
+                             for c in range(2)])
+        ms = timed_steps(torch, lambda i: gr[i % 2].replay(), K * 2, W, flush, stream)
+        st = sum(ms) / len(ms)
+        byts = N * Kd * 2 + N * Kd * bits // 8 + 2 * N * (Kd // 64) * 2
+        out[f"quantize_affine{bits}_14336x7168"] = {
+            "ms": round(st, 4), "gbs": round(byts / st / 1e6, 1),
+            "frac_hbm": round(byts / st / 1e6 / hbm_peak, 4)}
+        del gr
+    del ws_bf
     return out
 
 

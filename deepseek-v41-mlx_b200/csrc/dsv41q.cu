@@ -216,6 +216,34 @@ extern "C" int dsv41_quantize_affine(const void *w, int dtype, int64_t rows, int
   DSV41_REQUIRE(w && wq && scales && biases, DSV41_ERR_BAD_ARG, "NULL pointer");
   cudaStream_t st = STREAM(stream);
   ProfScope prof("quantize_affine", st);
+  if (aligned(w, 16) && aligned(wq, 16)) {
+    // a thread per group, 16-byte loads (rows of 32k elements stay aligned)
+    const unsigned tb = unsigned(ceil_div(rows * (cols / group), 256));
+#define QT(T, G, B)                                                                             \
+  k_quantize_affine_t<T, G, B><<<tb, 256, 0, st>>>(static_cast<const T *>(w), rows, cols, wq, \
+                                                   static_cast<T *>(scales),                  \
+                                                   static_cast<T *>(biases))
+#define QTB(T, G)                                                                               \
+  do {                                                                                          \
+    if (bits == 2) QT(T, G, 2);                                                                 \
+    else if (bits == 4) QT(T, G, 4);                                                            \
+    else QT(T, G, 8);                                                                           \
+  } while (0)
+#define QTG(T)                                                                                  \
+  do {                                                                                          \
+    if (group == 32) QTB(T, 32);                                                                \
+    else if (group == 64) QTB(T, 64);                                                           \
+    else QTB(T, 128);                                                                           \
+  } while (0)
+    if (dtype == DSV41_BF16) QTG(__nv_bfloat16);
+    else QTG(float);
+#undef QTG
+#undef QTB
+#undef QT
+    DSV41_CHECK_LAUNCH("quantize_affine");
+    return DSV41_OK;
+  }
+  // unaligned input or output: a warp per group, element loads
   const unsigned blocks = unsigned(ceil_div(rows * (cols / group) * 32, 256));
 #define QA(T, V)                                                                                 \
   k_quantize_affine<T, V><<<blocks, 256, 0, st>>>(static_cast<const T *>(w), rows, cols, bits, \

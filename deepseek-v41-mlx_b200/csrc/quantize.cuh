@@ -29,6 +29,21 @@ template <> __device__ __forceinline__ void qa_store<__nv_bfloat16>(__nv_bfloat1
   *p = __float2bfloat16_rn(v);
 }
 
+// The group's parameters from its range (the steps of the header comment).
+__device__ __forceinline__ void qa_params(float hi, float lo, float nb, float &scale,
+                                          float &bias) {
+  scale = fmaxf(__fdiv_rn(__fsub_rn(hi, lo), nb), 1e-7f);
+  const bool side = fabsf(lo) > fabsf(hi);
+  scale = side ? scale : -scale;
+  const float edge = side ? lo : hi;
+  const float q0 = roundf(__fdiv_rn(edge, scale));
+  bias = 0.0f;
+  if (q0 != 0.0f) {
+    scale = __fdiv_rn(edge, q0);
+    bias = edge;
+  }
+}
+
 // One warp per group; lane l holds the V = group / 32 values l*V .. l*V + V - 1 of its group
 // (V * bits divides 32, so a lane's codes never straddle a word); the lanes sharing a word
 // OR their pieces together and the first of them stores it.
@@ -59,16 +74,8 @@ __global__ void __launch_bounds__(256) k_quantize_affine(const T *__restrict__ w
     lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
   }
   const float nb = float((1 << bits) - 1);
-  float scale = fmaxf(__fdiv_rn(__fsub_rn(hi, lo), nb), 1e-7f);
-  const bool side = fabsf(lo) > fabsf(hi);
-  scale = side ? scale : -scale;
-  const float edge = side ? lo : hi;
-  const float q0 = roundf(__fdiv_rn(edge, scale));
-  float bias = 0.0f;
-  if (q0 != 0.0f) {
-    scale = __fdiv_rn(edge, q0);
-    bias = edge;
-  }
+  float scale, bias;
+  qa_params(hi, lo, nb, scale, bias);
   uint32_t piece = 0;
   const int e0 = lane * V;
   const int off = (e0 * bits) & 31;
@@ -85,6 +92,82 @@ __global__ void __launch_bounds__(256) k_quantize_affine(const T *__restrict__ w
     qa_store<T>(scales + row * gpr + g, scale);
     qa_store<T>(biases + row * gpr + g, bias);
   }
+}
+
+// 16 bytes of T as floats (8 bf16 or 4 fp32)
+__device__ __forceinline__ void qa_load16(const __nv_bfloat16 *p, float (&f)[8]) {
+  const uint4 v = *reinterpret_cast<const uint4 *>(p);
+  const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(u[i] << 16);
+    f[2 * i + 1] = __uint_as_float(u[i] & 0xFFFF0000u);
+  }
+}
+__device__ __forceinline__ void qa_load16(const float *p, float (&f)[4]) {
+  const float4 v = *reinterpret_cast<const float4 *>(p);
+  f[0] = v.x; f[1] = v.y; f[2] = v.z; f[3] = v.w;
+}
+
+// One thread per group: 16-byte loads of the group (all of a thread's loads in flight at
+// once), its range, then a second read of the same bytes (from L1) to quantize, and the
+// group's G * BITS / 32 words stored together.  Needs w and every row 16-byte aligned and wq
+// 16-byte aligned (the host checks; otherwise k_quantize_affine runs).  Same arithmetic as
+// k_quantize_affine, so the same bits.
+template <typename T, int G, int BITS>
+__global__ void __launch_bounds__(256) k_quantize_affine_t(const T *__restrict__ w, int64_t rows,
+                                                           int64_t cols,
+                                                           uint32_t *__restrict__ wq,
+                                                           T *__restrict__ scales,
+                                                           T *__restrict__ biases) {
+  constexpr int EPV = 16 / int(sizeof(T));         // elements a 16-byte load
+  constexpr int NV = G / EPV;
+  constexpr int WORDS = G * BITS / 32, PER = 32 / BITS;
+  const int64_t gpr = cols / G;
+  const int64_t gi = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (gi >= rows * gpr) return;
+  const int64_t row = gi / gpr, g = gi % gpr;
+  const T *src = w + row * cols + g * G;
+  float hi = -INFINITY, lo = INFINITY;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    float f[EPV];
+    qa_load16(src + k * EPV, f);
+#pragma unroll
+    for (int j = 0; j < EPV; ++j) {
+      hi = fmaxf(hi, f[j]);
+      lo = fminf(lo, f[j]);
+    }
+  }
+  const float nb = float((1 << BITS) - 1);
+  float scale, bias;
+  qa_params(hi, lo, nb, scale, bias);
+  uint32_t word[WORDS];
+#pragma unroll
+  for (int i = 0; i < WORDS; ++i) word[i] = 0u;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    float f[EPV];
+    qa_load16(src + k * EPV, f);
+#pragma unroll
+    for (int j = 0; j < EPV; ++j) {
+      const int e = k * EPV + j;
+      const float q = fminf(fmaxf(roundf(__fdiv_rn(__fsub_rn(f[j], bias), scale)), 0.0f), nb);
+      word[e / PER] |= uint32_t(q) << ((e % PER) * BITS);
+    }
+  }
+  uint32_t *dst = wq + row * (cols * BITS / 32) + g * WORDS;
+  if constexpr (WORDS % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < WORDS; i += 4)
+      *reinterpret_cast<uint4 *>(dst + i) = make_uint4(word[i], word[i + 1], word[i + 2], word[i + 3]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < WORDS; i += 2)
+      *reinterpret_cast<uint2 *>(dst + i) = make_uint2(word[i], word[i + 1]);
+  }
+  qa_store<T>(scales + row * gpr + g, scale);
+  qa_store<T>(biases + row * gpr + g, bias);
 }
 
 }  // namespace dsv41

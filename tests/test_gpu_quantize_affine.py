@@ -126,3 +126,33 @@ def test_engram_table_from_checkpoint_matches_in_memory(cuda, tmp_path):
     for k in ("scales", "biases"):
         assert torch.equal(got[k], want[k]), k
     assert got["weight"].shape == (RF.ROWS, RF.HD * 4 // 32)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+@pytest.mark.parametrize("group,bits", [(32, 2), (64, 4), (128, 8)])
+def test_quantize_affine_unaligned_input(cuda, dtype, group, bits):
+    """Input not 16-byte aligned (one element past an aligned base): the warp-per-group
+    kernel runs instead of the thread-per-group one, with the same bits as the oracle."""
+    from deepseek_v41_mlx_b200 import _lib as L
+    rng = np.random.default_rng(group + bits)
+    rows, cols = 9, 256
+    w = _weights(rng, rows, cols, group)
+    tdt = torch.bfloat16 if dtype == "bf16" else torch.float32
+    if dtype == "bf16":
+        w = F.round_bf16(w)
+    base = torch.zeros(rows * cols + 8, dtype=tdt, device="cuda")
+    base[1:1 + rows * cols] = torch.from_numpy(w.reshape(-1)).cuda().to(tdt)
+    ptr = base.data_ptr() + base.element_size()               # 2 or 4 bytes past alignment
+    wq = torch.empty((rows, cols * bits // 32), dtype=torch.int32, device="cuda")
+    s = torch.empty((rows, cols // group), dtype=tdt, device="cuda")
+    b = torch.empty_like(s)
+    L.call("dsv41_quantize_affine", ptr, L.dtype_code(tdt), rows, cols, group, bits, L.ptr(wq),
+           L.ptr(s), L.ptr(b), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    owq, os_, ob = F.quantize_affine(w, group, bits, dtype)
+    assert np.array_equal(wq.cpu().numpy().view(np.uint32), owq)
+    if dtype == "bf16":
+        assert np.array_equal(_u16(s), os_) and np.array_equal(_u16(b), ob)
+    else:
+        assert np.array_equal(s.cpu().numpy().view(np.uint32), os_.view(np.uint32))
+        assert np.array_equal(b.cpu().numpy().view(np.uint32), ob.view(np.uint32))
