@@ -94,6 +94,19 @@ __global__ void __launch_bounds__(256) k_quantize_affine(const T *__restrict__ w
   }
 }
 
+// round(RN(a / s)) (a correctly rounded divide, then round half away from zero) from the
+// product y = RN(a * rs), rs = RN(1 / s): y is within 1.2e-7 |y| of a / s and RN(a / s) within
+// 6e-8 |y| of it, so when y lies farther than m = 4e-7 |y| + 1e-6 (which also covers the
+// error of computing y - floor(y)) from every half-integer, both round to the same integer;
+// otherwise -- near a half-integer, or |y| above about 2^20 where m reaches 0.5 -- the divide
+// itself decides.
+__device__ __forceinline__ float qa_round_div(float a, float s, float rs) {
+  const float y = __fmul_rn(a, rs);
+  const float d = fabsf(__fsub_rn(__fsub_rn(y, floorf(y)), 0.5f));
+  const float m = __fmaf_rn(fabsf(y), 4e-7f, 1e-6f);
+  return d > m ? roundf(y) : roundf(__fdiv_rn(a, s));
+}
+
 // 16 bytes of T as floats (8 bf16 or 4 fp32)
 __device__ __forceinline__ void qa_load16(const __nv_bfloat16 *p, float (&f)[8]) {
   const uint4 v = *reinterpret_cast<const uint4 *>(p);
@@ -112,8 +125,8 @@ __device__ __forceinline__ void qa_load16(const float *p, float (&f)[4]) {
 // One thread per group: 16-byte loads of the group (all of a thread's loads in flight at
 // once), its range, then a second read of the same bytes (from L1) to quantize, and the
 // group's G * BITS / 32 words stored together.  Needs w and every row 16-byte aligned and wq
-// 16-byte aligned (the host checks; otherwise k_quantize_affine runs).  Same arithmetic as
-// k_quantize_affine, so the same bits.
+// 16-byte aligned (the host checks; otherwise k_quantize_affine runs).  The same results as
+// k_quantize_affine: the per-element divide is qa_round_div, which rounds identically.
 template <typename T, int G, int BITS>
 __global__ void __launch_bounds__(256) k_quantize_affine_t(const T *__restrict__ w, int64_t rows,
                                                            int64_t cols,
@@ -142,6 +155,7 @@ __global__ void __launch_bounds__(256) k_quantize_affine_t(const T *__restrict__
   const float nb = float((1 << BITS) - 1);
   float scale, bias;
   qa_params(hi, lo, nb, scale, bias);
+  const float rs = __frcp_rn(scale);
   uint32_t word[WORDS];
 #pragma unroll
   for (int i = 0; i < WORDS; ++i) word[i] = 0u;
@@ -152,7 +166,7 @@ __global__ void __launch_bounds__(256) k_quantize_affine_t(const T *__restrict__
 #pragma unroll
     for (int j = 0; j < EPV; ++j) {
       const int e = k * EPV + j;
-      const float q = fminf(fmaxf(roundf(__fdiv_rn(__fsub_rn(f[j], bias), scale)), 0.0f), nb);
+      const float q = fminf(fmaxf(qa_round_div(__fsub_rn(f[j], bias), scale, rs), 0.0f), nb);
       word[e / PER] |= uint32_t(q) << ((e % PER) * BITS);
     }
   }
