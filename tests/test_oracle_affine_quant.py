@@ -54,3 +54,42 @@ def test_quantize_affine_bf16_scales_are_rounded_fp32():
 def test_round_half_away():
     x = np.array([0.5, 1.5, 2.5, -0.5, -2.5, 0.49999997, -0.49999997, 0.0], np.float32)
     assert F._round_half_away(x).tolist() == [1, 2, 3, -1, -3, 0, 0, 0]
+
+
+def _round_div_by_reciprocal(a, s):
+    """The kernel's per-element rounding, restated with the same IEEE fp32 steps: y =
+    RN(a * RN(1/s)); y's rounding is taken when y is farther than 4e-7|y| + 1e-6 from every
+    half-integer, the exact quotient's otherwise.  Returns (result, used_the_product)."""
+    a = np.asarray(a, np.float32)
+    s = np.asarray(s, np.float32)
+    rs = np.float32(1.0) / s
+    y = (a * rs).astype(np.float32)
+    d = np.abs((y - np.floor(y)).astype(np.float32) - np.float32(0.5)).astype(np.float32)
+    m = (np.abs(y).astype(np.float64) * np.float64(np.float32(4e-7))
+         + np.float64(np.float32(1e-6))).astype(np.float32)
+    fast = d > m
+    exact = F._round_half_away((a / s).astype(np.float32))
+    return np.where(fast, F._round_half_away(y), exact), fast
+
+
+def test_reciprocal_rounding_matches_the_divide():
+    """Random operands and adversarial ones a few ulps from (k + 0.5) * s: the product's
+    rounding, where the margin lets it stand, equals the correctly rounded quotient's."""
+    rng = np.random.default_rng(11)
+    s = rng.uniform(1e-4, 3.0, 200000).astype(np.float32) * rng.choice([-1, 1], 200000)
+    a = (rng.uniform(-300, 300, 200000).astype(np.float32) * np.abs(s)).astype(np.float32)
+    k = rng.integers(-260, 260, 200000).astype(np.float32)
+    tie = ((k + np.float32(0.5)) * s).astype(np.float32)
+    for ulps in (-3, -1, 0, 1, 3):
+        adv = np.nextafter(tie, np.float32(np.inf) if ulps > 0 else np.float32(-np.inf)) \
+            if ulps else tie
+        for _ in range(abs(ulps) - 1 if ulps else 0):
+            adv = np.nextafter(adv, np.float32(np.inf) if ulps > 0 else np.float32(-np.inf))
+        a = np.concatenate([a, adv.astype(np.float32)])
+    s_all = np.resize(s, a.shape)
+    got, fast = _round_div_by_reciprocal(a, s_all)
+    want = F._round_half_away((a / s_all).astype(np.float32))
+    assert np.array_equal(got, want)
+    assert fast[:200000].mean() > 0.9             # random operands: the divide is rare
+    near = np.abs((a / s_all) - np.floor(a / s_all) - 0.5) < 1e-7
+    assert not fast[near].any()
