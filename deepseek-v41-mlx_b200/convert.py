@@ -141,12 +141,8 @@ def quantize_engram_table_from_checkpoint(ckpt, weight_name: str, bits: int, gro
     so the result is identical to converting the table in one piece."""
     t = L.torch()
     sname = weight_name[:-len(".weight")] + ".scale"
-    first_w = ckpt.get(weight_name, "cuda", rows=(0, 1))
-    first_s = ckpt.get(sname, "cuda", rows=(0, 1))
-    d = first_w.shape[-1]
-    block = d // first_s.shape[-1]
-    with ckpt._open(ckpt.where[weight_name], framework="pt") as f:
-        rows = f.get_slice(weight_name).get_shape()[0]
+    rows, d = ckpt.shape(weight_name)
+    block = d // ckpt.shape(sname)[-1]
     out_w = t.empty((rows, d * bits // 32), dtype=t.uint32, device="cuda")
     out_s = t.empty((rows, d // group_size), dtype=t.bfloat16, device="cuda")
     out_b = t.empty_like(out_s)

@@ -88,6 +88,13 @@ class Checkpoint:
     def __contains__(self, key):
         return key in self.where
 
+    def shape(self, key):
+        """The stored shape of tensor ``key`` (read from the shard header, no data)."""
+        if key not in self.where:
+            raise KeyError(f"{key} is not in the checkpoint")
+        with self._open(self.where[key], framework="pt") as f:
+            return tuple(f.get_slice(key).get_shape())
+
     def get(self, key, device="cuda", rows=None):
         """The tensor ``key`` (rows [lo, hi) of it with ``rows=(lo, hi)``) on ``device``; fp8,
         ue8m0 and int8 tensors come back as their bytes (uint8), others as stored."""

@@ -71,3 +71,12 @@ def test_engram_tables_and_row_shards(ckpt):
         lo, hi = rank * part, min(RF.ROWS, (rank + 1) * part)
         assert gs.embed.part == part and gs.embed.row_lo == lo
         assert np.array_equal(gs.embed.weight.numpy(), arr["table"][lo:hi])
+
+
+def test_shapes_from_headers(ckpt):
+    c, _ = ckpt
+    assert c.shape(f"layers.{RF.ENGRAM_LAYER}.engram.embed.weight") == (RF.ROWS, RF.HD)
+    assert c.shape(f"layers.{RF.ENGRAM_LAYER}.engram.embed.scale") == (RF.ROWS, RF.HD // 32)
+    assert c.shape(f"layers.{RF.MOE_LAYER}.ffn.experts.0.w1.weight") == (RF.I, RF.D // 2)
+    with pytest.raises(KeyError):
+        c.shape("no.such.weight")
