@@ -10,7 +10,6 @@ order), so the result must equal the single-process lookup of the whole table ex
 from __future__ import annotations
 
 import os
-import socket
 
 import pytest
 import torch
@@ -19,13 +18,6 @@ import torch.multiprocessing as mp
 
 ROWS, D, BLOCK = 50, 64, 32
 
-
-def _free_port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    port = s.getsockname()[1]
-    s.close()
-    return port
 
 
 def _table(world):
@@ -88,16 +80,14 @@ def _cases(world):
             torch.randint(0, part * world, (9, 3), generator=g)]   # ids in the pad rows too
 
 
-def _worker(rank, world, port, out_q):
+def _worker(rank, world, init, out_q):
     import sys
     here = os.path.dirname(os.path.abspath(__file__))
     sys.path.insert(0, here)
     import conftest  # noqa: F401  (registers the package)
     import importlib
     engram = importlib.import_module("deepseek_v41_mlx_b200.engram")
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    dist.init_process_group("gloo", init_method=init, rank=rank, world_size=world)
     try:
         codes, scale = _table(world)
         emb = engram.ParallelEngramEmbedding(ROWS, D, BLOCK, ops=CpuRowOps())
@@ -117,11 +107,11 @@ def _worker(rank, world, port, out_q):
 
 
 @pytest.mark.parametrize("world", [2, 3])
-def test_parallel_engram_matches_single_table(world):
+def test_parallel_engram_matches_single_table(world, tmp_path):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    init = f"file://{tmp_path / 'rendezvous'}"   # no TCP port to race for
+    procs = [ctx.Process(target=_worker, args=(r, world, init, q)) for r in range(world)]
     for p in procs:
         p.start()
     got = {}

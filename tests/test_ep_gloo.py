@@ -9,7 +9,6 @@ single-process computation of the same pairs exactly (same fp32 operations).
 from __future__ import annotations
 
 import os
-import socket
 
 import pytest
 import torch
@@ -18,13 +17,6 @@ import torch.multiprocessing as mp
 
 E, D, T, K = 12, 16, 7, 3
 
-
-def _free_port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    port = s.getsockname()[1]
-    s.close()
-    return port
 
 
 def _problem(seed):
@@ -43,16 +35,14 @@ def _reference(W, x, idx, w):
     return ep.weighted_sum(Y, w)
 
 
-def _worker(rank, world, port, out_q):
+def _worker(rank, world, init, out_q):
     import sys
     here = os.path.dirname(os.path.abspath(__file__))
     sys.path.insert(0, here)
     import conftest  # noqa: F401  (registers the package)
     import importlib
     ep = importlib.import_module("deepseek_v41_mlx_b200.ep")
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    dist.init_process_group("gloo", init_method=init, rank=rank, world_size=world)
     try:
         W, xs, idx, wts = _problem(0)
         epr = E // world
@@ -84,16 +74,14 @@ def _prefill_reference(W, x, idx, w, shared):
     return ep.ascending_sum(Y, idx, shared)
 
 
-def _prefill_worker(rank, world, port, out_q):
+def _prefill_worker(rank, world, init, out_q):
     import sys
     here = os.path.dirname(os.path.abspath(__file__))
     sys.path.insert(0, here)
     import conftest  # noqa: F401
     import importlib
     ep = importlib.import_module("deepseek_v41_mlx_b200.ep")
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    dist.init_process_group("gloo", init_method=init, rank=rank, world_size=world)
     try:
         W, xs, idx, wts = _problem(1)
         epr = E // world
@@ -118,13 +106,13 @@ def _prefill_worker(rank, world, port, out_q):
 
 
 @pytest.mark.parametrize("world", [2, 3])
-def test_ep_prefill_weights_travel_gloo(world):
+def test_ep_prefill_weights_travel_gloo(world, tmp_path):
     """Prefill form: routing weights travel with the pairs, outputs return as bf16 and are
     summed in ascending expert order -- exactly the single-process result."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_prefill_worker, args=(r, world, port, q)) for r in range(world)]
+    init = f"file://{tmp_path / 'rendezvous'}"   # no TCP port to race for
+    procs = [ctx.Process(target=_prefill_worker, args=(r, world, init, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=120) for _ in range(world)]
@@ -146,11 +134,11 @@ def test_ascending_sum_order():
 
 
 @pytest.mark.parametrize("world", [2, 3])
-def test_ep_dispatch_combine_gloo(world):
+def test_ep_dispatch_combine_gloo(world, tmp_path):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    init = f"file://{tmp_path / 'rendezvous'}"   # no TCP port to race for
+    procs = [ctx.Process(target=_worker, args=(r, world, init, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=120) for _ in range(world)]
