@@ -54,6 +54,7 @@ PROTOTYPES = {
     "dsv41_get_last_error": (C.c_char_p, []),
     "dsv41_abi_version": (_I, []),
     "dsv41_device_status": (_I, [_P, _U32P]),
+    "dsv41_set_wait_limit_ns": (_I, [C.c_uint64]),
     "dsv41_prof_enable": (_I, [_I]),
     "dsv41_prof_reset": (_I, []),
     "dsv41_prof_report": (_I, [C.c_char_p, _SZ]),
@@ -82,6 +83,7 @@ PROTOTYPES = {
     "dsv41_ep_handle": (_I, [_P, _P]),
     "dsv41_ep_connect": (_I, [_P, _P]),
     "dsv41_ep_destroy": (_I, [_P]),
+    "dsv41_ep_wait": (_I, [_P, _I, _P]),
     "dsv41_moe_ep_decode_workspace_size": (_SZ, [C.POINTER(MoeConfig), _P, _I64]),
     "dsv41_moe_ep_decode": (_I, [C.POINTER(MoeConfig), C.POINTER(MoeWeights), _P, _P, _I64, _I,
                                  _P, _P, _P, _P, _SZ, _P]),

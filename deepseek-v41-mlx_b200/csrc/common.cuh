@@ -205,16 +205,37 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
-// Bounded wait: gives up after DSV41_WAIT_NS of wall time (checked every 256
-// polls) or 2^26 polls, whichever comes first.  On expiry the device status
-// flag is raised and false is returned so the caller can bail out.
+// Wall-time limit of every bounded device wait, per device (dsv41_set_wait_limit_ns;
+// default 2 s).
 #define DSV41_WAIT_NS 2000000000ull
+__device__ unsigned long long g_wait_ns = DSV41_WAIT_NS;
+
+// Bounded wait: gives up after g_wait_ns of wall time (checked every 256 polls) or
+// 2^26 polls, whichever comes first.  On expiry the device status flag is raised and
+// false is returned so the caller can bail out.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
+  const unsigned long long lim = g_wait_ns;
   for (uint32_t i = 1; i < (1u << 26); ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0 && globaltimer_ns() - t0 > DSV41_WAIT_NS) break;
+    if ((i & 255u) == 0 && globaltimer_ns() - t0 > lim) break;
+  }
+  dev_flag(DSV41_DEVST_TIMEOUT);
+  return false;
+}
+
+// The same wait, which also gives up as soon as *abort (a shared-memory flag that a warp of
+// this CTA sets when its own wait ran out) is non-zero, so that the CTA's warps give up
+// together instead of leaving some of them at a barrier the others never reach.
+__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t *bar, uint32_t parity,
+                                                   const volatile int *abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  const unsigned long long lim = g_wait_ns;
+  for (uint32_t i = 1; i < (1u << 26); ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 0 && (*abort != 0 || globaltimer_ns() - t0 > lim)) break;
   }
   dev_flag(DSV41_DEVST_TIMEOUT);
   return false;

@@ -36,6 +36,13 @@ extern "C" int dsv41_device_status(void *stream, uint32_t *flags_out) {
   return cuda_status(e, "dsv41_device_status");
 }
 
+extern "C" int dsv41_set_wait_limit_ns(uint64_t ns) {
+  DSV41_REQUIRE(ns == 0 || (ns >= 100000ull && ns <= 60000000000ull), DSV41_ERR_BAD_ARG,
+                "wait limit must be 0 (default) or within [1e5, 6e10] ns");
+  const unsigned long long v = ns ? ns : DSV41_WAIT_NS;
+  return cuda_status(cudaMemcpyToSymbol(g_wait_ns, &v, sizeof(v)), "dsv41_set_wait_limit_ns");
+}
+
 // ======================================================================= profiling
 
 extern "C" int dsv41_prof_enable(int on) {
@@ -1106,6 +1113,15 @@ extern "C" int dsv41_ep_connect(dsv41_ep_ctx *c, const void *handles) {
     c->opened[r] = true;
   }
   c->connected = true;
+  return DSV41_OK;
+}
+
+extern "C" int dsv41_ep_wait(const dsv41_ep_ctx *c, int which, void *stream) {
+  DSV41_REQUIRE(c, DSV41_ERR_BAD_ARG, "NULL context");
+  DSV41_REQUIRE(which == 0 || which == 1, DSV41_ERR_BAD_ARG,
+                "which must be 0 (rows received) or 1 (outputs returned)");
+  k_ep_wait<<<1, 64, 0, STREAM(stream)>>>(c->buf, c->L, which, c->dseq);
+  DSV41_CHECK_LAUNCH("ep_wait");
   return DSV41_OK;
 }
 
@@ -2457,7 +2473,9 @@ extern "C" int dsv41_engram_dequant_rows(const void *packed, int64_t n_rows, int
 //
 // The first call on a device looks up the array's device address for that device
 // (cudaGetSymbolAddress, with that device current); make that first call before
-// any stream capture.  All calls on a device share the one array and it keeps the
+// any stream capture.  The address is kept for the life of the process: after a
+// cudaDeviceReset of that device it is stale, so do not call this entry point again
+// in a process that reset the device.  All calls on a device share the one array and it keeps the
 // previous call's contents: the tickets are cleared on every call, and calls whose
 // kernels overlap on the GPU (different streams, no ordering between them) race on
 // the array and give wrong results -- order them on one stream.
@@ -2499,8 +2517,11 @@ extern "C" int dsv41_gemv_fp8_block_noalloc(const void *x, int64_t M, int64_t K,
                                             void *stream) {
   DSV41_REQUIRE(out_dtype == DSV41_F32 || out_dtype == DSV41_BF16, DSV41_ERR_BAD_DTYPE,
                 "out_dtype must be F32 or BF16");
-  DSV41_REQUIRE(K > 0 && K % 32 == 0, DSV41_ERR_BAD_SHAPE, "K must be a positive multiple of 32");
-  DSV41_REQUIRE(M >= 1 && M <= 32 && M * K <= 262144 && N >= 1 && N <= 16384,
+  DSV41_REQUIRE(M >= 0 && N >= 0 && K >= 0 && K % 32 == 0, DSV41_ERR_BAD_SHAPE,
+                "negative shape, or K not a multiple of 32");
+  if (M == 0 || N == 0) return DSV41_OK;          // as dsv41_gemv_fp8_block: nothing to do
+  DSV41_REQUIRE(K > 0, DSV41_ERR_BAD_SHAPE, "K must be positive");
+  DSV41_REQUIRE(M <= 32 && M * K <= 262144 && N <= 16384,
                 DSV41_ERR_UNSUPPORTED,
                 "gemv_fp8_block_noalloc: needs 1 <= M <= 32, M*K <= 262144, 1 <= N <= 16384 "
                 "(got M=%lld K=%lld N=%lld); use dsv41_gemv_fp8_block with a workspace",

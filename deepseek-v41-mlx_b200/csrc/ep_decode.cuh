@@ -156,10 +156,11 @@ __global__ void k_ep_wait(const uint8_t *own, EpLayout L, int which,
       reinterpret_cast<const unsigned long long *>(own + L.flags) + which * L.ws + s;
   if (ld_acquire_sys_u64(f) >= seq) return;
   const uint64_t t0 = globaltimer_ns();
+  const unsigned long long lim = g_wait_ns;
   for (uint32_t it = 0; it < (1u << 26); ++it) {
     __nanosleep(128);
     if (ld_acquire_sys_u64(f) >= seq) return;
-    if ((it & 255u) == 0 && globaltimer_ns() - t0 > DSV41_WAIT_NS) break;
+    if ((it & 255u) == 0 && globaltimer_ns() - t0 > lim) break;
   }
   dev_flag(DSV41_DEVST_TIMEOUT);
 }

@@ -330,6 +330,18 @@ __device__ __forceinline__ void qg_cp_arrive(uint64_t *bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 __device__ __forceinline__ void qg_cp_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Producer exit: its scale copies and the last ST stages' TMA copies have landed (bounded
+// waits on the stages' full barriers), so no copy can arrive after the CTA has exited even
+// when the consumers gave up early.  On the normal path those phases completed already.
+template <int ST>
+__device__ __forceinline__ void qg_drain(uint64_t *full, uint32_t issued, int lane) {
+  qg_cp_wait_all();
+  if (lane == 0)
+    for (uint32_t i = issued > uint32_t(ST) ? issued - ST : 0u; i < issued; ++i)
+      mbar_wait(&full[i % ST], (i / ST) & 1);
+  __syncwarp();
+}
 // bulk copy global -> shared (16-byte aligned, size a multiple of 16), completes on `bar`
 __device__ __forceinline__ void qg_bulk_load(uint32_t dst, const void *src, uint32_t bytes,
                                              uint64_t *bar) {
@@ -433,8 +445,13 @@ __global__ void __launch_bounds__(QG_THREADS, QG_MIN_CTAS)
   uint64_t *full = reinterpret_cast<uint64_t *>(sc_ring + ST * C::SC_BYTES);
   uint64_t *empty = full + ST;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // set by the first warp whose bounded wait ran out: the others then give up at their
+  // next wait, and consumer warps that gave up keep taking part in the split-K barriers, so
+  // no warp is left at a barrier that another warp never reaches
+  __shared__ volatile int s_abort;
 
   if (threadIdx.x == 0) {
+    s_abort = 0;
     for (int s = 0; s < ST; ++s) {
       mbar_init(&full[s], 33);     // TMA tx arrival + one scale-store arrival per producer lane
       mbar_init(&empty[s], QG_CW);
@@ -480,10 +497,11 @@ __global__ void __launch_bounds__(QG_THREADS, QG_MIN_CTAS)
         const int slot = it % ST;
         const uint32_t ph = (it / ST) & 1;
         bool ok = true;
-        if (lane == 0) ok = mbar_wait(&empty[slot], ph ^ 1);
+        if (lane == 0) ok = mbar_wait_or_abort(&empty[slot], ph ^ 1, &s_abort);
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) {
-          qg_cp_wait_all();      // no copy may land after the CTA is gone
+          s_abort = 1;
+          qg_drain<ST>(full, it, lane);   // no copy may land after the CTA is gone
           return;
         }
         uint8_t *st = smem + slot * C::TILE_BYTES;
@@ -519,7 +537,7 @@ __global__ void __launch_bounds__(QG_THREADS, QG_MIN_CTAS)
         }
       }
     }
-    qg_cp_wait_all();
+    qg_drain<ST>(full, it, lane);
     return;
   }
 
@@ -530,6 +548,7 @@ __global__ void __launch_bounds__(QG_THREADS, QG_MIN_CTAS)
   const int xb = xcol_perm<WF>(g);                // x smem row (mod 8) for mma column g
   const int cs[2] = {xcol_perm<WF>(2 * t), xcol_perm<WF>(2 * t + 1)};  // slots of my columns
   uint32_t it = 0;
+  bool dead = false;                // this warp's wait ran out (warp-uniform)
 
   QChunk pre{};
   chunk_prefetch(p, blockIdx.x, nitems, pre);
@@ -553,7 +572,15 @@ __global__ void __launch_bounds__(QG_THREADS, QG_MIN_CTAS)
     for (int ks = kb; ks < ke; ++ks, ++it) {
       const int slot = it % ST;
       const uint32_t ph = (it / ST) & 1;
-      if (!mbar_wait(&full[slot], ph)) return;
+      if (!dead) {
+        bool ok = mbar_wait_or_abort(&full[slot], ph, &s_abort);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) {
+          dead = true;
+          s_abort = 1;
+        }
+      }
+      if (dead) continue;           // no data, no compute; barriers below are still met
       const uint32_t st = smem_u32(smem + slot * C::TILE_BYTES);
       const uint32_t xst = st + NMAT * C::W_BYTES;
       const uint32_t scb = smem_u32(sc_ring + slot * C::SC_BYTES);

@@ -168,7 +168,7 @@ class MoE:
         objs = (self.gate.weight, self.gate.bias, e.gate_proj.weight, e.gate_proj.scales,
                 e.up_proj.weight, e.up_proj.scales, e.down_proj.weight, e.down_proj.scales,
                 s.w1.weight, s.w1.scales, s.w3.weight, s.w3.scales, s.w2.weight, s.w2.scales)
-        return (self.pack_decode_scales, self.row_pair_down) + tuple(
+        return (self.pack_decode_scales, self.row_pair_down, self.round_bf16) + tuple(
             (id(o), o.data_ptr() if hasattr(o, "data_ptr") else 0, getattr(o, "_version", 0))
             for o in objs)
 

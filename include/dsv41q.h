@@ -84,6 +84,13 @@ int dsv41_abi_version(void);
 /* Reads and clears the device-side status flags of the current device
  * (bit 0: a bounded wait ran out).  Synchronises `stream`. */
 int dsv41_device_status(void *stream, uint32_t *flags_out);
+/* Wall-time limit of every bounded device wait (mbarrier waits of the pipelined
+ * kernels, waits on peers' flags in expert-parallel decode) on the current device, in
+ * nanoseconds; 0 restores the default of 2 s.  A wait that runs out raises bit 0 of
+ * dsv41_device_status and its kernel returns.  Set it while no kernel of this library
+ * runs on the device.  No counterpart in the reference (MLX has no bounded device waits;
+ * its own failure handling is the Metal-timeout retry of deepseek_v41_mlx/generate.py:47-67). */
+int dsv41_set_wait_limit_ns(uint64_t ns);
 
 /* ---- launch timing (no reference counterpart; the reference times with
  * ad-hoc time.time(), scripts/ppl_large.py:81-84).  When enabled, every hot
@@ -342,6 +349,12 @@ size_t dsv41_ep_handle_bytes(void);
 int dsv41_ep_handle(const dsv41_ep_ctx *ctx, void *handle_out);
 int dsv41_ep_connect(dsv41_ep_ctx *ctx, const void *handles);
 int dsv41_ep_destroy(dsv41_ep_ctx *ctx);
+/* The bounded wait of one exchange direction of dsv41_moe_ep_decode, on its own: until
+ * every rank has published the current step's flag (which = 0: its rows arrived in this
+ * rank's buffer; which = 1: its outputs arrived back), or the wait limit runs out (bit 0 of
+ * dsv41_device_status).  Stream-ordered; does not advance the step.  Part of the
+ * exchange that replaces upstream's fp32 all_reduce (docs/reference/model.py:895-902). */
+int dsv41_ep_wait(const dsv41_ep_ctx *ctx, int which, void *stream);
 size_t dsv41_moe_ep_decode_workspace_size(const dsv41_moe_config *cfg, const dsv41_ep_ctx *ctx,
                                           int64_t T);
 int dsv41_moe_ep_decode(const dsv41_moe_config *cfg, const dsv41_moe_weights *w,

@@ -43,6 +43,14 @@ def test_host_side_validation_without_gpu():
     st = lib.dsv41_act_quant_fp8(None, 2, 40, 32, 1, None, None, 0, None, None)
     assert st == L.BAD_SHAPE
     assert lib.dsv41_gemv_workspace_size(32, 4096, 7168) > 32 * 7168 * 2
+    assert lib.dsv41_set_wait_limit_ns(10) == L.BAD_ARG          # below 0.1 ms
+    assert lib.dsv41_ep_wait(None, 0, None) == L.BAD_ARG
+    # the allocation-free GEMV: empty shapes are a no-op (as for the workspace entry point),
+    # oversized ones are refused before any device work
+    assert lib.dsv41_gemv_fp8_block_noalloc(None, 0, 1024, None, None, 64, L.F32, None, None) == 0
+    assert lib.dsv41_gemv_fp8_block_noalloc(None, 4, 1024, None, None, 0, L.F32, None, None) == 0
+    assert lib.dsv41_gemv_fp8_block_noalloc(None, 33, 1024, None, None, 64, L.F32, None,
+                                            None) == L.UNSUPPORTED
     cfg = L.MoeConfig(dim=7168, inter=2048, n_experts=384, topk=6, score_func=0, gate_temp=1.0,
                       norm_topk_prob=1, route_scale=1.5, swiglu_limit=10.0, flags=1)
     assert lib.dsv41_moe_decode_workspace_size(ctypes.byref(cfg), 64) > 64 * 6 * 7168 * 4
