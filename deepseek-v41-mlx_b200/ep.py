@@ -136,19 +136,21 @@ class EPMoE:
         self._ws = None
 
     # ---------------------------------------------------------------- GPU path
-    @classmethod
-    def random_init(cls, q, torch, dev, rank, world, E, D, I, topk, seed=0):
-        """Random weights of the release layout; the router and shared expert are the
-        same on every rank (same seed), each rank draws only its own experts."""
+    @staticmethod
+    def _random_layer(q, torch, dev, n_experts, D, I, topk, seed):
+        """An empty MoE layer of ``n_experts`` experts and the generator that draws the parts
+        every rank holds alike (the router over all experts and the shared expert)."""
         import types
-        if E % world:
-            raise ValueError(f"{E} experts do not split over {world} ranks")
         g = torch.Generator(device=dev).manual_seed(seed)
         args = types.SimpleNamespace(n_activated_experts=topk, score_func="sqrtsoftplus",
                                      gate_temp=1.0, norm_topk_prob=True, route_scale=1.5,
-                                     n_routed_experts=E // world, dim=D, moe_inter_dim=I,
+                                     n_routed_experts=n_experts, dim=D, moe_inter_dim=I,
                                      swiglu_limit=10.0)
         m = q.moe.MoE(args, round_bf16=True, cuda_graph=False)
+        return m, g
+
+    @staticmethod
+    def _draw_replicated(torch, dev, m, g, E, D, I):
         gate_w = (torch.randn(E, D, device=dev, generator=g) * D ** -0.5).to(torch.bfloat16)
         gate_b = torch.randn(E, device=dev, generator=g) * 0.01
         for key, (n, k) in (("1", (I, D)), ("3", (I, D)), ("2", (D, I))):
@@ -158,21 +160,60 @@ class EPMoE:
             pr.weight = w
             pr.scales = torch.randint(118, 128, (n // 32, k // 32), dtype=torch.uint8, device=dev,
                                       generator=g)
+        return gate_w, gate_b
+
+    @staticmethod
+    def _draw_shard(torch, dev, rank, epr, D, I, seed):
+        """Rank ``rank``'s experts: {projection: (weight, scales)}, from its own generator."""
         gl = torch.Generator(device=dev).manual_seed(seed + 1000 + rank)
+        out = {}
+        for name, (n, k) in (("gate_proj", (I, D)), ("up_proj", (I, D)), ("down_proj", (D, I))):
+            w = torch.randint(0, 256, (epr, n, k // 2), dtype=torch.uint8, device=dev, generator=gl)
+            s = torch.randint(120, 129, (epr, n, k // 32), dtype=torch.uint8, device=dev,
+                              generator=gl)
+            out[name] = (w, s)
+        return out
+
+    @classmethod
+    def random_init(cls, q, torch, dev, rank, world, E, D, I, topk, seed=0):
+        """Random weights of the release layout; the router and shared expert are the
+        same on every rank (same seed), each rank draws only its own experts."""
+        if E % world:
+            raise ValueError(f"{E} experts do not split over {world} ranks")
         epr = E // world
+        m, g = cls._random_layer(q, torch, dev, epr, D, I, topk, seed)
+        gate_w, gate_b = cls._draw_replicated(torch, dev, m, g, E, D, I)
         # the local layer's own router is not used (routing is over all E experts)
         m.gate.weight = gate_w[rank * epr:(rank + 1) * epr].contiguous()
         m.gate.bias = gate_b[rank * epr:(rank + 1) * epr].contiguous()
-        for name, (n, k) in (("gate_proj", (I, D)), ("up_proj", (I, D)), ("down_proj", (D, I))):
+        for name, (w, s) in cls._draw_shard(torch, dev, rank, epr, D, I, seed).items():
             pr = getattr(m.experts, name)
-            pr.weight = torch.randint(0, 256, (epr, n, k // 2), dtype=torch.uint8, device=dev,
-                                      generator=gl)
-            pr.scales = torch.randint(120, 129, (epr, n, k // 32), dtype=torch.uint8, device=dev,
-                                      generator=gl)
+            pr.weight, pr.scales = w, s
         ep = cls(m, world, rank, E)
         ep.gate_w, ep.gate_b = gate_w, gate_b
         ep.topk = topk
         return ep
+
+    @classmethod
+    def random_init_full(cls, q, torch, dev, world, E, D, I, topk, seed=0):
+        """The single-GPU layer holding what ``random_init`` gives the ``world`` ranks
+        together: the same router and shared expert, every rank's experts in rank order
+        (a single-GPU reference for the sharded layer)."""
+        if E % world:
+            raise ValueError(f"{E} experts do not split over {world} ranks")
+        epr = E // world
+        m, g = cls._random_layer(q, torch, dev, E, D, I, topk, seed)
+        m.gate.weight, m.gate.bias = cls._draw_replicated(torch, dev, m, g, E, D, I)
+        parts = {"gate_proj": [], "up_proj": [], "down_proj": []}
+        for r in range(world):
+            for name, ws in cls._draw_shard(torch, dev, r, epr, D, I, seed).items():
+                parts[name].append(ws)
+        for name, lst in parts.items():
+            pr = getattr(m.experts, name)
+            pr.weight = torch.cat([w for w, _ in lst])
+            pr.scales = torch.cat([s for _, s in lst])
+            lst.clear()
+        return m
 
     def route(self, xf):
         """Replicated router over all E experts (moe.py:58-74)."""

@@ -1,5 +1,6 @@
 """bench.py's reference arm on CPU: one JSON line with the contract's keys (the numpy
-restatement of the path timed on the host cores); ranks other than 0 print nothing."""
+restatement of the path timed on the host cores, whole steps; 16 experts here to keep the
+test short); ranks other than 0 print nothing."""
 
 from __future__ import annotations
 
@@ -14,7 +15,7 @@ from conftest import ROOT
 def _run(extra_env=None):
     env = dict(os.environ, **(extra_env or {}))
     return subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference",
-                           "--steps", "1", "--warmup", "0", "--ref-sample", "1"],
+                           "--steps", "2", "--warmup", "0", "--experts", "16"],
                           capture_output=True, text=True, timeout=600, env=env, cwd=ROOT)
 
 
@@ -32,6 +33,9 @@ def test_reference_arm_json_line():
     cb = d["cpu_baseline"]
     assert cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["sample"]
     assert cb["value"] == d["value"]
+    # whole steps were timed (not a sample scaled up), and the count printed is the count run
+    assert d["estimated"] is False and cb["estimated"] is False
+    assert d["steps"] == 2 and d["steps"] * d["ms_per_step"] / 1e3 <= d["wall_s"]
     assert d["e2e"] == {"value": d["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}
 

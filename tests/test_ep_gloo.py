@@ -160,3 +160,26 @@ def test_plan_dispatch_orders_by_owner():
     assert counts.tolist() == [3, 2, 1]        # owners 1,0,2,0,1,0
     # stable inside an owner: row-major pair order
     assert order.tolist()[:3] == [1, 3, 5]
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_random_init_full_is_the_union_of_shards(world):
+    """The single-GPU reference layer the bench checks expert parallelism against holds the
+    same router, shared expert and experts as the ranks' shards together (CPU tensors)."""
+    import deepseek_v41_mlx_b200 as q
+    from deepseek_v41_mlx_b200.ep import EPMoE
+    dev = torch.device("cpu")
+    E, D, I, k = 8, 64, 32, 2
+    full = EPMoE.random_init_full(q, torch, dev, world, E, D, I, k)
+    epr = E // world
+    for r in range(world):
+        part = EPMoE.random_init(q, torch, dev, r, world, E, D, I, k)
+        assert torch.equal(part.gate_w, full.gate.weight)
+        assert torch.equal(part.gate_b, full.gate.bias)
+        for name in ("gate_proj", "up_proj", "down_proj"):
+            a, b = getattr(part.local.experts, name), getattr(full.experts, name)
+            assert torch.equal(a.weight, b.weight[r * epr:(r + 1) * epr])
+            assert torch.equal(a.scales, b.scales[r * epr:(r + 1) * epr])
+        for key in ("w1", "w2", "w3"):
+            a, b = getattr(part.local.shared_experts, key), getattr(full.shared_experts, key)
+            assert torch.equal(a.weight, b.weight) and torch.equal(a.scales, b.scales)
