@@ -291,7 +291,7 @@ def e2e_measure(torch, fn, host_in, dev_in, out_host, K, W, flush, stream):
 
 # ---------------------------------------------------------------- d1: fp8 dense GEMV --
 
-def d1_measure(q, torch, dev, flush, stream, K, W, peaks):
+def d1_measure(q, torch, dev, flush, stream, K, W, peaks, ms_list=(1, 32)):
     hbm, _, src = peaks
     N, Kd = D1_N, D1_K
     g = torch.Generator(device=dev).manual_seed(11)
@@ -303,7 +303,7 @@ def d1_measure(q, torch, dev, flush, stream, K, W, peaks):
     for w in ws:
         w[(w & 0x7F) == 0x7F] = 0
     out = {}
-    for M in (1, 32):
+    for M in ms_list:
         x = torch.randn(M, Kd, device=dev, generator=g).to(torch.bfloat16)
         byts = N * Kd + (N // 32) * (Kd // 32) + M * Kd * 2 + M * N * 2
         gr = graphed(torch, [lambda c=c: q.linear.linear_fp8(x, ws[c], ss[c]) for c in range(copies)])
@@ -512,7 +512,8 @@ def _engram_args(vocab):
                                  engram_compressed_vocab_size=99092)
 
 
-def engram_measurement(q, torch, dev, flush, stream, K, W, vocab=4_000_000, peaks=None):
+def engram_measurement(q, torch, dev, flush, stream, K, W, vocab=4_000_000, peaks=None,
+                       tokens=(1, PREFILL_T)):
     """d5: engram table fp8 e4m3 [96,000,xxx x 1024] (one ue8m0 per row, [115, 127]) built on
     the device, 24 rows per token (2/3/4-gram x 8 heads, one layer, primes from 4,000,000)
     hashed from uniform compressed ids in [0, 99092); a step = hash + gather + dequant + fp32
@@ -540,7 +541,7 @@ def engram_measurement(q, torch, dev, flush, stream, K, W, vocab=4_000_000, peak
     emb = q.engram.EngramEmbedding(rows, d, block=d)
     emb.packed = table
     out = {}
-    for T in (1, PREFILL_T):
+    for T in tokens:
         start = 100 if T == 1 else 0
         ids = [torch.randint(0, 99092, (1, T), dtype=torch.int64, device=dev, generator=g)
                for _ in range(8)]
@@ -834,13 +835,20 @@ def _verdict(torch, dist, dev, rank, res, tol):
 
 
 def ep_check_decode(q, torch, dist, dev, layer, rank, world):
-    """One decode batch through the expert-parallel layer (fp32 output) on every rank,
-    against rank 0's single-GPU layer over all experts on the gathered tokens."""
+    """One decode batch through the expert-parallel layer on every rank, against rank 0's
+    single-GPU layer over all experts on the gathered tokens.  Both run the exact numerics
+    (fp32 intermediates, fp32 output): a K split that depends on the batch (the shared
+    expert's, at 64 tokens a rank against 64 x world on one GPU) then changes only the
+    fp32 summation order, where the port's bf16 rounding of intermediates could turn such an
+    order difference into a whole bf16 step."""
     from importlib import import_module
     ep = import_module("deepseek_v41_mlx_b200.ep")
     g = torch.Generator(device=dev).manual_seed(777 + rank)
     x = torch.randn(T_HEAD, D, device=dev, generator=g).to(torch.bfloat16)
+    mode = layer.local.round_bf16
+    layer.local.round_bf16 = False
     y = layer.forward(x.float())                       # fp32 out, peer-memory exchange
+    layer.local.round_bf16 = mode
     xs = [torch.empty_like(x) for _ in range(world)]
     ys = [torch.empty_like(y) for _ in range(world)]
     dist.all_gather(xs, x)
@@ -848,6 +856,7 @@ def ep_check_decode(q, torch, dist, dev, layer, rank, world):
     res = None
     if rank == 0:
         full = ep.EPMoE.random_init_full(q, torch, dev, world, E, D, I, TOPK)
+        full.round_bf16 = False
         yref = full(torch.cat(xs).float())
         yep = torch.cat(ys)
         res = [float(torch.equal(yref, yep)), _rel(yep, yref)]
@@ -1102,7 +1111,8 @@ def run_engram_only(args):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     with Clocks(0) as clk:
         r = engram_measurement(q, torch, dev, flush, torch.cuda.current_stream(), args.steps,
-                               args.warmup, args.engram_vocab)
+                               args.warmup, args.engram_vocab,
+                               tokens=tuple(int(v) for v in args.engram_tokens.split(",")))
     r["clocks"] = clk.summary()
     print(json.dumps(r))
 
@@ -1126,7 +1136,7 @@ def run_gemv_only(args):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     with Clocks(0) as clk:
         r = d1_measure(q, torch, dev, flush, torch.cuda.current_stream(), args.steps,
-                       args.warmup, _peaks())
+                       args.warmup, _peaks(), tuple(int(v) for v in args.gemv_m.split(",")))
     r["clocks"] = clk.summary()
     print(json.dumps(r))
 
@@ -1432,6 +1442,10 @@ def main():
                     help="only the fp8 dense GEMV (d1) measurements (one JSON line)")
     ap.add_argument("--engram-only", action="store_true",
                     help="only the engram d5 measurement (one JSON line)")
+    ap.add_argument("--engram-tokens", default="1,8192",
+                    help="engram positions a step (comma list; only with --engram-only)")
+    ap.add_argument("--gemv-m", default="1,32",
+                    help="activation rows of the d1 GEMV (comma list; only with --gemv-only)")
     ap.add_argument("--engram-vocab", type=int, default=4_000_000,
                     help="engram_vocab_size of d5 (4,000,000 = BASELINE; smaller only for ncu "
                          "captures)")

@@ -770,7 +770,7 @@ int side_stream(SideStream **out) {
 int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, const void *x,
                      const MoeDims &d, MoeWs &ws, const int32_t *idx, float *Y, bool shared,
                      cudaStream_t st, cudaStream_t st_shared, bool routed = true,
-                     const int32_t *tok_map = nullptr) {
+                     const int32_t *tok_map = nullptr, const int *n_valid = nullptr) {
   const int64_t T = d.T;
   const int round = (cfg->flags & DSV41_MOE_ROUND_BF16) ? 1 : 0;
   int rc;
@@ -778,7 +778,8 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
   // plan
   { ProfScope prof("moe_plan", st);
   DSV41_LAUNCH(launch_pdl(k_moe_plan, dim3(1), dim3(1024), 4 * d.E * sizeof(int), st,
-                          static_cast<const int32_t *>(idx), T, cfg->topk, d.E, ws.plan, tok_map),
+                          static_cast<const int32_t *>(idx), T, cfg->topk, d.E, ws.plan, tok_map,
+                          n_valid),
                "moe_plan"); }
   DSV41_CHECK_LAUNCH("moe_plan");
   // activations gathered per pair
@@ -1242,11 +1243,13 @@ extern "C" int dsv41_moe_ep_decode(const dsv41_moe_config *cfg, const dsv41_moe_
   // owner: experts on the received rows
   {
     ProfScope prof("ep_ids", st);
-    k_ep_ids<<<unsigned(ceil_div(dw.T, 256)), 256, 0, st>>>(c->buf, L, ids, rowmap);
+    k_ep_ids<<<unsigned(ceil_div(dw.T, 256)), 256, 0, st>>>(c->buf, L, ids, rowmap,
+                                                           wo.plan.counts + 5);
   }
   DSV41_CHECK_LAUNCH("ep_ids");
   float *Yr = wo.Y;
-  rc = moe_experts_impl(&lc, W, c->buf + L.rows, dw, wo, ids, Yr, false, st, st, true, rowmap);
+  rc = moe_experts_impl(&lc, W, c->buf + L.rows, dw, wo, ids, Yr, false, st, st, true, rowmap,
+                        wo.plan.counts + 5);
   if (rc) return rc;
   {
     ProfScope prof("ep_return", st);
@@ -2134,8 +2137,8 @@ extern "C" int dsv41_engram_lookup_sum(const int64_t *input_ids, int64_t B, int6
   ProfScope prof("engram_lookup_sum", st);
   const int G = max_ngram, H = n_heads, cols = (G - 1) * H;
   const int64_t rb = int64_t(dsv41_engram_row_bytes(d, block));
-  const unsigned blocks = unsigned(ceil_div(B * L * (d / 256) * 32, 256));
   const uint8_t *tab = static_cast<const uint8_t *>(packed);
+  const unsigned blocks = unsigned(ceil_div(B * L * (d / 256) * 32, 256));
 #define LS(T)                                                                                    \
   k_engram_lookup_sum<T><<<blocks, 256, 0, st>>>(                                                \
       input_ids, B, L, start_pos, token_map, vocab, ids_cache, max_seq, multipliers + layer * G, \

@@ -175,12 +175,14 @@ __device__ __forceinline__ int ep_rows_before(const uint8_t *own, const EpLayout
 
 // Owner side: the received rows listed compactly, source by source -- ids[j] the owner-local
 // expert of the j-th valid row and rowmap[j] its row in the receive buffer; -1 ids after
-// the last valid row (padding, skipped), so the plan's ranking only scans real pairs.
+// the last valid row (padding), and their count in *n_valid, so the plan reads only the
+// rows that arrived.
 __global__ void k_ep_ids(const uint8_t *own, EpLayout L, int32_t *__restrict__ ids,
-                         int32_t *__restrict__ rowmap) {
+                         int32_t *__restrict__ rowmap, int *__restrict__ n_valid) {
   const int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (j >= L.ws * L.C) return;
   const int32_t *cnt = reinterpret_cast<const int32_t *>(own + L.cnt);
+  if (j == 0) *n_valid = ep_rows_before(own, L, L.ws);     // every received row
+  if (j >= L.ws * L.C) return;
   int64_t before = 0;
   for (int s = 0; s < L.ws; ++s) {
     const int n = cnt[s];

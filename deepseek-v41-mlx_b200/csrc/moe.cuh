@@ -31,9 +31,13 @@ constexpr int MOE_DN_CHUNK = 4;
 // expert.  Offsets come from block-wide exclusive scans over the experts.
 // tok_map (optional): the activation row of pair p's token, instead of p / topk (expert-
 // parallel owners list their received rows compactly, valid rows first).
+// n_valid (optional): the pairs past this count are padding (-1) and are not read -- an
+// expert-parallel owner lists its received rows first in a buffer sized for the most it
+// can receive, so the plan's work follows the rows that arrived.
 __global__ void __launch_bounds__(1024) k_moe_plan(const int32_t *__restrict__ indices, int64_t T,
                                                    int topk, int64_t E, MoePlan plan,
-                                                   const int32_t *__restrict__ tok_map) {
+                                                   const int32_t *__restrict__ tok_map,
+                                                   const int *__restrict__ n_valid) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ int sh[];
@@ -42,7 +46,11 @@ __global__ void __launch_bounds__(1024) k_moe_plan(const int32_t *__restrict__ i
   int *coff = sh + 2 * E;   // [E] gate/up chunk offset
   int *doff = sh + 3 * E;   // [E] down chunk offset
   __shared__ int wtot[3][32];
-  const int64_t P = T * topk;
+  int64_t P = T * topk;
+  if (n_valid) {
+    const int64_t nv = *n_valid;
+    P = nv < P ? (nv > 0 ? nv : 0) : P;
+  }
   const int e = threadIdx.x, lane = e & 31, wid = e >> 5;
   if (e < E) cnt[e] = 0;
   __syncthreads();

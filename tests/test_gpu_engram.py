@@ -92,6 +92,36 @@ def test_gather_rows_golden(cuda):
     assert bits_equal(got, g["out"])
 
 
+@pytest.mark.parametrize("d,block", [(256, 32), (1024, 1024), (512, 64), (1024, 32)])
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_gather_sum_every_scale_and_code(cuda, d, block, dtype):
+    """Every ue8m0 byte (0 .. 255: subnormal to infinite scales, where products overflow) and
+    every e4m3 code (NaN included), plain and packed rows: the bits of the oracle's rounded
+    product then rounded sum, NaN for NaN."""
+    rng = np.random.default_rng(7 * d + block)
+    rows = 3000
+    table = rng.integers(0, 256, size=(rows, d), dtype=np.uint8)
+    scale = rng.integers(0, 256, size=(rows, d // block), dtype=np.uint8)
+    idx = rng.integers(0, rows, size=(29, 24))
+    tdt = torch.float32 if dtype == "f32" else torch.bfloat16
+    want = OE.gather_sum(table, scale, idx, block, dtype)
+    for packed in (False, True):
+        emb = q.engram.EngramEmbedding(rows, d, block)
+        emb.weight, emb.scale = _d(table), _d(scale)
+        if packed:
+            emb.pack()
+        got = emb.gather_sum(_d(idx), tdt)
+        got = got.cpu().numpy() if dtype == "f32" else got.view(torch.int16).cpu().numpy().view(np.uint16)
+        if dtype == "bf16":              # any NaN pattern is NaN
+            nan_w = (want & 0x7F80) == 0x7F80
+            nan_w &= (want & 0x7F) != 0
+            nan_g = ((got & 0x7F80) == 0x7F80) & ((got & 0x7F) != 0)
+            assert np.array_equal(nan_w, nan_g), packed
+            assert np.array_equal(np.where(nan_w, 0, want), np.where(nan_g, 0, got)), packed
+        else:
+            assert bits_equal(got, want), packed
+
+
 @pytest.mark.parametrize("d,block", [(256, 32), (1024, 1024), (512, 64)])
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
 def test_gather_sum(cuda, d, block, dtype):
