@@ -627,12 +627,39 @@ struct MoeDims {
   int64_t T, D, I, E, P, Pmax, Cmax, Tp, tiles_gu, tiles_dn;
   // what the launches use: K-split counts (routed / shared gate/up and down, router), the
   // row-pair down projection and its tiles; split-K partials are carved only where a count
-  // exceeds 1
+  // exceeds 1; the routed kernels' n8 activation tiles per chunk (gu_nt, dn_nt: 1, 2 or 4)
   int ns_gu, ns_dn, ns_sgu, ns_sdn, nks, rowpair;
   int64_t tiles_dnx;
+  int gu_nt, dn_nt;
 };
 
-MoeDims moe_dims(const dsv41_moe_config *c, int64_t T) {
+// n8 tiles per routed chunk for `n` expected pairs of one expert: a chunk of 8 * nt (gate/up)
+// or 4 * nt (down: hi/lo halves) pairs; every further chunk of an expert streams its weights
+// again.  DSV41_MOE_CHUNK_NT="g,d" fixes both (tuning).
+int chunk_nt(double n, int base) { return n <= base ? 1 : (n <= 2 * base ? 2 : 4); }
+
+void moe_chunk_override(int &gu, int &dn) {
+  static int g = -1, dd = -1;
+  if (g < 0) {
+    g = dd = 0;
+    const char *e = getenv("DSV41_MOE_CHUNK_NT");
+    int a = 0, b = 0;
+    if (e && sscanf(e, "%d,%d", &a, &b) == 2 && (a == 1 || a == 2 || a == 4) &&
+        (b == 1 || b == 2 || b == 4)) {
+      g = a;
+      dd = b;
+    }
+  }
+  if (g) {
+    gu = g;
+    dn = dd;
+  }
+}
+
+// expect: pairs an active expert is expected to receive (<= 0: the batch's own average,
+// P over the active experts; an expert-parallel owner passes its estimate, since it is sized
+// for the most rows it can receive)
+MoeDims moe_dims(const dsv41_moe_config *c, int64_t T, double expect = -1.0) {
   MoeDims d;
   d.T = T;
   d.D = c->dim;
@@ -640,8 +667,15 @@ MoeDims moe_dims(const dsv41_moe_config *c, int64_t T) {
   d.E = c->n_experts;
   d.P = T * c->topk;
   const int64_t act = d.P < d.E ? d.P : d.E;
+  // chunks wide enough for 1.5x the expected pairs of an expert, so that most experts stream
+  // their weights once
+  const double avg = expect > 0 ? expect : double(d.P) / double(act > 0 ? act : 1);
+  d.gu_nt = chunk_nt(1.5 * avg, 8);
+  d.dn_nt = chunk_nt(1.5 * avg, 4);
+  moe_chunk_override(d.gu_nt, d.dn_nt);
   d.Pmax = d.P + 3 * act;
-  d.Cmax = ceil_div(d.P, MOE_DN_CHUNK) + act;   // the down list is the longer one
+  const int64_t c_gu = ceil_div(d.P, 8 * d.gu_nt), c_dn = ceil_div(d.P, 4 * d.dn_nt);
+  d.Cmax = (c_gu > c_dn ? c_gu : c_dn) + act;
   d.Tp = ceil_div(T, 4) * 4;
   d.tiles_gu = ceil_div(d.I, QG_ROWS);
   d.tiles_dn = ceil_div(d.D, QG_ROWS);
@@ -693,8 +727,8 @@ MoeWs moe_carve(const MoeDims &d, void *base, size_t cap) {
   auto parts = [&](int64_t tiles, int ns, size_t floats) -> size_t {
     return ns > 1 ? size_t(tiles) * size_t(ns) * ct * floats : 0;
   };
-  w.part_gu = wc.take<float>(parts(d.Cmax * d.tiles_gu, d.ns_gu, 8));
-  w.part_dn = wc.take<float>(parts(d.Cmax * d.tiles_dnx, d.ns_dn, 8));
+  w.part_gu = wc.take<float>(parts(d.Cmax * d.tiles_gu, d.ns_gu, 8 * d.gu_nt));
+  w.part_dn = wc.take<float>(parts(d.Cmax * d.tiles_dnx, d.ns_dn, 8 * d.dn_nt));
   w.part_sgu = wc.take<float>(parts(ceil_div(d.T, 8) * d.tiles_gu, d.ns_sgu, 32));
   w.part_sdn = wc.take<float>(parts(ceil_div(d.T, 4) * d.tiles_dn, d.ns_sdn, 16));
   w.cnt_gu = wc.take<int>(d.Cmax * d.tiles_gu);
@@ -779,7 +813,7 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
   { ProfScope prof("moe_plan", st);
   DSV41_LAUNCH(launch_pdl(k_moe_plan, dim3(1), dim3(1024), 4 * d.E * sizeof(int), st,
                           static_cast<const int32_t *>(idx), T, cfg->topk, d.E, ws.plan, tok_map,
-                          n_valid),
+                          n_valid, 8 * d.gu_nt, 4 * d.dn_nt),
                "moe_plan"); }
   DSV41_CHECK_LAUNCH("moe_plan");
   // activations gathered per pair
@@ -826,8 +860,16 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
       cudaError_t e = cudaMemsetAsync(ws.cnt_gu, 0, sizeof(int) * d.Cmax * d.tiles_gu, st);
       if (e != cudaSuccess) return cuda_status(e, "memset");
     }
-    rc = qgemv_launch<WF_FP4, 2, 1>("moe_expert_gate_up_fp4", m_w1, m_w3, xg[0], xg[1], xg[2], p,
-                                     int(d.Cmax * d.tiles_gu * p.nsplit), st);
+    const int items = int(d.Cmax * d.tiles_gu * p.nsplit);
+    if (d.gu_nt == 1)
+      rc = qgemv_launch<WF_FP4, 2, 1>("moe_expert_gate_up_fp4", m_w1, m_w3, xg[0], xg[1], xg[2], p,
+                                       items, st);
+    else if (d.gu_nt == 2)
+      rc = qgemv_launch<WF_FP4, 2, 2>("moe_expert_gate_up_fp4", m_w1, m_w3, xg[0], xg[1], xg[2], p,
+                                       items, st);
+    else
+      rc = qgemv_launch<WF_FP4, 2, 4>("moe_expert_gate_up_fp4", m_w1, m_w3, xg[0], xg[1], xg[2], p,
+                                       items, st);
     if (rc) return rc;
   }
   {  // routed down -> Y[t*k + j]
@@ -857,12 +899,28 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
       cudaError_t e = cudaMemsetAsync(ws.cnt_dn, 0, sizeof(int) * d.Cmax * d.tiles_dn, st);
       if (e != cudaSuccess) return cuda_status(e, "memset");
     }
-    if (p.rowpair)
-      rc = qgemv_launch<WF_FP4, 2, 1>("moe_expert_down_fp4_pairs", m_w2, m_w2, hx[0], hx[1], hx[2], p,
-                                       int(d.Cmax * p.tiles * p.nsplit), st);
-    else
-      rc = qgemv_launch<WF_FP4, 1, 1>("moe_expert_down_fp4", m_w2, m_w2, hx[0], hx[1], hx[2], p,
-                                       int(d.Cmax * d.tiles_dn * p.nsplit), st);
+    const int items = int(d.Cmax * p.tiles * p.nsplit);
+    if (p.rowpair) {
+      if (d.dn_nt == 1)
+        rc = qgemv_launch<WF_FP4, 2, 1>("moe_expert_down_fp4_pairs", m_w2, m_w2, hx[0], hx[1],
+                                         hx[2], p, items, st);
+      else if (d.dn_nt == 2)
+        rc = qgemv_launch<WF_FP4, 2, 2>("moe_expert_down_fp4_pairs", m_w2, m_w2, hx[0], hx[1],
+                                         hx[2], p, items, st);
+      else
+        rc = qgemv_launch<WF_FP4, 2, 4>("moe_expert_down_fp4_pairs", m_w2, m_w2, hx[0], hx[1],
+                                         hx[2], p, items, st);
+    } else {
+      if (d.dn_nt == 1)
+        rc = qgemv_launch<WF_FP4, 1, 1>("moe_expert_down_fp4", m_w2, m_w2, hx[0], hx[1], hx[2], p,
+                                         items, st);
+      else if (d.dn_nt == 2)
+        rc = qgemv_launch<WF_FP4, 1, 2>("moe_expert_down_fp4", m_w2, m_w2, hx[0], hx[1], hx[2], p,
+                                         items, st);
+      else
+        rc = qgemv_launch<WF_FP4, 1, 4>("moe_expert_down_fp4", m_w2, m_w2, hx[0], hx[1], hx[2], p,
+                                         items, st);
+    }
     if (rc) return rc;
   }
   }  // routed
@@ -1140,16 +1198,20 @@ extern "C" int dsv41_ep_destroy(dsv41_ep_ctx *c) {
 
 namespace {
 
-// The owner runs its experts on ws*C received rows (padding rows skipped), one pair each.
-MoeDims ep_owner_dims_decode(const dsv41_moe_config *cfg, const dsv41_ep_ctx *c) {
+// The owner runs its experts on ws*C received rows (padding rows skipped), one pair each;
+// every rank is taken to route about as many pairs as this one (T * topk), spread over the
+// owner's experts, for the chunk width.
+MoeDims ep_owner_dims_decode(const dsv41_moe_config *cfg, const dsv41_ep_ctx *c, int64_t T) {
   dsv41_moe_config lc = *cfg;
   lc.n_experts = cfg->n_experts / c->world;
   lc.topk = 1;
-  return moe_dims(&lc, int64_t(c->world) * c->L.C);
+  const double pairs = double(T < 1 ? 1 : T) * cfg->topk;
+  const double act = pairs < double(lc.n_experts) ? pairs : double(lc.n_experts);
+  return moe_dims(&lc, int64_t(c->world) * c->L.C, pairs / act);
 }
 
 size_t ep_decode_ws_bytes(const dsv41_moe_config *cfg, const dsv41_ep_ctx *c, int64_t T) {
-  const MoeDims dl = moe_dims(cfg, T < 1 ? 1 : T), dw = ep_owner_dims_decode(cfg, c);
+  const MoeDims dl = moe_dims(cfg, T < 1 ? 1 : T), dw = ep_owner_dims_decode(cfg, c, T);
   const size_t a = moe_carve(dl, nullptr, ~size_t(0)).used;
   const size_t b = moe_carve(dw, nullptr, ~size_t(0)).used;
   return align_up(a, 256) + align_up(b, 256) + 2 * align_up(size_t(dw.T) * 4, 256) +
@@ -1193,7 +1255,7 @@ extern "C" int dsv41_moe_ep_decode(const dsv41_moe_config *cfg, const dsv41_moe_
   DSV41_REQUIRE(workspace && workspace_bytes >= need, DSV41_ERR_WORKSPACE,
                 "workspace too small: need %zu bytes", need);
   cudaStream_t st = STREAM(stream);
-  const MoeDims dl = moe_dims(cfg, T < 1 ? 1 : T), dw = ep_owner_dims_decode(cfg, c);
+  const MoeDims dl = moe_dims(cfg, T < 1 ? 1 : T), dw = ep_owner_dims_decode(cfg, c, T);
   WsCarve wc{static_cast<uint8_t *>(workspace), workspace_bytes, 0};
   uint8_t *ws_loc = wc.take<uint8_t>(moe_carve(dl, nullptr, ~size_t(0)).used);
   uint8_t *ws_own = wc.take<uint8_t>(moe_carve(dw, nullptr, ~size_t(0)).used);

@@ -21,10 +21,9 @@ struct MoePlan {
   int *counts;          // [0] n_gu, [1] n_dn, [2] n_pairs_padded, [3] n_sgu, [4] n_sdn
 };
 
-// Pairs per chunk: one n8 tile of activation rows for gate/up (8 pairs), and for
-// down 8 H rows = 4 pairs (hi/lo halves).  Experts with more pairs get more chunks.
-constexpr int MOE_GU_CHUNK = 8;
-constexpr int MOE_DN_CHUNK = 4;
+// Pairs per chunk: gu_chunk = 8 * nt for gate/up (nt n8 tiles of activation rows) and
+// dn_chunk = 4 * nt for down (8 H rows = 4 pairs an n8 tile, hi/lo halves), nt = 1, 2 or 4
+// chosen per launch.  Experts with more pairs get more chunks.
 
 // One CTA of 1024 threads (E <= 1024).  Deterministic: a pair's rank inside its
 // expert is the number of earlier pairs (row-major over [T, k]) routed to the same
@@ -37,7 +36,8 @@ constexpr int MOE_DN_CHUNK = 4;
 __global__ void __launch_bounds__(1024) k_moe_plan(const int32_t *__restrict__ indices, int64_t T,
                                                    int topk, int64_t E, MoePlan plan,
                                                    const int32_t *__restrict__ tok_map,
-                                                   const int *__restrict__ n_valid) {
+                                                   const int *__restrict__ n_valid, int gu_chunk,
+                                                   int dn_chunk) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ int sh[];
@@ -61,8 +61,7 @@ __global__ void __launch_bounds__(1024) k_moe_plan(const int32_t *__restrict__ i
   }
   __syncthreads();
   const int n = e < E ? cnt[e] : 0;
-  int v[3] = {(n + 3) & ~3, (n + MOE_GU_CHUNK - 1) / MOE_GU_CHUNK,
-              (n + MOE_DN_CHUNK - 1) / MOE_DN_CHUNK};
+  int v[3] = {(n + 3) & ~3, (n + gu_chunk - 1) / gu_chunk, (n + dn_chunk - 1) / dn_chunk};
   int inc[3] = {v[0], v[1], v[2]};
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -107,14 +106,14 @@ __global__ void __launch_bounds__(1024) k_moe_plan(const int32_t *__restrict__ i
   __syncthreads();
   // chunks and padding slots, one thread per expert
   if (e < E && n > 0) {
-    for (int c = 0; c * MOE_GU_CHUNK < n; ++c) {
-      const int q0 = poff[e] + c * MOE_GU_CHUNK;
-      const int np = min(MOE_GU_CHUNK, n - c * MOE_GU_CHUNK);
+    for (int c = 0; c * gu_chunk < n; ++c) {
+      const int q0 = poff[e] + c * gu_chunk;
+      const int np = min(gu_chunk, n - c * gu_chunk);
       plan.gu_chunks[coff[e] + c] = QChunk{e, q0, np, q0};
     }
-    for (int c = 0; c * MOE_DN_CHUNK < n; ++c) {
-      const int q0 = poff[e] + c * MOE_DN_CHUNK;   // multiple of 4: H rows 2*q0 ..
-      const int np = min(MOE_DN_CHUNK, n - c * MOE_DN_CHUNK);
+    for (int c = 0; c * dn_chunk < n; ++c) {
+      const int q0 = poff[e] + c * dn_chunk;       // multiple of 4: H rows 2*q0 ..
+      const int np = min(dn_chunk, n - c * dn_chunk);
       plan.dn_chunks[doff[e] + c] = QChunk{e, 2 * q0, 8 * ((np + 3) / 4), q0};
     }
     for (int q = poff[e] + n; q < poff[e] + ((n + 3) & ~3); ++q) {
