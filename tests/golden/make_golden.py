@@ -1,9 +1,9 @@
 """Generate the golden fixtures in this directory from the reference's own CPU code.
 
-Run here, where the reference checkout is mounted (default /root/reference, or
-$DSV41_REFERENCE):
+Run where a checkout of the reference repository is available, naming its root in
+$DSV41_REFERENCE:
 
-    python tests/golden/make_golden.py
+    DSV41_REFERENCE=<path to the reference checkout> python tests/golden/make_golden.py
 
 What each fixture pins (all from code that ships in the reference repo and
 runs without MLX):
@@ -43,7 +43,7 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("DSV41_REFERENCE", "/root/reference")
+REF = os.environ.get("DSV41_REFERENCE", "")
 
 
 def _setup_imports():
@@ -313,6 +313,8 @@ def golden_engram_gate():
 
 
 def main():
+    if not REF or not os.path.isdir(os.path.join(REF, "deepseek_v41_mlx")):
+        sys.exit("set DSV41_REFERENCE to the root of a checkout of the reference repository")
     torch.set_default_dtype(torch.float32)
     ks = _setup_imports()
     golden_dequant()
