@@ -1291,7 +1291,9 @@ extern "C" int dsv41_moe_ep_decode(const dsv41_moe_config *cfg, const dsv41_moe_
   const int P = int(T * cfg->topk);
   {
     ProfScope prof("ep_dispatch", st);
-    const unsigned nb = unsigned(std::max<int64_t>(1, std::min<int64_t>(16, ceil_div(P, c->world))));
+    // up to 64 CTAs an owner, two rows each: enough stores in flight to keep NVLink busy
+    const unsigned nb =
+        unsigned(std::max<int64_t>(1, std::min<int64_t>(64, ceil_div(P, 2 * c->world))));
     k_ep_dispatch<<<dim3(c->world, nb), 256, P * sizeof(int), st>>>(
         static_cast<const __nv_bfloat16 *>(x), idx, int(T), cfg->topk, epr, c->rank, L, c->peers,
         c->dseq, slot_pos, c->done);
@@ -1315,7 +1317,10 @@ extern "C" int dsv41_moe_ep_decode(const dsv41_moe_config *cfg, const dsv41_moe_
   if (rc) return rc;
   {
     ProfScope prof("ep_return", st);
-    const unsigned nb = unsigned(std::max<int64_t>(1, std::min<int64_t>(16, ceil_div(L.C, 4))));
+    // the rows each source sent are known only on the device: as many CTAs as the expected
+    // rows (this rank's own pair count spread over the sources) need at two rows each
+    const unsigned nb = unsigned(
+        std::max<int64_t>(1, std::min<int64_t>(64, ceil_div(T * cfg->topk, 2 * c->world))));
     k_ep_return<<<dim3(c->world, nb), 256, 0, st>>>(Yr, c->buf, c->rank, L, c->peers, c->dseq,
                                                      c->done + c->world);
     DSV41_CHECK_LAUNCH("ep_return");
