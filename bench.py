@@ -678,9 +678,18 @@ def run_ours(args):
         del steps
     q._lib.prof_select(None)
     q._lib.prof_enable(False)
-    # per-kernel breakdown (every kernel bracketed by events): a separate, untimed pass
+    # per-kernel breakdown (every kernel bracketed by events): a separate, untimed pass; at
+    # N > 1 a barrier before each step, so that the waits on peers' flags measure the
+    # exchange and not the ranks' skew in starting the step
     q._lib.prof_enable(True)
-    timed_steps(torch, lambda i: fwd(xs[i % len(xs)]), max(3, K // 4), 0, flush, stream)
+    if world > 1:
+        def kstep(i):
+            torch.cuda.synchronize()
+            dist.barrier()
+            fwd(xs[i % len(xs)])
+    else:
+        kstep = lambda i: fwd(xs[i % len(xs)])
+    timed_steps(torch, kstep, max(3, K // 4), 0, flush, stream)
     kprof = q._lib.prof_report()
     q._lib.prof_enable(False)
     step_ms = sum(ms) / len(ms)

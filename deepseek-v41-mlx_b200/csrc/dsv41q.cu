@@ -481,6 +481,14 @@ int gemv_common(const void *x, int64_t M, int64_t K, const void *w, int64_t w_ro
   p.tiles = int(tiles);
   p.kstages = int(ceil_div(K, KS));
   p.nsplit = pick_nsplit(tiles * nch, p.kstages);
+  {  // tuning: DSV41_GEMV_MAX_SPLIT caps the K splits (never above the workspace's sizing)
+    static int cap = -1;
+    if (cap < 0) {
+      const char *e = getenv("DSV41_GEMV_MAX_SPLIT");
+      cap = e ? atoi(e) : 0;
+    }
+    if (cap > 0 && p.nsplit > cap) p.nsplit = cap;
+  }
   p.xscale = ws.xscale;
   p.xsum = ws.xsum;
   p.chunks = nullptr;
