@@ -427,6 +427,60 @@ def prefill_measurement(q, torch, dev, layer, flush, stream, peaks, K, W, T=PREF
     return r
 
 
+A16_ROUTED = ("a16_gate_up_fp4", "a16_down_fp4")
+
+
+def prefill_a16_measurement(q, torch, dev, layer, flush, stream, peaks, K, W, T=PREFILL_T,
+                            e2e=True):
+    """d3 in the port's numerics (MoE.prefill_a16): bf16 activations x exactly decoded
+    weights on kind::f16 tensor cores, the routed down projection on the fp32 SwiGLU output as
+    bf16 hi + lo (two MMAs a K step), so the routed GEMMs execute 4/3 of the layer's 4.33
+    TFLOP; measured against the bf16 peak with the model's FLOPs."""
+    hbm_peak, bf16_peak, peak_src = peaks
+    g = torch.Generator(device=dev).manual_seed(4321)
+    x = torch.randn(T, D, device=dev, generator=g).to(torch.bfloat16)
+    w, idx = zipf_routing(torch, dev, x, layer.gate.weight, T)
+    counts = torch.bincount(idx.reshape(-1).long(), minlength=E)
+    fn = lambda i: layer.prefill_a16(x, weights=w, indices=idx)
+    st = statistics.median(timed_steps(torch, fn, K, W, flush, stream))
+    kt = kernel_ms(q, torch, fn, [], max(3, K // 2), flush, stream)
+    f_routed = 2.0 * T * TOPK * 3 * I * D
+    f_shared = 2.0 * 3 * T * I * D
+    kern = {k: round(v[1] * v[0], 4) for k, v in kt.items()}
+    routed_ms = sum(kern.get(k, 0.0) for k in A16_ROUTED)
+    active = int((counts > 0).sum())
+    wbytes = active * BYTES_PER_EXPERT
+    floor_ms = max(f_routed / (bf16_peak * 1e12), wbytes / (hbm_peak * 1e9)) * 1e3
+    r = {
+        "config": "BASELINE.json configs[2] in the port's numerics (deepseek_v41_mlx/moe.py): T=8192 "
+                  "bf16 N(0,1), Zipf(1.1) top-6 routing, fp4 experts 384 x [2048 x 7168], bf16 "
+                  "activations (no act_quant), gate/up rounded to bf16",
+        "metric": "MoE-layer prefill tok/s (port numerics)", "unit": "tok/s",
+        "value": round(T / (st / 1e3), 1), "ms": round(st, 4), "tokens": T,
+        "tflops_layer": round((f_routed + f_shared) / (st / 1e3) / 1e12, 1),
+        "routed_gemm_ms": round(routed_ms, 4),
+        "routed_gemm_tflops": round(f_routed / (routed_ms / 1e3) / 1e12, 1) if routed_ms else None,
+        "routed_executed_tflops": round(f_routed * 4 / 3 / (routed_ms / 1e3) / 1e12, 1)
+        if routed_ms else None,
+        "routed_roofline_ms": round(floor_ms, 4),
+        "routed_frac_of_roofline": round(floor_ms / routed_ms, 4) if routed_ms else None,
+        "kernel_ms": kern, "experts_active": active,
+        "roofline": _roofline("tensor", "routed a16 GEMMs (k_a16gemm: gate/up + down, wide and "
+                              "narrow tile lists)", f_routed, routed_ms, bf16_peak,
+                              peak_src + " bf16_tflops (cuBLAS burst)"),
+    }
+    if e2e:
+        xh = [[x.cpu().pin_memory(), w.cpu().pin_memory(), idx.cpu().pin_memory()]]
+        xd, wd, idd = torch.empty_like(x), torch.empty_like(w), torch.empty_like(idx)
+        yh = torch.empty((T, D), dtype=torch.bfloat16).pin_memory()
+        e_ms, bi, bo = e2e_measure(torch, lambda i: layer.prefill_a16(xd, weights=wd, indices=idd),
+                                   xh, [xd, wd, idd], yh, max(3, K // 2), W, flush, stream)
+        r["e2e"] = {"value": round(T / (e_ms / 1e3), 1), "unit": "tok/s", "ms": round(e_ms, 4),
+                    "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo,
+                    "api": "moe.MoE.prefill_a16(x, weights, indices)"}
+    return r
+
+
 # ---------------------------------------------------------------- d4: MLX affine --
 
 def d4_measure(q, torch, dev, flush, stream, K, W, peaks):
@@ -768,6 +822,8 @@ def run_ours(args):
         sub.update(d4_measure(q, torch, dev, flush, stream, Ks, W, peaks))
         sub["moe_prefill_T8192_a8"] = prefill_measurement(
             q, torch, dev, layer, flush, stream, peaks, max(3, K // 4), W)
+        sub["moe_prefill_T8192_a16"] = prefill_a16_measurement(
+            q, torch, dev, layer, flush, stream, peaks, max(3, K // 4), W)
         layer = fwd = e2e_step = None          # the 99.8 GB engram table comes next
         torch.cuda.empty_cache()
         sub.update(engram_measurement(q, torch, dev, flush, stream, Ks, W, peaks=peaks))
@@ -1085,10 +1141,10 @@ def run_prefill_only(args):
     dev = torch.device("cuda", 0)
     layer = make_moe(q, torch, dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    fn = prefill_a16_measurement if args.prefill_a16 else prefill_measurement
     with Clocks(0) as clk:
-        r = prefill_measurement(q, torch, dev, layer, flush, torch.cuda.current_stream(),
-                                _peaks(), args.steps, args.warmup, T=args.prefill_tokens,
-                                e2e=False)
+        r = fn(q, torch, dev, layer, flush, torch.cuda.current_stream(), _peaks(), args.steps,
+               args.warmup, T=args.prefill_tokens, e2e=False)
     r["clocks"] = clk.summary()
     print(json.dumps(r))
 
@@ -1295,8 +1351,14 @@ def cpu_sub_baselines(sub, seconds):
                                                    f"matmul ({t:.2f} s)")
     # d3: prefill in a8 numerics; a sample of experts timed, scaled (stated)
     if "moe_prefill_T8192_a8" in sub:
-        sub["moe_prefill_T8192_a8"]["cpu_baseline"] = dict(base, **cpu_prefill_estimate(
-            sub["moe_prefill_T8192_a8"], seconds))
+        est = cpu_prefill_estimate(sub["moe_prefill_T8192_a8"], seconds)
+        sub["moe_prefill_T8192_a8"]["cpu_baseline"] = dict(base, **est)
+        if "moe_prefill_T8192_a16" in sub:
+            # the port's CPU path has the same weight decode and the same products (bf16
+            # activations, no act_quant), so the sampled costs carry over
+            sub["moe_prefill_T8192_a16"]["cpu_baseline"] = dict(
+                base, **est, note="the a8 sample's decode and product costs (the port decodes "
+                                  "the same weights and multiplies the same shapes)")
     # d5: hash + gather + dequant + sum on a host table (the BASELINE table does not fit)
     for T in (1, PREFILL_T):
         key = f"engram_T{T}"
@@ -1445,6 +1507,8 @@ def main():
     ap.add_argument("--prefill-only", action="store_true",
                     help="only the T=8192 a8 prefill measurement (one JSON line)")
     ap.add_argument("--prefill-tokens", type=int, default=PREFILL_T)
+    ap.add_argument("--prefill-a16", action="store_true",
+                    help="with --prefill-only: the port's numerics (MoE.prefill_a16)")
     ap.add_argument("--affine-only", action="store_true",
                     help="only the affine (d4) measurements (one JSON line)")
     ap.add_argument("--gemv-only", action="store_true",

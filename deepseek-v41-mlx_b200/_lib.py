@@ -100,6 +100,9 @@ PROTOTYPES = {
     "dsv41_moe_prefill_workspace_size": (_SZ, [C.POINTER(MoeConfig), _I64, _I, _I]),
     "dsv41_moe_prefill": (_I, [C.POINTER(MoeConfig), C.POINTER(MoeWeights), _P, _P, _I64, _P, _P,
                                _I, _P, _P, _SZ, _P]),
+    "dsv41_moe_prefill_a16_workspace_size": (_SZ, [C.POINTER(MoeConfig), _I64, _I]),
+    "dsv41_moe_prefill_a16": (_I, [C.POINTER(MoeConfig), C.POINTER(MoeWeights), _P, _I64, _P,
+                                   _P, _I, _P, _P, _SZ, _P]),
     "dsv41_moe_ep_row_bytes": (_SZ, [_I64]),
     "dsv41_moe_ep_pack_workspace_size": (_SZ, [C.POINTER(MoeConfig), _I64]),
     "dsv41_moe_ep_pack": (_I, [C.POINTER(MoeConfig), _P, _I64, _P, _P, _I, _P, _P, _P, _P, _SZ,

@@ -12,6 +12,7 @@
 #include "ep_decode.cuh"
 #include "quantize.cuh"
 #include "aqgemm.cuh"
+#include "a16gemm.cuh"
 
 #include <mutex>
 
@@ -1993,6 +1994,286 @@ PfDims ep_owner_dims(const dsv41_moe_config *cfg, int64_t R) {
   return pf_dims(&c, R);
 }
 }  // namespace
+
+// ======================================================================= prefill, port numerics
+//
+// The MoE layer at prefill sizes as the port computes it (deepseek_v41_mlx/moe.py:101-112):
+// bf16 activations times the exactly decoded weights on kind::f16 tensor cores (a16gemm.cuh),
+// expert outputs weighted and summed in top-k order after the down projection.
+namespace {
+
+struct A16Ws {
+  float *w;
+  int32_t *idx;
+  float *rpart;
+  __nv_bfloat16 *xg, *hhi, *hlo, *shi, *slo;
+  float *Y, *Ys;
+  int *chunk_cnt;
+  PfPlan plan;
+};
+
+size_t a16_carve(const PfDims &d, bool route, bool routed, bool shared, bool round, uint8_t *base,
+                 size_t cap, A16Ws *ws) {
+  WsCarve c{base, cap, 0};
+  A16Ws w;
+  memset(&w, 0, sizeof(w));
+  if (route) {
+    w.w = c.take<float>(d.P);
+    w.idx = c.take<int32_t>(d.P);
+    w.rpart = c.take<float>(dsv41_moe_route_workspace_size(d.T, d.D, d.E) / sizeof(float));
+  }
+  if (routed) {
+    w.xg = c.take<__nv_bfloat16>(d.P * d.D);
+    w.hhi = c.take<__nv_bfloat16>(d.P * d.I);
+    w.hlo = c.take<__nv_bfloat16>(d.P * d.I);     // the down projection takes the fp32 h
+    w.Y = c.take<float>(d.P * d.D);
+    w.chunk_cnt = c.take<int>(d.nchunks * d.E);
+    w.plan.chunk_base = w.chunk_cnt;
+    w.plan.grp_off = c.take<int>(d.E);
+    w.plan.grp_rt0 = c.take<int>(d.E);
+    w.plan.pair_tok = c.take<int>(d.P);
+    w.plan.pair_w = c.take<float>(d.P);
+    w.plan.slot_pos = c.take<int>(d.P);
+    w.plan.row_tile = c.take<int>(d.P);
+    const int64_t mts[2] = {d.I / 64, d.D / BS_BM};
+    for (int pj = 0; pj < 2; ++pj) {
+      w.plan.tiles[2 * pj] = c.take<int4>(mts[pj] * d.cap_w);
+      w.plan.tiles[2 * pj + 1] = c.take<int4>(mts[pj] * d.cap_n);
+    }
+    w.plan.ntiles = c.take<int>(4);
+    w.plan.next_tile = c.take<int>(4);
+  }
+  if (shared) {
+    w.shi = c.take<__nv_bfloat16>(d.T * d.I);
+    if (!round) w.slo = c.take<__nv_bfloat16>(d.T * d.I);
+    w.Ys = c.take<float>(d.T * d.D);
+  }
+  if (ws) *ws = w;
+  return c.off + 256;
+}
+
+// codes as bytes [rows, K * bits / 8], box {64 codes, box_rows}, no swizzle
+int a16_wmap(CUtensorMap *m, const uint8_t *w, int wfmt, int64_t rows, int64_t K, uint32_t box_rows) {
+  const uint64_t rb = wfmt == BS_W_FP4 ? uint64_t(K / 2) : uint64_t(K);
+  return make_tmap_2d(m, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, rb, uint64_t(rows), rb,
+                      wfmt == BS_W_FP4 ? 32u : 64u, box_rows, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+// bf16 rows [rows, K], box {64, 32 / 64 / 128 / 224 rows}, 128-byte swizzle
+int a16_xmaps(CUtensorMap (&m)[4], const void *x, int64_t rows, int64_t K) {
+  for (int i = 0; i < 4; ++i) {
+    int rc = make_tmap_2d(&m[i], x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, uint64_t(K),
+                          uint64_t(rows < 1 ? 1 : rows), uint64_t(K) * 2, 64, bs_box_rows(i));
+    if (rc) return rc;
+  }
+  return DSV41_OK;
+}
+
+template <int WFMT, int EPI, bool HILO>
+int a16_launch(const char *name, const A16Maps &maps, const A16Args &a, int grid, cudaStream_t st) {
+  using Cfg = A16Cfg<WFMT, HILO>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(k_a16gemm<WFMT, EPI, HILO>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+    if (e != cudaSuccess) return cuda_status(e, "a16 smem attribute");
+    attr_set[dev] = true;
+  }
+  ProfScope prof(name, st);
+  k_a16gemm<WFMT, EPI, HILO><<<unsigned(grid < 1 ? 1 : grid), A16_THREADS, Cfg::SMEM, st>>>(maps, a);
+  DSV41_CHECK_LAUNCH(name);
+  return DSV41_OK;
+}
+
+A16Args a16_dense(int64_t rows, int64_t mtiles) {
+  A16Args a;
+  memset(&a, 0, sizeof(a));
+  a.dense_nt = int(ceil_div(rows, A16_BN));
+  a.dense_rows = int(rows);
+  a.dense_tiles = int(mtiles) * a.dense_nt;
+  return a;
+}
+
+}  // namespace
+
+extern "C" size_t dsv41_moe_prefill_a16_workspace_size(const dsv41_moe_config *cfg, int64_t T,
+                                                       int with_routing) {
+  if (!cfg || T <= 0) return 256;
+  const bool shared = (cfg->flags & DSV41_MOE_NO_SHARED) == 0;
+  const bool routed = (cfg->flags & DSV41_MOE_SHARED_ONLY) == 0;
+  const bool round = (cfg->flags & DSV41_MOE_ROUND_BF16) != 0;
+  return a16_carve(pf_dims_for(cfg, T), routed && with_routing == 0, routed, shared, round,
+                   nullptr, ~size_t(0) >> 1, nullptr);
+}
+
+extern "C" int dsv41_moe_prefill_a16(const dsv41_moe_config *cfg, const dsv41_moe_weights *W,
+                                     const void *x, int64_t T, const float *route_weights,
+                                     const int32_t *route_indices, int out_dtype, void *y,
+                                     void *workspace, size_t workspace_bytes, void *stream) {
+  const bool shared = cfg && (cfg->flags & DSV41_MOE_NO_SHARED) == 0;
+  const bool routed = cfg && (cfg->flags & DSV41_MOE_SHARED_ONLY) == 0;
+  int rc = pf_check(cfg, W, T, shared, routed);
+  if (rc) return rc;
+  if (T == 0) return DSV41_OK;
+  DSV41_REQUIRE(out_dtype == DSV41_F32 || out_dtype == DSV41_BF16, DSV41_ERR_BAD_DTYPE,
+                "output must be F32 or BF16");
+  DSV41_REQUIRE(x && y && aligned(x, 16) && aligned(y, 16), DSV41_ERR_MISALIGNED,
+                "x and y must be 16-byte aligned");
+  DSV41_REQUIRE(T <= (int64_t(1) << 24), DSV41_ERR_UNSUPPORTED, "T above 2^24 tokens");
+  const bool round = (cfg->flags & DSV41_MOE_ROUND_BF16) != 0;
+  const bool route = routed && route_indices == nullptr;
+  DSV41_REQUIRE(!route || W->gate_w, DSV41_ERR_BAD_ARG, "NULL gate weight");
+  DSV41_REQUIRE(!routed || route || route_weights, DSV41_ERR_BAD_ARG,
+                "route_indices given without route_weights");
+  const PfDims d = pf_dims_for(cfg, T);
+  A16Ws ws;
+  const size_t need = a16_carve(d, route, routed, shared, round,
+                                reinterpret_cast<uint8_t *>(workspace), workspace_bytes, &ws);
+  DSV41_REQUIRE(workspace && workspace_bytes >= need, DSV41_ERR_WORKSPACE,
+                "workspace too small (%zu < %zu)", workspace_bytes, need);
+  cudaStream_t st = STREAM(stream);
+  const float *rw = route_weights;
+  const int32_t *ri = route_indices;
+  if (route) {
+    DSV41_REQUIRE(aligned(W->gate_w, 16), DSV41_ERR_MISALIGNED, "gate_w must be 16-byte aligned");
+    rc = route_impl(x, T, d.D, W->gate_w, W->gate_bias, d.E, d.k, cfg->score_func,
+                    cfg->gate_temp, cfg->norm_topk_prob, cfg->route_scale, ws.w, ws.idx, ws.rpart,
+                    st);
+    if (rc) return rc;
+    rw = ws.w;
+    ri = ws.idx;
+  }
+  const int sms = num_sms();
+  if (routed) {
+    {  // stable sort of the (token, slot) pairs by expert + tile lists, as the a8 prefill
+      ProfScope prof("a16_plan", st);
+      const size_t sm = size_t(16) * d.E * sizeof(int);
+      if (sm > 48 * 1024) {
+        cudaFuncSetAttribute(k_pf_count, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+        cudaFuncSetAttribute(k_pf_place, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+      }
+      k_pf_count<<<unsigned(d.nchunks), PF_CHUNK, sm, st>>>(ri, d.P, int(d.E), ws.chunk_cnt);
+      DSV41_CHECK_LAUNCH("a16 count");
+      k_pf_scan<<<1, 1024, 0, st>>>(ws.chunk_cnt, int(d.nchunks), int(d.E), int(d.I / 64),
+                                    int(d.D / BS_BM), ws.plan);
+      DSV41_CHECK_LAUNCH("a16 scan");
+      k_pf_place<<<unsigned(d.nchunks), PF_CHUNK, sm, st>>>(ri, rw, d.P, d.k, int(d.E), ws.plan);
+      DSV41_CHECK_LAUNCH("a16 place");
+    }
+    {
+      ProfScope prof("a16_gather", st);
+      k_a16_gather<<<unsigned(ceil_div(d.P * 32, 256)), 256, 0, st>>>(
+          static_cast<const __nv_bfloat16 *>(x), ws.plan.pair_tok, d.T, d.P, d.D, ws.xg);
+      DSV41_CHECK_LAUNCH("a16 gather");
+    }
+    // routed gate/up: SwiGLU -> h as bf16 hi + lo
+    A16Maps m1;
+    memset(&m1, 0, sizeof(m1));
+    rc = a16_wmap(&m1.w, W->w1, BS_W_FP4, d.E * d.I, d.D, 64);
+    if (!rc) rc = a16_wmap(&m1.w2, W->w3, BS_W_FP4, d.E * d.I, d.D, 64);
+    if (!rc) rc = a16_xmaps(m1.x, ws.xg, d.P, d.D);
+    if (rc) return rc;
+    A16Args a;
+    memset(&a, 0, sizeof(a));
+    a.nkb = int(d.D / A16_BK);
+    a.a_rows = int(d.I);
+    a.s = W->s1;
+    a.s2 = W->s3;
+    a.sld = d.D / 32;
+    a.hhi = ws.hhi;
+    a.hlo = ws.hlo;
+    a.ldh = d.I;
+    a.round_gu = round ? 1 : 0;
+    a.limit = cfg->swiglu_limit;
+    for (int list = 0; list < 2; ++list) {
+      a.tiles = ws.plan.tiles[list];
+      a.ntiles = ws.plan.ntiles + list;
+      rc = a16_launch<BS_W_FP4, A16_EPI_SWIGLU, false>("a16_gate_up_fp4", m1, a, sms, st);
+      if (rc) return rc;
+    }
+    // routed down (input h = hi + lo) -> Y fp32 per sorted pair
+    A16Maps m2;
+    memset(&m2, 0, sizeof(m2));
+    rc = a16_wmap(&m2.w, W->w2, BS_W_FP4, d.E * d.D, d.I, 128);
+    if (!rc) rc = a16_xmaps(m2.x, ws.hhi, d.P, d.I);
+    if (!rc) rc = a16_xmaps(m2.xlo, ws.hlo, d.P, d.I);
+    if (rc) return rc;
+    A16Args b;
+    memset(&b, 0, sizeof(b));
+    b.nkb = int(d.I / A16_BK);
+    b.a_rows = int(d.D);
+    b.s = W->s2;
+    b.sld = d.I / 32;
+    b.out = ws.Y;
+    b.ldo = d.D;
+    for (int list = 2; list < 4; ++list) {
+      b.tiles = ws.plan.tiles[list];
+      b.ntiles = ws.plan.ntiles + list;
+      rc = a16_launch<BS_W_FP4, A16_EPI_F32, true>("a16_down_fp4", m2, b, sms, st);
+      if (rc) return rc;
+    }
+  }
+  if (shared) {  // fp8 32x32 shared expert over all T rows (dense tiles)
+    A16Maps m1;
+    memset(&m1, 0, sizeof(m1));
+    rc = a16_wmap(&m1.w, W->sw1, BS_W_FP8, d.I, d.D, 64);
+    if (!rc) rc = a16_wmap(&m1.w2, W->sw3, BS_W_FP8, d.I, d.D, 64);
+    if (!rc) rc = a16_xmaps(m1.x, x, d.T, d.D);
+    if (rc) return rc;
+    A16Args a = a16_dense(d.T, d.I / 64);
+    a.nkb = int(d.D / A16_BK);
+    a.a_rows = int(d.I);
+    a.s = W->ss1;
+    a.s2 = W->ss3;
+    a.sld = ceil_div(d.D, 32);
+    a.sshift = 5;
+    a.hhi = ws.shi;
+    a.hlo = ws.slo;             // null in the port's numerics: h is rounded to bf16
+    a.ldh = d.I;
+    a.round_gu = round ? 1 : 0;
+    a.limit = cfg->swiglu_limit;
+    rc = a16_launch<BS_W_FP8, A16_EPI_SWIGLU, false>("a16_shared_gate_up_fp8", m1, a,
+                                                     std::min(sms, a.dense_tiles), st);
+    if (rc) return rc;
+    A16Maps m2;
+    memset(&m2, 0, sizeof(m2));
+    rc = a16_wmap(&m2.w, W->sw2, BS_W_FP8, d.D, d.I, 128);
+    if (!rc) rc = a16_xmaps(m2.x, ws.shi, d.T, d.I);
+    if (!rc && !round) rc = a16_xmaps(m2.xlo, ws.slo, d.T, d.I);
+    if (rc) return rc;
+    A16Args b = a16_dense(d.T, d.D / A16_BM);
+    b.nkb = int(d.I / A16_BK);
+    b.a_rows = int(d.D);
+    b.s = W->ss2;
+    b.sld = ceil_div(d.I, 32);
+    b.sshift = 5;
+    b.out = ws.Ys;
+    b.ldo = d.D;
+    b.round_out = round ? 1 : 0;
+    if (round)
+      rc = a16_launch<BS_W_FP8, A16_EPI_F32, false>("a16_shared_down_fp8", m2, b,
+                                                    std::min(sms, b.dense_tiles), st);
+    else
+      rc = a16_launch<BS_W_FP8, A16_EPI_F32, true>("a16_shared_down_fp8", m2, b,
+                                                   std::min(sms, b.dense_tiles), st);
+    if (rc) return rc;
+  }
+  {
+    const int64_t n = d.T * (d.D / 8);
+    ProfScope prof("a16_combine", st);
+    if (out_dtype == DSV41_F32)
+      k_a16_combine<float><<<unsigned(ceil_div(n, 256)), 256, 0, st>>>(
+          ws.Y, shared ? ws.Ys : nullptr, rw, routed ? ws.plan.slot_pos : nullptr, d.T,
+          routed ? d.k : 0, d.D, static_cast<float *>(y));
+    else
+      k_a16_combine<__nv_bfloat16><<<unsigned(ceil_div(n, 256)), 256, 0, st>>>(
+          ws.Y, shared ? ws.Ys : nullptr, rw, routed ? ws.plan.slot_pos : nullptr, d.T,
+          routed ? d.k : 0, d.D, static_cast<__nv_bfloat16 *>(y));
+    DSV41_CHECK_LAUNCH("a16 combine");
+  }
+  return DSV41_OK;
+}
 
 extern "C" size_t dsv41_moe_ep_row_bytes(int64_t dim) { return size_t(ep_row_bytes(dim)); }
 

@@ -358,6 +358,39 @@ class MoE:
                L.dtype_code(odt), L.ptr(y), L.ptr(ws), ws.numel(), L.stream_of(xf))
         return y.reshape(shape)
 
+    # -- prefill, the port's numerics ----------------------------------------
+    def prefill_a16(self, x, weights=None, indices=None, out_dtype=None, shared=True,
+                    routed=True):
+        """The layer at prefill sizes as the port computes it (moe.py:96-112): bf16
+        activations times the release's fp4 experts and fp8 shared expert decoded exactly to
+        bf16, on the tensor cores (``dsv41_moe_prefill_a16``); gate/up outputs and the shared
+        expert's intermediates rounded to bf16 when ``round_bf16`` (else fp32 throughout),
+        the down projection on the fp32 SwiGLU output, expert outputs weighted and summed in
+        top-k order.  Routing is computed by the router unless ``weights``/``indices``
+        [T, topk] are given; ``shared=False`` / ``routed=False`` leave one part out."""
+        t = _torch()
+        xt = L.cuda_tensor(x, "x")
+        shape = xt.shape
+        xf = xt.to(t.bfloat16).reshape(-1, self.dim).contiguous()
+        T = xf.shape[0]
+        odt = out_dtype or (t.float32 if xt.dtype == t.float32 else t.bfloat16)
+        se = self.shared_experts
+        has_shared = shared and se is not None and se.w1.weight is not None
+        flags = (0 if has_shared else L.MOE_NO_SHARED) | (0 if routed else L.MOE_SHARED_ONLY)
+        cfg = self._cfg(flags)
+        W = self._weights()
+        has_idx = indices is not None
+        if has_idx:
+            idx = L.cuda_tensor(indices, "indices").to(t.int32).reshape(T, -1).contiguous()
+            wts = L.cuda_tensor(weights, "weights").float().reshape(T, -1).contiguous()
+        need = L.load().dsv41_moe_prefill_a16_workspace_size(C.byref(cfg), T, 1 if has_idx else 0)
+        ws = L.workspace(need, xf.device)
+        y = t.empty((T, self.dim), dtype=odt, device=xf.device)
+        L.call("dsv41_moe_prefill_a16", C.byref(cfg), C.byref(W), L.ptr(xf), T,
+               L.ptr(wts) if has_idx else None, L.ptr(idx) if has_idx else None,
+               L.dtype_code(odt), L.ptr(y), L.ptr(ws), ws.numel(), L.stream_of(xf))
+        return y.reshape(shape)
+
     def _packed_scales(self, cfg, W, device):
         """Expert scales in the tensor-core layout, rebuilt when a scale tensor changes."""
         e, se = self.experts, self.shared_experts

@@ -305,6 +305,24 @@ int dsv41_moe_prefill(const dsv41_moe_config *cfg, const dsv41_moe_weights *w,
                       const float *route_weights, const int32_t *route_indices, int out_dtype,
                       void *y, void *workspace, size_t workspace_bytes, void *stream);
 
+/* ---- a10 + a13 at prefill sizes in the port's numerics ("a16"): the MoE layer of
+ * deepseek_v41_mlx/moe.py:96-112 (SwitchGLU over the release's fp4 experts decoded exactly to
+ * bf16, dequant.py:63-68; the fp8 shared expert, moe.py:77-93) with bf16 activations as they
+ * are, on tcgen05 kind::f16 tensor cores: routed gate/up -> clamped SwiGLU in fp32 -> down on
+ * that fp32 h (as bf16 hi + lo halves) -> expert outputs weighted and summed in top-k order,
+ * fp32, + the shared expert.  cfg->flags: DSV41_MOE_ROUND_BF16 = the port's bf16 rounding of
+ * the gate/up outputs and of the shared expert's intermediates (else every intermediate stays
+ * fp32); DSV41_MOE_NO_SHARED / DSV41_MOE_SHARED_ONLY as for dsv41_moe_prefill.  Routing is
+ * computed (route_indices NULL) or given (weights f32 [T, topk], indices int32 [T, topk]).
+ * dim % 128 == 0, moe_inter_dim % 128 == 0, topk <= 8; x bf16 [T, dim], y F32 or BF16
+ * [T, dim], both 16-byte aligned. */
+size_t dsv41_moe_prefill_a16_workspace_size(const dsv41_moe_config *cfg, int64_t T,
+                                            int with_routing);
+int dsv41_moe_prefill_a16(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, const void *x,
+                          int64_t T, const float *route_weights, const int32_t *route_indices,
+                          int out_dtype, void *y, void *workspace, size_t workspace_bytes,
+                          void *stream);
+
 /* ---- (e) expert-parallel prefill (replaces upstream's replicate + fp32 all_reduce,
  * docs/reference/model.py:854-904).  Source rank: dsv41_moe_ep_pack quantizes its tokens
  * (act_quant), sorts the (token, slot) pairs by global expert (hence by owner rank) and packs

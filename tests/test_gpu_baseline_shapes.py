@@ -142,3 +142,35 @@ def test_prefill_a8_d3_shape(layer):
                                             routing=(w_np[sample], idx_np[sample]))
     got = y.cpu().numpy()[sample]
     assert rel_fro(got, want) < 1e-2
+
+
+def test_prefill_a16_d3_shape(layer):
+    """BASELINE configs[2] in the port's numerics on the tensor cores (MoE.prefill_a16):
+    exact mode, fp32 output, against oracle.moe.moe_forward (float64 accumulation) on
+    sampled tokens.  The tensor cores accumulate a tile's whole K (7168 for gate/up, 2 x 2048
+    for the hi + lo down projection) in one fp32 accumulator, whose rounding grows with the
+    number of MMA steps: measured 8.4e-5 here (the small shapes of test_gpu_prefill_a16.py,
+    K <= 512, stay under 1e-5; the decode engine, which sums per-32 partials, meets 1e-5 at
+    this shape).  Bound: 2e-4."""
+    T = 8192
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(4322)
+    x = torch.randn(T, D, device=dev, generator=g).to(torch.bfloat16)
+    w, idx = bench.zipf_routing(torch, dev, x, layer.gate.weight, T)
+    layer.round_bf16 = False
+    try:
+        y = layer.prefill_a16(x, weights=w, indices=idx, out_dtype=torch.float32)
+        torch.cuda.synchronize()
+    finally:
+        layer.round_bf16 = True
+    w_np, idx_np = w.cpu().numpy(), idx.cpu().numpy()
+    counts = np.bincount(idx_np.reshape(-1), minlength=E)
+    rng = np.random.default_rng(8193)
+    light = np.nonzero((counts[idx_np] <= 64).any(-1))[0]
+    sample = np.unique(np.concatenate([rng.choice(T, 12, replace=False),
+                                       rng.choice(light, 12, replace=False)]))
+    xf = _bf16_values(x[torch.from_numpy(sample).to(dev)])
+    p = _oracle_params(layer, np.unique(idx_np[sample]))
+    want, _, _ = OM.moe_forward(xf, p, CFG, round_bf16_io=False,
+                                routing=(w_np[sample], idx_np[sample]))
+    assert rel_fro(y.cpu().numpy()[sample], want) < 2e-4
