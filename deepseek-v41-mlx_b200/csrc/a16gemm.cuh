@@ -20,8 +20,9 @@
 // and lo = bf16(h - hi) and the stage runs the MMAs for both (HILO): the product then carries
 // ~16 significant bits of h, a relative error of ~2^-18 per element.
 //
-// One persistent CTA per SM, 448 threads: warp 0 TMA producer, warp 1 TMEM allocator + MMA
-// issuer, warps 2-5 epilogue, warps 6-13 decoders.  Tiles are taken in a fixed stride
+// One persistent CTA per SM, 704 threads: warp 0 TMA producer, warp 1 TMEM allocator + MMA
+// issuer (each a whole warp whose elect.sync lane issues), warps 2-5 epilogue, warps 6-21
+// decoders (a tile row quarter, 16 codes, each).  Tiles are taken in a fixed stride
 // (tile blockIdx.x + i * gridDim.x) by every role from the prefill's grouped tile lists
 // (expert, m-tile, first row, rows) or, dense, over all rows.  Accumulators are
 // double-buffered (2 x 224 TMEM columns).  Epilogues: SwiGLU (the tile's 128 weight rows are
@@ -34,8 +35,9 @@
 namespace dsv41 {
 
 constexpr int A16_BM = 128, A16_BK = 64, A16_BN = 224;
-constexpr int A16_THREADS = 448;
-constexpr int A16_DEC_WARPS = 8;
+constexpr int A16_DEC_WARPS = 16;
+constexpr int A16_PF = 16;   // k-blocks of weight codes prefetched into L2 ahead of their load
+constexpr int A16_THREADS = 32 * (6 + A16_DEC_WARPS);
 
 enum { A16_EPI_SWIGLU = 0, A16_EPI_F32 = 1 };
 
@@ -67,6 +69,7 @@ struct A16Args {
   const uint8_t *s, *s2;     // ue8m0 weight scales (s2: the up projection's, SwiGLU)
   int64_t sld;               // scale bytes a scale row (K / 32)
   int sshift;                // scale row of weight row r: r >> sshift (0 fp4; 5 fp8 32x32)
+  int svec;                  // scale rows 16-byte aligned and sld % 16 == 0 (vector loads)
   const int4 *tiles;         // grouped tiles {group, m-tile, first row, rows | row tile << 8}
   const int *ntiles;         //   and their count (device); null tiles = dense
   int dense_nt, dense_rows, dense_tiles;   // dense: m-tiles x ceil(rows / 224) tiles
@@ -141,13 +144,31 @@ __global__ void __launch_bounds__(A16_THREADS, 1)
   constexpr int WROWS = SWI ? 64 : A16_BM;            // weight rows a TMA box covers
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      prefetch_tmap(&maps.w);
-      if (SWI) prefetch_tmap(&maps.w2);
+    // ------------------------------------------------------------ producer (whole warp; one
+    // elected lane issues)
+    {
+      if (lane == 0) {
+        prefetch_tmap(&maps.w);
+        if (SWI) prefetch_tmap(&maps.w2);
+      }
       // an expert's m-tile is read by its consecutive row tiles (neighbouring CTAs): keep it
       const uint64_t pol_w = l2_policy_evict_normal();
       const uint64_t pol_x = l2_policy_evict_normal();
+      // The weight codes come from HBM as 32- or 64-byte pieces of 128 rows, the slowest
+      // copies of a stage: the producer prefetches them into L2 A16_PF k-blocks ahead (into
+      // the CTA's next tile), so the stage ring waits on L2 rather than HBM latency.
+      auto wrow_of = [&](int t) {
+        const int4 tl = a16_tile(args, t);
+        return int32_t(int64_t(tl.x) * args.a_rows + int64_t(tl.y) * WROWS);
+      };
+      auto prefetch_w = [&](int32_t wrow, int kb) {
+        tma_prefetch_2d_el(&maps.w, kb * Cfg::RB, wrow);
+        if (SWI) tma_prefetch_2d_el(&maps.w2, kb * Cfg::RB, wrow);
+      };
+      if (blockIdx.x < ntiles) {
+        const int32_t w0 = wrow_of(blockIdx.x);
+        for (int kb = 0; kb < A16_PF && kb < nkb; ++kb) prefetch_w(w0, kb);
+      }
       int it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
@@ -155,43 +176,49 @@ __global__ void __launch_bounds__(A16_THREADS, 1)
         const int nmma = bs_nmma<A16_BN>(tl.w & 0xFF), bi = bs_box(nmma);
         const uint32_t xbytes = bs_box_rows(bi) * A16_BK * 2;
         const int32_t wrow0 = int32_t(int64_t(tl.x) * args.a_rows + int64_t(tl.y) * WROWS);
+        const int tn = t + int(gridDim.x);
+        const int32_t wnext = tn < ntiles ? wrow_of(tn) : 0;
         for (int kb = 0; kb < nkb; ++kb, ++it) {
           const int s = it % S;
-          if (!mbar_wait(&empty[s], (uint32_t(it / S) & 1u) ^ 1u)) {
+          const int kp = kb + A16_PF;
+          if (kp < nkb) prefetch_w(wrow0, kp);
+          else if (tn < ntiles && kp - nkb < nkb) prefetch_w(wnext, kp - nkb);
+          if (!warp_wait(&empty[s], (uint32_t(it / S) & 1u) ^ 1u)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], uint32_t(Cfg::RAW) + uint32_t(Cfg::NB) * xbytes);
+          mbar_arrive_expect_tx_el(&full[s], uint32_t(Cfg::RAW) + uint32_t(Cfg::NB) * xbytes);
           uint8_t *raw = smem + Cfg::OFF_RAW + s * Cfg::RAW;
-          tma_load_2d(raw, &maps.w, &full[s], kb * Cfg::RB, wrow0, pol_w);
-          if (SWI) tma_load_2d(raw + 64 * Cfg::RB, &maps.w2, &full[s], kb * Cfg::RB, wrow0, pol_w);
+          tma_load_2d_el(raw, &maps.w, &full[s], kb * Cfg::RB, wrow0, pol_w);
+          if (SWI) tma_load_2d_el(raw + 64 * Cfg::RB, &maps.w2, &full[s], kb * Cfg::RB, wrow0, pol_w);
           uint8_t *b = smem + Cfg::OFF_B + s * Cfg::NB * Cfg::B_BYTES;
-          tma_load_2d(b, &maps.x[bi], &full[s], kb * A16_BK, tl.z, pol_x);
-          if (HILO) tma_load_2d(b + Cfg::B_BYTES, &maps.xlo[bi], &full[s], kb * A16_BK, tl.z, pol_x);
+          tma_load_2d_el(b, &maps.x[bi], &full[s], kb * A16_BK, tl.z, pol_x);
+          if (HILO) tma_load_2d_el(b + Cfg::B_BYTES, &maps.xlo[bi], &full[s], kb * A16_BK, tl.z, pol_x);
         }
       }
       // every copy issued has landed before the CTA can finish
       for (int j = it - S < 0 ? 0 : it - S; j < it; ++j)
-        mbar_wait(&full[j % S], uint32_t(j / S) & 1u);
+        warp_wait(&full[j % S], uint32_t(j / S) & 1u);
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // ------------------------------------------------------------ MMA issuer (whole warp; one
+    // elected lane issues)
+    {
       int it = 0, tc = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++tc) {
         const int4 tl = a16_tile(args, t);
         const int nmma = bs_nmma<A16_BN>(tl.w & 0xFF);
         const int ab = tc & 1;
-        if (!mbar_wait(&acc_empty[ab], (uint32_t(tc >> 1) & 1u) ^ 1u)) break;
+        if (!warp_wait(&acc_empty[ab], (uint32_t(tc >> 1) & 1u) ^ 1u)) break;
         tc_fence_after();
         const uint32_t tacc = tmem + uint32_t(ab) * A16_BN;
         const uint32_t idesc = idesc_bf16(uint32_t(nmma));
         for (int kb = 0; kb < nkb; ++kb, ++it) {
           const int s = it % S;
           const uint32_t ph = uint32_t(it / S) & 1u;
-          if (!mbar_wait(&full[s], ph) || !mbar_wait(&afull[s], ph)) {
+          if (!warp_wait(&full[s], ph) || !warp_wait(&afull[s], ph)) {
             ok = false;
             break;
           }
@@ -201,21 +228,21 @@ __global__ void __launch_bounds__(A16_THREADS, 1)
           const uint64_t db = sdesc_sw128(b0);
 #pragma unroll
           for (int k = 0; k < 4; ++k)   // K = 16 bf16 = 32 bytes an MMA
-            tc_mma_bf16(tacc, da + uint64_t(2 * k), db + uint64_t(2 * k), idesc,
-                        (kb | k) != 0 ? 1u : 0u);
+            tc_mma_bf16_el(tacc, da + uint64_t(2 * k), db + uint64_t(2 * k), idesc,
+                           (kb | k) != 0 ? 1u : 0u);
           if (HILO) {
             const uint64_t dl = sdesc_sw128(b0 + Cfg::B_BYTES);
 #pragma unroll
             for (int k = 0; k < 4; ++k)
-              tc_mma_bf16(tacc, da + uint64_t(2 * k), dl + uint64_t(2 * k), idesc, 1u);
+              tc_mma_bf16_el(tacc, da + uint64_t(2 * k), dl + uint64_t(2 * k), idesc, 1u);
           }
-          tc_commit(&empty[s]);
+          tc_commit_el(&empty[s]);
         }
         if (!ok) break;
-        tc_commit(&acc_full[ab]);
+        tc_commit_el(&acc_full[ab]);
       }
-      tc_commit(mma_done);
-      mbar_wait(mma_done, 0);
+      tc_commit_el(mma_done);
+      warp_wait(mma_done, 0);
     }
     __syncwarp();
   } else if (warp < 6) {
@@ -321,8 +348,9 @@ __global__ void __launch_bounds__(A16_THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ decoders
-    const int dt = (warp - 6) * 32 + lane;             // 0 .. 255
-    const int row = dt >> 1, half = dt & 1;             // tile row, 32-wide k half
+    // thread dt: tile row dt / 4, K quarter dt % 4 (16 codes) of every stage
+    const int dt = (warp - 6) * 32 + lane;             // 0 .. 511
+    const int row = dt >> 2, q = dt & 3, half = q >> 1;  // half: the quarter's 32-wide scale block
     int it = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
@@ -330,24 +358,45 @@ __global__ void __launch_bounds__(A16_THREADS, 1)
       // this row's scales: gate rows from s, up rows from s2 (SwiGLU), K block 2 kb + half
       const uint8_t *sv = (SWI && row >= 64) ? args.s2 : args.s;
       const int64_t wr = int64_t(tl.x) * args.a_rows + int64_t(tl.y) * WROWS + (SWI ? (row & 63) : row);
-      const uint8_t *sp = sv + (wr >> args.sshift) * args.sld + half;
-      uint32_t sb = __ldg(sp);
+      const uint8_t *srow = sv + (wr >> args.sshift) * args.sld;   // the row's K/32 scale bytes
+      // The row's scales 16 bytes (8 stages) a load, the next block fetched 8 stages ahead,
+      // so no stage waits on a global load (rows 16-byte aligned: args.svec); else a byte a
+      // stage, one stage ahead.
+      uint4 blk = make_uint4(0, 0, 0, 0), nxt = make_uint4(0, 0, 0, 0);
+      uint32_t sb = 0;
+      if (args.svec) {
+        blk = __ldg(reinterpret_cast<const uint4 *>(srow));
+        if (nkb > 8) nxt = __ldg(reinterpret_cast<const uint4 *>(srow) + 1);
+      } else {
+        sb = __ldg(srow + half);
+      }
       uint8_t *arow = smem + Cfg::OFF_A + (row >> 3) * 1024 + (row & 7) * 128;
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const int s = it % S;
-        const uint32_t sb_next = kb + 1 < nkb ? uint32_t(__ldg(sp + 2 * (kb + 1))) : 0u;
+        uint32_t sb_next = 0;
+        if (args.svec) {
+          if (kb > 0 && (kb & 7) == 0) {
+            blk = nxt;
+            if (kb + 8 < nkb) nxt = __ldg(reinterpret_cast<const uint4 *>(srow) + (kb >> 3) + 1);
+          }
+          const uint32_t wsel = (kb & 7) >> 1;             // word of the block
+          const uint32_t wv = wsel == 0 ? blk.x : wsel == 1 ? blk.y : wsel == 2 ? blk.z : blk.w;
+          sb = (wv >> (8 * (2 * (kb & 1) + half))) & 0xFFu;
+        } else {
+          sb_next = kb + 1 < nkb ? uint32_t(__ldg(srow + 2 * (kb + 1) + half)) : 0u;
+        }
         if (!warp_wait(&full[s], uint32_t(it / S) & 1u)) {
           ok = false;
           break;
         }
         const float sc = e8m0f(sb);
-        const uint8_t *src = smem + Cfg::OFF_RAW + s * Cfg::RAW + row * Cfg::RB + half * (Cfg::RB / 2);
-        uint32_t wv[16];                                 // 32 bf16 of this row's half
+        const uint8_t *src = smem + Cfg::OFF_RAW + s * Cfg::RAW + row * Cfg::RB + q * (Cfg::RB / 4);
+        uint32_t wv[8];                                  // 16 bf16 of this row's quarter
         if constexpr (WFMT == BS_W_FP4) {
-          const uint4 c = *reinterpret_cast<const uint4 *>(src);   // 32 codes, low nibble first
-          const uint32_t cw[4] = {c.x, c.y, c.z, c.w};
+          const uint2 c = *reinterpret_cast<const uint2 *>(src);   // 16 codes, low nibble first
+          const uint32_t cw[2] = {c.x, c.y};
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
+          for (int i = 0; i < 2; ++i) {
             uint32_t h4[4];
             e2m1x8_to_f16x8(cw[i], h4[0], h4[1], h4[2], h4[3]);
 #pragma unroll
@@ -358,11 +407,10 @@ __global__ void __launch_bounds__(A16_THREADS, 1)
             }
           }
         } else {
-          const uint4 c0 = reinterpret_cast<const uint4 *>(src)[0];
-          const uint4 c1 = reinterpret_cast<const uint4 *>(src)[1];
-          const uint32_t cw[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+          const uint4 c = *reinterpret_cast<const uint4 *>(src);
+          const uint32_t cw[4] = {c.x, c.y, c.z, c.w};
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
+          for (int i = 0; i < 4; ++i) {
             uint32_t h2[2];
             e4m3x4_to_f16x4(cw[i], h2[0], h2[1]);
 #pragma unroll
@@ -375,15 +423,15 @@ __global__ void __launch_bounds__(A16_THREADS, 1)
         }
         uint8_t *a = arow + s * Cfg::A_BYTES;
 #pragma unroll
-        for (int cl = 0; cl < 4; ++cl) {               // 16-byte chunks 4 half .. 4 half + 3
-          const int c = 4 * half + cl;
+        for (int cl = 0; cl < 2; ++cl) {               // 16-byte chunks 2 q, 2 q + 1
+          const int c = 2 * q + cl;
           *reinterpret_cast<uint4 *>(a + ((c ^ (row & 7)) << 4)) =
               make_uint4(wv[4 * cl], wv[4 * cl + 1], wv[4 * cl + 2], wv[4 * cl + 3]);
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&afull[s]);
-        sb = sb_next;
+        if (!args.svec) sb = sb_next;
       }
     }
   }

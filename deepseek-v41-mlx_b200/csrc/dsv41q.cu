@@ -2181,6 +2181,7 @@ extern "C" int dsv41_moe_prefill_a16(const dsv41_moe_config *cfg, const dsv41_mo
     a.s = W->s1;
     a.s2 = W->s3;
     a.sld = d.D / 32;
+    a.svec = (a.sld % 16 == 0 && aligned(W->s1, 16) && aligned(W->s3, 16)) ? 1 : 0;
     a.hhi = ws.hhi;
     a.hlo = ws.hlo;
     a.ldh = d.I;
@@ -2205,6 +2206,7 @@ extern "C" int dsv41_moe_prefill_a16(const dsv41_moe_config *cfg, const dsv41_mo
     b.a_rows = int(d.D);
     b.s = W->s2;
     b.sld = d.I / 32;
+    b.svec = (b.sld % 16 == 0 && aligned(W->s2, 16)) ? 1 : 0;
     b.out = ws.Y;
     b.ldo = d.D;
     for (int list = 2; list < 4; ++list) {
@@ -2228,6 +2230,7 @@ extern "C" int dsv41_moe_prefill_a16(const dsv41_moe_config *cfg, const dsv41_mo
     a.s2 = W->ss3;
     a.sld = ceil_div(d.D, 32);
     a.sshift = 5;
+    a.svec = (a.sld % 16 == 0 && aligned(W->ss1, 16) && aligned(W->ss3, 16)) ? 1 : 0;
     a.hhi = ws.shi;
     a.hlo = ws.slo;             // null in the port's numerics: h is rounded to bf16
     a.ldh = d.I;
@@ -2248,6 +2251,7 @@ extern "C" int dsv41_moe_prefill_a16(const dsv41_moe_config *cfg, const dsv41_mo
     b.s = W->ss2;
     b.sld = ceil_div(d.I, 32);
     b.sshift = 5;
+    b.svec = (b.sld % 16 == 0 && aligned(W->ss2, 16)) ? 1 : 0;
     b.out = ws.Ys;
     b.ldo = d.D;
     b.round_out = round ? 1 : 0;

@@ -119,3 +119,24 @@ def test_prefill_a16_matches_decode_path(cuda):
     y_dec, w, idx = m(_bf(xb), with_routing=True, out_dtype=torch.float32)
     y_pf = m.prefill_a16(_bf(xb), weights=w, indices=idx, out_dtype=torch.float32)
     assert rel_fro(y_pf.cpu().numpy(), y_dec.cpu().numpy()) < 1e-5
+
+
+def test_prefill_a16_scale_byte_edges(cuda):
+    """Scale bytes far from 127: down-projection scale bytes drawn from 8..16 (weights near
+    2^-115, the outputs near 2^-110, still normal fp32; the error bound is relative) decode
+    exactly like the release's scales."""
+    rng = np.random.default_rng(33)
+    T, E, D, I, k = 150, 8, 256, 256, 3
+    p = moe_params(rng, E, D, I)
+    p["s2"] = rng.integers(8, 17, size=p["s2"].shape, dtype=np.uint8)
+    p["s1"] = rng.integers(15, 17, size=p["s1"].shape, dtype=np.uint8) + np.uint8(105)
+    args = _args(E, D, I, k)
+    xb, xf = bf16_acts(rng, T, D)
+    w, idx, _ = OM.gate(xf, p["gate_w"], p["gate_bias"], k)
+    m = _moe(p, args, round_bf16=False)
+    y = m.prefill_a16(_bf(xb), weights=_d(w), indices=_d(idx.astype(np.int32)),
+                      out_dtype=torch.float32, shared=False)
+    want, _, _ = OM.moe_forward(xf, p, _cfg(args), round_bf16_io=False, with_shared=False,
+                                routing=(w, idx))
+    assert np.abs(want).max() > 0 and np.isfinite(y.cpu().numpy()).all()
+    assert rel_fro(y.cpu().numpy(), want) < 1e-5
