@@ -69,7 +69,7 @@ __device__ __forceinline__ void tc_mma_bf16(uint32_t d, uint64_t a, uint64_t b, 
       : "memory");
 }
 
-// tcgen05.mma / tcgen05.commit issued by one elect.sync lane of a converged warp (the whole
+// tcgen05.mma issued by one elect.sync lane of a converged warp (the whole
 // warp runs the issuing loop with warp-uniform operands): back-to-back M=128 N=224 K=16 MMAs
 // then run at the tensor pipe's rate, where a single-lane branch issuing them was measured
 // ~40% slower on B200.
@@ -79,13 +79,6 @@ __device__ __forceinline__ void tc_mma_bf16_el(uint32_t d, uint64_t a, uint64_t 
       "{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
       "l"(a), "l"(b), "r"(idesc), "r"(accum)
-      : "memory");
-}
-__device__ __forceinline__ void tc_commit_el(uint64_t *bar) {
-  asm volatile(
-      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
-          smem_u32(bar))
       : "memory");
 }
 
@@ -132,10 +125,13 @@ __global__ void __launch_bounds__(AQ_THREADS, 1)
   const int nkb = args.nkb;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      prefetch_tmap(&maps.w);
-      prefetch_tmap(&maps.x);
+    // ------------------------------------------------------------ producer (whole warp; one
+    // elected lane issues)
+    {
+      if (lane == 0) {
+        prefetch_tmap(&maps.w);
+        prefetch_tmap(&maps.x);
+      }
       const uint64_t pol_w = l2_policy_evict_normal();
       const uint64_t pol_x = l2_policy_evict_normal();
       int it = 0;
@@ -144,35 +140,36 @@ __global__ void __launch_bounds__(AQ_THREADS, 1)
         const int mt = t / args.nt, nt = t % args.nt;
         for (int kb = 0; kb < nkb; ++kb, ++it) {
           const int s = it % S;
-          if (!mbar_wait(&empty[s], (uint32_t(it / S) & 1u) ^ 1u)) {
+          if (!warp_wait(&empty[s], (uint32_t(it / S) & 1u) ^ 1u)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], AQ_BM * RAW_ROW + AQ_B_BYTES);
-          tma_load_2d(smem + AQ_OFF_RAW + s * AQ_RAW_BYTES, &maps.w, &full[s],
-                      int32_t(kb * RAW_ROW), mt * AQ_BM, pol_w);
-          tma_load_2d(smem + AQ_OFF_B + s * AQ_B_BYTES, &maps.x, &full[s], kb * AQ_BK,
-                      nt * AQ_BN, pol_x);
+          mbar_arrive_expect_tx_el(&full[s], AQ_BM * RAW_ROW + AQ_B_BYTES);
+          tma_load_2d_el(smem + AQ_OFF_RAW + s * AQ_RAW_BYTES, &maps.w, &full[s],
+                         int32_t(kb * RAW_ROW), mt * AQ_BM, pol_w);
+          tma_load_2d_el(smem + AQ_OFF_B + s * AQ_B_BYTES, &maps.x, &full[s], kb * AQ_BK,
+                         nt * AQ_BN, pol_x);
         }
       }
       for (int j = it - S < 0 ? 0 : it - S; j < it; ++j)
-        mbar_wait(&full[j % S], uint32_t(j / S) & 1u);
+        warp_wait(&full[j % S], uint32_t(j / S) & 1u);
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // ------------------------------------------------------------ MMA issuer (whole warp; one
+    // elected lane issues)
+    {
       int it = 0, tc = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < args.tiles && ok; t += gridDim.x, ++tc) {
         const int ab = tc & 1;
-        if (!mbar_wait(&acc_empty[ab], (uint32_t(tc >> 1) & 1u) ^ 1u)) break;
+        if (!warp_wait(&acc_empty[ab], (uint32_t(tc >> 1) & 1u) ^ 1u)) break;
         tc_fence_after();
         const uint32_t tacc = tmem + uint32_t(ab) * AQ_BN;
         for (int kb = 0; kb < nkb; ++kb, ++it) {
           const int s = it % S;
           const uint32_t ph = uint32_t(it / S) & 1u;
-          if (!mbar_wait(&full[s], ph) || !mbar_wait(&afull[s], ph)) {
+          if (!warp_wait(&full[s], ph) || !warp_wait(&afull[s], ph)) {
             ok = false;
             break;
           }
@@ -181,15 +178,15 @@ __global__ void __launch_bounds__(AQ_THREADS, 1)
           const uint64_t db = sdesc_sw128(sbase + AQ_OFF_B + s * AQ_B_BYTES);
 #pragma unroll
           for (int k = 0; k < 4; ++k)   // K = 16 bf16 = 32 bytes per MMA
-            tc_mma_bf16(tacc, da + uint64_t(2 * k), db + uint64_t(2 * k), idesc_bf16(AQ_BN),
-                        (kb | k) != 0 ? 1u : 0u);
-          tc_commit(&empty[s]);
+            tc_mma_bf16_el(tacc, da + uint64_t(2 * k), db + uint64_t(2 * k), idesc_bf16(AQ_BN),
+                           (kb | k) != 0 ? 1u : 0u);
+          tc_commit_el(&empty[s]);
         }
         if (!ok) break;
-        tc_commit(&acc_full[ab]);
+        tc_commit_el(&acc_full[ab]);
       }
-      tc_commit(mma_done);
-      mbar_wait(mma_done, 0);
+      tc_commit_el(mma_done);
+      warp_wait(mma_done, 0);
     }
     __syncwarp();
   } else if (warp < 6) {
