@@ -126,7 +126,10 @@ class SharedExpert:
 
 
 class MoE:
-    """moe.py:96-112 (decode path: up to 4096 tokens per call).
+    """moe.py:96-112.  Up to ``a16_min_tokens`` tokens a call (default 2048) run on the
+    decode engine; larger calls run the same numerics on the tensor cores
+    (``prefill_a16``), which is faster there (measured on B200 with the release shapes:
+    T=2048 7.6 vs 7.7 ms, T=4096 13.8 vs 8.6 ms) and has no token limit.
 
     With ``cuda_graph=True`` (default) each (tokens, output dtype, device) shape is
     captured once into a CUDA graph (router, plan, expert kernels, shared expert
@@ -145,8 +148,10 @@ class MoE:
     """
 
     def __init__(self, args, round_bf16: bool = True, cuda_graph: bool = True,
-                 pack_decode_scales: bool = True, row_pair_down: bool = True):
+                 pack_decode_scales: bool = True, row_pair_down: bool = True,
+                 a16_min_tokens: int = 2048):
         self.args = args
+        self.a16_min_tokens = a16_min_tokens
         self.dim = args.dim
         self.gate = Gate(args)
         self.experts = SwitchGLU(args.dim, args.moe_inter_dim, args.n_routed_experts,
@@ -306,6 +311,11 @@ class MoE:
         xf = xt.to(t.bfloat16).reshape(-1, self.dim)
         T = xf.shape[0]
         odt = out_dtype or (t.float32 if xt.dtype == t.float32 else t.bfloat16)
+        if T > self.a16_min_tokens:
+            weights, indices = self.gate(xf)
+            y = self.prefill_a16(xf, weights=weights, indices=indices, out_dtype=odt)
+            y = y.reshape(shape)
+            return (y, weights, indices) if with_routing else y
         if self.cuda_graph and not t.cuda.is_current_stream_capturing():
             y, weights, indices = self._graph_call(xf, odt, with_routing)
             y = y.reshape(shape)

@@ -140,3 +140,19 @@ def test_prefill_a16_scale_byte_edges(cuda):
                                 routing=(w, idx))
     assert np.abs(want).max() > 0 and np.isfinite(y.cpu().numpy()).all()
     assert rel_fro(y.cpu().numpy(), want) < 1e-5
+
+
+def test_moe_call_above_crossover_runs_a16(cuda):
+    """``MoE.__call__`` above ``a16_min_tokens`` tokens runs the tensor-core path: the same
+    routing and the decode engine's outputs within 1e-5 (exact mode, fp32)."""
+    rng = np.random.default_rng(23)
+    T, E, D, I, k = 40, 12, 256, 128, 4
+    p = moe_params(rng, E, D, I)
+    args = _args(E, D, I, k)
+    xb, _ = bf16_acts(rng, T, D)
+    m = _moe(p, args, round_bf16=False)
+    y_dec, w_dec, i_dec = m(_bf(xb), with_routing=True, out_dtype=torch.float32)
+    m.a16_min_tokens = 16
+    y_a16, w_a16, i_a16 = m(_bf(xb), with_routing=True, out_dtype=torch.float32)
+    assert torch.equal(i_dec, i_a16) and torch.equal(w_dec, w_a16)
+    assert rel_fro(y_a16.cpu().numpy(), y_dec.cpu().numpy()) < 1e-5
