@@ -308,29 +308,38 @@ __global__ void k_pf_combine(const __nv_bfloat16 *__restrict__ Yp, const __nv_bf
   const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= T * groups) return;
   const int64_t t = i / groups, c0 = (i % groups) * 8;
+  // the token's (expert, slot) pairs, sorted by expert id with a fixed compare-exchange
+  // network (registers only; unused entries sort last), then all its rows loaded at once and
+  // added in that order
   int ids[8], pos[8];
-  for (int j = 0; j < topk; ++j) {
-    ids[j] = idx[t * topk + j];
-    pos[j] = slot_pos[t * topk + j];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    ids[j] = j < topk ? idx[t * topk + j] : 0x7fffffff;
+    pos[j] = j < topk ? slot_pos[t * topk + j] : -1;
   }
-  for (int a = 1; a < topk; ++a) {       // insertion sort by expert id
-    const int ki = ids[a], kp = pos[a];
-    int b = a - 1;
-    while (b >= 0 && ids[b] > ki) {
-      ids[b + 1] = ids[b];
-      pos[b + 1] = pos[b];
-      --b;
-    }
-    ids[b + 1] = ki;
-    pos[b + 1] = kp;
-  }
+#pragma unroll
+  for (int a = 0; a < 7; ++a)
+#pragma unroll
+    for (int b = 0; b < 7 - a; ++b)
+      if (ids[b] > ids[b + 1]) {
+        const int ti = ids[b], tp = pos[b];
+        ids[b] = ids[b + 1];
+        pos[b] = pos[b + 1];
+        ids[b + 1] = ti;
+        pos[b + 1] = tp;
+      }
+  uint4 rv[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    rv[j] = pos[j] >= 0 ? *reinterpret_cast<const uint4 *>(Yp + int64_t(pos[j]) * D + c0)
+                        : make_uint4(0, 0, 0, 0);
   float acc[8];
 #pragma unroll
   for (int c = 0; c < 8; ++c) acc[c] = 0.0f;
-  for (int j = 0; j < topk; ++j) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
     if (pos[j] < 0) continue;
-    const uint4 v = *reinterpret_cast<const uint4 *>(Yp + int64_t(pos[j]) * D + c0);
-    const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+    const uint32_t wv[4] = {rv[j].x, rv[j].y, rv[j].z, rv[j].w};
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       acc[2 * c] = __fadd_rn(acc[2 * c], bf_bits2f(uint16_t(wv[c] & 0xFFFF)));
