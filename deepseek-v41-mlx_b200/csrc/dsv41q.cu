@@ -355,8 +355,8 @@ int qgemv_launch(const char *name, const CUtensorMap &w0, const CUtensorMap &w1,
     sv = sv && aligned(p.aff_s, 2 * NG) && aligned(p.aff_b, 2 * NG);
   pv.svec = sv ? 1 : 0;
   ProfScope prof(name, st);
-  DSV41_LAUNCH(launch_pdl(k_qgemv<WF, NMAT, NT>, dim3(grid), dim3(QG_THREADS), Cfg::SMEM, st, w0,
-                          w1, x8, x16, x32, pv),
+  DSV41_LAUNCH(launch_pdl_if(pdl_enabled() || pv.pdl_early != 0, k_qgemv<WF, NMAT, NT>, dim3(grid),
+                             dim3(QG_THREADS), Cfg::SMEM, st, w0, w1, x8, x16, x32, pv),
                "qgemv");
   DSV41_CHECK_LAUNCH("qgemv");
   return DSV41_OK;
@@ -457,20 +457,6 @@ int gemv_common(const void *x, int64_t M, int64_t K, const void *w, int64_t w_ro
 
   constexpr bool AFF = WF == WF_AFF4 || WF == WF_AFF8;
   const int perm = WF == WF_AFF4 ? 4 : (WF == WF_AFF8 ? 8 : 0);
-  { ProfScope prof("qx_prep", st);
-  DSV41_LAUNCH(launch_pdl(k_qx_prep, dim3(unsigned(M)), dim3(256), 0, st,
-                          reinterpret_cast<const __nv_bfloat16 *>(x), M, K,
-                          static_cast<const int32_t *>(nullptr), static_cast<const int *>(nullptr),
-                          ws.x16, ws.xscale, AFF ? ws.xsum : static_cast<float *>(nullptr), perm),
-               "qx_prep"); }
-  DSV41_CHECK_LAUNCH("qx_prep");
-
-  CUtensorMap wm, xm[3];
-  int rc = weight_map(&wm, w, N, w_row_bytes);
-  if (rc) return rc;
-  rc = make_x_maps(xm, ws.x16, M, K);
-  if (rc) return rc;
-
   QParams p{};
   p.scale[0] = s;
   p.scale[1] = s;
@@ -490,6 +476,24 @@ int gemv_common(const void *x, int64_t M, int64_t K, const void *w, int64_t w_ro
     }
     if (cap > 0 && p.nsplit > cap) p.nsplit = cap;
   }
+  // The prep kernel also zeroes the split-K tickets, and the GEMV is launched as its
+  // programmatic dependent: the GEMV's first weight copies are issued while the prep runs.
+  { ProfScope prof("qx_prep", st);
+  DSV41_LAUNCH(launch_pdl(k_qx_prep, dim3(unsigned(M)), dim3(256), 0, st,
+                          reinterpret_cast<const __nv_bfloat16 *>(x), M, K,
+                          static_cast<const int32_t *>(nullptr), static_cast<const int *>(nullptr),
+                          ws.x16, ws.xscale, AFF ? ws.xsum : static_cast<float *>(nullptr), perm,
+                          p.nsplit > 1 ? ws.counters : static_cast<int *>(nullptr),
+                          int64_t(p.nsplit > 1 ? tiles * nch : 0)),
+               "qx_prep"); }
+  DSV41_CHECK_LAUNCH("qx_prep");
+
+  CUtensorMap wm, xm[3];
+  int rc = weight_map(&wm, w, N, w_row_bytes);
+  if (rc) return rc;
+  rc = make_x_maps(xm, ws.x16, M, K);
+  if (rc) return rc;
+
   p.xscale = ws.xscale;
   p.xsum = ws.xsum;
   p.chunks = nullptr;
@@ -501,10 +505,7 @@ int gemv_common(const void *x, int64_t M, int64_t K, const void *w, int64_t w_ro
   p.ldo = N;
   p.partial = ws.partial;
   p.counters = ws.counters;
-  if (p.nsplit > 1) {
-    cudaError_t e = cudaMemsetAsync(ws.counters, 0, sizeof(int) * tiles * nch, st);
-    if (e != cudaSuccess) return cuda_status(e, "memset counters");
-  }
+  p.pdl_early = 1;
   const int items = int(tiles * nch * p.nsplit);
   if (M <= 8) return qgemv_launch<WF, 1, 1>("qgemv_dense", wm, wm, xm[0], xm[1], xm[2], p, items, st);
   if (M <= 16) return qgemv_launch<WF, 1, 2>("qgemv_dense", wm, wm, xm[0], xm[1], xm[2], p, items, st);
@@ -831,7 +832,7 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
                           reinterpret_cast<const __nv_bfloat16 *>(x), T, d.D,
                           static_cast<const int32_t *>(ws.plan.pair_tok),
                           static_cast<const int *>(ws.plan.counts + 2), ws.x16g, ws.xsg,
-                          static_cast<float *>(nullptr), 0),
+                          static_cast<float *>(nullptr), 0, static_cast<int *>(nullptr), int64_t(0)),
                "qx_prep gathered"); }
   DSV41_CHECK_LAUNCH("qx_prep gathered");
 
@@ -940,7 +941,8 @@ int moe_experts_impl(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, co
   DSV41_LAUNCH(launch_pdl(k_qx_prep, dim3(unsigned(T)), dim3(256), 0, st,
                           reinterpret_cast<const __nv_bfloat16 *>(x), T, d.D,
                           static_cast<const int32_t *>(nullptr), static_cast<const int *>(nullptr),
-                          ws.x16, ws.xs, static_cast<float *>(nullptr), 0),
+                          ws.x16, ws.xs, static_cast<float *>(nullptr), 0,
+                          static_cast<int *>(nullptr), int64_t(0)),
                "qx_prep shared"); }
   DSV41_CHECK_LAUNCH("qx_prep shared");
   CUtensorMap m_s1, m_s3, m_s2, xs[3], hs[3];
@@ -2934,7 +2936,7 @@ extern "C" int dsv41_gemv_fp8_block_noalloc(const void *x, int64_t M, int64_t K,
   {
     ProfScope prof("qx_prep", st);
     k_qx_prep<<<unsigned(M), 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16 *>(x), M, K,
-                                            nullptr, nullptr, x16, xscale, nullptr, 0);
+                                            nullptr, nullptr, x16, xscale, nullptr, 0, nullptr, 0);
   }
   DSV41_CHECK_LAUNCH("qx_prep (noalloc)");
   CUtensorMap wm, xm[3];

@@ -95,6 +95,10 @@ struct QParams {
   int round_out;               // DOWN: round output to bf16 (stored as f32)
   float *partial;              // split-K fragments
   int *counters;               // split-K tickets, zero on entry
+  int pdl_early;               // dense: launched as a programmatic dependent of the activation
+                               // prep, the producer issues its first item's weight copies (and
+                               // scale copies) before waiting for that kernel; only the
+                               // activation copies wait
 };
 
 __device__ __forceinline__ int rhoA(int g) { return ((g & 3) << 1) | (g >> 2); }  // 0,2,4,6,1,3,5,7
@@ -461,7 +465,12 @@ __global__ void __launch_bounds__(QG_THREADS, QG_MIN_CTAS)
     if (NMAT == 2) prefetch_tmap(&wmap1);
   }
   __syncthreads();
-  pdl_wait();       // the plan, activations and split-K state come from earlier kernels
+  // Dense lists launched with pdl_early: the producer issues its first item's weight copies
+  // before waiting for the previous kernel (the weights are not written by it); everything
+  // else waits first -- the plan, activations and split-K state come from earlier kernels.
+  // Not for the affine formats: their stage copies carry the activations' group sums too.
+  const bool early = p.pdl_early && !p.chunks && !AFF;
+  if (!early || warp != QG_CW) pdl_wait();
   pdl_trigger();
   const int nchunks = p.chunks ? *p.nchunks_dev : p.nchunks_host;
   const int nitems = nchunks * p.tiles * p.nsplit;
@@ -476,8 +485,51 @@ __global__ void __launch_bounds__(QG_THREADS, QG_MIN_CTAS)
     const uint64_t pol_x = l2_policy_evict_last();
     uint32_t it = 0;
     const uint32_t sc0 = smem_u32(sc_ring);
+    const bool packed = WF == WF_FP4 && p.spack;
+    // a stage's weight side: the barrier's byte count (weights, scales, activations), the weight
+    // tiles and the scale copies (whose arrivals complete the barrier's count)
+    auto issue_w = [&](int slot, int ks, const QChunk &c, int64_t nbase, int32_t wrow,
+                       int32_t wrow1, int64_t sblk, uint32_t bytes) {
+      uint8_t *st = smem + slot * C::TILE_BYTES;
+      const uint32_t scb = sc0 + slot * C::SC_BYTES;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&full[slot], bytes + (packed ? NMAT * QG_ROWS * 8 : 0));
+        if (WF == WF_FP4 && packed) {
+#pragma unroll
+          for (int m = 0; m < NMAT; ++m) {
+            const int64_t blk = p.rowpair ? 2 * sblk + m : sblk;
+            qg_bulk_load(scb + m * QG_ROWS * 8, p.scale[m] + (blk * p.kstages + ks) * (QG_ROWS * 8),
+                         QG_ROWS * 8, &full[slot]);
+          }
+        }
+        tma_load_2d(st, &wmap0, &full[slot], ks * 128, wrow, pol_w);
+        if (NMAT == 2) tma_load_2d(st + C::W_BYTES, &wmap1, &full[slot], ks * 128, wrow1, pol_w);
+      }
+      if (packed) {
+        mbar_arrive(&full[slot]);        // the scales came with the stage's bulk copies
+      } else if (p.svec) {
+        scales_issue<WF, NMAT, NT>(p, c, nbase, ks, lane, scb);
+        qg_cp_arrive(&full[slot]);       // every lane: arrives when its copies land
+      } else {
+        ScaleRaw<WF, NMAT, NT> raw;
+        scales_fetch<WF, NMAT, NT>(p, c, nbase, ks, lane, raw);
+        scales_raw_store<WF, NMAT, NT>(scb, lane, raw);
+        mbar_arrive(&full[slot]);        // every lane: its scale stores are in
+      }
+    };
+    auto issue_x = [&](int slot, int ks, const QChunk &c, const CUtensorMap *xm) {
+      if (lane == 0) {
+        uint8_t *st = smem + slot * C::TILE_BYTES;
+#pragma unroll
+        for (int b = 0; b < C::NBOX; ++b)
+          tma_load_2d(st + NMAT * C::W_BYTES + b * C::XBOX_BYTES, xm, &full[slot],
+                      ks * KS + b * 64, c.xrow, pol_x);
+      }
+    };
     QChunk pre{};
     chunk_prefetch(p, blockIdx.x, nitems, pre);
+    uint32_t npre = 0;                 // stages of the first item whose weight side is issued
+    bool first = true;
     for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
       int chunk, tile, split;
       QChunk c;
@@ -493,50 +545,33 @@ __global__ void __launch_bounds__(QG_THREADS, QG_MIN_CTAS)
       const int32_t wrow1 = wrow + (p.rowpair ? QG_ROWS : 0);     // matrix 1's first row
       // packed scale blocks are per 64-row tile: rowpair tile t holds tiles 2t and 2t + 1
       const int64_t sblk = (int64_t)c.mat * p.tiles + tile;
+      if (first && early) {
+        // the first ST stages' slots are free: their weight side goes out now, the
+        // activations after the previous kernel has finished
+        npre = uint32_t(min(ST, ke - kb));
+        for (uint32_t i = 0; i < npre; ++i)
+          issue_w(int(i), kb + int(i), c, nbase, wrow, wrow1, sblk, bytes);
+        pdl_wait();
+      }
+      first = false;
       for (int ks = kb; ks < ke; ++ks, ++it) {
         const int slot = it % ST;
         const uint32_t ph = (it / ST) & 1;
-        bool ok = true;
-        if (lane == 0) ok = mbar_wait_or_abort(&empty[slot], ph ^ 1, &s_abort);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) {
-          s_abort = 1;
-          qg_drain<ST>(full, it, lane);   // no copy may land after the CTA is gone
-          return;
-        }
-        uint8_t *st = smem + slot * C::TILE_BYTES;
-        const uint32_t scb = sc0 + slot * C::SC_BYTES;
-        const bool packed = WF == WF_FP4 && p.spack;
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&full[slot], bytes + (packed ? NMAT * QG_ROWS * 8 : 0));
-          if (WF == WF_FP4 && packed) {
-#pragma unroll
-            for (int m = 0; m < NMAT; ++m) {
-              const int64_t blk = p.rowpair ? 2 * sblk + m : sblk;
-              qg_bulk_load(scb + m * QG_ROWS * 8, p.scale[m] + (blk * p.kstages + ks) * (QG_ROWS * 8),
-                           QG_ROWS * 8, &full[slot]);
-            }
+        if (it >= npre) {
+          bool ok = true;
+          if (lane == 0) ok = mbar_wait_or_abort(&empty[slot], ph ^ 1, &s_abort);
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (!ok) {
+            s_abort = 1;
+            qg_drain<ST>(full, it, lane);   // no copy may land after the CTA is gone
+            return;
           }
-          tma_load_2d(st, &wmap0, &full[slot], ks * 128, wrow, pol_w);
-          if (NMAT == 2) tma_load_2d(st + C::W_BYTES, &wmap1, &full[slot], ks * 128, wrow1, pol_w);
-#pragma unroll
-          for (int b = 0; b < C::NBOX; ++b)
-            tma_load_2d(st + NMAT * C::W_BYTES + b * C::XBOX_BYTES, xm, &full[slot],
-                        ks * KS + b * 64, c.xrow, pol_x);
+          issue_w(slot, ks, c, nbase, wrow, wrow1, sblk, bytes);
         }
-        if (packed) {
-          mbar_arrive(&full[slot]);        // the scales came with the stage's bulk copies
-        } else if (p.svec) {
-          scales_issue<WF, NMAT, NT>(p, c, nbase, ks, lane, scb);
-          qg_cp_arrive(&full[slot]);       // every lane: arrives when its copies land
-        } else {
-          ScaleRaw<WF, NMAT, NT> raw;
-          scales_fetch<WF, NMAT, NT>(p, c, nbase, ks, lane, raw);
-          scales_raw_store<WF, NMAT, NT>(scb, lane, raw);
-          mbar_arrive(&full[slot]);        // every lane: its scale stores are in
-        }
+        issue_x(slot, ks, c, xm);
       }
     }
+    if (early && first) pdl_wait();      // a CTA without items still waits (no early exit race)
     qg_drain<ST>(full, it, lane);
     return;
   }
@@ -912,10 +947,14 @@ __global__ void __launch_bounds__(256) k_qx_prep(const __nv_bfloat16 *__restrict
                                                  int64_t K, const int32_t *__restrict__ gather,
                                                  const int *__restrict__ nrows_dev,
                                                  __half *__restrict__ xq, float *__restrict__ xscale,
-                                                 float *__restrict__ xsum, int perm) {
+                                                 float *__restrict__ xsum, int perm,
+                                                 int *__restrict__ zero_ctr, int64_t nzero) {
   pdl_wait();
   pdl_trigger();
   const int64_t r = blockIdx.x;
+  // the dense GEMV's split-K tickets, zeroed here so that no separate memset precedes it
+  if (zero_ctr && r == 0)
+    for (int64_t i = threadIdx.x; i < nzero; i += blockDim.x) zero_ctr[i] = 0;
   const int64_t nrows = nrows_dev ? *nrows_dev : M;
   if (r >= nrows) return;
   const int64_t src = gather ? gather[r] : r;
