@@ -120,3 +120,35 @@ def test_gemv_large_activations(cuda):
     got = q.linear.linear_fp8(_x(xb), _d(w), _d(s), out_dtype=torch.float32).cpu().numpy()
     for r in range(3):
         assert rel_fro(got[r], want[r]) < TOL_F32
+
+
+@pytest.mark.parametrize("M", [1, 32])
+def test_gemv_chain_in_graph_matches_eager(cuda, M):
+    """Consecutive dense GEMVs replayed from one CUDA graph -- each one launched as the
+    programmatic dependent of its activation prep, issuing weight copies before that kernel
+    has finished, with the split-K tickets zeroed by the prep -- give the bits of the same
+    calls made one at a time, and the oracle's values."""
+    rng = np.random.default_rng(41 + M)
+    N, K, n = 4096, 7168, 3
+    ws = [fp8_weight(rng, N, K) for _ in range(n)]
+    xs = [bf16_acts(rng, M, K) for _ in range(n)]
+    tw = [(_d(w), _d(s)) for w, s in ws]
+    tx = [_x(xb) for xb, _ in xs]
+    eager = [q.linear.linear_fp8(tx[i], *tw[i], out_dtype=torch.float32) for i in range(n)]
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        [q.linear.linear_fp8(tx[i], *tw[i], out_dtype=torch.float32) for i in range(n)]
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        outs = [q.linear.linear_fp8(tx[i], *tw[i], out_dtype=torch.float32) for i in range(n)]
+    for _ in range(2):
+        for o in outs:
+            o.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        for i in range(n):
+            assert torch.equal(outs[i], eager[i]), i
+    want = OL.linear_fp8_block(xs[0][1], ws[0][0], ws[0][1])
+    assert rel_fro(outs[0].cpu().numpy(), want) < TOL_F32
