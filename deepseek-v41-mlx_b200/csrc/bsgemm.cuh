@@ -49,15 +49,17 @@ constexpr int BS_RING = 4;                     // tile-ring slots (producer -> M
 // 64 rows, 4 stages of 256 K (32 + 16 KB): the tiles of lightly routed experts only stream
 // weights, and a stage that carries two 128-wide K blocks halves the waits and commits the
 // single MMA-issuing thread spends per weight byte.
-template <bool NARROW>
+template <bool NARROW, bool PAIR = false>
 struct BsCfg {
   static constexpr int BN = NARROW ? BS_BN_NARROW : BS_BN;
+  // PAIR (2-CTA MMA): each CTA of the pair holds half of the activation rows, at most 128
+  static constexpr int B_ROWS = PAIR ? 128 : BN;
   static constexpr int STAGES = 4;
   static constexpr int KSUB = NARROW ? 2 : 1;            // 128-wide K blocks per stage
   static constexpr int NBOX = NARROW ? 2 : 4;            // activation boxes 32/64(/128/224)
   static constexpr int SFB_CHUNKS = NARROW ? 4 : 8;      // 32-row scale chunks staged
   static constexpr int A_SUB = BS_BM * BS_BK;            // fp8, or fp4 padded to a byte/code
-  static constexpr int B_SUB = BN * BS_BK;
+  static constexpr int B_SUB = B_ROWS * BS_BK;
   static constexpr int SFB_SUB = SFB_CHUNKS * 128;
   static constexpr int A_BYTES = KSUB * A_SUB;
   static constexpr int B_BYTES = KSUB * B_SUB;
@@ -127,6 +129,8 @@ struct BsMaps {
   CUtensorMap w;       // weights, box {128 K, 128 rows} (64 rows in SwiGLU mode)
   CUtensorMap w2;      // up-projection weights (SwiGLU mode)
   CUtensorMap x[4];    // activations, box {128 K, bs_box_rows(i)}
+  CUtensorMap sfa;     // PAIR: weight scale atoms as 256-byte rows, box {256, 2} (one atom)
+  CUtensorMap sfb;     // PAIR: activation scale atoms as 256-byte rows, box {256, 4} (two)
 };
 
 // ------------------------------------------------------------------ tcgen05 wrappers
@@ -262,8 +266,106 @@ __device__ __forceinline__ uint64_t sdesc_sf(uint32_t saddr) {
 // Instruction descriptor of kind::mxf8f6f4: A format (e4m3 0, e2m1 5) bits 7-9, B e4m3,
 // K-major both, N>>3 bits 17-22, ue8m0 scales bit 23, M>>4 = 8 bits 24-28, scale-factor id
 // of A bits 29-30 and of B bits 4-5.
-__device__ __forceinline__ uint32_t idesc_mx(uint32_t a_fmt, uint32_t n, uint32_t sf_id) {
-  return (a_fmt << 7) | ((n >> 3) << 17) | (1u << 23) | (8u << 24) | (sf_id << 29) | (sf_id << 4);
+__device__ __forceinline__ uint32_t idesc_mx(uint32_t a_fmt, uint32_t n, uint32_t sf_id,
+                                             uint32_t m = 128) {
+  return (a_fmt << 7) | ((n >> 3) << 17) | (1u << 23) | ((m >> 4) << 24) | (sf_id << 29) |
+         (sf_id << 4);
+}
+
+// ------------------------------------------------------------------ 2-CTA (CTA pair) helpers
+// A pair is a cluster of 2 CTAs; rank 0 issues the M = 256 MMAs for both.  Each CTA loads its
+// own operands (no multicast copies); its copies complete on rank 0's stage barrier, rank 0's
+// MMA commits arrive on both CTAs' barriers, and rank 1's epilogue releases an accumulator on
+// rank 0's barrier by a remote arrival (mapa).
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t ncluster_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// the shared::cluster address of the same shared variable in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t mapa_rank(const void *p, uint32_t rank) {
+  uint32_t d;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(smem_u32(p)), "r"(rank));
+  return d;
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init_cluster() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+// every thread of both CTAs (a hardware barrier: both CTAs are resident together)
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(slot)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+// 2D TMA load into this CTA's shared memory that completes on the barrier at `bar_cluster`
+// (rank 0's full barrier), one elected lane
+__device__ __forceinline__ void tma_load_2d_pair_el(void *dst, const CUtensorMap *map,
+                                                    uint32_t bar_cluster, int32_t x, int32_t y,
+                                                    uint64_t policy) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;\n\t}" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ void tc_cp_sf_pair_el(uint32_t taddr, uint64_t sdesc) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;\n\t}" ::"r"(taddr),
+      "l"(sdesc)
+      : "memory");
+}
+__device__ __forceinline__ void tc_mma_mx_pair_el(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                                  uint32_t sfa, uint32_t sfb, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accum), "r"(sfa), "r"(sfb)
+      : "memory");
+}
+// commit of the pair's MMAs to a barrier of this (rank 0) CTA
+__device__ __forceinline__ void tc_commit_pair_el(uint64_t *bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+// the same commit arriving on the barrier at this offset in both CTAs of the pair (an
+// arrival signal, not a copy: no data moves)
+__device__ __forceinline__ void tc_commit_pair_both_el(uint64_t *bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n\t}" ::"r"(
+          smem_u32(bar)),
+      "h"((unsigned short)3)
+      : "memory");
 }
 
 // cp.async of the 4 per-32 scales of (row, K stage kb) to shared address dst.
@@ -302,10 +404,11 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity) {
   return __all_sync(0xffffffffu, ok);
 }
 
-template <int WFMT, int EPI, bool NARROW>
+template <int WFMT, int EPI, bool NARROW, bool PAIR = false>
 __global__ void __launch_bounds__(BS_THREADS, 1)
     k_bsgemm(const __grid_constant__ BsMaps maps, const BsArgs args) {
-  using Cfg = BsCfg<NARROW>;
+  static_assert(!(PAIR && NARROW), "the 2-CTA form is the wide shape");
+  using Cfg = BsCfg<NARROW, PAIR>;
   constexpr int S = Cfg::STAGES;
   extern __shared__ uint8_t bs_raw[];
   const uint32_t raw_s = smem_u32(bs_raw);
@@ -316,7 +419,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
   uint64_t *full = bars;                    // [S] count 33 (1 when all scales are atoms)
   uint64_t *empty = bars + S;               // [S] count 1 (tcgen05.commit)
   uint64_t *acc_full = bars + 2 * S;        // [2] count 1 (tcgen05.commit)
-  uint64_t *acc_empty = acc_full + 2;       // [2] count 4 (epilogue warps)
+  uint64_t *acc_empty = acc_full + 2;       // [2] count 4 (epilogue warps; 8: both CTAs' in PAIR)
   uint64_t *xfull = acc_full + 4;           // [2] count 64 (SwiGLU pair exchange)
   uint64_t *xempty = acc_full + 6;          // [2] count 64
   uint64_t *tfull = acc_full + 8;           // [BS_RING] count 1 (producer)
@@ -325,6 +428,9 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // PAIR: rank 0 of the CTA pair issues the MMAs; rank 1 only loads its operands and drains
+  // its half of the accumulators
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;
   if (threadIdx.x == 0) {
     const bool lanes = !(args.sfa_atoms && args.sfb_atoms);   // some scales staged by lanes
     for (int s = 0; s < S; ++s) {
@@ -333,7 +439,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 4);
+      mbar_init(&acc_empty[i], PAIR ? 8 : 4);
       mbar_init(&xfull[i], 64);
       mbar_init(&xempty[i], 64);
     }
@@ -343,13 +449,20 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
     }
     mbar_init(mma_done, 1);
     fence_barrier_init();
+    if (PAIR) fence_mbar_init_cluster();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) cluster_sync();   // both CTAs' barriers exist before either reaches them
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int nkb = args.nkb;
@@ -361,6 +474,10 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
       prefetch_tmap(&maps.w);
       if (EPI == BS_EPI_SWIGLU) prefetch_tmap(&maps.w2);
       for (int i = 0; i < Cfg::NBOX; ++i) prefetch_tmap(&maps.x[i]);
+      if (PAIR) {
+        prefetch_tmap(&maps.sfa);
+        prefetch_tmap(&maps.sfb);
+      }
     }
     // narrow tiles read their weights once; activation rows are reused by the m-tiles of
     // their expert, which the tile order keeps close together in time
@@ -375,8 +492,15 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
       if (!warp_wait(&tempty[slot], (uint32_t(ti / BS_RING) & 1u) ^ 1u)) break;
       int4 tl = make_int4(-1, 0, 0, 0);
       if (lane == 0) {
-        const int t = args.tiles ? atomicAdd(args.next_tile, 1) : int(blockIdx.x) + ti * int(gridDim.x);
-        if (t < ntiles) tl = args.tiles ? args.tiles[t] : bs_dense_tile(args, t);
+        if constexpr (PAIR) {
+          // pairs of consecutive list entries (m-tiles 2i, 2i + 1 of one token tile) in a
+          // fixed stride over the clusters; rank r takes entry 2i + r
+          const int pi = int(cluster_id_x()) + ti * int(ncluster_x());
+          if (2 * pi + 1 < ntiles) tl = args.tiles[2 * pi + int(rank)];
+        } else {
+          const int t = args.tiles ? atomicAdd(args.next_tile, 1) : int(blockIdx.x) + ti * int(gridDim.x);
+          if (t < ntiles) tl = args.tiles ? args.tiles[t] : bs_dense_tile(args, t);
+        }
         ring[slot] = tl;
         mbar_arrive(&tfull[slot]);
       }
@@ -402,6 +526,26 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
         }
         uint8_t *sa = smem + Cfg::OFF_A + s * Cfg::A_BYTES;
         uint8_t *sb = smem + Cfg::OFF_B + s * Cfg::B_BYTES;
+        if constexpr (PAIR) {
+          // this CTA's weight rows (its m-tile), its half of the activation rows, its m-tile's
+          // weight scale atom and the whole tile's activation scale atoms, all completing on
+          // rank 0's barrier, which expects both CTAs' bytes
+          const int half = nmma >> 1, bih = bs_box(half);
+          const uint32_t xh_tx = bs_box_rows(bih) * BS_BK;
+          const uint32_t fb = mapa_rank(&full[s], 0);
+          if (rank == 0) mbar_arrive_expect_tx_el(&full[s], 2u * (W_TX + xh_tx + 512u + 1024u));
+          const int kx = kb * BS_BK;
+          tma_load_2d_pair_el(sa, &maps.w, fb, kx, int32_t(wrow0), pol_w);
+          if (EPI == BS_EPI_SWIGLU)
+            tma_load_2d_pair_el(sa + Cfg::A_SUB / 2, &maps.w2, fb, kx, int32_t(wrow0), pol_w);
+          tma_load_2d_pair_el(sb, &maps.x[bih], fb, kx, tl.z + int(rank) * half, pol_x);
+          tma_load_2d_pair_el(smem + Cfg::OFF_SFA + s * Cfg::SFA_BYTES, &maps.sfa, fb, 0,
+                              int32_t(((int64_t(tl.x) * args.mtiles + tl.y) * args.nkq + kb) * 2),
+                              pol_x);
+          tma_load_2d_pair_el(smem + Cfg::OFF_SFB + s * Cfg::SFB_BYTES, &maps.sfb, fb, 0,
+                              int32_t((int64_t(rtile) * args.nkq + kb) * 4), pol_x);
+          continue;
+        }
         {   // one elected lane of the converged warp issues (warp-uniform operands)
           mbar_arrive_expect_tx_el(&full[s], uint32_t(Cfg::KSUB) * (W_TX + x_tx) + sf_tx);
           if (args.sfa_atoms)
@@ -483,13 +627,26 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
         }
       }
     }
-    // every copy this warp issued has landed before the CTA can finish
-    for (int j = it - S < 0 ? 0 : it - S; j < it; ++j)
-      mbar_wait(&full[j % S], uint32_t(j / S) & 1u);
+    // every copy this warp issued has landed before the CTA can finish (in a pair, rank 1's
+    // copies complete on rank 0's barriers, which rank 0 drains before the final cluster
+    // barrier)
+    if (!PAIR || rank == 0)
+      for (int j = it - S < 0 ? 0 : it - S; j < it; ++j)
+        mbar_wait(&full[j % S], uint32_t(j / S) & 1u);
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer: the whole warp
     // runs the loop, one elect.sync lane issues
-    {
+    if (PAIR && rank != 0) {
+      // rank 1 of a pair issues nothing: it only releases its tile-ring slots
+      for (int ti = 0;; ++ti) {
+        const int slot = ti % BS_RING;
+        if (!warp_wait(&tfull[slot], uint32_t(ti / BS_RING) & 1u)) break;
+        const int4 tl = ring[slot];
+        if (tl.x < 0) break;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[slot]);
+      }
+    } else {
       int it = 0;
       for (int ti = 0;; ++ti) {
         const int slot = ti % BS_RING;
@@ -518,28 +675,45 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
             const uint32_t ta = t_sfa + 4u * ks, tb = t_sfb + 4u * Cfg::SFB_ATOMS * ks;
             const uint32_t s_sfa = sbase + Cfg::OFF_SFA + s * Cfg::SFA_BYTES + ks * 512;
             const uint32_t s_sfb = sbase + Cfg::OFF_SFB + s * Cfg::SFB_BYTES + ks * Cfg::SFB_SUB;
-            tc_cp_sf_el(ta, sdesc_sf(s_sfa));
-            tc_cp_sf_el(tb, sdesc_sf(s_sfb));
-            if (Cfg::SFB_ATOMS > 1 && nmma > 128) tc_cp_sf_el(tb + 4u, sdesc_sf(s_sfb + 512u));
             const uint64_t da = sdesc_sw128(sbase + Cfg::OFF_A + s * Cfg::A_BYTES + ks * Cfg::A_SUB);
             const uint64_t db = sdesc_sw128(sbase + Cfg::OFF_B + s * Cfg::B_BYTES + ks * Cfg::B_SUB);
+            if constexpr (PAIR) {
+              // both CTAs' scale atoms into both TMEMs, then M = 256 MMAs over both CTAs'
+              // weight rows and activation halves
+              tc_cp_sf_pair_el(ta, sdesc_sf(s_sfa));
+              tc_cp_sf_pair_el(tb, sdesc_sf(s_sfb));
+              if (nmma > 128) tc_cp_sf_pair_el(tb + 4u, sdesc_sf(s_sfb + 512u));
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              // +32 bytes along K inside the swizzle atom = +2 in the descriptor's address field
-              tc_mma_mx_el(tacc, da + uint64_t(2 * k), db + uint64_t(2 * k),
-                           idesc_mx(WFMT == BS_W_FP4 ? 5u : 0u, uint32_t(nmma), uint32_t(k)),
-                           ta | (uint32_t(k) << 30), tb | (uint32_t(k) << 30),
-                           (kb | ks | k) != 0 ? 1u : 0u);
+              for (int k = 0; k < 4; ++k)
+                tc_mma_mx_pair_el(tacc, da + uint64_t(2 * k), db + uint64_t(2 * k),
+                                  idesc_mx(WFMT == BS_W_FP4 ? 5u : 0u, uint32_t(nmma), uint32_t(k), 256u),
+                                  ta | (uint32_t(k) << 30), tb | (uint32_t(k) << 30),
+                                  (kb | ks | k) != 0 ? 1u : 0u);
+            } else {
+              tc_cp_sf_el(ta, sdesc_sf(s_sfa));
+              tc_cp_sf_el(tb, sdesc_sf(s_sfb));
+              if (Cfg::SFB_ATOMS > 1 && nmma > 128) tc_cp_sf_el(tb + 4u, sdesc_sf(s_sfb + 512u));
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                // +32 bytes along K inside the swizzle atom = +2 in the descriptor's address field
+                tc_mma_mx_el(tacc, da + uint64_t(2 * k), db + uint64_t(2 * k),
+                             idesc_mx(WFMT == BS_W_FP4 ? 5u : 0u, uint32_t(nmma), uint32_t(k)),
+                             ta | (uint32_t(k) << 30), tb | (uint32_t(k) << 30),
+                             (kb | ks | k) != 0 ? 1u : 0u);
+              }
             }
           }
-          tc_commit_el(&empty[s]);
+          if constexpr (PAIR) tc_commit_pair_both_el(&empty[s]);   // both CTAs refill
+          else tc_commit_el(&empty[s]);
         }
         if (!ok) break;
-        tc_commit_el(&acc_full[ab]);
+        if constexpr (PAIR) tc_commit_pair_both_el(&acc_full[ab]);   // both CTAs drain
+        else tc_commit_el(&acc_full[ab]);
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[slot]);
       }
-      tc_commit_el(mma_done);
+      if constexpr (PAIR) tc_commit_pair_el(mma_done);
+      else tc_commit_el(mma_done);
       warp_wait(mma_done, 0);
     }
     __syncwarp();
@@ -679,17 +853,26 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&acc_empty[ab]);
+        if (PAIR && rank != 0) mbar_arrive_cluster(mapa_rank(&acc_empty[ab], 0));
+        else mbar_arrive(&acc_empty[ab]);
         mbar_arrive(&tempty[slot]);
       }
       if (!ok) break;
     }
   }
   tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  if constexpr (PAIR) {
+    cluster_sync();   // no CTA leaves while the other may still reach its barriers or TMEM
+    if (warp == 1) {
+      tc_fence_after();
+      tmem_dealloc_pair(tmem, Cfg::TMEM_COLS);
+    }
+  } else {
+    __syncthreads();
+    if (warp == 1) {
+      tc_fence_after();
+      tmem_dealloc(tmem, Cfg::TMEM_COLS);
+    }
   }
 }
 

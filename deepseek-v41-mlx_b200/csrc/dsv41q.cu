@@ -1415,6 +1415,60 @@ int bs_launch(const char *name, const BsMaps &maps, const BsArgs &a, int grid, c
 
 int bs_grid(int tiles) { return tiles < num_sms() ? tiles : num_sms(); }
 
+// The 2-CTA form of the wide kernel: clusters of 2 CTAs, one pair of m-tiles a cluster at a
+// time (tiles from a grouped list whose m-tile count per token tile is even; every scale
+// operand as atoms, loaded through maps.sfa / maps.sfb).
+template <int WF, int EPI>
+int bs_launch_pair(const char *name, const BsMaps &maps, const BsArgs &a, cudaStream_t st) {
+  using Cfg = BsCfg<false, true>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(k_bsgemm<WF, EPI, false, true>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+    if (e != cudaSuccess) return cuda_status(e, "bsgemm pair smem attribute");
+    attr_set[dev] = true;
+  }
+  const int grid = num_sms() & ~1;
+  if (grid < 2) return DSV41_OK;
+  BsArgs g = a;
+  g.sf_async = 0;
+  g.nkb = a.nkb;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(grid));
+  cfg.blockDim = dim3(BS_THREADS);
+  cfg.dynamicSmemBytes = Cfg::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  ProfScope prof(name, st);
+  DSV41_LAUNCH(cudaLaunchKernelEx(&cfg, k_bsgemm<WF, EPI, false, true>, maps, g), name);
+  DSV41_CHECK_LAUNCH(name);
+  return DSV41_OK;
+}
+
+// scale atoms [..][512 bytes] as a 2D byte tensor of 256-byte rows, box {256, box_rows}
+int bs_atom_map(CUtensorMap *m, const uint8_t *atoms, size_t bytes, uint32_t box_rows) {
+  return make_tmap_2d(m, atoms, CU_TENSOR_MAP_DATA_TYPE_UINT8, 256, uint64_t(bytes / 256), 256,
+                      256, box_rows, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+// the 2-CTA wide kernel is on unless DSV41_NO_PAIR=1 (kept for comparisons)
+bool bs_pair_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char *e = getenv("DSV41_NO_PAIR");
+    on = (e && e[0] == '1') ? 0 : 1;
+  }
+  return on == 1;
+}
+
 // Dense problem: static tiles of 128 weight rows (64 + 64 in SwiGLU mode) x BN activation
 // rows, the narrow shape when all activation rows fit one narrow tile.
 template <int WF, int EPI>
@@ -1434,11 +1488,13 @@ int bs_dense_launch(const char *name, const BsMaps &maps, BsArgs a, int64_t N, i
 // Grouped problem: the wide tile list, then the narrow one, each taken from a work counter.
 template <int WF, int EPI>
 int bs_grouped_launch(const char *name_w, const char *name_n, const BsMaps &maps, BsArgs a,
-                      const PfPlan &plan, int list, cudaStream_t st) {
+                      const PfPlan &plan, int list, cudaStream_t st, bool pair = false) {
   a.tiles = plan.tiles[list];
   a.ntiles = plan.ntiles + list;
   a.next_tile = plan.next_tile + list;
-  int rc = bs_launch<WF, EPI, false>(name_w, maps, a, num_sms(), st);
+  int rc = (pair && bs_pair_enabled() && a.sfa_atoms && a.sfb_atoms)
+               ? bs_launch_pair<WF, EPI>(name_w, maps, a, st)
+               : bs_launch<WF, EPI, false>(name_w, maps, a, num_sms(), st);
   if (rc) return rc;
   a.tiles = plan.tiles[list + 1];
   a.ntiles = plan.ntiles + list + 1;
@@ -1833,8 +1889,15 @@ int pf_routed(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, const uin
     a.hs_atoms = ws.sfx_dn;
     a.ldh = d.I;
     a.limit = cfg->swiglu_limit;
+    // 2-CTA wide tiles: m-tiles of 64 gate + 64 up rows, taken two at a time
+    const bool pair = (d.I / 64) % 2 == 0;
+    if (pair) {
+      rc = bs_atom_map(&maps.sfa, packed, pf_packed_gu_bytes(cfg), 2);
+      if (!rc) rc = bs_atom_map(&maps.sfb, ws.sfx_gu, size_t(d.cap_rt) * (d.D / 128) * 1024, 4);
+      if (rc) return rc;
+    }
     rc = bs_grouped_launch<BS_W_FP4, BS_EPI_SWIGLU>("pf_gate_up_fp4", "pf_gate_up_fp4_narrow",
-                                                    maps, a, ws.plan, 0, st);
+                                                    maps, a, ws.plan, 0, st, pair);
     if (rc) return rc;
   }
   // routed down -> yp (bf16 per pair)
@@ -1854,8 +1917,14 @@ int pf_routed(const dsv41_moe_config *cfg, const dsv41_moe_weights *W, const uin
     a.sfb_atoms = ws.sfx_dn;
     a.out = ws.yp;
     a.ldo = d.D;
+    const bool pair = (d.D / BS_BM) % 2 == 0;
+    if (pair) {
+      rc = bs_atom_map(&maps.sfa, packed + pf_packed_gu_bytes(cfg), pf_packed_dn_bytes(cfg), 2);
+      if (!rc) rc = bs_atom_map(&maps.sfb, ws.sfx_dn, size_t(d.cap_rt) * (d.I / 128) * 1024, 4);
+      if (rc) return rc;
+    }
     rc = bs_grouped_launch<BS_W_FP4, BS_EPI_BF16>("pf_down_fp4", "pf_down_fp4_narrow", maps, a,
-                                                  ws.plan, 2, st);
+                                                  ws.plan, 2, st, pair);
     if (rc) return rc;
   }
 

@@ -156,8 +156,10 @@ __global__ void __launch_bounds__(1024) k_pf_scan(int *__restrict__ chunk_cnt, i
     for (int pj = 0; pj < 2; ++pj) {
       const int mt_n = mts[pj];
       int4 *tw = plan.tiles[2 * pj] + int64_t(s_excl_w[ee]) * mt_n;
+      // token tile by token tile, the m-tiles of one next to each other (a CTA pair takes
+      // m-tiles 2i and 2i + 1 of one token tile)
       for (int i = lane; i < mt_n * nw; i += 32) {
-        const int mt = i / nw, j = i % nw;
+        const int mt = i % mt_n, j = i / mt_n;
         tw[i] = make_int4(ee, mt, off + j * PF_TILE_ROWS,
                           min(PF_TILE_ROWS, rn - j * PF_TILE_ROWS) | ((r0 + j) << 8));
       }
