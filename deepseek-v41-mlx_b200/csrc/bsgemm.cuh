@@ -30,8 +30,14 @@
 //              Expert.forward (docs/reference/model.py:841-851) with linear() in a8 form
 //              (:181-207).
 //
+// 2-CTA form (PAIR, wide tiles of grouped lists): clusters of 2 CTAs take m-tiles 2i, 2i + 1
+// of one token tile; each CTA loads its weights and half of the activation rows, rank 0
+// issues tcgen05.mma.cta_group::2 (M = 256) for both, so each activation byte is read from L2
+// once per two m-tiles.
+//
 // Every wait is bounded (2 s); on expiry the device status flag is raised and the CTA
-// drains its own copies and MMAs before freeing TMEM.  No multicast anywhere.
+// drains its own copies and MMAs before freeing TMEM.  No copy is multicast (in the 2-CTA
+// form only MMA-completion arrivals reach both CTAs).
 #pragma once
 #include "act_quant.cuh"
 #include "common.cuh"
