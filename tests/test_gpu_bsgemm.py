@@ -127,8 +127,11 @@ def _cfg(args):
                 norm_topk_prob=True, route_scale=1.5, swiglu_limit=args.swiglu_limit)
 
 
+# (600, 4, 512, 128, 2) and (900, 4, 384, 256, 2) have wide tiles: the 2-CTA form runs both
+# wide launches of the first, and the gate/up one of the second (its down projection has 3
+# m-tiles, an odd count, and takes the 1-CTA form)
 @pytest.mark.parametrize("T,E,D,I,k", [(5, 8, 256, 128, 3), (70, 8, 256, 256, 3),
-                                       (600, 4, 512, 128, 2)])
+                                       (600, 4, 512, 128, 2), (900, 4, 384, 256, 2)])
 def test_moe_prefill_given_routing(cuda, T, E, D, I, k):
     rng = np.random.default_rng(T + E + D)
     p = moe_params(rng, E, D, I)
