@@ -2519,18 +2519,12 @@ extern "C" int dsv41_engram_hash(const int64_t *input_ids, int64_t B, int64_t L,
   DSV41_REQUIRE(input_ids && token_map && ids_cache && multipliers && primes && offsets && out,
                 DSV41_ERR_BAD_ARG, "NULL pointer");
   cudaStream_t st = STREAM(stream);
-  const int64_t n1 = B * L;
-  k_engram_compress<<<unsigned(ceil_div(n1, 256)), 256, 0, st>>>(input_ids, B, L, start_pos,
-                                                                 token_map, vocab, ids_cache,
-                                                                 max_seq);
-  DSV41_CHECK_LAUNCH("engram_compress");
-  const int64_t n2 = B * L * n_layers;
+  const int64_t n = B * L * n_layers * (max_ngram - 1) * n_heads;
   const size_t hash_smem = sizeof(uint64_t) * size_t(n_layers) * (max_ngram - 1) * n_heads;
   DSV41_REQUIRE(hash_smem <= 48 * 1024, DSV41_ERR_UNSUPPORTED, "too many hash primes");
-  k_engram_hash<<<unsigned(ceil_div(n2, 128)), 128, hash_smem, st>>>(B, L, start_pos, ids_cache, max_seq,
-                                                             multipliers, primes, offsets,
-                                                             n_layers, max_ngram, n_heads, pad_id,
-                                                             out);
+  k_engram_hash_cols<<<unsigned(ceil_div(n, 256)), 256, hash_smem, st>>>(
+      input_ids, B, L, start_pos, token_map, vocab, ids_cache, max_seq, multipliers, primes,
+      offsets, n_layers, max_ngram, n_heads, pad_id, out);
   DSV41_CHECK_LAUNCH("engram_hash");
   return DSV41_OK;
 }

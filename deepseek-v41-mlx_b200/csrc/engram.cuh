@@ -17,70 +17,63 @@
 
 namespace dsv41 {
 
-// step 1: compressed ids into the caller's cache (engram.py:163-164)
-__global__ void k_engram_compress(const int64_t *__restrict__ ids, int64_t B, int64_t L,
-                                  int64_t start, const int64_t *__restrict__ token_map,
-                                  int64_t vocab, int64_t *__restrict__ cache, int64_t max_seq) {
-  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (i >= B * L) return;
-  const int64_t b = i / L, l = i % L;
-  int64_t id = ids[i];
-  if (id < 0 || id >= vocab) {
-    dev_flag(DSV41_DEVST_BAD_INDEX);
-    id = 0;
-  }
-  cache[b * max_seq + start + l] = token_map[id];
-}
-
-// step 2: hashes; one thread per (b, l, layer).  x % p by Barrett reduction: with
-// m = floor((2^64 - 1) / p), q = hi64(x * m) is floor(x / p) or one less, so one
-// conditional subtraction gives the exact remainder (x < 2^63, p < 2^63).  The block
-// computes the m of every prime once into shared memory.
-__global__ void k_engram_hash(int64_t B, int64_t L, int64_t start,
-                              const int64_t *__restrict__ cache, int64_t max_seq,
-                              const int64_t *__restrict__ mult, const int64_t *__restrict__ primes,
-                              const int64_t *__restrict__ offsets, int nL, int G, int H,
-                              int64_t pad_id, int64_t *__restrict__ out) {
+// Hash (engram.py:163-180): compressed ids (engram.py:163-164) and the n-gram hashes in one
+// launch, one thread per (b, l, layer, column): column c = (shift - 1) * H + head hashes the
+// (shift + 1)-gram ending at its position, reading the compressed ids of
+// positions pos - s (s <= shift) from input_ids through token_map inside this call's
+// positions and from the cache before them (pad_id before position 0), as the hasher does;
+// the (layer 0, column 0) thread of each position writes that position's compressed id into
+// the cache.  The cache is read only below start and written only from start on.  x % p by
+// Barrett reduction: with m = floor((2^64 - 1) / p), q = hi64(x * m) is floor(x / p) or one
+// less, so one conditional subtraction gives the exact remainder (x < 2^63, p < 2^63); each
+// block computes the m of every prime once into shared memory.
+__global__ void k_engram_hash_cols(const int64_t *__restrict__ ids, int64_t B, int64_t L,
+                                   int64_t start, const int64_t *__restrict__ token_map,
+                                   int64_t vocab, int64_t *__restrict__ cache, int64_t max_seq,
+                                   const int64_t *__restrict__ mult,
+                                   const int64_t *__restrict__ primes,
+                                   const int64_t *__restrict__ offsets, int nL, int G, int H,
+                                   int64_t pad_id, int64_t *__restrict__ out) {
   extern __shared__ uint64_t s_recip[];   // [nL * (G - 1) * H]
-  const int np = nL * (G - 1) * H;
+  const int cols = (G - 1) * H;
+  const int np = nL * cols;
   for (int k = threadIdx.x; k < np; k += blockDim.x) {
     const uint64_t pk = uint64_t(primes[k]);
     s_recip[k] = pk > 1 ? ~0ull / pk : 0ull;
   }
   __syncthreads();
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (i >= B * L * nL) return;
-  const int layer = int(i % nL);
-  const int64_t bl = i / nL, b = bl / L, l = bl % L;
+  if (i >= B * L * np) return;
+  const int k = int(i % np);                            // layer * cols + column
+  const int64_t bl = i / np, b = bl / L, l = bl % L;
+  const int layer = k / cols, c = k % cols, shift = c / H + 1;
   const int64_t pos = start + l;
-  const int cols = (G - 1) * H;
-  int64_t *o = out + (bl * nL + layer) * cols;
-  const int64_t *mrow = mult + (int64_t)layer * G;
-  bool blocked = false;
-  int64_t rolling = 0;
-  for (int shift = 0; shift < G; ++shift) {
-    const int64_t src = pos - shift < 0 ? 0 : pos - shift;
-    blocked = blocked || (pos < shift);
-    const int64_t tok = blocked ? pad_id : cache[b * max_seq + src];
-    const int64_t prod = tok * mrow[shift];
-    rolling = shift == 0 ? prod : (rolling ^ prod);
-    if (shift >= 1) {
-      const int base = (layer * (G - 1) + (shift - 1)) * H;
-      const int64_t *of = offsets + (int64_t)layer * cols + (shift - 1) * H;
-      const uint64_t x = uint64_t(rolling);
-      for (int h = 0; h < H; ++h) {
-        const uint64_t p = uint64_t(primes[base + h]);
-        uint64_t r;
-        if (p > 1) {
-          r = x - __umul64hi(x, s_recip[base + h]) * p;
-          if (r >= p) r -= p;
-        } else {
-          r = 0;
-        }
-        o[(shift - 1) * H + h] = int64_t(r) + of[h];
-      }
+  const int64_t *bids = ids + b * L;
+  int64_t *bcache = cache + b * max_seq;
+  auto compressed = [&](int64_t q) -> int64_t {       // position q's compressed id, q <= pos
+    if (q < start) return bcache[q];
+    int64_t id = bids[q - start];
+    if (id < 0 || id >= vocab) {
+      dev_flag(DSV41_DEVST_BAD_INDEX);
+      id = 0;
     }
+    return token_map[id];
+  };
+  const int64_t *mrow = mult + (int64_t)layer * G;
+  int64_t rolling = 0;
+  for (int sh = 0; sh <= shift; ++sh) {
+    const int64_t tok = pos < sh ? pad_id : compressed(pos - sh);
+    const int64_t prod = tok * mrow[sh];
+    rolling = sh == 0 ? prod : (rolling ^ prod);
   }
+  const uint64_t x = uint64_t(rolling), pr = uint64_t(primes[k]);
+  uint64_t r = 0;
+  if (pr > 1) {
+    r = x - __umul64hi(x, s_recip[k]) * pr;
+    if (r >= pr) r -= pr;
+  }
+  out[bl * np + k] = int64_t(r) + offsets[k];
+  if (k == 0) bcache[pos] = compressed(pos);
 }
 
 // 8 consecutive outputs from one 16-byte (bf16) or 32-byte (fp32) store.
@@ -172,20 +165,46 @@ __device__ __forceinline__ uint64_t f32x2_fma(uint64_t a, uint64_t b, uint64_t c
   return d;
 }
 
-// acc2[q] += the row's codes (cw bytes as 32-bit words w) x 2^(sb - 127), column pairs q.
-// e4m3 x a power of two is exact in fp32 whenever the scale byte is below 240 (no
-// overflow; the smallest product, 2^-9 x 2^-127, is still a whole multiple of 2^-149), so
-// there one fused multiply-add gives the bits of the reference's rounded product then
-// rounded sum.  From 240 on a product can overflow to infinity, and the reference's sum
-// then sees that infinity (inf + -inf = NaN, inf + finite = inf): those rows take scalar
-// __fmul_rn / __fadd_rn, which are never contracted into a fused multiply-add (the packed
-// f32x2 multiply followed by the packed add measured as fused here: an overflowing
-// product came back finite).
+// The row scale 2^(sb - 127) as the accumulation takes it: the f16 bits of the scale when it
+// is an f16 (sb in [103, 142], the scales real tables use), else 0x10000 | sb.
+constexpr uint32_t GS_SV_ONE = 0x3C00u;               // 1.0: the scale of a skipped row
+__device__ __forceinline__ uint32_t gs_sv(uint32_t sb) {
+  return sb - 103u <= 39u ? (sb >= 113u ? (sb - 112u) << 10 : 1u << (sb - 103u))
+                          : (0x10000u | sb);
+}
+
+// a[j] += code j of the row (NW 32-bit words w) x its scale sv (gs_sv), in fp32 with the
+// reference's roundings: its product, rounded, then its sum, rounded.
+// f16 scale: the codes stay f16 and the mixed-precision fused multiply-add
+// (`fma.rn.f32.f16`, sm_100) forms the exact product of code and scale and adds it to the
+// fp32 sum with one rounding -- the same bits, since that product is exact.  Other scales:
+// e4m3 x a power of two is exact in fp32 whenever the scale byte is below 240 (no overflow;
+// the smallest product, 2^-9 x 2^-127, is still a whole multiple of 2^-149), so there one
+// fp32 fused multiply-add gives the same bits.  From 240 on a product can overflow to
+// infinity, and the reference's sum then sees that infinity (inf + -inf = NaN, inf + finite =
+// inf): those rows take __fmul_rn / __fadd_rn, which are never contracted into a fused
+// multiply-add.  A skipped row (codes 0, scale 1) adds +0.0, which leaves every sum as it was
+// (a sum that starts at +0.0 is never -0.0).
 template <int NW>
-__device__ __forceinline__ void gs_accum(uint64_t (&acc2)[2 * NW], const uint32_t (&w)[NW],
-                                         uint32_t sb) {
-  const float s = e8m0f(uint8_t(sb));
-  const uint64_t s2 = f32x2(s, s);
+__device__ __forceinline__ void gs_accum(float (&a)[4 * NW], const uint32_t (&w)[NW],
+                                         uint32_t sv) {
+  if (sv < 0x10000u) {
+    const uint16_t s16 = uint16_t(sv);
+#pragma unroll
+    for (int k = 0; k < NW; ++k) {
+      uint32_t hq[2];
+      e4m3x4_to_f16x4(w[k], hq[0], hq[1]);
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+        asm("{\n\t.reg .b16 a, b;\n\tmov.b32 {a, b}, %2;\n\t"
+            "fma.rn.f32.f16 %0, a, %3, %0;\n\tfma.rn.f32.f16 %1, b, %3, %1;\n\t}"
+            : "+f"(a[4 * k + 2 * j]), "+f"(a[4 * k + 2 * j + 1])
+            : "r"(hq[j]), "h"(s16));
+    }
+    return;
+  }
+  const uint32_t sb = sv & 0xFFu;
+  const float s = e8m0f(sb);
 #pragma unroll
   for (int k = 0; k < NW; ++k) {
     uint32_t hq[2];
@@ -193,26 +212,27 @@ __device__ __forceinline__ void gs_accum(uint64_t (&acc2)[2 * NW], const uint32_
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       const float2 p = h2f2(hq[j]);
+      float &lo = a[4 * k + 2 * j], &hi = a[4 * k + 2 * j + 1];
       if (sb < 240u) {
-        acc2[2 * k + j] = f32x2_fma(f32x2(p.x, p.y), s2, acc2[2 * k + j]);
+        lo = __fmaf_rn(p.x, s, lo);
+        hi = __fmaf_rn(p.y, s, hi);
       } else {
-        const float lo = __fadd_rn(f32x2_lo(acc2[2 * k + j]), __fmul_rn(p.x, s));
-        const float hi = __fadd_rn(f32x2_hi(acc2[2 * k + j]), __fmul_rn(p.y, s));
-        acc2[2 * k + j] = f32x2(lo, hi);
+        lo = __fadd_rn(lo, __fmul_rn(p.x, s));
+        hi = __fadd_rn(hi, __fmul_rn(p.y, s));
       }
     }
   }
 }
 
-// Sums into acc2 (the 8 columns of this lane, as fp32 pairs) the nh <= 32 rows whose ids
-// lane l holds in `mine` (-1 past the token's ids), in lane order: each lane resolves its
-// own row once (pointers and range, and its scale byte when the warp's columns share one
-// scale block, `uscale`), then the rows are read 8 at a time, the pointers broadcast by
-// shuffle, 8-byte streaming loads a lane.  Rows outside the table are skipped.
+// Sums into acc (the 8 columns of this lane) the nh <= 32 rows whose ids lane l holds in
+// `mine` (-1 past the token's ids), in lane order: each lane resolves its own row once
+// (pointers and range, and its scale when the warp's columns share one scale block,
+// `uscale`), then the rows are read 8 at a time, the pointers broadcast by shuffle, 8-byte
+// streaming loads a lane.  Rows outside the table add nothing (codes 0, scale 1).
 // (16-byte loads, two warps a 1 KB row, measured slower: 0.072 against 0.066 ms for 8192
 // tokens of 24 rows.)
 template <bool PEERS>
-__device__ __forceinline__ void gs_rows(uint64_t (&acc2)[4], int64_t mine, int nh,
+__device__ __forceinline__ void gs_rows(float (&acc)[8], int64_t mine, int nh,
                                         int64_t col, int soff, bool uscale,
                                         const uint8_t *__restrict__ table,
                                         const uint8_t *__restrict__ scale, int64_t rows,
@@ -225,11 +245,11 @@ __device__ __forceinline__ void gs_rows(uint64_t (&acc2)[4], int64_t mine, int n
   const bool in_m = gs_row<PEERS>(mine, rt_m, rs_m, table, scale, rows, row_lo, tld, sld, tabs,
                                   scs, nsh, total);
   const unsigned inmask = __ballot_sync(0xffffffffu, in_m);
-  const uint32_t sb_m = (uscale && in_m) ? uint32_t(rs_m[soff]) : 0u;
+  const uint32_t sv_m = (uscale && in_m) ? gs_sv(uint32_t(rs_m[soff])) : GS_SV_ONE;
   const uint64_t pt_m = reinterpret_cast<uint64_t>(rt_m), ps_m = reinterpret_cast<uint64_t>(rs_m);
   for (int h = 0; h < nh; h += 8) {               // h + u <= 31: every source lane exists
     uint32_t w[8][NW];
-    uint32_t sb[8];
+    uint32_t sv[8];
     // the batch's row loads first: nothing in front of them waits on a load
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
@@ -240,36 +260,22 @@ __device__ __forceinline__ void gs_rows(uint64_t (&acc2)[4], int64_t mine, int n
       w[u][0] = uint32_t(v);
       w[u][1] = uint32_t(v >> 32);
     }
-    // then the scale bytes: broadcast from the row's own lane, or loaded per lane when the
-    // warp's columns span several scale blocks
+    // then the scales: broadcast from the row's own lane, or loaded per lane when the warp's
+    // columns span several scale blocks
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int src = h + u;
       if (uscale) {
-        sb[u] = __shfl_sync(0xffffffffu, sb_m, src);
+        sv[u] = __shfl_sync(0xffffffffu, sv_m, src);
       } else {
         const bool in = (inmask >> src) & 1u;
         const uint8_t *rs = reinterpret_cast<const uint8_t *>(__shfl_sync(0xffffffffu, ps_m, src));
-        sb[u] = in ? uint32_t(rs[soff]) : 0u;
+        sv[u] = in ? gs_sv(uint32_t(rs[soff])) : GS_SV_ONE;
       }
     }
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      if (!((inmask >> (h + u)) & 1u)) continue;
-      gs_accum<NW>(acc2, w[u], sb[u]);
-    }
+    for (int u = 0; u < 8; ++u) gs_accum<NW>(acc, w[u], sv[u]);
   }
-}
-
-template <typename T>
-__device__ __forceinline__ void gs_store(T *o, const uint64_t (&acc2)[4]) {
-  float acc[8];
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    acc[2 * q] = f32x2_lo(acc2[q]);
-    acc[2 * q + 1] = f32x2_hi(acc2[q]);
-  }
-  store8(o, acc);
 }
 
 // Warps per token = d / 256: a warp covers 256 columns, its lanes 8-column chunks at
@@ -298,19 +304,19 @@ __global__ void __launch_bounds__(256, 4) k_engram_gather_sum(
   const int64_t col = (gw % wpt) * 256 + lane * 8;
   const int soff = int(col / block);            // 8 | block keeps a chunk in one scale block
   const bool uscale = block % 256 == 0;         // the warp's columns share one scale block
-  uint64_t acc2[4] = {};                        // columns (2q, 2q + 1) as fp32 pairs
+  float acc[8] = {};
   const int64_t *ti = idx + tok * n_per_tok;
   for (int h0 = 0; h0 < n_per_tok; h0 += 32) {
     // lane l holds id h0 + l (-1 past the token's ids)
     const int64_t mine = h0 + lane < n_per_tok ? ti[h0 + lane] : -1;
-    gs_rows<PEERS>(acc2, mine, min(32, n_per_tok - h0), col, soff, uscale, table, scale, rows,
+    gs_rows<PEERS>(acc, mine, min(32, n_per_tok - h0), col, soff, uscale, table, scale, rows,
                    row_lo, tld, sld, tabs, scs, nsh, total);
   }
-  gs_store(out + tok * D + col, acc2);
+  store8(out + tok * D + col, acc);
 }
 
 // a15 + a16 in one pass: the (G-1)*H <= 32 row ids of each position of one hash layer
-// (k_engram_compress + k_engram_hash, same arithmetic) computed by the lanes that would have
+// (k_engram_hash_cols, same arithmetic) computed by the lanes that would have
 // loaded them, summed as rows of a packed table (codes then scale bytes, rb bytes a row).
 // Lane c < (G-1)*H hashes column c = (shift-1)*H + head: the compressed ids of positions
 // pos - s (s <= shift) come from input_ids through token_map inside this call's positions and
@@ -385,10 +391,10 @@ __global__ void __launch_bounds__(256, 4) k_engram_lookup_sum(
   const int64_t col = (gw % wpt) * 256 + lane * 8;
   const int soff = int(col / block);
   const bool uscale = block % 256 == 0;
-  uint64_t acc2[4] = {};
-  gs_rows<PEERS>(acc2, mine, cols, col, soff, uscale, table, scale, rows, row_lo, tld, sld, tabs,
+  float acc[8] = {};
+  gs_rows<PEERS>(acc, mine, cols, col, soff, uscale, table, scale, rows, row_lo, tld, sld, tabs,
                  scs, nsh, total);
-  gs_store(out + tok * D + col, acc2);
+  store8(out + tok * D + col, acc);
 }
 
 // Row-sharded tables: the owner of rows [row_lo, row_lo + rows) copies the raw rows

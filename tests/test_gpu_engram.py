@@ -92,17 +92,19 @@ def test_gather_rows_golden(cuda):
     assert bits_equal(got, g["out"])
 
 
+# T=400: more tokens than the GPU holds warps at once
 @pytest.mark.parametrize("d,block", [(256, 32), (1024, 1024), (512, 64), (1024, 32)])
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
-def test_gather_sum_every_scale_and_code(cuda, d, block, dtype):
+@pytest.mark.parametrize("T", [29, 400])
+def test_gather_sum_every_scale_and_code(cuda, d, block, dtype, T):
     """Every ue8m0 byte (0 .. 255: subnormal to infinite scales, where products overflow) and
     every e4m3 code (NaN included), plain and packed rows: the bits of the oracle's rounded
     product then rounded sum, NaN for NaN."""
-    rng = np.random.default_rng(7 * d + block)
+    rng = np.random.default_rng(7 * d + block + T)
     rows = 3000
     table = rng.integers(0, 256, size=(rows, d), dtype=np.uint8)
     scale = rng.integers(0, 256, size=(rows, d // block), dtype=np.uint8)
-    idx = rng.integers(0, rows, size=(29, 24))
+    idx = rng.integers(0, rows, size=(T, 24))
     tdt = torch.float32 if dtype == "f32" else torch.bfloat16
     want = OE.gather_sum(table, scale, idx, block, dtype)
     for packed in (False, True):
@@ -252,13 +254,17 @@ def test_engram_module_fp8_wkv(cuda):
     assert rel_fro(got.reshape(B * Lq, hc, D), want) < 1e-2
 
 
-@pytest.mark.parametrize("d,block,row_lo", [(1024, 1024, 0), (256, 32, 0), (512, 64, 700)])
-def test_packed_table_lookups_identical(cuda, d, block, row_lo):
+# up to 1000 tokens, up to 32 rows a token, a single row, rows off the shard
+@pytest.mark.parametrize("d,block,row_lo,T,H", [(1024, 1024, 0, 29, 24), (256, 32, 0, 29, 24),
+                                                (512, 64, 700, 29, 24), (1024, 1024, 0, 700, 24),
+                                                (1024, 128, 300, 500, 32), (512, 64, 0, 333, 1),
+                                                (256, 256, 50, 1000, 7)])
+def test_packed_table_lookups_identical(cuda, d, block, row_lo, T, H):
     """A table stored as packed rows (EngramEmbedding.pack) gives the same bits as the codes
     and scales stored apart, for the summed and the per-row lookups; ids outside this shard
     read zero rows either way."""
-    rng = np.random.default_rng(d + row_lo)
-    rows, T, H = 3000, 29, 24
+    rng = np.random.default_rng(d + row_lo + T)
+    rows = 3000
     table = rng.integers(0, 256, size=(rows, d), dtype=np.uint8)
     table[(table & 0x7F) == 0x7F] = 0
     scale = rng.integers(112, 130, size=(rows, d // block), dtype=np.uint8)
