@@ -13,6 +13,7 @@
 #include "quantize.cuh"
 #include "aqgemm.cuh"
 #include "a16gemm.cuh"
+#include "gemv_m1.cuh"
 
 #include <mutex>
 
@@ -541,6 +542,26 @@ extern "C" int dsv41_gemv_affine(const void *x, int64_t M, int64_t K, const uint
   DSV41_REQUIRE(bits == 4 || bits == 8, DSV41_ERR_UNSUPPORTED,
                 "gemv_affine supports bits 4 and 8 (group 64)");
   DSV41_REQUIRE((scales && biases) || M == 0 || N == 0, DSV41_ERR_BAD_ARG, "NULL scales/biases");
+  // one activation row, 4-bit: the CUDA-core kernel (no activation prep, no workspace use)
+  if (bits == 4 && M == 1 && N > 0 && K > 0 && K % 64 == 0 && K <= 16384 && x && wq && y &&
+      aligned(x, 16) && aligned(wq, 16) && (out_dtype == DSV41_F32 || out_dtype == DSV41_BF16)) {
+    DSV41_REQUIRE(N <= (int64_t)INT32_MAX, DSV41_ERR_BAD_SHAPE, "shape too large");
+    cudaStream_t st = STREAM(stream);
+    const int64_t want = ceil_div(N, int64_t(GM1_THREADS / 32));
+    const unsigned grid = unsigned(std::min<int64_t>(want, 4 * int64_t(num_sms())));
+    const size_t smem = size_t(K) * 2 + size_t(K / 32) * 4;
+    ProfScope prof("gemv_affine4_m1", st);
+    const uint16_t *xs = static_cast<const uint16_t *>(x);
+    const uint16_t *sc = static_cast<const uint16_t *>(scales);
+    const uint16_t *bi = static_cast<const uint16_t *>(biases);
+    if (out_dtype == DSV41_F32)
+      k_gemv_affine4_m1<float><<<grid, GM1_THREADS, smem, st>>>(xs, K, wq, sc, bi, N, (float *)y);
+    else
+      k_gemv_affine4_m1<__nv_bfloat16><<<grid, GM1_THREADS, smem, st>>>(xs, K, wq, sc, bi, N,
+                                                                       (__nv_bfloat16 *)y);
+    DSV41_CHECK_LAUNCH("gemv_affine4_m1");
+    return DSV41_OK;
+  }
   if (bits == 4)
     return gemv_common<WF_AFF4>(x, M, K, wq, K / 2, nullptr, K / 64, scales, biases, N, out_dtype,
                                 y, workspace, workspace_bytes, STREAM(stream));

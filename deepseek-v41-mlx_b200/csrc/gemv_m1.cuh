@@ -1,0 +1,150 @@
+// gemv_m1.cuh -- one activation row times an MLX affine 4-bit weight (a14 at M = 1).
+//
+// y[n] = sum_g ( s[n,g] * sum_{k in g} q[n,k] x[k]  +  b[n,g] * sum_{k in g} x[k] ), the form
+// mx.quantized_matmul evaluates (deepseek_v41_mlx/load.py:124-131): per 64-code group the
+// scale times the codes' dot product with x, plus the bias times the sum of x.  With a single
+// activation row the tensor-core engine (qgemv.cuh) computes 8 columns for every useful one and
+// needs a separate activation-prep launch; here the CUDA cores do it in one launch:
+//   * every CTA copies x (bf16) into shared memory once, in an order that matches how the codes
+//     are unpacked (see below), together with the fp32 sum of each 32-code chunk of x;
+//   * a warp takes one weight row at a time, each lane 16-byte streaming loads of 32 codes
+//     (lane l: chunks l, l + 32, ... of the row -- coalesced 512-byte spans), all of the
+//     lane's loads in flight before the first is used;
+//   * codes become exact bf16 through the 0x4300 exponent (bf16 128 + q, minus 128 in one
+//     bf16x2 subtract), two codes a word k and k + 4 of each 8-code word;
+//   * sm_100's mixed-precision `fma.rn.f32.bf16` multiplies a bf16 code by a bf16 activation
+//     exactly and adds the product to an fp32 sum with one rounding;
+//   * the lane folds scale and bias per chunk in fp32, the warp sums its lanes in a fixed
+//     butterfly order, lane 0 stores.
+// Deterministic: every order is fixed by the shapes alone.
+#pragma once
+#include "common.cuh"
+
+namespace dsv41 {
+
+constexpr int GM1_THREADS = 256;
+constexpr int GM1_U = 8;              // 16-byte chunks a lane keeps in flight per row
+
+// a0 += q.lo * x.lo, a1 += q.hi * x.hi (bf16 halves; exact products, fp32 sums)
+__device__ __forceinline__ void gm1_fma2(uint32_t q2, uint32_t x2, float &a0, float &a1) {
+  asm("{\n\t.reg .b16 q0, q1, x0, x1;\n\tmov.b32 {q0, q1}, %2;\n\tmov.b32 {x0, x1}, %3;\n\t"
+      "fma.rn.f32.bf16 %0, q0, x0, %0;\n\tfma.rn.f32.bf16 %1, q1, x1, %1;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "r"(q2), "r"(x2));
+}
+
+// codes of nibbles j and j + 4 of w (MLX packs code 8i + j at bits 4j of word i) as exact
+// bf16x2: (0x4300 | q) is bf16 128 + q, minus 128
+__device__ __forceinline__ uint32_t gm1_pair(uint32_t w, int j) {
+  const uint32_t t = ((w >> (4 * j)) & 0x000F000Fu) | 0x43004300u;
+  uint32_t r;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(t), "r"(0x43004300u));
+  return r;
+}
+
+// x: [K] bf16 (16-byte aligned); wq: [N, K/8] u32 rows (16-byte aligned); scales, biases:
+// [N, K/64] bf16; K % 64 == 0, K <= 16384.  Dynamic shared memory: 2K + 4(K/32) bytes.
+template <typename TO>
+__global__ void __launch_bounds__(GM1_THREADS, 4) k_gemv_affine4_m1(
+    const uint16_t *__restrict__ x, int64_t K, const uint32_t *__restrict__ wq,
+    const uint16_t *__restrict__ scales, const uint16_t *__restrict__ biases, int64_t N,
+    TO *__restrict__ y) {
+  extern __shared__ __align__(16) uint8_t gm1_smem[];
+  const int nch = int(K / 32);                     // 16-byte code chunks a row
+  // x as 16-byte segments: the 8 activations of word i of chunk c (x[32c + 8i ..]) at
+  // xt[i * nch + c], as words (x0, x4), (x1, x5), (x2, x6), (x3, x7) -- the code pairs that
+  // gm1_pair produces; a warp's lanes then read consecutive segments
+  uint4 *xt = reinterpret_cast<uint4 *>(gm1_smem);
+  float *xsum = reinterpret_cast<float *>(gm1_smem + size_t(K) * 2);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = int(K / 64);
+  const int64_t row0 = int64_t(blockIdx.x) * (GM1_THREADS / 32) + warp;
+  const int64_t rstride = int64_t(gridDim.x) * (GM1_THREADS / 32);
+  // the first row's loads go out before the set-up below: the lane's GM1_U code chunks, and
+  // the scale and bias of groups c0/2 + 32j + lane (j < GM1_U/2), which the chunks' lanes take
+  // by shuffle (chunk c belongs to group c/2)
+  uint4 v[GM1_U];
+  uint32_t sbv[GM1_U / 2];                         // scale bits << 16 | bias bits
+  auto load_row = [&](int64_t r, int c0) {
+    const uint4 *wr = reinterpret_cast<const uint4 *>(wq + r * (K / 8));
+#pragma unroll
+    for (int u = 0; u < GM1_U; ++u) {
+      const int c = c0 + u * 32 + lane;
+      v[u] = (r < N && c < nch) ? __ldcs(wr + c) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int j = 0; j < GM1_U / 2; ++j) {
+      const int g = c0 / 2 + 32 * j + lane;
+      sbv[j] = (r < N && g < G) ? (uint32_t(__ldcs(scales + r * G + g)) << 16) |
+                                      uint32_t(__ldcs(biases + r * G + g))
+                                : 0u;
+    }
+  };
+  load_row(row0, 0);
+  for (int s = threadIdx.x; s < 4 * nch; s += GM1_THREADS) {
+    const int c = s >> 2, i = s & 3;
+    const uint4 in = __ldg(reinterpret_cast<const uint4 *>(x) + (c * 4 + i));
+    uint4 o;
+    o.x = __byte_perm(in.x, in.z, 0x5410);
+    o.y = __byte_perm(in.x, in.z, 0x7632);
+    o.z = __byte_perm(in.y, in.w, 0x5410);
+    o.w = __byte_perm(in.y, in.w, 0x7632);
+    xt[i * nch + c] = o;
+  }
+  __syncthreads();
+  // chunk sums of x in the segments' order (word by word, lo halves then hi halves)
+  for (int c = threadIdx.x; c < nch; c += GM1_THREADS) {
+    float sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 xv = xt[i * nch + c];
+      const uint32_t wv[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) sum += __uint_as_float(wv[j] << 16);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) sum += __uint_as_float(wv[j] & 0xFFFF0000u);
+    }
+    xsum[c] = sum;
+  }
+  __syncthreads();
+  for (int64_t r = row0; r < N; r += rstride) {
+    float acc = 0.0f;
+    for (int c0 = 0; c0 < nch; c0 += 32 * GM1_U) {
+      if (c0 > 0) load_row(r, c0);
+#pragma unroll
+      for (int u = 0; u < GM1_U; ++u) {
+        if (c0 + u * 32 >= nch) break;                 // warp-uniform
+        const int c = c0 + u * 32 + lane;
+        // group c/2 - c0/2 = 16u + lane/2: word u/2 of lane (16(u&1) + lane/2)
+        const uint32_t sb = __shfl_sync(0xffffffffu, sbv[u >> 1], 16 * (u & 1) + (lane >> 1));
+        if (c >= nch) continue;
+        const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+        float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint4 xv = xt[i * nch + c];
+          gm1_fma2(gm1_pair(w[i], 0), xv.x, a0, a1);
+          gm1_fma2(gm1_pair(w[i], 1), xv.y, a0, a1);
+          gm1_fma2(gm1_pair(w[i], 2), xv.z, a0, a1);
+          gm1_fma2(gm1_pair(w[i], 3), xv.w, a0, a1);
+        }
+        const float s = __uint_as_float(sb & 0xFFFF0000u);
+        const float b = __uint_as_float(sb << 16);
+        acc = __fmaf_rn(s, a0 + a1, acc);
+        acc = __fmaf_rn(b, xsum[c], acc);
+      }
+    }
+    // the next row's loads go out before this row's reduction
+    if (r + rstride < N) load_row(r + rstride, 0);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) {
+      if constexpr (sizeof(TO) == 4)
+        y[r] = acc;
+      else
+        y[r] = __float2bfloat16_rn(acc);
+    }
+  }
+}
+
+}  // namespace dsv41
