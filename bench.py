@@ -309,8 +309,12 @@ def d1_measure(q, torch, dev, flush, stream, K, W, peaks, ms_list=(1, 32)):
         gr = graphed(torch, [lambda c=c: q.linear.linear_fp8(x, ws[c], ss[c]) for c in range(copies)])
         st = statistics.mean(timed_steps(torch, lambda i: gr[i % copies].replay(), K * 4, W, flush,
                                          stream))
+        # one activation row: the single-launch CUDA-core kernel; more: the tensor-core engine
+        kname = "gemv_fp8_m1" if M == 1 else "qgemv_dense"
+        klabel = ("gemv_fp8_m1 (k_gemv_fp8_m1)" if M == 1
+                  else "qgemv_dense (k_qgemv<FP8B,1,NT>)")
         kt = kernel_ms(q, torch, lambda i: q.linear.linear_fp8(x, ws[i % copies], ss[i % copies]),
-                       ["qgemv_dense", "qx_prep"], K * 2, flush, stream)
+                       [kname, "qx_prep"], K * 2, flush, stream)
         # the GEMV over the 10 weight copies back to back in one graph (a decode step runs
         # many such products in a row): time per GEMV
         chain = graphed(torch, [lambda: [q.linear.linear_fp8(x, ws[c], ss[c])
@@ -323,7 +327,7 @@ def d1_measure(q, torch, dev, flush, stream, K, W, peaks, ms_list=(1, 32)):
         e_ms, bi, bo = e2e_measure(torch, lambda i: q.linear.linear_fp8(xd, ws[i % copies],
                                                                          ss[i % copies]),
                                    xh, [xd], yh, K * 2, W, flush, stream)
-        gk = kt.get("qgemv_dense", (0, None))[1]
+        gk = kt.get(kname, (0, None))[1]
         out[f"gemv_fp8_block_M{M}"] = {
             "config": f"BASELINE.json configs[0]: fp8 e4m3 [{N} x {Kd}], ue8m0 32x32, M={M}, "
                       f"bf16 out; {copies} weight copies rotated",
@@ -333,8 +337,8 @@ def d1_measure(q, torch, dev, flush, stream, K, W, peaks, ms_list=(1, 32)):
             "chained_ms": round(stc, 5), "chained_gbs": round(byts / stc / 1e6, 1),
             "chained_frac_hbm": round(byts / stc / 1e6 / hbm, 4),
             "kernel_ms": {k: round(v[1], 5) for k, v in kt.items()},
-            "roofline": _roofline("hbm", "qgemv_dense (k_qgemv<FP8B,1,NT>)", byts, gk, hbm,
-                                  src + " hbm_gbs (copy)", _traffic(f"qgemv_dense_fp8_M{M}")),
+            "roofline": _roofline("hbm", klabel, byts, gk, hbm,
+                                  src + " hbm_gbs (copy)", _traffic(f"{kname}_fp8_M{M}")),
             "e2e": {"value": round(byts / e_ms / 1e6, 1), "unit": "GB/s", "ms": round(e_ms, 5),
                     "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo,
                     "api": "linear.linear_fp8"},

@@ -523,6 +523,24 @@ extern "C" int dsv41_gemv_fp8_block(const void *x, int64_t M, int64_t K, const u
                                     const uint8_t *s, int64_t N, int out_dtype, void *y,
                                     void *workspace, size_t workspace_bytes, void *stream) {
   DSV41_REQUIRE(s || M == 0 || N == 0, DSV41_ERR_BAD_ARG, "scale is NULL");
+  // one activation row: the CUDA-core kernel (no activation prep, no workspace use)
+  if (M == 1 && N > 0 && K > 0 && K % 32 == 0 && K <= 16384 && x && w && y && aligned(x, 16) &&
+      aligned(w, 16) && (out_dtype == DSV41_F32 || out_dtype == DSV41_BF16)) {
+    DSV41_REQUIRE(N <= (int64_t)INT32_MAX, DSV41_ERR_BAD_SHAPE, "shape too large");
+    cudaStream_t st = STREAM(stream);
+    const int64_t want = ceil_div(N, int64_t(GM1_THREADS / 32));
+    const unsigned grid = unsigned(std::min<int64_t>(want, 2 * int64_t(num_sms())));
+    ProfScope prof("gemv_fp8_m1", st);
+    const uint16_t *xs = static_cast<const uint16_t *>(x);
+    if (out_dtype == DSV41_F32)
+      k_gemv_fp8_m1<float><<<grid, GM1_THREADS, size_t(K) * 2, st>>>(xs, K, w, s, K / 32, N,
+                                                                     (float *)y);
+    else
+      k_gemv_fp8_m1<__nv_bfloat16><<<grid, GM1_THREADS, size_t(K) * 2, st>>>(
+          xs, K, w, s, K / 32, N, (__nv_bfloat16 *)y);
+    DSV41_CHECK_LAUNCH("gemv_fp8_m1");
+    return DSV41_OK;
+  }
   return gemv_common<WF_FP8B>(x, M, K, w, K, s, ceil_div(K, 32), nullptr, nullptr, N, out_dtype,
                               y, workspace, workspace_bytes, STREAM(stream));
 }

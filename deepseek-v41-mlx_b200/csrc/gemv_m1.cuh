@@ -1,5 +1,7 @@
-// gemv_m1.cuh -- one activation row times an MLX affine 4-bit weight (a14 at M = 1).
+// gemv_m1.cuh -- one activation row times a quantized weight on the CUDA cores: MLX affine
+// 4-bit (a14 at M = 1) and fp8 e4m3 with 32 x 32 block scales (a13's dense linear at M = 1).
 //
+// Affine:
 // y[n] = sum_g ( s[n,g] * sum_{k in g} q[n,k] x[k]  +  b[n,g] * sum_{k in g} x[k] ), the form
 // mx.quantized_matmul evaluates (deepseek_v41_mlx/load.py:124-131): per 64-code group the
 // scale times the codes' dot product with x, plus the bias times the sum of x.  With a single
@@ -136,6 +138,148 @@ __global__ void __launch_bounds__(GM1_THREADS, 4) k_gemv_affine4_m1(
     }
     // the next row's loads go out before this row's reduction
     if (r + rstride < N) load_row(r + rstride, 0);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) {
+      if constexpr (sizeof(TO) == 4)
+        y[r] = acc;
+      else
+        y[r] = __float2bfloat16_rn(acc);
+    }
+  }
+}
+
+// a0 += h.lo * xh.lo, a1 += h.hi * xh.hi (f16 halves; exact products, fp32 sums)
+__device__ __forceinline__ void gm1_fma2_f16(uint32_t h, uint32_t xh, float &a0, float &a1) {
+  asm("{\n\t.reg .b16 q0, q1, x0, x1;\n\tmov.b32 {q0, q1}, %2;\n\tmov.b32 {x0, x1}, %3;\n\t"
+      "fma.rn.f32.f16 %0, q0, x0, %0;\n\tfma.rn.f32.f16 %1, q1, x1, %1;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "r"(h), "r"(xh));
+}
+
+// One activation row times an fp8 e4m3 weight with ue8m0 scales per 32 x 32 block (upstream
+// `weight_dequant` then the product; the d1 dense linear at decode).  The same arithmetic as
+// the tensor-core engine's single-row case, without its activation-prep launch: every CTA
+// finds the row's max |x|, keeps x * 2^-E as f16 in shared memory (E = exponent(max) - 14, the
+// engine's per-row multiplier: exact for bf16 values within 2^29 of the max), and per 32-code
+// block sums code x activation products (`cvt.rn.f16x2.e4m3x2`, then the mixed-precision
+// `fma.rn.f32.f16`: exact products, fp32 sums), folds the block scale (byte 0 applied as 0, as
+// the engine does) and finally 2^E.  A warp takes a row at a time, lane l the 16-code chunks
+// l, l + 32, ...; its 16 chunk slots (a whole row at K <= 8192) are refilled one step ahead (the
+// same slot of the next 512 chunks of the row, or of its next row) as soon as they are
+// consumed, so up to 8 KB of codes per warp stay in flight.  x: [K] bf16, w: [N, K] (both 16-byte aligned), s: [ceil(N/32), sld];
+// K % 32 == 0, K <= 16384.  Dynamic shared memory: 2K bytes.
+constexpr int GF8_U = 16;             // 16-byte chunk slots a lane (fp8)
+template <typename TO>
+__global__ void __launch_bounds__(GM1_THREADS, 2) k_gemv_fp8_m1(
+    const uint16_t *__restrict__ x, int64_t K, const uint8_t *__restrict__ w,
+    const uint8_t *__restrict__ s, int64_t sld, int64_t N, TO *__restrict__ y) {
+  extern __shared__ __align__(16) uint8_t gm1_smem[];
+  // x * 2^-E as f16, 16-byte segment i of 16-code chunk c (x[16c + 8i ..]) at xt[i*nch + c]
+  uint4 *xt = reinterpret_cast<uint4 *>(gm1_smem);
+  __shared__ float red[GM1_THREADS / 32];
+  __shared__ int s_e;
+  const int nch = int(K / 16);
+  const int npass = (nch + 32 * GF8_U - 1) / (32 * GF8_U);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row0 = int64_t(blockIdx.x) * (GM1_THREADS / 32) + warp;
+  const int64_t rstride = int64_t(gridDim.x) * (GM1_THREADS / 32);
+  uint4 v[GF8_U];
+  uint32_t sc[GF8_U];
+  // step t of this warp: row row0 + (t / npass) * rstride, chunks from 256 (t % npass)
+  auto load_slot = [&](int64_t t, int u) {
+    const int64_t r = row0 + (t / npass) * rstride;
+    const int c = int(t % npass) * (32 * GF8_U) + u * 32 + lane;
+    const bool in = r < N && c < nch;
+    v[u] = in ? __ldcs(reinterpret_cast<const uint4 *>(w + r * K) + c) : make_uint4(0u, 0u, 0u, 0u);
+    sc[u] = in ? uint32_t(__ldg(s + (r >> 5) * sld + (c >> 1))) : 0u;
+  };
+#pragma unroll
+  for (int u = 0; u < GF8_U; ++u) load_slot(0, u);
+  // the row's max |x| and the f16 copy: x's first 4 x 256 segments read once into registers,
+  // any further ones (K > 8192) read again for the copy
+  constexpr int XR = 4;
+  const int nseg = int(K / 8);
+  uint4 xr[XR];
+  float amax = 0.0f;
+  for (int i = threadIdx.x + XR * GM1_THREADS; i < nseg; i += GM1_THREADS) {
+    const uint4 xv = __ldg(reinterpret_cast<const uint4 *>(x) + i);
+    const uint32_t wv[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      amax = fmaxf(amax, fmaxf(fabsf(__uint_as_float(wv[j] << 16)),
+                               fabsf(__uint_as_float(wv[j] & 0xFFFF0000u))));
+  }
+#pragma unroll
+  for (int k = 0; k < XR; ++k) {
+    const int i = threadIdx.x + k * GM1_THREADS;
+    xr[k] = i < nseg ? __ldg(reinterpret_cast<const uint4 *>(x) + i) : make_uint4(0u, 0u, 0u, 0u);
+    const uint32_t wv[4] = {xr[k].x, xr[k].y, xr[k].z, xr[k].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      amax = fmaxf(amax, fmaxf(fabsf(__uint_as_float(wv[j] << 16)),
+                               fabsf(__uint_as_float(wv[j] & 0xFFFF0000u))));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if (lane == 0) red[warp] = amax;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float m = 0.0f;
+    for (int i = 0; i < GM1_THREADS / 32; ++i) m = fmaxf(m, red[i]);
+    int E = 0;
+    if (m > 0.0f && m < INFINITY) E = int((__float_as_uint(m) >> 23) & 0xFF) - 127 - 14;
+    s_e = E < -126 ? -126 : E;
+  }
+  __syncthreads();
+  const int E = s_e;
+  const float inv = ldexpf(1.0f, -E);
+  auto put = [&](const uint4 &xv, int i) {
+    const uint32_t wv[4] = {xv.x, xv.y, xv.z, xv.w};
+    uint32_t hv[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const __half2 h = __floats2half2_rn(__uint_as_float(wv[j] << 16) * inv,
+                                          __uint_as_float(wv[j] & 0xFFFF0000u) * inv);
+      hv[j] = *reinterpret_cast<const uint32_t *>(&h);
+    }
+    xt[(i & 1) * nch + (i >> 1)] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+  };
+#pragma unroll
+  for (int k = 0; k < XR; ++k) {
+    const int i = threadIdx.x + k * GM1_THREADS;
+    if (i < nseg) put(xr[k], i);
+  }
+  for (int i = threadIdx.x + XR * GM1_THREADS; i < nseg; i += GM1_THREADS)
+    put(__ldg(reinterpret_cast<const uint4 *>(x) + i), i);
+  __syncthreads();
+  const float out_scale = ldexpf(1.0f, E);
+  int64_t t = 0;
+  for (int64_t r = row0; r < N; r += rstride) {
+    float acc = 0.0f;
+    for (int pass = 0; pass < npass; ++pass, ++t) {
+      const int c0 = pass * (32 * GF8_U);
+#pragma unroll
+      for (int u = 0; u < GF8_U; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < nch) {
+          const uint4 xa = xt[c], xb = xt[nch + c];
+          const uint32_t wv[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+          const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+          float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint32_t h0, h1;
+            e4m3x4_to_f16x4(wv[j], h0, h1);
+            gm1_fma2_f16(h0, xw[2 * j], a0, a1);
+            gm1_fma2_f16(h1, xw[2 * j + 1], a0, a1);
+          }
+          acc = __fmaf_rn(__uint_as_float(sc[u] << 23), a0 + a1, acc);
+        }
+        load_slot(t + 1, u);                        // this slot's next step
+      }
+    }
+    acc *= out_scale;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
     if (lane == 0) {

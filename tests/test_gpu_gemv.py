@@ -28,8 +28,11 @@ def _x(bits):
     return _d(bits.view(np.int16)).view(torch.bfloat16)
 
 
+# M = 1 goes to the single-row CUDA-core kernel (k_gemv_fp8_m1): ragged N, K from one 32-code
+# block to four passes of a lane's chunk window
 @pytest.mark.parametrize("M,N,K", [(1, 256, 512), (5, 200, 256), (8, 64, 128), (16, 130, 384),
-                                   (32, 512, 1024), (40, 96, 7168), (1, 4096, 7168)])
+                                   (32, 512, 1024), (40, 96, 7168), (1, 4096, 7168),
+                                   (1, 70, 32), (1, 33, 16384), (1, 1000, 4160)])
 def test_gemv_fp8_block(cuda, M, N, K):
     rng = np.random.default_rng(M * 1000 + N)
     w, s = fp8_weight(rng, N, K)
