@@ -509,7 +509,7 @@ def d4_measure(q, torch, dev, flush, stream, K, W, peaks):
                 st = statistics.mean(timed_steps(torch, lambda i: gr[i % copies].replay(), K * 4,
                                                  W, flush, stream))
                 del gr
-                kname = "gemv_affine4_m1" if (M == 1 and bits == 4) else "qgemv_dense"
+                kname = f"gemv_affine{bits}_m1" if M == 1 else "qgemv_dense"
                 bound, work, pk = "hbm", byts, hbm
                 metric, unit = "dequant-GEMV HBM GB/s", "GB/s"
                 val = byts / st / 1e6

@@ -533,11 +533,11 @@ extern "C" int dsv41_gemv_fp8_block(const void *x, int64_t M, int64_t K, const u
     ProfScope prof("gemv_fp8_m1", st);
     const uint16_t *xs = static_cast<const uint16_t *>(x);
     if (out_dtype == DSV41_F32)
-      k_gemv_fp8_m1<float><<<grid, GM1_THREADS, size_t(K) * 2, st>>>(xs, K, w, s, K / 32, N,
-                                                                     (float *)y);
+      k_gemv_byte_m1<false, float><<<grid, GM1_THREADS, size_t(K) * 2, st>>>(
+          xs, K, w, s, nullptr, K / 32, N, (float *)y);
     else
-      k_gemv_fp8_m1<__nv_bfloat16><<<grid, GM1_THREADS, size_t(K) * 2, st>>>(
-          xs, K, w, s, K / 32, N, (__nv_bfloat16 *)y);
+      k_gemv_byte_m1<false, __nv_bfloat16><<<grid, GM1_THREADS, size_t(K) * 2, st>>>(
+          xs, K, w, s, nullptr, K / 32, N, (__nv_bfloat16 *)y);
     DSV41_CHECK_LAUNCH("gemv_fp8_m1");
     return DSV41_OK;
   }
@@ -578,6 +578,27 @@ extern "C" int dsv41_gemv_affine(const void *x, int64_t M, int64_t K, const uint
       k_gemv_affine4_m1<__nv_bfloat16><<<grid, GM1_THREADS, smem, st>>>(xs, K, wq, sc, bi, N,
                                                                        (__nv_bfloat16 *)y);
     DSV41_CHECK_LAUNCH("gemv_affine4_m1");
+    return DSV41_OK;
+  }
+  // one activation row, 8-bit: the byte-code CUDA-core kernel in its affine form
+  if (bits == 8 && M == 1 && N > 0 && K > 0 && K % 64 == 0 && K <= 16384 && x && wq && y &&
+      aligned(x, 16) && aligned(wq, 16) && (out_dtype == DSV41_F32 || out_dtype == DSV41_BF16)) {
+    DSV41_REQUIRE(N <= (int64_t)INT32_MAX, DSV41_ERR_BAD_SHAPE, "shape too large");
+    cudaStream_t st = STREAM(stream);
+    const int64_t want = ceil_div(N, int64_t(GM1_THREADS / 32));
+    const unsigned grid = unsigned(std::min<int64_t>(want, 2 * int64_t(num_sms())));
+    const size_t smem = size_t(K) * 2 + size_t(K / 8) * 4;
+    ProfScope prof("gemv_affine8_m1", st);
+    const uint16_t *xs = static_cast<const uint16_t *>(x);
+    const uint8_t *wb = reinterpret_cast<const uint8_t *>(wq);
+    const uint16_t *bi = static_cast<const uint16_t *>(biases);
+    if (out_dtype == DSV41_F32)
+      k_gemv_byte_m1<true, float><<<grid, GM1_THREADS, smem, st>>>(xs, K, wb, scales, bi, K / 64,
+                                                                   N, (float *)y);
+    else
+      k_gemv_byte_m1<true, __nv_bfloat16><<<grid, GM1_THREADS, smem, st>>>(
+          xs, K, wb, scales, bi, K / 64, N, (__nv_bfloat16 *)y);
+    DSV41_CHECK_LAUNCH("gemv_affine8_m1");
     return DSV41_OK;
   }
   if (bits == 4)

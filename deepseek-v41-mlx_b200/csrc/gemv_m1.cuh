@@ -157,7 +157,8 @@ __device__ __forceinline__ void gm1_fma2_f16(uint32_t h, uint32_t xh, float &a0,
       : "r"(h), "r"(xh));
 }
 
-// One activation row times an fp8 e4m3 weight with ue8m0 scales per 32 x 32 block (upstream
+// k_gemv_byte_m1<false>: one activation row times an fp8 e4m3 weight with ue8m0 scales per
+// 32 x 32 block (upstream
 // `weight_dequant` then the product; the d1 dense linear at decode).  The same arithmetic as
 // the tensor-core engine's single-row case, without its activation-prep launch: every CTA
 // finds the row's max |x|, keeps x * 2^-E as f16 in shared memory (E = exponent(max) - 14, the
@@ -169,14 +170,23 @@ __device__ __forceinline__ void gm1_fma2_f16(uint32_t h, uint32_t xh, float &a0,
 // same slot of the next 512 chunks of the row, or of its next row) as soon as they are
 // consumed, so up to 8 KB of codes per warp stay in flight.  x: [K] bf16, w: [N, K] (both 16-byte aligned), s: [ceil(N/32), sld];
 // K % 32 == 0, K <= 16384.  Dynamic shared memory: 2K bytes.
+//
+// AFF: the same kernel for MLX affine 8-bit codes (a14 at M = 1, [N, K/4] u32 words, bf16
+// scales and biases per 64-code group): codes become exact f16 through the 0x6400 exponent
+// (1024 + q, minus 1024), bytes 0 and 2 of a word together, then 1 and 3, with x kept in that
+// order; the lane sums scale x (codes . x * 2^-E) and, apart, bias x (sum of x) per 16-code
+// chunk, the first scaled by 2^E at the end.  s: scales, b: biases (AFF); s: ue8m0 (fp8).
 constexpr int GF8_U = 16;             // 16-byte chunk slots a lane (fp8)
-template <typename TO>
-__global__ void __launch_bounds__(GM1_THREADS, 2) k_gemv_fp8_m1(
+template <bool AFF, typename TO>
+__global__ void __launch_bounds__(GM1_THREADS, 2) k_gemv_byte_m1(
     const uint16_t *__restrict__ x, int64_t K, const uint8_t *__restrict__ w,
-    const uint8_t *__restrict__ s, int64_t sld, int64_t N, TO *__restrict__ y) {
+    const void *__restrict__ sv, const uint16_t *__restrict__ bv, int64_t sld, int64_t N,
+    TO *__restrict__ y) {
   extern __shared__ __align__(16) uint8_t gm1_smem[];
   // x * 2^-E as f16, 16-byte segment i of 16-code chunk c (x[16c + 8i ..]) at xt[i*nch + c]
+  // (AFF: pairs (x0, x2), (x1, x3) of every 4); AFF: then the fp32 sum of each segment of x
   uint4 *xt = reinterpret_cast<uint4 *>(gm1_smem);
+  float *xsum8 = reinterpret_cast<float *>(gm1_smem + size_t(K) * 2);
   __shared__ float red[GM1_THREADS / 32];
   __shared__ int s_e;
   const int nch = int(K / 16);
@@ -192,7 +202,15 @@ __global__ void __launch_bounds__(GM1_THREADS, 2) k_gemv_fp8_m1(
     const int c = int(t % npass) * (32 * GF8_U) + u * 32 + lane;
     const bool in = r < N && c < nch;
     v[u] = in ? __ldcs(reinterpret_cast<const uint4 *>(w + r * K) + c) : make_uint4(0u, 0u, 0u, 0u);
-    sc[u] = in ? uint32_t(__ldg(s + (r >> 5) * sld + (c >> 1))) : 0u;
+    if constexpr (AFF) {
+      const int64_t gi = r * sld + (c >> 2);
+      sc[u] = in ? (uint32_t(__ldg(static_cast<const uint16_t *>(sv) + gi)) << 16) |
+                       uint32_t(__ldg(bv + gi))
+                 : 0u;
+    } else {
+      sc[u] = in ? uint32_t(__ldg(static_cast<const uint8_t *>(sv) + (r >> 5) * sld + (c >> 1)))
+                 : 0u;
+    }
   };
 #pragma unroll
   for (int u = 0; u < GF8_U; ++u) load_slot(0, u);
@@ -235,7 +253,19 @@ __global__ void __launch_bounds__(GM1_THREADS, 2) k_gemv_fp8_m1(
   const int E = s_e;
   const float inv = ldexpf(1.0f, -E);
   auto put = [&](const uint4 &xv, int i) {
-    const uint32_t wv[4] = {xv.x, xv.y, xv.z, xv.w};
+    uint32_t wv[4] = {xv.x, xv.y, xv.z, xv.w};
+    if constexpr (AFF) {
+      float sum = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        sum += __uint_as_float(wv[j] << 16) + __uint_as_float(wv[j] & 0xFFFF0000u);
+      xsum8[i] = sum;
+      const uint32_t a = wv[0], b = wv[1], c = wv[2], d = wv[3];
+      wv[0] = __byte_perm(a, b, 0x5410);        // (x0, x2)
+      wv[1] = __byte_perm(a, b, 0x7632);        // (x1, x3)
+      wv[2] = __byte_perm(c, d, 0x5410);        // (x4, x6)
+      wv[3] = __byte_perm(c, d, 0x7632);        // (x5, x7)
+    }
     uint32_t hv[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -256,7 +286,7 @@ __global__ void __launch_bounds__(GM1_THREADS, 2) k_gemv_fp8_m1(
   const float out_scale = ldexpf(1.0f, E);
   int64_t t = 0;
   for (int64_t r = row0; r < N; r += rstride) {
-    float acc = 0.0f;
+    float acc = 0.0f, accb = 0.0f;                   // AFF: accb = the bias terms
     for (int pass = 0; pass < npass; ++pass, ++t) {
       const int c0 = pass * (32 * GF8_U);
 #pragma unroll
@@ -270,16 +300,32 @@ __global__ void __launch_bounds__(GM1_THREADS, 2) k_gemv_fp8_m1(
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             uint32_t h0, h1;
-            e4m3x4_to_f16x4(wv[j], h0, h1);
+            if constexpr (AFF) {
+              // (0x6400 | q) is f16 1024 + q: bytes 0, 2 and then 1, 3 of the word
+              const __half2 m = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
+              uint32_t t0 = (wv[j] & 0x00FF00FFu) | 0x64006400u;
+              uint32_t t1 = ((wv[j] >> 8) & 0x00FF00FFu) | 0x64006400u;
+              const __half2 q0 = __hsub2(*reinterpret_cast<const __half2 *>(&t0), m);
+              const __half2 q1 = __hsub2(*reinterpret_cast<const __half2 *>(&t1), m);
+              h0 = *reinterpret_cast<const uint32_t *>(&q0);
+              h1 = *reinterpret_cast<const uint32_t *>(&q1);
+            } else {
+              e4m3x4_to_f16x4(wv[j], h0, h1);
+            }
             gm1_fma2_f16(h0, xw[2 * j], a0, a1);
             gm1_fma2_f16(h1, xw[2 * j + 1], a0, a1);
           }
-          acc = __fmaf_rn(__uint_as_float(sc[u] << 23), a0 + a1, acc);
+          if constexpr (AFF) {
+            acc = __fmaf_rn(__uint_as_float(sc[u] & 0xFFFF0000u), a0 + a1, acc);
+            accb = __fmaf_rn(__uint_as_float(sc[u] << 16), xsum8[2 * c] + xsum8[2 * c + 1], accb);
+          } else {
+            acc = __fmaf_rn(__uint_as_float(sc[u] << 23), a0 + a1, acc);
+          }
         }
         load_slot(t + 1, u);                        // this slot's next step
       }
     }
-    acc *= out_scale;
+    acc = acc * out_scale + accb;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
     if (lane == 0) {

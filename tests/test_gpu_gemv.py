@@ -73,24 +73,25 @@ def test_gemv_affine(cuda, bits, M, N, K):
     assert rel_fro(gotb, want) < TOL_BF16
 
 
-# one activation row, 4-bit: the CUDA-core kernel (k_gemv_affine4_m1); K from one chunk group
-# to two passes of the lane's 8-chunk window, ragged N
+# one activation row: the CUDA-core kernels (k_gemv_affine4_m1, k_gemv_byte_m1<affine>); K from
+# one group to two passes of a lane's chunk window, ragged N
+@pytest.mark.parametrize("bits", [4, 8])
 @pytest.mark.parametrize("N,K", [(14336, 7168), (37, 64), (300, 16384), (1000, 4160)])
-def test_gemv_affine4_single_row(cuda, N, K):
-    rng = np.random.default_rng(N + K)
-    wq, s, b = affine_weight(rng, N, K, 4)
+def test_gemv_affine_single_row(cuda, bits, N, K):
+    rng = np.random.default_rng(N + K + bits)
+    wq, s, b = affine_weight(rng, N, K, bits)
     xb, xf = bf16_acts(rng, 1, K)
     ts = _d(s.view(np.int16)).view(torch.bfloat16)
     tb = _d(b.view(np.int16)).view(torch.bfloat16)
     rows = rng.choice(N, min(N, 512), replace=False)
-    want = OL.linear_affine(xf, wq[rows], s[rows], b[rows], 4)
-    got = q.linear.linear_affine(_x(xb), _d(wq.view(np.int32)), ts, tb, 4,
+    want = OL.linear_affine(xf, wq[rows], s[rows], b[rows], bits)
+    got = q.linear.linear_affine(_x(xb), _d(wq.view(np.int32)), ts, tb, bits,
                                  out_dtype=torch.float32)
     assert rel_fro(got.cpu().numpy()[:, rows], want) < TOL_F32
-    again = q.linear.linear_affine(_x(xb), _d(wq.view(np.int32)), ts, tb, 4,
+    again = q.linear.linear_affine(_x(xb), _d(wq.view(np.int32)), ts, tb, bits,
                                    out_dtype=torch.float32)
     assert torch.equal(got, again)                         # fixed summation order
-    gotb = q.linear.linear_affine(_x(xb), _d(wq.view(np.int32)), ts, tb, 4).float().cpu().numpy()
+    gotb = q.linear.linear_affine(_x(xb), _d(wq.view(np.int32)), ts, tb, bits).float().cpu().numpy()
     assert rel_fro(gotb[:, rows], want) < TOL_BF16
 
 
