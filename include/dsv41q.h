@@ -162,7 +162,9 @@ int dsv41_act_quant_fp8(const void *x, int64_t M, int64_t K, int block, int roun
  * activations are NOT quantized) and mx.quantized_matmul behind
  * nn.QuantizedLinear (deepseek_v41_mlx/load.py:124-131).
  * Requires K % 32 == 0 (fp8/fp4) or K % group == 0 (affine); N arbitrary.
- * out_dtype F32 or BF16. */
+ * out_dtype F32 or BF16.  A single activation row (M == 1) of dsv41_gemv_fp8_block or
+ * dsv41_gemv_affine with K <= 16384 and 16-byte aligned x and weights runs as one
+ * CUDA-core launch and leaves the workspace untouched (pass it all the same). */
 size_t dsv41_gemv_workspace_size(int64_t M, int64_t N, int64_t K);
 int dsv41_gemv_fp8_block(const void *x, int64_t M, int64_t K, const uint8_t *w,
                          const uint8_t *s, int64_t N, int out_dtype, void *y, void *workspace,
