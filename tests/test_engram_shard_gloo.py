@@ -99,7 +99,9 @@ def _worker(rank, world, init, out_q):
             s = emb.gather_sum(idx, out_dtype=torch.float32)
             r = emb(idx, out_dtype=torch.float32)
             results.append((s, r))
-        out_q.put((rank, [(s.clone(), r.clone()) for s, r in results], None))
+        # numpy copies travel by plain pickling: a torch tensor put on the queue goes through a
+        # shared-memory handle that can vanish when this process exits before it is read
+        out_q.put((rank, [(s.numpy().copy(), r.numpy().copy()) for s, r in results], None))
     except Exception as e:  # noqa: BLE001
         out_q.put((rank, None, repr(e)))
     finally:
@@ -127,7 +129,7 @@ def test_parallel_engram_matches_single_table(world, tmp_path):
         want_sum = _reference_sum(codes, scale, idx)
         want_rows = _dequant(codes, scale)[idx.reshape(-1)].reshape(tuple(idx.shape) + (D,))
         for rank in range(world):
-            s, r = got[rank][ci]
+            s, r = (torch.from_numpy(a) for a in got[rank][ci])
             assert torch.equal(s, want_sum), f"case {ci} rank {rank}: summed rows differ"
             assert torch.equal(r, want_rows), f"case {ci} rank {rank}: rows differ"
 
