@@ -147,6 +147,50 @@ def test_gemv_large_activations(cuda):
         assert rel_fro(got[r], want[r]) < TOL_F32
 
 
+@pytest.mark.parametrize("bits", [0, 4, 8])
+def test_gemv_single_row_large_activations(cuda, bits):
+    """The single-row kernels (fp8: per-row power-of-two f16 copy of x; affine: bf16 / f16 x)
+    on huge and tiny activation rows: each row alone against the oracle."""
+    rng = np.random.default_rng(13 + bits)
+    N, K = 96, 1024
+    for mult in (1e30, 1e-30, 1.0):
+        xb, xf = bf16_acts(rng, 1, K)
+        xb = F.f32_to_bf16_bits(xf * np.float32(mult))
+        xf = F.bf16_bits_to_f32(xb)
+        if bits == 0:
+            w, sc = fp8_weight(rng, N, K)
+            want = OL.linear_fp8_block(xf, w, sc)
+            got = q.linear.linear_fp8(_x(xb), _d(w), _d(sc), out_dtype=torch.float32)
+        else:
+            wq, sa, ba = affine_weight(rng, N, K, bits)
+            want = OL.linear_affine(xf, wq, sa, ba, bits)
+            got = q.linear.linear_affine(_x(xb), _d(wq.view(np.int32)),
+                                         _d(sa.view(np.int16)).view(torch.bfloat16),
+                                         _d(ba.view(np.int16)).view(torch.bfloat16), bits,
+                                         out_dtype=torch.float32)
+        assert rel_fro(got.cpu().numpy(), want) < TOL_F32, mult
+
+
+def test_gemv_fp8_single_row_matches_engine_on_edge_codes(cuda):
+    """NaN codes, scale bytes 0 (applied as 0) to 200: the single-row kernel and the
+    tensor-core engine (a two-row call) give the same NaN pattern and agree elsewhere."""
+    rng = np.random.default_rng(14)
+    N, K = 160, 2048
+    w = rng.integers(0, 256, size=(N, K), dtype=np.uint8)
+    w[(w & 0x7F) == 0x7F] = 0
+    w[5, 100] = 0x7F                                     # NaN codes in rows 5 and 77
+    w[77, 2000] = 0xFF
+    s = rng.integers(0, 201, size=((N + 31) // 32, K // 32), dtype=np.uint8)
+    s[0, 0] = 0
+    xb, _ = bf16_acts(rng, 2, K)
+    one = q.linear.linear_fp8(_x(xb[:1]), _d(w), _d(s), out_dtype=torch.float32).cpu().numpy()
+    two = q.linear.linear_fp8(_x(xb), _d(w), _d(s), out_dtype=torch.float32).cpu().numpy()[:1]
+    assert np.array_equal(np.isnan(one), np.isnan(two))
+    assert np.isnan(one[0, 5]) and np.isnan(one[0, 77])
+    fin = ~np.isnan(one) & np.isfinite(two)
+    assert rel_fro(one[fin], two[fin]) < TOL_F32
+
+
 @pytest.mark.parametrize("M", [1, 32])
 def test_gemv_chain_in_graph_matches_eager(cuda, M):
     """Consecutive dense GEMVs replayed from one CUDA graph -- each one launched as the
