@@ -256,6 +256,23 @@ def kernel_ms(q, torch, fn, names, K, flush, stream):
     return {k: (v[0] / K, v[1] / v[0]) for k, v in rep.items() if v[0]}
 
 
+def capture(torch, fn):
+    """fn's launches as a CUDA graph; Python's cycle collector runs first and is off during the
+    capture, so that no finalizer destroys a CUDA graph or event inside it."""
+    import gc
+    g = torch.cuda.CUDAGraph()
+    gc_on = gc.isenabled()
+    gc.collect()
+    gc.disable()
+    try:
+        with torch.cuda.graph(g):
+            fn()
+    finally:
+        if gc_on:
+            gc.enable()
+    return g
+
+
 def graphed(torch, fns):
     """Capture each call (through the public API) into a CUDA graph, after one warm-up."""
     out = []
@@ -266,10 +283,7 @@ def graphed(torch, fns):
             f()
     torch.cuda.current_stream().wait_stream(side)
     for f in fns:
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            f()
-        out.append(g)
+        out.append(capture(torch, f))
     return out
 
 
@@ -715,10 +729,7 @@ def run_ours(args):
     if world == 1:
         steps = []
         for i in range(K):                            # one graph per timed step
-            gr = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(gr):
-                fwd(xs[i % len(xs)])
-            steps.append(gr)
+            steps.append(capture(torch, lambda i=i: fwd(xs[i % len(xs)])))
         launches = q._lib.prof_launches()             # counted once per captured launch
         for i in range(W):
             steps[i % K].replay()

@@ -23,6 +23,7 @@ intermediate in fp32 (``round_bf16=False``).
 from __future__ import annotations
 
 import ctypes as C
+import gc
 
 from . import _lib as L
 
@@ -207,8 +208,17 @@ class MoE:
                 self._decode_into(sx, sy, sw, si, W, ws, cfg)
             t.cuda.current_stream(xf.device).wait_stream(side)
             g = t.cuda.CUDAGraph()
-            with t.cuda.graph(g):
-                self._decode_into(sx, sy, sw, si, W, ws, cfg)
+            # dead Python cycles that own CUDA graphs or events are collected now: a collection
+            # inside the capture would destroy them there and invalidate the capture
+            gc_on = gc.isenabled()
+            gc.collect()
+            gc.disable()
+            try:
+                with t.cuda.graph(g):
+                    self._decode_into(sx, sy, sw, si, W, ws, cfg)
+            finally:
+                if gc_on:
+                    gc.enable()
             ent = (g, sx, sy, sw, si, ws, W, keep, cfg)
             self._graphs[key] = ent
         g, sx, sy, sw, si = ent[:5]

@@ -5,6 +5,8 @@ Tolerances (relative Frobenius): 1e-5 with fp32 output, 1e-2 with bf16 output.
 
 from __future__ import annotations
 
+import gc
+
 import numpy as np
 import pytest
 import torch
@@ -210,8 +212,13 @@ def test_gemv_chain_in_graph_matches_eager(cuda, M):
         [q.linear.linear_fp8(tx[i], *tw[i], out_dtype=torch.float32) for i in range(n)]
     torch.cuda.current_stream().wait_stream(side)
     g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
-        outs = [q.linear.linear_fp8(tx[i], *tw[i], out_dtype=torch.float32) for i in range(n)]
+    gc.collect()                  # no finalizer of an earlier test's CUDA objects mid-capture
+    gc.disable()
+    try:
+        with torch.cuda.graph(g):
+            outs = [q.linear.linear_fp8(tx[i], *tw[i], out_dtype=torch.float32) for i in range(n)]
+    finally:
+        gc.enable()
     for _ in range(2):
         for o in outs:
             o.zero_()
