@@ -962,16 +962,26 @@ __global__ void __launch_bounds__(256) k_qx_prep(const __nv_bfloat16 *__restrict
   __shared__ float s_inv;
   const int64_t nv = K / 8;
   const uint4 *xv = reinterpret_cast<const uint4 *>(x + (src >= 0 ? src : 0) * K);
+  // the row is read once: a thread's first QXP_R vectors stay in registers for the conversion
+  // (all of it for K <= QXP_R * 8 * blockDim.x), any further ones are read again
+  constexpr int QXP_R = 4;
+  uint4 xr[QXP_R];
   float amax = 0.0f;
-  if (src >= 0) {
-    for (int64_t i = threadIdx.x; i < nv; i += blockDim.x) {
-      const uint4 v = __ldg(xv + i);
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  auto absmax = [&](const uint4 &v) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        amax = fmaxf(amax, fmaxf(fabsf(bf_bits2f(uint16_t(w[j]))), fabsf(bf_bits2f(uint16_t(w[j] >> 16)))));
-    }
+    for (int j = 0; j < 4; ++j)
+      amax = fmaxf(amax, fmaxf(fabsf(bf_bits2f(uint16_t(w[j]))), fabsf(bf_bits2f(uint16_t(w[j] >> 16)))));
+  };
+#pragma unroll
+  for (int k = 0; k < QXP_R; ++k) {
+    const int64_t i = threadIdx.x + int64_t(k) * blockDim.x;
+    xr[k] = (src >= 0 && i < nv) ? __ldg(xv + i) : make_uint4(0u, 0u, 0u, 0u);
+    absmax(xr[k]);
   }
+  if (src >= 0)
+    for (int64_t i = threadIdx.x + int64_t(QXP_R) * blockDim.x; i < nv; i += blockDim.x)
+      absmax(__ldg(xv + i));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
@@ -988,19 +998,14 @@ __global__ void __launch_bounds__(256) k_qx_prep(const __nv_bfloat16 *__restrict
   __syncthreads();
   const float inv = s_inv;
   uint4 *qv = reinterpret_cast<uint4 *>(xq + r * K);
-  for (int64_t i = threadIdx.x; i < nv; i += blockDim.x) {
+  // vector i of the row (zeros for a padding row) -> f16 * 2^-E, in the format's k order
+  auto emit = [&](const uint4 &v, int64_t i) {
     float f[8];
-    if (src >= 0) {
-      const uint4 v = __ldg(xv + i);
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        f[2 * j] = bf_bits2f(uint16_t(w[j])) * inv;
-        f[2 * j + 1] = bf_bits2f(uint16_t(w[j] >> 16)) * inv;
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) f[j] = 0.0f;
+    for (int j = 0; j < 4; ++j) {
+      f[2 * j] = bf_bits2f(uint16_t(w[j])) * inv;
+      f[2 * j + 1] = bf_bits2f(uint16_t(w[j] >> 16)) * inv;
     }
     __half h[8];
 #pragma unroll
@@ -1025,7 +1030,14 @@ __global__ void __launch_bounds__(256) k_qx_prep(const __nv_bfloat16 *__restrict
       s += __shfl_xor_sync(gmask, s, 4);
       if ((threadIdx.x & 7) == 0) xsum[r * (K / 64) + i / 8] = s;
     }
+  };
+#pragma unroll
+  for (int k = 0; k < QXP_R; ++k) {
+    const int64_t i = threadIdx.x + int64_t(k) * blockDim.x;
+    if (i < nv) emit(xr[k], i);
   }
+  for (int64_t i = threadIdx.x + int64_t(QXP_R) * blockDim.x; i < nv; i += blockDim.x)
+    emit(src >= 0 ? __ldg(xv + i) : make_uint4(0u, 0u, 0u, 0u), i);
 }
 
 // ------------------------------------------------------------------ decode scale pack
