@@ -1,5 +1,6 @@
 // gemv_m1.cuh -- one activation row times a quantized weight on the CUDA cores: MLX affine
-// 4-bit (a14 at M = 1) and fp8 e4m3 with 32 x 32 block scales (a13's dense linear at M = 1).
+// 4-bit and 8-bit (mx.quantized_matmul at M = 1) and fp8 e4m3 with 32 x 32 block scales (the
+// dense fp8 linear at M = 1).
 //
 // Affine:
 // y[n] = sum_g ( s[n,g] * sum_{k in g} q[n,k] x[k]  +  b[n,g] * sum_{k in g} x[k] ), the form
@@ -158,8 +159,8 @@ __device__ __forceinline__ void gm1_fma2_f16(uint32_t h, uint32_t xh, float &a0,
 }
 
 // k_gemv_byte_m1<false>: one activation row times an fp8 e4m3 weight with ue8m0 scales per
-// 32 x 32 block (upstream
-// `weight_dequant` then the product; the d1 dense linear at decode).  The same arithmetic as
+// 32 x 32 block (upstream `weight_dequant` then the product; the dense linear at decode).  The
+// same arithmetic as
 // the tensor-core engine's single-row case, without its activation-prep launch: every CTA
 // finds the row's max |x|, keeps x * 2^-E as f16 in shared memory (E = exponent(max) - 14, the
 // engine's per-row multiplier: exact for bf16 values within 2^29 of the max), and per 32-code
@@ -168,10 +169,11 @@ __device__ __forceinline__ void gm1_fma2_f16(uint32_t h, uint32_t xh, float &a0,
 // the engine does) and finally 2^E.  A warp takes a row at a time, lane l the 16-code chunks
 // l, l + 32, ...; its 16 chunk slots (a whole row at K <= 8192) are refilled one step ahead (the
 // same slot of the next 512 chunks of the row, or of its next row) as soon as they are
-// consumed, so up to 8 KB of codes per warp stay in flight.  x: [K] bf16, w: [N, K] (both 16-byte aligned), s: [ceil(N/32), sld];
-// K % 32 == 0, K <= 16384.  Dynamic shared memory: 2K bytes.
+// consumed, so up to 8 KB of codes per warp stay in flight.  x: [K] bf16, w: [N, K] (both
+// 16-byte aligned), s: [ceil(N/32), sld]; K % 32 == 0, K <= 16384.  Dynamic shared memory: 2K
+// bytes (AFF: 2K + K/2).
 //
-// AFF: the same kernel for MLX affine 8-bit codes (a14 at M = 1, [N, K/4] u32 words, bf16
+// AFF: the same kernel for MLX affine 8-bit codes ([N, K/4] u32 words, bf16
 // scales and biases per 64-code group): codes become exact f16 through the 0x6400 exponent
 // (1024 + q, minus 1024), bytes 0 and 2 of a word together, then 1 and 3, with x kept in that
 // order; the lane sums scale x (codes . x * 2^-E) and, apart, bias x (sum of x) per 16-code
@@ -196,7 +198,7 @@ __global__ void __launch_bounds__(GM1_THREADS, 2) k_gemv_byte_m1(
   const int64_t rstride = int64_t(gridDim.x) * (GM1_THREADS / 32);
   uint4 v[GF8_U];
   uint32_t sc[GF8_U];
-  // step t of this warp: row row0 + (t / npass) * rstride, chunks from 256 (t % npass)
+  // step t of this warp: row row0 + (t / npass) * rstride, chunks from 512 (t % npass)
   auto load_slot = [&](int64_t t, int u) {
     const int64_t r = row0 + (t / npass) * rstride;
     const int c = int(t % npass) * (32 * GF8_U) + u * 32 + lane;
